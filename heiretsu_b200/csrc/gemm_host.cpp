@@ -1,0 +1,89 @@
+// Torch-facing entry point of the tcgen05 GEMM: validates tensors, builds
+// the TMA descriptors and picks the instantiation (gemm_inst_*.cu).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <torch/extension.h>
+
+#include "gemm_params.h"
+#include "host_utils.h"
+#include "ops.h"
+
+namespace hb {
+
+void gemm_launch_128_kk(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+void gemm_launch_128_kn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+void gemm_launch_128_nn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+void gemm_launch_256_kk(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+void gemm_launch_256_kn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+void gemm_launch_256_nn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+
+// Tensor map over a row-major bf16 matrix [rows, cols] (cols contiguous):
+// box = 64 columns (one 128-byte swizzle row) x box_rows rows.
+static CUtensorMap operand_map(const at::Tensor& t, int box_rows) {
+  return make_tmap_2d_bf16(t.data_ptr(), t.size(1), t.size(0), t.stride(0) * 2, 64, box_rows);
+}
+
+void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, int64_t epi, bool a_mn, bool b_mn,
+          const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux,
+          const c10::optional<at::Tensor>& resid, int64_t block_n) {
+  TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: tensors must be on CUDA");
+  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: operands must be bf16");
+  TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D tensors expected");
+  TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm: inner dim must be contiguous");
+  TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm: row strides must be multiples of 16 bytes");
+  TORCH_CHECK(N % 8 == 0 && c.stride(0) % 8 == 0, "gemm: N and ldc must be multiples of 8");
+  TORCH_CHECK(!(a_mn && !b_mn), "gemm: A MN-major with B K-major is not instantiated");
+  c10::cuda::CUDAGuard guard(a.device());
+  const int M = a_mn ? a.size(1) : a.size(0);
+  const int K = a_mn ? a.size(0) : a.size(1);
+  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm: K mismatch");
+  TORCH_CHECK((b_mn ? b.size(1) : b.size(0)) <= N, "gemm: B has more rows than N");
+  TORCH_CHECK(c.size(0) >= M && c.size(1) >= N, "gemm: output too small");
+  const bool out_bf16 = (epi == kEpiBf16 || epi == kEpiBf16Gelu || epi == kEpiBf16Dgelu);
+  TORCH_CHECK(c.scalar_type() == (out_bf16 ? at::kBFloat16 : at::kFloat), "gemm: wrong output dtype for epilogue");
+  if (M == 0 || N == 0) return;
+  if (K == 0) TORCH_CHECK(false, "gemm: K == 0 not supported");
+  const int BN = (block_n == 256) ? 256 : 128;
+
+  GemmParams p{};
+  p.M = M;
+  p.N = static_cast<int>(N);
+  p.K = K;
+  p.C = c.data_ptr();
+  p.ldc = c.stride(0);
+  p.status = device_status_ptr(a.get_device());
+  if (bias && bias->defined()) {
+    TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() >= N && N % 4 == 0,
+                "gemm: bias must be fp32 contiguous with >= N elements");
+    p.bias = bias->data_ptr<float>();
+  }
+  if (epi == kEpiBf16Gelu || epi == kEpiBf16Dgelu) {
+    TORCH_CHECK(aux && aux->defined() && aux->scalar_type() == at::kBFloat16 && aux->stride(1) == 1 &&
+                    aux->stride(0) % 8 == 0,
+                "gemm: bf16 aux tensor required");
+    p.aux = aux->data_ptr();
+    p.ldaux = aux->stride(0);
+  }
+  if (epi == kEpiF32Resid) {
+    TORCH_CHECK(resid && resid->defined() && resid->scalar_type() == at::kFloat && resid->stride(1) == 1 &&
+                    resid->stride(0) % 4 == 0,
+                "gemm: fp32 resid tensor required");
+    p.resid = resid->data_ptr<float>();
+    p.ldr = resid->stride(0);
+  }
+  const CUtensorMap ta = operand_map(a, a_mn ? 64 : 128);
+  const CUtensorMap tb = operand_map(b, b_mn ? 64 : BN);
+  cudaStream_t s = at::cuda::getCurrentCUDAStream();
+  const int e = static_cast<int>(epi);
+  if (BN == 256) {
+    if (!a_mn && !b_mn) gemm_launch_256_kk(e, ta, tb, p, s);
+    else if (!a_mn) gemm_launch_256_kn(e, ta, tb, p, s);
+    else gemm_launch_256_nn(e, ta, tb, p, s);
+  } else {
+    if (!a_mn && !b_mn) gemm_launch_128_kk(e, ta, tb, p, s);
+    else if (!a_mn) gemm_launch_128_kn(e, ta, tb, p, s);
+    else gemm_launch_128_nn(e, ta, tb, p, s);
+  }
+}
+
+}  // namespace hb

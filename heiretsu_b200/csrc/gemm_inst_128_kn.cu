@@ -1,0 +1,9 @@
+// Instantiations of the tcgen05 GEMM for BN=128, A_MN=false, B_MN=true (split
+// across files so the build compiles them in parallel).
+#include "gemm_kernel.cuh"
+
+namespace hb {
+void gemm_launch_128_kn(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+  gemm_dispatch_epi<128, false, true>(epi, ta, tb, p, s);
+}
+}  // namespace hb

@@ -1,0 +1,303 @@
+#pragma once
+// tcgen05 GEMM core for sm_100a.
+//
+// D[m, n] = sum_k A(m, k) * B(n, k), bf16 operands, fp32 accumulation in
+// tensor memory, fused epilogues. This single kernel template serves every
+// linear layer of the model (reference: tp_linear.py:148, :224, :301 einsums;
+// moe.py:45, :90-92 nn.Linear; gpt_model.py:240 lm_head):
+//   forward  y = x W^T        A = x  [M,K] K-major,  B = W [N,K] K-major
+//   dgrad    dx = dy W        A = dy [M,N] K-major,  B = W stored [N,K] -> MN-major
+//   wgrad    dW = dy^T x      A = dy stored [M,N] -> MN-major, B = x stored [M,K] -> MN-major
+// so no transposed copy of any activation or weight is ever materialised.
+//
+// Structure (one CTA per SM, persistent over output tiles):
+//   warp 0      TMA producer: streams 128xBK A tiles and BNxBK B tiles into a
+//               STAGES-deep shared-memory ring (128-byte swizzle, no multicast).
+//   warp 1      allocates TMEM; one elected thread issues tcgen05.mma
+//               (128 x BN x 16) and commits each stage back to the producer.
+//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator (thread = row),
+//               apply bias / GELU / dGELU / residual, store to global memory.
+// The accumulator is double-buffered in TMEM (2 x BN columns) so the
+// epilogue of tile i overlaps the main loop of tile i+1.
+#include "common.cuh"
+#include "host_utils.h"
+#include "gemm_params.h"
+
+namespace hb {
+
+template <int BN>
+struct GemmCfg {
+  static constexpr int BM = 128;
+  static constexpr int BK = 64;
+  static constexpr int A_BYTES = BM * BK * 2;
+  static constexpr int B_BYTES = BN * BK * 2;
+  static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
+  static constexpr int STAGES = (BN >= 256) ? 4 : 6;
+  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+};
+
+template <int EPI>
+__device__ __forceinline__ void gemm_epilogue_store(const GemmParams& p, int m, int n0, float (&v)[32]) {
+  if (p.bias != nullptr && (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      if (n0 + j < p.N) {
+        float4 b = *reinterpret_cast<const float4*>(p.bias + n0 + j);
+        v[j] += b.x;
+        v[j + 1] += b.y;
+        v[j + 2] += b.z;
+        v[j + 3] += b.w;
+      }
+    }
+  }
+  if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiBf16Dgelu) {
+    __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.C) + (long)m * p.ldc + n0;
+    __nv_bfloat16* arow =
+        (EPI != kEpiBf16) ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (long)m * p.ldaux + n0 : nullptr;
+#pragma unroll
+    for (int j = 0; j < 32; j += 8) {
+      if (n0 + j >= p.N) break;
+      uint4 out;
+      if constexpr (EPI == kEpiBf16) {
+        out = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]), pack_bf16(v[j + 4], v[j + 5]),
+                         pack_bf16(v[j + 6], v[j + 7]));
+      } else if constexpr (EPI == kEpiBf16Gelu) {
+        uint4 pre = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
+                               pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
+        *reinterpret_cast<uint4*>(arow + j) = pre;
+        // GELU of the bf16-rounded pre-activation, so that backward (which
+        // only sees the stored bf16 value) differentiates the same function.
+        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pre);
+        float g[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) g[q] = gelu_tanh(__bfloat162float(pb[q]));
+        out = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+      } else {  // dgelu
+        uint4 pre = *reinterpret_cast<const uint4*>(arow + j);
+        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pre);
+        float g[8];
+#pragma unroll
+        for (int q = 0; q < 8; ++q) g[q] = v[j + q] * gelu_tanh_grad(__bfloat162float(pb[q]));
+        out = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+      }
+      *reinterpret_cast<uint4*>(crow + j) = out;
+    }
+  } else {
+    float* crow = reinterpret_cast<float*>(p.C) + (long)m * p.ldc + n0;
+    const float* rrow = (EPI == kEpiF32Resid) ? p.resid + (long)m * p.ldr + n0 : nullptr;
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      if (n0 + j >= p.N) break;
+      float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
+      if constexpr (EPI == kEpiF32Acc) {
+        float4 c = *reinterpret_cast<const float4*>(crow + j);
+        o.x += c.x;
+        o.y += c.y;
+        o.z += c.z;
+        o.w += c.w;
+      } else if constexpr (EPI == kEpiF32Resid) {
+        float4 r = *reinterpret_cast<const float4*>(rrow + j);
+        o.x += r.x;
+        o.y += r.y;
+        o.z += r.z;
+        o.w += r.w;
+      }
+      *reinterpret_cast<float4*>(crow + j) = o;
+    }
+  }
+}
+
+template <int BN, bool A_MN, bool B_MN, int EPI>
+__global__ void __launch_bounds__(192, 1)
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+  using Cfg = GemmCfg<BN>;
+  constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
+  constexpr int A_BYTES = Cfg::A_BYTES, STAGE_BYTES = Cfg::STAGE_BYTES;
+  constexpr uint32_t TMEM_COLS = Cfg::TMEM_COLS;
+
+  extern __shared__ uint8_t smem_raw[];
+  uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* empty = full + STAGES;
+  uint64_t* tfull = empty + STAGES;
+  uint64_t* tempty = tfull + 2;
+  uint64_t* mma_done = tempty + 2;
+  uint32_t* tmem_slot = reinterpret_cast<uint32_t*>(mma_done + 1);
+
+  const int warp = threadIdx.x >> 5;
+  const int lane = threadIdx.x & 31;
+  const int num_m = (p.M + BM - 1) / BM;
+  const int num_n = (p.N + BN - 1) / BN;
+  const int num_tiles = num_m * num_n;
+  const int num_kb = (p.K + BK - 1) / BK;
+
+  if (warp == 0 && lane == 0) {
+    for (int s = 0; s < STAGES; ++s) {
+      mbar_init(&full[s], 1);
+      mbar_init(&empty[s], 1);
+    }
+    for (int a = 0; a < 2; ++a) {
+      mbar_init(&tfull[a], 1);
+      mbar_init(&tempty[a], 4);
+    }
+    mbar_init(mma_done, 1);
+    fence_barrier_init();
+    tma_prefetch_desc(&tmA);
+    tma_prefetch_desc(&tmB);
+  }
+  if (warp == 1) {
+    tmem_alloc(tmem_slot, TMEM_COLS);
+    tmem_relinquish();
+  }
+  tc_fence_before();
+  __syncthreads();
+  tc_fence_after();
+  const uint32_t tmem_base = *tmem_slot;
+
+  if (warp == 0) {
+    if (elect_one()) {
+      int stage = 0;
+      uint32_t phase = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
+        const int mb = t % num_m, nb = t / num_m;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, 1)) {
+            ok = false;
+            break;
+          }
+          mbar_arrive_expect_tx(&full[stage], STAGE_BYTES);
+          uint8_t* sA = smem + stage * STAGE_BYTES;
+          uint8_t* sB = sA + A_BYTES;
+          if constexpr (!A_MN) {
+            tma_load_2d(sA, &tmA, &full[stage], kb * BK, mb * BM);
+          } else {
+#pragma unroll
+            for (int a = 0; a < BM / 64; ++a) tma_load_2d(sA + a * 8192, &tmA, &full[stage], mb * BM + a * 64, kb * BK);
+          }
+          if constexpr (!B_MN) {
+            tma_load_2d(sB, &tmB, &full[stage], kb * BK, nb * BN);
+          } else {
+#pragma unroll
+            for (int a = 0; a < BN / 64; ++a) tma_load_2d(sB + a * 8192, &tmB, &full[stage], nb * BN + a * 64, kb * BK);
+          }
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+      }
+      // Never leave the CTA with TMA writes into shared memory in flight:
+      // wait (bounded) for the last load issued into every stage.
+      if (!ok) {
+        for (int s = 0; s < STAGES; ++s) {
+          const int back = (stage - 1 - s + 2 * STAGES) % STAGES;
+          const uint32_t ph = (back < stage) ? phase : (phase ^ 1u);
+          mbar_wait(&full[back], ph, nullptr, 0);
+        }
+      }
+    }
+  } else if (warp == 1) {
+    if (elect_one()) {
+      constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN, true);
+      int stage = 0;
+      uint32_t phase = 0;
+      int local = 0;
+      bool ok = true;
+      for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x, ++local) {
+        const int acc = local & 1;
+        const uint32_t acc_phase = (local >> 1) & 1;
+        if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, 2)) break;
+        tc_fence_after();
+        const uint32_t d_tmem = tmem_base + acc * BN;
+        for (int kb = 0; kb < num_kb; ++kb) {
+          if (!mbar_wait(&full[stage], phase, p.status, 3)) {
+            ok = false;
+            break;
+          }
+          tc_fence_after();
+          const uint32_t a_addr = smem_u32(smem + stage * STAGE_BYTES);
+          const uint32_t b_addr = a_addr + A_BYTES;
+#pragma unroll
+          for (int k = 0; k < BK / 16; ++k) {
+            const uint64_t ad = A_MN ? sw128_desc(a_addr + k * 2048, 8192, 1024) : sw128_desc(a_addr + k * 32, 16, 1024);
+            const uint64_t bd = B_MN ? sw128_desc(b_addr + k * 2048, 8192, 1024) : sw128_desc(b_addr + k * 32, 16, 1024);
+            mma_f16_ss(d_tmem, ad, bd, idesc, (kb | k) ? 1u : 0u);
+          }
+          mma_commit(&empty[stage]);
+          if (++stage == STAGES) {
+            stage = 0;
+            phase ^= 1u;
+          }
+        }
+        mma_commit(&tfull[acc]);
+      }
+      // All MMAs issued by this thread must be complete before TMEM is freed.
+      mma_commit(mma_done);
+      mbar_wait(mma_done, 0, p.status, 5);
+    }
+  } else {
+    const int sub = warp & 3;
+    const int row = sub * 32 + lane;
+    int local = 0;
+    for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
+      const int acc = local & 1;
+      const uint32_t acc_phase = (local >> 1) & 1;
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
+      tc_fence_after();
+      const int mb = t % num_m, nb = t / num_m;
+      const int m = mb * BM + row;
+#pragma unroll 1
+      for (int c = 0; c < BN / 32; ++c) {
+        const int n0 = nb * BN + c * 32;
+        if (n0 >= p.N) break;
+        float v[32];
+        tmem_ld32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN + c * 32, v);
+        if (m < p.M) gemm_epilogue_store<EPI>(p, m, n0, v);
+      }
+      tc_fence_before();
+      __syncwarp();
+      if (lane == 0) mbar_arrive(&tempty[acc]);
+    }
+  }
+  __syncthreads();
+  if (warp == 1) {
+    tc_fence_after();
+    tmem_dealloc(tmem_base, TMEM_COLS);
+  }
+}
+
+
+// Launch one instantiation (defined in gemm_inst_*.cu).
+template <int BN, bool A_MN, bool B_MN, int EPI>
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+  using Cfg = GemmCfg<BN>;
+  auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
+  static bool attr_set[64] = {};
+  const int dev = current_device();
+  if (!attr_set[dev]) {
+    HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
+    attr_set[dev] = true;
+  }
+  const int num_tiles = ((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
+  const int grid = num_tiles < num_sms(dev) ? num_tiles : num_sms(dev);
+  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Dispatch over epilogues for one (BN, majors) combination.
+template <int BN, bool A_MN, bool B_MN>
+void gemm_dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+  switch (epi) {
+    case kEpiBf16: return launch_gemm<BN, A_MN, B_MN, kEpiBf16>(ta, tb, p, s);
+    case kEpiBf16Gelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Gelu>(ta, tb, p, s);
+    case kEpiF32: return launch_gemm<BN, A_MN, B_MN, kEpiF32>(ta, tb, p, s);
+    case kEpiF32Acc: return launch_gemm<BN, A_MN, B_MN, kEpiF32Acc>(ta, tb, p, s);
+    case kEpiF32Resid: return launch_gemm<BN, A_MN, B_MN, kEpiF32Resid>(ta, tb, p, s);
+    case kEpiBf16Dgelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Dgelu>(ta, tb, p, s);
+    default: throw std::runtime_error("gemm: unknown epilogue");
+  }
+}
+
+}  // namespace hb

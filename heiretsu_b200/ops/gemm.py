@@ -1,0 +1,88 @@
+"""Python wrappers of the tcgen05 GEMM (heiretsu_b200/csrc/gemm_kernel.cuh).
+
+Three layouts cover every linear layer of the model without transposed
+copies (reference einsums: tp_linear.py:148, :224, :301):
+
+* ``linear_fwd``   y[M,N]  = x[M,K] @ W[N,K]^T   (+ bias, GELU or residual)
+* ``linear_dgrad`` dx[M,K] = dy[M,N] @ W[N,K]    (optionally times GELU'(pre))
+* ``linear_wgrad`` dW[N,K] (+)= dy[M,N]^T @ x[M,K]
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ._C import load
+
+EPI_BF16 = 0
+EPI_BF16_GELU = 1
+EPI_F32 = 2
+EPI_F32_ACC = 3
+EPI_F32_RESID = 4
+EPI_BF16_DGELU = 5
+
+
+def _bn(n: int) -> int:
+    # 256-wide tiles when N is large enough to keep every SM busy at M=8k.
+    return 256 if n >= 2048 else 128
+
+
+def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None):
+    load().gemm(a, b, c, int(n), int(epi), bool(a_mn), bool(b_mn), bias, aux, resid,
+                int(block_n if block_n is not None else _bn(n)))
+    return c
+
+
+def linear_fwd(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
+               out: Optional[torch.Tensor] = None, n: Optional[int] = None) -> torch.Tensor:
+    """bf16 y = x @ w^T + bias. `n` may exceed w.shape[0] (rows beyond are zero)."""
+    M = x.shape[0]
+    N = int(n if n is not None else w.shape[0])
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    return gemm(x, w, out, N, EPI_BF16, False, False, bias=bias)
+
+
+def linear_fwd_gelu(x, w, bias, *, out=None, pre=None):
+    """Returns (gelu(x @ w^T + b), x @ w^T + b), both bf16."""
+    M, N = x.shape[0], w.shape[0]
+    if out is None:
+        out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    if pre is None:
+        pre = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+    gemm(x, w, out, N, EPI_BF16_GELU, False, False, bias=bias, aux=pre)
+    return out, pre
+
+
+def linear_fwd_resid(x, w, bias, resid, *, out=None):
+    """fp32 out = resid + x @ w^T + bias (out may be resid itself)."""
+    N = w.shape[0]
+    if out is None:
+        out = torch.empty_like(resid)
+    return gemm(x, w, out, N, EPI_F32_RESID, False, False, bias=bias, resid=resid)
+
+
+def linear_dgrad(dy, w, *, out=None, gelu_pre=None, f32=False):
+    """dx = dy @ w (w: [N, K]); with `gelu_pre`, dx *= gelu'(gelu_pre)."""
+    M, K = dy.shape[0], w.shape[1]
+    if gelu_pre is not None:
+        epi, dt = EPI_BF16_DGELU, torch.bfloat16
+    else:
+        epi, dt = (EPI_F32, torch.float32) if f32 else (EPI_BF16, torch.bfloat16)
+    if out is None:
+        out = torch.empty(M, K, device=dy.device, dtype=dt)
+    return gemm(dy, w, out, K, epi, False, True, aux=gelu_pre)
+
+
+def linear_wgrad(dy, x, *, out=None, accumulate=False, n_rows=None):
+    """dW[N,K] (+)= dy[:, :N]^T @ x in fp32; `n_rows` limits N (e.g. an unpadded vocab)."""
+    N = int(n_rows if n_rows is not None else dy.shape[1])
+    K = x.shape[1]
+    if out is None:
+        out = torch.zeros(N, K, device=dy.device, dtype=torch.float32)
+        accumulate = False
+    a = dy if N == dy.shape[1] else dy[:, :N]
+    # Kernel view: D[n, k] = sum_m A(n, m) B(k, m) with A = dy and B = x both
+    # stored with the reduction (token) dimension outermost: MN-major.
+    return gemm(a, x, out, K, EPI_F32_ACC if accumulate else EPI_F32, True, True)

@@ -1,0 +1,113 @@
+"""Kernel micro-benchmarks: the model's hot ops against their PyTorch/cuBLAS
+counterparts on the GPT-2 shapes (M = 8 x 1024 tokens).
+
+    python -m heiretsu_b200.ops.microbench [--only gemm] [--json out.json]
+
+Timing: CUDA events on the launching stream, warm-up first, L2 flushed by
+writing a 256 MB buffer before every timed launch, median of the repeats.
+"""
+from __future__ import annotations
+
+import argparse
+import json
+import statistics
+
+import torch
+
+
+def _flush_buf():
+    return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+
+
+def time_fn(fn, reps=20, warmup=5, flush=None):
+    for _ in range(warmup):
+        fn()
+    torch.cuda.synchronize()
+    times = []
+    for _ in range(reps):
+        if flush is not None:
+            flush.zero_()
+        s = torch.cuda.Event(enable_timing=True)
+        e = torch.cuda.Event(enable_timing=True)
+        s.record()
+        fn()
+        e.record()
+        torch.cuda.synchronize()
+        times.append(s.elapsed_time(e))
+    return statistics.median(times)
+
+
+GEMM_SHAPES = [
+    # name, M, N, K, layout
+    ("qkv_fwd", 8192, 2304, 768, "fwd"),
+    ("attnproj_fwd", 8192, 768, 768, "fwd"),
+    ("fc_fwd", 8192, 3072, 768, "fwd"),
+    ("mlpproj_fwd", 8192, 768, 3072, "fwd"),
+    ("lmhead_fwd", 8192, 50304, 768, "fwd"),
+    ("fc_dgrad", 8192, 768, 3072, "dgrad"),  # dx[M,K=768] = dy[M,N=3072] @ W[3072,768]
+    ("fc_wgrad", 8192, 3072, 768, "wgrad"),  # dW[3072,768] = dy^T @ x
+    ("lmhead_dgrad", 8192, 768, 50304, "dgrad"),
+    ("lmhead_wgrad", 8192, 50304, 768, "wgrad"),
+    ("square_8192", 8192, 8192, 8192, "fwd"),
+]
+
+
+def bench_gemm(flush):
+    from . import gemm as g
+    from ._C import check_status
+
+    rows = []
+    for name, M, N, K, kind in GEMM_SHAPES:
+        torch.manual_seed(0)
+        if kind == "fwd":
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ours = lambda: g.gemm(x, w, out, N, g.EPI_BF16, False, False)
+            ref = lambda: torch.matmul(x, w.t())
+            flops = 2.0 * M * N * K
+        elif kind == "dgrad":
+            # output [M, N] from dy [M, K] and W [K, N]
+            dy = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            w = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
+            out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+            ours = lambda: g.gemm(dy, w, out, N, g.EPI_BF16, False, True)
+            ref = lambda: torch.matmul(dy, w)
+            flops = 2.0 * M * N * K
+        else:
+            dy = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            out = torch.zeros(N, K, device="cuda", dtype=torch.float32)
+            ours = lambda: g.gemm(dy, x, out, K, g.EPI_F32_ACC, True, True)
+            ref = lambda: torch.matmul(dy.t(), x)
+            flops = 2.0 * M * N * K
+        t_ours = time_fn(ours, flush=flush)
+        check_status()
+        t_ref = time_fn(ref, flush=flush)
+        rows.append(dict(op="gemm", name=name, M=M, N=N, K=K, kind=kind, ms=t_ours, ref_ms=t_ref,
+                         tflops=flops / t_ours / 1e9, ref_tflops=flops / t_ref / 1e9))
+    return rows
+
+
+def main(argv=None):
+    ap = argparse.ArgumentParser()
+    ap.add_argument("--only", default=None)
+    ap.add_argument("--json", default=None)
+    args = ap.parse_args(argv)
+    flush = _flush_buf()
+    rows = []
+    if args.only in (None, "gemm"):
+        rows += bench_gemm(flush)
+    extra = globals().get("EXTRA_BENCHES", {})
+    for k, fn in extra.items():
+        if args.only in (None, k):
+            rows += fn(flush)
+    for r in rows:
+        print(json.dumps(r))
+    if args.json:
+        with open(args.json, "w") as f:
+            json.dump(rows, f, indent=1)
+
+
+if __name__ == "__main__":
+    main()
