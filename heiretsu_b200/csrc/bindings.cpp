@@ -9,4 +9,19 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("gemm", &hb::gemm, "tcgen05 GEMM with fused epilogue", py::arg("a"), py::arg("b"), py::arg("c"),
         py::arg("N"), py::arg("epi"), py::arg("a_mn"), py::arg("b_mn"), py::arg("bias") = py::none(),
         py::arg("aux") = py::none(), py::arg("resid") = py::none(), py::arg("block_n") = 128);
+  m.def("layernorm_fwd", &hb::layernorm_fwd);
+  m.def("layernorm_bwd_scratch_rows", &hb::layernorm_bwd_scratch_rows);
+  m.def("layernorm_bwd", &hb::layernorm_bwd);
+  m.def("colsum_bf16", &hb::colsum_bf16);
+  m.def("cross_entropy_fwd", &hb::cross_entropy_fwd);
+  m.def("cross_entropy_bwd", &hb::cross_entropy_bwd);
+  m.def("embedding_fwd", &hb::embedding_fwd);
+  m.def("embedding_bwd", &hb::embedding_bwd);
+  m.def("sumsq_scratch_size", &hb::sumsq_scratch_size);
+  m.def("sumsq", &hb::sumsq);
+  m.def("clip_coef", &hb::clip_coef);
+  m.def("adamw_step", &hb::adamw_step);
+  m.def("f32_to_bf16", &hb::f32_to_bf16);
+  m.def("attention_fwd", &hb::attention_fwd);
+  m.def("attention_bwd", &hb::attention_bwd);
 }

@@ -1,0 +1,157 @@
+// Softmax cross-entropy over the vocabulary and the MoE aux-loss reduction.
+//
+// Replaces F.cross_entropy on materialised fp32 logits (reference
+// gpt_model.py:284-287, pipeline.py:139-142). The logits stay in bf16 (written
+// by the lm_head GEMM, row stride Vp >= V, a multiple of 8):
+//   forward   per row: lse = log sum_j exp(l_j) over j < V; loss = lse - l_t
+//   backward  in place: l_j <- (softmax_j - [j == t]) * scale (0 for j >= V)
+// Targets equal to `ignore_index` contribute no loss and a zero gradient row.
+#include <cuda_bf16.h>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace hb {
+
+template <int THREADS>
+__device__ __forceinline__ float block_reduce_max(float v, float* sh) {
+  v = warp_max(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < THREADS / 32) ? sh[l] : -INFINITY;
+    v = warp_max(v);
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  v = sh[0];
+  __syncthreads();
+  return v;
+}
+
+template <int THREADS>
+__device__ __forceinline__ float block_reduce_sum(float v, float* sh) {
+  v = warp_sum(v);
+  const int w = threadIdx.x >> 5, l = threadIdx.x & 31;
+  if (l == 0) sh[w] = v;
+  __syncthreads();
+  if (w == 0) {
+    v = (l < THREADS / 32) ? sh[l] : 0.f;
+    v = warp_sum(v);
+    if (l == 0) sh[0] = v;
+  }
+  __syncthreads();
+  v = sh[0];
+  __syncthreads();
+  return v;
+}
+
+constexpr int CE_THREADS = 512;
+
+// One CTA per row. Online (max, sum-exp) per thread over 8-element chunks.
+__global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16* __restrict__ logits, long ld, int V,
+                                                            const int64_t* __restrict__ targets, int ignore_index,
+                                                            float* __restrict__ lse_out,
+                                                            float* __restrict__ loss_rows) {
+  __shared__ float sh[32];
+  const long row = blockIdx.x;
+  const __nv_bfloat16* lr = logits + row * ld;
+  float m = -INFINITY, s = 0.f;
+  const int nchunk = V >> 3;  // full 8-wide chunks
+  for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float v[8];
+    float cm = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[q] = __bfloat162float(e[q]);
+      cm = fmaxf(cm, v[q]);
+    }
+    const float nm = fmaxf(m, cm);
+    float acc = s * __expf(m - nm);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc += __expf(v[q] - nm);
+    m = nm;
+    s = acc;
+  }
+  for (int j = nchunk * 8 + threadIdx.x; j < V; j += CE_THREADS) {
+    const float v = __bfloat162float(lr[j]);
+    const float nm = fmaxf(m, v);
+    s = s * __expf(m - nm) + __expf(v - nm);
+    m = nm;
+  }
+  const float gm = block_reduce_max<CE_THREADS>(m, sh);
+  const float gs = block_reduce_sum<CE_THREADS>((m == -INFINITY) ? 0.f : s * __expf(m - gm), sh);
+  if (threadIdx.x == 0) {
+    const float lse = gm + __logf(gs);
+    lse_out[row] = lse;
+    const int64_t t = targets[row];
+    loss_rows[row] = (t == ignore_index) ? 0.f : lse - __bfloat162float(lr[t]);
+  }
+}
+
+// In-place gradient: l_j <- (exp(l_j - lse) - [j == t]) * scale; j in [V, Vp) -> 0.
+__global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, long ld, int V,
+                                                            int Vp, const int64_t* __restrict__ targets,
+                                                            int ignore_index, const float* __restrict__ lse_in,
+                                                            const float* __restrict__ scale_ptr, float scale_mul) {
+  const long row = blockIdx.x;
+  __nv_bfloat16* lr = logits + row * ld;
+  const int64_t t = targets[row];
+  const float scale = (t == ignore_index) ? 0.f : scale_mul * (scale_ptr ? *scale_ptr : 1.f);
+  const float lse = lse_in[row];
+  const int nchunk = Vp >> 3;
+  for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
+    uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float g[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = c * 8 + q;
+      g[q] = (j < V) ? (__expf(__bfloat162float(e[q]) - lse) - (j == t ? 1.f : 0.f)) * scale : 0.f;
+    }
+    *reinterpret_cast<uint4*>(lr + c * 8) =
+        make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+  }
+}
+
+// out[0] (+)= mean over rows of loss_rows (rows with ignore_index excluded from the count).
+__global__ void __launch_bounds__(1024) mean_loss_kernel(const float* __restrict__ loss_rows,
+                                                         const int64_t* __restrict__ targets, int M,
+                                                         int ignore_index, float* __restrict__ out,
+                                                         float* __restrict__ count_out) {
+  __shared__ float sh[32];
+  float s = 0.f, n = 0.f;
+  for (int i = threadIdx.x; i < M; i += 1024) {
+    s += loss_rows[i];
+    n += (targets[i] == ignore_index) ? 0.f : 1.f;
+  }
+  s = block_reduce_sum<1024>(s, sh);
+  n = block_reduce_sum<1024>(n, sh);
+  if (threadIdx.x == 0) {
+    out[0] = s / fmaxf(n, 1.f);
+    if (count_out) count_out[0] = n;
+  }
+}
+
+void ce_fwd_launch(const __nv_bfloat16* logits, long ld, int M, int V, const int64_t* targets, int ignore_index,
+                   float* lse, float* loss_rows, float* loss_mean, float* count, cudaStream_t s) {
+  if (ld % 8 != 0) throw std::runtime_error("cross_entropy: logits row stride must be a multiple of 8");
+  if (M == 0) return;
+  ce_fwd_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, targets, ignore_index, lse, loss_rows);
+  HB_CUDA_CHECK(cudaGetLastError());
+  mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, count);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_bwd_launch(__nv_bfloat16* logits, long ld, int M, int V, int Vp, const int64_t* targets, int ignore_index,
+                   const float* lse, const float* scale_ptr, float scale_mul, cudaStream_t s) {
+  if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
+  if (M == 0) return;
+  ce_bwd_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets, ignore_index, lse, scale_ptr, scale_mul);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace hb

@@ -8,4 +8,28 @@ int64_t read_and_clear_status(int64_t device);
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, int64_t epi, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux,
           const c10::optional<at::Tensor>& resid, int64_t block_n);
+
+void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, at::Tensor& y, at::Tensor& mean,
+                   at::Tensor& rstd, double eps);
+int64_t layernorm_bwd_scratch_rows(int64_t M);
+void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
+                   const at::Tensor& w, const at::Tensor& dres_in, at::Tensor& dres, at::Tensor& dres16,
+                   at::Tensor& scratch, at::Tensor& dgamma, at::Tensor& dbeta);
+void colsum_bf16(const at::Tensor& x, at::Tensor& out);
+void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                       at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean);
+void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                       const at::Tensor& lse, const c10::optional<at::Tensor>& scale, double scale_mul);
+void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const at::Tensor& wpe, at::Tensor& out);
+void embedding_bwd(const at::Tensor& idx, const at::Tensor& dx, const c10::optional<at::Tensor>& dwte,
+                   const c10::optional<at::Tensor>& dwpe);
+int64_t sumsq_scratch_size();
+void sumsq(const at::Tensor& x, at::Tensor& scratch, double weight, at::Tensor& out, bool accumulate);
+void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm);
+void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& p16, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
+void f32_to_bf16(const at::Tensor& x, at::Tensor& y);
+void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse);
+void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
+                   int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv);
 }  // namespace hb

@@ -1,0 +1,231 @@
+// Torch-facing entry points of the non-GEMM kernels: argument validation,
+// stream selection, then a call into the raw launchers in the .cu files.
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+
+#include <initializer_list>
+
+#include "host_utils.h"
+#include "ops.h"
+
+namespace hb {
+
+// launchers (norm.cu, loss.cu, embed_optim.cu, attention.cu)
+void ln_fwd_launch(const float*, const float*, const float*, __nv_bfloat16*, float*, float*, int, int, float,
+                   cudaStream_t);
+int ln_bwd_num_ctas(int M, int device);
+void ln_bwd_launch(const float*, const float*, const float*, const float*, const float*, const float*, float*,
+                   __nv_bfloat16*, float*, int, float*, float*, int, int, cudaStream_t);
+void colsum_bf16_launch(const __nv_bfloat16*, long, int, int, float*, cudaStream_t);
+void ce_fwd_launch(const __nv_bfloat16*, long, int, int, const int64_t*, int, float*, float*, float*, float*,
+                   cudaStream_t);
+void ce_bwd_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, const float*, const float*, float,
+                   cudaStream_t);
+void embed_fwd_launch(const int64_t*, const float*, const float*, float*, int, int, int, cudaStream_t);
+void embed_bwd_launch(const int64_t*, const float*, float*, float*, int, int, int, cudaStream_t);
+int sumsq_num_parts(int device);
+void sumsq_launch(const float*, long, float*, int, float, float*, bool, cudaStream_t);
+void clip_coef_launch(const float*, float, float*, float*, cudaStream_t);
+void adamw_launch(float*, const float*, float*, float*, __nv_bfloat16*, long, const void*, const float*,
+                  cudaStream_t);
+void f32_to_bf16_launch(const float*, __nv_bfloat16*, long, cudaStream_t);
+void attn_fwd_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int, int*,
+                     cudaStream_t);
+void attn_bwd_launch(const __nv_bfloat16*, long, const __nv_bfloat16*, long, const __nv_bfloat16*, long,
+                     const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, int*, cudaStream_t);
+
+#define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
+#define CHECK_DT(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has the wrong dtype")
+#define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
+#define CHECK_ROWS(t) TORCH_CHECK((t).dim() == 2 && (t).stride(1) == 1, #t " must be 2-D with contiguous rows")
+
+static cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
+template <typename T>
+static T* ptr(const at::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+
+void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, at::Tensor& y, at::Tensor& mean,
+                   at::Tensor& rstd, double eps) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, at::kFloat);
+  CHECK_CONTIG(x);
+  CHECK_DT(w, at::kFloat);
+  CHECK_DT(b, at::kFloat);
+  CHECK_DT(y, at::kBFloat16);
+  CHECK_CONTIG(y);
+  c10::cuda::CUDAGuard g(x.device());
+  const int H = x.size(-1);
+  const int M = x.numel() / H;
+  ln_fwd_launch(ptr<float>(x), ptr<float>(w), ptr<float>(b), ptr<__nv_bfloat16>(y), ptr<float>(mean),
+                ptr<float>(rstd), M, H, static_cast<float>(eps), stream());
+}
+
+int64_t layernorm_bwd_scratch_rows(int64_t M) { return ln_bwd_num_ctas(static_cast<int>(M), current_device()); }
+
+void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
+                   const at::Tensor& w, const at::Tensor& dres_in, at::Tensor& dres, at::Tensor& dres16,
+                   at::Tensor& scratch, at::Tensor& dgamma, at::Tensor& dbeta) {
+  CHECK_CUDA(dy);
+  CHECK_DT(dy, at::kFloat);
+  CHECK_CONTIG(dy);
+  CHECK_DT(x, at::kFloat);
+  CHECK_CONTIG(x);
+  CHECK_DT(dres, at::kFloat);
+  CHECK_CONTIG(dres);
+  CHECK_DT(dres_in, at::kFloat);
+  CHECK_CONTIG(dres_in);
+  CHECK_DT(dres16, at::kBFloat16);
+  CHECK_CONTIG(dres16);
+  CHECK_DT(scratch, at::kFloat);
+  c10::cuda::CUDAGuard g(x.device());
+  const int H = x.size(-1);
+  const int M = x.numel() / H;
+  const int ctas = ln_bwd_num_ctas(M, x.get_device());
+  TORCH_CHECK(scratch.numel() >= (int64_t)ctas * 2 * H, "layernorm_bwd: scratch too small");
+  ln_bwd_launch(ptr<float>(dy), ptr<float>(x), ptr<float>(mean), ptr<float>(rstd), ptr<float>(w),
+                ptr<float>(dres_in), ptr<float>(dres), ptr<__nv_bfloat16>(dres16), ptr<float>(scratch), ctas,
+                ptr<float>(dgamma), ptr<float>(dbeta), M, H, stream());
+}
+
+void colsum_bf16(const at::Tensor& x, at::Tensor& out) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, at::kBFloat16);
+  CHECK_ROWS(x);
+  CHECK_DT(out, at::kFloat);
+  TORCH_CHECK(x.size(1) % 2 == 0 && x.stride(0) % 2 == 0, "colsum_bf16: even column count required");
+  c10::cuda::CUDAGuard g(x.device());
+  colsum_bf16_launch(ptr<__nv_bfloat16>(x), x.stride(0), x.size(0), x.size(1), ptr<float>(out), stream());
+}
+
+void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                       at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean) {
+  CHECK_CUDA(logits);
+  CHECK_DT(logits, at::kBFloat16);
+  CHECK_ROWS(logits);
+  CHECK_DT(targets, at::kLong);
+  CHECK_CONTIG(targets);
+  c10::cuda::CUDAGuard g(logits.device());
+  ce_fwd_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, ptr<int64_t>(targets),
+                ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), nullptr, stream());
+}
+
+void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                       const at::Tensor& lse, const c10::optional<at::Tensor>& scale, double scale_mul) {
+  CHECK_CUDA(logits);
+  CHECK_DT(logits, at::kBFloat16);
+  CHECK_ROWS(logits);
+  c10::cuda::CUDAGuard g(logits.device());
+  const float* sp = (scale && scale->defined()) ? ptr<float>(*scale) : nullptr;
+  ce_bwd_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, logits.size(1),
+                ptr<int64_t>(targets), ignore_index, ptr<float>(lse), sp, static_cast<float>(scale_mul), stream());
+}
+
+void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const at::Tensor& wpe, at::Tensor& out) {
+  CHECK_CUDA(idx);
+  CHECK_DT(idx, at::kLong);
+  CHECK_CONTIG(idx);
+  CHECK_DT(wte, at::kFloat);
+  CHECK_CONTIG(wte);
+  CHECK_DT(wpe, at::kFloat);
+  CHECK_CONTIG(wpe);
+  CHECK_CONTIG(out);
+  c10::cuda::CUDAGuard g(idx.device());
+  embed_fwd_launch(ptr<int64_t>(idx), ptr<float>(wte), ptr<float>(wpe), ptr<float>(out), idx.size(0), idx.size(1),
+                   wte.size(1), stream());
+}
+
+void embedding_bwd(const at::Tensor& idx, const at::Tensor& dx, const c10::optional<at::Tensor>& dwte,
+                   const c10::optional<at::Tensor>& dwpe) {
+  CHECK_CUDA(dx);
+  CHECK_DT(dx, at::kFloat);
+  CHECK_CONTIG(dx);
+  c10::cuda::CUDAGuard g(dx.device());
+  const int H = dx.size(-1);
+  embed_bwd_launch(ptr<int64_t>(idx), ptr<float>(dx), (dwte && dwte->defined()) ? ptr<float>(*dwte) : nullptr,
+                   (dwpe && dwpe->defined()) ? ptr<float>(*dwpe) : nullptr, idx.size(0), idx.size(1), H, stream());
+}
+
+int64_t sumsq_scratch_size() { return sumsq_num_parts(current_device()); }
+
+void sumsq(const at::Tensor& x, at::Tensor& scratch, double weight, at::Tensor& out, bool accumulate) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, at::kFloat);
+  CHECK_CONTIG(x);
+  c10::cuda::CUDAGuard g(x.device());
+  const int parts = sumsq_num_parts(x.get_device());
+  TORCH_CHECK(scratch.numel() >= parts, "sumsq: scratch too small");
+  sumsq_launch(ptr<float>(x), x.numel(), ptr<float>(scratch), parts, static_cast<float>(weight), ptr<float>(out),
+               accumulate, stream());
+}
+
+void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm) {
+  c10::cuda::CUDAGuard g(norm2.device());
+  clip_coef_launch(ptr<float>(norm2), static_cast<float>(max_norm), ptr<float>(coef),
+                   (norm && norm->defined()) ? ptr<float>(*norm) : nullptr, stream());
+}
+
+void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
+                const c10::optional<at::Tensor>& p16, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef) {
+  CHECK_CUDA(p);
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&p, &grad, &m, &v}) {
+    TORCH_CHECK(t->scalar_type() == at::kFloat && t->is_contiguous() && t->numel() == p.numel(),
+                "adamw_step: p, grad, m, v must be contiguous fp32 of equal size");
+  }
+  TORCH_CHECK(hyper.scalar_type() == at::kFloat && hyper.numel() >= 8 && hyper.is_cuda(), "adamw_step: hyper");
+  c10::cuda::CUDAGuard g(p.device());
+  __nv_bfloat16* p16p = nullptr;
+  if (p16 && p16->defined()) {
+    TORCH_CHECK(p16->scalar_type() == at::kBFloat16 && p16->numel() == p.numel() && p16->is_contiguous(), "p16");
+    p16p = ptr<__nv_bfloat16>(*p16);
+  }
+  adamw_launch(ptr<float>(p), ptr<float>(grad), ptr<float>(m), ptr<float>(v), p16p, p.numel(), hyper.data_ptr(),
+               (coef && coef->defined()) ? ptr<float>(*coef) : nullptr, stream());
+}
+
+void f32_to_bf16(const at::Tensor& x, at::Tensor& y) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, at::kFloat);
+  CHECK_CONTIG(x);
+  CHECK_DT(y, at::kBFloat16);
+  CHECK_CONTIG(y);
+  TORCH_CHECK(x.numel() == y.numel(), "f32_to_bf16: size mismatch");
+  c10::cuda::CUDAGuard g(x.device());
+  f32_to_bf16_launch(ptr<float>(x), ptr<__nv_bfloat16>(y), x.numel(), stream());
+}
+
+void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse) {
+  CHECK_CUDA(qkv);
+  CHECK_DT(qkv, at::kBFloat16);
+  CHECK_ROWS(qkv);
+  CHECK_DT(out, at::kBFloat16);
+  CHECK_ROWS(out);
+  TORCH_CHECK(qkv.size(0) == B * T && qkv.size(1) == 3 * nh * 64, "attention_fwd: qkv must be [B*T, 3*nh*64]");
+  TORCH_CHECK(qkv.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "attention_fwd: row strides must be 16B multiples");
+  const int64_t Tpad = (T + 127) / 128 * 128;
+  TORCH_CHECK(lse.numel() >= B * nh * Tpad && lse.scalar_type() == at::kFloat, "attention_fwd: lse [B, nh, Tpad]");
+  c10::cuda::CUDAGuard g(qkv.device());
+  attn_fwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<float>(lse), B,
+                  T, nh, Tpad, device_status_ptr(qkv.get_device()), stream());
+}
+
+void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
+                   int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv) {
+  CHECK_CUDA(qkv);
+  for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&qkv, &out, &dout, &dqkv}) {
+    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 && t->stride(0) % 8 == 0,
+                "attention_bwd: bf16 2-D tensors with 16B-aligned rows expected");
+  }
+  const int64_t Tpad = (T + 127) / 128 * 128;
+  TORCH_CHECK(dvec.numel() >= B * nh * Tpad && lse.numel() >= B * nh * Tpad, "attention_bwd: lse/dvec size");
+  TORCH_CHECK(dq_acc.numel() >= B * T * nh * 64 && dq_acc.scalar_type() == at::kFloat, "attention_bwd: dq_acc");
+  c10::cuda::CUDAGuard g(qkv.device());
+  attn_bwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0),
+                  ptr<__nv_bfloat16>(dout), dout.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc),
+                  ptr<__nv_bfloat16>(dqkv), dqkv.stride(0), B, T, nh, Tpad, device_status_ptr(qkv.get_device()),
+                  stream());
+}
+
+}  // namespace hb

@@ -1,0 +1,228 @@
+"""Fused sm_100a execution of the GPT model (forward and backward).
+
+The model is executed as three autograd functions:
+
+* ``_Embed``  idx -> x0 = wte[idx] + wpe[t]                (fp32 residual stream)
+* ``_Body``   x0 -> x_L through every block, explicit backward
+* ``_Head``   x_L -> ln_f -> lm_head -> cross-entropy        (loss, fused bwd)
+
+Inside ``_Body`` each dense block runs 6 kernels forward:
+
+    LN1 -> QKV GEMM(+bias) -> flash attention -> proj GEMM(+bias+residual)
+    LN2 -> FC GEMM(+bias, GELU; pre-activation kept) -> proj GEMM(+bias+residual)
+
+and the mirror image backward (dgrad GEMMs with the GELU derivative fused
+into the epilogue, wgrad GEMMs accumulating straight into the fp32 gradient
+buffer, LayerNorm backward updating the residual gradient in place). Weights
+are read through their bf16 shadows (``p.w16``); gradients are written to
+``p.main_grad`` (see heiretsu_b200/parallel/flat.py), so autograd never
+allocates or adds parameter gradients.
+
+Numerics: bf16 operands, fp32 accumulation, fp32 residual stream and fp32
+LayerNorm statistics -- the same precision split as the reference under
+``torch.autocast(bf16)`` (gemm in bf16, bias add / LN / residual in fp32).
+"""
+from __future__ import annotations
+
+from typing import List, Optional, Tuple
+
+import torch
+
+from ..ops import gemm as G
+from ..ops import kernels as K
+
+LN_EPS = 1e-5
+
+
+def fused_supported(cfg, topo=None) -> Tuple[bool, str]:
+    """Whether the fused path covers this configuration (else the plain path runs)."""
+    if cfg.n_embed % cfg.n_head or cfg.n_embed // cfg.n_head != 64:
+        return False, "fused attention needs head_dim == 64"
+    if cfg.n_embed % 128:
+        return False, "fused path needs n_embed % 128 == 0"
+    if cfg.dropout > 0:
+        return False, "fused path runs without dropout (dropout > 0 uses the plain path)"
+    if cfg.num_experts > 0:
+        return False, "MoE blocks use the plain path"
+    if topo is not None and getattr(topo, "tp", 1) > 1:
+        return False, "tensor parallelism uses the plain path"
+    return True, ""
+
+
+def _vpad(V: int) -> int:
+    return (V + 127) // 128 * 128
+
+
+# ---------------------------------------------------------------------------
+class _Embed(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, idx, wte, wpe):
+        ctx.save_for_backward(idx)
+        ctx.wte, ctx.wpe = wte, wpe
+        return K.embedding_fwd(idx, wte.detach(), wpe.detach())
+
+    @staticmethod
+    def backward(ctx, dx):
+        (idx,) = ctx.saved_tensors
+        K.embedding_bwd(idx, dx.contiguous(), ctx.wte.main_grad, ctx.wpe.main_grad)
+        return None, None, None
+
+
+def embed_fused(wte: torch.nn.Parameter, wpe: torch.nn.Parameter, idx: torch.Tensor) -> torch.Tensor:
+    B, T = idx.shape
+    return _Embed.apply(idx.contiguous(), wte, wpe).view(B, T, -1)
+
+
+# ---------------------------------------------------------------------------
+def _dense_block_fwd(blk, x: torch.Tensor, B: int, T: int, keep: bool):
+    """x fp32 [M, H] -> x2 fp32 [M, H] (new tensor); returns (x2, saved activations)."""
+    attn, mlp = blk.attn, blk.mlp
+    nh = attn.nh_tp
+    xn, m1, r1 = K.layernorm_fwd(x, blk.ln_1.weight, blk.ln_1.bias, LN_EPS)
+    qkv = G.linear_fwd(xn, attn.c_attn.weight.w16, attn.c_attn.bias)
+    y, lse = K.attention_fwd(qkv, B, T, nh)
+    x1 = G.linear_fwd_resid(y, attn.c_proj.weight.w16, attn.c_proj.bias, x)
+    xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
+    h, pre = G.linear_fwd_gelu(xn2, mlp.c_fc.weight.w16, mlp.c_fc.bias)
+    x2 = G.linear_fwd_resid(h, mlp.c_proj.weight.w16, mlp.c_proj.bias, x1)
+    saved = (x, xn, m1, r1, qkv, y, lse, x1, xn2, m2, r2, pre, h) if keep else None
+    return x2, saved
+
+
+def _dense_block_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: int, T: int, ws: dict):
+    """In place: dres (fp32) / dres16 (bf16) go from d(x2) to d(x)."""
+    attn, mlp = blk.attn, blk.mlp
+    nh = attn.nh_tp
+    x, xn, m1, r1, qkv, y, lse, x1, xn2, m2, r2, pre, h = saved
+    # MLP sub-layer: x2 = x1 + c_proj(gelu(c_fc(ln_2(x1))))
+    dpre = G.linear_dgrad(dres16, mlp.c_proj.weight.w16, gelu_pre=pre)
+    G.linear_wgrad(dres16, h, out=mlp.c_proj.weight.main_grad, accumulate=True)
+    K.colsum_bf16(dres16, mlp.c_proj.bias.main_grad)
+    dxn2 = G.linear_dgrad(dpre, mlp.c_fc.weight.w16, f32=True)
+    G.linear_wgrad(dpre, xn2, out=mlp.c_fc.weight.main_grad, accumulate=True)
+    K.colsum_bf16(dpre, mlp.c_fc.bias.main_grad)
+    del dpre
+    K.layernorm_bwd(dxn2, x1, m2, r2, blk.ln_2.weight, dres, dres, dres16, blk.ln_2.weight.main_grad,
+                    blk.ln_2.bias.main_grad, scratch=ws["ln_scratch"])
+    del dxn2
+    # attention sub-layer: x1 = x + c_proj(attn(c_attn(ln_1(x))))
+    dy = G.linear_dgrad(dres16, attn.c_proj.weight.w16)
+    G.linear_wgrad(dres16, y, out=attn.c_proj.weight.main_grad, accumulate=True)
+    K.colsum_bf16(dres16, attn.c_proj.bias.main_grad)
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, nh)
+    del dy
+    G.linear_wgrad(dqkv, xn, out=attn.c_attn.weight.main_grad, accumulate=True)
+    K.colsum_bf16(dqkv, attn.c_attn.bias.main_grad)
+    dxn = G.linear_dgrad(dqkv, attn.c_attn.weight.w16, f32=True)
+    del dqkv
+    K.layernorm_bwd(dxn, x, m1, r1, blk.ln_1.weight, dres, dres, dres16, blk.ln_1.weight.main_grad,
+                    blk.ln_1.bias.main_grad, scratch=ws["ln_scratch"])
+
+
+def _ln_scratch(M: int, H: int, device) -> torch.Tensor:
+    from ..ops._C import load
+    rows = load().layernorm_bwd_scratch_rows(M)
+    return torch.empty(rows * 2 * H, device=device, dtype=torch.float32)
+
+
+class _Body(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, blocks, B, T):
+        keep = torch.is_grad_enabled() or x.requires_grad
+        saved: List = []
+        for blk in blocks:
+            x, s = _dense_block_fwd(blk, x, B, T, keep)
+            saved.append(s)
+        ctx.blocks, ctx.saved, ctx.B, ctx.T = blocks, saved, B, T
+        return x
+
+    @staticmethod
+    def backward(ctx, dx):
+        B, T = ctx.B, ctx.T
+        dres = dx.contiguous().clone()
+        dres16 = K.f32_to_bf16(dres)
+        M, H = dres.shape
+        ws = {"ln_scratch": _ln_scratch(M, H, dres.device)}
+        for blk, s in zip(reversed(ctx.blocks), reversed(ctx.saved)):
+            _dense_block_bwd(blk, s, dres, dres16, B, T, ws)
+        ctx.saved = None
+        return dres, None, None, None
+
+
+def blocks_fused(blocks, x: torch.Tensor, cfg) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Run a list of dense blocks on x [B, T, H] (any float dtype); returns (fp32 x, aux=0)."""
+    B, T, H = x.shape
+    x2 = x.reshape(B * T, H)
+    if x2.dtype != torch.float32:
+        x2 = x2.float()
+    out = _Body.apply(x2.contiguous(), list(blocks), B, T)
+    return out.view(B, T, H), torch.zeros((), device=x.device, dtype=torch.float32)
+
+
+# ---------------------------------------------------------------------------
+class _Head(torch.autograd.Function):
+    @staticmethod
+    def forward(ctx, x, ln_w, ln_b, wte, targets, V, want_logits):
+        M, H = x.shape
+        Vp = _vpad(V)
+        xn, mean, rstd = K.layernorm_fwd(x, ln_w, ln_b, LN_EPS)
+        logits = torch.empty(M, Vp, device=x.device, dtype=torch.bfloat16)
+        G.gemm(xn, wte.w16, logits, Vp, G.EPI_BF16, False, False)
+        logits_out = logits[:, :V].float() if want_logits else None
+        if targets is None:
+            ctx.mark_non_differentiable(logits_out) if logits_out is not None else None
+            return torch.zeros((), device=x.device), logits_out
+        loss, lse, _ = K.cross_entropy_fwd(logits, V, targets)
+        ctx.save_for_backward(x, xn, mean, rstd, logits, lse, targets)
+        ctx.ln_w, ctx.ln_b, ctx.wte, ctx.V = ln_w, ln_b, wte, V
+        if logits_out is not None:
+            ctx.mark_non_differentiable(logits_out)
+        return loss, logits_out
+
+    @staticmethod
+    def backward(ctx, dloss, _dlogits):
+        x, xn, mean, rstd, logits, lse, targets = ctx.saved_tensors
+        V = ctx.V
+        M, H = x.shape
+        dl = K.cross_entropy_bwd_(logits, V, targets, lse, dloss.reshape(1).float().contiguous(), 1.0 / M)
+        dlv = dl[:, :V]
+        dxn = G.linear_dgrad(dlv, ctx.wte.w16, f32=True)
+        G.linear_wgrad(dl, xn, out=ctx.wte.main_grad, accumulate=True, n_rows=V)
+        dx = torch.empty_like(x)
+        dx16 = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+        zero = torch.zeros_like(x)
+        K.layernorm_bwd(dxn, x, mean, rstd, ctx.ln_w, zero, dx, dx16, ctx.ln_w.main_grad, ctx.ln_b.main_grad)
+        return dx, None, None, None, None, None, None
+
+
+def head_fused(ln_f, wte: torch.nn.Parameter, x: torch.Tensor, targets: Optional[torch.Tensor], V: int,
+               want_logits: bool = True):
+    """ln_f -> lm_head (tied to wte) -> cross-entropy. Returns (logits fp32 | None, loss | None)."""
+    B, T, H = x.shape
+    x2 = x.reshape(B * T, H)
+    if x2.dtype != torch.float32:
+        x2 = x2.float()
+    t = targets.reshape(-1).contiguous() if targets is not None else None
+    loss, logits = _Head.apply(x2.contiguous(), ln_f.weight, ln_f.bias, wte, t, V, want_logits)
+    if logits is not None:
+        logits = logits.view(B, T, V)
+    return logits, (loss if targets is not None else None)
+
+
+def gpt_forward_fused(model, idx: torch.Tensor, targets: Optional[torch.Tensor], return_logits: bool = True):
+    cfg = model.cfg
+    x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx)
+    x, aux = blocks_fused(model.tr.h, x, cfg)
+    logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x, targets, cfg.vocab_size,
+                              want_logits=return_logits)
+    return logits, loss, aux
+
+
+def enable_fused(module: torch.nn.Module, cfg, topo=None) -> bool:
+    """Switch a GPT / StageModule to the fused path if the config is covered.
+
+    Requires parameters already flattened (``p.w16`` / ``p.main_grad``)."""
+    ok, why = fused_supported(cfg, topo)
+    if ok:
+        module.fused = True
+    return ok

@@ -1,0 +1,128 @@
+"""Thin Python wrappers over the extension's non-GEMM kernels.
+
+Every wrapper allocates its outputs (unless given) with the PyTorch caching
+allocator on the current stream and launches exactly one sm_100a kernel
+sequence; nothing here falls back to a PyTorch implementation.
+"""
+from __future__ import annotations
+
+from typing import Optional
+
+import torch
+
+from ._C import load
+
+
+def _ext():
+    return load()
+
+
+# ---------------------------------------------------------------------------
+# LayerNorm
+# ---------------------------------------------------------------------------
+def layernorm_fwd(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float = 1e-5):
+    """fp32 x [M, H] -> (bf16 y [M, H], mean [M], rstd [M])."""
+    M = x.numel() // x.shape[-1]
+    y = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+    mean = torch.empty(M, device=x.device, dtype=torch.float32)
+    rstd = torch.empty(M, device=x.device, dtype=torch.float32)
+    _ext().layernorm_fwd(x, w, b, y, mean, rstd, eps)
+    return y, mean, rstd
+
+
+def layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dgamma, dbeta, scratch=None):
+    """dres = dres_in + dLN/dx(dy); dres16 = bf16(dres); dgamma/dbeta (fp32) += partials."""
+    H = x.shape[-1]
+    M = x.numel() // H
+    if scratch is None:
+        rows = _ext().layernorm_bwd_scratch_rows(M)
+        scratch = torch.empty(rows * 2 * H, device=x.device, dtype=torch.float32)
+    _ext().layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, scratch, dgamma, dbeta)
+
+
+def colsum_bf16(x: torch.Tensor, out: torch.Tensor) -> None:
+    """out (fp32) += column sums of bf16 x [M, N]."""
+    _ext().colsum_bf16(x, out)
+
+
+# ---------------------------------------------------------------------------
+# Cross-entropy
+# ---------------------------------------------------------------------------
+def cross_entropy_fwd(logits: torch.Tensor, V: int, targets: torch.Tensor, ignore_index: int = -100):
+    """bf16 logits [M, Vp] -> (mean loss (0-d fp32), lse [M], per-row loss [M])."""
+    M = logits.shape[0]
+    lse = torch.empty(M, device=logits.device, dtype=torch.float32)
+    rows = torch.empty(M, device=logits.device, dtype=torch.float32)
+    mean = torch.empty((), device=logits.device, dtype=torch.float32)
+    _ext().cross_entropy_fwd(logits, V, targets, ignore_index, lse, rows, mean)
+    return mean, lse, rows
+
+
+def cross_entropy_bwd_(logits, V, targets, lse, scale: Optional[torch.Tensor], scale_mul: float,
+                       ignore_index: int = -100) -> torch.Tensor:
+    """In place: logits <- (softmax - onehot) * scale * scale_mul (columns >= V zeroed)."""
+    _ext().cross_entropy_bwd(logits, V, targets, ignore_index, lse, scale, scale_mul)
+    return logits
+
+
+# ---------------------------------------------------------------------------
+# Embedding
+# ---------------------------------------------------------------------------
+def embedding_fwd(idx: torch.Tensor, wte: torch.Tensor, wpe: torch.Tensor) -> torch.Tensor:
+    B, T = idx.shape
+    out = torch.empty(B * T, wte.shape[1], device=idx.device, dtype=torch.float32)
+    _ext().embedding_fwd(idx, wte, wpe, out)
+    return out
+
+
+def embedding_bwd(idx, dx, dwte: Optional[torch.Tensor], dwpe: Optional[torch.Tensor]) -> None:
+    _ext().embedding_bwd(idx, dx, dwte, dwpe)
+
+
+# ---------------------------------------------------------------------------
+# Optimizer pieces
+# ---------------------------------------------------------------------------
+def sumsq(x: torch.Tensor, out: torch.Tensor, weight: float = 1.0, accumulate: bool = False, scratch=None):
+    """out (0-d fp32) (+)= weight * sum(x^2), deterministic two-pass."""
+    if scratch is None:
+        scratch = torch.empty(_ext().sumsq_scratch_size(), device=x.device, dtype=torch.float32)
+    _ext().sumsq(x, scratch, weight, out, accumulate)
+
+
+def clip_coef(norm2: torch.Tensor, max_norm: float, coef: torch.Tensor, norm: Optional[torch.Tensor] = None):
+    _ext().clip_coef(norm2, max_norm, coef, norm)
+
+
+def adamw_step(p, grad, m, v, p16, hyper, coef=None):
+    _ext().adamw_step(p, grad, m, v, p16, hyper, coef)
+
+
+def f32_to_bf16(x: torch.Tensor, y: Optional[torch.Tensor] = None) -> torch.Tensor:
+    if y is None:
+        y = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+    _ext().f32_to_bf16(x, y)
+    return y
+
+
+# ---------------------------------------------------------------------------
+# Attention (head_dim 64, causal)
+# ---------------------------------------------------------------------------
+def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torch.Tensor] = None):
+    """qkv bf16 [B*T, 3*nh*64] -> (y bf16 [B*T, nh*64], lse fp32 [B, nh, Tpad])."""
+    Tpad = (T + 127) // 128 * 128
+    if out is None:
+        out = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.bfloat16)
+    lse = torch.empty(B, nh, Tpad, device=qkv.device, dtype=torch.float32)
+    _ext().attention_fwd(qkv, B, T, nh, out, lse)
+    return out, lse
+
+
+def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv: Optional[torch.Tensor] = None):
+    """Returns dqkv bf16 [B*T, 3*nh*64] (columns [dQ | dK | dV])."""
+    Tpad = (T + 127) // 128 * 128
+    if dqkv is None:
+        dqkv = torch.empty(B * T, 3 * nh * 64, device=qkv.device, dtype=torch.bfloat16)
+    dvec = torch.empty(B, nh, Tpad, device=qkv.device, dtype=torch.float32)
+    dq_acc = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.float32)
+    _ext().attention_bwd(qkv, out, dout, lse, B, T, nh, dvec, dq_acc, dqkv)
+    return dqkv

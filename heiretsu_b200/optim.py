@@ -1,0 +1,82 @@
+"""Fused AdamW with global-norm gradient clipping over a ``FlatParams`` buffer.
+
+Semantics follow torch.optim.AdamW (decoupled weight decay applied to every
+parameter, as the reference does: train.py:346-351) and
+torch.nn.utils.clip_grad_norm_ (train.py:446), except that the norm is the
+*global* norm over all model-parallel shards (each replicated parameter
+counted once) rather than each shard's local norm.
+
+One step = sum-of-squares reductions (one per replication class) ->
+optional all-reduce of the squared norm over the model-parallel group ->
+clip coefficient -> one AdamW kernel that also refreshes the bf16 GEMM
+shadow. No host synchronisation: the coefficient stays on the device, and a
+non-finite norm (fp16 overflow) skips the update inside the kernel.
+"""
+from __future__ import annotations
+
+import math
+from typing import Optional
+
+import torch
+import torch.distributed as dist
+
+from .ops import kernels as K
+from .parallel.flat import FlatParams
+
+
+class FusedAdamW:
+    def __init__(self, flat: FlatParams, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
+                 weight_decay: float = 0.1, max_grad_norm: float = 0.0, mp_group: Optional[dist.ProcessGroup] = None):
+        self.flat = flat
+        self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
+        self.max_grad_norm = max_grad_norm
+        self.mp_group = mp_group
+        dev = flat.device
+        self.m = torch.zeros_like(flat.data)
+        self.v = torch.zeros_like(flat.data)
+        self.step_count = 0
+        self.hyper = torch.zeros(8, device=dev, dtype=torch.float32)
+        self.norm2 = torch.zeros((), device=dev, dtype=torch.float32)
+        self.norm = torch.zeros((), device=dev, dtype=torch.float32)
+        self.coef = torch.ones((), device=dev, dtype=torch.float32)
+        self.grad_scale = 1.0
+        self.param_groups = [{"lr": lr}]  # logging compatibility with torch optimizers
+
+    def compute_grad_norm(self) -> torch.Tensor:
+        """Global L2 norm of the gradients (device tensor), each replicated parameter counted once."""
+        g = self.flat.grad
+        first = True
+        for start, end, wgt in self.flat.ranges:
+            if end > start:
+                K.sumsq(g[start:end], self.norm2, weight=wgt, accumulate=not first)
+                first = False
+        if first:
+            self.norm2.zero_()
+        if self.mp_group is not None and dist.is_initialized() and dist.get_world_size(self.mp_group) > 1:
+            dist.all_reduce(self.norm2, group=self.mp_group)
+        K.clip_coef(self.norm2, self.max_grad_norm, self.coef, self.norm)
+        return self.norm
+
+    def step(self) -> None:
+        self.step_count += 1
+        lr = self.param_groups[0]["lr"]
+        b1, b2 = self.betas
+        # A fresh pageable host tensor: the copy is staged before copy_ returns,
+        # so the host may run ahead without overwriting an in-flight source.
+        h = torch.tensor([lr, b1, b2, self.eps, self.wd, 1.0 - b1 ** self.step_count,
+                          math.sqrt(1.0 - b2 ** self.step_count), self.grad_scale], dtype=torch.float32)
+        self.hyper.copy_(h)
+        self.compute_grad_norm()
+        K.adamw_step(self.flat.data, self.flat.grad, self.m, self.v, self.flat.data16, self.hyper, self.coef)
+
+    def zero_grad(self, set_to_none: bool = True) -> None:
+        self.flat.zero_grad()
+
+    def state_dict(self) -> dict:
+        return {"m": self.m.cpu(), "v": self.v.cpu(), "step": self.step_count, "lr": self.param_groups[0]["lr"],
+                "betas": self.betas, "eps": self.eps, "weight_decay": self.wd, "names": list(self.flat.names)}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.m.copy_(sd["m"].to(self.m.device))
+        self.v.copy_(sd["v"].to(self.v.device))
+        self.step_count = int(sd["step"])

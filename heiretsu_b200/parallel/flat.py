@@ -1,0 +1,83 @@
+"""Flat parameter / gradient / bf16-shadow buffers.
+
+All parameters of a module are moved into one fp32 buffer (each parameter
+becomes a view, so ``state_dict`` and the module code are unchanged), with
+a matching fp32 gradient buffer (``p.main_grad``) and a bf16 shadow
+(``p.w16``) that the GEMMs read. One flat layout means one AdamW kernel, one
+gradient-norm reduction and large, contiguous DP reduction buckets.
+
+Parameters are grouped by how they are replicated across model-parallel
+ranks, so the global gradient norm is a handful of range reductions:
+``class_of(p)`` returns the factor by which a parameter's squared norm is
+counted too often when summed over the TP x EP ranks of one replica.
+"""
+from __future__ import annotations
+
+from typing import Callable, Dict, List, Optional, Tuple
+
+import torch
+
+ALIGN = 128  # elements: keeps every view 256-byte aligned in bf16 and 512 in fp32
+
+
+def _align(n: int) -> int:
+    return (n + ALIGN - 1) // ALIGN * ALIGN
+
+
+class FlatParams:
+    def __init__(self, module: torch.nn.Module, device: torch.device,
+                 weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None):
+        named: List[Tuple[str, torch.nn.Parameter]] = []
+        seen = set()
+        for name, p in module.named_parameters():
+            if id(p) in seen:
+                continue
+            seen.add(id(p))
+            named.append((name, p))
+        weight_of = weight_of or (lambda n, p: 1.0)
+        # Group by norm weight (stable within a group: module order).
+        groups: Dict[float, List[Tuple[str, torch.nn.Parameter]]] = {}
+        for name, p in named:
+            groups.setdefault(float(weight_of(name, p)), []).append((name, p))
+        self.ranges: List[Tuple[int, int, float]] = []  # (start, end, weight)
+        order: List[Tuple[str, torch.nn.Parameter]] = []
+        total = 0
+        for wgt in sorted(groups):
+            start = total
+            for name, p in groups[wgt]:
+                order.append((name, p))
+                total += _align(p.numel())
+            self.ranges.append((start, total, wgt))
+        self.numel = total
+        self.device = device
+        self.data = torch.zeros(total, device=device, dtype=torch.float32)
+        self.grad = torch.zeros(total, device=device, dtype=torch.float32)
+        self.data16 = torch.zeros(total, device=device, dtype=torch.bfloat16)
+        self.params: List[torch.nn.Parameter] = []
+        self.names: List[str] = []
+        self.offsets: List[int] = []
+        off = 0
+        with torch.no_grad():
+            for name, p in order:
+                n = p.numel()
+                view = self.data[off:off + n].view(p.shape)
+                view.copy_(p.data.to(device))
+                p.data = view
+                p.main_grad = self.grad[off:off + n].view(p.shape)
+                p.w16 = self.data16[off:off + n].view(p.shape)
+                self.params.append(p)
+                self.names.append(name)
+                self.offsets.append(off)
+                off += _align(n)
+        self.refresh_bf16()
+
+    def refresh_bf16(self) -> None:
+        """Re-derive the bf16 shadow from the fp32 master (after init / checkpoint load)."""
+        if self.device.type == "cuda":
+            from ..ops.kernels import f32_to_bf16
+            f32_to_bf16(self.data, self.data16)
+        else:
+            self.data16.copy_(self.data)
+
+    def zero_grad(self) -> None:
+        self.grad.zero_()

@@ -1,0 +1,255 @@
+"""GPipe pipeline parallelism (fill / drain) with NCCL point-to-point.
+
+Same stage partition, parameter names and schedule as the reference
+(pipeline.py:19-340): contiguous balanced layer ranges; the first stage owns
+``wte``/``wpe``, the last ``ln_f``/``lm_head`` (tied only when both live on
+the same stage); all M forwards, then all M backwards in reverse.
+
+Differences, all deliberate:
+
+* The activation boundary travels in one declared dtype on both sides
+  (``boundary_dtype``, default fp32 = the residual stream's dtype), so an AMP
+  run never sends fp32 bytes into a bf16 receive buffer.
+* Communication overlaps compute: the receive for microbatch m+1 is posted
+  before microbatch m is computed, sends are not waited for until the end of
+  the phase, and waits are stream waits (``Work.wait``), not host blocks.
+"""
+from __future__ import annotations
+
+from dataclasses import dataclass, field
+from typing import List, Optional, Tuple
+
+import torch
+import torch.distributed as dist
+import torch.nn as nn
+import torch.nn.functional as F
+
+from ..config import GPTConfig
+from ..topo import rank_from_coords
+
+
+def _partition_layers(n_layer: int, pp: int) -> List[Tuple[int, int]]:
+    """Balanced contiguous [start, end) layer ranges; earlier stages take the remainder."""
+    if pp <= 0:
+        raise ValueError("pp must be >= 1")
+    if pp > n_layer:
+        raise ValueError(f"pp {pp} > n_layer {n_layer} (would create empty stages)")
+    base, rem = divmod(n_layer, pp)
+    out, start = [], 0
+    for i in range(pp):
+        end = start + base + (1 if i < rem else 0)
+        out.append((start, end))
+        start = end
+    return out
+
+
+class StageModule(nn.Module):
+    """The blocks of one pipeline stage plus the embedding (first) and head (last)."""
+
+    def __init__(self, cfg: GPTConfig, topo, stage_idx: int, num_stages: int):
+        super().__init__()
+        from ..models.gpt import init_gpt_weights, make_block
+
+        self.cfg = cfg
+        self.stage_idx, self.num_stages = stage_idx, num_stages
+        self.is_first = stage_idx == 0
+        self.is_last = stage_idx == num_stages - 1
+        self.tp, self.tp_rank, self.tp_group = topo.tp, topo.tp_rank, topo.tp_group
+        self.ep = getattr(topo, "ep", 1)
+        self.ep_rank = getattr(topo, "ep_rank", 0)
+        self.ep_group = getattr(topo, "ep_group", None)
+        self.topo = topo
+        self.block_start, self.block_end = _partition_layers(cfg.n_layer, num_stages)[stage_idx]
+        self.blocks = nn.ModuleList([
+            make_block(cfg, i, self.tp_group, self.tp_rank, self.tp, self.ep_group, self.ep_rank, self.ep)
+            for i in range(self.block_start, self.block_end)])
+        if self.is_first:
+            self.wte = nn.Embedding(cfg.vocab_size, cfg.n_embed)
+            self.wpe = nn.Embedding(cfg.block_size, cfg.n_embed)
+        else:
+            self.wte = None
+            self.wpe = None
+        if self.is_last:
+            self.ln_f = nn.LayerNorm(cfg.n_embed)
+            self.lm_head = nn.Linear(cfg.n_embed, cfg.vocab_size, bias=False)
+        else:
+            self.ln_f = None
+            self.lm_head = None
+        if self.is_first and self.is_last:
+            self.wte.weight = self.lm_head.weight
+        init_gpt_weights(self, cfg.n_layer)
+        self.fused = False
+
+    def embed(self, idx: torch.Tensor) -> torch.Tensor:
+        B, T = idx.shape
+        if T > self.cfg.block_size:
+            raise ValueError(f"Sequence length {T} > block_size {self.cfg.block_size}")
+        if self.fused and idx.is_cuda:
+            from ..models.fused import embed_fused
+            return embed_fused(self.wte.weight, self.wpe.weight, idx)
+        return self.wte(idx) + self.wpe(torch.arange(T, device=idx.device))[None]
+
+    def forward_blocks(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        if self.fused and x.is_cuda:
+            from ..models.fused import blocks_fused
+            return blocks_fused(self.blocks, x, self.cfg)
+        aux = torch.zeros((), device=x.device, dtype=x.dtype)
+        for blk in self.blocks:
+            x, a = blk(x)
+            aux = aux + a
+        return x, aux
+
+    def forward_head(self, x: torch.Tensor, targets: Optional[torch.Tensor]):
+        if self.fused and x.is_cuda:
+            from ..models.fused import head_fused
+            return head_fused(self.ln_f, self.lm_head.weight, x, targets, self.cfg.vocab_size)
+        x = self.ln_f(x)
+        logits = self.lm_head(x)
+        loss = None
+        if targets is not None:
+            loss = F.cross_entropy(logits.reshape(-1, logits.size(-1)), targets.reshape(-1))
+        return logits, loss
+
+
+@dataclass
+class PipelineState:
+    boundaries: List[torch.Tensor] = field(default_factory=list)
+    recv_inputs: List[torch.Tensor] = field(default_factory=list)
+    losses: List[torch.Tensor] = field(default_factory=list)
+    aux_losses: List[torch.Tensor] = field(default_factory=list)
+
+
+class GPipeEngine:
+    """Fill/drain schedule over the stages of one pipeline group."""
+
+    def __init__(self, stage: StageModule, topo, boundary_dtype: torch.dtype = torch.float32):
+        self.stage, self.topo = stage, topo
+        self.pp_rank, self.pp_size = topo.pp_rank, topo.pp
+        self.is_first, self.is_last = stage.is_first, stage.is_last
+        self.boundary_dtype = boundary_dtype
+        self.prev_rank = self.next_rank = None
+        if self.pp_size > 1:
+            rc = lambda p: rank_from_coords(topo.dp_rank, topo.ep_rank, p, topo.tp_rank, topo.dp, topo.ep, topo.tp,
+                                            topo.pp)
+            if self.pp_rank > 0:
+                self.prev_rank = rc(self.pp_rank - 1)
+            if self.pp_rank < self.pp_size - 1:
+                self.next_rank = rc(self.pp_rank + 1)
+
+    # -- point-to-point -----------------------------------------------------
+    def _isend(self, t: torch.Tensor, peer: int, tag: int):
+        return dist.batch_isend_irecv([dist.P2POp(dist.isend, t.contiguous(), peer, tag=tag)])
+
+    def _irecv(self, t: torch.Tensor, peer: int, tag: int):
+        return dist.batch_isend_irecv([dist.P2POp(dist.irecv, t, peer, tag=tag)])
+
+    @staticmethod
+    def _wait(works) -> None:
+        for w in works:
+            w.wait()
+
+    def _fwd_tag(self, m: int) -> int:
+        return 1000 + m
+
+    def _bwd_tag(self, m: int) -> int:
+        return 2000 + m
+
+    def _recv_fwd(self, m: int, B: int, S: int, H: int, device):
+        buf = torch.empty((B, S, H), device=device, dtype=self.boundary_dtype)
+        return buf, self._irecv(buf, self.prev_rank, self._fwd_tag(m))
+
+    # -- schedule -------------------------------------------------------------
+    def _run_forward(self, loader, micro_batches, device, use_amp, amp_dtype, batch_size, state, keep_graph):
+        cfg = self.stage.cfg
+        B, S, H = batch_size, cfg.block_size, cfg.n_embed
+        pending_recv = self._recv_fwd(0, B, S, H, device) if not self.is_first else None
+        sends = []
+        for m in range(micro_batches):
+            idx, targets = loader.next_batch(device)
+            if not self.is_last:
+                targets = None
+            recv_x = None
+            if not self.is_first:
+                buf, works = pending_recv
+                self._wait(works)
+                if m + 1 < micro_batches:
+                    pending_recv = self._recv_fwd(m + 1, B, S, H, device)
+                recv_x = buf.to(torch.float32) if buf.dtype != torch.float32 else buf
+                if keep_graph:
+                    recv_x.requires_grad_(True)
+            ctx = torch.autocast(device_type=device.type, dtype=amp_dtype, enabled=use_amp and not self.stage.fused)
+            with ctx:
+                x = self.stage.embed(idx) if self.is_first else recv_x
+                x, aux = self.stage.forward_blocks(x)
+                loss = self.stage.forward_head(x, targets)[1] if self.is_last else None
+            if not self.is_last:
+                out = x.detach().to(self.boundary_dtype)
+                sends.append((out, self._isend(out, self.next_rank, self._fwd_tag(m))))
+                if keep_graph:
+                    state.boundaries.append(x)
+            if keep_graph and not self.is_first:
+                state.recv_inputs.append(recv_x)
+            if self.is_last and loss is not None:
+                state.losses.append(loss)
+            state.aux_losses.append(aux)
+        for _, works in sends:
+            self._wait(works)
+
+    def forward_backward(self, loader, micro_batches: int, device: torch.device, use_amp: bool,
+                         amp_dtype: torch.dtype, scaler=None, batch_size: int = 1,
+                         aux_loss_coef: float = 0.01) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
+        """One optimizer step's worth of forward and backward; returns (mean loss on the last stage | None, aux)."""
+        state = PipelineState()
+        self._run_forward(loader, micro_batches, device, use_amp, amp_dtype, batch_size, state, keep_graph=True)
+        total_aux = (torch.stack([a.detach().float() for a in state.aux_losses]).sum()
+                     if state.aux_losses else torch.zeros((), device=device))
+        if self.pp_size > 1 and dist.is_initialized() and self.topo.pp_group is not None:
+            dist.all_reduce(total_aux, op=dist.ReduceOp.SUM, group=self.topo.pp_group)
+
+        sends = []
+        pending = None
+        if not self.is_last:
+            g0 = torch.empty_like(state.boundaries[micro_batches - 1], dtype=self.boundary_dtype)
+            pending = (g0, self._irecv(g0, self.next_rank, self._bwd_tag(micro_batches - 1)))
+        for m in reversed(range(micro_batches)):
+            aux = state.aux_losses[m]
+            if self.is_last:
+                loss_mb = (state.losses[m] + aux) / micro_batches
+                if scaler is not None and scaler.is_enabled():
+                    scaler.scale(loss_mb).backward()
+                else:
+                    loss_mb.backward()
+            else:
+                gbuf, works = pending
+                self._wait(works)
+                if m > 0:
+                    nxt = torch.empty_like(state.boundaries[m - 1], dtype=self.boundary_dtype)
+                    pending = (nxt, self._irecv(nxt, self.next_rank, self._bwd_tag(m - 1)))
+                grad = gbuf.to(state.boundaries[m].dtype)
+                if aux.requires_grad:
+                    if scaler is not None and scaler.is_enabled():
+                        torch.autograd.backward([state.boundaries[m], scaler.scale(aux / micro_batches)],
+                                                [grad, None])
+                    else:
+                        torch.autograd.backward([state.boundaries[m], aux / micro_batches], [grad, None])
+                else:
+                    state.boundaries[m].backward(grad)
+            if not self.is_first:
+                gin = state.recv_inputs[m].grad.to(self.boundary_dtype)
+                sends.append((gin, self._isend(gin, self.prev_rank, self._bwd_tag(m))))
+        for _, works in sends:
+            self._wait(works)
+
+        if self.is_last and state.losses:
+            with torch.no_grad():
+                return torch.stack([l.detach().float() for l in state.losses]).mean(), total_aux.detach()
+        return None, total_aux.detach()
+
+    @torch.no_grad()
+    def forward_only(self, loader, micro_batches: int, device: torch.device, use_amp: bool, amp_dtype: torch.dtype,
+                     batch_size: int) -> Optional[torch.Tensor]:
+        state = PipelineState()
+        self._run_forward(loader, micro_batches, device, use_amp, amp_dtype, batch_size, state, keep_graph=False)
+        if self.is_last and state.losses:
+            return torch.stack([l.detach().float() for l in state.losses]).mean()
+        return None

@@ -1,0 +1,449 @@
+"""Training driver: the reference's train.py CLI on the heiretsu_b200 engine.
+
+Every reference flag is accepted with the same name, default and choices
+(reference train.py:171-226); added flags are additive only. The loop does
+the same work per step as the reference (train.py:400-524): ``grad_accum``
+microbatches of forward + backward, loss all-reduce over DP, DP gradient
+averaging, gradient clipping, AdamW, logging, periodic eval and checkpoints.
+
+Two engines share this loop:
+
+* **fused** (CUDA, bf16, configs covered by ``fused_supported``): flat fp32
+  master/grad buffers, sm_100a kernels for every op, fused AdamW with global
+  norm clipping, DP reduction of the flat gradient buffer.
+* **plain** (CPU, fp32, fp16 AMP, or configs the fused path does not cover):
+  PyTorch modules with autocast, ``average_gradients``, ``clip_grad_norm_``
+  and ``torch.optim.AdamW`` -- the reference's numerics.
+
+Deliberate differences from the reference (each a fix of a reference quirk):
+the model init seed is the same on every TP rank (the TP model equals the
+dense model), gradient clipping uses the global norm (``--clip_mode local``
+restores per-shard clipping), EP dispatch/combine are differentiable, and the
+pipeline boundary has one declared dtype.
+"""
+from __future__ import annotations
+
+import argparse
+import math
+import os
+import random
+import time
+from dataclasses import asdict
+from datetime import timedelta
+from typing import Optional
+
+import numpy as np
+import torch
+import torch.distributed as dist
+
+from .config import GPTConfig
+from .models.gpt import GPT
+from .parallel.dp import average_gradients
+from .parallel.pipeline import GPipeEngine, StageModule
+from .topo import cleanup, init_topology
+from .utils.ckpt import load_checkpoint, save_checkpoint
+from .utils.data import RandomBatchLoader, SyntheticLoader
+
+try:  # optional, as in the reference
+    import wandb  # type: ignore
+
+    WANDB_AVAILABLE = True
+except Exception:  # pragma: no cover
+    wandb = None
+    WANDB_AVAILABLE = False
+
+
+def build_argparser() -> argparse.ArgumentParser:
+    p = argparse.ArgumentParser(description="GPT trainer (heiretsu_b200): DP/EP/TP/PP, AMP, grad accumulation")
+    # data / batching
+    p.add_argument("--data_dir", type=str, default="fineweb10B")
+    p.add_argument("--num_train_chunks", type=int, default=None)
+    p.add_argument("--num_val_chunks", type=int, default=1)
+    p.add_argument("--batch_size", type=int, default=64)
+    p.add_argument("--block_size", type=int, default=512)
+    p.add_argument("--eval_interval", type=int, default=1000)
+    p.add_argument("--eval_iters", type=int, default=200)
+    # model
+    p.add_argument("--n_layer", type=int, default=6)
+    p.add_argument("--n_head", type=int, default=6)
+    p.add_argument("--n_embed", type=int, default=768)
+    p.add_argument("--dropout", type=float, default=0.2)
+    # optimisation
+    p.add_argument("--max_iters", type=int, default=50000)
+    p.add_argument("--learning_rate", type=float, default=3e-4)
+    p.add_argument("--weight_decay", type=float, default=0.1)
+    p.add_argument("--betas", type=float, nargs=2, default=(0.9, 0.95))
+    p.add_argument("--grad_clip", type=float, default=1.0)
+    p.add_argument("--grad_accum_steps", type=int, default=1)
+    p.add_argument("--amp", type=str, choices=["none", "fp16", "bf16"], default="none")
+    p.add_argument("--compile", action="store_true", help="torch.compile the plain path (the fused path ignores it)")
+    p.add_argument("--device", type=str, default="auto", choices=["auto", "cpu", "cuda", "mps"])
+    p.add_argument("--seed", type=int, default=1337)
+    # topology
+    p.add_argument("--dp", type=int, default=1)
+    p.add_argument("--ep", type=int, default=1)
+    p.add_argument("--tp", type=int, default=1)
+    p.add_argument("--pp", type=int, default=1)
+    p.add_argument("--dp_share_data", action="store_true")
+    p.add_argument("--dist_backend", type=str, default="nccl", choices=["nccl", "gloo"])
+    # MoE
+    p.add_argument("--num_experts", type=int, default=0)
+    p.add_argument("--top_k", type=int, default=2)
+    p.add_argument("--moe_freq", type=int, default=2)
+    p.add_argument("--aux_loss_coef", type=float, default=0.01)
+    # wandb / checkpoints
+    p.add_argument("--wandb", action="store_true")
+    p.add_argument("--wandb_project", type=str, default="fineweb10B-gpt")
+    p.add_argument("--wandb_entity", type=str, default=None)
+    p.add_argument("--wandb_mode", type=str, default="online", choices=["online", "offline", "disabled"])
+    p.add_argument("--run_name", type=str, default=None)
+    p.add_argument("--save_interval", type=int, default=0)
+    # additive flags
+    p.add_argument("--synthetic_data", action="store_true", help="uniform-random token ids instead of .bin files")
+    p.add_argument("--engine", type=str, default="auto", choices=["auto", "fused", "plain"])
+    p.add_argument("--clip_mode", type=str, default="global", choices=["global", "local"])
+    p.add_argument("--pp_boundary_dtype", type=str, default="fp32", choices=["fp32", "bf16"])
+    p.add_argument("--resume", type=str, default=None, help="checkpoint file to load before training")
+    p.add_argument("--out_dir", type=str, default=".")
+    p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
+    p.add_argument("--log_interval", type=int, default=None)
+    return p
+
+
+def pick_device(arg: str):
+    if arg == "auto":
+        if torch.cuda.is_available():
+            lr = int(os.environ.get("LOCAL_RANK", "0"))
+            return torch.device("cuda", lr), lr
+        return torch.device("cpu"), 0
+    dev = torch.device(arg)
+    if dev.type == "cuda":
+        lr = int(os.environ.get("LOCAL_RANK", "0")) if dev.index is None else dev.index
+        return torch.device("cuda", lr), lr
+    return dev, 0
+
+
+def mp_group_of(topo):
+    """Group of all ranks with this rank's dp_rank (the model-parallel replica), or None."""
+    if topo.world_size == 1 or topo.tp * topo.pp * topo.ep == 1:
+        return None
+    groups = {}
+    for d in range(topo.dp):
+        ranks = [r for r in range(topo.world_size) if r // (topo.ep * topo.pp * topo.tp) == d]
+        groups[d] = dist.new_group(ranks=ranks)
+    return groups[topo.dp_rank]
+
+
+def replication_weight(topo):
+    """Norm weight of each parameter: 1 / (number of model-parallel ranks holding a copy)."""
+
+    def fn(name: str, p) -> float:
+        w = 1.0
+        tp_sharded = getattr(p, "tp_sharded", False)
+        expert = ".experts." in name
+        if topo.tp > 1 and not tp_sharded:
+            w /= topo.tp
+        if topo.ep > 1 and not expert:
+            w /= topo.ep
+        return w
+
+    return fn
+
+
+def mark_tp_sharded(module: torch.nn.Module) -> None:
+    from .parallel.tp import ColumnParallelLinear, ColumnParallelLinearQKV, RowParallelLinear
+
+    for m in module.modules():
+        if isinstance(m, (ColumnParallelLinear, ColumnParallelLinearQKV)):
+            m.weight.tp_sharded = True
+            if m.bias is not None:
+                m.bias.tp_sharded = True
+        elif isinstance(m, RowParallelLinear):
+            m.weight.tp_sharded = True
+
+
+class Engine:
+    """Owns the model/stage, optimizer and one training step."""
+
+    def __init__(self, args, topo, device, cfg):
+        self.args, self.topo, self.device, self.cfg = args, topo, device, cfg
+        self.use_pipeline = topo.pp > 1
+        if self.use_pipeline:
+            self.module = StageModule(cfg, topo, topo.pp_rank, topo.pp)
+        else:
+            self.module = GPT(cfg, topo=topo)
+        mark_tp_sharded(self.module)
+        self.module.to(device)
+        self.amp = args.amp if device.type == "cuda" else "none"
+        from .models.fused import fused_supported
+
+        ok, why = fused_supported(cfg, topo)
+        want = args.engine
+        if want == "fused" and not ok:
+            raise ValueError(f"--engine fused: {why}")
+        if want == "fused" and (device.type != "cuda" or self.amp != "bf16"):
+            raise ValueError("--engine fused needs --device cuda and --amp bf16")
+        self.fused = (want in ("auto", "fused")) and ok and device.type == "cuda" and self.amp == "bf16"
+        if self.fused:
+            from .ops._C import load as _load
+            _load()  # fail loudly if the extension is missing
+        self.mp_group = mp_group_of(topo)
+        if self.fused:
+            from .optim import FusedAdamW
+            from .parallel.flat import FlatParams
+
+            self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo))
+            self.module.fused = True
+            self.optimizer = FusedAdamW(self.flat, lr=args.learning_rate, betas=args.betas,
+                                        weight_decay=args.weight_decay, max_grad_norm=args.grad_clip,
+                                        mp_group=self.mp_group if args.clip_mode == "global" else None)
+            self.scaler = None
+        else:
+            self.flat = None
+            self.optimizer = torch.optim.AdamW(self.module.parameters(), lr=args.learning_rate,
+                                               betas=tuple(args.betas), weight_decay=args.weight_decay)
+            self.scaler = torch.amp.GradScaler("cuda", enabled=(self.amp == "fp16"))
+        self.amp_dtype = torch.float16 if self.amp == "fp16" else torch.bfloat16
+        self.use_amp = self.amp in ("fp16", "bf16") and not self.fused
+        self.forward_module = self.module
+        if args.compile and not self.fused:
+            self.forward_module = torch.compile(self.module)
+        self.reducer = None
+        if topo.dp > 1 and self.fused:
+            from .parallel.grad_reduce import FlatGradReducer
+            self.reducer = FlatGradReducer(self.flat, topo.dp_group, topo)
+        if self.use_pipeline:
+            bd = torch.float32 if args.pp_boundary_dtype == "fp32" else torch.bfloat16
+            self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd)
+
+    # -- one optimizer step ---------------------------------------------------
+    def train_step(self, loader) -> tuple:
+        args, topo = self.args, self.topo
+        accum = args.grad_accum_steps
+        if self.use_pipeline:
+            loss_scalar, aux = self.pipe.forward_backward(loader, micro_batches=accum, device=self.device,
+                                                          use_amp=self.use_amp, amp_dtype=self.amp_dtype,
+                                                          scaler=self.scaler, batch_size=args.batch_size,
+                                                          aux_loss_coef=args.aux_loss_coef)
+        else:
+            aux = torch.zeros((), device=self.device)
+            loss_sum = torch.zeros((), device=self.device)
+            for _ in range(accum):
+                x, y = loader.next_batch(self.device)
+                with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype, enabled=self.use_amp):
+                    _, loss, aux_mb = self.forward_module(x, y, return_logits=False) if self.fused else \
+                        self.forward_module(x, y)
+                    combined = (loss + aux_mb) / accum
+                aux = aux + aux_mb.detach().float()
+                loss_sum = loss_sum + loss.detach().float()
+                if self.scaler is not None and self.scaler.is_enabled():
+                    self.scaler.scale(combined).backward()
+                else:
+                    combined.backward()
+            loss_scalar = loss_sum / accum
+        if loss_scalar is not None and topo.dp_group is not None and dist.is_initialized():
+            dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            loss_scalar = loss_scalar / topo.dp
+        if aux is not None and topo.dp_group is not None and dist.is_initialized():
+            dist.all_reduce(aux, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            aux = aux / topo.dp
+        self.sync_and_step()
+        return loss_scalar, aux
+
+    def sync_and_step(self) -> None:
+        args = self.args
+        if self.fused:
+            if self.reducer is not None:
+                self.reducer.reduce()
+            self.optimizer.step()
+            self.optimizer.zero_grad()
+            return
+        if self.scaler is not None and self.scaler.is_enabled():
+            self.scaler.unscale_(self.optimizer)
+        average_gradients(self.module, self.topo.dp_group)
+        if args.grad_clip > 0:
+            self.clip_plain(args.grad_clip)
+        if self.scaler is not None and self.scaler.is_enabled():
+            self.scaler.step(self.optimizer)
+            self.scaler.update()
+        else:
+            self.optimizer.step()
+        self.optimizer.zero_grad(set_to_none=True)
+
+    def clip_plain(self, max_norm: float) -> None:
+        params = [p for p in self.module.parameters() if p.grad is not None]
+        if self.args.clip_mode == "local" or self.mp_group is None:
+            torch.nn.utils.clip_grad_norm_(params, max_norm)
+            return
+        wfn = replication_weight(self.topo)
+        names = {id(p): n for n, p in self.module.named_parameters()}
+        tot = torch.zeros((), device=self.device)
+        for p in params:
+            tot = tot + wfn(names[id(p)], p) * p.grad.detach().float().pow(2).sum()
+        dist.all_reduce(tot, group=self.mp_group)
+        coef = torch.clamp(max_norm / (tot.sqrt() + 1e-6), max=1.0)
+        for p in params:
+            p.grad.detach().mul_(coef.to(p.grad.dtype))
+
+    # -- eval -----------------------------------------------------------------
+    @torch.no_grad()
+    def estimate_loss(self, loader, eval_iters: int) -> Optional[float]:
+        self.module.eval()
+        losses = []
+        for _ in range(eval_iters):
+            if self.use_pipeline:
+                l = self.pipe.forward_only(loader, self.args.grad_accum_steps, self.device, self.use_amp,
+                                           self.amp_dtype, loader.B)
+                if l is not None and self.topo.dp_group is not None and dist.is_initialized():
+                    dist.all_reduce(l, group=self.topo.dp_group)
+                    l = l / self.topo.dp
+                if l is not None:
+                    losses.append(float(l.item()))
+            else:
+                x, y = loader.next_batch(self.device)
+                with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype, enabled=self.use_amp):
+                    _, loss, _ = self.forward_module(x, y)
+                losses.append(float(loss.item()))
+        self.module.train()
+        return sum(losses) / len(losses) if losses else None
+
+    def after_load(self) -> None:
+        if self.flat is not None:
+            self.flat.refresh_bf16()
+
+
+def main(argv=None) -> None:
+    args = build_argparser().parse_args(argv)
+    world_env = int(os.environ.get("WORLD_SIZE", "1"))
+    distributed = world_env > 1
+    device, local_rank = pick_device(args.device)
+    if device.type == "cuda":
+        torch.cuda.set_device(local_rank)
+    if distributed:
+        if args.dist_backend == "nccl" and device.type != "cuda":
+            raise RuntimeError("nccl backend requires CUDA; use gloo or run on CUDA.")
+        kw = {"timeout": timedelta(seconds=args.pg_timeout_s)}
+        if args.dist_backend == "nccl":
+            kw["device_id"] = device
+        dist.init_process_group(backend=args.dist_backend, **kw)
+    topo = init_topology(dp=args.dp, ep=args.ep, tp=args.tp, pp=args.pp,
+                         timeout=timedelta(seconds=args.pg_timeout_s))
+    rank = topo.rank
+
+    # Same init seed on every TP rank (shards are slices of one full matrix).
+    torch.manual_seed(args.seed)
+    if device.type == "cuda":
+        torch.cuda.manual_seed_all(args.seed)
+    cfg = GPTConfig(block_size=args.block_size, n_layer=args.n_layer, n_head=args.n_head, n_embed=args.n_embed,
+                    dropout=args.dropout, num_experts=args.num_experts, top_k=args.top_k, moe_freq=args.moe_freq,
+                    aux_loss_coef=args.aux_loss_coef)
+    engine = Engine(args, topo, device, cfg)
+    module = engine.module
+    if args.resume:
+        obj = load_checkpoint(module, args.resume)
+        engine.after_load()
+        if rank == 0:
+            print(f"[resume] loaded {args.resume} (step {obj.get('step')})")
+    n_params = sum(p.numel() for p in module.parameters())
+    if rank == 0:
+        print(f"[model] parameters: {n_params:,} ({n_params / 1e6:.1f}M) | engine="
+              f"{'fused' if engine.fused else 'plain'}")
+        if args.num_experts > 0:
+            nm = sum(1 for i in range(args.n_layer) if cfg.is_moe_layer(i))
+            print(f"[MoE] num_experts={args.num_experts}, top_k={args.top_k}, moe_layers={nm}/{args.n_layer}, "
+                  f"ep={args.ep}")
+
+    data_seed = args.seed if args.dp_share_data else args.seed + topo.dp_rank
+    random.seed(data_seed)
+    np.random.seed(data_seed)
+    torch_seed = args.seed if args.dp_share_data else args.seed + topo.dp_rank * 1000 + topo.pp_rank
+    torch.manual_seed(torch_seed)
+    if device.type == "cuda":
+        torch.cuda.manual_seed_all(torch_seed)
+    rank_for_data = 0 if args.dp_share_data else topo.dp_rank
+    if args.synthetic_data:
+        train_loader = SyntheticLoader(args.batch_size, args.block_size, cfg.vocab_size, seed=args.seed,
+                                       rank=rank_for_data)
+        val_loader = SyntheticLoader(args.batch_size, args.block_size, cfg.vocab_size, seed=args.seed + 999)
+    else:
+        train_loader = RandomBatchLoader(args.data_dir, "train", args.batch_size, args.block_size,
+                                         args.num_train_chunks, seed=args.seed, rank=rank_for_data,
+                                         dp_rank=0 if args.dp_share_data else topo.dp_rank,
+                                         dp_size=1 if args.dp_share_data else topo.dp, log_rank=rank)
+        val_loader = RandomBatchLoader(args.data_dir, "val", args.batch_size, args.block_size, args.num_val_chunks,
+                                       seed=args.seed + 999, rank=0, dp_rank=0, dp_size=1, log_rank=rank)
+
+    is_main = topo.is_main
+    if is_main:
+        print(f"device={device} | world_size={topo.world_size} | dp={topo.dp} ep={topo.ep} tp={topo.tp} "
+              f"pp={topo.pp}")
+    run = None
+    if is_main and args.wandb and WANDB_AVAILABLE and args.wandb_mode != "disabled":
+        run = wandb.init(project=args.wandb_project, entity=args.wandb_entity or None,
+                         config={**vars(args), **asdict(cfg), "device": device.type}, mode=args.wandb_mode,
+                         name=args.run_name or None)
+    elif is_main and args.wandb and not WANDB_AVAILABLE:
+        print("wandb not available; proceeding without external logging.")
+
+    module.train()
+    t0 = time.time()
+    tokens_per_step = args.batch_size * args.block_size * args.grad_accum_steps
+    last = time.time()
+    log_every = args.log_interval or max(1, args.eval_interval // 10)
+    for step in range(1, args.max_iters + 1):
+        loss_scalar, aux = engine.train_step(train_loader)
+        now = time.time()
+        dt = now - last
+        last = now
+        eff = tokens_per_step / dt if dt > 0 else float("inf")
+        if is_main and (step % log_every == 0 or step == 1):
+            aux_str = f" | aux_loss {aux.item():.4f}" if args.num_experts > 0 else ""
+            ls = f"{loss_scalar.item():.4f}" if loss_scalar is not None else "n/a"
+            print(f"step {step:6d} | train_loss (mean micro) {ls}{aux_str} | eff_tok/s {eff:,.0f}")
+        if is_main and run:
+            log = {"train/loss_mean_micro": float(loss_scalar.item()) if loss_scalar is not None else float("nan"),
+                   "opt/lr": float(engine.optimizer.param_groups[0]["lr"]), "speed/eff_tokens_per_sec": eff,
+                   "amp/enabled": int(engine.amp != "none"), "amp/mode": args.amp,
+                   "accum/steps": args.grad_accum_steps, "step": step}
+            if args.num_experts > 0:
+                log["train/aux_loss"] = float(aux.item())
+                log.update(expert_load_metrics(module))
+            wandb.log(log, step=step)
+        if step % args.eval_interval == 0 or step == args.max_iters:
+            ev = engine.estimate_loss(val_loader, args.eval_iters)
+            if is_main and ev is not None:
+                print(f"[eval] step {step} | eval_loss {ev:.4f} | elapsed {time.time() - t0:.1f}s")
+                if run:
+                    wandb.log({"eval/loss": ev, "step": step}, step=step)
+        if args.save_interval and step % args.save_interval == 0:
+            save_checkpoint(module, cfg, step, topo, args.out_dir,
+                            optimizer_state=engine.optimizer.state_dict() if engine.fused else None)
+    if is_main and run:
+        run.finish()
+    if is_main:
+        print("training finished.")
+    if distributed and dist.is_initialized():
+        cleanup()
+
+
+def expert_load_metrics(module) -> dict:
+    """Per-expert token counts summed over MoE layers (reference train.py:359-370, :478-499)."""
+    from .models.moe import MoELayer
+
+    total = None
+    for m in module.modules():
+        if isinstance(m, MoELayer) and m._expert_counts is not None:
+            total = m._expert_counts.float().clone() if total is None else total + m._expert_counts.float()
+    if total is None:
+        return {}
+    out = {}
+    s = total.sum().item()
+    if s > 0:
+        fr = total / s
+        for i in range(total.numel()):
+            out[f"expert_load/expert_{i}"] = float(total[i].item())
+            out[f"expert_frac/expert_{i}"] = float(fr[i].item())
+        out["expert_load/max_frac"] = float(fr.max().item())
+        out["expert_load/min_frac"] = float(fr.min().item())
+        out["expert_load/imbalance_ratio"] = float(fr.max().item() / max(fr.min().item(), 1e-9))
+    return out

@@ -1,0 +1,153 @@
+"""Numerics of the non-GEMM sm_100a kernels against plain PyTorch fp32 references."""
+import math
+
+import pytest
+import torch
+import torch.nn.functional as F
+
+pytestmark = pytest.mark.gpu
+
+
+def K():
+    from heiretsu_b200.ops import kernels
+    return kernels
+
+
+def check():
+    from heiretsu_b200.ops._C import check_status
+    check_status()
+
+
+@pytest.mark.parametrize("M,H", [(8192, 768), (300, 1024), (17, 128), (64, 32)])
+def test_layernorm_fwd_bwd(M, H):
+    torch.manual_seed(0)
+    x = torch.randn(M, H, device="cuda") * 2 + 0.5
+    w = torch.randn(H, device="cuda")
+    b = torch.randn(H, device="cuda")
+    y, mean, rstd = K().layernorm_fwd(x, w, b)
+    check()
+    xr = x.clone().requires_grad_(True)
+    wr = w.clone().requires_grad_(True)
+    br = b.clone().requires_grad_(True)
+    yr = F.layer_norm(xr, (H,), wr, br, 1e-5)
+    # bf16 output: relative rounding 2^-8 of |y| (|y| up to ~6 here)
+    assert ((y.float() - yr).abs() / (yr.abs() + 1.0)).max().item() < 1e-2
+    dy = torch.randn(M, H, device="cuda")
+    yr.backward(dy)
+    dres_in = torch.randn(M, H, device="cuda")
+    dres = torch.empty_like(dres_in)
+    dres16 = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    dg = torch.zeros(H, device="cuda")
+    db = torch.ones(H, device="cuda")
+    K().layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dg, db)
+    check()
+    assert torch.allclose(dres, dres_in + xr.grad, atol=1e-3, rtol=1e-3)
+    assert (dres16.float() - dres).abs().max().item() <= 1e-2 * dres.abs().max().item()
+    assert torch.allclose(dg, wr.grad, atol=1e-2, rtol=1e-3)
+    assert torch.allclose(db, 1 + br.grad, atol=1e-2, rtol=1e-3)
+
+
+@pytest.mark.parametrize("M,V", [(512, 50257), (64, 128), (33, 1000)])
+def test_cross_entropy(M, V):
+    torch.manual_seed(1)
+    Vp = (V + 127) // 128 * 128
+    logits = torch.zeros(M, Vp, device="cuda", dtype=torch.bfloat16)
+    logits[:, :V] = (torch.randn(M, V, device="cuda") * 3).bfloat16()
+    t = torch.randint(0, V, (M,), device="cuda")
+    loss, lse, rows = K().cross_entropy_fwd(logits, V, t)
+    check()
+    lr = logits[:, :V].float().requires_grad_(True)
+    ref = F.cross_entropy(lr, t)
+    assert abs(loss.item() - ref.item()) < 1e-4 * max(1.0, abs(ref.item()))
+    ref.backward(torch.tensor(0.5, device="cuda"))
+    K().cross_entropy_bwd_(logits, V, t, lse, torch.tensor([0.5], device="cuda"), 1.0 / M)
+    check()
+    assert (logits[:, :V].float() - lr.grad).abs().max().item() < 2e-3 / M + 1e-6 * 0 + 4e-3 * lr.grad.abs().max().item()
+    assert logits[:, V:].float().abs().max().item() == 0.0
+
+
+def test_embedding():
+    torch.manual_seed(2)
+    B, T, V, H = 4, 256, 1000, 768
+    idx = torch.randint(0, V, (B, T), device="cuda")
+    wte = torch.randn(V, H, device="cuda")
+    wpe = torch.randn(T, H, device="cuda")
+    out = K().embedding_fwd(idx, wte, wpe)
+    check()
+    ref = wte[idx] + wpe[None]
+    assert torch.allclose(out.view(B, T, H), ref)
+    dx = torch.randn(B * T, H, device="cuda")
+    dwte = torch.zeros_like(wte)
+    dwpe = torch.zeros_like(wpe)
+    K().embedding_bwd(idx, dx, dwte, dwpe)
+    check()
+    rwte = torch.zeros_like(wte).index_add_(0, idx.reshape(-1), dx)
+    assert torch.allclose(dwte, rwte, atol=1e-4)
+    assert torch.allclose(dwpe, dx.view(B, T, H).sum(0), atol=1e-4)
+
+
+def test_colsum():
+    torch.manual_seed(3)
+    x = torch.randn(8192, 3072, device="cuda").bfloat16()
+    out = torch.ones(3072, device="cuda")
+    K().colsum_bf16(x, out)
+    check()
+    assert torch.allclose(out, 1 + x.float().sum(0), atol=1e-2, rtol=1e-4)
+
+
+def test_adamw_matches_torch():
+    from heiretsu_b200.optim import FusedAdamW
+    from heiretsu_b200.parallel.flat import FlatParams
+
+    torch.manual_seed(4)
+    m1 = torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.LayerNorm(96), torch.nn.Linear(96, 40)).cuda()
+    m2 = torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.LayerNorm(96), torch.nn.Linear(96, 40)).cuda()
+    m2.load_state_dict(m1.state_dict())
+    flat = FlatParams(m2, torch.device("cuda"))
+    opt1 = torch.optim.AdamW(m1.parameters(), lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1)
+    opt2 = FusedAdamW(flat, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
+    for _ in range(4):
+        x = torch.randn(32, 64, device="cuda")
+        l1 = m1(x).pow(2).mean()
+        l1.backward()
+        torch.nn.utils.clip_grad_norm_(m1.parameters(), 1.0)
+        opt1.step()
+        opt1.zero_grad()
+        with torch.no_grad():
+            xx = x.clone().requires_grad_(False)
+        l2 = m2(xx).pow(2).mean()
+        grads = torch.autograd.grad(l2, list(m2.parameters()))
+        for p, g in zip(m2.parameters(), grads):
+            p.main_grad.copy_(g)
+        opt2.step()
+        opt2.zero_grad()
+    check()
+    for (n, a), b in zip(m1.named_parameters(), m2.parameters()):
+        assert torch.allclose(a, b, atol=1e-5, rtol=1e-4), n
+        assert torch.allclose(b.w16.float(), b, atol=1e-2, rtol=1e-2), n
+
+
+@pytest.mark.parametrize("B,T,nh", [(2, 256, 2), (1, 1024, 4), (2, 200, 3), (8, 1024, 12)])
+def test_attention_fwd_bwd(B, T, nh):
+    torch.manual_seed(5)
+    H = nh * 64
+    qkv = (torch.randn(B * T, 3 * H, device="cuda")).bfloat16()
+    y, lse = K().attention_fwd(qkv, B, T, nh)
+    check()
+    q, k, v = qkv.float().view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4).unbind(0)
+    q.requires_grad_(True)
+    k.requires_grad_(True)
+    v.requires_grad_(True)
+    ref = F.scaled_dot_product_attention(q, k, v, is_causal=True)
+    ref2 = ref.transpose(1, 2).reshape(B * T, H)
+    err = (y.float() - ref2).abs().max().item()
+    assert err < 2e-2, err
+    dy = torch.randn(B * T, H, device="cuda").bfloat16()
+    ref2.backward(dy.float())
+    dqkv = K().attention_bwd(qkv, y, dy, lse, B, T, nh)
+    check()
+    d = dqkv.float().view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4)
+    for i, (name, g) in enumerate((("q", q.grad), ("k", k.grad), ("v", v.grad))):
+        e = (d[i] - g).abs().max().item()
+        scale = g.abs().max().item()
+        assert e <= 3e-2 * scale + 1e-3, (name, e, scale)
