@@ -89,6 +89,65 @@ def bench_gemm(flush):
     return rows
 
 
+def bench_attention(flush):
+    """Causal attention fwd / bwd, GPT-2 small shape (B=8, T=1024, 12 heads of 64) vs torch SDPA."""
+    import torch.nn.functional as F
+
+    from . import kernels as K
+    from ._C import check_status
+
+    B, T, nh = 8, 1024, 12
+    H = nh * 64
+    qkv = torch.randn(B * T, 3 * H, device="cuda", dtype=torch.bfloat16)
+    y, lse = K.attention_fwd(qkv, B, T, nh)
+    dy = torch.randn_like(y)
+    q, k, v = qkv.view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4).unbind(0)
+    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+    fwd_flops = 4.0 * B * nh * T * T * 64 / 2
+    rows = []
+    t = time_fn(lambda: K.attention_fwd(qkv, B, T, nh, out=y), flush=flush)
+    tr = time_fn(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), flush=flush)
+    rows.append(dict(op="attention", name="fwd", ms=t, ref_ms=tr, tflops=fwd_flops / t / 1e9,
+                     ref_tflops=fwd_flops / tr / 1e9))
+    t = time_fn(lambda: K.attention_bwd(qkv, y, dy, lse, B, T, nh), flush=flush)
+    qg, kg, vg = (x.detach().requires_grad_(True) for x in (q, k, v))
+    o = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
+    g = torch.randn_like(o)
+    tr = time_fn(lambda: torch.autograd.grad(o, (qg, kg, vg), g, retain_graph=True), flush=flush)
+    rows.append(dict(op="attention", name="bwd", ms=t, ref_ms=tr, tflops=2.5 * fwd_flops / t / 1e9,
+                     ref_tflops=2.5 * fwd_flops / tr / 1e9))
+    check_status()
+    return rows
+
+
+def bench_norm(flush):
+    """LayerNorm fwd/bwd at [8192, 768] vs torch (bytes moved / time)."""
+    import torch.nn.functional as F
+
+    from . import kernels as K
+
+    M, H = 8192, 768
+    x = torch.randn(M, H, device="cuda")
+    w = torch.randn(H, device="cuda")
+    b = torch.randn(H, device="cuda")
+    rows = []
+    t = time_fn(lambda: K.layernorm_fwd(x, w, b), flush=flush)
+    tr = time_fn(lambda: F.layer_norm(x, (H,), w, b), flush=flush)
+    rows.append(dict(op="layernorm", name="fwd", ms=t, ref_ms=tr, gbs=(M * H * 6) / t / 1e6))
+    y, mean, rstd = K.layernorm_fwd(x, w, b)
+    dy = torch.randn(M, H, device="cuda")
+    dres = torch.zeros(M, H, device="cuda")
+    d16 = torch.empty(M, H, device="cuda", dtype=torch.bfloat16)
+    dg = torch.zeros(H, device="cuda")
+    db = torch.zeros(H, device="cuda")
+    t = time_fn(lambda: K.layernorm_bwd(dy, x, mean, rstd, w, dres, dres, d16, dg, db), flush=flush)
+    rows.append(dict(op="layernorm", name="bwd", ms=t, gbs=(M * H * 18) / t / 1e6))
+    return rows
+
+
+EXTRA_BENCHES = {"attention": bench_attention, "norm": bench_norm}
+
+
 def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)

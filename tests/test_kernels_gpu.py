@@ -63,7 +63,8 @@ def test_cross_entropy(M, V):
     K().cross_entropy_bwd_(logits, V, t, lse, torch.tensor([0.5], device="cuda"), 1.0 / M)
     check()
     assert (logits[:, :V].float() - lr.grad).abs().max().item() < 2e-3 / M + 1e-6 * 0 + 4e-3 * lr.grad.abs().max().item()
-    assert logits[:, V:].float().abs().max().item() == 0.0
+    if Vp > V:
+        assert logits[:, V:].float().abs().max().item() == 0.0
 
 
 def test_embedding():
