@@ -155,3 +155,57 @@ void ce_bwd_launch(__nv_bfloat16* logits, long ld, int M, int V, int Vp, const i
 }
 
 }  // namespace hb
+
+// ============================================================================
+// Allocation-free cross-entropy forward (declared in noalloc.h).
+//
+// Same kernels as ce_fwd_launch, but the per-row loss scratch lives in a
+// file-scope device array instead of a buffer the caller allocates. See
+// noalloc.h for who needs this, its limits and its concurrency rules.
+// ============================================================================
+#include <mutex>
+
+#include "noalloc.h"
+
+namespace {
+
+// Per-row losses of the most recent call (every call overwrites rows [0, M)).
+// Held by every GPU that loads the library, until the process exits.
+__device__ __align__(256) float g_ce_noalloc_rows[HB_CE_NOALLOC_MAX_ROWS];
+
+std::mutex g_ce_noalloc_mu;
+float* g_ce_noalloc_ptr[64] = {};
+
+// Device address of the scratch array for the current device; resolved once
+// per device (the host-side name of the array is only a stand-in).
+int ce_noalloc_scratch(float** out) {
+  int dev = 0;
+  if (cudaGetDevice(&dev) != cudaSuccess || dev < 0 || dev >= 64) return HB_NOALLOC_ERR_CUDA;
+  std::lock_guard<std::mutex> lk(g_ce_noalloc_mu);
+  if (g_ce_noalloc_ptr[dev] == nullptr) {
+    void* p = nullptr;
+    if (cudaGetSymbolAddress(&p, g_ce_noalloc_rows) != cudaSuccess || p == nullptr) return HB_NOALLOC_ERR_CUDA;
+    g_ce_noalloc_ptr[dev] = static_cast<float*>(p);
+  }
+  *out = g_ce_noalloc_ptr[dev];
+  return HB_NOALLOC_OK;
+}
+
+}  // namespace
+
+extern "C" int hb_cross_entropy_fwd_noalloc(const void* logits, long ld, int M, int V, const int64_t* targets,
+                                            int ignore_index, float* lse, float* loss_mean, cudaStream_t stream) {
+  if (logits == nullptr || targets == nullptr || lse == nullptr || loss_mean == nullptr) return HB_NOALLOC_ERR_ARG;
+  if (M < 0 || V <= 0 || ld < V || ld % 8 != 0) return HB_NOALLOC_ERR_ARG;
+  if (M > HB_CE_NOALLOC_MAX_ROWS) return HB_NOALLOC_ERR_TOO_LARGE;
+  if (M == 0) return HB_NOALLOC_OK;
+  float* rows = nullptr;
+  const int rc = ce_noalloc_scratch(&rows);
+  if (rc != HB_NOALLOC_OK) return rc;
+  hb::ce_fwd_kernel<<<M, hb::CE_THREADS, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, targets,
+                                                      ignore_index, lse, rows);
+  if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_ERR_CUDA;
+  hb::mean_loss_kernel<<<1, 1024, 0, stream>>>(rows, targets, M, ignore_index, loss_mean, nullptr);
+  if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_ERR_CUDA;
+  return HB_NOALLOC_OK;
+}
