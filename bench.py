@@ -209,6 +209,8 @@ def run_ours(args, world, rank, dev):
 
     dl = DeviceBatches()
     step = lambda: eng.train_step(dl)
+    # Launch counting runs one eager step: the captured graph replays exactly this kernel sequence.
+    eng.count_step = lambda: eng._eager_step(dl)
     return eng, step, (lambda: SyntheticLoader(MICRO_BATCH, SEQ, cfg.vocab_size, seed=7, rank=rank)), "hb::"
 
 
@@ -305,7 +307,8 @@ def main():
         dist.all_gather_object(gathered, rows)
         rows = [r for g in gathered for r in g]
     clocks = summarize_clocks(rows)
-    launches = count_launches(step, prefix) if (args.impl == "ours" and not args.no_launch_count) else -1
+    launches = (count_launches(getattr(eng, "count_step", step), prefix)
+                if (args.impl == "ours" and not args.no_launch_count) else -1)
     tokens = world * MICRO_BATCH * SEQ * ACCUM
     value = tokens / (ms / 1e3)
 

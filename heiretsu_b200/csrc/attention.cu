@@ -6,21 +6,28 @@
 // head h at h*64) through one 3-D TMA map {3*Hs, T, B}: a 128-token tile
 // never crosses into the next sequence, and rows >= T read as zeros.
 //
-// Forward, one CTA per (query tile of 128, head, batch), 192 threads:
-//   warp 0     TMA: Q once, then K0, K1, V0, K2, V1, ... into a 3-slot ring
-//   warp 1     MMA: S = Q K^T (128x128, fp32 in TMEM); O_j = P_j V_j (128x64)
-//   warps 2-5  softmax: thread = query row; two passes over S in TMEM (row
-//              max, then exp2 + row sum), P -> bf16 in 128B-swizzled smem
-//              (the A operand of the PV MMA), O accumulated in registers with
-//              the online-softmax rescale, final O / l and LSE stored.
-//   TMEM: S [0,128), O double buffer [128,192) [192,256). 96 KB smem, so two
-//   CTAs share an SM and one's softmax overlaps the other's MMAs.
+// Forward, one CTA per (pair of query tiles, head, batch), 320 threads. The
+// pair is (i, n-1-i), so every CTA does the same causal work, and both tiles
+// share each K/V tile load:
+//   warp 0      TMA: Q_A, Q_B, then K0, K1, V0, K2, V1, ... into a 3-slot ring
+//   warp 1      MMA: S_X = Q_X K_j^T (128x128 fp32 in TMEM), O_X = P_X V_j
+//   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B (thread =
+//               query row): row max and exp2 over S in TMEM, P -> bf16 in
+//               128B-swizzled smem (A operand of the PV MMA), O accumulated
+//               in registers with the online-softmax rescale.
+//   While one warpgroup runs its softmax, the MMA warp computes the other
+//   tile's S or PV, so tensor core and ALUs overlap inside the CTA.
+//   TMEM: per tile S [128 cols] + O double buffer [2 x 64 cols].
 //
-// Backward, one CTA per (key tile of 128, head, batch), FA2 order:
-//   S^T = K Q_i^T and dP^T = V dO_i^T (thread = key row), P^T and
-//   dS^T = P^T (dP^T - D) * scale to smem, then dV += P^T dO_i,
-//   dK += dS^T Q_i and dQ_i = dS K (the same smem tiles serve as K-major or
-//   MN-major operands), dQ_i added to an fp32 accumulator with vector atomics.
+// Backward, one CTA per (key tile of 128, head, batch), 320 threads, FA2
+// order over the query tiles i >= key tile:
+//   S^T = K Q_i^T and dP^T = V dO_i^T are issued as two 64-query halves; the
+//   warpgroup of half g (warps 2-5: g = 0, warps 6-9: g = 1; thread = key
+//   row) turns its half into P^T and dS^T = P^T (dP^T - D) * scale in smem,
+//   then dV += P^T dO_i, dK += dS^T Q_i and dQ_i = dS K (the same smem tiles
+//   serve as K-major or MN-major operands); dQ_i is added to an fp32
+//   accumulator with vector atomics. The next tile's first half is computed
+//   while the second half of the current one is still in its softmax.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -59,29 +66,87 @@ constexpr int kTile = 128;
 constexpr int kD = 64;
 constexpr int kTileBytes = kTile * kD * 2;  // 16 KB
 
+// exp2 on the special-function unit (PTX ex2.approx, flush-to-zero).
+__device__ __forceinline__ float fast_exp2(float x) {
+  float y;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
+  return y;
+}
+
 // ============================================================================
 // Forward
 // ============================================================================
 constexpr int FWD_SLOTS = 3;
-constexpr int FWD_SMEM = kTileBytes /*Q*/ + FWD_SLOTS * kTileBytes + 2 * kTileBytes /*P*/ + 1024;
+constexpr int FWD_THREADS = 320;
+constexpr int FWD_SMEM = 2 * kTileBytes /*Q_A, Q_B*/ + FWD_SLOTS * kTileBytes + 4 * kTileBytes /*P_A, P_B*/ + 1024;
 
-__global__ void __launch_bounds__(192) attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, AttnParams p) {
+// Position of K_j / V_j in the load sequence K0, K1, V0, K2, V1, ..., K_{n-1}, V_{n-2}, V_{n-1}.
+__device__ __forceinline__ int fwd_k_item(int j) { return j == 0 ? 0 : 2 * j - 1; }
+__device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 2 * n - 1 : 2 * j + 2; }
+
+// Online softmax of one 128x128 score tile held in TMEM, for the calling
+// thread's row: updates (m, l), writes P (bf16) to the swizzled smem tile and
+// returns the rescale factor of the previous accumulator.
+template <bool DIAG>
+__device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
+                                              float scale_log2, float& m, float& l) {
+  float v[32];
+  float mt = -INFINITY;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    tmem_ld32(tS + lane_off + c * 32, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      const float sv = v[i] * scale_log2;
+      mt = (DIAG && key0 + c * 32 + i > q) ? mt : fmaxf(mt, sv);
+    }
+  }
+  const float m_new = fmaxf(m, mt);
+  const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
+  float rs = 0.f;
+#pragma unroll 1
+  for (int c = 0; c < 4; ++c) {
+    tmem_ld32(tS + lane_off + c * 32, v);
+#pragma unroll
+    for (int i = 0; i < 32; ++i) {
+      float pv = fast_exp2(fmaf(v[i], scale_log2, -m_new));
+      if (DIAG && key0 + c * 32 + i > q) pv = 0.f;
+      v[i] = pv;
+      rs += pv;
+    }
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint4 pk = make_uint4(pack_bf16(v[g * 8 + 0], v[g * 8 + 1]), pack_bf16(v[g * 8 + 2], v[g * 8 + 3]),
+                                  pack_bf16(v[g * 8 + 4], v[g * 8 + 5]), pack_bf16(v[g * 8 + 6], v[g * 8 + 7]));
+      *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 4 + g)) = pk;
+    }
+  }
+  l = l * alpha + rs;
+  m = m_new;
+  return alpha;
+}
+
+__global__ void __launch_bounds__(FWD_THREADS, 1)
+    attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint8_t* sQ = smem;
-  uint8_t* sSlot = smem + kTileBytes;
-  uint8_t* sP = sSlot + FWD_SLOTS * kTileBytes;
-  __shared__ uint64_t bar_q, bar_full[FWD_SLOTS], bar_empty[FWD_SLOTS], bar_s, bar_p, bar_o[2], bar_done;
+  uint8_t* sQ = smem;                          // [2][16 KB]
+  uint8_t* sSlot = smem + 2 * kTileBytes;      // [3][16 KB]
+  uint8_t* sP = sSlot + FWD_SLOTS * kTileBytes;  // [2][32 KB]
+  __shared__ uint64_t bar_q, bar_full[FWD_SLOTS], bar_empty[FWD_SLOTS], bar_s[2], bar_p[2], bar_o[2][2], bar_done;
   __shared__ uint32_t tmem_slot;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + kTile - 1) / kTile;
+  const int n_pairs = (n_qt + 1) / 2;
   int bid = blockIdx.x;
-  const int qt = n_qt - 1 - (bid % n_qt);  // heaviest tiles first
-  bid /= n_qt;
+  const int pair = bid % n_pairs;
+  bid /= n_pairs;
   const int h = bid % p.nh;
   const int b = bid / p.nh;
-  const int n_kv = qt + 1;
+  const int qt[2] = {pair, n_qt - 1 - pair};
+  const bool hasA = qt[0] < qt[1];
+  const int n_kv = qt[1] + 1;
 
   if (threadIdx.x == 0) {
     mbar_init(&bar_q, 1);
@@ -89,199 +154,178 @@ __global__ void __launch_bounds__(192) attn_fwd_kernel(const __grid_constant__ C
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_s, 1);
-    mbar_init(&bar_p, 4);
-    mbar_init(&bar_o[0], 1);
-    mbar_init(&bar_o[1], 1);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&bar_s[g], 1);
+      mbar_init(&bar_p[g], 4);
+      mbar_init(&bar_o[g][0], 1);
+      mbar_init(&bar_o[g][1], 1);
+    }
     mbar_init(&bar_done, 1);
     fence_barrier_init();
     tma_prefetch_desc(&tm_qkv);
   }
   if (warp == 1) {
-    tmem_alloc(&tmem_slot, 256);
+    tmem_alloc(&tmem_slot, 512);
     tmem_relinquish();
   }
   tc_fence_before();
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
-  const uint32_t tS = tmem, tO0 = tmem + 128;
+  // per tile g: S at g*256, O buffers at g*256 + 128 + {0, 64}
 
   if (warp == 0) {
     if (elect_one()) {
-      mbar_arrive_expect_tx(&bar_q, kTileBytes);
-      tma_load_3d(sQ, &tm_qkv, &bar_q, h * kD, qt * kTile, b);
-      // Ring order = MMA consumption order: K0, then (K_{j+1}, V_j) for each j.
-      int slot = 0;
-      uint32_t phase = 0;
-      auto load = [&](int kv, int is_v) -> bool {
-        if (!mbar_wait(&bar_empty[slot], phase ^ 1u, p.status, 20)) return false;
+      mbar_arrive_expect_tx(&bar_q, (hasA ? 2 : 1) * kTileBytes);
+      tma_load_3d(sQ + kTileBytes, &tm_qkv, &bar_q, h * kD, qt[1] * kTile, b);
+      if (hasA) tma_load_3d(sQ, &tm_qkv, &bar_q, h * kD, qt[0] * kTile, b);
+      for (int idx = 0; idx < 2 * n_kv; ++idx) {
+        int kv, is_v;
+        if (idx == 0) {
+          kv = 0, is_v = 0;
+        } else if (idx == 2 * n_kv - 1) {
+          kv = n_kv - 1, is_v = 1;
+        } else if (idx & 1) {
+          kv = (idx + 1) >> 1, is_v = 0;
+        } else {
+          kv = (idx - 2) >> 1, is_v = 1;
+        }
+        const int slot = idx % FWD_SLOTS;
+        const uint32_t ph = (idx / FWD_SLOTS) & 1;
+        if (!mbar_wait(&bar_empty[slot], ph ^ 1u, p.status, 20)) break;
         mbar_arrive_expect_tx(&bar_full[slot], kTileBytes);
         tma_load_3d(sSlot + slot * kTileBytes, &tm_qkv, &bar_full[slot], (is_v ? 2 : 1) * p.Hs + h * kD,
                     kv * kTile, b);
-        if (++slot == FWD_SLOTS) {
-          slot = 0;
-          phase ^= 1u;
-        }
-        return true;
-      };
-      if (load(0, 0)) {
-        for (int j = 0; j < n_kv; ++j) {
-          if (j + 1 < n_kv && !load(j + 1, 0)) break;
-          if (!load(j, 1)) break;
-        }
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
       constexpr uint32_t idS = make_idesc_f16(128, 128, false, false, true);
       constexpr uint32_t idO = make_idesc_f16(128, 64, false, true, true);
-      const uint32_t qa = smem_u32(sQ), pa = smem_u32(sP);
-      int slot = 0;
-      uint32_t phase = 0;
       bool ok = mbar_wait(&bar_q, 0, p.status, 21);
-      auto take = [&](uint32_t& addr) -> bool {
-        if (!mbar_wait(&bar_full[slot], phase, p.status, 22)) return false;
+      auto item = [&](int idx, uint32_t& addr) -> bool {
+        const int slot = idx % FWD_SLOTS;
+        if (!mbar_wait(&bar_full[slot], (idx / FWD_SLOTS) & 1, p.status, 22)) return false;
         tc_fence_after();
         addr = smem_u32(sSlot + slot * kTileBytes);
         return true;
       };
-      auto release = [&]() {
-        mma_commit(&bar_empty[slot]);
-        if (++slot == FWD_SLOTS) {
-          slot = 0;
-          phase ^= 1u;
-        }
-      };
-      uint32_t ka = 0, va = 0;
-      if (ok && take(ka)) {
-        tc_fence_after();
+      auto issue_s = [&](int g, uint32_t ka) {
+        const uint32_t qa = smem_u32(sQ + g * kTileBytes);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_f16_ss(tS, sw128_desc(qa + k * 32, 16, 1024), sw128_desc(ka + k * 32, 16, 1024), idS, k > 0);
-        release();
-        mma_commit(&bar_s);
+          mma_f16_ss(tmem + g * 256, sw128_desc(qa + k * 32, 16, 1024), sw128_desc(ka + k * 32, 16, 1024), idS, k > 0);
+        mma_commit(&bar_s[g]);
+      };
+      auto issue_pv = [&](int g, int j, uint32_t va) {
+        const uint32_t pa = smem_u32(sP + g * 2 * kTileBytes);
+        const uint32_t tO = tmem + g * 256 + 128 + (j & 1) * 64;
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
+          mma_f16_ss(tO, sw128_desc(pa + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
+                     sw128_desc(va + ks * 2048, 8192, 1024), idO, ks > 0);
+        mma_commit(&bar_o[g][j & 1]);
+      };
+      uint32_t ka = 0, va = 0;
+      if (ok && item(fwd_k_item(0), ka)) {
+        if (hasA) issue_s(0, ka);
+        issue_s(1, ka);
+        mma_commit(&bar_empty[fwd_k_item(0) % FWD_SLOTS]);
       } else {
         ok = false;
       }
       for (int j = 0; j < n_kv && ok; ++j) {
-        if (!mbar_wait(&bar_p, j & 1, p.status, 23)) break;
+        const bool next = j + 1 < n_kv;
+        if (hasA && j <= qt[0]) {
+          if (!mbar_wait(&bar_p[0], j & 1, p.status, 23)) break;
+          tc_fence_after();
+          if (j + 1 <= qt[0]) {
+            if (!item(fwd_k_item(j + 1), ka)) break;
+            issue_s(0, ka);
+          }
+          if (!item(fwd_v_item(j, n_kv), va)) break;
+          issue_pv(0, j, va);
+        }
+        if (!mbar_wait(&bar_p[1], j & 1, p.status, 24)) break;
         tc_fence_after();
-        if (j + 1 < n_kv) {
-          if (!take(ka)) break;
-#pragma unroll
-          for (int k = 0; k < 4; ++k)
-            mma_f16_ss(tS, sw128_desc(qa + k * 32, 16, 1024), sw128_desc(ka + k * 32, 16, 1024), idS, k > 0);
-          release();
-          mma_commit(&bar_s);
+        if (next) {
+          if (!item(fwd_k_item(j + 1), ka)) break;
+          issue_s(1, ka);
+          mma_commit(&bar_empty[fwd_k_item(j + 1) % FWD_SLOTS]);
         }
-        if (!take(va)) break;
-        const uint32_t tO = tO0 + (j & 1) * 64;
-#pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint64_t ad = sw128_desc(pa + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024);
-          const uint64_t bd = sw128_desc(va + ks * 2048, 8192, 1024);
-          mma_f16_ss(tO, ad, bd, idO, ks > 0);
-        }
-        release();
-        mma_commit(&bar_o[j & 1]);
+        if (!item(fwd_v_item(j, n_kv), va)) break;
+        issue_pv(1, j, va);
+        mma_commit(&bar_empty[fwd_v_item(j, n_kv) % FWD_SLOTS]);
       }
       mma_commit(&bar_done);
-      mbar_wait(&bar_done, 0, p.status, 24);
+      mbar_wait(&bar_done, 0, p.status, 25);
     }
   } else {
-    // Softmax / output warps: thread <-> query row.
+    const int g = (warp >= 6) ? 1 : 0;
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-    const int q = qt * kTile + row;
-    float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-    float o[64];
+    if (g == 1 || hasA) {
+      const int my_qt = qt[g];
+      const int n = my_qt + 1;
+      const int q = my_qt * kTile + row;
+      const uint32_t tS = tmem + g * 256, tO0 = tmem + g * 256 + 128;
+      uint8_t* myP = sP + g * 2 * kTileBytes;
+      float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+      float o[64];
 #pragma unroll
-    for (int i = 0; i < 64; ++i) o[i] = 0.f;
-    bool ok = true;
-    for (int j = 0; j < n_kv && ok; ++j) {
-      if (!mbar_wait(&bar_s, j & 1, p.status, 25)) {
-        ok = false;
-        break;
-      }
-      tc_fence_after();
-      const bool diag = (j == qt);
-      float v[32];
-      float mt = -INFINITY;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + lane_off + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = j * kTile + c * 32 + i;
-          const float s = (diag && key > q) ? -INFINITY : v[i] * p.scale_log2;
-          mt = fmaxf(mt, s);
+      for (int i = 0; i < 64; ++i) o[i] = 0.f;
+      bool ok = true;
+      for (int j = 0; j < n && ok; ++j) {
+        if (!mbar_wait(&bar_s[g], j & 1, p.status, 26)) {
+          ok = false;
+          break;
         }
-      }
-      const float m_new = fmaxf(m, mt);
-      const float alpha = (m == -INFINITY) ? 0.f : exp2f(m - m_new);
-      // P smem is free once PV_{j-1} has completed.
-      if (j > 0 && !mbar_wait(&bar_o[(j - 1) & 1], ((j - 1) >> 1) & 1, p.status, 26)) {
-        ok = false;
-        break;
-      }
-      float rs = 0.f;
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + lane_off + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int key = j * kTile + c * 32 + i;
-          const float pv = (diag && key > q) ? 0.f : exp2f(v[i] * p.scale_log2 - m_new);
-          v[i] = pv;
-          rs += pv;
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const uint4 pk = make_uint4(pack_bf16(v[g * 8 + 0], v[g * 8 + 1]), pack_bf16(v[g * 8 + 2], v[g * 8 + 3]),
-                                      pack_bf16(v[g * 8 + 4], v[g * 8 + 5]), pack_bf16(v[g * 8 + 6], v[g * 8 + 7]));
-          *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 4 + g)) = pk;
-        }
-      }
-      l = l * alpha + rs;
-      m = m_new;
-      fence_proxy_async_smem();
-      tc_fence_before();
-      __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_p);
-      if (j > 0) {
-        const uint32_t tO = tO0 + ((j - 1) & 1) * 64;
         tc_fence_after();
+        // P smem is free once PV_{j-1} has completed.
+        if (j > 0 && !mbar_wait(&bar_o[g][(j - 1) & 1], ((j - 1) >> 1) & 1, p.status, 27)) {
+          ok = false;
+          break;
+        }
+        const float alpha = (j == my_qt)
+                                ? softmax_tile<true>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l)
+                                : softmax_tile<false>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l);
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_p[g]);
+        if (j > 0) {
+          tc_fence_after();
+          float v[32];
+#pragma unroll
+          for (int c = 0; c < 2; ++c) {
+            tmem_ld32(tO0 + ((j - 1) & 1) * 64 + lane_off + c * 32, v);
+#pragma unroll
+            for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_prev, v[i]);
+          }
+        }
+        alpha_prev = alpha;
+      }
+      if (ok && mbar_wait(&bar_o[g][(n - 1) & 1], ((n - 1) >> 1) & 1, p.status, 28)) {
+        tc_fence_after();
+        float v[32];
 #pragma unroll
         for (int c = 0; c < 2; ++c) {
-          tmem_ld32(tO + lane_off + c * 32, v);
+          tmem_ld32(tO0 + ((n - 1) & 1) * 64 + lane_off + c * 32, v);
 #pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + v[i];
+          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_prev, v[i]);
         }
-      }
-      alpha_prev = alpha;
-    }
-    if (ok && mbar_wait(&bar_o[(n_kv - 1) & 1], ((n_kv - 1) >> 1) & 1, p.status, 27)) {
-      tc_fence_after();
-      const uint32_t tO = tO0 + ((n_kv - 1) & 1) * 64;
-      float v[32];
+        if (q < p.T) {
+          const float inv = 1.f / l;
+          __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD;
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        tmem_ld32(tO + lane_off + c * 32, v);
-#pragma unroll
-        for (int i = 0; i < 32; ++i) o[c * 32 + i] = o[c * 32 + i] * alpha_prev + v[i];
-      }
-      if (q < p.T) {
-        const float inv = 1.f / l;
-        __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD;
-#pragma unroll
-        for (int g = 0; g < 8; ++g) {
-          *reinterpret_cast<uint4*>(dst + g * 8) =
-              make_uint4(pack_bf16(o[g * 8 + 0] * inv, o[g * 8 + 1] * inv), pack_bf16(o[g * 8 + 2] * inv, o[g * 8 + 3] * inv),
-                         pack_bf16(o[g * 8 + 4] * inv, o[g * 8 + 5] * inv), pack_bf16(o[g * 8 + 6] * inv, o[g * 8 + 7] * inv));
+          for (int gg = 0; gg < 8; ++gg) {
+            *reinterpret_cast<uint4*>(dst + gg * 8) = make_uint4(
+                pack_bf16(o[gg * 8 + 0] * inv, o[gg * 8 + 1] * inv), pack_bf16(o[gg * 8 + 2] * inv, o[gg * 8 + 3] * inv),
+                pack_bf16(o[gg * 8 + 4] * inv, o[gg * 8 + 5] * inv), pack_bf16(o[gg * 8 + 6] * inv, o[gg * 8 + 7] * inv));
+          }
+          p.lse[((long)b * p.nh + h) * p.Tpad + q] = m + log2f(l);
         }
-        p.lse[((long)b * p.nh + h) * p.Tpad + q] = m + log2f(l);
       }
     }
     tc_fence_before();
@@ -289,19 +333,21 @@ __global__ void __launch_bounds__(192) attn_fwd_kernel(const __grid_constant__ C
   __syncthreads();
   if (warp == 1) {
     tc_fence_after();
-    tmem_dealloc(tmem, 256);
+    tmem_dealloc(tmem, 512);
   }
 }
 
 // ============================================================================
 // Backward
 // ============================================================================
-constexpr int BWD_STAGE = 2 * kTileBytes + 1024;  // Q_i, dO_i, lse_i (512 B), D_i (512 B)
+constexpr int BWD_STAGE = 2 * kTileBytes + 2048;  // Q_i, dO_i, lse_i (512 B), D_i (512 B), padded to 1 KB multiple
 constexpr int BWD_STAGES = 2;
+constexpr int BWD_THREADS = 320;
 constexpr int BWD_SMEM = 2 * kTileBytes /*K,V*/ + BWD_STAGES * BWD_STAGE + 4 * kTileBytes /*P^T, dS^T*/ + 1024;
 
-__global__ void __launch_bounds__(192) attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv,
-                                                       const __grid_constant__ CUtensorMap tm_do, AttnParams p) {
+__global__ void __launch_bounds__(BWD_THREADS, 1)
+    attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
+                    AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
@@ -309,13 +355,13 @@ __global__ void __launch_bounds__(192) attn_bwd_kernel(const __grid_constant__ C
   uint8_t* sStage = smem + 2 * kTileBytes;
   uint8_t* sP = sStage + BWD_STAGES * BWD_STAGE;
   uint8_t* sDS = sP + 2 * kTileBytes;
-  __shared__ uint64_t bar_kv, bar_full[BWD_STAGES], bar_empty[BWD_STAGES], bar_sdp, bar_p, bar_mma, bar_done;
+  __shared__ uint64_t bar_kv, bar_full[BWD_STAGES], bar_empty[BWD_STAGES], bar_h[2], bar_p[2], bar_mma, bar_done;
   __shared__ uint32_t tmem_slot;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = (p.T + kTile - 1) / kTile;
   int bid = blockIdx.x;
-  const int kt = bid % n_t;  // low key tiles have the most query tiles: launched first
+  const int kt = bid % n_t;
   bid /= n_t;
   const int h = bid % p.nh;
   const int b = bid / p.nh;
@@ -327,8 +373,10 @@ __global__ void __launch_bounds__(192) attn_bwd_kernel(const __grid_constant__ C
       mbar_init(&bar_full[s], 1);
       mbar_init(&bar_empty[s], 1);
     }
-    mbar_init(&bar_sdp, 1);
-    mbar_init(&bar_p, 4);
+    for (int g = 0; g < 2; ++g) {
+      mbar_init(&bar_h[g], 1);
+      mbar_init(&bar_p[g], 4);
+    }
     mbar_init(&bar_mma, 1);
     mbar_init(&bar_done, 1);
     fence_barrier_init();
@@ -351,164 +399,172 @@ __global__ void __launch_bounds__(192) attn_bwd_kernel(const __grid_constant__ C
       mbar_arrive_expect_tx(&bar_kv, 2 * kTileBytes);
       tma_load_3d(sK, &tm_qkv, &bar_kv, p.Hs + h * kD, kt * kTile, b);
       tma_load_3d(sV, &tm_qkv, &bar_kv, 2 * p.Hs + h * kD, kt * kTile, b);
-      int st = 0;
-      uint32_t phase = 0;
       for (int ii = 0; ii < n_i; ++ii) {
-        const int qi = kt + ii;
-        if (!mbar_wait(&bar_empty[st], phase ^ 1u, p.status, 40)) break;
+        const int qi = kt + ii, st = ii % BWD_STAGES;
+        if (!mbar_wait(&bar_empty[st], ((ii / BWD_STAGES) & 1) ^ 1u, p.status, 40)) break;
         uint8_t* s = sStage + st * BWD_STAGE;
         mbar_arrive_expect_tx(&bar_full[st], 2 * kTileBytes + 1024);
         tma_load_3d(s, &tm_qkv, &bar_full[st], h * kD, qi * kTile, b);
         tma_load_3d(s + kTileBytes, &tm_do, &bar_full[st], h * kD, qi * kTile, b);
         bulk_load(s + 2 * kTileBytes, p.lse + lse_base + qi * kTile, 512, &bar_full[st]);
         bulk_load(s + 2 * kTileBytes + 512, p.dvec + lse_base + qi * kTile, 512, &bar_full[st]);
-        if (++st == BWD_STAGES) {
-          st = 0;
-          phase ^= 1u;
-        }
       }
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idSS = make_idesc_f16(128, 128, false, false, true);  // S^T, dP^T
-      constexpr uint32_t idKM = make_idesc_f16(128, 64, false, true, true);    // dV, dK
-      constexpr uint32_t idQ = make_idesc_f16(128, 64, true, true, true);      // dQ
+      constexpr uint32_t idH = make_idesc_f16(128, 64, false, false, true);   // S^T / dP^T halves
+      constexpr uint32_t idKM = make_idesc_f16(128, 64, false, true, true);   // dV, dK
+      constexpr uint32_t idQ = make_idesc_f16(128, 64, true, true, true);     // dQ
       const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP), dsa = smem_u32(sDS);
-      int st = 0;
-      uint32_t phase = 0;
-      bool ok = mbar_wait(&bar_kv, 0, p.status, 41);
-      for (int ii = 0; ii < n_i && ok; ++ii) {
-        if (!mbar_wait(&bar_full[st], phase, p.status, 42)) break;
+      auto stage_ready = [&](int ii) -> bool {
+        if (!mbar_wait(&bar_full[ii % BWD_STAGES], (ii / BWD_STAGES) & 1, p.status, 41)) return false;
         tc_fence_after();
-        const uint32_t qa = smem_u32(sStage + st * BWD_STAGE);
+        return true;
+      };
+      auto issue_half = [&](int ii, int g) {
+        const uint32_t qa = smem_u32(sStage + (ii % BWD_STAGES) * BWD_STAGE) + g * 8192;
         const uint32_t doa = qa + kTileBytes;
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_f16_ss(tS, sw128_desc(ka + k * 32, 16, 1024), sw128_desc(qa + k * 32, 16, 1024), idSS, k > 0);
+          mma_f16_ss(tS + g * 64, sw128_desc(ka + k * 32, 16, 1024), sw128_desc(qa + k * 32, 16, 1024), idH, k > 0);
 #pragma unroll
         for (int k = 0; k < 4; ++k)
-          mma_f16_ss(tDP, sw128_desc(va + k * 32, 16, 1024), sw128_desc(doa + k * 32, 16, 1024), idSS, k > 0);
-        mma_commit(&bar_sdp);
-        if (!mbar_wait(&bar_p, ii & 1, p.status, 43)) break;
+          mma_f16_ss(tDP + g * 64, sw128_desc(va + k * 32, 16, 1024), sw128_desc(doa + k * 32, 16, 1024), idH, k > 0);
+        mma_commit(&bar_h[g]);
+      };
+      bool ok = mbar_wait(&bar_kv, 0, p.status, 42) && stage_ready(0);
+      if (ok) {
+        issue_half(0, 0);
+        issue_half(0, 1);
+      }
+      for (int ii = 0; ii < n_i && ok; ++ii) {
+        const uint32_t qa = smem_u32(sStage + (ii % BWD_STAGES) * BWD_STAGE);
+        const uint32_t doa = qa + kTileBytes;
+        // half 0 of P^T / dS^T (queries 0..63) is in smem
+        if (!mbar_wait(&bar_p[0], ii & 1, p.status, 43)) break;
         tc_fence_after();
 #pragma unroll
-        for (int ks = 0; ks < 8; ++ks) {
-          const uint32_t aoff = (ks >> 2) * 16384 + (ks & 3) * 32;
-          // dV += P^T dO_i   (B = dO_i viewed MN-major: N = d, K = query)
-          mma_f16_ss(tDV, sw128_desc(pa + aoff, 16, 1024), sw128_desc(doa + ks * 2048, 8192, 1024), idKM,
+        for (int ks = 0; ks < 4; ++ks) {
+          mma_f16_ss(tDV, sw128_desc(pa + ks * 32, 16, 1024), sw128_desc(doa + ks * 2048, 8192, 1024), idKM,
                      (ii > 0 || ks > 0));
-          // dK += dS^T Q_i
-          mma_f16_ss(tDK, sw128_desc(dsa + aoff, 16, 1024), sw128_desc(qa + ks * 2048, 8192, 1024), idKM,
+          mma_f16_ss(tDK, sw128_desc(dsa + ks * 32, 16, 1024), sw128_desc(qa + ks * 2048, 8192, 1024), idKM,
                      (ii > 0 || ks > 0));
-          // dQ_i = dS K   (A = dS^T viewed MN-major: M = query, K = key)
+        }
+        const bool next = ii + 1 < n_i;
+        if (next) {
+          if (!stage_ready(ii + 1)) break;
+          issue_half(ii + 1, 0);
+        }
+        if (!mbar_wait(&bar_p[1], ii & 1, p.status, 44)) break;
+        tc_fence_after();
+#pragma unroll
+        for (int ks = 4; ks < 8; ++ks) {
+          mma_f16_ss(tDV, sw128_desc(pa + 16384 + (ks - 4) * 32, 16, 1024), sw128_desc(doa + ks * 2048, 8192, 1024),
+                     idKM, 1u);
+          mma_f16_ss(tDK, sw128_desc(dsa + 16384 + (ks - 4) * 32, 16, 1024), sw128_desc(qa + ks * 2048, 8192, 1024),
+                     idKM, 1u);
+        }
+#pragma unroll
+        for (int ks = 0; ks < 8; ++ks)
           mma_f16_ss(tDQ, sw128_desc(dsa + ks * 2048, 16384, 1024), sw128_desc(ka + ks * 2048, 8192, 1024), idQ,
                      ks > 0);
-        }
-        mma_commit(&bar_empty[st]);
         mma_commit(&bar_mma);
-        if (++st == BWD_STAGES) {
-          st = 0;
-          phase ^= 1u;
-        }
+        mma_commit(&bar_empty[ii % BWD_STAGES]);
+        if (next) issue_half(ii + 1, 1);
       }
       mma_commit(&bar_done);
-      mbar_wait(&bar_done, 0, p.status, 44);
+      mbar_wait(&bar_done, 0, p.status, 45);
     }
   } else {
+    const int g = (warp >= 6) ? 1 : 0;  // query half handled by this warpgroup
     const int sub = warp & 3;
-    const int r = sub * 32 + lane;  // key row for S^T/dP^T/dK/dV, query row for dQ
+    const int r = sub * 32 + lane;  // key row (S^T, dP^T, dK, dV) / query row (dQ)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const int key = kt * kTile + r;
-    int st = 0;
-    uint32_t phase = 0;
     bool ok = true;
     auto flush_dq = [&](int qi) {
-      // dQ_i (fp32, TMEM) -> global accumulator.
       tc_fence_after();
       const int qrow = qi * kTile + r;
       float v[32];
-#pragma unroll 1
-      for (int c = 0; c < 2; ++c) {
-        tmem_ld32(tDQ + lane_off + c * 32, v);
-        if (qrow < p.T) {
-          float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((long)b * p.T + qrow) * p.Hs + h * kD + c * 32);
+      tmem_ld32(tDQ + g * 32 + lane_off, v);
+      if (qrow < p.T) {
+        float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((long)b * p.T + qrow) * p.Hs + h * kD + g * 32);
 #pragma unroll
-          for (int g = 0; g < 8; ++g) atomicAdd(dst + g, make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]));
-        }
+        for (int q4 = 0; q4 < 8; ++q4)
+          atomicAdd(dst + q4, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
       }
     };
     for (int ii = 0; ii < n_i && ok; ++ii) {
-      const int qi = kt + ii;
-      if (!mbar_wait(&bar_full[st], phase, p.status, 45) || !mbar_wait(&bar_sdp, ii & 1, p.status, 46)) {
+      const int qi = kt + ii, st = ii % BWD_STAGES;
+      if (!mbar_wait(&bar_full[st], (ii / BWD_STAGES) & 1, p.status, 46) ||
+          !mbar_wait(&bar_h[g], ii & 1, p.status, 47)) {
         ok = false;
         break;
       }
       tc_fence_after();
-      const float* s_lse = reinterpret_cast<const float*>(sStage + st * BWD_STAGE + 2 * kTileBytes);
+      const float* s_lse = reinterpret_cast<const float*>(sStage + st * BWD_STAGE + 2 * kTileBytes) + g * 64;
       const float* s_d = s_lse + 128;
-      // P^T / dS^T smem and the dQ TMEM columns are free once the MMAs of the
-      // previous query tile are complete; flush that tile's dQ first.
+      const bool diag = (qi == kt);
+      // P^T and dS^T of this half, packed to bf16 in registers.
+      uint32_t pk[2][32];
+#pragma unroll
+      for (int c = 0; c < 2; ++c) {
+        float sv[32], dp[32];
+        tmem_ld32(tS + g * 64 + c * 32 + lane_off, sv);
+        tmem_ld32(tDP + g * 64 + c * 32 + lane_off, dp);
+#pragma unroll
+        for (int i = 0; i < 32; i += 2) {
+          float pr[2], ds[2];
+#pragma unroll
+          for (int e = 0; e < 2; ++e) {
+            const int col = c * 32 + i + e;
+            const int qq = qi * kTile + g * 64 + col;
+            const bool masked = (diag && key > qq) || qq >= p.T;
+            const float pv = fast_exp2(fmaf(sv[i + e], p.scale_log2, -s_lse[col]));
+            pr[e] = masked ? 0.f : pv;
+            ds[e] = masked ? 0.f : pv * (dp[i + e] - s_d[col]) * p.scale;
+          }
+          pk[0][c * 16 + i / 2] = pack_bf16(pr[0], pr[1]);
+          pk[1][c * 16 + i / 2] = pack_bf16(ds[0], ds[1]);
+        }
+      }
+      // The previous tile's MMAs read P^T / dS^T smem and wrote dQ: wait,
+      // flush that dQ half, then overwrite this half of P^T / dS^T.
       if (ii > 0) {
-        if (!mbar_wait(&bar_mma, (ii - 1) & 1, p.status, 47)) {
+        if (!mbar_wait(&bar_mma, (ii - 1) & 1, p.status, 48)) {
           ok = false;
           break;
         }
         flush_dq(qi - 1);
       }
-      const bool diag = (qi == kt);
-      float sv[32], dp[32];
-#pragma unroll 1
-      for (int c = 0; c < 4; ++c) {
-        tmem_ld32(tS + lane_off + c * 32, sv);
-        tmem_ld32(tDP + lane_off + c * 32, dp);
 #pragma unroll
-        for (int i = 0; i < 32; ++i) {
-          const int qq = qi * kTile + c * 32 + i;
-          const bool masked = (diag && key > qq) || qq >= p.T;
-          const float pr = masked ? 0.f : exp2f(sv[i] * p.scale_log2 - s_lse[c * 32 + i]);
-          sv[i] = pr;
-          dp[i] = masked ? 0.f : pr * (dp[i] - s_d[c * 32 + i]) * p.scale;
-        }
-#pragma unroll
-        for (int g = 0; g < 4; ++g) {
-          const uint32_t off = sw128_off(r, c * 4 + g);
-          *reinterpret_cast<uint4*>(sP + off) =
-              make_uint4(pack_bf16(sv[g * 8 + 0], sv[g * 8 + 1]), pack_bf16(sv[g * 8 + 2], sv[g * 8 + 3]),
-                         pack_bf16(sv[g * 8 + 4], sv[g * 8 + 5]), pack_bf16(sv[g * 8 + 6], sv[g * 8 + 7]));
-          *reinterpret_cast<uint4*>(sDS + off) =
-              make_uint4(pack_bf16(dp[g * 8 + 0], dp[g * 8 + 1]), pack_bf16(dp[g * 8 + 2], dp[g * 8 + 3]),
-                         pack_bf16(dp[g * 8 + 4], dp[g * 8 + 5]), pack_bf16(dp[g * 8 + 6], dp[g * 8 + 7]));
-        }
+      for (int c16 = 0; c16 < 8; ++c16) {
+        const uint32_t off = sw128_off(r, g * 8 + c16);
+        *reinterpret_cast<uint4*>(sP + off) =
+            make_uint4(pk[0][c16 * 4], pk[0][c16 * 4 + 1], pk[0][c16 * 4 + 2], pk[0][c16 * 4 + 3]);
+        *reinterpret_cast<uint4*>(sDS + off) =
+            make_uint4(pk[1][c16 * 4], pk[1][c16 * 4 + 1], pk[1][c16 * 4 + 2], pk[1][c16 * 4 + 3]);
       }
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
-      if (lane == 0) mbar_arrive(&bar_p);
-      if (++st == BWD_STAGES) {
-        st = 0;
-        phase ^= 1u;
-      }
+      if (lane == 0) mbar_arrive(&bar_p[g]);
     }
-    if (ok && mbar_wait(&bar_mma, (n_i - 1) & 1, p.status, 48)) {
+    if (ok && mbar_wait(&bar_mma, (n_i - 1) & 1, p.status, 49)) {
       flush_dq(kt + n_i - 1);
-      // dK, dV -> bf16 into the K / V columns of dqkv (tcgen05.ld is
-      // warp-collective, so every lane loads; only rows < T store).
+      // dK, dV columns [g*32, g*32+32) -> bf16 into the K / V columns of dqkv.
       __nv_bfloat16* drow = p.out + ((long)b * p.T + key) * p.ld_out;
       float v[32];
 #pragma unroll 1
       for (int which = 0; which < 2; ++which) {
-        const uint32_t tsrc = which == 0 ? tDK : tDV;
-        __nv_bfloat16* dst = drow + (which == 0 ? p.Hs : 2 * p.Hs) + h * kD;
-#pragma unroll 1
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(tsrc + lane_off + c * 32, v);
-          if (key < p.T) {
+        tmem_ld32((which == 0 ? tDK : tDV) + g * 32 + lane_off, v);
+        if (key < p.T) {
+          __nv_bfloat16* dst = drow + (which == 0 ? p.Hs : 2 * p.Hs) + h * kD + g * 32;
 #pragma unroll
-            for (int g = 0; g < 4; ++g)
-              *reinterpret_cast<uint4*>(dst + c * 32 + g * 8) =
-                  make_uint4(pack_bf16(v[g * 8 + 0], v[g * 8 + 1]), pack_bf16(v[g * 8 + 2], v[g * 8 + 3]),
-                             pack_bf16(v[g * 8 + 4], v[g * 8 + 5]), pack_bf16(v[g * 8 + 6], v[g * 8 + 7]));
-          }
+          for (int q8 = 0; q8 < 4; ++q8)
+            *reinterpret_cast<uint4*>(dst + q8 * 8) =
+                make_uint4(pack_bf16(v[q8 * 8 + 0], v[q8 * 8 + 1]), pack_bf16(v[q8 * 8 + 2], v[q8 * 8 + 3]),
+                           pack_bf16(v[q8 * 8 + 4], v[q8 * 8 + 5]), pack_bf16(v[q8 * 8 + 6], v[q8 * 8 + 7]));
         }
       }
     }
@@ -578,7 +634,8 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   p.status = status;
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
-  attn_fwd_kernel<<<B * nh * n_qt, 192, FWD_SMEM, s>>>(tm, p);
+  const int n_pairs = (n_qt + 1) / 2;
+  attn_fwd_kernel<<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -604,7 +661,7 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   const CUtensorMap tq = qkv_map(qkv, B, T, ld_qkv, 3 * Hs);
   const CUtensorMap td = qkv_map(dO, B, T, ld_do, Hs);
   const int n_t = (T + kTile - 1) / kTile;
-  attn_bwd_kernel<<<B * nh * n_t, 192, BWD_SMEM, s>>>(tq, td, p);
+  attn_bwd_kernel<<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, p);
   HB_CUDA_CHECK(cudaGetLastError());
   attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
   HB_CUDA_CHECK(cudaGetLastError());

@@ -25,6 +25,10 @@
 
 namespace hb {
 
+constexpr int kStgRowF32 = 144;   // bytes per staged row, fp32 view (32 + 4 floats)
+constexpr int kStgRowBf16 = 80;   // bytes per staged row, bf16 view (32 + 8 halves)
+constexpr int kStgBytes = 32 * kStgRowF32;  // per warp
+
 template <int BN>
 struct GemmCfg {
   static constexpr int BM = 128;
@@ -34,16 +38,112 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // 4 per-warp epilogue staging tiles
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 4 * kStgBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
+// ---------------------------------------------------------------------------
+// Epilogue. Each epilogue warp owns 32 accumulator rows (its TMEM lane
+// quarter) and processes 32 columns at a time: thread t holds row t's 32
+// values after tcgen05.ld. Global traffic goes through a per-warp staging
+// tile in shared memory, so every global load/store is coalesced (lanes
+// cover consecutive 16-byte segments of a row) while the arithmetic stays
+// row-per-thread. Staging rows are padded (fp32: 144 B, bf16: 80 B) so both
+// access patterns are free of bank conflicts.
+// ---------------------------------------------------------------------------
+
+// Coalesced copy global -> staging of a [32 rows][32 cols] tile (rows from m_base).
+template <bool F32>
+__device__ __forceinline__ void stg_load(uint8_t* stg, const void* src, long ld, int m_base, int n0, int M, int N,
+                                         int lane) {
+  constexpr int SEGS = F32 ? 8 : 4;  // 16-byte segments per row
+  constexpr int ESZ = F32 ? 4 : 2;
+  constexpr int ROWB = F32 ? kStgRowF32 : kStgRowBf16;
+#pragma unroll
+  for (int it = 0; it < SEGS; ++it) {
+    const int idx = it * 32 + lane;
+    const int r = idx / SEGS, seg = idx % SEGS;
+    const int gm = m_base + r, gn = n0 + seg * (16 / ESZ);
+    uint4 val = make_uint4(0, 0, 0, 0);
+    if (gm < M && gn < N)
+      val = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(src) + ((long)gm * ld + gn) * ESZ);
+    *reinterpret_cast<uint4*>(stg + r * ROWB + seg * 16) = val;
+  }
+}
+
+// Coalesced copy staging -> global.
+template <bool F32>
+__device__ __forceinline__ void stg_store(const uint8_t* stg, void* dst, long ld, int m_base, int n0, int M, int N,
+                                          int lane) {
+  constexpr int SEGS = F32 ? 8 : 4;
+  constexpr int ESZ = F32 ? 4 : 2;
+  constexpr int ROWB = F32 ? kStgRowF32 : kStgRowBf16;
+#pragma unroll
+  for (int it = 0; it < SEGS; ++it) {
+    const int idx = it * 32 + lane;
+    const int r = idx / SEGS, seg = idx % SEGS;
+    const int gm = m_base + r, gn = n0 + seg * (16 / ESZ);
+    if (gm < M && gn < N)
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst) + ((long)gm * ld + gn) * ESZ) =
+          *reinterpret_cast<const uint4*>(stg + r * ROWB + seg * 16);
+  }
+}
+
+// Row-per-thread write of 32 values into this thread's staging row.
+__device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float (&v)[32]) {
+  uint8_t* row = stg + lane * kStgRowBf16;
+#pragma unroll
+  for (int g = 0; g < 4; ++g)
+    *reinterpret_cast<uint4*>(row + g * 16) =
+        make_uint4(pack_bf16(v[8 * g], v[8 * g + 1]), pack_bf16(v[8 * g + 2], v[8 * g + 3]),
+                   pack_bf16(v[8 * g + 4], v[8 * g + 5]), pack_bf16(v[8 * g + 6], v[8 * g + 7]));
+}
+__device__ __forceinline__ void stg_put_f32(uint8_t* stg, int lane, const float (&v)[32]) {
+  uint8_t* row = stg + lane * kStgRowF32;
+#pragma unroll
+  for (int g = 0; g < 8; ++g)
+    *reinterpret_cast<float4*>(row + g * 16) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+}
+
 template <int EPI>
-__device__ __forceinline__ void gemm_epilogue_store(const GemmParams& p, int m, int n0, float (&v)[32]) {
+__device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int m_base, int n0, float (&v)[32],
+                                                    uint8_t* stg, int lane) {
+  // 1. operands read by the epilogue: staged, then each thread takes its row.
+  if constexpr (EPI == kEpiF32Resid || EPI == kEpiF32Acc) {
+    const float* src = (EPI == kEpiF32Resid) ? p.resid : reinterpret_cast<const float*>(p.C);
+    const long ld = (EPI == kEpiF32Resid) ? p.ldr : p.ldc;
+    stg_load<true>(stg, src, ld, m_base, n0, p.M, p.N, lane);
+    __syncwarp();
+    const uint8_t* row = stg + lane * kStgRowF32;
+#pragma unroll
+    for (int g = 0; g < 8; ++g) {
+      const float4 r = *reinterpret_cast<const float4*>(row + g * 16);
+      v[4 * g] += r.x;
+      v[4 * g + 1] += r.y;
+      v[4 * g + 2] += r.z;
+      v[4 * g + 3] += r.w;
+    }
+    __syncwarp();
+  }
+  if constexpr (EPI == kEpiBf16Dgelu) {
+    stg_load<false>(stg, p.aux, p.ldaux, m_base, n0, p.M, p.N, lane);
+    __syncwarp();
+    const uint8_t* row = stg + lane * kStgRowBf16;
+#pragma unroll
+    for (int g = 0; g < 4; ++g) {
+      const uint4 raw = *reinterpret_cast<const uint4*>(row + g * 16);
+      const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+#pragma unroll
+      for (int q = 0; q < 8; ++q) v[8 * g + q] *= gelu_tanh_grad(__bfloat162float(pb[q]));
+    }
+    __syncwarp();
+  }
+  // 2. bias
   if (p.bias != nullptr && (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       if (n0 + j < p.N) {
-        float4 b = *reinterpret_cast<const float4*>(p.bias + n0 + j);
+        const float4 b = *reinterpret_cast<const float4*>(p.bias + n0 + j);
         v[j] += b.x;
         v[j + 1] += b.y;
         v[j + 2] += b.z;
@@ -51,61 +151,29 @@ __device__ __forceinline__ void gemm_epilogue_store(const GemmParams& p, int m, 
       }
     }
   }
-  if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiBf16Dgelu) {
-    __nv_bfloat16* crow = reinterpret_cast<__nv_bfloat16*>(p.C) + (long)m * p.ldc + n0;
-    __nv_bfloat16* arow =
-        (EPI != kEpiBf16) ? reinterpret_cast<__nv_bfloat16*>(p.aux) + (long)m * p.ldaux + n0 : nullptr;
+  // 3. outputs
+  if constexpr (EPI == kEpiBf16Gelu) {
+    // Pre-activation (rounded to bf16) goes to AUX; GELU of that rounded value
+    // goes to C, so backward differentiates exactly what forward applied.
 #pragma unroll
-    for (int j = 0; j < 32; j += 8) {
-      if (n0 + j >= p.N) break;
-      uint4 out;
-      if constexpr (EPI == kEpiBf16) {
-        out = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]), pack_bf16(v[j + 4], v[j + 5]),
-                         pack_bf16(v[j + 6], v[j + 7]));
-      } else if constexpr (EPI == kEpiBf16Gelu) {
-        uint4 pre = make_uint4(pack_bf16(v[j], v[j + 1]), pack_bf16(v[j + 2], v[j + 3]),
-                               pack_bf16(v[j + 4], v[j + 5]), pack_bf16(v[j + 6], v[j + 7]));
-        *reinterpret_cast<uint4*>(arow + j) = pre;
-        // GELU of the bf16-rounded pre-activation, so that backward (which
-        // only sees the stored bf16 value) differentiates the same function.
-        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pre);
-        float g[8];
+    for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
+    stg_put_bf16(stg, lane, v);
+    __syncwarp();
+    stg_store<false>(stg, p.aux, p.ldaux, m_base, n0, p.M, p.N, lane);
+    __syncwarp();
 #pragma unroll
-        for (int q = 0; q < 8; ++q) g[q] = gelu_tanh(__bfloat162float(pb[q]));
-        out = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
-      } else {  // dgelu
-        uint4 pre = *reinterpret_cast<const uint4*>(arow + j);
-        const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&pre);
-        float g[8];
-#pragma unroll
-        for (int q = 0; q < 8; ++q) g[q] = v[j + q] * gelu_tanh_grad(__bfloat162float(pb[q]));
-        out = make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
-      }
-      *reinterpret_cast<uint4*>(crow + j) = out;
-    }
-  } else {
-    float* crow = reinterpret_cast<float*>(p.C) + (long)m * p.ldc + n0;
-    const float* rrow = (EPI == kEpiF32Resid) ? p.resid + (long)m * p.ldr + n0 : nullptr;
-#pragma unroll
-    for (int j = 0; j < 32; j += 4) {
-      if (n0 + j >= p.N) break;
-      float4 o = make_float4(v[j], v[j + 1], v[j + 2], v[j + 3]);
-      if constexpr (EPI == kEpiF32Acc) {
-        float4 c = *reinterpret_cast<const float4*>(crow + j);
-        o.x += c.x;
-        o.y += c.y;
-        o.z += c.z;
-        o.w += c.w;
-      } else if constexpr (EPI == kEpiF32Resid) {
-        float4 r = *reinterpret_cast<const float4*>(rrow + j);
-        o.x += r.x;
-        o.y += r.y;
-        o.z += r.z;
-        o.w += r.w;
-      }
-      *reinterpret_cast<float4*>(crow + j) = o;
-    }
+    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
   }
+  if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiBf16Dgelu) {
+    stg_put_bf16(stg, lane, v);
+    __syncwarp();
+    stg_store<false>(stg, p.C, p.ldc, m_base, n0, p.M, p.N, lane);
+  } else {
+    stg_put_f32(stg, lane, v);
+    __syncwarp();
+    stg_store<true>(stg, p.C, p.ldc, m_base, n0, p.M, p.N, lane);
+  }
+  __syncwarp();
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
@@ -118,7 +186,7 @@ __global__ void __launch_bounds__(192, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + STAGES * STAGE_BYTES);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STG_OFFSET + 4 * kStgBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -239,7 +307,7 @@ __global__ void __launch_bounds__(192, 1)
     }
   } else {
     const int sub = warp & 3;
-    const int row = sub * 32 + lane;
+    uint8_t* stg = smem + Cfg::STG_OFFSET + sub * kStgBytes;
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -247,14 +315,14 @@ __global__ void __launch_bounds__(192, 1)
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
       tc_fence_after();
       const int mb = t % num_m, nb = t / num_m;
-      const int m = mb * BM + row;
+      const int m_base = mb * BM + sub * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int n0 = nb * BN + c * 32;
         if (n0 >= p.N) break;
         float v[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN + c * 32, v);
-        if (m < p.M) gemm_epilogue_store<EPI>(p, m, n0, v);
+        gemm_epilogue_chunk<EPI>(p, m_base, n0, v, stg, lane);
       }
       tc_fence_before();
       __syncwarp();

@@ -3,8 +3,8 @@
 // Replaces nn.LayerNorm (reference gpt_model.py:111-119, :237, pipeline.py:83)
 // and the bias-gradient reductions autograd performs for tp_linear.py:226/:310.
 //
-// Layout: rows of H contiguous elements. One warp per row; each lane keeps its
-// share of the row in registers as float4 (H % 4 == 0, H <= 32*4*MAXV), so the
+// Layout: rows of H contiguous elements (H % 4 == 0, H <= 2048). One warp per
+// row; each lane keeps its share of the row in registers as float4, so the
 // row is read from HBM once and written once.
 #include <cuda_bf16.h>
 
@@ -13,32 +13,37 @@
 
 namespace hb {
 
-constexpr int LN_MAXV = 16;  // float4 per lane: H <= 2048
+// Rows are processed one per warp; each lane holds V4 float4 of the row
+// (V4 = ceil(H / 128), a template parameter so no register is wasted).
+// The backward kernel handles LN_BWD_ROWS rows per warp with all loads of a
+// row issued before any arithmetic, and writes one partial (dgamma, dbeta)
+// row per CTA; a second kernel reduces the partials in a fixed order.
+constexpr int LN_ROWS_PER_CTA = 8;   // forward: 8 warps, one row each
+constexpr int LN_BWD_WARPS = 8;
+constexpr int LN_BWD_ROWS = 4;       // rows per warp in backward
 
-// x fp32 [M, H] -> y bf16 [M, H]; mean, rstd fp32 [M].
+template <int V4>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                      const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
                                                      float* __restrict__ mean_out, float* __restrict__ rstd_out,
                                                      int M, int H, float eps) {
-  const int warp = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int row = blockIdx.x * LN_ROWS_PER_CTA + (threadIdx.x >> 5);
   const int lane = threadIdx.x & 31;
-  if (warp >= M) return;
+  if (row >= M) return;
   const int H4 = H >> 2;
-  const float4* xr = reinterpret_cast<const float4*>(x + (long)warp * H);
-  float4 v[LN_MAXV];
+  const float4* xr = reinterpret_cast<const float4*>(x + (long)row * H);
+  float4 v[V4];
   float s = 0.f;
 #pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) {
+  for (int i = 0; i < V4; ++i) {
     const int j = lane + 32 * i;
-    if (j < H4) {
-      v[i] = xr[j];
-      s += v[i].x + v[i].y + v[i].z + v[i].w;
-    }
+    v[i] = (j < H4) ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
   }
   const float mu = warp_sum(s) / H;
   float ss = 0.f;
 #pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) {
+  for (int i = 0; i < V4; ++i) {
     const int j = lane + 32 * i;
     if (j < H4) {
       const float a = v[i].x - mu, c = v[i].y - mu, d = v[i].z - mu, e = v[i].w - mu;
@@ -48,9 +53,9 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
   const float rstd = rsqrtf(warp_sum(ss) / H + eps);
   const float4* w4 = reinterpret_cast<const float4*>(w);
   const float4* b4 = reinterpret_cast<const float4*>(b);
-  uint2* yr = reinterpret_cast<uint2*>(y + (long)warp * H);
+  uint2* yr = reinterpret_cast<uint2*>(y + (long)row * H);
 #pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) {
+  for (int i = 0; i < V4; ++i) {
     const int j = lane + 32 * i;
     if (j < H4) {
       const float4 ww = w4[j], bb = b4[j];
@@ -62,105 +67,112 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
     }
   }
   if (lane == 0) {
-    mean_out[warp] = mu;
-    rstd_out[warp] = rstd;
+    mean_out[row] = mu;
+    rstd_out[row] = rstd;
   }
 }
 
 // Backward. dy fp32 [M, H] (gradient of the LN output), x fp32 [M, H].
-//   dres fp32 [M, H] += dx         (residual-stream gradient, updated in place)
-//   dres16 bf16 [M, H] = dres      (operand copy for the next dgrad/wgrad GEMMs)
-//   part fp32 [gridDim.x, 2, H]    per-CTA partial dgamma (row 0) and dbeta (row 1)
-// If `dres_in` differs from `dres`, the result is dres = dres_in + dx.
+//   dres fp32 [M, H] = dres_in + dx   (dres may alias dres_in: residual gradient in place)
+//   dres16 bf16 [M, H] = dres          (operand copy for the next dgrad/wgrad GEMMs)
+//   part fp32 [gridDim.x, 2, H]        per-CTA partial dgamma (row 0) and dbeta (row 1)
+// Per-CTA partials are accumulated with shared-memory atomics (no per-thread
+// accumulators), which keeps registers low enough for 3 CTAs per SM.
+template <int V4>
 __global__ void __launch_bounds__(256) ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
                                                      const float* __restrict__ w, const float* dres_in,
                                                      float* dres, __nv_bfloat16* __restrict__ dres16,
-                                                     float* __restrict__ part, int M, int H, int rows_per_cta) {
-  extern __shared__ float sred[];  // [8 warps][2][H]
+                                                     float* __restrict__ part, int M, int H) {
+  extern __shared__ float sacc[];  // [2][H]: dgamma, dbeta partials of this CTA
   const int warp_in = threadIdx.x >> 5;
-  const int nwarps = blockDim.x >> 5;
   const int lane = threadIdx.x & 31;
   const int H4 = H >> 2;
+  for (int c = threadIdx.x; c < 2 * H; c += blockDim.x) sacc[c] = 0.f;
+  __syncthreads();
   const float4* w4 = reinterpret_cast<const float4*>(w);
-  float4 dg[LN_MAXV], db[LN_MAXV];
-#pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) {
-    dg[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-    db[i] = make_float4(0.f, 0.f, 0.f, 0.f);
-  }
-  const int row0 = blockIdx.x * rows_per_cta;
-  const int row1 = min(M, row0 + rows_per_cta);
-  for (int r = row0 + warp_in; r < row1; r += nwarps) {
+  const int row0 = (blockIdx.x * LN_BWD_WARPS + warp_in) * LN_BWD_ROWS;
+#pragma unroll 1
+  for (int rr = 0; rr < LN_BWD_ROWS; ++rr) {
+    const int r = row0 + rr;
+    if (r >= M) break;
     const float4* xr = reinterpret_cast<const float4*>(x + (long)r * H);
     const float4* dyr = reinterpret_cast<const float4*>(dy + (long)r * H);
+    float4 xv[V4], dv[V4];
+#pragma unroll
+    for (int i = 0; i < V4; ++i) {
+      const int j = lane + 32 * i;
+      const bool in = j < H4;
+      xv[i] = in ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      dv[i] = in ? dyr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+    }
     const float mu = mean[r], rs = rstd[r];
-    float4 xh[LN_MAXV], g[LN_MAXV];
     float s1 = 0.f, s2 = 0.f;
 #pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i) {
+    for (int i = 0; i < V4; ++i) {
       const int j = lane + 32 * i;
+      xv[i] = make_float4((xv[i].x - mu) * rs, (xv[i].y - mu) * rs, (xv[i].z - mu) * rs, (xv[i].w - mu) * rs);
       if (j < H4) {
-        const float4 xv = xr[j], d = dyr[j], ww = w4[j];
-        xh[i] = make_float4((xv.x - mu) * rs, (xv.y - mu) * rs, (xv.z - mu) * rs, (xv.w - mu) * rs);
-        g[i] = make_float4(d.x * ww.x, d.y * ww.y, d.z * ww.z, d.w * ww.w);
-        s1 += g[i].x + g[i].y + g[i].z + g[i].w;
-        s2 += g[i].x * xh[i].x + g[i].y * xh[i].y + g[i].z * xh[i].z + g[i].w * xh[i].w;
-        dg[i].x += d.x * xh[i].x;
-        dg[i].y += d.y * xh[i].y;
-        dg[i].z += d.z * xh[i].z;
-        dg[i].w += d.w * xh[i].w;
-        db[i].x += d.x;
-        db[i].y += d.y;
-        db[i].z += d.z;
-        db[i].w += d.w;
+        float* g = sacc + 4 * j;
+        float* bsum = sacc + H + 4 * j;
+        atomicAdd(g + 0, dv[i].x * xv[i].x);
+        atomicAdd(g + 1, dv[i].y * xv[i].y);
+        atomicAdd(g + 2, dv[i].z * xv[i].z);
+        atomicAdd(g + 3, dv[i].w * xv[i].w);
+        atomicAdd(bsum + 0, dv[i].x);
+        atomicAdd(bsum + 1, dv[i].y);
+        atomicAdd(bsum + 2, dv[i].z);
+        atomicAdd(bsum + 3, dv[i].w);
+        const float4 ww = w4[j];
+        dv[i] = make_float4(dv[i].x * ww.x, dv[i].y * ww.y, dv[i].z * ww.z, dv[i].w * ww.w);  // g = dy * w
       }
+      s1 += dv[i].x + dv[i].y + dv[i].z + dv[i].w;
+      s2 += dv[i].x * xv[i].x + dv[i].y * xv[i].y + dv[i].z * xv[i].z + dv[i].w * xv[i].w;
     }
     const float m1 = warp_sum(s1) / H, m2 = warp_sum(s2) / H;
     const float4* rin = reinterpret_cast<const float4*>(dres_in + (long)r * H);
     float4* rout = reinterpret_cast<float4*>(dres + (long)r * H);
     uint2* r16 = reinterpret_cast<uint2*>(dres16 + (long)r * H);
 #pragma unroll
-    for (int i = 0; i < LN_MAXV; ++i) {
+    for (int i = 0; i < V4; ++i) {
       const int j = lane + 32 * i;
       if (j < H4) {
         float4 o = rin[j];
-        o.x += rs * (g[i].x - m1 - xh[i].x * m2);
-        o.y += rs * (g[i].y - m1 - xh[i].y * m2);
-        o.z += rs * (g[i].z - m1 - xh[i].z * m2);
-        o.w += rs * (g[i].w - m1 - xh[i].w * m2);
+        o.x += rs * (dv[i].x - m1 - xv[i].x * m2);
+        o.y += rs * (dv[i].y - m1 - xv[i].y * m2);
+        o.z += rs * (dv[i].z - m1 - xv[i].z * m2);
+        o.w += rs * (dv[i].w - m1 - xv[i].w * m2);
         rout[j] = o;
         r16[j] = make_uint2(pack_bf16(o.x, o.y), pack_bf16(o.z, o.w));
       }
     }
   }
-  // Reduce the per-warp partials through shared memory.
-  float* mine = sred + warp_in * 2 * H;
-#pragma unroll
-  for (int i = 0; i < LN_MAXV; ++i) {
-    const int j = lane + 32 * i;
-    if (j < H4) {
-      reinterpret_cast<float4*>(mine)[j] = dg[i];
-      reinterpret_cast<float4*>(mine + H)[j] = db[i];
-    }
-  }
   __syncthreads();
-  for (int c = threadIdx.x; c < 2 * H; c += blockDim.x) {
-    float acc = 0.f;
-    for (int q = 0; q < nwarps; ++q) acc += sred[q * 2 * H + c];
-    part[(long)blockIdx.x * 2 * H + c] = acc;
-  }
+  float* out = part + (long)blockIdx.x * 2 * H;
+  for (int c = threadIdx.x; c < 2 * H; c += blockDim.x) out[c] = sacc[c];
 }
 
-// out[c] += sum_r part[r, c] for c < n (fixed summation order: deterministic).
-__global__ void reduce_rows_kernel(const float* __restrict__ part, int rows, int n, float* __restrict__ out0,
-                                   float* __restrict__ out1, int split) {
-  const int c = blockIdx.x * blockDim.x + threadIdx.x;
-  if (c >= n) return;
+// out0[c] / out1[c - split] += sum_r part[r, c]: 32 columns x 8 row-slices per
+// block, fixed summation order (deterministic).
+__global__ void __launch_bounds__(256) reduce_rows_kernel(const float* __restrict__ part, int rows, int n,
+                                                          float* __restrict__ out0, float* __restrict__ out1,
+                                                          int split) {
+  __shared__ float red[8][33];
+  const int cl = threadIdx.x & 31, sl = threadIdx.x >> 5;
+  const int c = blockIdx.x * 32 + cl;
   float acc = 0.f;
-  for (int r = 0; r < rows; ++r) acc += part[(long)r * n + c];
-  if (c < split) out0[c] += acc;
-  else out1[c - split] += acc;
+  if (c < n) {
+    for (int r = sl; r < rows; r += 8) acc += part[(long)r * n + c];
+  }
+  red[sl][cl] = acc;
+  __syncthreads();
+  if (sl == 0 && c < n) {
+    float s = 0.f;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) s += red[q][cl];
+    if (c < split) out0[c] += s;
+    else out1[c - split] += s;
+  }
 }
 
 // Column sums of a bf16 matrix: out[c] += sum_r in[r, c]. Block = 8 warps
@@ -195,34 +207,51 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
 // ----------------------------------------------------------------------------
 // Host launchers (raw pointers; the torch-facing checks live in ops_host.cpp)
 // ----------------------------------------------------------------------------
+#define HB_LN_DISPATCH(V4, ...)                                  \
+  switch (V4) {                                                  \
+    case 1: { constexpr int kV = 1; __VA_ARGS__; } break;        \
+    case 2: { constexpr int kV = 2; __VA_ARGS__; } break;        \
+    case 4: { constexpr int kV = 4; __VA_ARGS__; } break;        \
+    case 6: { constexpr int kV = 6; __VA_ARGS__; } break;        \
+    case 8: { constexpr int kV = 8; __VA_ARGS__; } break;        \
+    case 10: { constexpr int kV = 10; __VA_ARGS__; } break;      \
+    case 12: { constexpr int kV = 12; __VA_ARGS__; } break;      \
+    case 16: { constexpr int kV = 16; __VA_ARGS__; } break;      \
+    default: throw std::runtime_error("layernorm: unsupported width"); \
+  }
+
+static int ln_v4(int H) {
+  if (H % 4 != 0 || H > 2048) throw std::runtime_error("layernorm: H must be a multiple of 4, <= 2048");
+  const int v = (H + 127) / 128;
+  const int allowed[] = {1, 2, 4, 6, 8, 10, 12, 16};
+  for (int a : allowed)
+    if (a >= v) return a;
+  return 16;
+}
+
 void ln_fwd_launch(const float* x, const float* w, const float* b, __nv_bfloat16* y, float* mean, float* rstd,
                    int M, int H, float eps, cudaStream_t s) {
-  if (H % 4 != 0 || H > 32 * 4 * LN_MAXV) throw std::runtime_error("layernorm: H must be a multiple of 4, <= 2048");
-  const int threads = 256;
-  const int blocks = (M * 32 + threads - 1) / threads;
-  ln_fwd_kernel<<<blocks, threads, 0, s>>>(x, w, b, y, mean, rstd, M, H, eps);
+  if (M == 0) return;
+  const int blocks = (M + LN_ROWS_PER_CTA - 1) / LN_ROWS_PER_CTA;
+  HB_LN_DISPATCH(ln_v4(H), ln_fwd_kernel<kV><<<blocks, 256, 0, s>>>(x, w, b, y, mean, rstd, M, H, eps));
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 int ln_bwd_num_ctas(int M, int device) {
-  const int ctas = 2 * num_sms(device);
-  return M < ctas ? (M > 0 ? M : 1) : ctas;
+  (void)device;
+  const int per = LN_BWD_WARPS * LN_BWD_ROWS;
+  return M > 0 ? (M + per - 1) / per : 1;
 }
 
 void ln_bwd_launch(const float* dy, const float* x, const float* mean, const float* rstd, const float* w,
                    const float* dres_in, float* dres, __nv_bfloat16* dres16, float* part, int num_ctas,
                    float* dgamma, float* dbeta, int M, int H, cudaStream_t s) {
-  if (H % 4 != 0 || H > 32 * 4 * LN_MAXV) throw std::runtime_error("layernorm: H must be a multiple of 4, <= 2048");
-  const int rows_per_cta = (M + num_ctas - 1) / num_ctas;
-  const size_t smem = 8 * 2 * H * sizeof(float);
-  static bool attr = false;
-  if (!attr) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, 8 * 2 * 2048 * 4));
-    attr = true;
-  }
-  ln_bwd_kernel<<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres, dres16, part, M, H, rows_per_cta);
+  if (M == 0) return;
+  const size_t smem = 2 * H * sizeof(float);
+  HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
+                                                                          dres16, part, M, H));
   HB_CUDA_CHECK(cudaGetLastError());
-  reduce_rows_kernel<<<(2 * H + 255) / 256, 256, 0, s>>>(part, num_ctas, 2 * H, dgamma, dbeta, H);
+  reduce_rows_kernel<<<(2 * H + 31) / 32, 256, 0, s>>>(part, num_ctas, 2 * H, dgamma, dbeta, H);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -57,7 +57,11 @@ class FusedAdamW:
         K.clip_coef(self.norm2, self.max_grad_norm, self.coef, self.norm)
         return self.norm
 
-    def step(self) -> None:
+    def prepare_step(self) -> None:
+        """Host part of a step: advance the step count and upload the hyper-parameters.
+
+        Kept separate from ``step_device`` so the device part can live in a
+        captured CUDA graph while learning rate and bias corrections change."""
         self.step_count += 1
         lr = self.param_groups[0]["lr"]
         b1, b2 = self.betas
@@ -66,8 +70,15 @@ class FusedAdamW:
         h = torch.tensor([lr, b1, b2, self.eps, self.wd, 1.0 - b1 ** self.step_count,
                           math.sqrt(1.0 - b2 ** self.step_count), self.grad_scale], dtype=torch.float32)
         self.hyper.copy_(h)
+
+    def step_device(self) -> None:
+        """Device part of a step (no host synchronisation; graph-capturable)."""
         self.compute_grad_norm()
         K.adamw_step(self.flat.data, self.flat.grad, self.m, self.v, self.flat.data16, self.hyper, self.coef)
+
+    def step(self) -> None:
+        self.prepare_step()
+        self.step_device()
 
     def zero_grad(self, set_to_none: bool = True) -> None:
         self.flat.zero_grad()

@@ -107,6 +107,8 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--out_dir", type=str, default=".")
     p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
     p.add_argument("--log_interval", type=int, default=None)
+    p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
+                   help="capture the fused training step in a CUDA graph after 2 eager steps")
     return p
 
 
@@ -162,6 +164,19 @@ def mark_tp_sharded(module: torch.nn.Module) -> None:
             m.weight.tp_sharded = True
 
 
+class _ListLoader:
+    """Serves a fixed list of device batches in order (graph capture / replay)."""
+
+    def __init__(self, batches):
+        self.batches, self.i = batches, 0
+        self.B = batches[0][0].shape[0]
+
+    def next_batch(self, device):
+        b = self.batches[self.i % len(self.batches)]
+        self.i += 1
+        return b
+
+
 class Engine:
     """Owns the model/stage, optimizer and one training step."""
 
@@ -215,9 +230,67 @@ class Engine:
         if self.use_pipeline:
             bd = torch.float32 if args.pp_boundary_dtype == "fp32" else torch.bfloat16
             self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd)
+        # CUDA-graph replay of the whole fused step (forward, backward, DP
+        # reduction, clipping, AdamW) once shapes are known; the first
+        # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).
+        self.use_graph = bool(getattr(args, "cuda_graph", 1)) and self.fused and not self.use_pipeline
+        self._graph = None
+        self._eager_steps = 0
+        self.GRAPH_WARMUP = 2
 
     # -- one optimizer step ---------------------------------------------------
     def train_step(self, loader) -> tuple:
+        if self.use_graph:
+            batches = [loader.next_batch(self.device) for _ in range(self.args.grad_accum_steps)]
+            return self._graph_step(batches)
+        return self._eager_step(loader)
+
+    def _graph_step(self, batches) -> tuple:
+        if self._graph is None and self._eager_steps < self.GRAPH_WARMUP:
+            self._eager_steps += 1
+            return self._eager_step(_ListLoader(batches))
+        if self._graph is None:
+            self._static = [(x.clone(), y.clone()) for x, y in batches]
+            torch.cuda.synchronize()
+            g = torch.cuda.CUDAGraph()
+            self.optimizer.prepare_step()
+            with torch.cuda.graph(g):
+                self._static_out = self._device_step(_ListLoader(self._static))
+            self._graph = g
+            g.replay()
+            return self._static_out
+        for (sx, sy), (x, y) in zip(self._static, batches):
+            sx.copy_(x, non_blocking=True)
+            sy.copy_(y, non_blocking=True)
+        self.optimizer.prepare_step()
+        self._graph.replay()
+        return self._static_out
+
+    def _device_step(self, loader) -> tuple:
+        """Forward/backward of every microbatch, loss all-reduce, DP reduction, optimizer (device work only)."""
+        args, topo = self.args, self.topo
+        accum = args.grad_accum_steps
+        aux = torch.zeros((), device=self.device)
+        loss_sum = torch.zeros((), device=self.device)
+        for _ in range(accum):
+            x, y = loader.next_batch(self.device)
+            _, loss, aux_mb = self.forward_module(x, y, return_logits=False)
+            ((loss + aux_mb) / accum).backward()
+            aux = aux + aux_mb.detach().float()
+            loss_sum = loss_sum + loss.detach().float()
+        loss_scalar = loss_sum / accum
+        if topo.dp_group is not None and dist.is_initialized():
+            dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            loss_scalar = loss_scalar / topo.dp
+            dist.all_reduce(aux, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            aux = aux / topo.dp
+        if self.reducer is not None:
+            self.reducer.reduce()
+        self.optimizer.step_device()
+        self.optimizer.zero_grad()
+        return loss_scalar, aux
+
+    def _eager_step(self, loader) -> tuple:
         args, topo = self.args, self.topo
         accum = args.grad_accum_steps
         if self.use_pipeline:
