@@ -1,5 +1,6 @@
 // Python bindings of the heiretsu_b200 native extension (module `_C`).
 #include <torch/extension.h>
+#include <pybind11/stl.h>
 
 #include "ops.h"
 
@@ -24,4 +25,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("f32_to_bf16", &hb::f32_to_bf16);
   m.def("attention_fwd", &hb::attention_fwd);
   m.def("attention_bwd", &hb::attention_bwd);
+  m.def("raw_malloc", &hb::raw_malloc);
+  m.def("raw_free", &hb::raw_free);
+  m.def("tensor_from_ptr", &hb::tensor_from_ptr);
+  m.def("ipc_handle", &hb::ipc_handle_py);
+  m.def("ipc_open", &hb::ipc_open_py);
+  m.def("ipc_close", &hb::ipc_close);
+  m.def("dp_allreduce", &hb::dp_allreduce);
+  m.def("group_barrier", &hb::group_barrier);
 }

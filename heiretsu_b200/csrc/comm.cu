@@ -1,0 +1,186 @@
+// NVLink peer-memory runtime and the fused data-parallel gradient reduction.
+//
+// Symmetric buffers: every rank of a group allocates the same number of
+// bytes with cudaMalloc, exports a CUDA IPC handle, and opens the handles of
+// its peers (handles travel over torch.distributed). A kernel then holds a
+// device pointer to every peer's buffer and moves data with plain loads and
+// stores over NVLink -- no staging copies, no library kernel touching peer
+// memory, no TMA multicast.
+//
+// Signal pads: a small symmetric uint32 array per group. Slot
+// [src_rank][block] on rank p is written (st.release.sys) by block `block`
+// of rank src_rank and polled (ld.acquire.sys) by block `block` of rank p.
+// Values are epoch-tagged and monotonic, and the epoch counter lives in
+// device memory (per block), so captured CUDA graphs replay correctly.
+// Every wait is bounded: on timeout the kernel records kPeerTimeout in the
+// device status word and returns (the host raises CommTimeoutError).
+//
+// Fused DP all-reduce (replaces reference dp.py:13-26): rank r owns chunk r
+// of the flat fp32 gradient buffer. Each block, for its part of chunk r,
+// loads the chunk from all peers (vector P2P loads issued back to back),
+// sums in a fixed rank order, multiplies by 1/world, and stores the result
+// into the same chunk of every peer's buffer (push all-gather). Two
+// per-block barriers bracket the data phase: "all inputs ready" and "all
+// results delivered". Every rank moves (world-1)/world of the buffer in each
+// direction over NVLink, once.
+#include <cuda_runtime.h>
+
+#include <cstring>
+#include <mutex>
+#include <stdexcept>
+#include <string>
+#include <vector>
+
+#include "common.cuh"
+#include "host_utils.h"
+
+namespace hb {
+
+constexpr int kMaxRanks = 8;
+constexpr int kMaxSignalBlocks = 1024;
+
+__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
+  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
+  uint32_t v;
+  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+struct PeerTable {
+  uint64_t data[kMaxRanks];    // peer data buffers (index = group rank)
+  uint64_t signal[kMaxRanks];  // peer signal pads, uint32 [kMaxRanks][kMaxSignalBlocks]
+};
+
+// Per-block barrier across the group. Called by all threads of the block.
+// `counter` is this rank's per-block epoch array (device memory, local).
+// Returns false (after recording an error) if a peer did not arrive in time.
+__device__ __forceinline__ bool group_barrier(const PeerTable& pt, int rank, int world, uint32_t* counter,
+                                              uint32_t phase_tag, int* status) {
+  __shared__ int ok_sh;
+  if (threadIdx.x == 0) {
+    ok_sh = 1;
+    const uint32_t epoch = counter[blockIdx.x] + 1;  // advanced once per call, after both barriers
+    const uint32_t val = epoch * 4u + phase_tag;
+    __threadfence_system();
+    for (int p = 0; p < world; ++p) {
+      if (p == rank) continue;
+      uint32_t* slot = reinterpret_cast<uint32_t*>(pt.signal[p]) + rank * kMaxSignalBlocks + blockIdx.x;
+      st_release_sys(slot, val);
+    }
+    const uint32_t* mine = reinterpret_cast<const uint32_t*>(pt.signal[rank]);
+    const uint64_t t0 = globaltimer_ns();
+    for (int p = 0; p < world && ok_sh; ++p) {
+      if (p == rank) continue;
+      const uint32_t* slot = mine + p * kMaxSignalBlocks + blockIdx.x;
+      int spins = 0;
+      while (static_cast<int32_t>(ld_acquire_sys(slot) - val) < 0) {
+        if (((++spins) & 255) == 0 && globaltimer_ns() - t0 > HB_WAIT_TIMEOUT_NS) {
+          record_error(status, kPeerTimeout, 100 + p);
+          ok_sh = 0;
+          break;
+        }
+      }
+    }
+  }
+  __syncthreads();
+  return ok_sh != 0;
+}
+
+__global__ void __launch_bounds__(512) dp_allreduce_kernel(PeerTable pt, int rank, int world, long n4, long chunk4,
+                                                           float scale, uint32_t* counter, int* status) {
+  if (!group_barrier(pt, rank, world, counter, 1, status)) return;
+  const long begin = (long)rank * chunk4;
+  const long end = min(n4, begin + chunk4);
+  for (long i = begin + (long)blockIdx.x * blockDim.x + threadIdx.x; i < end; i += (long)gridDim.x * blockDim.x) {
+    float4 v[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < world) v[p] = reinterpret_cast<const float4*>(pt.data[p])[i];
+    float4 s = make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p) {
+      if (p < world) {
+        s.x += v[p].x;
+        s.y += v[p].y;
+        s.z += v[p].z;
+        s.w += v[p].w;
+      }
+    }
+    s.x *= scale;
+    s.y *= scale;
+    s.z *= scale;
+    s.w *= scale;
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < world) reinterpret_cast<float4*>(pt.data[p])[i] = s;
+  }
+  if (!group_barrier(pt, rank, world, counter, 2, status)) return;
+  if (threadIdx.x == 0) counter[blockIdx.x] += 1;
+}
+
+// Bounded barrier kernel (also used by the tests' "peer never arrives" case).
+__global__ void group_barrier_kernel(PeerTable pt, int rank, int world, uint32_t* counter, int* status) {
+  if (!group_barrier(pt, rank, world, counter, 3, status)) return;
+  if (threadIdx.x == 0) counter[blockIdx.x] += 1;
+}
+
+// ---------------------------------------------------------------------------
+// Host side
+// ---------------------------------------------------------------------------
+static std::mutex g_ipc_mu;
+
+std::vector<uint8_t> ipc_handle(uint64_t ptr) {
+  cudaIpcMemHandle_t h;
+  HB_CUDA_CHECK(cudaIpcGetMemHandle(&h, reinterpret_cast<void*>(ptr)));
+  std::vector<uint8_t> out(sizeof(h));
+  std::memcpy(out.data(), &h, sizeof(h));
+  return out;
+}
+
+uint64_t ipc_open(const std::vector<uint8_t>& handle) {
+  if (handle.size() != sizeof(cudaIpcMemHandle_t)) throw std::runtime_error("ipc_open: bad handle size");
+  cudaIpcMemHandle_t h;
+  std::memcpy(&h, handle.data(), sizeof(h));
+  void* p = nullptr;
+  std::lock_guard<std::mutex> lk(g_ipc_mu);
+  HB_CUDA_CHECK(cudaIpcOpenMemHandle(&p, h, cudaIpcMemLazyEnablePeerAccess));
+  return reinterpret_cast<uint64_t>(p);
+}
+
+void ipc_close(uint64_t ptr) { HB_CUDA_CHECK(cudaIpcCloseMemHandle(reinterpret_cast<void*>(ptr))); }
+
+static PeerTable make_table(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal) {
+  if (data.size() > kMaxRanks || signal.size() != data.size())
+    throw std::runtime_error("peer table: at most 8 ranks, one signal pad per rank");
+  PeerTable t{};
+  for (size_t i = 0; i < data.size(); ++i) {
+    t.data[i] = data[i];
+    t.signal[i] = signal[i];
+  }
+  return t;
+}
+
+int dp_allreduce_blocks(int device) { return num_sms(device); }
+
+void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
+                         long n, float scale, uint32_t* counter, int* status, cudaStream_t s) {
+  const int world = static_cast<int>(data.size());
+  if (n % 4 != 0) throw std::runtime_error("dp_allreduce: element count must be a multiple of 4");
+  const PeerTable t = make_table(data, signal);
+  const long n4 = n / 4;
+  const long chunk4 = (n4 + world - 1) / world;
+  const int blocks = std::min(dp_allreduce_blocks(current_device()), kMaxSignalBlocks);
+  dp_allreduce_kernel<<<blocks, 512, 0, s>>>(t, rank, world, n4, chunk4, scale, counter, status);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void group_barrier_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
+                          uint32_t* counter, int* status, cudaStream_t s) {
+  const PeerTable t = make_table(data, signal);
+  group_barrier_kernel<<<1, 32, 0, s>>>(t, rank, static_cast<int>(data.size()), counter, status);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+}  // namespace hb

@@ -71,10 +71,47 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
     p.resid = resid->data_ptr<float>();
     p.ldr = resid->stride(0);
   }
+  // Rasterisation: CTAs in flight share tiles of the larger operand; the
+  // smaller one is re-read from L2.
+  const long n_real = b_mn ? b.size(1) : b.size(0);
+  p.raster_n = (M > n_real) ? 1 : 0;
+  // Split-K for fp32-output GEMMs whose tile count leaves SMs idle (few
+  // tiles, long K): partial sums are added with vector atomics.
+  p.splits = 1;
+  const int num_kb = (K + 63) / 64;
+  p.kb_per_split = num_kb;
+  int e_launch = static_cast<int>(epi);
+  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8) {
+    const int sms = num_sms(a.get_device());
+    const long tiles = (long)((M + 127) / 128) * ((N + BN - 1) / BN);
+    auto eff = [&](int s) {
+      const long units = tiles * s;
+      const long waves = (units + sms - 1) / sms;
+      return (double)units / (double)(waves * sms);
+    };
+    int best = 1;
+    double best_eff = eff(1);
+    for (int sp = 2; sp <= 16 && num_kb / sp >= 4; ++sp) {
+      const double e = eff(sp);
+      if (e > best_eff + 0.08) {
+        best = sp;
+        best_eff = e;
+      }
+    }
+    if (best > 1) {
+      p.kb_per_split = (num_kb + best - 1) / best;
+      p.splits = (num_kb + p.kb_per_split - 1) / p.kb_per_split;
+      if (epi == kEpiF32) {  // partial sums are accumulated into a zeroed output
+        HB_CUDA_CHECK(cudaMemset2DAsync(c.data_ptr(), c.stride(0) * sizeof(float), 0, sizeof(float) * N, M,
+                                        at::cuda::getCurrentCUDAStream()));
+      }
+      e_launch = kEpiF32Atomic;
+    }
+  }
   const CUtensorMap ta = operand_map(a, a_mn ? 64 : 128);
   const CUtensorMap tb = operand_map(b, b_mn ? 64 : BN);
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
-  const int e = static_cast<int>(epi);
+  const int e = e_launch;
   if (BN == 256) {
     if (!a_mn && !b_mn) gemm_launch_256_kk(e, ta, tb, p, s);
     else if (!a_mn) gemm_launch_256_kn(e, ta, tb, p, s);

@@ -89,6 +89,20 @@ __device__ __forceinline__ void stg_store(const uint8_t* stg, void* dst, long ld
   }
 }
 
+// Coalesced staging -> global vector atomic add (fp32 split-K partials).
+__device__ __forceinline__ void stg_atomic_add(const uint8_t* stg, float* dst, long ld, int m_base, int n0, int M,
+                                               int N, int lane) {
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int idx = it * 32 + lane;
+    const int r = idx / 8, seg = idx % 8;
+    const int gm = m_base + r, gn = n0 + seg * 4;
+    if (gm < M && gn < N)
+      atomicAdd(reinterpret_cast<float4*>(dst + (long)gm * ld + gn),
+                *reinterpret_cast<const float4*>(stg + r * kStgRowF32 + seg * 16));
+  }
+}
+
 // Row-per-thread write of 32 values into this thread's staging row.
 __device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float (&v)[32]) {
   uint8_t* row = stg + lane * kStgRowBf16;
@@ -168,6 +182,10 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int m_b
     stg_put_bf16(stg, lane, v);
     __syncwarp();
     stg_store<false>(stg, p.C, p.ldc, m_base, n0, p.M, p.N, lane);
+  } else if constexpr (EPI == kEpiF32Atomic) {
+    stg_put_f32(stg, lane, v);
+    __syncwarp();
+    stg_atomic_add(stg, reinterpret_cast<float*>(p.C), p.ldc, m_base, n0, p.M, p.N, lane);
   } else {
     stg_put_f32(stg, lane, v);
     __syncwarp();
@@ -197,8 +215,21 @@ __global__ void __launch_bounds__(192, 1)
   const int lane = threadIdx.x & 31;
   const int num_m = (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n;
-  const int num_kb = (p.K + BK - 1) / BK;
+  const int num_tiles = num_m * num_n * p.splits;
+  const int num_kb_total = (p.K + BK - 1) / BK;
+  // Tile t -> (split, m-block, n-block); rasterisation order set by the host.
+  auto decode = [&](int t, int& mb, int& nb, int& kb0, int& nkb) {
+    const int mn = num_m * num_n;
+    const int sp = t / mn;
+    const int r = t % mn;
+    if (p.raster_n) {
+      mb = r / num_n, nb = r % num_n;
+    } else {
+      mb = r % num_m, nb = r / num_m;
+    }
+    kb0 = sp * p.kb_per_split;
+    nkb = min(p.kb_per_split, num_kb_total - kb0);
+  };
 
   if (warp == 0 && lane == 0) {
     for (int s = 0; s < STAGES; ++s) {
@@ -229,8 +260,10 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        const int mb = t % num_m, nb = t / num_m;
-        for (int kb = 0; kb < num_kb; ++kb) {
+        int mb, nb, kb0, num_kb;
+        decode(t, mb, nb, kb0, num_kb);
+        for (int kbi = 0; kbi < num_kb; ++kbi) {
+          const int kb = kb0 + kbi;
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, 1)) {
             ok = false;
             break;
@@ -279,6 +312,8 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
+        int mb_, nb_, kb0_, num_kb;
+        decode(t, mb_, nb_, kb0_, num_kb);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, 3)) {
             ok = false;
@@ -314,7 +349,8 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
       tc_fence_after();
-      const int mb = t % num_m, nb = t / num_m;
+      int mb, nb, kb0_, nkb_;
+      decode(t, mb, nb, kb0_, nkb_);
       const int m_base = mb * BM + sub * 32;
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
@@ -348,7 +384,7 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams&
     HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     attr_set[dev] = true;
   }
-  const int num_tiles = ((p.M + 127) / 128) * ((p.N + BN - 1) / BN);
+  const int num_tiles = ((p.M + 127) / 128) * ((p.N + BN - 1) / BN) * p.splits;
   const int grid = num_tiles < num_sms(dev) ? num_tiles : num_sms(dev);
   kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
   HB_CUDA_CHECK(cudaGetLastError());
@@ -364,6 +400,7 @@ void gemm_dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, co
     case kEpiF32Acc: return launch_gemm<BN, A_MN, B_MN, kEpiF32Acc>(ta, tb, p, s);
     case kEpiF32Resid: return launch_gemm<BN, A_MN, B_MN, kEpiF32Resid>(ta, tb, p, s);
     case kEpiBf16Dgelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Dgelu>(ta, tb, p, s);
+    case kEpiF32Atomic: return launch_gemm<BN, A_MN, B_MN, kEpiF32Atomic>(ta, tb, p, s);
     default: throw std::runtime_error("gemm: unknown epilogue");
   }
 }

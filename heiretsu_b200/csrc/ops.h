@@ -32,4 +32,14 @@ void f32_to_bf16(const at::Tensor& x, at::Tensor& y);
 void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse);
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
                    int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv);
+uint64_t raw_malloc(int64_t bytes);
+void raw_free(uint64_t ptr);
+at::Tensor tensor_from_ptr(uint64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device);
+pybind11::bytes ipc_handle_py(uint64_t ptr);
+uint64_t ipc_open_py(pybind11::bytes handle);
+void ipc_close(uint64_t ptr);
+void dp_allreduce(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank, int64_t n,
+                  double scale, const at::Tensor& counter);
+void group_barrier(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,
+                   const at::Tensor& counter);
 }  // namespace hb

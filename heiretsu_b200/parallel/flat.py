@@ -26,7 +26,7 @@ def _align(n: int) -> int:
 
 class FlatParams:
     def __init__(self, module: torch.nn.Module, device: torch.device,
-                 weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None):
+                 weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None, grad_group=None):
         named: List[Tuple[str, torch.nn.Parameter]] = []
         seen = set()
         for name, p in module.named_parameters():
@@ -51,7 +51,15 @@ class FlatParams:
         self.numel = total
         self.device = device
         self.data = torch.zeros(total, device=device, dtype=torch.float32)
-        self.grad = torch.zeros(total, device=device, dtype=torch.float32)
+        # With a DP group on CUDA, the gradients live in a symmetric (peer-mapped)
+        # buffer so the fused all-reduce can read and write them over NVLink.
+        self.grad_symm = None
+        if grad_group is not None and device.type == "cuda":
+            from .symm import SymmetricBuffer
+            self.grad_symm = SymmetricBuffer(grad_group, total * 4, device)
+            self.grad = self.grad_symm.tensor(torch.float32, total)
+        else:
+            self.grad = torch.zeros(total, device=device, dtype=torch.float32)
         self.data16 = torch.zeros(total, device=device, dtype=torch.bfloat16)
         self.params: List[torch.nn.Parameter] = []
         self.names: List[str] = []

@@ -17,6 +17,7 @@ from typing import List, Optional, Tuple
 import torch
 import torch.distributed as dist
 
+from ..ops._C import load as load_ext
 from .flat import FlatParams
 
 BUCKET_ELEMS = 32 * 1024 * 1024  # 128 MB fp32 per bucket
@@ -32,11 +33,20 @@ class FlatGradReducer:
         n = flat.numel
         for s in range(0, n, bucket_elems):
             self.buckets.append((s, min(n, s + bucket_elems)))
-        self.backend = backend or os.environ.get("HB_DP_BACKEND", "nccl")
+        self.backend = backend or os.environ.get("HB_DP_BACKEND", "p2p")
         self._avg_ok = dist.is_initialized() and dist.get_backend(group) == "nccl"
+
+        self.symm = getattr(flat, "grad_symm", None)
+        if self.backend == "p2p" and self.symm is None:
+            self.backend = "nccl"
 
     def reduce(self) -> None:
         if self.world == 1:
+            return
+        if self.backend == "p2p":
+            # One fused kernel: reduce-scatter + 1/dp + all-gather over NVLink.
+            load_ext().dp_allreduce(self.symm.ptrs, self.symm.signal_ptrs, self.symm.rank, self.flat.numel,
+                                    1.0 / self.world, self.symm.counter)
             return
         g = self.flat.grad
         for s, e in self.buckets:

@@ -207,7 +207,9 @@ class Engine:
             from .optim import FusedAdamW
             from .parallel.flat import FlatParams
 
-            self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo))
+            use_p2p = topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
+            self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo),
+                                   grad_group=topo.dp_group if use_p2p else None)
             self.module.fused = True
             self.optimizer = FusedAdamW(self.flat, lr=args.learning_rate, betas=args.betas,
                                         weight_decay=args.weight_decay, max_grad_norm=args.grad_clip,

@@ -94,3 +94,21 @@ def test_resid_epilogue():
     g.linear_fwd_resid(x, w, b, r, out=r)
     check()
     _close(r, ref, 1e-2)
+
+
+@pytest.mark.parametrize("M,N,K", [(768, 768, 8192), (8192, 768, 50304), (2304, 768, 8192)])
+def test_split_k_fp32_paths(M, N, K):
+    """Shapes with few output tiles and long K take the split-K (atomic) epilogue."""
+    g, check = _ops()
+    torch.manual_seed(7)
+    a = torch.randn(M, K, device="cuda").bfloat16()
+    b = torch.randn(N, K, device="cuda").bfloat16()
+    ref = a.float() @ b.float().t()
+    out = torch.full((M, N), 3.0, device="cuda")
+    g.gemm(a, b, out, N, g.EPI_F32, False, False)
+    check()
+    _close(out, ref, 1e-2)
+    acc = torch.ones(M, N, device="cuda")
+    g.gemm(a, b, acc, N, g.EPI_F32_ACC, False, False)
+    check()
+    _close(acc, ref + 1, 1e-2)
