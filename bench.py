@@ -341,6 +341,8 @@ def main():
                "clocks": clocks, "e2e": e2e, "gpu_launches": launches * args.steps if launches >= 0 else (0 if args.impl == "reference" else None),
                "impl": args.impl}
         print(json.dumps(rec))
+    if hasattr(eng, "close"):
+        eng.close()  # the captured graph must be released before the process group
     if world > 1:
         dist.barrier()
         dist.destroy_process_group()

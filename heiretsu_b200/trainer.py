@@ -235,7 +235,8 @@ class Engine:
         # CUDA-graph replay of the whole fused step (forward, backward, DP
         # reduction, clipping, AdamW) once shapes are known; the first
         # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).
-        self.use_graph = bool(getattr(args, "cuda_graph", 1)) and self.fused and not self.use_pipeline
+        self.use_graph = (bool(getattr(args, "cuda_graph", 1)) and self.fused and not self.use_pipeline
+                          and (self.reducer is None or self.reducer.backend == "p2p"))
         self._graph = None
         self._eager_steps = 0
         self.GRAPH_WARMUP = 2
@@ -260,18 +261,29 @@ class Engine:
                 self._static_out = self._device_step(_ListLoader(self._static))
             self._graph = g
             g.replay()
-            return self._static_out
-        for (sx, sy), (x, y) in zip(self._static, batches):
-            sx.copy_(x, non_blocking=True)
-            sy.copy_(y, non_blocking=True)
-        self.optimizer.prepare_step()
-        self._graph.replay()
-        return self._static_out
+        else:
+            for (sx, sy), (x, y) in zip(self._static, batches):
+                sx.copy_(x, non_blocking=True)
+                sy.copy_(y, non_blocking=True)
+            self.optimizer.prepare_step()
+            self._graph.replay()
+        loss, aux = self._static_out
+        return self._average_scalars(loss.clone(), aux.clone())
+
+    def _average_scalars(self, loss_scalar, aux):
+        """Loss / aux all-reduce over DP (outside any captured graph: NCCL stays out of graphs)."""
+        topo = self.topo
+        if topo.dp_group is not None and dist.is_initialized():
+            both = torch.stack([loss_scalar, aux])
+            dist.all_reduce(both, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            both = both / topo.dp
+            return both[0], both[1]
+        return loss_scalar, aux
 
     def _device_step(self, loader) -> tuple:
-        """Forward/backward of every microbatch, loss all-reduce, DP reduction, optimizer (device work only)."""
-        args, topo = self.args, self.topo
-        accum = args.grad_accum_steps
+        """Forward/backward of every microbatch, DP gradient reduction and optimizer (device work only;
+        the DP reduction here is the fused peer-memory kernel, so a captured graph holds no NCCL call)."""
+        accum = self.args.grad_accum_steps
         aux = torch.zeros((), device=self.device)
         loss_sum = torch.zeros((), device=self.device)
         for _ in range(accum):
@@ -280,17 +292,19 @@ class Engine:
             ((loss + aux_mb) / accum).backward()
             aux = aux + aux_mb.detach().float()
             loss_sum = loss_sum + loss.detach().float()
-        loss_scalar = loss_sum / accum
-        if topo.dp_group is not None and dist.is_initialized():
-            dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.dp_group)
-            loss_scalar = loss_scalar / topo.dp
-            dist.all_reduce(aux, op=dist.ReduceOp.SUM, group=topo.dp_group)
-            aux = aux / topo.dp
         if self.reducer is not None:
             self.reducer.reduce()
         self.optimizer.step_device()
         self.optimizer.zero_grad()
-        return loss_scalar, aux
+        return loss_sum / accum, aux
+
+    def close(self) -> None:
+        """Release the captured graph (before destroy_process_group) and wait for the device."""
+        if self.device.type == "cuda":
+            torch.cuda.synchronize()
+        self._graph = None
+        self._static = None
+        self._static_out = None
 
     def _eager_step(self, loader) -> tuple:
         args, topo = self.args, self.topo
@@ -497,6 +511,7 @@ def main(argv=None) -> None:
         run.finish()
     if is_main:
         print("training finished.")
+    engine.close()
     if distributed and dist.is_initialized():
         cleanup()
 
