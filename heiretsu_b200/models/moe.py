@@ -106,6 +106,13 @@ class MoELayer(nn.Module):
         self.expert_group = ExpertGroup(self.num_local_experts, config.hidden_size, config.intermediate_size,
                                         ep_rank=ep_rank, num_experts=config.num_experts)
         self._expert_counts: Optional[torch.Tensor] = None
+        if ep_world_size > 1:
+            # The EP ranks of one data replica hold identical tokens, so every
+            # expert receives each token once per EP rank and its gradient sums
+            # ep identical contributions: average them (the dense gradient).
+            for p in self.expert_group.parameters():
+                p.register_hook(lambda g, s=1.0 / ep_world_size: g * s)
+                p.ep_grad_scale = 1.0 / ep_world_size
 
     def forward(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
         B, S, H = x.shape

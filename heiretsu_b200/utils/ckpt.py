@@ -49,3 +49,69 @@ def load_checkpoint(module: torch.nn.Module, path: str, strict: bool = True) -> 
     with torch.no_grad():
         module.load_state_dict(sd, strict=strict)
     return obj
+
+
+# ---------------------------------------------------------------------------
+# Topology changes: full (dense) state dict <-> per-rank shards
+# ---------------------------------------------------------------------------
+def _qkv_rows(out: int, tp_rank: int, tp: int) -> torch.Tensor:
+    per = out // tp
+    return torch.cat([torch.arange(i * out + tp_rank * per, i * out + (tp_rank + 1) * per) for i in range(3)])
+
+
+def _full_key(local_key: str, module) -> str:
+    """Map a key of a GPT / StageModule shard to the dense GPT's key."""
+    from ..parallel.pipeline import StageModule
+
+    if isinstance(module, StageModule):
+        if local_key.startswith("blocks."):
+            rest = local_key[len("blocks."):]
+            i, tail = rest.split(".", 1)
+            local_key = f"tr.h.{module.block_start + int(i)}.{tail}"
+        elif local_key.startswith(("wte.", "wpe.", "ln_f.")):
+            local_key = "tr." + local_key
+    if ".moe.expert_group.experts." in local_key:
+        pre, rest = local_key.split(".moe.expert_group.experts.", 1)
+        j, tail = rest.split(".", 1)
+        group = module.get_submodule(f"{local_key.split('.moe.')[0]}.moe.expert_group")
+        local_key = f"{pre}.moe.expert_group.experts.{group.ep_rank * group.num_local_experts + int(j)}.{tail}"
+    return local_key
+
+
+def shard_from_full(module, full_state: dict, tp_rank: int = 0, tp: int = 1) -> dict:
+    """Per-rank state dict for `module` (GPT or StageModule, any TP / EP / PP
+    position) sliced from a dense GPT state dict. Slicing rules follow the
+    checkpoint format: c_attn rows [Q_shard; K_shard; V_shard], column-parallel
+    rows, row-parallel columns, local experts = global ep_rank*E/ep + j."""
+    from ..parallel.tp import ColumnParallelLinear, ColumnParallelLinearQKV, RowParallelLinear
+
+    kinds = {}
+    for name, m in module.named_modules():
+        if isinstance(m, ColumnParallelLinearQKV):
+            kinds[name] = "qkv"
+        elif isinstance(m, ColumnParallelLinear):
+            kinds[name] = "col"
+        elif isinstance(m, RowParallelLinear):
+            kinds[name] = "row"
+    out = {}
+    for key, t in module.state_dict().items():
+        full = full_state[_full_key(key, module)]
+        owner, pname = key.rsplit(".", 1)
+        kind = kinds.get(owner)
+        if kind == "qkv":
+            full = full[_qkv_rows(full.shape[0] // 3, tp_rank, tp)]
+        elif kind == "col":
+            per = full.shape[0] // tp
+            full = full[tp_rank * per:(tp_rank + 1) * per]
+        elif kind == "row" and pname == "weight":
+            per = full.shape[1] // tp
+            full = full[:, tp_rank * per:(tp_rank + 1) * per]
+        out[key] = full.clone()
+    return out
+
+
+def load_from_full(module, full_state: dict, tp_rank: int = 0, tp: int = 1) -> None:
+    """Load a dense GPT state dict into a shard (TP / EP / PP slicing applied)."""
+    sd = shard_from_full(module, full_state, tp_rank, tp)
+    with torch.no_grad():
+        module.load_state_dict(sd, strict=True)

@@ -1,0 +1,140 @@
+"""Multi-process (gloo, CPU) parity of every parallelism against the dense model.
+
+The oracle is a dense fp32 GPT; each rank loads its shard of the same weights
+(TP slices, EP local experts, PP stages) and must reproduce the dense loss
+and the matching slices of the dense gradients.
+"""
+import pytest
+import torch
+
+from dist_util import run_ranks
+
+CFG = dict(block_size=32, vocab_size=96, n_layer=4, n_head=4, n_embed=32, dropout=0.0)
+
+
+def _batch(seed, B=4, T=32, V=96):
+    g = torch.Generator().manual_seed(seed)
+    return torch.randint(0, V, (B, T), generator=g), torch.randint(0, V, (B, T), generator=g)
+
+
+def _dense(cfg_kw, seed=11):
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.models.gpt import GPT
+
+    torch.manual_seed(seed)
+    m = GPT(GPTConfig(**cfg_kw))
+    return m
+
+
+def _dense_grads(cfg_kw, x, y):
+    m = _dense(cfg_kw)
+    _, loss, aux = m(x, y)
+    (loss + aux).backward()
+    return m.state_dict(), {n: p.grad.clone() for n, p in m.named_parameters()}, loss.item()
+
+
+def _worker_tp_dp(rank, world, dp, tp, moe, ep):
+    import torch.distributed as dist
+
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.models.gpt import GPT
+    from heiretsu_b200.parallel.dp import average_gradients
+    from heiretsu_b200.topo import init_topology
+    from heiretsu_b200.utils.ckpt import load_from_full, shard_from_full
+
+    cfg_kw = dict(CFG, **(dict(num_experts=4, top_k=2, moe_freq=2) if moe else {}))
+    topo = init_topology(dp=dp, ep=ep, tp=tp)
+    # every DP rank gets its own batch; the dense oracle sees their concatenation
+    xs = [_batch(100 + d) for d in range(dp)]
+    x, y = xs[topo.dp_rank]
+    full_x = torch.cat([a for a, _ in xs])
+    full_y = torch.cat([b for _, b in xs])
+    full_state, dense_grads, dense_loss = _dense_grads(cfg_kw, full_x, full_y)
+    model = GPT(GPTConfig(**cfg_kw), topo=topo)
+    load_from_full(model, full_state, topo.tp_rank, topo.tp)
+    _, loss, aux = model(x, y)
+    (loss + aux).backward()
+    average_gradients(model, topo.dp_group)
+    lt = loss.detach().clone()
+    if topo.dp_group is not None:
+        dist.all_reduce(lt, group=topo.dp_group)
+        lt /= topo.dp
+    # compare every gradient with the matching slice of the dense gradient
+    dense_grad_sd = {k: dense_grads[k] for k in dense_grads}
+    expect = shard_from_full(model, {**full_state, **dense_grad_sd}, topo.tp_rank, topo.tp)
+    errs = {}
+    for n, p in model.named_parameters():
+        errs[n] = (p.grad - expect[n]).abs().max().item() if p.grad is not None else float("inf")
+    return abs(lt.item() - dense_loss), max(errs.values()), max(errs, key=errs.get)
+
+
+@pytest.mark.parametrize("dp,tp,moe,ep", [(2, 1, False, 1), (1, 2, False, 1), (2, 2, False, 1), (1, 1, True, 2),
+                                          (1, 2, True, 2)])
+def test_parallel_matches_dense(dp, tp, moe, ep):
+    world = dp * tp * ep
+    res = run_ranks(_worker_tp_dp, world, dp, tp, moe, ep)
+    for rank, (dloss, gerr, worst) in enumerate(res):
+        assert dloss < 1e-5, (rank, dloss)
+        assert gerr < 1e-5, (rank, gerr, worst)
+
+
+def _worker_pp(rank, world, pp, tp, accum):
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.parallel.pipeline import GPipeEngine, StageModule
+    from heiretsu_b200.topo import init_topology
+    from heiretsu_b200.utils.ckpt import load_from_full
+
+    topo = init_topology(dp=1, tp=tp, pp=pp)
+    batches = [_batch(200 + m) for m in range(accum)]
+
+    class L:
+        B = 4
+
+        def __init__(self):
+            self.i = 0
+
+        def next_batch(self, device):
+            b = batches[self.i % accum]
+            self.i += 1
+            return b
+
+    # dense oracle: mean over microbatches of (loss)/accum accumulated
+    dense = _dense(CFG)
+    full_state = dense.state_dict()
+    tot = 0.0
+    for x, y in batches:
+        _, l, a = dense(x, y)
+        ((l + a) / accum).backward()
+        tot += l.item() / accum
+    stage = StageModule(GPTConfig(**CFG), topo, topo.pp_rank, topo.pp)
+    load_from_full(stage, full_state, topo.tp_rank, topo.tp)
+    eng = GPipeEngine(stage, topo)
+    loss, _ = eng.forward_backward(L(), accum, torch.device("cpu"), False, torch.bfloat16, None, 4)
+    from heiretsu_b200.utils.ckpt import shard_from_full
+    dgrads = {n: p.grad for n, p in dense.named_parameters()}
+    expect = shard_from_full(stage, {**full_state, **dgrads}, topo.tp_rank, topo.tp)
+    errs = []
+    for n, p in stage.named_parameters():
+        e = expect[n]
+        if n in ("wte.weight", "lm_head.weight") and pp > 1:
+            continue  # untied across stages: checked jointly below
+        errs.append((p.grad - e).abs().max().item())
+    out = {"loss_err": abs(loss.item() - tot) if loss is not None else 0.0, "gerr": max(errs) if errs else 0.0}
+    if stage.is_first:
+        out["wte_grad"] = stage.wte.weight.grad.clone()
+    if stage.is_last:
+        out["head_grad"] = stage.lm_head.weight.grad.clone()
+    out["tied_dense"] = dgrads["tr.wte.weight"].clone()
+    return out
+
+
+@pytest.mark.parametrize("pp,tp", [(2, 1), (2, 2)])
+def test_pipeline_matches_dense(pp, tp):
+    res = run_ranks(_worker_pp, pp * tp, pp, tp, 2)
+    for r in res:
+        assert r["loss_err"] < 1e-5
+        assert r["gerr"] < 1e-5
+    first = [r for r in res if "wte_grad" in r][0]
+    last = [r for r in res if "head_grad" in r][0]
+    tied = first["wte_grad"] + last["head_grad"]
+    assert (tied - first["tied_dense"]).abs().max().item() < 1e-5
