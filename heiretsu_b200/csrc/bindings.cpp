@@ -9,10 +9,16 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("read_and_clear_status", &hb::read_and_clear_status, "Read and clear the device status word");
   m.def("gemm", &hb::gemm, "tcgen05 GEMM with fused epilogue", py::arg("a"), py::arg("b"), py::arg("c"),
         py::arg("N"), py::arg("epi"), py::arg("a_mn"), py::arg("b_mn"), py::arg("bias") = py::none(),
-        py::arg("aux") = py::none(), py::arg("resid") = py::none(), py::arg("block_n") = 128);
+        py::arg("aux") = py::none(), py::arg("resid") = py::none(), py::arg("block_n") = 128,
+        py::arg("ag_src") = std::vector<uint64_t>{}, py::arg("ag_flags") = py::none(), py::arg("ag_rank") = 0,
+        py::arg("ag_rows") = 0, py::arg("rs_dst") = std::vector<uint64_t>{}, py::arg("rs_rank") = 0,
+        py::arg("rs_rows") = 0);
   m.def("layernorm_fwd", &hb::layernorm_fwd);
   m.def("layernorm_bwd_scratch_rows", &hb::layernorm_bwd_scratch_rows);
-  m.def("layernorm_bwd", &hb::layernorm_bwd);
+  m.def("layernorm_bwd", &hb::layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
+        py::arg("w"), py::arg("dres_in"), py::arg("dres"), py::arg("dres16"), py::arg("scratch"), py::arg("dgamma"),
+        py::arg("dbeta"), py::arg("dy_srcs") = 1);
+  m.def("resid_sum_ln", &hb::resid_sum_ln);
   m.def("colsum_bf16", &hb::colsum_bf16);
   m.def("cross_entropy_fwd", &hb::cross_entropy_fwd);
   m.def("cross_entropy_bwd", &hb::cross_entropy_bwd);

@@ -25,7 +25,9 @@ static CUtensorMap operand_map(const at::Tensor& t, int box_rows) {
 
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, int64_t epi, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux,
-          const c10::optional<at::Tensor>& resid, int64_t block_n) {
+          const c10::optional<at::Tensor>& resid, int64_t block_n, const std::vector<uint64_t>& ag_src,
+          const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
+          const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: operands must be bf16");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D tensors expected");
@@ -81,7 +83,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   const int num_kb = (K + 63) / 64;
   p.kb_per_split = num_kb;
   int e_launch = static_cast<int>(epi);
-  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8) {
+  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8 && ag_src.empty() && rs_dst.empty()) {
     const int sms = num_sms(a.get_device());
     const long tiles = (long)((M + 127) / 128) * ((N + BN - 1) / BN);
     auto eff = [&](int s) {
@@ -107,6 +109,31 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
       }
       e_launch = kEpiF32Atomic;
     }
+  }
+  if (!ag_src.empty()) {
+    // A = token-gathered activations [world * ag_rows, K], filled in-kernel from the peers' shards.
+    TORCH_CHECK(!a_mn && ag_src.size() <= 8 && ag_flags && ag_flags->defined(), "gemm: all-gather prologue args");
+    TORCH_CHECK(ag_rows % 128 == 0 && (int64_t)ag_src.size() * ag_rows == M, "gemm: all-gather rows");
+    TORCH_CHECK(a.stride(0) == K, "gemm: gathered A must be dense [M, K]");
+    TORCH_CHECK(ag_flags->scalar_type() == at::kInt && ag_flags->numel() >= M / 128, "gemm: ag_flags");
+    TORCH_CHECK(p.splits == 1, "gemm: split-K is not combined with the all-gather prologue");
+    p.ag_world = static_cast<int>(ag_src.size());
+    p.ag_rank = static_cast<int>(ag_rank);
+    p.ag_rows = static_cast<int>(ag_rows);
+    for (size_t i = 0; i < ag_src.size(); ++i) p.ag_src[i] = reinterpret_cast<const void*>(ag_src[i]);
+    p.ag_dst = a.data_ptr();
+    p.ag_flags = ag_flags->data_ptr<int>();
+    HB_CUDA_CHECK(cudaMemsetAsync(p.ag_flags, 0, sizeof(int) * (M / 128), at::cuda::getCurrentCUDAStream()));
+  }
+  if (!rs_dst.empty()) {
+    TORCH_CHECK(rs_dst.size() <= 8 && rs_rows % 128 == 0 && (int64_t)rs_dst.size() * rs_rows == M,
+                "gemm: reduce-scatter epilogue args");
+    TORCH_CHECK(epi == kEpiBf16 || epi == kEpiF32, "gemm: reduce-scatter epilogue needs a plain bf16/fp32 output");
+    TORCH_CHECK(p.splits == 1 && !(bias && bias->defined()), "gemm: reduce-scatter takes no bias / split-K");
+    p.rs_world = static_cast<int>(rs_dst.size());
+    p.rs_rank = static_cast<int>(rs_rank);
+    p.rs_rows = static_cast<int>(rs_rows);
+    for (size_t i = 0; i < rs_dst.size(); ++i) p.rs_dst[i] = reinterpret_cast<void*>(rs_dst[i]);
   }
   const CUtensorMap ta = operand_map(a, a_mn ? 64 : 128);
   const CUtensorMap tb = operand_map(b, b_mn ? 64 : BN);

@@ -194,6 +194,68 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int m_b
   __syncwarp();
 }
 
+// ---------------------------------------------------------------------------
+// All-gather prologue helpers
+// ---------------------------------------------------------------------------
+constexpr int kAgUnitRows = 16;
+
+__device__ __forceinline__ void red_release_gpu_add(int* p, int v) {
+  asm volatile("red.release.gpu.global.add.s32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
+}
+__device__ __forceinline__ int ld_acquire_gpu(const int* p) {
+  int v;
+  asm volatile("ld.acquire.gpu.global.s32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
+  return v;
+}
+
+// One warp copies 16-row units of the peers' shards (NVLink loads) into the
+// local gathered matrix, then publishes them on the m-block's counter.
+__device__ __forceinline__ void ag_copy_units(const GemmParams& p, int gw, int nw, int lane) {
+  const int units_per_rank = p.ag_rows / kAgUnitRows;
+  const int total = units_per_rank * p.ag_world;
+  const long row_bytes = (long)p.K * 2;
+  const long unit_vecs = kAgUnitRows * row_bytes / 16;
+  for (int u = gw; u < total; u += nw) {
+    const int src = (p.ag_rank + u / units_per_rank) % p.ag_world;
+    const int lu = u % units_per_rank;
+    const uint4* from = reinterpret_cast<const uint4*>(static_cast<const uint8_t*>(p.ag_src[src]) +
+                                                       (long)lu * kAgUnitRows * row_bytes);
+    uint4* to = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.ag_dst) +
+                                         ((long)src * p.ag_rows + (long)lu * kAgUnitRows) * row_bytes);
+    long i = lane;
+    for (; i + 96 < unit_vecs; i += 128) {
+      const uint4 a = from[i], b = from[i + 32], c = from[i + 64], d = from[i + 96];
+      to[i] = a;
+      to[i + 32] = b;
+      to[i + 64] = c;
+      to[i + 96] = d;
+    }
+    for (; i < unit_vecs; i += 32) to[i] = from[i];
+    __syncwarp();
+    __threadfence();
+    if (lane == 0) red_release_gpu_add(p.ag_flags + (src * p.ag_rows + lu * kAgUnitRows) / 128, 1);
+  }
+}
+
+// Producer side: wait (bounded) until all units of m-block mb are gathered,
+// then order those generic-proxy writes before this thread's TMA reads.
+__device__ __forceinline__ bool ag_wait_rows(const GemmParams& p, int mb) {
+  const int need = 128 / kAgUnitRows;
+  const int* f = p.ag_flags + mb;
+  if (ld_acquire_gpu(f) < need) {
+    const uint64_t t0 = globaltimer_ns();
+    int spins = 0;
+    while (ld_acquire_gpu(f) < need) {
+      if (((++spins) & 255) == 0 && globaltimer_ns() - t0 > HB_WAIT_TIMEOUT_NS) {
+        record_error(p.status, kPeerTimeout, 6);
+        return false;
+      }
+    }
+  }
+  asm volatile("fence.proxy.async.global;" ::: "memory");
+  return true;
+}
+
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(192, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
@@ -227,6 +289,7 @@ __global__ void __launch_bounds__(192, 1)
     } else {
       mb = r % num_m, nb = r / num_m;
     }
+    if (p.ag_world > 1) mb = (mb + p.ag_rank * (p.ag_rows / BM)) % num_m;  // local shard first, then ring order
     kb0 = sp * p.kb_per_split;
     nkb = min(p.kb_per_split, num_kb_total - kb0);
   };
@@ -262,6 +325,10 @@ __global__ void __launch_bounds__(192, 1)
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
         int mb, nb, kb0, num_kb;
         decode(t, mb, nb, kb0, num_kb);
+        if (p.ag_world > 1 && !ag_wait_rows(p, mb)) {
+          ok = false;
+          break;
+        }
         for (int kbi = 0; kbi < num_kb; ++kbi) {
           const int kb = kb0 + kbi;
           if (!mbar_wait(&empty[stage], phase ^ 1u, p.status, 1)) {
@@ -343,6 +410,7 @@ __global__ void __launch_bounds__(192, 1)
   } else {
     const int sub = warp & 3;
     uint8_t* stg = smem + Cfg::STG_OFFSET + sub * kStgBytes;
+    if (p.ag_world > 1) ag_copy_units(p, blockIdx.x * 4 + (warp - 2), gridDim.x * 4, lane);
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -358,7 +426,17 @@ __global__ void __launch_bounds__(192, 1)
         if (n0 >= p.N) break;
         float v[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN + c * 32, v);
-        gemm_epilogue_chunk<EPI>(p, m_base, n0, v, stg, lane);
+        if (p.rs_world > 1) {
+          // Partial tile -> slot rs_rank of the owning rank's receive buffer (over NVLink).
+          GemmParams q = p;
+          const int owner = m_base / p.rs_rows;
+          const int esz = (EPI == kEpiBf16) ? 2 : 4;
+          q.C = static_cast<uint8_t*>(p.rs_dst[owner]) +
+                ((long)p.rs_rank * p.rs_rows - (long)owner * p.rs_rows) * p.ldc * esz;
+          gemm_epilogue_chunk<EPI>(q, m_base, n0, v, stg, lane);
+        } else {
+          gemm_epilogue_chunk<EPI>(p, m_base, n0, v, stg, lane);
+        }
       }
       tc_fence_before();
       __syncwarp();

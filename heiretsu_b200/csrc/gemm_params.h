@@ -26,6 +26,26 @@ struct GemmParams {
   int splits;          // split-K factor (>= 1); tiles are (split, m-block, n-block)
   int kb_per_split;    // K blocks handled by one split
   int raster_n;        // 1: n-block fastest (CTAs in flight share A), 0: m-block fastest
+
+  // All-gather prologue (tensor parallelism): A is the token-gathered matrix
+  // [world * ag_rows, K] in local memory; rows [r * ag_rows, (r+1) * ag_rows)
+  // are copied from rank r's shard (ag_src[r], row stride K) by the
+  // epilogue warps at kernel start, and ag_flags[m-block] counts the 16-row
+  // units delivered. 0 = off.
+  int ag_world;
+  int ag_rank;
+  int ag_rows;
+  const void* ag_src[8];
+  void* ag_dst;
+  int* ag_flags;
+
+  // Reduce-scatter epilogue: the output tile of rows [m, m+128) belongs to
+  // rank m / rs_rows; it is stored (not reduced) into slot rs_rank of that
+  // rank's receive buffer rs_dst[owner] = [world][rs_rows][ldc]. 0 = off.
+  int rs_world;
+  int rs_rank;
+  int rs_rows;
+  void* rs_dst[8];
 };
 
 }  // namespace hb

@@ -72,6 +72,77 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
   }
 }
 
+// Reduce-scatter consumer: x_new = x + sum_s parts[s] + bias (fp32 residual
+// shard), and, if w != nullptr, y = LN(x_new) in bf16 with its statistics.
+// parts: `nsrc` bf16 slots of [M, H] at stride `src_stride` elements.
+template <int V4>
+__global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restrict__ x,
+                                                           const __nv_bfloat16* __restrict__ parts, int nsrc,
+                                                           long src_stride, const float* __restrict__ bias,
+                                                           float* __restrict__ x_new, const float* __restrict__ w,
+                                                           const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
+                                                           float* __restrict__ mean_out, float* __restrict__ rstd_out,
+                                                           int M, int H, float eps) {
+  const int row = blockIdx.x * LN_ROWS_PER_CTA + (threadIdx.x >> 5);
+  const int lane = threadIdx.x & 31;
+  if (row >= M) return;
+  const int H4 = H >> 2;
+  float4 v[V4];
+  float s = 0.f;
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    const int j = lane + 32 * i;
+    if (j < H4) {
+      float4 a = reinterpret_cast<const float4*>(x + (long)row * H)[j];
+      const float4 bb = reinterpret_cast<const float4*>(bias)[j];
+      a.x += bb.x;
+      a.y += bb.y;
+      a.z += bb.z;
+      a.w += bb.w;
+      for (int q = 0; q < nsrc; ++q) {
+        const uint2 raw = reinterpret_cast<const uint2*>(parts + q * src_stride + (long)row * H)[j];
+        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+        a.x += __bfloat162float(lo.x);
+        a.y += __bfloat162float(lo.y);
+        a.z += __bfloat162float(hi.x);
+        a.w += __bfloat162float(hi.y);
+      }
+      v[i] = a;
+      reinterpret_cast<float4*>(x_new + (long)row * H)[j] = a;
+    } else {
+      v[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+    }
+    s += v[i].x + v[i].y + v[i].z + v[i].w;
+  }
+  if (w == nullptr) return;
+  const float mu = warp_sum(s) / H;
+  float ss = 0.f;
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    const int j = lane + 32 * i;
+    if (j < H4) {
+      const float a = v[i].x - mu, c = v[i].y - mu, d = v[i].z - mu, e = v[i].w - mu;
+      ss += a * a + c * c + d * d + e * e;
+    }
+  }
+  const float rstd = rsqrtf(warp_sum(ss) / H + eps);
+  uint2* yr = reinterpret_cast<uint2*>(y + (long)row * H);
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    const int j = lane + 32 * i;
+    if (j < H4) {
+      const float4 ww = reinterpret_cast<const float4*>(w)[j], bb = reinterpret_cast<const float4*>(b)[j];
+      yr[j] = make_uint2(pack_bf16((v[i].x - mu) * rstd * ww.x + bb.x, (v[i].y - mu) * rstd * ww.y + bb.y),
+                         pack_bf16((v[i].z - mu) * rstd * ww.z + bb.z, (v[i].w - mu) * rstd * ww.w + bb.w));
+    }
+  }
+  if (lane == 0) {
+    mean_out[row] = mu;
+    rstd_out[row] = rstd;
+  }
+}
+
 // Backward. dy fp32 [M, H] (gradient of the LN output), x fp32 [M, H].
 //   dres fp32 [M, H] = dres_in + dx   (dres may alias dres_in: residual gradient in place)
 //   dres16 bf16 [M, H] = dres          (operand copy for the next dgrad/wgrad GEMMs)
@@ -83,7 +154,8 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const float* __restrict__ d
                                                      const float* __restrict__ mean, const float* __restrict__ rstd,
                                                      const float* __restrict__ w, const float* dres_in,
                                                      float* dres, __nv_bfloat16* __restrict__ dres16,
-                                                     float* __restrict__ part, int M, int H) {
+                                                     float* __restrict__ part, int M, int H, int dy_srcs,
+                                                     long dy_src_stride) {
   extern __shared__ float sacc[];  // [2][H]: dgamma, dbeta partials of this CTA
   const int warp_in = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
@@ -105,6 +177,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const float* __restrict__ d
       const bool in = j < H4;
       xv[i] = in ? xr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
       dv[i] = in ? dyr[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      // dy may arrive as several partial sums (reduce-scatter slots), fixed order.
+      for (int sidx = 1; sidx < dy_srcs && in; ++sidx) {
+        const float4 e = reinterpret_cast<const float4*>(dy + sidx * dy_src_stride + (long)r * H)[j];
+        dv[i].x += e.x;
+        dv[i].y += e.y;
+        dv[i].z += e.z;
+        dv[i].w += e.w;
+      }
     }
     const float mu = mean[r], rs = rstd[r];
     float s1 = 0.f, s2 = 0.f;
@@ -237,6 +317,16 @@ void ln_fwd_launch(const float* x, const float* w, const float* b, __nv_bfloat16
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
+void resid_sum_ln_launch(const float* x, const __nv_bfloat16* parts, int nsrc, long src_stride, const float* bias,
+                         float* x_new, const float* w, const float* b, __nv_bfloat16* y, float* mean, float* rstd,
+                         int M, int H, float eps, cudaStream_t s) {
+  if (M == 0) return;
+  const int blocks = (M + LN_ROWS_PER_CTA - 1) / LN_ROWS_PER_CTA;
+  HB_LN_DISPATCH(ln_v4(H), resid_sum_ln_kernel<kV><<<blocks, 256, 0, s>>>(x, parts, nsrc, src_stride, bias, x_new, w,
+                                                                           b, y, mean, rstd, M, H, eps));
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
 int ln_bwd_num_ctas(int M, int device) {
   (void)device;
   const int per = LN_BWD_WARPS * LN_BWD_ROWS;
@@ -245,11 +335,12 @@ int ln_bwd_num_ctas(int M, int device) {
 
 void ln_bwd_launch(const float* dy, const float* x, const float* mean, const float* rstd, const float* w,
                    const float* dres_in, float* dres, __nv_bfloat16* dres16, float* part, int num_ctas,
-                   float* dgamma, float* dbeta, int M, int H, cudaStream_t s) {
+                   float* dgamma, float* dbeta, int M, int H, int dy_srcs, long dy_src_stride, cudaStream_t s) {
   if (M == 0) return;
   const size_t smem = 2 * H * sizeof(float);
   HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
-                                                                          dres16, part, M, H));
+                                                                          dres16, part, M, H, dy_srcs,
+                                                                          dy_src_stride));
   HB_CUDA_CHECK(cudaGetLastError());
   reduce_rows_kernel<<<(2 * H + 31) / 32, 256, 0, s>>>(part, num_ctas, 2 * H, dgamma, dbeta, H);
   HB_CUDA_CHECK(cudaGetLastError());

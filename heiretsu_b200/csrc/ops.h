@@ -7,14 +7,20 @@ int64_t read_and_clear_status(int64_t device);
 
 void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, int64_t epi, bool a_mn, bool b_mn,
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux,
-          const c10::optional<at::Tensor>& resid, int64_t block_n);
+          const c10::optional<at::Tensor>& resid, int64_t block_n, const std::vector<uint64_t>& ag_src,
+          const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
+          const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows);
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, at::Tensor& y, at::Tensor& mean,
                    at::Tensor& rstd, double eps);
 int64_t layernorm_bwd_scratch_rows(int64_t M);
 void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                    const at::Tensor& w, const at::Tensor& dres_in, at::Tensor& dres, at::Tensor& dres16,
-                   at::Tensor& scratch, at::Tensor& dgamma, at::Tensor& dbeta);
+                   at::Tensor& scratch, at::Tensor& dgamma, at::Tensor& dbeta, int64_t dy_srcs);
+void resid_sum_ln(const at::Tensor& x, const at::Tensor& parts, int64_t nsrc, const at::Tensor& bias,
+                  at::Tensor& x_new, const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
+                  const c10::optional<at::Tensor>& y, const c10::optional<at::Tensor>& mean,
+                  const c10::optional<at::Tensor>& rstd, double eps);
 void colsum_bf16(const at::Tensor& x, at::Tensor& out);
 void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                        at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean);

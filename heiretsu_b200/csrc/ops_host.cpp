@@ -17,7 +17,9 @@ void ln_fwd_launch(const float*, const float*, const float*, __nv_bfloat16*, flo
                    cudaStream_t);
 int ln_bwd_num_ctas(int M, int device);
 void ln_bwd_launch(const float*, const float*, const float*, const float*, const float*, const float*, float*,
-                   __nv_bfloat16*, float*, int, float*, float*, int, int, cudaStream_t);
+                   __nv_bfloat16*, float*, int, float*, float*, int, int, int, long, cudaStream_t);
+void resid_sum_ln_launch(const float*, const __nv_bfloat16*, int, long, const float*, float*, const float*,
+                         const float*, __nv_bfloat16*, float*, float*, int, int, float, cudaStream_t);
 void colsum_bf16_launch(const __nv_bfloat16*, long, int, int, float*, cudaStream_t);
 void ce_fwd_launch(const __nv_bfloat16*, long, int, int, const int64_t*, int, float*, float*, float*, float*,
                    cudaStream_t);
@@ -67,7 +69,7 @@ int64_t layernorm_bwd_scratch_rows(int64_t M) { return ln_bwd_num_ctas(static_ca
 
 void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& mean, const at::Tensor& rstd,
                    const at::Tensor& w, const at::Tensor& dres_in, at::Tensor& dres, at::Tensor& dres16,
-                   at::Tensor& scratch, at::Tensor& dgamma, at::Tensor& dbeta) {
+                   at::Tensor& scratch, at::Tensor& dgamma, at::Tensor& dbeta, int64_t dy_srcs) {
   CHECK_CUDA(dy);
   CHECK_DT(dy, at::kFloat);
   CHECK_CONTIG(dy);
@@ -85,9 +87,30 @@ void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   const int M = x.numel() / H;
   const int ctas = ln_bwd_num_ctas(M, x.get_device());
   TORCH_CHECK(scratch.numel() >= (int64_t)ctas * 2 * H, "layernorm_bwd: scratch too small");
+  TORCH_CHECK(dy_srcs >= 1 && dy.numel() >= dy_srcs * (int64_t)M * H, "layernorm_bwd: dy holds dy_srcs slots of [M, H]");
   ln_bwd_launch(ptr<float>(dy), ptr<float>(x), ptr<float>(mean), ptr<float>(rstd), ptr<float>(w),
                 ptr<float>(dres_in), ptr<float>(dres), ptr<__nv_bfloat16>(dres16), ptr<float>(scratch), ctas,
-                ptr<float>(dgamma), ptr<float>(dbeta), M, H, stream());
+                ptr<float>(dgamma), ptr<float>(dbeta), M, H, static_cast<int>(dy_srcs), (long)M * H, stream());
+}
+
+void resid_sum_ln(const at::Tensor& x, const at::Tensor& parts, int64_t nsrc, const at::Tensor& bias,
+                  at::Tensor& x_new, const c10::optional<at::Tensor>& w, const c10::optional<at::Tensor>& b,
+                  const c10::optional<at::Tensor>& y, const c10::optional<at::Tensor>& mean,
+                  const c10::optional<at::Tensor>& rstd, double eps) {
+  CHECK_CUDA(x);
+  CHECK_DT(x, at::kFloat);
+  CHECK_CONTIG(x);
+  CHECK_DT(parts, at::kBFloat16);
+  CHECK_DT(x_new, at::kFloat);
+  const int H = x.size(-1);
+  const int M = x.numel() / H;
+  TORCH_CHECK(parts.numel() >= nsrc * (int64_t)M * H, "resid_sum_ln: parts holds nsrc slots of [M, H]");
+  const bool ln = w && w->defined();
+  c10::cuda::CUDAGuard g(x.device());
+  resid_sum_ln_launch(ptr<float>(x), ptr<__nv_bfloat16>(parts), static_cast<int>(nsrc), (long)M * H, ptr<float>(bias),
+                      ptr<float>(x_new), ln ? ptr<float>(*w) : nullptr, ln ? ptr<float>(*b) : nullptr,
+                      ln ? ptr<__nv_bfloat16>(*y) : nullptr, ln ? ptr<float>(*mean) : nullptr,
+                      ln ? ptr<float>(*rstd) : nullptr, M, H, static_cast<float>(eps), stream());
 }
 
 void colsum_bf16(const at::Tensor& x, at::Tensor& out) {

@@ -44,8 +44,8 @@ def fused_supported(cfg, topo=None) -> Tuple[bool, str]:
         return False, "fused path runs without dropout (dropout > 0 uses the plain path)"
     if cfg.num_experts > 0:
         return False, "MoE blocks use the plain path"
-    if topo is not None and getattr(topo, "tp", 1) > 1:
-        return False, "tensor parallelism uses the plain path"
+    if topo is not None and getattr(topo, "tp", 1) > 1 and getattr(topo, "pp", 1) > 1:
+        return False, "tensor x pipeline parallelism uses the plain path"
     return True, ""
 
 
@@ -211,11 +211,38 @@ def head_fused(ln_f, wte: torch.nn.Parameter, x: torch.Tensor, targets: Optional
 
 def gpt_forward_fused(model, idx: torch.Tensor, targets: Optional[torch.Tensor], return_logits: bool = True):
     cfg = model.cfg
+    topo = getattr(model, "topo", None)
+    if topo is not None and getattr(topo, "tp", 1) > 1:
+        return _gpt_forward_fused_tp(model, idx, targets)
     x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx)
     x, aux = blocks_fused(model.tr.h, x, cfg)
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x, targets, cfg.vocab_size,
                               want_logits=return_logits)
     return logits, loss, aux
+
+
+def _gpt_forward_fused_tp(model, idx, targets):
+    """Tensor-parallel forward on this rank's token shard (whole sequences).
+
+    The returned loss is this shard's mean loss divided by tp, so that the sum
+    over the TP group is the dense model's mean loss (and the gradients match)."""
+    from .fused_tp import blocks_fused_tp, tp_shard_rows, tp_supported
+
+    cfg, topo = model.cfg, model.topo
+    B, T = idx.shape
+    ok, why = tp_supported(cfg, topo, B, T)
+    if not ok:
+        raise ValueError(f"fused tensor parallelism: {why}")
+    r0, Ms = tp_shard_rows(topo, B, T)
+    Bs = Ms // T
+    idx_s = idx.reshape(-1)[r0:r0 + Ms].view(Bs, T)
+    x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx_s)
+    x = blocks_fused_tp(model.tr.h, x.reshape(Ms, -1), cfg, topo, B, T)
+    tgt = targets.reshape(-1)[r0:r0 + Ms].view(Bs, T) if targets is not None else None
+    logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x.view(Bs, T, -1), tgt, cfg.vocab_size,
+                              want_logits=False)
+    aux = torch.zeros((), device=idx.device, dtype=torch.float32)
+    return None, (loss / topo.tp if loss is not None else None), aux
 
 
 def enable_fused(module: torch.nn.Module, cfg, topo=None) -> bool:

@@ -30,14 +30,22 @@ def layernorm_fwd(x: torch.Tensor, w: torch.Tensor, b: torch.Tensor, eps: float 
     return y, mean, rstd
 
 
-def layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dgamma, dbeta, scratch=None):
-    """dres = dres_in + dLN/dx(dy); dres16 = bf16(dres); dgamma/dbeta (fp32) += partials."""
+def layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dgamma, dbeta, scratch=None, dy_srcs: int = 1):
+    """dres = dres_in + dLN/dx(dy); dres16 = bf16(dres); dgamma/dbeta (fp32) += partials.
+
+    With ``dy_srcs > 1`` the output gradient is the sum of that many [M, H]
+    slots of ``dy`` (the receive buffer of a reduce-scatter)."""
     H = x.shape[-1]
     M = x.numel() // H
     if scratch is None:
         rows = _ext().layernorm_bwd_scratch_rows(M)
         scratch = torch.empty(rows * 2 * H, device=x.device, dtype=torch.float32)
-    _ext().layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, scratch, dgamma, dbeta)
+    _ext().layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, scratch, dgamma, dbeta, dy_srcs)
+
+
+def resid_sum_ln(x, parts, nsrc, bias, x_new, w=None, b=None, y=None, mean=None, rstd=None, eps: float = 1e-5):
+    """x_new = x + sum of `nsrc` bf16 partial slots + bias; optionally y = LN(x_new) (bf16)."""
+    _ext().resid_sum_ln(x, parts, nsrc, bias, x_new, w, b, y, mean, rstd, eps)
 
 
 def colsum_bf16(x: torch.Tensor, out: torch.Tensor) -> None:

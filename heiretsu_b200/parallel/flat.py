@@ -26,7 +26,8 @@ def _align(n: int) -> int:
 
 class FlatParams:
     def __init__(self, module: torch.nn.Module, device: torch.device,
-                 weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None, grad_group=None):
+                 weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None, grad_group=None,
+                 tp_group=None):
         named: List[Tuple[str, torch.nn.Parameter]] = []
         seen = set()
         for name, p in module.named_parameters():
@@ -53,11 +54,19 @@ class FlatParams:
         self.data = torch.zeros(total, device=device, dtype=torch.float32)
         # With a DP group on CUDA, the gradients live in a symmetric (peer-mapped)
         # buffer so the fused all-reduce can read and write them over NVLink.
+        # The same allocation is peer-mapped in the DP group (gradient
+        # averaging) and in the TP group (summing TP-replicated gradients).
         self.grad_symm = None
-        if grad_group is not None and device.type == "cuda":
+        self.grad_symm_tp = None
+        if (grad_group is not None or tp_group is not None) and device.type == "cuda":
+            from ..ops._C import load as _load
             from .symm import SymmetricBuffer
-            self.grad_symm = SymmetricBuffer(grad_group, total * 4, device)
-            self.grad = self.grad_symm.tensor(torch.float32, total)
+            raw = _load().raw_malloc(total * 4)
+            if grad_group is not None:
+                self.grad_symm = SymmetricBuffer(grad_group, total * 4, device, local_ptr=raw)
+            if tp_group is not None:
+                self.grad_symm_tp = SymmetricBuffer(tp_group, total * 4, device, local_ptr=raw)
+            self.grad = _load().tensor_from_ptr(raw, total, torch.float32, device.index)
         else:
             self.grad = torch.zeros(total, device=device, dtype=torch.float32)
         self.data16 = torch.zeros(total, device=device, dtype=torch.bfloat16)

@@ -32,7 +32,9 @@ def _exchange(group, local_bytes: bytes) -> List[bytes]:
 
 
 class SymmetricBuffer:
-    def __init__(self, group, nbytes: int, device: torch.device):
+    def __init__(self, group, nbytes: int, device: torch.device, local_ptr: Optional[int] = None):
+        """Allocate (or, with ``local_ptr``, share an existing raw allocation of
+        this rank) and map every peer's copy in ``group``."""
         ext = load()
         self.group = group
         self.rank = dist.get_rank(group)
@@ -42,7 +44,7 @@ class SymmetricBuffer:
         self.device = device
         self.nbytes = nbytes
         with torch.cuda.device(device):
-            self.local_ptr = ext.raw_malloc(nbytes)
+            self.local_ptr = ext.raw_malloc(nbytes) if local_ptr is None else local_ptr
             self.signal_ptr = ext.raw_malloc(SIGNAL_BYTES)
             handles = _exchange(group, ext.ipc_handle(self.local_ptr))
             sig_handles = _exchange(group, ext.ipc_handle(self.signal_ptr))
@@ -60,7 +62,15 @@ class SymmetricBuffer:
         return load().tensor_from_ptr(self.local_ptr + offset_bytes, numel, dtype, self.device.index)
 
     def barrier(self) -> None:
+        """Device-side barrier of the group (bounded wait), ordered on the current stream."""
         load().group_barrier(self.ptrs, self.signal_ptrs, self.rank, self.counter)
+
+    def sum_range(self, start_elem: int, n_elem: int, scale: float = 1.0) -> None:
+        """In place over the group: fp32 elements [start, start+n) <- scale * sum over ranks (NVLink, one kernel)."""
+        if self.world == 1 or n_elem == 0:
+            return
+        off = start_elem * 4
+        load().dp_allreduce([p + off for p in self.ptrs], self.signal_ptrs, self.rank, n_elem, scale, self.counter)
 
 
 def check_comm_status(device: int) -> None:

@@ -209,7 +209,8 @@ class Engine:
 
             use_p2p = topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
             self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo),
-                                   grad_group=topo.dp_group if use_p2p else None)
+                                   grad_group=topo.dp_group if use_p2p else None,
+                                   tp_group=topo.tp_group if topo.tp > 1 else None)
             self.module.fused = True
             self.optimizer = FusedAdamW(self.flat, lr=args.learning_rate, betas=args.betas,
                                         weight_decay=args.weight_decay, max_grad_norm=args.grad_clip,
@@ -236,7 +237,7 @@ class Engine:
         # reduction, clipping, AdamW) once shapes are known; the first
         # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).
         self.use_graph = (bool(getattr(args, "cuda_graph", 1)) and self.fused and not self.use_pipeline
-                          and (self.reducer is None or self.reducer.backend == "p2p"))
+                          and (self.reducer is None or self.reducer.backend == "p2p") and self.mp_group is None)
         self._graph = None
         self._eager_steps = 0
         self.GRAPH_WARMUP = 2
@@ -292,6 +293,7 @@ class Engine:
             ((loss + aux_mb) / accum).backward()
             aux = aux + aux_mb.detach().float()
             loss_sum = loss_sum + loss.detach().float()
+        self.tp_sync_grads()
         if self.reducer is not None:
             self.reducer.reduce()
         self.optimizer.step_device()
@@ -330,6 +332,8 @@ class Engine:
                 else:
                     combined.backward()
             loss_scalar = loss_sum / accum
+            if self.fused and topo.tp > 1 and dist.is_initialized():
+                dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.tp_group)
         if loss_scalar is not None and topo.dp_group is not None and dist.is_initialized():
             dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.dp_group)
             loss_scalar = loss_scalar / topo.dp
@@ -339,9 +343,18 @@ class Engine:
         self.sync_and_step()
         return loss_scalar, aux
 
+    def tp_sync_grads(self) -> None:
+        """Sum the token-shard partial gradients of TP-replicated parameters over the TP group."""
+        if not self.fused or self.topo.tp == 1 or self.flat.grad_symm_tp is None:
+            return
+        for start, end, wgt in self.flat.ranges:
+            if wgt < 1.0 and end > start:
+                self.flat.grad_symm_tp.sum_range(start, end - start, 1.0)
+
     def sync_and_step(self) -> None:
         args = self.args
         if self.fused:
+            self.tp_sync_grads()
             if self.reducer is not None:
                 self.reducer.reduce()
             self.optimizer.step()
@@ -392,6 +405,9 @@ class Engine:
                 x, y = loader.next_batch(self.device)
                 with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype, enabled=self.use_amp):
                     _, loss, _ = self.forward_module(x, y)
+                if self.fused and self.topo.tp > 1 and dist.is_initialized():
+                    loss = loss.detach().clone()
+                    dist.all_reduce(loss, group=self.topo.tp_group)  # shard losses / tp sum to the mean
                 losses.append(float(loss.item()))
         self.module.train()
         return sum(losses) / len(losses) if losses else None
