@@ -12,7 +12,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("aux") = py::none(), py::arg("resid") = py::none(), py::arg("block_n") = 128,
         py::arg("ag_src") = std::vector<uint64_t>{}, py::arg("ag_flags") = py::none(), py::arg("ag_rank") = 0,
         py::arg("ag_rows") = 0, py::arg("rs_dst") = std::vector<uint64_t>{}, py::arg("rs_rank") = 0,
-        py::arg("rs_rows") = 0);
+        py::arg("rs_rows") = 0, py::arg("grp_mode") = 0, py::arg("grp_off") = py::none(), py::arg("grp_n") = 0,
+        py::arg("grp_b_off") = 0, py::arg("grp_c_off") = 0);
   m.def("layernorm_fwd", &hb::layernorm_fwd);
   m.def("layernorm_bwd_scratch_rows", &hb::layernorm_bwd_scratch_rows);
   m.def("layernorm_bwd", &hb::layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
@@ -39,4 +40,10 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &hb::ipc_close);
   m.def("dp_allreduce", &hb::dp_allreduce);
   m.def("group_barrier", &hb::group_barrier);
+  m.def("moe_route", &hb::moe_route);
+  m.def("moe_gather", &hb::moe_gather);
+  m.def("moe_combine", &hb::moe_combine);
+  m.def("moe_combine_bwd", &hb::moe_combine_bwd);
+  m.def("moe_unpermute", &hb::moe_unpermute);
+  m.def("moe_router_bwd", &hb::moe_router_bwd);
 }

@@ -27,7 +27,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux,
           const c10::optional<at::Tensor>& resid, int64_t block_n, const std::vector<uint64_t>& ag_src,
           const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
-          const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows) {
+          const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows, int64_t grp_mode,
+          const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: operands must be bf16");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D tensors expected");
@@ -38,8 +39,9 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   c10::cuda::CUDAGuard guard(a.device());
   const int M = a_mn ? a.size(1) : a.size(0);
   const int K = a_mn ? a.size(0) : a.size(1);
-  TORCH_CHECK((b_mn ? b.size(0) : b.size(1)) == K, "gemm: K mismatch");
-  TORCH_CHECK((b_mn ? b.size(1) : b.size(0)) <= N, "gemm: B has more rows than N");
+  TORCH_CHECK(grp_mode == 1 ? (b_mn ? b.size(0) % K == 0 : b.size(1) == K) : (b_mn ? b.size(0) : b.size(1)) == K,
+              "gemm: K mismatch");
+  TORCH_CHECK(grp_mode == 1 || (b_mn ? b.size(1) : b.size(0)) <= N, "gemm: B has more rows than N");
   TORCH_CHECK(c.size(0) >= M && c.size(1) >= N, "gemm: output too small");
   const bool out_bf16 = (epi == kEpiBf16 || epi == kEpiBf16Gelu || epi == kEpiBf16Dgelu);
   TORCH_CHECK(c.scalar_type() == (out_bf16 ? at::kBFloat16 : at::kFloat), "gemm: wrong output dtype for epilogue");
@@ -83,7 +85,19 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   const int num_kb = (K + 63) / 64;
   p.kb_per_split = num_kb;
   int e_launch = static_cast<int>(epi);
-  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8 && ag_src.empty() && rs_dst.empty()) {
+  if (grp_mode != 0) {
+    TORCH_CHECK(grp_off && grp_off->defined() && grp_off->scalar_type() == at::kInt && grp_off->is_cuda() &&
+                    grp_off->numel() >= grp_n + 1 && grp_n >= 1,
+                "gemm: grouped mode needs int32 device offsets [groups + 1]");
+    TORCH_CHECK(ag_src.empty() && rs_dst.empty(), "gemm: grouped mode excludes all-gather / reduce-scatter");
+    TORCH_CHECK(grp_mode == 1 || (grp_mode == 2 && a_mn && b_mn), "gemm: grouped mode 2 is the weight-gradient layout");
+    p.grp_mode = static_cast<int>(grp_mode);
+    p.grp_n = static_cast<int>(grp_n);
+    p.grp_off = grp_off->data_ptr<int>();
+    p.grp_b_off = static_cast<int>(grp_b_off);
+    p.grp_c_off = static_cast<int>(grp_c_off);
+  }
+  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8 && ag_src.empty() && rs_dst.empty() && grp_mode == 0) {
     const int sms = num_sms(a.get_device());
     const long tiles = (long)((M + 127) / 128) * ((N + BN - 1) / BN);
     auto eff = [&](int s) {

@@ -275,12 +275,13 @@ __global__ void __launch_bounds__(192, 1)
 
   const int warp = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
-  const int num_m = (p.M + BM - 1) / BM;
+  // Row-grouped GEMMs learn their row count from the device (padded expert segments).
+  const int num_m = (p.grp_mode == 1) ? p.grp_off[p.grp_n] / BM : (p.M + BM - 1) / BM;
   const int num_n = (p.N + BN - 1) / BN;
-  const int num_tiles = num_m * num_n * p.splits;
+  const int num_tiles = num_m * num_n * p.splits * (p.grp_mode == 2 ? p.grp_n : 1);
   const int num_kb_total = (p.K + BK - 1) / BK;
-  // Tile t -> (split, m-block, n-block); rasterisation order set by the host.
-  auto decode = [&](int t, int& mb, int& nb, int& kb0, int& nkb) {
+  // Tile t -> (group/split, m-block, n-block) and its k-block range.
+  auto decode = [&](int t, int& mb, int& nb, int& kb0, int& nkb, int& grp) {
     const int mn = num_m * num_n;
     const int sp = t / mn;
     const int r = t % mn;
@@ -290,6 +291,17 @@ __global__ void __launch_bounds__(192, 1)
       mb = r % num_m, nb = r / num_m;
     }
     if (p.ag_world > 1) mb = (mb + p.ag_rank * (p.ag_rows / BM)) % num_m;  // local shard first, then ring order
+    grp = 0;
+    if (p.grp_mode == 2) {
+      grp = sp;
+      kb0 = p.grp_off[grp] / BK;
+      nkb = (p.grp_off[grp + 1] - p.grp_off[grp]) / BK;
+      return;
+    }
+    if (p.grp_mode == 1) {
+      const int row = mb * BM;
+      while (grp + 1 < p.grp_n && p.grp_off[grp + 1] <= row) ++grp;
+    }
     kb0 = sp * p.kb_per_split;
     nkb = min(p.kb_per_split, num_kb_total - kb0);
   };
@@ -323,8 +335,9 @@ __global__ void __launch_bounds__(192, 1)
       uint32_t phase = 0;
       bool ok = true;
       for (int t = blockIdx.x; t < num_tiles && ok; t += gridDim.x) {
-        int mb, nb, kb0, num_kb;
-        decode(t, mb, nb, kb0, num_kb);
+        int mb, nb, kb0, num_kb, grp;
+        decode(t, mb, nb, kb0, num_kb, grp);
+        const int b_grp_off = (p.grp_mode == 1) ? grp * p.grp_b_off : 0;
         if (p.ag_world > 1 && !ag_wait_rows(p, mb)) {
           ok = false;
           break;
@@ -345,10 +358,11 @@ __global__ void __launch_bounds__(192, 1)
             for (int a = 0; a < BM / 64; ++a) tma_load_2d(sA + a * 8192, &tmA, &full[stage], mb * BM + a * 64, kb * BK);
           }
           if constexpr (!B_MN) {
-            tma_load_2d(sB, &tmB, &full[stage], kb * BK, nb * BN);
+            tma_load_2d(sB, &tmB, &full[stage], kb * BK, nb * BN + b_grp_off);
           } else {
 #pragma unroll
-            for (int a = 0; a < BN / 64; ++a) tma_load_2d(sB + a * 8192, &tmB, &full[stage], nb * BN + a * 64, kb * BK);
+            for (int a = 0; a < BN / 64; ++a)
+              tma_load_2d(sB + a * 8192, &tmB, &full[stage], nb * BN + a * 64, kb * BK + b_grp_off);
           }
           if (++stage == STAGES) {
             stage = 0;
@@ -379,8 +393,8 @@ __global__ void __launch_bounds__(192, 1)
         if (!mbar_wait(&tempty[acc], acc_phase ^ 1u, p.status, 2)) break;
         tc_fence_after();
         const uint32_t d_tmem = tmem_base + acc * BN;
-        int mb_, nb_, kb0_, num_kb;
-        decode(t, mb_, nb_, kb0_, num_kb);
+        int mb_, nb_, kb0_, num_kb, grp_;
+        decode(t, mb_, nb_, kb0_, num_kb, grp_);
         for (int kb = 0; kb < num_kb; ++kb) {
           if (!mbar_wait(&full[stage], phase, p.status, 3)) {
             ok = false;
@@ -417,16 +431,26 @@ __global__ void __launch_bounds__(192, 1)
       const uint32_t acc_phase = (local >> 1) & 1;
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
       tc_fence_after();
-      int mb, nb, kb0_, nkb_;
-      decode(t, mb, nb, kb0_, nkb_);
+      int mb, nb, kb0_, nkb_, grp;
+      decode(t, mb, nb, kb0_, nkb_, grp);
       const int m_base = mb * BM + sub * 32;
+      if (nkb_ <= 0) {  // empty expert segment: nothing was accumulated, nothing to store
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&tempty[acc]);
+        continue;
+      }
 #pragma unroll 1
       for (int c = 0; c < BN / 32; ++c) {
         const int n0 = nb * BN + c * 32;
         if (n0 >= p.N) break;
         float v[32];
         tmem_ld32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN + c * 32, v);
-        if (p.rs_world > 1) {
+        if (p.grp_mode == 2) {
+          GemmParams q = p;  // this expert's block of the stacked weight gradient
+          q.C = static_cast<uint8_t*>(p.C) + (long)grp * p.grp_c_off * p.ldc * 4;
+          gemm_epilogue_chunk<EPI>(q, m_base, n0, v, stg, lane);
+        } else if (p.rs_world > 1) {
           // Partial tile -> slot rs_rank of the owning rank's receive buffer (over NVLink).
           GemmParams q = p;
           const int owner = m_base / p.rs_rows;
@@ -462,7 +486,8 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams&
     HB_CUDA_CHECK(cudaFuncSetAttribute(kern, cudaFuncAttributeMaxDynamicSharedMemorySize, Cfg::SMEM_BYTES));
     attr_set[dev] = true;
   }
-  const int num_tiles = ((p.M + 127) / 128) * ((p.N + BN - 1) / BN) * p.splits;
+  const int num_tiles =
+      ((p.M + 127) / 128) * ((p.N + BN - 1) / BN) * p.splits * (p.grp_mode == 2 ? p.grp_n : 1);
   const int grid = num_tiles < num_sms(dev) ? num_tiles : num_sms(dev);
   kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
   HB_CUDA_CHECK(cudaGetLastError());

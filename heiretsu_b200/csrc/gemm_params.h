@@ -46,6 +46,20 @@ struct GemmParams {
   int rs_rank;
   int rs_rows;
   void* rs_dst[8];
+
+  // Expert-grouped GEMMs (mixture of experts). The rows of the permuted
+  // activations are grouped by expert in segments padded to 128 rows;
+  // grp_off[e] (device memory, grp_n + 1 entries) is the first row of expert e.
+  //   grp_mode 1, row-grouped (forward / dgrad): the m-block's expert e selects
+  //     the weights: B's row (K-major B) or k (MN-major B) coordinate is
+  //     offset by e * grp_b_off. The m-block count is read on the device.
+  //   grp_mode 2, reduction-grouped (weight gradients): tile (e, m, n) reduces
+  //     over the rows of expert e into C rows offset by e * grp_c_off.
+  int grp_mode;
+  int grp_n;
+  const int* grp_off;
+  int grp_b_off;
+  int grp_c_off;
 };
 
 }  // namespace hb

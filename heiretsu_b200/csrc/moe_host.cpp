@@ -1,0 +1,99 @@
+// Torch-facing entry points of the mixture-of-experts kernels (moe.cu).
+#include <ATen/cuda/CUDAContext.h>
+#include <c10/cuda/CUDAGuard.h>
+#include <cuda_bf16.h>
+#include <torch/extension.h>
+
+#include "host_utils.h"
+#include "ops.h"
+
+namespace hb {
+
+void moe_route_launch(const __nv_bfloat16*, const float*, int, int, int, int, float, float*, int*, float*, int*, float*,
+                      int*, float*, int*, cudaStream_t);
+void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, cudaStream_t);
+void moe_combine_launch(const __nv_bfloat16*, const int*, const float*, const float*, int, int, int, float*,
+                        cudaStream_t);
+void moe_combine_bwd_launch(const float*, const __nv_bfloat16*, const int*, const float*, int, int, int,
+                            __nv_bfloat16*, float*, cudaStream_t);
+void moe_unpermute_launch(const float*, const int*, int, int, int, float*, cudaStream_t);
+void moe_router_bwd_launch(const float*, const int*, const float*, const float*, const float*, const int*, float, int,
+                           int, int, int, const float*, __nv_bfloat16*, long, float*, cudaStream_t);
+
+template <typename T>
+static T* P(const at::Tensor& t) {
+  return reinterpret_cast<T*>(t.data_ptr());
+}
+static cudaStream_t S() { return at::cuda::getCurrentCUDAStream(); }
+
+static void check_i32(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kInt && t.is_contiguous(), what, ": int32 contiguous CUDA tensor");
+}
+static void check_f32(const at::Tensor& t, const char* what) {
+  TORCH_CHECK(t.is_cuda() && t.scalar_type() == at::kFloat && t.is_contiguous(), what, ": fp32 contiguous CUDA tensor");
+}
+
+void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef, at::Tensor& probs, at::Tensor& topi,
+               at::Tensor& topw, at::Tensor& counts, at::Tensor& probsum, at::Tensor& off, at::Tensor& aux,
+               at::Tensor& pos) {
+  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "moe_route: x bf16 [N, H]");
+  check_f32(wg, "moe_route: gate weight [E, H]");
+  check_f32(probs, "moe_route: probs");
+  check_i32(topi, "moe_route: topi");
+  check_i32(counts, "moe_route: counts");
+  check_i32(off, "moe_route: off");
+  check_i32(pos, "moe_route: pos");
+  c10::cuda::CUDAGuard g(x.device());
+  const int N = x.size(0), H = x.size(1), E = wg.size(0);
+  TORCH_CHECK(wg.size(1) == H && probs.numel() >= (int64_t)N * E && topi.numel() >= N * K && off.numel() >= E + 1 &&
+                  pos.numel() >= N * K,
+              "moe_route: shape mismatch");
+  moe_route_launch(P<__nv_bfloat16>(x), P<float>(wg), N, H, E, K, static_cast<float>(coef), P<float>(probs),
+                   P<int>(topi), P<float>(topw), P<int>(counts), P<float>(probsum), P<int>(off), P<float>(aux),
+                   P<int>(pos), S());
+}
+
+void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && xp.scalar_type() == at::kBFloat16 && x.size(1) == xp.size(1),
+              "moe_gather: bf16 [N, H] -> [R, H]");
+  c10::cuda::CUDAGuard g(x.device());
+  moe_gather_launch(P<__nv_bfloat16>(x), P<int>(pos), x.size(0), K, x.size(1), P<__nv_bfloat16>(xp), S());
+}
+
+void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw, const at::Tensor& resid,
+                 at::Tensor& out) {
+  check_f32(resid, "moe_combine: resid");
+  check_f32(out, "moe_combine: out");
+  c10::cuda::CUDAGuard g(yp.device());
+  const int N = resid.size(0), H = resid.size(1), K = topw.size(1);
+  moe_combine_launch(P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), P<float>(resid), N, K, H, P<float>(out), S());
+}
+
+void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
+                     at::Tensor& dyp, at::Tensor& dw) {
+  check_f32(dy, "moe_combine_bwd: dy");
+  c10::cuda::CUDAGuard g(dy.device());
+  const int N = dy.size(0), H = dy.size(1), K = topw.size(1);
+  moe_combine_bwd_launch(P<float>(dy), P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), N, K, H,
+                         P<__nv_bfloat16>(dyp), P<float>(dw), S());
+}
+
+void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx) {
+  check_f32(dxp, "moe_unpermute: dxp");
+  check_f32(dx, "moe_unpermute: dx");
+  c10::cuda::CUDAGuard g(dx.device());
+  moe_unpermute_launch(P<float>(dxp), P<int>(pos), dx.size(0), K, dx.size(1), P<float>(dx), S());
+}
+
+void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::Tensor& topw, const at::Tensor& dw,
+                    const at::Tensor& daux, const at::Tensor& counts, double coef, const at::Tensor& wg,
+                    at::Tensor& dlogits, at::Tensor& dx) {
+  check_f32(dx, "moe_router_bwd: dx");
+  c10::cuda::CUDAGuard g(probs.device());
+  const int N = probs.size(0), E = probs.size(1), K = topi.size(1), H = wg.size(1);
+  moe_router_bwd_launch(P<float>(probs), P<int>(topi), P<float>(topw), P<float>(dw), P<float>(daux), P<int>(counts),
+                        static_cast<float>(coef), N, H, E, K, P<float>(wg), P<__nv_bfloat16>(dlogits),
+                        dlogits.stride(0), P<float>(dx), S());
+}
+
+}  // namespace hb

@@ -9,7 +9,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& bias, const c10::optional<at::Tensor>& aux,
           const c10::optional<at::Tensor>& resid, int64_t block_n, const std::vector<uint64_t>& ag_src,
           const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
-          const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows);
+          const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows, int64_t grp_mode,
+          const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off);
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, at::Tensor& y, at::Tensor& mean,
                    at::Tensor& rstd, double eps);
@@ -48,4 +49,16 @@ void dp_allreduce(const std::vector<uint64_t>& data, const std::vector<uint64_t>
                   double scale, const at::Tensor& counter);
 void group_barrier(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,
                    const at::Tensor& counter);
+void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef, at::Tensor& probs, at::Tensor& topi,
+               at::Tensor& topw, at::Tensor& counts, at::Tensor& probsum, at::Tensor& off, at::Tensor& aux,
+               at::Tensor& pos);
+void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp);
+void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw, const at::Tensor& resid,
+                 at::Tensor& out);
+void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
+                     at::Tensor& dyp, at::Tensor& dw);
+void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx);
+void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::Tensor& topw, const at::Tensor& dw,
+                    const at::Tensor& daux, const at::Tensor& counts, double coef, const at::Tensor& wg,
+                    at::Tensor& dlogits, at::Tensor& dx);
 }  // namespace hb

@@ -42,8 +42,8 @@ def fused_supported(cfg, topo=None) -> Tuple[bool, str]:
         return False, "fused path needs n_embed % 128 == 0"
     if cfg.dropout > 0:
         return False, "fused path runs without dropout (dropout > 0 uses the plain path)"
-    if cfg.num_experts > 0:
-        return False, "MoE blocks use the plain path"
+    if cfg.num_experts > 0 and topo is not None and getattr(topo, "ep", 1) > 1:
+        return False, "expert parallelism uses the plain path"
     if topo is not None and getattr(topo, "tp", 1) > 1 and getattr(topo, "pp", 1) > 1:
         return False, "tensor x pipeline parallelism uses the plain path"
     return True, ""
@@ -74,27 +74,29 @@ def embed_fused(wte: torch.nn.Parameter, wpe: torch.nn.Parameter, idx: torch.Ten
 
 
 # ---------------------------------------------------------------------------
-def _dense_block_fwd(blk, x: torch.Tensor, B: int, T: int, keep: bool):
-    """x fp32 [M, H] -> x2 fp32 [M, H] (new tensor); returns (x2, saved activations)."""
-    attn, mlp = blk.attn, blk.mlp
-    nh = attn.nh_tp
+def _attn_fwd(blk, x: torch.Tensor, B: int, T: int, keep: bool):
+    """Attention sub-layer: x fp32 [M, H] -> x1 = x + c_proj(attn(c_attn(ln_1(x))))."""
+    attn = blk.attn
     xn, m1, r1 = K.layernorm_fwd(x, blk.ln_1.weight, blk.ln_1.bias, LN_EPS)
     qkv = G.linear_fwd(xn, attn.c_attn.weight.w16, attn.c_attn.bias)
-    y, lse = K.attention_fwd(qkv, B, T, nh)
+    y, lse = K.attention_fwd(qkv, B, T, attn.nh_tp)
     x1 = G.linear_fwd_resid(y, attn.c_proj.weight.w16, attn.c_proj.bias, x)
+    return x1, ((x, xn, m1, r1, qkv, y, lse) if keep else None)
+
+
+def _mlp_fwd(blk, x1: torch.Tensor, keep: bool):
+    """Dense MLP sub-layer: x2 = x1 + c_proj(gelu(c_fc(ln_2(x1))))."""
+    mlp = blk.mlp
     xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
     h, pre = G.linear_fwd_gelu(xn2, mlp.c_fc.weight.w16, mlp.c_fc.bias)
     x2 = G.linear_fwd_resid(h, mlp.c_proj.weight.w16, mlp.c_proj.bias, x1)
-    saved = (x, xn, m1, r1, qkv, y, lse, x1, xn2, m2, r2, pre, h) if keep else None
-    return x2, saved
+    return x2, ((x1, xn2, m2, r2, pre, h) if keep else None)
 
 
-def _dense_block_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: int, T: int, ws: dict):
-    """In place: dres (fp32) / dres16 (bf16) go from d(x2) to d(x)."""
-    attn, mlp = blk.attn, blk.mlp
-    nh = attn.nh_tp
-    x, xn, m1, r1, qkv, y, lse, x1, xn2, m2, r2, pre, h = saved
-    # MLP sub-layer: x2 = x1 + c_proj(gelu(c_fc(ln_2(x1))))
+def _mlp_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, ws: dict):
+    """In place: dres (fp32) / dres16 (bf16) go from d(x2) to d(x1)."""
+    mlp = blk.mlp
+    x1, xn2, m2, r2, pre, h = saved
     dpre = G.linear_dgrad(dres16, mlp.c_proj.weight.w16, gelu_pre=pre)
     G.linear_wgrad(dres16, h, out=mlp.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(dres16, mlp.c_proj.bias.main_grad)
@@ -104,12 +106,16 @@ def _dense_block_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: in
     del dpre
     K.layernorm_bwd(dxn2, x1, m2, r2, blk.ln_2.weight, dres, dres, dres16, blk.ln_2.weight.main_grad,
                     blk.ln_2.bias.main_grad, scratch=ws["ln_scratch"])
-    del dxn2
-    # attention sub-layer: x1 = x + c_proj(attn(c_attn(ln_1(x))))
+
+
+def _attn_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: int, T: int, ws: dict):
+    """In place: dres / dres16 go from d(x1) to d(x)."""
+    attn = blk.attn
+    x, xn, m1, r1, qkv, y, lse = saved
     dy = G.linear_dgrad(dres16, attn.c_proj.weight.w16)
     G.linear_wgrad(dres16, y, out=attn.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(dres16, attn.c_proj.bias.main_grad)
-    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, nh)
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, attn.nh_tp)
     del dy
     G.linear_wgrad(dqkv, xn, out=attn.c_attn.weight.main_grad, accumulate=True)
     K.colsum_bf16(dqkv, attn.c_attn.bias.main_grad)
@@ -125,38 +131,58 @@ def _ln_scratch(M: int, H: int, device) -> torch.Tensor:
     return torch.empty(rows * 2 * H, device=device, dtype=torch.float32)
 
 
+def _is_moe(blk) -> bool:
+    return hasattr(blk, "moe")
+
+
 class _Body(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x, blocks, B, T):
-        keep = torch.is_grad_enabled() or x.requires_grad
+        from .fused_moe import moe_sublayer_fwd
+
+        keep = x.requires_grad
         saved: List = []
+        aux_total = torch.zeros((), device=x.device, dtype=torch.float32)
         for blk in blocks:
-            x, s = _dense_block_fwd(blk, x, B, T, keep)
-            saved.append(s)
+            x, sa = _attn_fwd(blk, x, B, T, keep)
+            if _is_moe(blk):
+                x, aux, sm = moe_sublayer_fwd(blk, None, x, keep)
+                aux_total = aux_total + aux
+            else:
+                x, sm = _mlp_fwd(blk, x, keep)
+            saved.append((sa, sm))
         ctx.blocks, ctx.saved, ctx.B, ctx.T = blocks, saved, B, T
-        return x
+        return x, aux_total
 
     @staticmethod
-    def backward(ctx, dx):
+    def backward(ctx, dx, daux):
+        from .fused_moe import moe_sublayer_bwd
+
         B, T = ctx.B, ctx.T
         dres = dx.contiguous().clone()
         dres16 = K.f32_to_bf16(dres)
         M, H = dres.shape
         ws = {"ln_scratch": _ln_scratch(M, H, dres.device)}
-        for blk, s in zip(reversed(ctx.blocks), reversed(ctx.saved)):
-            _dense_block_bwd(blk, s, dres, dres16, B, T, ws)
+        if daux is None:
+            daux = torch.zeros((), device=dres.device)
+        for blk, (sa, sm) in zip(reversed(ctx.blocks), reversed(ctx.saved)):
+            if _is_moe(blk):
+                moe_sublayer_bwd(blk, None, sm, dres, dres16, daux, ws["ln_scratch"])
+            else:
+                _mlp_bwd(blk, sm, dres, dres16, ws)
+            _attn_bwd(blk, sa, dres, dres16, B, T, ws)
         ctx.saved = None
         return dres, None, None, None
 
 
 def blocks_fused(blocks, x: torch.Tensor, cfg) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Run a list of dense blocks on x [B, T, H] (any float dtype); returns (fp32 x, aux=0)."""
+    """Run a list of blocks (dense or MoE) on x [B, T, H]; returns (fp32 x, summed MoE aux loss)."""
     B, T, H = x.shape
     x2 = x.reshape(B * T, H)
     if x2.dtype != torch.float32:
         x2 = x2.float()
-    out = _Body.apply(x2.contiguous(), list(blocks), B, T)
-    return out.view(B, T, H), torch.zeros((), device=x.device, dtype=torch.float32)
+    out, aux = _Body.apply(x2.contiguous(), list(blocks), B, T)
+    return out.view(B, T, H), aux
 
 
 # ---------------------------------------------------------------------------
@@ -237,12 +263,13 @@ def _gpt_forward_fused_tp(model, idx, targets):
     Bs = Ms // T
     idx_s = idx.reshape(-1)[r0:r0 + Ms].view(Bs, T)
     x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx_s)
-    x = blocks_fused_tp(model.tr.h, x.reshape(Ms, -1), cfg, topo, B, T)
+    x, aux = blocks_fused_tp(model.tr.h, x.reshape(Ms, -1), cfg, topo, B, T)
     tgt = targets.reshape(-1)[r0:r0 + Ms].view(Bs, T) if targets is not None else None
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x.view(Bs, T, -1), tgt, cfg.vocab_size,
                               want_logits=False)
-    aux = torch.zeros((), device=idx.device, dtype=torch.float32)
-    return None, (loss / topo.tp if loss is not None else None), aux
+    # Each TP rank routes only its token shard; the shard aux losses / tp sum to
+    # the mean over shards (the dense aux uses all tokens at once).
+    return None, (loss / topo.tp if loss is not None else None), aux / topo.tp
 
 
 def enable_fused(module: torch.nn.Module, cfg, topo=None) -> bool:

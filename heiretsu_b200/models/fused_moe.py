@@ -1,0 +1,127 @@
+"""Fused mixture-of-experts sub-layer (router, permutation, grouped expert GEMMs, combine).
+
+Forward, for the LayerNorm output xn [N, H] of this rank's tokens:
+
+    route      logits = xn Wg^T -> softmax -> top-k -> renormalise; per-expert
+               counts, padded segment offsets, row positions and the
+               load-balancing aux loss (moe.cu; no host synchronisation)
+    gather     xp[pos[t, k]] = xn[t]                 (expert-grouped, 128-padded)
+    expert 1   hp = GELU(xp W1_e^T)                  (row-grouped tcgen05 GEMM)
+    expert 2   yp = hp W2_e^T                        (row-grouped tcgen05 GEMM)
+    combine    x_new[t] = x[t] + sum_k w[t, k] yp[pos[t, k]]
+
+The local experts' w1 (and w2) are stored back to back in the flat parameter
+buffer, so each grouped GEMM reads one [E*I, H] weight matrix and picks the
+expert's block from the m-block's segment. Backward mirrors every step; the
+weight gradients use the reduction-grouped GEMM (tile = expert, m, n) over
+exactly that expert's rows. Semantics are the reference's MoELayer
+(moe.py:245-405) with routing weights and aux loss differentiable.
+"""
+from __future__ import annotations
+
+import torch
+
+from ..ops import gemm as G
+from ..ops import kernels as K
+from ..ops._C import load as _ext
+
+LN_EPS = 1e-5
+PAD = 128
+
+
+def _stacks(moe, flat=None):
+    ex = moe.expert_group.experts
+    flat = flat or ex[0].w1.weight.flat_owner
+    w1, g1 = flat.stacked([e.w1.weight for e in ex])
+    w2, g2 = flat.stacked([e.w2.weight for e in ex])
+    return w1, g1, w2, g2
+
+
+def moe_route_and_experts(moe, xn2: torch.Tensor, flat=None):
+    """Router + permutation + the two grouped expert GEMMs for bf16 xn2 [N, H].
+
+    Returns (aux, state) where state holds everything combine / backward need."""
+    ext = _ext()
+    N, H = xn2.shape
+    E = moe.num_local_experts
+    Kk = moe.top_k
+    I = moe.config.intermediate_size
+    dev = xn2.device
+    probs = torch.empty(N, E, device=dev, dtype=torch.float32)
+    topi = torch.empty(N, Kk, device=dev, dtype=torch.int32)
+    topw = torch.empty(N, Kk, device=dev, dtype=torch.float32)
+    counts = torch.empty(E, device=dev, dtype=torch.int32)
+    probsum = torch.empty(E, device=dev, dtype=torch.float32)
+    off = torch.empty(E + 1, device=dev, dtype=torch.int32)
+    aux = torch.empty((), device=dev, dtype=torch.float32)
+    pos = torch.empty(N * Kk, device=dev, dtype=torch.int32)
+    ext.moe_route(xn2, moe.router.gate.weight, Kk, moe.aux_loss_coef, probs, topi, topw, counts, probsum, off, aux,
+                  pos)
+    with torch.no_grad():
+        moe._expert_counts = counts  # diagnostics (reference moe.py:329-332)
+    R = (N * Kk + E * (PAD - 1) + PAD - 1) // PAD * PAD  # capacity: every segment padded to 128 rows
+    xp = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
+    ext.moe_gather(xn2, pos, Kk, xp)
+    w1, _, w2, _ = _stacks(moe, flat)
+    hp = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+    prep = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+    G.gemm(xp, w1, hp, I, G.EPI_BF16_GELU, False, False, aux=prep, grp=(1, off, E, I, 0))
+    yp = torch.empty(R, H, device=dev, dtype=torch.bfloat16)
+    G.gemm(hp, w2, yp, H, G.EPI_BF16, False, False, grp=(1, off, E, H, 0))
+    return aux, (probs, topi, topw, counts, off, pos, xp, hp, prep, yp)
+
+
+def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: torch.Tensor, flat=None):
+    """Backward of route + experts + combine. dx_res: fp32 gradient of the
+    combined output [N, H]. Returns dxn2 (fp32 [N, H]) and accumulates the
+    expert and gate weight gradients."""
+    ext = _ext()
+    probs, topi, topw, counts, off, pos, xp, hp, prep, yp = state
+    N, H = xn2.shape
+    E = moe.num_local_experts
+    Kk = moe.top_k
+    I = moe.config.intermediate_size
+    R = xp.shape[0]
+    dev = xn2.device
+    w1, g1, w2, g2 = _stacks(moe, flat)
+    dyp = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
+    dw = torch.empty(N, Kk, device=dev, dtype=torch.float32)
+    ext.moe_combine_bwd(dx_res, yp, pos, topw, dyp, dw)
+    dprep = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+    G.gemm(dyp, w2, dprep, I, G.EPI_BF16_DGELU, False, True, aux=prep, grp=(1, off, E, H, 0))
+    G.gemm(dyp, hp, g2, I, G.EPI_F32_ACC, True, True, grp=(2, off, E, 0, H))
+    dxp = torch.empty(R, H, device=dev, dtype=torch.float32)
+    G.gemm(dprep, w1, dxp, H, G.EPI_F32, False, True, grp=(1, off, E, I, 0))
+    G.gemm(dprep, xp, g1, H, G.EPI_F32_ACC, True, True, grp=(2, off, E, 0, I))
+    del dyp, dprep
+    dxn2 = torch.empty(N, H, device=dev, dtype=torch.float32)
+    ext.moe_unpermute(dxp, pos, Kk, dxn2)
+    del dxp
+    Ep = (E + 7) // 8 * 8  # row stride of the logits gradient: 16-byte aligned for TMA
+    dlog = torch.zeros(N, Ep, device=dev, dtype=torch.bfloat16)
+    ext.moe_router_bwd(probs, topi, topw, dw, daux.reshape(1).float().contiguous(), counts, moe.aux_loss_coef,
+                       moe.router.gate.weight, dlog, dxn2)
+    G.gemm(dlog[:, :E], xn2, moe.router.gate.weight.main_grad, H, G.EPI_F32_ACC, True, True)
+    return dxn2
+
+
+def moe_sublayer_fwd(blk, flat, x1: torch.Tensor, keep: bool):
+    """x1: fp32 residual [N, H] -> (x2 = x1 + MoE(ln_2(x1)) fp32, aux (0-d), saved)."""
+    moe = blk.moe
+    if moe.ep_world_size != 1:
+        raise NotImplementedError("fused MoE runs with ep == 1 (expert parallelism uses the plain path)")
+    xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
+    aux, state = moe_route_and_experts(moe, xn2, flat)
+    probs, topi, topw, counts, off, pos, xp, hp, prep, yp = state
+    x2 = torch.empty_like(x1)
+    _ext().moe_combine(yp, pos, topw, x1, x2)
+    saved = (x1, xn2, m2, r2, state) if keep else None
+    return x2, aux, saved
+
+
+def moe_sublayer_bwd(blk, flat, saved, dres: torch.Tensor, dres16: torch.Tensor, daux: torch.Tensor, ln_scratch):
+    """In place: dres / dres16 go from d(x2) to d(x1)."""
+    x1, xn2, m2, r2, state = saved
+    dxn2 = moe_experts_bwd(blk.moe, xn2, state, dres, daux, flat)
+    K.layernorm_bwd(dxn2, x1, m2, r2, blk.ln_2.weight, dres, dres, dres16, blk.ln_2.weight.main_grad,
+                    blk.ln_2.bias.main_grad, scratch=ln_scratch)

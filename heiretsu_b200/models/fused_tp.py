@@ -89,8 +89,8 @@ def _empty(*shape, dtype=torch.bfloat16, device=None):
 
 
 def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: bool):
-    """x_s: fp32 residual token shard [Ms, H] -> next residual shard; returns (x2_s, saved)."""
-    attn, mlp = blk.attn, blk.mlp
+    """x_s: fp32 residual token shard [Ms, H] -> next residual shard; returns (x2_s, aux | None, saved)."""
+    attn, mlp = blk.attn, getattr(blk, "mlp", None)
     tp, Ms, H = comm.tp, comm.Ms, comm.H
     M = tp * Ms
     dev = x_s.device
@@ -111,6 +111,14 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
     G.gemm(y, attn.c_proj.weight.w16, comm.recv16_all(), H, G.EPI_BF16, False, False, rs=comm.rs16())
     comm.barrier()
     x1_s = _empty(Ms, H, dtype=torch.float32, device=dev)
+    if hasattr(blk, "moe"):
+        # MoE sub-layer on this rank's tokens: no TP communication (experts are TP-replicated).
+        from .fused_moe import moe_sublayer_fwd
+
+        K.resid_sum_ln(x_s, comm.recv16_all(), tp, attn.c_proj.bias, x1_s)
+        x2_s, aux, sm = moe_sublayer_fwd(blk, None, x1_s, keep)
+        saved = ((x_s, m1, r1, xn_full, qkv, y, lse), sm) if keep else None
+        return x2_s, aux, saved
     xn2_s = comm.src_view(1)
     m2 = _empty(Ms, dtype=torch.float32, device=dev)
     r2 = _empty(Ms, dtype=torch.float32, device=dev)
@@ -127,19 +135,27 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
     comm.barrier()
     x2_s = _empty(Ms, H, dtype=torch.float32, device=dev)
     K.resid_sum_ln(x1_s, comm.recv16_all(), tp, mlp.c_proj.bias, x2_s)
-    saved = (x_s, m1, r1, xn_full, qkv, y, lse, x1_s, m2, r2, xn2_full, pre, h) if keep else None
-    return x2_s, saved
+    saved = ((x_s, m1, r1, xn_full, qkv, y, lse), (x1_s, m2, r2, xn2_full, pre, h)) if keep else None
+    return x2_s, None, saved
 
 
-def tp_block_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T: int, ln_scratch) -> int:
+def tp_block_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T: int, ln_scratch,
+                 daux: Optional[torch.Tensor] = None) -> int:
     """dres: fp32 residual-gradient shard (updated in place); its bf16 copy is in gather source k.
     Returns the gather source holding the bf16 copy of the new dres."""
-    attn, mlp = blk.attn, blk.mlp
+    attn, mlp = blk.attn, getattr(blk, "mlp", None)
     tp, Ms, H = comm.tp, comm.Ms, comm.H
     M = tp * Ms
     dev = dres.device
     nh = attn.nh_tp
-    x_s, m1, r1, xn_full, qkv, y, lse, x1_s, m2, r2, xn2_full, pre, h = saved
+    (x_s, m1, r1, xn_full, qkv, y, lse), sm = saved
+    if hasattr(blk, "moe"):
+        from .fused_moe import moe_sublayer_bwd
+
+        k = 1 - k
+        moe_sublayer_bwd(blk, None, sm, dres, comm.src_view(k), daux, ln_scratch)
+        return _tp_attn_bwd(blk, comm, (x_s, m1, r1, xn_full, qkv, y, lse), dres, k, B, T, ln_scratch)
+    x1_s, m2, r2, xn2_full, pre, h = sm
     n_fc = mlp.c_fc.out_per_partition
     # --- MLP: x2 = x1 + RS(c_proj(gelu(c_fc(AG(ln_2(x1))))))
     comm.barrier()
@@ -156,7 +172,17 @@ def tp_block_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
     k = 1 - k
     K.layernorm_bwd(comm.recv32_all(), x1_s, m2, r2, blk.ln_2.weight, dres, dres, comm.src_view(k),
                     blk.ln_2.weight.main_grad, blk.ln_2.bias.main_grad, scratch=ln_scratch, dy_srcs=tp)
-    # --- attention: x1 = x + RS(c_proj(attn(c_attn(AG(ln_1(x))))))
+    return _tp_attn_bwd(blk, comm, (x_s, m1, r1, xn_full, qkv, y, lse), dres, k, B, T, ln_scratch)
+
+
+def _tp_attn_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T: int, ln_scratch) -> int:
+    """Attention sub-layer backward: x1 = x + RS(c_proj(attn(c_attn(AG(ln_1(x))))))."""
+    attn = blk.attn
+    tp, Ms, H = comm.tp, comm.Ms, comm.H
+    M = tp * Ms
+    dev = dres.device
+    nh = attn.nh_tp
+    x_s, m1, r1, xn_full, qkv, y, lse = saved
     comm.barrier()
     dx1_full = _empty(M, H, device=dev)
     dy = _empty(M, attn.h_tp, device=dev)
@@ -181,16 +207,21 @@ class _TPBody(torch.autograd.Function):
     def forward(ctx, x_s, blocks, comm, B, T):
         keep = x_s.requires_grad
         saved = []
+        aux_total = torch.zeros((), device=x_s.device, dtype=torch.float32)
         comm.barrier()
         for blk in blocks:
-            x_s, s = tp_block_fwd(blk, comm, x_s, B, T, keep)
+            x_s, aux, s = tp_block_fwd(blk, comm, x_s, B, T, keep)
+            if aux is not None:
+                aux_total = aux_total + aux
             saved.append(s)
         ctx.blocks, ctx.saved, ctx.comm, ctx.B, ctx.T = blocks, saved, comm, B, T
-        return x_s
+        return x_s, aux_total
 
     @staticmethod
-    def backward(ctx, dx):
+    def backward(ctx, dx, daux):
         comm = ctx.comm
+        if daux is None:
+            daux = torch.zeros((), device=dx.device)
         dres = dx.contiguous().clone()
         comm.barrier()
         K.f32_to_bf16(dres, comm.src_view(0))
@@ -198,7 +229,7 @@ class _TPBody(torch.autograd.Function):
         ln_scratch = torch.empty(rows * 2 * comm.H, device=dres.device, dtype=torch.float32)
         k = 0
         for blk, s in zip(reversed(ctx.blocks), reversed(ctx.saved)):
-            k = tp_block_bwd(blk, comm, s, dres, k, ctx.B, ctx.T, ln_scratch)
+            k = tp_block_bwd(blk, comm, s, dres, k, ctx.B, ctx.T, ln_scratch, daux)
         ctx.saved = None
         return dres, None, None, None, None
 
@@ -222,6 +253,7 @@ def tp_supported(cfg, topo, B: int, T: int) -> Tuple[bool, str]:
     return True, ""
 
 
-def blocks_fused_tp(blocks, x_s: torch.Tensor, cfg, topo, B: int, T: int) -> torch.Tensor:
+def blocks_fused_tp(blocks, x_s: torch.Tensor, cfg, topo, B: int, T: int):
+    """Returns (x_L token shard, aux loss of this shard's MoE layers)."""
     comm = get_comm(topo, x_s.shape[0], x_s.shape[1], x_s.device)
     return _TPBody.apply(x_s.contiguous(), list(blocks), comm, B, T)

@@ -28,15 +28,18 @@ def _bn(n: int) -> int:
     return 256 if n >= 2048 else 128
 
 
-def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None):
+def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None, grp=None):
     """D = A.B^T-style GEMM (see module doc). ``ag = (src_ptrs, flags, rank, rows)`` turns on
     the in-kernel all-gather of A's token shards; ``rs = (dst_ptrs, rank, rows)`` stores each
-    output tile into its token owner's receive slot (reduce-scatter epilogue)."""
+    output tile into its token owner's receive slot (reduce-scatter epilogue);
+    ``grp = (mode, offsets, n_groups, b_off, c_off)`` runs an expert-grouped GEMM."""
     ag_src, ag_flags, ag_rank, ag_rows = ag if ag is not None else ([], None, 0, 0)
     rs_dst, rs_rank, rs_rows = rs if rs is not None else ([], 0, 0)
+    g_mode, g_off, g_n, g_b, g_c = grp if grp is not None else (0, None, 0, 0, 0)
     load().gemm(a, b, c, int(n), int(epi), bool(a_mn), bool(b_mn), bias, aux, resid,
                 int(block_n if block_n is not None else _bn(n)), list(ag_src), ag_flags, int(ag_rank),
-                int(ag_rows), list(rs_dst), int(rs_rank), int(rs_rows))
+                int(ag_rows), list(rs_dst), int(rs_rank), int(rs_rows), int(g_mode), g_off, int(g_n), int(g_b),
+                int(g_c))
     return c
 
 

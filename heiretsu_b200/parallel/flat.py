@@ -24,6 +24,27 @@ def _align(n: int) -> int:
     return (n + ALIGN - 1) // ALIGN * ALIGN
 
 
+def _stack_experts(named: List[Tuple[str, torch.nn.Parameter]]) -> List[Tuple[str, torch.nn.Parameter]]:
+    """Order parameters so that each MoE layer's expert weights are contiguous:
+    all w1 (expert order), then all w2, at the position of the layer's first expert."""
+    out: List[Tuple[str, torch.nn.Parameter]] = []
+    placed = set()
+    for name, p in named:
+        if name in placed:
+            continue
+        if ".experts." in name:
+            layer = name.split(".experts.")[0]
+            members = [(n, q) for n, q in named if n.startswith(layer + ".experts.")]
+            key = lambda nq: (nq[0].rsplit(".", 2)[-2], int(nq[0].split(".experts.")[1].split(".")[0]))
+            for n, q in sorted(members, key=key):
+                out.append((n, q))
+                placed.add(n)
+            continue
+        out.append((name, p))
+        placed.add(name)
+    return out
+
+
 class FlatParams:
     def __init__(self, module: torch.nn.Module, device: torch.device,
                  weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None, grad_group=None,
@@ -45,7 +66,7 @@ class FlatParams:
         total = 0
         for wgt in sorted(groups):
             start = total
-            for name, p in groups[wgt]:
+            for name, p in _stack_experts(groups[wgt]):
                 order.append((name, p))
                 total += _align(p.numel())
             self.ranges.append((start, total, wgt))
@@ -82,11 +103,26 @@ class FlatParams:
                 p.data = view
                 p.main_grad = self.grad[off:off + n].view(p.shape)
                 p.w16 = self.data16[off:off + n].view(p.shape)
+                p.flat_owner = self
                 self.params.append(p)
                 self.names.append(name)
                 self.offsets.append(off)
                 off += _align(n)
         self.refresh_bf16()
+
+    def stacked(self, params: List[torch.nn.Parameter]):
+        """(bf16 weights, fp32 gradients) of same-shaped parameters stored back to back,
+        viewed as one [len * rows, cols] matrix (the experts of one MoE layer)."""
+        first = params[0]
+        idx = [next(i for i, q in enumerate(self.params) if q is p) for p in params]
+        n = first.numel()
+        for a, b in zip(idx, idx[1:]):
+            if self.offsets[b] != self.offsets[a] + n:
+                raise RuntimeError("stacked parameters are not contiguous in the flat buffer")
+        off = self.offsets[idx[0]]
+        rows, cols = first.shape[0] * len(params), first.shape[1]
+        return (self.data16[off:off + n * len(params)].view(rows, cols),
+                self.grad[off:off + n * len(params)].view(rows, cols))
 
     def refresh_bf16(self) -> None:
         """Re-derive the bf16 shadow from the fp32 master (after init / checkpoint load)."""
