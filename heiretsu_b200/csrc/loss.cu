@@ -171,7 +171,7 @@ namespace {
 
 // Per-row losses of the most recent call (every call overwrites rows [0, M)).
 // Held by every GPU that loads the library, until the process exits.
-__device__ __align__(256) float g_ce_noalloc_rows[HB_CE_NOALLOC_MAX_ROWS];
+static __device__ __align__(256) float g_ce_noalloc_rows[HB_CE_NOALLOC_MAX_ROWS];
 
 std::mutex g_ce_noalloc_mu;
 float* g_ce_noalloc_ptr[64] = {};
@@ -184,7 +184,7 @@ int ce_noalloc_scratch(float** out) {
   std::lock_guard<std::mutex> lk(g_ce_noalloc_mu);
   if (g_ce_noalloc_ptr[dev] == nullptr) {
     void* p = nullptr;
-    if (cudaGetSymbolAddress(&p, g_ce_noalloc_rows) != cudaSuccess || p == nullptr) return HB_NOALLOC_ERR_CUDA;
+    if (cudaGetSymbolAddress((void**)&p, g_ce_noalloc_rows) != cudaSuccess || p == nullptr) return HB_NOALLOC_ERR_CUDA;
     g_ce_noalloc_ptr[dev] = static_cast<float*>(p);
   }
   *out = g_ce_noalloc_ptr[dev];
