@@ -250,25 +250,42 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn, b
 // ---------------------------------------------------------------------------
 // Small numeric helpers
 // ---------------------------------------------------------------------------
-// tanh-approximation GELU, written from its definition
-//   gelu(x) = 0.5 x (1 + tanh(sqrt(2/pi) (x + 0.044715 x^3)))
-// using the CUDA tanhf function.
+// GELU, tanh approximation (the GELU(approximate="tanh") of the model):
+//   gelu(x) = 0.5 x (1 + tanh(u)),  u = sqrt(2/pi) (x + 0.044715 x^3).
+// Evaluated through the identity 1 + tanh(u) = 2 sigmoid(2u), so
+//   gelu(x) = x * s,  s = 1 / (1 + 2^(-2u log2 e)).
+// The exponential is one ex2.approx; the reciprocal stays off the
+// transcendental unit (which the epilogue's bf16 conversions also use):
+// an integer-subtraction initial estimate (exponent negation, the classic
+// fast-reciprocal bit trick with constant 0x7EF311C7: |rel err| < 5.1% for
+// d in [1, 2^64]) refined by two Newton steps r <- r (2 - d r), giving
+// |rel err| < 7e-6 -- far below bf16 resolution. The exponent is clamped at
+// 64 so d stays finite; gelu -> x * 2^-64 ~ 0 there.
+__device__ __forceinline__ float sigmoid_2u(float u) {
+  float e;
+  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fminf(-2.8853900817779268f * u, 64.f)));  // -2 log2(e) u
+  const float d = 1.f + e;
+  float r = __int_as_float(0x7EF311C7 - __float_as_int(d));
+  r = r * fmaf(-d, r, 2.f);
+  r = r * fmaf(-d, r, 2.f);
+  return r;
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
-  float u = k0 * (x + k1 * x * x * x);
-  return 0.5f * x * (1.f + tanhf(u));
+  return x * sigmoid_2u(k0 * fmaf(k1 * x, x * x, x));
 }
 
-// d/dx of gelu_tanh (product rule on the definition above).
+// d/dx gelu(x) = s + 2 x s (1 - s) du/dx,  du/dx = sqrt(2/pi) (1 + 3 * 0.044715 x^2)
+// (product rule on x * sigmoid(2u); equals 0.5(1+t) + 0.5 x (1-t^2) du/dx with t = tanh u).
 __device__ __forceinline__ float gelu_tanh_grad(float x) {
   const float k0 = 0.7978845608028654f;
   const float k1 = 0.044715f;
-  float x2 = x * x;
-  float u = k0 * (x + k1 * x2 * x);
-  float t = tanhf(u);
-  float du = k0 * (1.f + 3.f * k1 * x2);
-  return 0.5f * (1.f + t) + 0.5f * x * (1.f - t * t) * du;
+  const float x2 = x * x;
+  const float s = sigmoid_2u(k0 * fmaf(k1 * x, x2, x));
+  const float du = k0 * fmaf(3.f * k1, x2, 1.f);
+  return fmaf(2.f * x * s * (1.f - s), du, s);
 }
 
 __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {

@@ -97,9 +97,14 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
     p.grp_b_off = static_cast<int>(grp_b_off);
     p.grp_c_off = static_cast<int>(grp_c_off);
   }
-  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8 && ag_src.empty() && rs_dst.empty() && grp_mode == 0) {
-    const int sms = num_sms(a.get_device());
-    const long tiles = (long)((M + 127) / 128) * ((N + BN - 1) / BN);
+  // Only outputs smaller than one wave are split: for larger ones the atomic
+  // traffic (splits x M x N x 4 bytes through L2) costs more than the tail wave.
+  const int sms_dev = num_sms(a.get_device());
+  const long tiles_mn = (long)((M + 127) / 128) * ((N + BN - 1) / BN);
+  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8 && tiles_mn < sms_dev && ag_src.empty() &&
+      rs_dst.empty() && grp_mode == 0) {
+    const int sms = sms_dev;
+    const long tiles = tiles_mn;
     auto eff = [&](int s) {
       const long units = tiles * s;
       const long waves = (units + sms - 1) / sms;

@@ -15,8 +15,11 @@
 //               STAGES-deep shared-memory ring (128-byte swizzle, no multicast).
 //   warp 1      allocates TMEM; one elected thread issues tcgen05.mma
 //               (128 x BN x 16) and commits each stage back to the producer.
-//   warps 2..5  epilogue: tcgen05.ld the fp32 accumulator (thread = row),
+//   warps 2..9  epilogue: tcgen05.ld the fp32 accumulator (thread = row),
 //               apply bias / GELU / dGELU / residual, store to global memory.
+//               Two warps share each TMEM lane quarter and split the tile's
+//               columns, so eight warps drain a tile while the next one
+//               accumulates.
 // The accumulator is double-buffered in TMEM (2 x BN columns) so the
 // epilogue of tile i overlaps the main loop of tile i+1.
 #include "common.cuh"
@@ -25,9 +28,9 @@
 
 namespace hb {
 
-constexpr int kStgRowF32 = 144;   // bytes per staged row, fp32 view (32 + 4 floats)
-constexpr int kStgRowBf16 = 80;   // bytes per staged row, bf16 view (32 + 8 halves)
-constexpr int kStgBytes = 32 * kStgRowF32;  // per warp
+constexpr int kEpiWarps = 8;
+constexpr int kGemmThreads = 64 + 32 * kEpiWarps;
+constexpr int kStgBytes = 32 * 128;  // per epilogue warp: 32 rows x 128 bytes, XOR-swizzled
 
 template <int BN>
 struct GemmCfg {
@@ -38,8 +41,8 @@ struct GemmCfg {
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
   static constexpr int STAGES = (BN >= 256) ? 4 : 6;
   static constexpr int TMEM_COLS = 2 * BN;
-  static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // 4 per-warp epilogue staging tiles
-  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + 4 * kStgBytes + 1024 /*align*/ + 256 /*barriers*/;
+  static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // per-warp epilogue staging tiles
+  static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiWarps * kStgBytes + 1024 /*align*/ + 256 /*barriers*/;
 };
 
 // ---------------------------------------------------------------------------
@@ -48,90 +51,127 @@ struct GemmCfg {
 // values after tcgen05.ld. Global traffic goes through a per-warp staging
 // tile in shared memory, so every global load/store is coalesced (lanes
 // cover consecutive 16-byte segments of a row) while the arithmetic stays
-// row-per-thread. Staging rows are padded (fp32: 144 B, bf16: 80 B) so both
-// access patterns are free of bank conflicts.
+// row-per-thread. The staging tile is XOR-swizzled on 16-byte segments
+// (fp32 rows of 128 B: seg ^ (row & 7); bf16 rows of 64 B: seg ^ ((row >> 1) & 3)),
+// which makes both access patterns bank-conflict free without padding.
+// Operands the epilogue reads (residual, GELU pre-activation, accumulated
+// gradient) are fetched into registers one chunk ahead -- the first chunk
+// before the accumulator is even ready -- so DRAM latency overlaps the MMAs.
 // ---------------------------------------------------------------------------
-
-// Coalesced copy global -> staging of a [32 rows][32 cols] tile (rows from m_base).
 template <bool F32>
-__device__ __forceinline__ void stg_load(uint8_t* stg, const void* src, long ld, int m_base, int n0, int M, int N,
-                                         int lane) {
+__device__ __forceinline__ int stg_off(int r, int seg) {
+  return F32 ? r * 128 + ((seg ^ (r & 7)) << 4) : r * 64 + ((seg ^ ((r >> 1) & 3)) << 4);
+}
+
+// Coalesced global loads of a [32 rows][32 cols] tile into registers (zeros outside M x N).
+template <bool F32>
+__device__ __forceinline__ void gload_tile(uint4 (&pre)[8], const void* src, long ld, int m_base, int n0, int M, int N,
+                                           int lane) {
   constexpr int SEGS = F32 ? 8 : 4;  // 16-byte segments per row
   constexpr int ESZ = F32 ? 4 : 2;
-  constexpr int ROWB = F32 ? kStgRowF32 : kStgRowBf16;
 #pragma unroll
   for (int it = 0; it < SEGS; ++it) {
     const int idx = it * 32 + lane;
     const int r = idx / SEGS, seg = idx % SEGS;
     const int gm = m_base + r, gn = n0 + seg * (16 / ESZ);
-    uint4 val = make_uint4(0, 0, 0, 0);
+    pre[it] = make_uint4(0, 0, 0, 0);
     if (gm < M && gn < N)
-      val = *reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(src) + ((long)gm * ld + gn) * ESZ);
-    *reinterpret_cast<uint4*>(stg + r * ROWB + seg * 16) = val;
+      pre[it] = __ldg(reinterpret_cast<const uint4*>(reinterpret_cast<const uint8_t*>(src) + ((long)gm * ld + gn) * ESZ));
   }
 }
 
-// Coalesced copy staging -> global.
+template <bool F32>
+__device__ __forceinline__ void stg_fill(uint8_t* stg, const uint4 (&pre)[8], int lane) {
+  constexpr int SEGS = F32 ? 8 : 4;
+#pragma unroll
+  for (int it = 0; it < SEGS; ++it) {
+    const int idx = it * 32 + lane;
+    *reinterpret_cast<uint4*>(stg + stg_off<F32>(idx / SEGS, idx % SEGS)) = pre[it];
+  }
+}
+
+// Coalesced copy staging -> global (all shared loads first, then the stores).
 template <bool F32>
 __device__ __forceinline__ void stg_store(const uint8_t* stg, void* dst, long ld, int m_base, int n0, int M, int N,
                                           int lane) {
   constexpr int SEGS = F32 ? 8 : 4;
   constexpr int ESZ = F32 ? 4 : 2;
-  constexpr int ROWB = F32 ? kStgRowF32 : kStgRowBf16;
+  uint4 val[SEGS];
+#pragma unroll
+  for (int it = 0; it < SEGS; ++it) {
+    const int idx = it * 32 + lane;
+    val[it] = *reinterpret_cast<const uint4*>(stg + stg_off<F32>(idx / SEGS, idx % SEGS));
+  }
 #pragma unroll
   for (int it = 0; it < SEGS; ++it) {
     const int idx = it * 32 + lane;
     const int r = idx / SEGS, seg = idx % SEGS;
     const int gm = m_base + r, gn = n0 + seg * (16 / ESZ);
     if (gm < M && gn < N)
-      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst) + ((long)gm * ld + gn) * ESZ) =
-          *reinterpret_cast<const uint4*>(stg + r * ROWB + seg * 16);
+      *reinterpret_cast<uint4*>(reinterpret_cast<uint8_t*>(dst) + ((long)gm * ld + gn) * ESZ) = val[it];
   }
 }
 
 // Coalesced staging -> global vector atomic add (fp32 split-K partials).
 __device__ __forceinline__ void stg_atomic_add(const uint8_t* stg, float* dst, long ld, int m_base, int n0, int M,
                                                int N, int lane) {
+  float4 val[8];
+#pragma unroll
+  for (int it = 0; it < 8; ++it) {
+    const int idx = it * 32 + lane;
+    val[it] = *reinterpret_cast<const float4*>(stg + stg_off<true>(idx / 8, idx % 8));
+  }
 #pragma unroll
   for (int it = 0; it < 8; ++it) {
     const int idx = it * 32 + lane;
     const int r = idx / 8, seg = idx % 8;
     const int gm = m_base + r, gn = n0 + seg * 4;
-    if (gm < M && gn < N)
-      atomicAdd(reinterpret_cast<float4*>(dst + (long)gm * ld + gn),
-                *reinterpret_cast<const float4*>(stg + r * kStgRowF32 + seg * 16));
+    if (gm < M && gn < N) atomicAdd(reinterpret_cast<float4*>(dst + (long)gm * ld + gn), val[it]);
   }
 }
 
 // Row-per-thread write of 32 values into this thread's staging row.
 __device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float (&v)[32]) {
-  uint8_t* row = stg + lane * kStgRowBf16;
 #pragma unroll
   for (int g = 0; g < 4; ++g)
-    *reinterpret_cast<uint4*>(row + g * 16) =
+    *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
         make_uint4(pack_bf16(v[8 * g], v[8 * g + 1]), pack_bf16(v[8 * g + 2], v[8 * g + 3]),
                    pack_bf16(v[8 * g + 4], v[8 * g + 5]), pack_bf16(v[8 * g + 6], v[8 * g + 7]));
 }
 __device__ __forceinline__ void stg_put_f32(uint8_t* stg, int lane, const float (&v)[32]) {
-  uint8_t* row = stg + lane * kStgRowF32;
 #pragma unroll
   for (int g = 0; g < 8; ++g)
-    *reinterpret_cast<float4*>(row + g * 16) = make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
+    *reinterpret_cast<float4*>(stg + stg_off<true>(lane, g)) =
+        make_float4(v[4 * g], v[4 * g + 1], v[4 * g + 2], v[4 * g + 3]);
 }
 
 template <int EPI>
-__device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int m_base, int n0, float (&v)[32],
-                                                    uint8_t* stg, int lane) {
-  // 1. operands read by the epilogue: staged, then each thread takes its row.
+constexpr bool epi_reads_operand() {
+  return EPI == kEpiF32Resid || EPI == kEpiF32Acc || EPI == kEpiBf16Dgelu;
+}
+
+// Fetch the operand tile this epilogue chunk reads (if any) into registers.
+template <int EPI>
+__device__ __forceinline__ void epi_prefetch(const GemmParams& p, const void* C, int m_base, int n0, int lane,
+                                             uint4 (&pre)[8]) {
+  if constexpr (EPI == kEpiF32Resid) {
+    gload_tile<true>(pre, p.resid, p.ldr, m_base, n0, p.M, p.N, lane);
+  } else if constexpr (EPI == kEpiF32Acc) {
+    gload_tile<true>(pre, C, p.ldc, m_base, n0, p.M, p.N, lane);
+  } else if constexpr (EPI == kEpiBf16Dgelu) {
+    gload_tile<false>(pre, p.aux, p.ldaux, m_base, n0, p.M, p.N, lane);
+  }
+}
+
+// Step 1: combine the prefetched operand with the accumulator row (frees `pre`).
+template <int EPI>
+__device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, const uint4 (&pre)[8], int lane) {
   if constexpr (EPI == kEpiF32Resid || EPI == kEpiF32Acc) {
-    const float* src = (EPI == kEpiF32Resid) ? p.resid : reinterpret_cast<const float*>(p.C);
-    const long ld = (EPI == kEpiF32Resid) ? p.ldr : p.ldc;
-    stg_load<true>(stg, src, ld, m_base, n0, p.M, p.N, lane);
+    stg_fill<true>(stg, pre, lane);
     __syncwarp();
-    const uint8_t* row = stg + lane * kStgRowF32;
 #pragma unroll
     for (int g = 0; g < 8; ++g) {
-      const float4 r = *reinterpret_cast<const float4*>(row + g * 16);
+      const float4 r = *reinterpret_cast<const float4*>(stg + stg_off<true>(lane, g));
       v[4 * g] += r.x;
       v[4 * g + 1] += r.y;
       v[4 * g + 2] += r.z;
@@ -140,24 +180,28 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int m_b
     __syncwarp();
   }
   if constexpr (EPI == kEpiBf16Dgelu) {
-    stg_load<false>(stg, p.aux, p.ldaux, m_base, n0, p.M, p.N, lane);
+    stg_fill<false>(stg, pre, lane);
     __syncwarp();
-    const uint8_t* row = stg + lane * kStgRowBf16;
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
-      const uint4 raw = *reinterpret_cast<const uint4*>(row + g * 16);
+      const uint4 raw = *reinterpret_cast<const uint4*>(stg + stg_off<false>(lane, g));
       const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&raw);
 #pragma unroll
       for (int q = 0; q < 8; ++q) v[8 * g + q] *= gelu_tanh_grad(__bfloat162float(pb[q]));
     }
     __syncwarp();
   }
-  // 2. bias
+}
+
+// Step 2: bias, activation and the stores of one 32x32 chunk into C.
+template <int EPI>
+__device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_base, int n0, float (&v)[32],
+                                           uint8_t* stg, int lane) {
   if (p.bias != nullptr && (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       if (n0 + j < p.N) {
-        const float4 b = *reinterpret_cast<const float4*>(p.bias + n0 + j);
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
         v[j] += b.x;
         v[j + 1] += b.y;
         v[j + 2] += b.z;
@@ -165,31 +209,37 @@ __device__ __forceinline__ void gemm_epilogue_chunk(const GemmParams& p, int m_b
       }
     }
   }
-  // 3. outputs
   if constexpr (EPI == kEpiBf16Gelu) {
     // Pre-activation (rounded to bf16) goes to AUX; GELU of that rounded value
     // goes to C, so backward differentiates exactly what forward applied.
+    uint32_t pk[16];
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = __bfloat162float(__float2bfloat16_rn(v[j]));
-    stg_put_bf16(stg, lane, v);
+    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
+          make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
     __syncwarp();
     stg_store<false>(stg, p.aux, p.ldaux, m_base, n0, p.M, p.N, lane);
     __syncwarp();
 #pragma unroll
-    for (int j = 0; j < 32; ++j) v[j] = gelu_tanh(v[j]);
+    for (int j = 0; j < 16; ++j) {  // unpack the rounded values (bit moves, no conversion)
+      v[2 * j] = gelu_tanh(__uint_as_float(pk[j] << 16));
+      v[2 * j + 1] = gelu_tanh(__uint_as_float(pk[j] & 0xffff0000u));
+    }
   }
   if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiBf16Dgelu) {
     stg_put_bf16(stg, lane, v);
     __syncwarp();
-    stg_store<false>(stg, p.C, p.ldc, m_base, n0, p.M, p.N, lane);
+    stg_store<false>(stg, C, p.ldc, m_base, n0, p.M, p.N, lane);
   } else if constexpr (EPI == kEpiF32Atomic) {
     stg_put_f32(stg, lane, v);
     __syncwarp();
-    stg_atomic_add(stg, reinterpret_cast<float*>(p.C), p.ldc, m_base, n0, p.M, p.N, lane);
+    stg_atomic_add(stg, reinterpret_cast<float*>(C), p.ldc, m_base, n0, p.M, p.N, lane);
   } else {
     stg_put_f32(stg, lane, v);
     __syncwarp();
-    stg_store<true>(stg, p.C, p.ldc, m_base, n0, p.M, p.N, lane);
+    stg_store<true>(stg, C, p.ldc, m_base, n0, p.M, p.N, lane);
   }
   __syncwarp();
 }
@@ -257,7 +307,7 @@ __device__ __forceinline__ bool ag_wait_rows(const GemmParams& p, int mb) {
 }
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
-__global__ void __launch_bounds__(192, 1)
+__global__ void __launch_bounds__(kGemmThreads, 1)
     gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
@@ -266,7 +316,7 @@ __global__ void __launch_bounds__(192, 1)
 
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
-  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STG_OFFSET + 4 * kStgBytes);
+  uint64_t* full = reinterpret_cast<uint64_t*>(smem + Cfg::STG_OFFSET + kEpiWarps * kStgBytes);
   uint64_t* empty = full + STAGES;
   uint64_t* tfull = empty + STAGES;
   uint64_t* tempty = tfull + 2;
@@ -313,7 +363,7 @@ __global__ void __launch_bounds__(192, 1)
     }
     for (int a = 0; a < 2; ++a) {
       mbar_init(&tfull[a], 1);
-      mbar_init(&tempty[a], 4);
+      mbar_init(&tempty[a], kEpiWarps);
     }
     mbar_init(mma_done, 1);
     fence_barrier_init();
@@ -422,44 +472,46 @@ __global__ void __launch_bounds__(192, 1)
       mbar_wait(mma_done, 0, p.status, 5);
     }
   } else {
-    const int sub = warp & 3;
-    uint8_t* stg = smem + Cfg::STG_OFFSET + sub * kStgBytes;
-    if (p.ag_world > 1) ag_copy_units(p, blockIdx.x * 4 + (warp - 2), gridDim.x * 4, lane);
+    const int eid = warp - 2;       // 0 .. kEpiWarps-1
+    const int quarter = warp & 3;   // TMEM lanes this warp may access: 32 * (warp % 4) ..
+    constexpr int CH = BN / 64;     // 32-column chunks per warp (the two warps of a quarter split the tile)
+    const int c0 = (eid >> 2) * CH;
+    uint8_t* stg = smem + Cfg::STG_OFFSET + eid * kStgBytes;
+    if (p.ag_world > 1) ag_copy_units(p, blockIdx.x * kEpiWarps + eid, gridDim.x * kEpiWarps, lane);
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
       const uint32_t acc_phase = (local >> 1) & 1;
-      if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
-      tc_fence_after();
       int mb, nb, kb0_, nkb_, grp;
       decode(t, mb, nb, kb0_, nkb_, grp);
-      const int m_base = mb * BM + sub * 32;
-      if (nkb_ <= 0) {  // empty expert segment: nothing was accumulated, nothing to store
-        tc_fence_before();
-        __syncwarp();
-        if (lane == 0) mbar_arrive(&tempty[acc]);
-        continue;
+      const int m_base = mb * BM + quarter * 32;
+      void* C = p.C;
+      if (p.grp_mode == 2) {
+        // this expert's block of the stacked weight gradient
+        C = static_cast<uint8_t*>(p.C) + (long)grp * p.grp_c_off * p.ldc * 4;
+      } else if (p.rs_world > 1) {
+        // partial tile -> slot rs_rank of the owning rank's receive buffer (over NVLink)
+        const int owner = m_base / p.rs_rows;
+        const int esz = (EPI == kEpiBf16) ? 2 : 4;
+        C = static_cast<uint8_t*>(p.rs_dst[owner]) +
+            ((long)p.rs_rank * p.rs_rows - (long)owner * p.rs_rows) * p.ldc * esz;
       }
+      uint4 pre[8];
+      const int n_first = nb * BN + c0 * 32;
+      if (epi_reads_operand<EPI>() && nkb_ > 0 && n_first < p.N) epi_prefetch<EPI>(p, C, m_base, n_first, lane, pre);
+      if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
+      tc_fence_after();
+      if (nkb_ > 0) {  // an empty expert segment accumulated nothing and stores nothing
 #pragma unroll 1
-      for (int c = 0; c < BN / 32; ++c) {
-        const int n0 = nb * BN + c * 32;
-        if (n0 >= p.N) break;
-        float v[32];
-        tmem_ld32(tmem_base + (static_cast<uint32_t>(sub * 32) << 16) + acc * BN + c * 32, v);
-        if (p.grp_mode == 2) {
-          GemmParams q = p;  // this expert's block of the stacked weight gradient
-          q.C = static_cast<uint8_t*>(p.C) + (long)grp * p.grp_c_off * p.ldc * 4;
-          gemm_epilogue_chunk<EPI>(q, m_base, n0, v, stg, lane);
-        } else if (p.rs_world > 1) {
-          // Partial tile -> slot rs_rank of the owning rank's receive buffer (over NVLink).
-          GemmParams q = p;
-          const int owner = m_base / p.rs_rows;
-          const int esz = (EPI == kEpiBf16) ? 2 : 4;
-          q.C = static_cast<uint8_t*>(p.rs_dst[owner]) +
-                ((long)p.rs_rank * p.rs_rows - (long)owner * p.rs_rows) * p.ldc * esz;
-          gemm_epilogue_chunk<EPI>(q, m_base, n0, v, stg, lane);
-        } else {
-          gemm_epilogue_chunk<EPI>(p, m_base, n0, v, stg, lane);
+        for (int c = 0; c < CH; ++c) {
+          const int n0 = n_first + c * 32;
+          if (n0 >= p.N) break;
+          float v[32];
+          tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + (c0 + c) * 32, v);
+          epi_apply_operand<EPI>(v, stg, pre, lane);
+          if (epi_reads_operand<EPI>() && c + 1 < CH && n0 + 32 < p.N)
+            epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
+          epi_finish<EPI>(p, C, m_base, n0, v, stg, lane);
         }
       }
       tc_fence_before();
@@ -489,7 +541,7 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams&
   const int num_tiles =
       ((p.M + 127) / 128) * ((p.N + BN - 1) / BN) * p.splits * (p.grp_mode == 2 ? p.grp_n : 1);
   const int grid = num_tiles < num_sms(dev) ? num_tiles : num_sms(dev);
-  kern<<<grid, 192, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -49,6 +49,12 @@ GEMM_SHAPES = [
     ("lmhead_dgrad", 8192, 768, 50304, "dgrad"),
     ("lmhead_wgrad", 8192, 50304, 768, "wgrad"),
     ("square_8192", 8192, 8192, 8192, "fwd"),
+    # fused epilogues as the model uses them (reference time: the plain cuBLAS GEMM)
+    ("attnproj_resid", 8192, 768, 768, "resid"),     # x_new = x + y W^T + b   (fp32 out)
+    ("mlpproj_resid", 8192, 768, 3072, "resid"),
+    ("fc_gelu", 8192, 3072, 768, "gelu"),            # h = GELU(x W^T + b), pre-activation kept
+    ("fc_dgrad_dgelu", 8192, 3072, 768, "dgelu"),    # dpre = (dy W) * GELU'(pre)
+    ("qkv_dgrad_f32", 8192, 768, 2304, "dgrad32"),   # dx (fp32) = dqkv W
 ]
 
 
@@ -74,12 +80,38 @@ def bench_gemm(flush):
             ours = lambda: g.gemm(dy, w, out, N, g.EPI_BF16, False, True)
             ref = lambda: torch.matmul(dy, w)
             flops = 2.0 * M * N * K
-        else:
+        elif kind == "wgrad":
             dy = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
             x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
             out = torch.zeros(N, K, device="cuda", dtype=torch.float32)
             ours = lambda: g.gemm(dy, x, out, K, g.EPI_F32_ACC, True, True)
             ref = lambda: torch.matmul(dy.t(), x)
+            flops = 2.0 * M * N * K
+        elif kind in ("resid", "gelu"):
+            x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            w = torch.randn(N, K, device="cuda", dtype=torch.bfloat16)
+            bias = torch.randn(N, device="cuda")
+            if kind == "resid":
+                res = torch.randn(M, N, device="cuda")
+                out = torch.empty(M, N, device="cuda")
+                ours = lambda: g.gemm(x, w, out, N, g.EPI_F32_RESID, False, False, bias=bias, resid=res)
+            else:
+                out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+                pre = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+                ours = lambda: g.gemm(x, w, out, N, g.EPI_BF16_GELU, False, False, bias=bias, aux=pre)
+            ref = lambda: torch.matmul(x, w.t())
+            flops = 2.0 * M * N * K
+        else:  # dgelu / dgrad32: output [M, N] from dy [M, K] and W stored [K, N]
+            dy = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
+            w = torch.randn(K, N, device="cuda", dtype=torch.bfloat16)
+            if kind == "dgelu":
+                pre = torch.randn(M, N, device="cuda", dtype=torch.bfloat16)
+                out = torch.empty(M, N, device="cuda", dtype=torch.bfloat16)
+                ours = lambda: g.gemm(dy, w, out, N, g.EPI_BF16_DGELU, False, True, aux=pre)
+            else:
+                out = torch.empty(M, N, device="cuda")
+                ours = lambda: g.gemm(dy, w, out, N, g.EPI_F32, False, True)
+            ref = lambda: torch.matmul(dy, w)
             flops = 2.0 * M * N * K
         t_ours = time_fn(ours, flush=flush)
         check_status()
