@@ -107,6 +107,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--out_dir", type=str, default=".")
     p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
     p.add_argument("--log_interval", type=int, default=None)
+    p.add_argument("--watchdog_s", type=float, default=300.0,
+                   help="multi-process runs: abort when a peer announces a failure or makes no progress "
+                        "for this many seconds (0 = off)")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
     return p
@@ -492,11 +495,43 @@ def main(argv=None) -> None:
 
     module.train()
     t0 = time.time()
+    wd = None
+    if distributed and args.watchdog_s > 0:
+        from .utils.fault import StepWatchdog, default_store
+        wd = StepWatchdog(default_store(), dist.get_rank(), dist.get_world_size(), timeout_s=args.watchdog_s)
+    try:
+        _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0)
+    except BaseException as e:
+        if wd is not None:
+            wd.mark_failed(f"{type(e).__name__}: {e}")
+            wd.stop()
+        try:
+            engine.close()
+        except Exception:
+            pass
+        raise
+    if wd is not None:
+        wd.finish()
+    if is_main and run:
+        run.finish()
+    if is_main:
+        print("training finished.")
+    engine.close()
+    if distributed and dist.is_initialized():
+        cleanup()
+
+
+def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0) -> None:
+    is_main = topo.is_main
     tokens_per_step = args.batch_size * args.block_size * args.grad_accum_steps
     last = time.time()
     log_every = args.log_interval or max(1, args.eval_interval // 10)
     for step in range(1, args.max_iters + 1):
+        if wd is not None:
+            wd.check()  # a failed peer is noticed here, before this step launches anything
         loss_scalar, aux = engine.train_step(train_loader)
+        if wd is not None:
+            wd.beat(step)
         now = time.time()
         dt = now - last
         last = now
@@ -523,13 +558,6 @@ def main(argv=None) -> None:
         if args.save_interval and step % args.save_interval == 0:
             save_checkpoint(module, cfg, step, topo, args.out_dir,
                             optimizer_state=engine.optimizer.state_dict() if engine.fused else None)
-    if is_main and run:
-        run.finish()
-    if is_main:
-        print("training finished.")
-    engine.close()
-    if distributed and dist.is_initialized():
-        cleanup()
 
 
 def expert_load_metrics(module) -> dict:
