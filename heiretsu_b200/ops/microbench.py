@@ -1,7 +1,7 @@
 """Kernel micro-benchmarks: the model's hot ops against their PyTorch/cuBLAS
 counterparts on the GPT-2 shapes (M = 8 x 1024 tokens).
 
-    python -m heiretsu_b200.ops.microbench [--only gemm] [--json out.json]
+    python -m heiretsu_b200.ops.microbench [--only gemm] [--shape fc_gelu] [--reps 20 --warmup 5] [--json out.json]
 
 Timing: CUDA events on the launching stream, warm-up first, L2 flushed by
 writing a 256 MB buffer before every timed launch, median of the repeats.
@@ -19,7 +19,13 @@ def _flush_buf():
     return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
 
 
-def time_fn(fn, reps=20, warmup=5, flush=None):
+REPS, WARMUP = 20, 5
+SHAPE = None
+
+
+def time_fn(fn, reps=None, warmup=None, flush=None):
+    reps = REPS if reps is None else reps
+    warmup = WARMUP if warmup is None else warmup
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
@@ -64,6 +70,8 @@ def bench_gemm(flush):
 
     rows = []
     for name, M, N, K, kind in GEMM_SHAPES:
+        if SHAPE is not None and name != SHAPE:
+            continue
         torch.manual_seed(0)
         if kind == "fwd":
             x = torch.randn(M, K, device="cuda", dtype=torch.bfloat16)
@@ -184,7 +192,12 @@ def main(argv=None):
     ap = argparse.ArgumentParser()
     ap.add_argument("--only", default=None)
     ap.add_argument("--json", default=None)
+    ap.add_argument("--shape", default=None, help="run only this GEMM shape (by name)")
+    ap.add_argument("--reps", type=int, default=20)
+    ap.add_argument("--warmup", type=int, default=5)
     args = ap.parse_args(argv)
+    global REPS, WARMUP, SHAPE
+    REPS, WARMUP, SHAPE = args.reps, args.warmup, args.shape
     flush = _flush_buf()
     rows = []
     if args.only in (None, "gemm"):
