@@ -40,10 +40,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_close", &hb::ipc_close);
   m.def("dp_allreduce", &hb::dp_allreduce);
   m.def("group_barrier", &hb::group_barrier);
+  m.def("peer_sum", &hb::peer_sum);
   m.def("moe_route", &hb::moe_route);
   m.def("moe_gather", &hb::moe_gather);
   m.def("moe_combine", &hb::moe_combine);
   m.def("moe_combine_bwd", &hb::moe_combine_bwd);
   m.def("moe_unpermute", &hb::moe_unpermute);
+  m.def("moe_local_offsets", &hb::moe_local_offsets);
   m.def("moe_router_bwd", &hb::moe_router_bwd);
 }

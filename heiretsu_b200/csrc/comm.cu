@@ -31,62 +31,11 @@
 #include <string>
 #include <vector>
 
+#include "comm.cuh"
 #include "common.cuh"
 #include "host_utils.h"
 
 namespace hb {
-
-constexpr int kMaxRanks = 8;
-constexpr int kMaxSignalBlocks = 1024;
-
-__device__ __forceinline__ void st_release_sys(uint32_t* p, uint32_t v) {
-  asm volatile("st.release.sys.global.u32 [%0], %1;" ::"l"(p), "r"(v) : "memory");
-}
-__device__ __forceinline__ uint32_t ld_acquire_sys(const uint32_t* p) {
-  uint32_t v;
-  asm volatile("ld.acquire.sys.global.u32 %0, [%1];" : "=r"(v) : "l"(p) : "memory");
-  return v;
-}
-
-struct PeerTable {
-  uint64_t data[kMaxRanks];    // peer data buffers (index = group rank)
-  uint64_t signal[kMaxRanks];  // peer signal pads, uint32 [kMaxRanks][kMaxSignalBlocks]
-};
-
-// Per-block barrier across the group. Called by all threads of the block.
-// `counter` is this rank's per-block epoch array (device memory, local).
-// Returns false (after recording an error) if a peer did not arrive in time.
-__device__ __forceinline__ bool group_barrier(const PeerTable& pt, int rank, int world, uint32_t* counter,
-                                              uint32_t phase_tag, int* status) {
-  __shared__ int ok_sh;
-  if (threadIdx.x == 0) {
-    ok_sh = 1;
-    const uint32_t epoch = counter[blockIdx.x] + 1;  // advanced once per call, after both barriers
-    const uint32_t val = epoch * 4u + phase_tag;
-    __threadfence_system();
-    for (int p = 0; p < world; ++p) {
-      if (p == rank) continue;
-      uint32_t* slot = reinterpret_cast<uint32_t*>(pt.signal[p]) + rank * kMaxSignalBlocks + blockIdx.x;
-      st_release_sys(slot, val);
-    }
-    const uint32_t* mine = reinterpret_cast<const uint32_t*>(pt.signal[rank]);
-    const uint64_t t0 = globaltimer_ns();
-    for (int p = 0; p < world && ok_sh; ++p) {
-      if (p == rank) continue;
-      const uint32_t* slot = mine + p * kMaxSignalBlocks + blockIdx.x;
-      int spins = 0;
-      while (static_cast<int32_t>(ld_acquire_sys(slot) - val) < 0) {
-        if (((++spins) & 255) == 0 && globaltimer_ns() - t0 > HB_WAIT_TIMEOUT_NS) {
-          record_error(status, kPeerTimeout, 100 + p);
-          ok_sh = 0;
-          break;
-        }
-      }
-    }
-  }
-  __syncthreads();
-  return ok_sh != 0;
-}
 
 __global__ void __launch_bounds__(512) dp_allreduce_kernel(PeerTable pt, int rank, int world, long n4, long chunk4,
                                                            float scale, uint32_t* counter, int* status) {
@@ -117,6 +66,38 @@ __global__ void __launch_bounds__(512) dp_allreduce_kernel(PeerTable pt, int ran
       if (p < world) reinterpret_cast<float4*>(pt.data[p])[i] = s;
   }
   if (!group_barrier(pt, rank, world, counter, 2, status)) return;
+  if (threadIdx.x == 0) counter[blockIdx.x] += 1;
+}
+
+// Sum of peer partials (expert-parallel combine and its backward):
+//   dst[i] = addend[i] (or 0) + sum_{r = 0 .. world-1} data_r[i]
+// after one bounded barrier ("every rank's partial is written"). Every rank
+// computes the whole sum in the same rank order, so all replicas hold
+// bitwise-identical results. One barrier per call is enough when each call
+// site owns its buffer: a rank writes that buffer again only after a later
+// barrier, which its peers reach only after finishing this read.
+__global__ void __launch_bounds__(512) peer_sum_kernel(PeerTable pt, int rank, int world, const float* addend,
+                                                        float* dst, long n4, uint32_t* counter, int* status) {
+  if (!group_barrier(pt, rank, world, counter, 1, status)) return;
+  const float4* add4 = reinterpret_cast<const float4*>(addend);
+  float4* dst4 = reinterpret_cast<float4*>(dst);
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    float4 v[kMaxRanks];
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p)
+      if (p < world) v[p] = reinterpret_cast<const float4*>(pt.data[p])[i];
+    float4 s = add4 ? add4[i] : make_float4(0.f, 0.f, 0.f, 0.f);
+#pragma unroll
+    for (int p = 0; p < kMaxRanks; ++p) {
+      if (p < world) {
+        s.x += v[p].x;
+        s.y += v[p].y;
+        s.z += v[p].z;
+        s.w += v[p].w;
+      }
+    }
+    dst4[i] = s;
+  }
   if (threadIdx.x == 0) counter[blockIdx.x] += 1;
 }
 
@@ -173,6 +154,20 @@ void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<ui
   const long chunk4 = (n4 + world - 1) / world;
   const int blocks = std::min(dp_allreduce_blocks(current_device()), kMaxSignalBlocks);
   dp_allreduce_kernel<<<blocks, 512, 0, s>>>(t, rank, world, n4, chunk4, scale, counter, status);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void peer_sum_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
+                     const float* addend, float* dst, long n, uint32_t* counter, int* status, cudaStream_t s) {
+  const int world = static_cast<int>(data.size());
+  if (n % 4 != 0) throw std::runtime_error("peer_sum: element count must be a multiple of 4");
+  for (uint64_t ptr : data)
+    if (ptr % 16) throw std::runtime_error("peer_sum: peer buffers must be 16-byte aligned");
+  if ((reinterpret_cast<uintptr_t>(dst) | reinterpret_cast<uintptr_t>(addend)) % 16)
+    throw std::runtime_error("peer_sum: dst / addend must be 16-byte aligned");
+  const PeerTable t = make_table(data, signal);
+  const int blocks = std::min(num_sms(current_device()), kMaxSignalBlocks);
+  peer_sum_kernel<<<blocks, 512, 0, s>>>(t, rank, world, addend, dst, n / 4, counter, status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

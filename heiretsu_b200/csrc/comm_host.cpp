@@ -17,6 +17,8 @@ void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<ui
                          float scale, uint32_t* counter, int* status, cudaStream_t s);
 void group_barrier_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
                           uint32_t* counter, int* status, cudaStream_t s);
+void peer_sum_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
+                     const float* addend, float* dst, long n, uint32_t* counter, int* status, cudaStream_t s);
 
 uint64_t raw_malloc(int64_t bytes) {
   void* p = nullptr;
@@ -59,6 +61,24 @@ void group_barrier(const std::vector<uint64_t>& data, const std::vector<uint64_t
   c10::cuda::CUDAGuard g(counter.device());
   group_barrier_launch(data, signal, static_cast<int>(rank), reinterpret_cast<uint32_t*>(counter.data_ptr()),
                        device_status_ptr(counter.get_device()), at::cuda::getCurrentCUDAStream());
+}
+
+void peer_sum(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,
+              const c10::optional<at::Tensor>& addend, const at::Tensor& dst, int64_t n, const at::Tensor& counter) {
+  TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt && counter.numel() >= 1024,
+              "peer_sum: counter must be int32 [>=1024] on the device");
+  TORCH_CHECK(dst.is_cuda() && dst.scalar_type() == at::kFloat && dst.is_contiguous() && dst.numel() >= n,
+              "peer_sum: dst must be contiguous fp32 with >= n elements");
+  const float* add = nullptr;
+  if (addend && addend->defined()) {
+    TORCH_CHECK(addend->scalar_type() == at::kFloat && addend->is_contiguous() && addend->numel() >= n,
+                "peer_sum: addend must be contiguous fp32 with >= n elements");
+    add = addend->data_ptr<float>();
+  }
+  c10::cuda::CUDAGuard g(counter.device());
+  peer_sum_launch(data, signal, static_cast<int>(rank), add, dst.data_ptr<float>(), n,
+                  reinterpret_cast<uint32_t*>(counter.data_ptr()), device_status_ptr(counter.get_device()),
+                  at::cuda::getCurrentCUDAStream());
 }
 
 }  // namespace hb

@@ -129,57 +129,64 @@ __global__ void __launch_bounds__(1024) moe_positions_kernel(const int* __restri
 
 // Gather rows into the permuted matrix: one warp per slot.
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ pos, int NK, int K,
-                                  int H, __nv_bfloat16* __restrict__ xp) {
+                                  int H, __nv_bfloat16* __restrict__ xp, const int* __restrict__ off, int e0, int e1) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= NK) return;
+  const int lo = off[e0], r = pos[i];
+  if (r < lo || r >= off[e1]) return;  // routed to an expert outside this rank's window
   const uint4* src = reinterpret_cast<const uint4*>(x + (long)(i / K) * H);
-  uint4* dst = reinterpret_cast<uint4*>(xp + (long)pos[i] * H);
+  uint4* dst = reinterpret_cast<uint4*>(xp + (long)(r - lo) * H);
   for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
 }
-
-// x_new[t] = resid[t] + sum_k w[t,k] * yp[pos[t,k]]   (fp32 out, bf16 expert outputs)
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const int* __restrict__ pos,
                                    const float* __restrict__ topw, const float* __restrict__ resid, int N, int K,
-                                   int H, float* __restrict__ out) {
+                                   int H, float* __restrict__ out, const int* __restrict__ off, int e0, int e1) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= N) return;
+  const int lo = off[e0], hi = off[e1];
   for (int j = lane * 4; j < H; j += 128) {
-    float4 acc = *reinterpret_cast<const float4*>(resid + (long)t * H + j);
+    float4 acc = resid ? *reinterpret_cast<const float4*>(resid + (long)t * H + j) : make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
+      const int r = pos[t * K + k];
+      if (r < lo || r >= hi) continue;
       const float wk = topw[(long)t * K + k];
-      const uint2 raw = *reinterpret_cast<const uint2*>(yp + (long)pos[t * K + k] * H + j);
-      const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-      const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-      acc.x += wk * __bfloat162float(lo.x);
-      acc.y += wk * __bfloat162float(lo.y);
-      acc.z += wk * __bfloat162float(hi.x);
-      acc.w += wk * __bfloat162float(hi.y);
+      const uint2 raw = *reinterpret_cast<const uint2*>(yp + (long)(r - lo) * H + j);
+      const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+      acc.x += wk * __bfloat162float(a.x);
+      acc.y += wk * __bfloat162float(a.y);
+      acc.z += wk * __bfloat162float(b.x);
+      acc.w += wk * __bfloat162float(b.y);
     }
     *reinterpret_cast<float4*>(out + (long)t * H + j) = acc;
   }
 }
-
-// Backward of the combine: dyp[pos[t,k]] = w[t,k] * dy[t] (bf16);
-// dw[t,k] = <dy[t], yp[pos[t,k]]>.
 __global__ void moe_combine_bwd_kernel(const float* __restrict__ dy, const __nv_bfloat16* __restrict__ yp,
                                        const int* __restrict__ pos, const float* __restrict__ topw, int N, int K,
-                                       int H, __nv_bfloat16* __restrict__ dyp, float* __restrict__ dw) {
+                                       int H, __nv_bfloat16* __restrict__ dyp, float* __restrict__ dw,
+                                       const int* __restrict__ off, int e0, int e1) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= N) return;
+  const int lo = off[e0], hi = off[e1];
   for (int k = 0; k < K; ++k) {
+    const int r = pos[t * K + k];
+    if (r < lo || r >= hi) {  // another rank's expert: its weight gradient comes from that rank
+      if (lane == 0) dw[(long)t * K + k] = 0.f;
+      continue;
+    }
     const float wk = topw[(long)t * K + k];
-    const long row = pos[t * K + k];
+    const long row = r - lo;
     float dot = 0.f;
     for (int j = lane * 4; j < H; j += 128) {
       const float4 g = *reinterpret_cast<const float4*>(dy + (long)t * H + j);
       const uint2 raw = *reinterpret_cast<const uint2*>(yp + row * H + j);
-      const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-      const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-      dot += g.x * __bfloat162float(lo.x) + g.y * __bfloat162float(lo.y) + g.z * __bfloat162float(hi.x) +
-             g.w * __bfloat162float(hi.y);
+      const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
+      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
+      dot += g.x * __bfloat162float(a.x) + g.y * __bfloat162float(a.y) + g.z * __bfloat162float(b.x) +
+             g.w * __bfloat162float(b.y);
       *reinterpret_cast<uint2*>(dyp + row * H + j) =
           make_uint2(pack_bf16(wk * g.x, wk * g.y), pack_bf16(wk * g.z, wk * g.w));
     }
@@ -187,17 +194,18 @@ __global__ void moe_combine_bwd_kernel(const float* __restrict__ dy, const __nv_
     if (lane == 0) dw[(long)t * K + k] = dot;
   }
 }
-
-// dx[t] = sum_k dxp[pos[t,k]]   (fp32 out)
 __global__ void moe_unpermute_kernel(const float* __restrict__ dxp, const int* __restrict__ pos, int N, int K, int H,
-                                     float* __restrict__ dx) {
+                                     float* __restrict__ dx, const int* __restrict__ off, int e0, int e1) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= N) return;
+  const int lo = off[e0], hi = off[e1];
   for (int j = lane * 4; j < H; j += 128) {
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
-      const float4 v = *reinterpret_cast<const float4*>(dxp + (long)pos[t * K + k] * H + j);
+      const int r = pos[t * K + k];
+      if (r < lo || r >= hi) continue;
+      const float4 v = *reinterpret_cast<const float4*>(dxp + (long)(r - lo) * H + j);
       acc.x += v.x;
       acc.y += v.y;
       acc.z += v.z;
@@ -205,6 +213,12 @@ __global__ void moe_unpermute_kernel(const float* __restrict__ dxp, const int* _
     }
     *reinterpret_cast<float4*>(dx + (long)t * H + j) = acc;
   }
+}
+
+// Offsets of the window's experts relative to its first row: out[i] = off[e0 + i] - off[e0], i = 0 .. n.
+__global__ void moe_local_offsets_kernel(const int* __restrict__ off, int e0, int n, int* __restrict__ out) {
+  const int i = threadIdx.x;
+  if (i <= n) out[i] = off[e0 + i] - off[e0];
 }
 
 // Router backward, one warp per token. Upstream: dw (gradient of the
@@ -261,25 +275,33 @@ void moe_route_launch(const __nv_bfloat16* x, const float* wg, int N, int H, int
 }
 
 void moe_gather_launch(const __nv_bfloat16* x, const int* pos, int N, int K, int H, __nv_bfloat16* xp,
-                       cudaStream_t s) {
-  moe_gather_kernel<<<(N * K * 32 + 255) / 256, 256, 0, s>>>(x, pos, N * K, K, H, xp);
+                       const int* off, int e0, int e1, cudaStream_t s) {
+  moe_gather_kernel<<<(N * K * 32 + 255) / 256, 256, 0, s>>>(x, pos, N * K, K, H, xp, off, e0, e1);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void moe_combine_launch(const __nv_bfloat16* yp, const int* pos, const float* topw, const float* resid, int N, int K,
-                        int H, float* out, cudaStream_t s) {
-  moe_combine_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(yp, pos, topw, resid, N, K, H, out);
+                        int H, float* out, const int* off, int e0, int e1, cudaStream_t s) {
+  moe_combine_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(yp, pos, topw, resid, N, K, H, out, off, e0, e1);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void moe_combine_bwd_launch(const float* dy, const __nv_bfloat16* yp, const int* pos, const float* topw, int N,
-                            int K, int H, __nv_bfloat16* dyp, float* dw, cudaStream_t s) {
-  moe_combine_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dy, yp, pos, topw, N, K, H, dyp, dw);
+                            int K, int H, __nv_bfloat16* dyp, float* dw, const int* off, int e0, int e1,
+                            cudaStream_t s) {
+  moe_combine_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dy, yp, pos, topw, N, K, H, dyp, dw, off, e0, e1);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-void moe_unpermute_launch(const float* dxp, const int* pos, int N, int K, int H, float* dx, cudaStream_t s) {
-  moe_unpermute_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dxp, pos, N, K, H, dx);
+void moe_unpermute_launch(const float* dxp, const int* pos, int N, int K, int H, float* dx, const int* off, int e0,
+                          int e1, cudaStream_t s) {
+  moe_unpermute_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dxp, pos, N, K, H, dx, off, e0, e1);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_local_offsets_launch(const int* off, int e0, int n, int* out, cudaStream_t s) {
+  if (n + 1 > 1024) throw std::runtime_error("moe_local_offsets: too many experts");
+  moe_local_offsets_kernel<<<1, 1024, 0, s>>>(off, e0, n, out);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

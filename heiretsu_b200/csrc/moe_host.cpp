@@ -11,12 +11,14 @@ namespace hb {
 
 void moe_route_launch(const __nv_bfloat16*, const float*, int, int, int, int, float, float*, int*, float*, int*, float*,
                       int*, float*, int*, cudaStream_t);
-void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, cudaStream_t);
+void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, const int*, int, int,
+                       cudaStream_t);
 void moe_combine_launch(const __nv_bfloat16*, const int*, const float*, const float*, int, int, int, float*,
-                        cudaStream_t);
+                        const int*, int, int, cudaStream_t);
 void moe_combine_bwd_launch(const float*, const __nv_bfloat16*, const int*, const float*, int, int, int,
-                            __nv_bfloat16*, float*, cudaStream_t);
-void moe_unpermute_launch(const float*, const int*, int, int, int, float*, cudaStream_t);
+                            __nv_bfloat16*, float*, const int*, int, int, cudaStream_t);
+void moe_unpermute_launch(const float*, const int*, int, int, int, float*, const int*, int, int, cudaStream_t);
+void moe_local_offsets_launch(const int*, int, int, int*, cudaStream_t);
 void moe_router_bwd_launch(const float*, const int*, const float*, const float*, const float*, const int*, float, int,
                            int, int, int, const float*, __nv_bfloat16*, long, float*, cudaStream_t);
 
@@ -53,36 +55,67 @@ void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef
                    P<int>(pos), S());
 }
 
-void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp) {
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && xp.scalar_type() == at::kBFloat16 && x.size(1) == xp.size(1),
-              "moe_gather: bf16 [N, H] -> [R, H]");
-  c10::cuda::CUDAGuard g(x.device());
-  moe_gather_launch(P<__nv_bfloat16>(x), P<int>(pos), x.size(0), K, x.size(1), P<__nv_bfloat16>(xp), S());
+// Expert window [e0, e1): only rows of padded expert segments e0 .. e1-1 take
+// part (this rank's experts under expert parallelism; e0 = 0, e1 = E
+// otherwise). Rows are addressed relative to the window's first row off[e0].
+static void check_window(const at::Tensor& off, int64_t e0, int64_t e1) {
+  check_i32(off, "moe: expert offsets");
+  TORCH_CHECK(0 <= e0 && e0 < e1 && e1 < off.numel(), "moe: expert window out of range");
 }
 
-void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw, const at::Tensor& resid,
-                 at::Tensor& out) {
-  check_f32(resid, "moe_combine: resid");
+void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp, const at::Tensor& off,
+                int64_t e0, int64_t e1) {
+  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && xp.scalar_type() == at::kBFloat16 && x.size(1) == xp.size(1),
+              "moe_gather: bf16 [N, H] -> [R, H]");
+  check_window(off, e0, e1);
+  c10::cuda::CUDAGuard g(x.device());
+  moe_gather_launch(P<__nv_bfloat16>(x), P<int>(pos), x.size(0), K, x.size(1), P<__nv_bfloat16>(xp), P<int>(off),
+                    e0, e1, S());
+}
+
+void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
+                 const c10::optional<at::Tensor>& resid, at::Tensor& out, const at::Tensor& off, int64_t e0,
+                 int64_t e1) {
   check_f32(out, "moe_combine: out");
+  const float* r = nullptr;
+  if (resid && resid->defined()) {
+    check_f32(*resid, "moe_combine: resid");
+    TORCH_CHECK(resid->sizes() == out.sizes(), "moe_combine: resid / out shapes");
+    r = P<float>(*resid);
+  }
+  check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(yp.device());
-  const int N = resid.size(0), H = resid.size(1), K = topw.size(1);
-  moe_combine_launch(P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), P<float>(resid), N, K, H, P<float>(out), S());
+  const int N = out.size(0), H = out.size(1), K = topw.size(1);
+  moe_combine_launch(P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), r, N, K, H, P<float>(out), P<int>(off), e0,
+                     e1, S());
 }
 
 void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
-                     at::Tensor& dyp, at::Tensor& dw) {
+                     at::Tensor& dyp, at::Tensor& dw, const at::Tensor& off, int64_t e0, int64_t e1) {
   check_f32(dy, "moe_combine_bwd: dy");
+  check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(dy.device());
   const int N = dy.size(0), H = dy.size(1), K = topw.size(1);
   moe_combine_bwd_launch(P<float>(dy), P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), N, K, H,
-                         P<__nv_bfloat16>(dyp), P<float>(dw), S());
+                         P<__nv_bfloat16>(dyp), P<float>(dw), P<int>(off), e0, e1, S());
 }
 
-void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx) {
+void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx, const at::Tensor& off,
+                   int64_t e0, int64_t e1) {
   check_f32(dxp, "moe_unpermute: dxp");
   check_f32(dx, "moe_unpermute: dx");
+  check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(dx.device());
-  moe_unpermute_launch(P<float>(dxp), P<int>(pos), dx.size(0), K, dx.size(1), P<float>(dx), S());
+  moe_unpermute_launch(P<float>(dxp), P<int>(pos), dx.size(0), K, dx.size(1), P<float>(dx), P<int>(off), e0, e1,
+                       S());
+}
+
+void moe_local_offsets(const at::Tensor& off, int64_t e0, int64_t n, at::Tensor& out) {
+  check_window(off, e0, e0 + n);
+  check_i32(out, "moe_local_offsets: out");
+  TORCH_CHECK(out.numel() >= n + 1, "moe_local_offsets: out too small");
+  c10::cuda::CUDAGuard g(off.device());
+  moe_local_offsets_launch(P<int>(off), e0, n, P<int>(out), S());
 }
 
 void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::Tensor& topw, const at::Tensor& dw,

@@ -49,15 +49,21 @@ void dp_allreduce(const std::vector<uint64_t>& data, const std::vector<uint64_t>
                   double scale, const at::Tensor& counter);
 void group_barrier(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,
                    const at::Tensor& counter);
+void peer_sum(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,
+              const c10::optional<at::Tensor>& addend, const at::Tensor& dst, int64_t n, const at::Tensor& counter);
 void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef, at::Tensor& probs, at::Tensor& topi,
                at::Tensor& topw, at::Tensor& counts, at::Tensor& probsum, at::Tensor& off, at::Tensor& aux,
                at::Tensor& pos);
-void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp);
-void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw, const at::Tensor& resid,
-                 at::Tensor& out);
+void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp, const at::Tensor& off,
+                int64_t e0, int64_t e1);
+void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
+                 const c10::optional<at::Tensor>& resid, at::Tensor& out, const at::Tensor& off, int64_t e0,
+                 int64_t e1);
 void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
-                     at::Tensor& dyp, at::Tensor& dw);
-void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx);
+                     at::Tensor& dyp, at::Tensor& dw, const at::Tensor& off, int64_t e0, int64_t e1);
+void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx, const at::Tensor& off,
+                   int64_t e0, int64_t e1);
+void moe_local_offsets(const at::Tensor& off, int64_t e0, int64_t n, at::Tensor& out);
 void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::Tensor& topw, const at::Tensor& dw,
                     const at::Tensor& daux, const at::Tensor& counts, double coef, const at::Tensor& wg,
                     at::Tensor& dlogits, at::Tensor& dx);

@@ -16,8 +16,25 @@ expert's block from the m-block's segment. Backward mirrors every step; the
 weight gradients use the reduction-grouped GEMM (tile = expert, m, n) over
 exactly that expert's rows. Semantics are the reference's MoELayer
 (moe.py:245-405) with routing weights and aux loss differentiable.
+
+Expert parallelism (ep > 1). The EP ranks of one data replica hold the same
+tokens (the reference shards data by DP rank only, train.py:322), so no
+token ever has to travel: every EP rank routes all of its tokens (the router
+is replicated), gathers only the rows of its own experts (window
+[e0, e0 + E/ep) of the padded segments) and runs those experts once. The
+combine becomes a sum of per-rank partial outputs: each rank writes
+sum_{k: expert local} w_k y_k into a peer-mapped buffer, and one kernel waits
+on a bounded NVLink barrier and adds x + sum over ranks, in rank order, so
+every replica gets the same bits. In backward the combine needs no traffic
+(every partial receives the full gradient). The input gradients of the local
+experts and the routing-weight gradients of the local slots are summed the
+same way before the replicated router backward. Compared with the
+reference's two all-to-alls per layer (moe.py:349-386; every token sent once
+per EP rank), each token is processed once, and each rank reads
+(ep-1) x N x H fp32 of partials per layer in each direction.
 """
 from __future__ import annotations
+
 
 import torch
 
@@ -37,13 +54,57 @@ def _stacks(moe, flat=None):
     return w1, g1, w2, g2
 
 
+def _window(moe):
+    """(first global expert of this rank, one past its last, global expert count)."""
+    El = moe.num_local_experts
+    e0 = moe.ep_rank * El
+    return e0, e0 + El, moe.num_experts
+
+
+class _EPBuffers:
+    """Peer-mapped partial buffers of one MoE layer over its EP group: one for
+    the forward combine (N x H) and one for the backward sums (N x H input
+    gradient + N x K routing-weight gradient). Each call site owns its buffer,
+    which is what makes one barrier per exchange sufficient."""
+
+    def __init__(self, moe, N: int, H: int, K: int, device):
+        from ..parallel.symm import SymmetricBuffer
+        self.N, self.H, self.K = N, H, K
+        self.nb = (N * H + N * K + 3) // 4 * 4
+        self.fwd = SymmetricBuffer(moe.ep_group, N * H * 4, device)
+        self.bwd = SymmetricBuffer(moe.ep_group, self.nb * 4, device)
+        self.rank = self.fwd.rank
+
+    def fwd_partial(self) -> torch.Tensor:
+        return self.fwd.tensor(torch.float32, self.N * self.H).view(self.N, self.H)
+
+    def bwd_parts(self):
+        t = self.bwd.tensor(torch.float32, self.nb)
+        NH = self.N * self.H
+        return t, t[:NH].view(self.N, self.H), t[NH:NH + self.N * self.K].view(self.N, self.K)
+
+
+def _ep_buffers(moe, N: int, H: int, K: int, device) -> _EPBuffers:
+    cache = moe.__dict__.setdefault("_hb_ep_buffers", {})
+    key = (N, H, K, str(device))
+    if key not in cache:
+        cache[key] = _EPBuffers(moe, N, H, K, device)
+    return cache[key]
+
+
+def _peer_sum(buf, addend, dst, n: int) -> None:
+    _ext().peer_sum(buf.ptrs, buf.signal_ptrs, buf.rank, addend, dst, n, buf.counter)
+
+
 def moe_route_and_experts(moe, xn2: torch.Tensor, flat=None):
-    """Router + permutation + the two grouped expert GEMMs for bf16 xn2 [N, H].
+    """Router + permutation + the two grouped expert GEMMs for bf16 xn2 [N, H],
+    over this rank's experts.
 
     Returns (aux, state) where state holds everything combine / backward need."""
     ext = _ext()
     N, H = xn2.shape
-    E = moe.num_local_experts
+    e0, e1, E = _window(moe)
+    El = e1 - e0
     Kk = moe.top_k
     I = moe.config.intermediate_size
     dev = xn2.device
@@ -59,16 +120,38 @@ def moe_route_and_experts(moe, xn2: torch.Tensor, flat=None):
                   pos)
     with torch.no_grad():
         moe._expert_counts = counts  # diagnostics (reference moe.py:329-332)
-    R = (N * Kk + E * (PAD - 1) + PAD - 1) // PAD * PAD  # capacity: every segment padded to 128 rows
+    if El == E:
+        off_l = off
+    else:
+        off_l = torch.empty(El + 1, device=dev, dtype=torch.int32)
+        ext.moe_local_offsets(off, e0, El, off_l)
+    # capacity of this rank's rows: every local segment padded to 128 rows
+    R = (N * Kk + El * (PAD - 1) + PAD - 1) // PAD * PAD
     xp = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
-    ext.moe_gather(xn2, pos, Kk, xp)
+    ext.moe_gather(xn2, pos, Kk, xp, off, e0, e1)
     w1, _, w2, _ = _stacks(moe, flat)
     hp = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
     prep = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
-    G.gemm(xp, w1, hp, I, G.EPI_BF16_GELU, False, False, aux=prep, grp=(1, off, E, I, 0))
+    G.gemm(xp, w1, hp, I, G.EPI_BF16_GELU, False, False, aux=prep, grp=(1, off_l, El, I, 0))
     yp = torch.empty(R, H, device=dev, dtype=torch.bfloat16)
-    G.gemm(hp, w2, yp, H, G.EPI_BF16, False, False, grp=(1, off, E, H, 0))
-    return aux, (probs, topi, topw, counts, off, pos, xp, hp, prep, yp)
+    G.gemm(hp, w2, yp, H, G.EPI_BF16, False, False, grp=(1, off_l, El, H, 0))
+    return aux, (probs, topi, topw, counts, off, off_l, pos, xp, hp, prep, yp)
+
+
+def moe_combine_fwd(moe, state, x1: torch.Tensor) -> torch.Tensor:
+    """x2 = x1 + sum_k w_k y_k (over all experts of all EP ranks)."""
+    ext = _ext()
+    probs, topi, topw, counts, off, off_l, pos, xp, hp, prep, yp = state
+    e0, e1, E = _window(moe)
+    x2 = torch.empty_like(x1)
+    if moe.ep_world_size == 1:
+        ext.moe_combine(yp, pos, topw, x1, x2, off, e0, e1)
+        return x2
+    N, H = x1.shape
+    buf = _ep_buffers(moe, N, H, moe.top_k, x1.device)
+    ext.moe_combine(yp, pos, topw, None, buf.fwd_partial(), off, e0, e1)
+    _peer_sum(buf.fwd, x1, x2, N * H)
+    return x2
 
 
 def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: torch.Tensor, flat=None):
@@ -76,27 +159,41 @@ def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: t
     combined output [N, H]. Returns dxn2 (fp32 [N, H]) and accumulates the
     expert and gate weight gradients."""
     ext = _ext()
-    probs, topi, topw, counts, off, pos, xp, hp, prep, yp = state
+    probs, topi, topw, counts, off, off_l, pos, xp, hp, prep, yp = state
     N, H = xn2.shape
-    E = moe.num_local_experts
+    e0, e1, E = _window(moe)
+    El = e1 - e0
     Kk = moe.top_k
     I = moe.config.intermediate_size
     R = xp.shape[0]
     dev = xn2.device
+    ep = moe.ep_world_size
     w1, g1, w2, g2 = _stacks(moe, flat)
+    if ep > 1:
+        buf = _ep_buffers(moe, N, H, Kk, dev)
+        whole, dxn2_part, dw = buf.bwd_parts()
+    else:
+        dxn2_part = torch.empty(N, H, device=dev, dtype=torch.float32)
+        dw = torch.empty(N, Kk, device=dev, dtype=torch.float32)
     dyp = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
-    dw = torch.empty(N, Kk, device=dev, dtype=torch.float32)
-    ext.moe_combine_bwd(dx_res, yp, pos, topw, dyp, dw)
+    ext.moe_combine_bwd(dx_res, yp, pos, topw, dyp, dw, off, e0, e1)
     dprep = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
-    G.gemm(dyp, w2, dprep, I, G.EPI_BF16_DGELU, False, True, aux=prep, grp=(1, off, E, H, 0))
-    G.gemm(dyp, hp, g2, I, G.EPI_F32_ACC, True, True, grp=(2, off, E, 0, H))
+    G.gemm(dyp, w2, dprep, I, G.EPI_BF16_DGELU, False, True, aux=prep, grp=(1, off_l, El, H, 0))
+    G.gemm(dyp, hp, g2, I, G.EPI_F32_ACC, True, True, grp=(2, off_l, El, 0, H))
     dxp = torch.empty(R, H, device=dev, dtype=torch.float32)
-    G.gemm(dprep, w1, dxp, H, G.EPI_F32, False, True, grp=(1, off, E, I, 0))
-    G.gemm(dprep, xp, g1, H, G.EPI_F32_ACC, True, True, grp=(2, off, E, 0, I))
+    G.gemm(dprep, w1, dxp, H, G.EPI_F32, False, True, grp=(1, off_l, El, I, 0))
+    G.gemm(dprep, xp, g1, H, G.EPI_F32_ACC, True, True, grp=(2, off_l, El, 0, I))
     del dyp, dprep
-    dxn2 = torch.empty(N, H, device=dev, dtype=torch.float32)
-    ext.moe_unpermute(dxp, pos, Kk, dxn2)
+    ext.moe_unpermute(dxp, pos, Kk, dxn2_part, off, e0, e1)
     del dxp
+    if ep > 1:
+        # input and routing-weight gradients of every rank's experts, summed over NVLink
+        summed = torch.empty(buf.nb, device=dev, dtype=torch.float32)
+        _peer_sum(buf.bwd, None, summed, buf.nb)
+        dxn2 = summed[:N * H].view(N, H)
+        dw = summed[N * H:N * H + N * Kk].view(N, Kk)
+    else:
+        dxn2 = dxn2_part
     Ep = (E + 7) // 8 * 8  # row stride of the logits gradient: 16-byte aligned for TMA
     dlog = torch.zeros(N, Ep, device=dev, dtype=torch.bfloat16)
     ext.moe_router_bwd(probs, topi, topw, dw, daux.reshape(1).float().contiguous(), counts, moe.aux_loss_coef,
@@ -108,16 +205,11 @@ def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: t
 def moe_sublayer_fwd(blk, flat, x1: torch.Tensor, keep: bool):
     """x1: fp32 residual [N, H] -> (x2 = x1 + MoE(ln_2(x1)) fp32, aux (0-d), saved)."""
     moe = blk.moe
-    if moe.ep_world_size != 1:
-        raise NotImplementedError("fused MoE runs with ep == 1 (expert parallelism uses the plain path)")
     xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
     aux, state = moe_route_and_experts(moe, xn2, flat)
-    probs, topi, topw, counts, off, pos, xp, hp, prep, yp = state
-    x2 = torch.empty_like(x1)
-    _ext().moe_combine(yp, pos, topw, x1, x2)
+    x2 = moe_combine_fwd(moe, state, x1)
     saved = (x1, xn2, m2, r2, state) if keep else None
     return x2, aux, saved
-
 
 def moe_sublayer_bwd(blk, flat, saved, dres: torch.Tensor, dres16: torch.Tensor, daux: torch.Tensor, ln_scratch):
     """In place: dres / dres16 go from d(x2) to d(x1)."""

@@ -9,7 +9,8 @@ counted once) rather than each shard's local norm.
 One step = sum-of-squares reductions (one per replication class) ->
 optional all-reduce of the squared norm over the model-parallel group ->
 clip coefficient -> one AdamW kernel that also refreshes the bf16 GEMM
-shadow. No host synchronisation: the coefficient stays on the device, and a
+shadow. Within one node the model-parallel sum runs over NVLink in a
+kernel, so the whole step stays inside one captured CUDA graph. No host synchronisation: the coefficient stays on the device, and a
 non-finite norm (fp16 overflow) skips the update inside the kernel.
 """
 from __future__ import annotations
@@ -26,12 +27,18 @@ from .parallel.flat import FlatParams
 
 class FusedAdamW:
     def __init__(self, flat: FlatParams, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
-                 weight_decay: float = 0.1, max_grad_norm: float = 0.0, mp_group: Optional[dist.ProcessGroup] = None):
+                 weight_decay: float = 0.1, max_grad_norm: float = 0.0, mp_group: Optional[dist.ProcessGroup] = None,
+                 mp_symm=None):
+        """``mp_symm``: optional peer-mapped buffer (>= 16 bytes) over ``mp_group``;
+        with it the squared norm is summed over NVLink by a kernel (graph-capturable)
+        instead of an NCCL all-reduce."""
         self.flat = flat
         self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.mp_group = mp_group
+        self.mp_symm = mp_symm
         dev = flat.device
+        self._norm_slot = mp_symm.tensor(torch.float32, 4) if mp_symm is not None else None
         self.m = torch.zeros_like(flat.data)
         self.v = torch.zeros_like(flat.data)
         self.step_count = 0
@@ -52,7 +59,12 @@ class FusedAdamW:
                 first = False
         if first:
             self.norm2.zero_()
-        if self.mp_group is not None and dist.is_initialized() and dist.get_world_size(self.mp_group) > 1:
+        if self._norm_slot is not None:
+            self._norm_slot.zero_()
+            self._norm_slot[0].copy_(self.norm2)
+            self.mp_symm.sum_range(0, 4, 1.0)
+            self.norm2.copy_(self._norm_slot[0])
+        elif self.mp_group is not None and dist.is_initialized() and dist.get_world_size(self.mp_group) > 1:
             dist.all_reduce(self.norm2, group=self.mp_group)
         K.clip_coef(self.norm2, self.max_grad_norm, self.coef, self.norm)
         return self.norm

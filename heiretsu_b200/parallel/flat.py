@@ -48,7 +48,11 @@ def _stack_experts(named: List[Tuple[str, torch.nn.Parameter]]) -> List[Tuple[st
 class FlatParams:
     def __init__(self, module: torch.nn.Module, device: torch.device,
                  weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None, grad_group=None,
-                 tp_group=None):
+                 tp_group=None, tp_sum_of: Optional[Callable[[str, torch.nn.Parameter], bool]] = None):
+        """``tp_sum_of(name, p)``: whether p's gradient is a per-token-shard partial
+        that must be summed over the TP group (TP-replicated parameters under
+        sequence-sharded TP). Parameters are grouped by (norm weight, tp_sum),
+        and ``tp_sum[i]`` tells it for ``ranges[i]``."""
         named: List[Tuple[str, torch.nn.Parameter]] = []
         seen = set()
         for name, p in module.named_parameters():
@@ -57,19 +61,22 @@ class FlatParams:
             seen.add(id(p))
             named.append((name, p))
         weight_of = weight_of or (lambda n, p: 1.0)
-        # Group by norm weight (stable within a group: module order).
-        groups: Dict[float, List[Tuple[str, torch.nn.Parameter]]] = {}
+        tp_sum_of = tp_sum_of or (lambda n, p: False)
+        # Group by (norm weight, TP-sum flag); stable within a group: module order.
+        groups: Dict[Tuple[float, bool], List[Tuple[str, torch.nn.Parameter]]] = {}
         for name, p in named:
-            groups.setdefault(float(weight_of(name, p)), []).append((name, p))
+            groups.setdefault((float(weight_of(name, p)), bool(tp_sum_of(name, p))), []).append((name, p))
         self.ranges: List[Tuple[int, int, float]] = []  # (start, end, weight)
+        self.tp_sum: List[bool] = []
         order: List[Tuple[str, torch.nn.Parameter]] = []
         total = 0
-        for wgt in sorted(groups):
+        for key in sorted(groups):
             start = total
-            for name, p in _stack_experts(groups[wgt]):
+            for name, p in _stack_experts(groups[key]):
                 order.append((name, p))
                 total += _align(p.numel())
-            self.ranges.append((start, total, wgt))
+            self.ranges.append((start, total, key[0]))
+            self.tp_sum.append(key[1])
         self.numel = total
         self.device = device
         self.data = torch.zeros(total, device=device, dtype=torch.float32)

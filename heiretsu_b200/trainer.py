@@ -213,11 +213,17 @@ class Engine:
             use_p2p = topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
             self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo),
                                    grad_group=topo.dp_group if use_p2p else None,
-                                   tp_group=topo.tp_group if topo.tp > 1 else None)
+                                   tp_group=topo.tp_group if topo.tp > 1 else None,
+                                   tp_sum_of=lambda n, p: topo.tp > 1 and not getattr(p, "tp_sharded", False))
             self.module.fused = True
+            clip_group = self.mp_group if args.clip_mode == "global" else None
+            mp_symm = None
+            if clip_group is not None and device.type == "cuda":
+                from .parallel.symm import SymmetricBuffer
+                mp_symm = SymmetricBuffer(clip_group, 16, device)
             self.optimizer = FusedAdamW(self.flat, lr=args.learning_rate, betas=args.betas,
                                         weight_decay=args.weight_decay, max_grad_norm=args.grad_clip,
-                                        mp_group=self.mp_group if args.clip_mode == "global" else None)
+                                        mp_group=clip_group, mp_symm=mp_symm)
             self.scaler = None
         else:
             self.flat = None
@@ -240,7 +246,9 @@ class Engine:
         # reduction, clipping, AdamW) once shapes are known; the first
         # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).
         self.use_graph = (bool(getattr(args, "cuda_graph", 1)) and self.fused and not self.use_pipeline
-                          and (self.reducer is None or self.reducer.backend == "p2p") and self.mp_group is None)
+                          and (self.reducer is None or self.reducer.backend == "p2p")
+                          and (self.mp_group is None or args.clip_mode != "global"
+                               or self.optimizer.mp_symm is not None))
         self._graph = None
         self._eager_steps = 0
         self.GRAPH_WARMUP = 2
@@ -277,6 +285,8 @@ class Engine:
     def _average_scalars(self, loss_scalar, aux):
         """Loss / aux all-reduce over DP (outside any captured graph: NCCL stays out of graphs)."""
         topo = self.topo
+        if self.fused and topo.tp > 1 and dist.is_initialized():
+            dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.tp_group)  # shard losses / tp
         if topo.dp_group is not None and dist.is_initialized():
             both = torch.stack([loss_scalar, aux])
             dist.all_reduce(both, op=dist.ReduceOp.SUM, group=topo.dp_group)
@@ -350,8 +360,8 @@ class Engine:
         """Sum the token-shard partial gradients of TP-replicated parameters over the TP group."""
         if not self.fused or self.topo.tp == 1 or self.flat.grad_symm_tp is None:
             return
-        for start, end, wgt in self.flat.ranges:
-            if wgt < 1.0 and end > start:
+        for (start, end, _), tp_sum in zip(self.flat.ranges, self.flat.tp_sum):
+            if tp_sum and end > start:
                 self.flat.grad_symm_tp.sum_range(start, end - start, 1.0)
 
     def sync_and_step(self) -> None:

@@ -53,14 +53,15 @@ def _worker(rank, world, port, q):
         model = GPT(cfg, topo=topo).to(dev)
         load_from_full(model, full, topo.tp_rank, topo.tp)
         mark_tp_sharded(model)
-        flat = FlatParams(model, dev, weight_of=replication_weight(topo), tp_group=topo.tp_group)
+        flat = FlatParams(model, dev, weight_of=replication_weight(topo), tp_group=topo.tp_group,
+                          tp_sum_of=lambda n, p: not getattr(p, "tp_sharded", False))
         model.fused = True
         for _ in range(2):  # twice: the second pass reuses every buffer and barrier epoch
             flat.zero_grad()
             _, loss_s, _ = model(x, y, return_logits=False)
             loss_s.backward()
-            for start, end, wgt in flat.ranges:
-                if wgt < 1.0:
+            for (start, end, _), tp_sum in zip(flat.ranges, flat.tp_sum):
+                if tp_sum:
                     flat.grad_symm_tp.sum_range(start, end - start, 1.0)
             torch.cuda.synchronize()
             check_status()
