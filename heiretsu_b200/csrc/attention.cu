@@ -46,7 +46,20 @@ struct AttnParams {
   float scale;              // 1/sqrt(64)
   float scale_log2;         // scale * log2(e)
   int* status;
+  uint64_t* trace;          // optional phase timestamps [grid][kTraceSlots] (nullptr: off)
 };
+
+// Phase tracing: with a trace buffer set, the kernels stamp %globaltimer at
+// their pipeline hand-offs (slot layout documented at each kernel), which
+// turns "where does a tile's time go" into a measurement. Off by default;
+// one predicated branch per hand-off when off.
+constexpr int kTraceSlots = 80;
+static uint64_t* g_attn_trace = nullptr;
+#define HB_TRACE(slot)                                                                \
+  do {                                                                                \
+    if (p.trace != nullptr && (slot) < kTraceSlots)                                   \
+      p.trace[(long)blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns();            \
+  } while (0)
 
 __device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
   asm volatile(
@@ -86,44 +99,81 @@ __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 
 
 // Online softmax of one 128x128 score tile held in TMEM, for the calling
 // thread's row: updates (m, l), writes P (bf16) to the swizzled smem tile and
-// returns the rescale factor of the previous accumulator.
+// returns the rescale factor of the previous accumulator. TMEM is read in
+// pairs of 32-column chunks (two loads in flight, one wait); the row max and
+// row sum use four independent chains. The max is taken on raw scores
+// (the scale is positive) and scaled once.
 template <bool DIAG>
 __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
                                               float scale_log2, float& m, float& l) {
-  float v[32];
-  float mt = -INFINITY;
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    tmem_ld32(tS + lane_off + c * 32, v);
+  for (int h = 0; h < 2; ++h) {
+    uint32_t va[32], vb[32];
+    tmem_ld32_issue(tS + lane_off + (2 * h) * 32, va);
+    tmem_ld32_issue(tS + lane_off + (2 * h + 1) * 32, vb);
+    tmem_wait_ld_regs(va);
+    tmem_pin_regs(vb);
 #pragma unroll
     for (int i = 0; i < 32; ++i) {
-      const float sv = v[i] * scale_log2;
-      mt = (DIAG && key0 + c * 32 + i > q) ? mt : fmaxf(mt, sv);
+      float x = __uint_as_float(va[i]), y = __uint_as_float(vb[i]);
+      if (DIAG) {
+        if (key0 + 2 * h * 32 + i > q) x = -INFINITY;
+        if (key0 + (2 * h + 1) * 32 + i > q) y = -INFINITY;
+      }
+      mx[i & 3] = fmaxf(mx[i & 3], fmaxf(x, y));
     }
   }
+  const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
   const float m_new = fmaxf(m, mt);
   const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
-  float rs = 0.f;
+  float sum[4] = {0.f, 0.f, 0.f, 0.f};
 #pragma unroll 1
-  for (int c = 0; c < 4; ++c) {
-    tmem_ld32(tS + lane_off + c * 32, v);
+  for (int h = 0; h < 2; ++h) {
+    uint32_t va[32], vb[32];
+    tmem_ld32_issue(tS + lane_off + (2 * h) * 32, va);
+    tmem_ld32_issue(tS + lane_off + (2 * h + 1) * 32, vb);
+    tmem_wait_ld_regs(va);
+    tmem_pin_regs(vb);
 #pragma unroll
-    for (int i = 0; i < 32; ++i) {
-      float pv = fast_exp2(fmaf(v[i], scale_log2, -m_new));
-      if (DIAG && key0 + c * 32 + i > q) pv = 0.f;
-      v[i] = pv;
-      rs += pv;
-    }
+    for (int half = 0; half < 2; ++half) {
+      const uint32_t* v = half ? vb : va;
+      const int c = 2 * h + half;
+      uint32_t pk[16];
 #pragma unroll
-    for (int g = 0; g < 4; ++g) {
-      const uint4 pk = make_uint4(pack_bf16(v[g * 8 + 0], v[g * 8 + 1]), pack_bf16(v[g * 8 + 2], v[g * 8 + 3]),
-                                  pack_bf16(v[g * 8 + 4], v[g * 8 + 5]), pack_bf16(v[g * 8 + 6], v[g * 8 + 7]));
-      *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 4 + g)) = pk;
+      for (int i = 0; i < 32; i += 2) {
+        float p0 = fast_exp2(fmaf(__uint_as_float(v[i]), scale_log2, -m_new));
+        float p1 = fast_exp2(fmaf(__uint_as_float(v[i + 1]), scale_log2, -m_new));
+        if (DIAG) {
+          if (key0 + c * 32 + i > q) p0 = 0.f;
+          if (key0 + c * 32 + i + 1 > q) p1 = 0.f;
+        }
+        sum[(i >> 1) & 3] += p0 + p1;
+        pk[i >> 1] = pack_bf16(p0, p1);
+      }
+#pragma unroll
+      for (int g = 0; g < 4; ++g)
+        *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 4 + g)) =
+            make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
     }
   }
-  l = l * alpha + rs;
+  l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
   m = m_new;
   return alpha;
+}
+
+// o = o * alpha + (PV result in TMEM, 64 columns of this thread's row).
+__device__ __forceinline__ void accumulate_o(float (&o)[64], uint32_t tO, float alpha) {
+  uint32_t va[32], vb[32];
+  tmem_ld32_issue(tO, va);
+  tmem_ld32_issue(tO + 32, vb);
+  tmem_wait_ld_regs(va);
+  tmem_pin_regs(vb);
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    o[i] = fmaf(o[i], alpha, __uint_as_float(va[i]));
+    o[32 + i] = fmaf(o[32 + i], alpha, __uint_as_float(vb[i]));
+  }
 }
 
 __global__ void __launch_bounds__(FWD_THREADS, 1)
@@ -139,12 +189,15 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_qt = (p.T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
-  int bid = blockIdx.x;
-  const int pair = bid % n_pairs;
-  bid /= n_pairs;
-  const int h = bid % p.nh;
-  const int b = bid / p.nh;
-  const int qt[2] = {pair, n_qt - 1 - pair};
+  // Adjacent query tiles (2q, 2q+1) share a CTA, so the two softmax
+  // warpgroups see 2q+1 and 2q+2 key tiles: always both busy. Pairs are
+  // launched heaviest first (pair index slowest-varying, descending), which
+  // keeps the causal work imbalance out of the tail wave.
+  const int bh = blockIdx.x % (p.B * p.nh);
+  const int pair = n_pairs - 1 - blockIdx.x / (p.B * p.nh);
+  const int h = bh % p.nh;
+  const int b = bh / p.nh;
+  const int qt[2] = {2 * pair, min(2 * pair + 1, n_qt - 1)};
   const bool hasA = qt[0] < qt[1];
   const int n_kv = qt[1] + 1;
 
@@ -172,6 +225,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  if (threadIdx.x == 0) HB_TRACE(0);
   // per tile g: S at g*256, O buffers at g*256 + 128 + {0, 64}
 
   if (warp == 0) {
@@ -203,6 +257,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       constexpr uint32_t idS = make_idesc_f16(128, 128, false, false, true);
       constexpr uint32_t idO = make_idesc_f16(128, 64, false, true, true);
       bool ok = mbar_wait(&bar_q, 0, p.status, 21);
+      HB_TRACE(1);
       auto item = [&](int idx, uint32_t& addr) -> bool {
         const int slot = idx % FWD_SLOTS;
         if (!mbar_wait(&bar_full[slot], (idx / FWD_SLOTS) & 1, p.status, 22)) return false;
@@ -281,12 +336,14 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           ok = false;
           break;
         }
+        if (lane == 0 && sub == 0 && j < 8) HB_TRACE(8 + 24 * g + j);
         tc_fence_after();
         // P smem is free once PV_{j-1} has completed.
         if (j > 0 && !mbar_wait(&bar_o[g][(j - 1) & 1], ((j - 1) >> 1) & 1, p.status, 27)) {
           ok = false;
           break;
         }
+        if (lane == 0 && sub == 0 && j < 8) HB_TRACE(16 + 24 * g + j);
         const float alpha = (j == my_qt)
                                 ? softmax_tile<true>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l)
                                 : softmax_tile<false>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l);
@@ -294,27 +351,16 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         tc_fence_before();
         __syncwarp();
         if (lane == 0) mbar_arrive(&bar_p[g]);
+        if (lane == 0 && sub == 0 && j < 8) HB_TRACE(24 + 24 * g + j);
         if (j > 0) {
           tc_fence_after();
-          float v[32];
-#pragma unroll
-          for (int c = 0; c < 2; ++c) {
-            tmem_ld32(tO0 + ((j - 1) & 1) * 64 + lane_off + c * 32, v);
-#pragma unroll
-            for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_prev, v[i]);
-          }
+          accumulate_o(o, tO0 + ((j - 1) & 1) * 64 + lane_off, alpha_prev);
         }
         alpha_prev = alpha;
       }
       if (ok && mbar_wait(&bar_o[g][(n - 1) & 1], ((n - 1) >> 1) & 1, p.status, 28)) {
         tc_fence_after();
-        float v[32];
-#pragma unroll
-        for (int c = 0; c < 2; ++c) {
-          tmem_ld32(tO0 + ((n - 1) & 1) * 64 + lane_off + c * 32, v);
-#pragma unroll
-          for (int i = 0; i < 32; ++i) o[c * 32 + i] = fmaf(o[c * 32 + i], alpha_prev, v[i]);
-        }
+        accumulate_o(o, tO0 + ((n - 1) & 1) * 64 + lane_off, alpha_prev);
         if (q < p.T) {
           const float inv = 1.f / l;
           __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD;
@@ -335,6 +381,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) HB_TRACE(2);
 }
 
 // ============================================================================
@@ -360,11 +407,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
   const int n_t = (p.T + kTile - 1) / kTile;
-  int bid = blockIdx.x;
-  const int kt = bid % n_t;
-  bid /= n_t;
-  const int h = bid % p.nh;
-  const int b = bid / p.nh;
+  // Key tile slowest-varying, ascending: the CTAs with the most query tiles launch first.
+  const int bh = blockIdx.x % (p.B * p.nh);
+  const int kt = blockIdx.x / (p.B * p.nh);
+  const int h = bh % p.nh;
+  const int b = bh / p.nh;
   const int n_i = n_t - kt;  // query tiles kt .. n_t-1
 
   if (threadIdx.x == 0) {
@@ -391,6 +438,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   __syncthreads();
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
+  if (threadIdx.x == 0) HB_TRACE(0);
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
   const long lse_base = ((long)b * p.nh + h) * p.Tpad;
 
@@ -433,6 +481,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         mma_commit(&bar_h[g]);
       };
       bool ok = mbar_wait(&bar_kv, 0, p.status, 42) && stage_ready(0);
+      HB_TRACE(1);
       if (ok) {
         issue_half(0, 0);
         issue_half(0, 1);
@@ -442,6 +491,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         const uint32_t doa = qa + kTileBytes;
         // half 0 of P^T / dS^T (queries 0..63) is in smem
         if (!mbar_wait(&bar_p[0], ii & 1, p.status, 43)) break;
+        if (ii < 8) HB_TRACE(8 + ii);
         tc_fence_after();
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
@@ -456,6 +506,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           issue_half(ii + 1, 0);
         }
         if (!mbar_wait(&bar_p[1], ii & 1, p.status, 44)) break;
+        if (ii < 8) HB_TRACE(16 + ii);
         tc_fence_after();
 #pragma unroll
         for (int ks = 4; ks < 8; ++ks) {
@@ -501,54 +552,77 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         ok = false;
         break;
       }
+      if (lane == 0 && sub == 0 && ii < 8) HB_TRACE(24 + 24 * g + ii);
       tc_fence_after();
       const float* s_lse = reinterpret_cast<const float*>(sStage + st * BWD_STAGE + 2 * kTileBytes) + g * 64;
       const float* s_d = s_lse + 128;
       const bool diag = (qi == kt);
-      // P^T and dS^T of this half, packed to bf16 in registers.
-      uint32_t pk[2][32];
+      // Only the diagonal tile and a tile crossing T need per-element masks.
+      const bool masked_tile = diag || (qi + 1) * kTile > p.T;
+      const float4* lse4 = reinterpret_cast<const float4*>(s_lse);
+      const float4* d4 = reinterpret_cast<const float4*>(s_d);
+      bool waited = (ii == 0);  // P^T / dS^T smem is free before the first tile
+      // Two 32-column chunks of this half: both TMEM loads in flight at once,
+      // P^T and dS^T packed to bf16 and stored right away (few live registers).
+#pragma unroll 1
+      for (int c = 0; c < 2 && ok; ++c) {
+        uint32_t sr[32], dr[32];
+        tmem_ld32_issue(tS + g * 64 + c * 32 + lane_off, sr);
+        tmem_ld32_issue(tDP + g * 64 + c * 32 + lane_off, dr);
+        tmem_wait_ld_regs(sr);
+        tmem_pin_regs(dr);
+        uint32_t pp[16], dd[16];
 #pragma unroll
-      for (int c = 0; c < 2; ++c) {
-        float sv[32], dp[32];
-        tmem_ld32(tS + g * 64 + c * 32 + lane_off, sv);
-        tmem_ld32(tDP + g * 64 + c * 32 + lane_off, dp);
+        for (int i4 = 0; i4 < 8; ++i4) {
+          const float4 L = lse4[c * 8 + i4];
+          const float4 Dv = d4[c * 8 + i4];
+          const float lv[4] = {L.x, L.y, L.z, L.w};
+          const float dv[4] = {Dv.x, Dv.y, Dv.z, Dv.w};
+          float pr[4], ds[4];
 #pragma unroll
-        for (int i = 0; i < 32; i += 2) {
-          float pr[2], ds[2];
-#pragma unroll
-          for (int e = 0; e < 2; ++e) {
-            const int col = c * 32 + i + e;
-            const int qq = qi * kTile + g * 64 + col;
-            const bool masked = (diag && key > qq) || qq >= p.T;
-            const float pv = fast_exp2(fmaf(sv[i + e], p.scale_log2, -s_lse[col]));
-            pr[e] = masked ? 0.f : pv;
-            ds[e] = masked ? 0.f : pv * (dp[i + e] - s_d[col]) * p.scale;
+          for (int e = 0; e < 4; ++e) {
+            const int i = i4 * 4 + e;
+            const float pv = fast_exp2(fmaf(__uint_as_float(sr[i]), p.scale_log2, -lv[e]));
+            const float dsv = pv * (__uint_as_float(dr[i]) - dv[e]) * p.scale;
+            if (masked_tile) {
+              const int qq = qi * kTile + g * 64 + c * 32 + i;
+              const bool masked = (diag && key > qq) || qq >= p.T;
+              pr[e] = masked ? 0.f : pv;
+              ds[e] = masked ? 0.f : dsv;
+            } else {
+              pr[e] = pv;
+              ds[e] = dsv;
+            }
           }
-          pk[0][c * 16 + i / 2] = pack_bf16(pr[0], pr[1]);
-          pk[1][c * 16 + i / 2] = pack_bf16(ds[0], ds[1]);
+          pp[2 * i4] = pack_bf16(pr[0], pr[1]);
+          pp[2 * i4 + 1] = pack_bf16(pr[2], pr[3]);
+          dd[2 * i4] = pack_bf16(ds[0], ds[1]);
+          dd[2 * i4 + 1] = pack_bf16(ds[2], ds[3]);
         }
-      }
-      // The previous tile's MMAs read P^T / dS^T smem and wrote dQ: wait,
-      // flush that dQ half, then overwrite this half of P^T / dS^T.
-      if (ii > 0) {
-        if (!mbar_wait(&bar_mma, (ii - 1) & 1, p.status, 48)) {
-          ok = false;
-          break;
+        // The previous tile's MMAs read P^T / dS^T smem and wrote dQ: wait once,
+        // flush that dQ half, then overwrite this half of P^T / dS^T.
+        if (!waited) {
+          if (!mbar_wait(&bar_mma, (ii - 1) & 1, p.status, 48)) {
+            ok = false;
+            break;
+          }
+          if (lane == 0 && sub == 0 && ii < 8) HB_TRACE(32 + 24 * g + ii);
+          flush_dq(qi - 1);
+          waited = true;
         }
-        flush_dq(qi - 1);
-      }
 #pragma unroll
-      for (int c16 = 0; c16 < 8; ++c16) {
-        const uint32_t off = sw128_off(r, g * 8 + c16);
-        *reinterpret_cast<uint4*>(sP + off) =
-            make_uint4(pk[0][c16 * 4], pk[0][c16 * 4 + 1], pk[0][c16 * 4 + 2], pk[0][c16 * 4 + 3]);
-        *reinterpret_cast<uint4*>(sDS + off) =
-            make_uint4(pk[1][c16 * 4], pk[1][c16 * 4 + 1], pk[1][c16 * 4 + 2], pk[1][c16 * 4 + 3]);
+        for (int q = 0; q < 4; ++q) {
+          const uint32_t off = sw128_off(r, g * 8 + c * 4 + q);
+          *reinterpret_cast<uint4*>(sP + off) = make_uint4(pp[4 * q], pp[4 * q + 1], pp[4 * q + 2], pp[4 * q + 3]);
+          *reinterpret_cast<uint4*>(sDS + off) = make_uint4(dd[4 * q], dd[4 * q + 1], dd[4 * q + 2], dd[4 * q + 3]);
+        }
       }
+      if (!ok) break;
       fence_proxy_async_smem();
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_p[g]);
+      if (lane == 0 && sub == 0 && ii < 8) HB_TRACE(40 + 24 * g + ii);
     }
     if (ok && mbar_wait(&bar_mma, (n_i - 1) & 1, p.status, 49)) {
       flush_dq(kt + n_i - 1);
@@ -575,6 +649,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     tc_fence_after();
     tmem_dealloc(tmem, 512);
   }
+  if (threadIdx.x == 0) HB_TRACE(2);
 }
 
 // D[b, h, t] = sum_d dO[b*T+t, h*64+d] * O[b*T+t, h*64+d]   (fp32)
@@ -632,6 +707,7 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   p.status = status;
+  p.trace = g_attn_trace;
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
@@ -658,6 +734,7 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   p.status = status;
+  p.trace = g_attn_trace;
   const CUtensorMap tq = qkv_map(qkv, B, T, ld_qkv, 3 * Hs);
   const CUtensorMap td = qkv_map(dO, B, T, ld_do, Hs);
   const int n_t = (T + kTile - 1) / kTile;
@@ -666,5 +743,13 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
   HB_CUDA_CHECK(cudaGetLastError());
 }
+
+// Trace buffer for the next attention launches (nullptr turns tracing off).
+// Forward slots per CTA: 0 start, 1 Q ready (MMA warp), 2 end; for KV tile j < 8
+// and query tile g: 8+24g+j S ready, 16+24g+j previous PV done, 24+24g+j P written.
+// Backward slots per CTA: 0 start, 1 K/V and first Q/dO ready, 2 end; for query
+// tile i < 8: 8+i / 16+i P^T half 0 / half 1 consumed by the MMA warp; for half g:
+// 24+24g+i S^T/dP^T ready, 32+24g+i previous tile's MMAs done, 40+24g+i P^T/dS^T written.
+void attn_set_trace(uint64_t* trace) { g_attn_trace = trace; }
 
 }  // namespace hb

@@ -30,6 +30,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("clip_coef", &hb::clip_coef);
   m.def("adamw_step", &hb::adamw_step);
   m.def("f32_to_bf16", &hb::f32_to_bf16);
+  m.def("attention_set_trace", &hb::attention_set_trace);
   m.def("attention_fwd", &hb::attention_fwd);
   m.def("attention_bwd", &hb::attention_bwd);
   m.def("raw_malloc", &hb::raw_malloc);

@@ -36,6 +36,7 @@ void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const
 void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 const c10::optional<at::Tensor>& p16, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
 void f32_to_bf16(const at::Tensor& x, at::Tensor& y);
+void attention_set_trace(const c10::optional<at::Tensor>& trace);
 void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse);
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
                    int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv);

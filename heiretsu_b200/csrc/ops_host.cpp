@@ -219,6 +219,20 @@ void f32_to_bf16(const at::Tensor& x, at::Tensor& y) {
   f32_to_bf16_launch(ptr<float>(x), ptr<__nv_bfloat16>(y), x.numel(), stream());
 }
 
+void attn_set_trace(uint64_t* trace);
+
+// Phase timestamps of the following attention launches go to `trace`
+// (int64 [grid * 80] on the device); None turns tracing off.
+void attention_set_trace(const c10::optional<at::Tensor>& trace) {
+  if (trace && trace->defined()) {
+    TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous(),
+                "attention_set_trace: int64 contiguous CUDA tensor");
+    attn_set_trace(reinterpret_cast<uint64_t*>(trace->data_ptr()));
+  } else {
+    attn_set_trace(nullptr);
+  }
+}
+
 void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse) {
   CHECK_CUDA(qkv);
   CHECK_DT(qkv, at::kBFloat16);
