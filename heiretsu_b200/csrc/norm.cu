@@ -15,12 +15,13 @@ namespace hb {
 
 // Rows are processed one per warp; each lane holds V4 float4 of the row
 // (V4 = ceil(H / 128), a template parameter so no register is wasted).
-// The backward kernel handles LN_BWD_ROWS rows per warp with all loads of a
-// row issued before any arithmetic, and writes one partial (dgamma, dbeta)
-// row per CTA; a second kernel reduces the partials in a fixed order.
+// The backward kernel runs two CTAs per SM whose warps stride over the rows
+// (all loads of a row issued before any arithmetic), keeps the dgamma /
+// dbeta partials in registers, sums its warps' partials in a fixed order
+// and writes one partial row per CTA; a second kernel reduces those rows in
+// a fixed order, so the result is deterministic.
 constexpr int LN_ROWS_PER_CTA = 8;   // forward: 8 warps, one row each
 constexpr int LN_BWD_WARPS = 8;
-constexpr int LN_BWD_ROWS = 4;       // rows per warp in backward
 
 template <int V4>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
@@ -150,24 +151,23 @@ __global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restri
 // Per-CTA partials are accumulated with shared-memory atomics (no per-thread
 // accumulators), which keeps registers low enough for 3 CTAs per SM.
 template <int V4>
-__global__ void __launch_bounds__(256) ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
-                                                     const float* __restrict__ mean, const float* __restrict__ rstd,
-                                                     const float* __restrict__ w, const float* dres_in,
-                                                     float* dres, __nv_bfloat16* __restrict__ dres16,
-                                                     float* __restrict__ part, int M, int H, int dy_srcs,
-                                                     long dy_src_stride) {
-  extern __shared__ float sacc[];  // [2][H]: dgamma, dbeta partials of this CTA
+__global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
+                                                        const float* __restrict__ mean, const float* __restrict__ rstd,
+                                                        const float* __restrict__ w, const float* dres_in,
+                                                        float* dres, __nv_bfloat16* __restrict__ dres16,
+                                                        float* __restrict__ part, int M, int H, int dy_srcs,
+                                                        long dy_src_stride) {
+  extern __shared__ float sacc[];  // [LN_BWD_WARPS][2][H]: each warp's dgamma, dbeta partials
   const int warp_in = threadIdx.x >> 5;
   const int lane = threadIdx.x & 31;
   const int H4 = H >> 2;
-  for (int c = threadIdx.x; c < 2 * H; c += blockDim.x) sacc[c] = 0.f;
-  __syncthreads();
   const float4* w4 = reinterpret_cast<const float4*>(w);
-  const int row0 = (blockIdx.x * LN_BWD_WARPS + warp_in) * LN_BWD_ROWS;
+  float4 gacc[V4], bacc[V4];
+#pragma unroll
+  for (int i = 0; i < V4; ++i) gacc[i] = bacc[i] = make_float4(0.f, 0.f, 0.f, 0.f);
+  // Warps stride over rows; dgamma / dbeta partials stay in registers.
 #pragma unroll 1
-  for (int rr = 0; rr < LN_BWD_ROWS; ++rr) {
-    const int r = row0 + rr;
-    if (r >= M) break;
+  for (int r = blockIdx.x * LN_BWD_WARPS + warp_in; r < M; r += gridDim.x * LN_BWD_WARPS) {
     const float4* xr = reinterpret_cast<const float4*>(x + (long)r * H);
     const float4* dyr = reinterpret_cast<const float4*>(dy + (long)r * H);
     float4 xv[V4], dv[V4];
@@ -193,16 +193,14 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const float* __restrict__ d
       const int j = lane + 32 * i;
       xv[i] = make_float4((xv[i].x - mu) * rs, (xv[i].y - mu) * rs, (xv[i].z - mu) * rs, (xv[i].w - mu) * rs);
       if (j < H4) {
-        float* g = sacc + 4 * j;
-        float* bsum = sacc + H + 4 * j;
-        atomicAdd(g + 0, dv[i].x * xv[i].x);
-        atomicAdd(g + 1, dv[i].y * xv[i].y);
-        atomicAdd(g + 2, dv[i].z * xv[i].z);
-        atomicAdd(g + 3, dv[i].w * xv[i].w);
-        atomicAdd(bsum + 0, dv[i].x);
-        atomicAdd(bsum + 1, dv[i].y);
-        atomicAdd(bsum + 2, dv[i].z);
-        atomicAdd(bsum + 3, dv[i].w);
+        gacc[i].x = fmaf(dv[i].x, xv[i].x, gacc[i].x);
+        gacc[i].y = fmaf(dv[i].y, xv[i].y, gacc[i].y);
+        gacc[i].z = fmaf(dv[i].z, xv[i].z, gacc[i].z);
+        gacc[i].w = fmaf(dv[i].w, xv[i].w, gacc[i].w);
+        bacc[i].x += dv[i].x;
+        bacc[i].y += dv[i].y;
+        bacc[i].z += dv[i].z;
+        bacc[i].w += dv[i].w;
         const float4 ww = w4[j];
         dv[i] = make_float4(dv[i].x * ww.x, dv[i].y * ww.y, dv[i].z * ww.z, dv[i].w * ww.w);  // g = dy * w
       }
@@ -227,9 +225,24 @@ __global__ void __launch_bounds__(256) ln_bwd_kernel(const float* __restrict__ d
       }
     }
   }
+  // Per-CTA reduction of the warps' partials in a fixed order (deterministic).
+  float4* mine = reinterpret_cast<float4*>(sacc + (long)warp_in * 2 * H);
+#pragma unroll
+  for (int i = 0; i < V4; ++i) {
+    const int j = lane + 32 * i;
+    if (j < H4) {
+      mine[j] = gacc[i];
+      mine[H4 + j] = bacc[i];
+    }
+  }
   __syncthreads();
   float* out = part + (long)blockIdx.x * 2 * H;
-  for (int c = threadIdx.x; c < 2 * H; c += blockDim.x) out[c] = sacc[c];
+  for (int c = threadIdx.x; c < 2 * H; c += blockDim.x) {
+    float acc = 0.f;
+#pragma unroll
+    for (int wi = 0; wi < LN_BWD_WARPS; ++wi) acc += sacc[(long)wi * 2 * H + c];
+    out[c] = acc;
+  }
 }
 
 // out0[c] / out1[c - split] += sum_r part[r, c]: 32 columns x 8 row-slices per
@@ -328,16 +341,27 @@ void resid_sum_ln_launch(const float* x, const __nv_bfloat16* parts, int nsrc, l
 }
 
 int ln_bwd_num_ctas(int M, int device) {
-  (void)device;
-  const int per = LN_BWD_WARPS * LN_BWD_ROWS;
-  return M > 0 ? (M + per - 1) / per : 1;
+  // Two resident CTAs per SM, never more CTAs than there are 8-row groups.
+  const int full = 2 * num_sms(device);
+  const int need = M > 0 ? (M + LN_BWD_WARPS - 1) / LN_BWD_WARPS : 1;
+  return need < full ? need : full;
 }
 
 void ln_bwd_launch(const float* dy, const float* x, const float* mean, const float* rstd, const float* w,
                    const float* dres_in, float* dres, __nv_bfloat16* dres16, float* part, int num_ctas,
                    float* dgamma, float* dbeta, int M, int H, int dy_srcs, long dy_src_stride, cudaStream_t s) {
   if (M == 0) return;
-  const size_t smem = 2 * H * sizeof(float);
+  const size_t smem = (size_t)LN_BWD_WARPS * 2 * H * sizeof(float);
+  if (smem > 48 * 1024) {
+    static bool attr_set[64][17] = {};
+    const int dev = current_device();
+    const int v = ln_v4(H);
+    if (!attr_set[dev][v]) {
+      HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<kV>,
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
+      attr_set[dev][v] = true;
+    }
+  }
   HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
                                                                           dres16, part, M, H, dy_srcs,
                                                                           dy_src_stride));
