@@ -1,6 +1,7 @@
 // Torch-facing entry point of the tcgen05 GEMM: validates tensors, builds
 // the TMA descriptors and picks the instantiation (gemm_inst_*.cu).
 #include <ATen/cuda/CUDAContext.h>
+#include <cstdlib>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
 
@@ -10,15 +11,30 @@
 
 namespace hb {
 
-void gemm_launch_128_kk(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-void gemm_launch_128_kn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-void gemm_launch_128_nn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-void gemm_launch_256_kk(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-void gemm_launch_256_kn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
-void gemm_launch_256_nn(int, const CUtensorMap&, const CUtensorMap&, const GemmParams&, cudaStream_t);
+void gemm_launch_128_kk(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_128_kn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_128_nn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_256_kk(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_256_kn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_256_nn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
 
 // Tensor map over a row-major bf16 matrix [rows, cols] (cols contiguous):
 // box = 64 columns (one 128-byte swizzle row) x box_rows rows.
+// HB_GEMM_TMA_EPILOGUE=0 selects the per-lane store epilogue (for comparisons).
+static bool tma_epilogue_enabled() {
+  static const bool on = [] {
+    const char* v = std::getenv("HB_GEMM_TMA_EPILOGUE");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
 static CUtensorMap operand_map(const at::Tensor& t, int box_rows) {
   return make_tmap_2d_bf16(t.data_ptr(), t.size(1), t.size(0), t.stride(0) * 2, 64, box_rows);
 }
@@ -156,16 +172,44 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   }
   const CUtensorMap ta = operand_map(a, a_mn ? 64 : 128);
   const CUtensorMap tb = operand_map(b, b_mn ? 64 : BN);
+  // Epilogue output maps (bulk tensor stores / fp32 reduce-adds of 32x32
+  // chunks, swizzled like the staging tile). Peer outputs (reduce-scatter)
+  // and outputs smaller than one chunk keep per-lane stores.
+  CUtensorMap tc{}, tx{};
+  p.tma_epi = 0;
+  {
+    const bool c_f32 = !(epi == kEpiBf16 || epi == kEpiBf16Gelu || epi == kEpiBf16Dgelu);
+    const long esz = c_f32 ? 4 : 2;
+    const long c_rows = (grp_mode == 2) ? (long)grp_n * grp_c_off : M;
+    bool ok = tma_epilogue_enabled() && rs_dst.empty() && M >= 32 && N >= 32 && (grp_mode != 2 || M % 128 == 0) &&
+              reinterpret_cast<uintptr_t>(c.data_ptr()) % 16 == 0 && (c.stride(0) * esz) % 16 == 0 &&
+              c.size(0) >= c_rows && c.size(1) >= N;
+    if (epi == kEpiBf16Gelu)
+      ok = ok && reinterpret_cast<uintptr_t>(p.aux) % 16 == 0 && (p.ldaux * 2) % 16 == 0;
+    if (ok) {
+      const uint64_t cdims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(c_rows)};
+      const uint64_t cstr[1] = {static_cast<uint64_t>(c.stride(0) * esz)};
+      const uint32_t box[2] = {32, 32};
+      tc = make_tmap(c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c.data_ptr(),
+                     cdims, cstr, box, c_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+      if (epi == kEpiBf16Gelu) {
+        const uint64_t xdims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
+        const uint64_t xstr[1] = {static_cast<uint64_t>(p.ldaux * 2)};
+        tx = make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.aux, xdims, xstr, box, CU_TENSOR_MAP_SWIZZLE_64B);
+      }
+      p.tma_epi = 1;
+    }
+  }
   cudaStream_t s = at::cuda::getCurrentCUDAStream();
   const int e = e_launch;
   if (BN == 256) {
-    if (!a_mn && !b_mn) gemm_launch_256_kk(e, ta, tb, p, s);
-    else if (!a_mn) gemm_launch_256_kn(e, ta, tb, p, s);
-    else gemm_launch_256_nn(e, ta, tb, p, s);
+    if (!a_mn && !b_mn) gemm_launch_256_kk(e, ta, tb, tc, tx, p, s);
+    else if (!a_mn) gemm_launch_256_kn(e, ta, tb, tc, tx, p, s);
+    else gemm_launch_256_nn(e, ta, tb, tc, tx, p, s);
   } else {
-    if (!a_mn && !b_mn) gemm_launch_128_kk(e, ta, tb, p, s);
-    else if (!a_mn) gemm_launch_128_kn(e, ta, tb, p, s);
-    else gemm_launch_128_nn(e, ta, tb, p, s);
+    if (!a_mn && !b_mn) gemm_launch_128_kk(e, ta, tb, tc, tx, p, s);
+    else if (!a_mn) gemm_launch_128_kn(e, ta, tb, tc, tx, p, s);
+    else gemm_launch_128_nn(e, ta, tb, tc, tx, p, s);
   }
 }
 

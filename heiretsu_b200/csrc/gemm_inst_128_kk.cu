@@ -3,7 +3,8 @@
 #include "gemm_kernel.cuh"
 
 namespace hb {
-void gemm_launch_128_kk(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
-  gemm_dispatch_epi<128, false, false>(epi, ta, tb, p, s);
+void gemm_launch_128_kk(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                        const CUtensorMap& tx, const GemmParams& p, cudaStream_t s) {
+  gemm_dispatch_epi<128, false, false>(epi, ta, tb, tc, tx, p, s);
 }
 }  // namespace hb

@@ -244,6 +244,70 @@ __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_b
   __syncwarp();
 }
 
+// Step 2, TMA form: bias / activation, stage the chunk, one lane issues the
+// bulk store (or reduce-add). `row` is the chunk's first row in the C map.
+// The caller has waited for the previous bulk copies to finish reading `stg`.
+template <int EPI>
+__device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmX,
+                                               int row, int n0, float (&v)[32], uint8_t* stg, int lane) {
+  if (p.bias != nullptr && (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      if (n0 + j < p.N) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
+        v[j] += b.x;
+        v[j + 1] += b.y;
+        v[j + 2] += b.z;
+        v[j + 3] += b.w;
+      }
+    }
+  }
+  if constexpr (EPI == kEpiBf16Gelu) {
+    // pre-activation (bf16) -> first 2 KB of the staging tile; GELU of the
+    // rounded value -> second 2 KB; two stores.
+    uint32_t pk[16];
+#pragma unroll
+    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+    for (int g = 0; g < 4; ++g)
+      *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
+          make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[2 * j] = gelu_tanh(__uint_as_float(pk[j] << 16));
+      v[2 * j + 1] = gelu_tanh(__uint_as_float(pk[j] & 0xffff0000u));
+    }
+    stg_put_bf16(stg + 2048, lane, v);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmX, stg, n0, row);
+      tma_store_2d(tmC, stg + 2048, n0, row);
+      bulk_commit_group();
+    }
+  } else if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Dgelu) {
+    stg_put_bf16(stg, lane, v);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      tma_store_2d(tmC, stg, n0, row);
+      bulk_commit_group();
+    }
+  } else {
+    stg_put_f32(stg, lane, v);
+    fence_proxy_async_smem();
+    __syncwarp();
+    if (lane == 0) {
+      if constexpr (EPI == kEpiF32Acc || EPI == kEpiF32Atomic) {
+        tma_reduce_add_2d(tmC, stg, n0, row);  // C += chunk, added in L2
+      } else {
+        tma_store_2d(tmC, stg, n0, row);
+      }
+      bulk_commit_group();
+    }
+  }
+}
+
 // ---------------------------------------------------------------------------
 // All-gather prologue helpers
 // ---------------------------------------------------------------------------
@@ -308,7 +372,8 @@ __device__ __forceinline__ bool ag_wait_rows(const GemmParams& p, int mb) {
 
 template <int BN, bool A_MN, bool B_MN, int EPI>
 __global__ void __launch_bounds__(kGemmThreads, 1)
-    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB, GemmParams p) {
+    gemm_tc_kernel(const __grid_constant__ CUtensorMap tmA, const __grid_constant__ CUtensorMap tmB,
+                   const __grid_constant__ CUtensorMap tmC, const __grid_constant__ CUtensorMap tmX, GemmParams p) {
   using Cfg = GemmCfg<BN>;
   constexpr int BM = Cfg::BM, BK = Cfg::BK, STAGES = Cfg::STAGES;
   constexpr int A_BYTES = Cfg::A_BYTES, STAGE_BYTES = Cfg::STAGE_BYTES;
@@ -496,9 +561,13 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
         C = static_cast<uint8_t*>(p.rs_dst[owner]) +
             ((long)p.rs_rank * p.rs_rows - (long)owner * p.rs_rows) * p.ldc * esz;
       }
+      const bool tma = p.tma_epi != 0;
+      const int row = (p.grp_mode == 2 ? grp * p.grp_c_off : 0) + m_base;  // chunk row in the C map
+      // With TMA the accumulating epilogue is a reduce-add in L2: no operand read.
+      const bool reads = epi_reads_operand<EPI>() && !(tma && EPI == kEpiF32Acc);
       uint4 pre[8];
       const int n_first = nb * BN + c0 * 32;
-      if (epi_reads_operand<EPI>() && nkb_ > 0 && n_first < p.N) epi_prefetch<EPI>(p, C, m_base, n_first, lane, pre);
+      if (reads && nkb_ > 0 && n_first < p.N) epi_prefetch<EPI>(p, C, m_base, n_first, lane, pre);
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
       tc_fence_after();
       if (nkb_ > 0) {  // an empty expert segment accumulated nothing and stores nothing
@@ -508,16 +577,25 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (n0 >= p.N) break;
           float v[32];
           tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + (c0 + c) * 32, v);
-          epi_apply_operand<EPI>(v, stg, pre, lane);
-          if (epi_reads_operand<EPI>() && c + 1 < CH && n0 + 32 < p.N)
-            epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
-          epi_finish<EPI>(p, C, m_base, n0, v, stg, lane);
+          if (tma) {  // the staging tile is reused: the previous bulk copies must have read it
+            if (lane == 0) bulk_wait_group_read0();
+            __syncwarp();
+          }
+          if (reads) epi_apply_operand<EPI>(v, stg, pre, lane);
+          if (reads && c + 1 < CH && n0 + 32 < p.N) epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
+          if (tma) {
+            epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane);
+          } else {
+            epi_finish<EPI>(p, C, m_base, n0, v, stg, lane);
+          }
         }
       }
       tc_fence_before();
       __syncwarp();
       if (lane == 0) mbar_arrive(&tempty[acc]);
     }
+    if (p.tma_epi && lane == 0) bulk_wait_group0();  // every bulk store / reduce has landed
+    __syncwarp();
   }
   __syncthreads();
   if (warp == 1) {
@@ -529,7 +607,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
 
 // Launch one instantiation (defined in gemm_inst_*.cu).
 template <int BN, bool A_MN, bool B_MN, int EPI>
-void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t stream) {
+void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc, const CUtensorMap& tx,
+                 const GemmParams& p, cudaStream_t stream) {
   using Cfg = GemmCfg<BN>;
   auto kern = gemm_tc_kernel<BN, A_MN, B_MN, EPI>;
   static bool attr_set[64] = {};
@@ -541,21 +620,22 @@ void launch_gemm(const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams&
   const int num_tiles =
       ((p.M + 127) / 128) * ((p.N + BN - 1) / BN) * p.splits * (p.grp_mode == 2 ? p.grp_n : 1);
   const int grid = num_tiles < num_sms(dev) ? num_tiles : num_sms(dev);
-  kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, p);
+  kern<<<grid, kGemmThreads, Cfg::SMEM_BYTES, stream>>>(ta, tb, tc, tx, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 // Dispatch over epilogues for one (BN, majors) combination.
 template <int BN, bool A_MN, bool B_MN>
-void gemm_dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const GemmParams& p, cudaStream_t s) {
+void gemm_dispatch_epi(int epi, const CUtensorMap& ta, const CUtensorMap& tb, const CUtensorMap& tc,
+                       const CUtensorMap& tx, const GemmParams& p, cudaStream_t s) {
   switch (epi) {
-    case kEpiBf16: return launch_gemm<BN, A_MN, B_MN, kEpiBf16>(ta, tb, p, s);
-    case kEpiBf16Gelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Gelu>(ta, tb, p, s);
-    case kEpiF32: return launch_gemm<BN, A_MN, B_MN, kEpiF32>(ta, tb, p, s);
-    case kEpiF32Acc: return launch_gemm<BN, A_MN, B_MN, kEpiF32Acc>(ta, tb, p, s);
-    case kEpiF32Resid: return launch_gemm<BN, A_MN, B_MN, kEpiF32Resid>(ta, tb, p, s);
-    case kEpiBf16Dgelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Dgelu>(ta, tb, p, s);
-    case kEpiF32Atomic: return launch_gemm<BN, A_MN, B_MN, kEpiF32Atomic>(ta, tb, p, s);
+    case kEpiBf16: return launch_gemm<BN, A_MN, B_MN, kEpiBf16>(ta, tb, tc, tx, p, s);
+    case kEpiBf16Gelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Gelu>(ta, tb, tc, tx, p, s);
+    case kEpiF32: return launch_gemm<BN, A_MN, B_MN, kEpiF32>(ta, tb, tc, tx, p, s);
+    case kEpiF32Acc: return launch_gemm<BN, A_MN, B_MN, kEpiF32Acc>(ta, tb, tc, tx, p, s);
+    case kEpiF32Resid: return launch_gemm<BN, A_MN, B_MN, kEpiF32Resid>(ta, tb, tc, tx, p, s);
+    case kEpiBf16Dgelu: return launch_gemm<BN, A_MN, B_MN, kEpiBf16Dgelu>(ta, tb, tc, tx, p, s);
+    case kEpiF32Atomic: return launch_gemm<BN, A_MN, B_MN, kEpiF32Atomic>(ta, tb, tc, tx, p, s);
     default: throw std::runtime_error("gemm: unknown epilogue");
   }
 }

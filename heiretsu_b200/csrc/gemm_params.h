@@ -60,6 +60,12 @@ struct GemmParams {
   const int* grp_off;
   int grp_b_off;
   int grp_c_off;
+
+  // Epilogue output through TMA: each 32x32 chunk leaves the swizzled staging
+  // tile with one bulk tensor store (or an fp32 bulk reduce-add for the
+  // accumulating epilogues) through the C / AUX tensor maps. 0 = per-lane
+  // global stores (always the case for reduce-scatter peer outputs).
+  int tma_epi;
 };
 
 }  // namespace hb

@@ -32,6 +32,10 @@ int* device_status_ptr(int device);
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
                               uint32_t box_inner, uint32_t box_outer);
 
+// Tensor map of any element type with a chosen swizzle.
+CUtensorMap make_tmap(CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle);
+
 // Generic 2-D/3-D tensor map (any 2-byte dtype) with a chosen swizzle.
 CUtensorMap make_tmap_bf16(int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
                            const uint32_t* box, CUtensorMapSwizzle swizzle);

@@ -73,8 +73,8 @@ static EncodeTiledFn get_encode_fn() {
   return fn;
 }
 
-CUtensorMap make_tmap_bf16(int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
-                           const uint32_t* box, CUtensorMapSwizzle swizzle) {
+CUtensorMap make_tmap(CUtensorMapDataType dtype, int rank, const void* base, const uint64_t* dims,
+                      const uint64_t* strides_bytes, const uint32_t* box, CUtensorMapSwizzle swizzle) {
   CUtensorMap m;
   cuuint64_t gdim[5];
   cuuint64_t gstride[4];
@@ -90,13 +90,18 @@ CUtensorMap make_tmap_bf16(int rank, const void* base, const uint64_t* dims, con
     gstride[i] = strides_bytes[i];
   }
   if (reinterpret_cast<uintptr_t>(base) % 16 != 0) throw std::runtime_error("tensor map base must be 16B aligned");
-  CUresult r = get_encode_fn()(&m, CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, const_cast<void*>(base), gdim, gstride,
-                               bdim, estride, CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle,
-                               CU_TENSOR_MAP_L2_PROMOTION_L2_256B, CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
+  CUresult r = get_encode_fn()(&m, dtype, rank, const_cast<void*>(base), gdim, gstride, bdim, estride,
+                               CU_TENSOR_MAP_INTERLEAVE_NONE, swizzle, CU_TENSOR_MAP_L2_PROMOTION_L2_256B,
+                               CU_TENSOR_MAP_FLOAT_OOB_FILL_NONE);
   if (r != CUDA_SUCCESS) {
     throw std::runtime_error("cuTensorMapEncodeTiled failed with code " + std::to_string(static_cast<int>(r)));
   }
   return m;
+}
+
+CUtensorMap make_tmap_bf16(int rank, const void* base, const uint64_t* dims, const uint64_t* strides_bytes,
+                           const uint32_t* box, CUtensorMapSwizzle swizzle) {
+  return make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, rank, base, dims, strides_bytes, box, swizzle);
 }
 
 CUtensorMap make_tmap_2d_bf16(const void* base, uint64_t inner, uint64_t outer, uint64_t row_stride_bytes,
