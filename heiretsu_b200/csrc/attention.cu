@@ -39,9 +39,10 @@ struct AttnParams {
   int B, T, nh, Hs;         // Hs = nh * 64 (this rank's heads)
   __nv_bfloat16* out;       // forward: y [B*T, ld_out]; backward: dqkv [B*T, ld_out]
   long ld_out;
-  float* lse;               // [B, nh, Tpad] log2-domain LSE of the scaled scores
+  float* lse;               // [B, nh, Tpad] NEGATED log2-domain LSE of the scaled scores (-lse, the
+                            // form the backward's fma consumes)
   int Tpad;
-  const float* dvec;        // backward: D = rowsum(dO * O) [B, nh, Tpad]
+  const float* dvec;        // backward: -scale * D, D = rowsum(dO * O) [B, nh, Tpad]
   float* dq_acc;            // backward: fp32 dQ accumulator [B*T, Hs]
   float scale;              // 1/sqrt(64)
   float scale_log2;         // scale * log2(e)
@@ -100,9 +101,10 @@ __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 
 // Online softmax of one 128x128 score tile held in TMEM, for the calling
 // thread's row: updates (m, l), writes P (bf16) to the swizzled smem tile and
 // returns the rescale factor of the previous accumulator. TMEM is read in
-// pairs of 32-column chunks (two loads in flight, one wait); the row max and
-// row sum use four independent chains. The max is taken on raw scores
-// (the scale is positive) and scaled once.
+// pairs of 32-column chunks (two loads in flight, one wait). The row max
+// uses three-input max over independent chains and is taken on raw scores
+// (the scale is positive); exponent arguments and row sums are computed on
+// fp32 pairs (one f32x2 instruction for two columns).
 template <bool DIAG>
 __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
                                               float scale_log2, float& m, float& l) {
@@ -121,13 +123,14 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
         if (key0 + 2 * h * 32 + i > q) x = -INFINITY;
         if (key0 + (2 * h + 1) * 32 + i > q) y = -INFINITY;
       }
-      mx[i & 3] = fmaxf(mx[i & 3], fmaxf(x, y));
+      mx[i & 3] = max3f(mx[i & 3], x, y);
     }
   }
-  const float mt = fmaxf(fmaxf(mx[0], mx[1]), fmaxf(mx[2], mx[3])) * scale_log2;
+  const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * scale_log2;
   const float m_new = fmaxf(m, mt);
   const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
-  float sum[4] = {0.f, 0.f, 0.f, 0.f};
+  const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_new, -m_new);
+  uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
     uint32_t va[32], vb[32];
@@ -142,13 +145,14 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
       uint32_t pk[16];
 #pragma unroll
       for (int i = 0; i < 32; i += 2) {
-        float p0 = fast_exp2(fmaf(__uint_as_float(v[i]), scale_log2, -m_new));
-        float p1 = fast_exp2(fmaf(__uint_as_float(v[i + 1]), scale_log2, -m_new));
+        float t0, t1;
+        f2_unpack(f2_fma(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), t0, t1);
+        float p0 = fast_exp2(t0), p1 = fast_exp2(t1);
         if (DIAG) {
           if (key0 + c * 32 + i > q) p0 = 0.f;
           if (key0 + c * 32 + i + 1 > q) p1 = 0.f;
         }
-        sum[(i >> 1) & 3] += p0 + p1;
+        sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));
         pk[i >> 1] = pack_bf16(p0, p1);
       }
 #pragma unroll
@@ -157,22 +161,27 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
             make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
     }
   }
-  l = l * alpha + ((sum[0] + sum[1]) + (sum[2] + sum[3]));
+  float s0, s1, s2, s3;
+  f2_unpack(sum2[0], s0, s1);
+  f2_unpack(sum2[1], s2, s3);
+  l = l * alpha + ((s0 + s1) + (s2 + s3));
   m = m_new;
   return alpha;
 }
 
-// o = o * alpha + (PV result in TMEM, 64 columns of this thread's row).
-__device__ __forceinline__ void accumulate_o(float (&o)[64], uint32_t tO, float alpha) {
+// o = o * alpha + (PV result in TMEM, 64 columns of this thread's row); o
+// holds column pairs.
+__device__ __forceinline__ void accumulate_o(uint64_t (&o)[32], uint32_t tO, float alpha) {
   uint32_t va[32], vb[32];
   tmem_ld32_issue(tO, va);
   tmem_ld32_issue(tO + 32, vb);
   tmem_wait_ld_regs(va);
   tmem_pin_regs(vb);
+  const uint64_t a2 = f2_pack(alpha, alpha);
 #pragma unroll
-  for (int i = 0; i < 32; ++i) {
-    o[i] = fmaf(o[i], alpha, __uint_as_float(va[i]));
-    o[32 + i] = fmaf(o[32 + i], alpha, __uint_as_float(vb[i]));
+  for (int i = 0; i < 16; ++i) {
+    o[i] = f2_fma(o[i], a2, f2_pack(__uint_as_float(va[2 * i]), __uint_as_float(va[2 * i + 1])));
+    o[16 + i] = f2_fma(o[16 + i], a2, f2_pack(__uint_as_float(vb[2 * i]), __uint_as_float(vb[2 * i + 1])));
   }
 }
 
@@ -327,9 +336,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       const uint32_t tS = tmem + g * 256, tO0 = tmem + g * 256 + 128;
       uint8_t* myP = sP + g * 2 * kTileBytes;
       float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
-      float o[64];
+      uint64_t o[32];  // output row as 32 column pairs
 #pragma unroll
-      for (int i = 0; i < 64; ++i) o[i] = 0.f;
+      for (int i = 0; i < 32; ++i) o[i] = f2_pack(0.f, 0.f);
       bool ok = true;
       for (int j = 0; j < n && ok; ++j) {
         if (!mbar_wait(&bar_s[g], j & 1, p.status, 26)) {
@@ -363,14 +372,19 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         accumulate_o(o, tO0 + ((n - 1) & 1) * 64 + lane_off, alpha_prev);
         if (q < p.T) {
           const float inv = 1.f / l;
+          const uint64_t inv2 = f2_pack(inv, inv);
+          uint32_t w[32];
+#pragma unroll
+          for (int i = 0; i < 32; ++i) {
+            float a0, a1;
+            f2_unpack(f2_mul(o[i], inv2), a0, a1);
+            w[i] = pack_bf16(a0, a1);
+          }
           __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD;
 #pragma unroll
-          for (int gg = 0; gg < 8; ++gg) {
-            *reinterpret_cast<uint4*>(dst + gg * 8) = make_uint4(
-                pack_bf16(o[gg * 8 + 0] * inv, o[gg * 8 + 1] * inv), pack_bf16(o[gg * 8 + 2] * inv, o[gg * 8 + 3] * inv),
-                pack_bf16(o[gg * 8 + 4] * inv, o[gg * 8 + 5] * inv), pack_bf16(o[gg * 8 + 6] * inv, o[gg * 8 + 7] * inv));
-          }
-          p.lse[((long)b * p.nh + h) * p.Tpad + q] = m + log2f(l);
+          for (int gg = 0; gg < 8; ++gg)
+            *reinterpret_cast<uint4*>(dst + gg * 8) = make_uint4(w[4 * gg], w[4 * gg + 1], w[4 * gg + 2], w[4 * gg + 3]);
+          p.lse[((long)b * p.nh + h) * p.Tpad + q] = -(m + log2f(l));
         }
       }
     }
@@ -572,32 +586,32 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tmem_wait_ld_regs(sr);
         tmem_pin_regs(dr);
         uint32_t pp[16], dd[16];
+        const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2), sc2 = f2_pack(p.scale, p.scale);
 #pragma unroll
         for (int i4 = 0; i4 < 8; ++i4) {
+          // staged per query column: -lse (log2 domain) and -scale * D
           const float4 L = lse4[c * 8 + i4];
           const float4 Dv = d4[c * 8 + i4];
-          const float lv[4] = {L.x, L.y, L.z, L.w};
-          const float dv[4] = {Dv.x, Dv.y, Dv.z, Dv.w};
-          float pr[4], ds[4];
 #pragma unroll
-          for (int e = 0; e < 4; ++e) {
+          for (int e = 0; e < 4; e += 2) {
             const int i = i4 * 4 + e;
-            const float pv = fast_exp2(fmaf(__uint_as_float(sr[i]), p.scale_log2, -lv[e]));
-            const float dsv = pv * (__uint_as_float(dr[i]) - dv[e]) * p.scale;
+            const uint64_t nl = e ? f2_pack(L.z, L.w) : f2_pack(L.x, L.y);
+            const uint64_t nd = e ? f2_pack(Dv.z, Dv.w) : f2_pack(Dv.x, Dv.y);
+            float t0, t1;
+            f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])), sl2, nl), t0, t1);
+            float p0 = fast_exp2(t0), p1 = fast_exp2(t1);  // P = 2^(s * scale * log2 e - lse)
+            // dS = P * (dP * scale - D * scale)
+            const uint64_t u = f2_fma(f2_pack(__uint_as_float(dr[i]), __uint_as_float(dr[i + 1])), sc2, nd);
+            float d0, d1;
+            f2_unpack(f2_mul(u, f2_pack(p0, p1)), d0, d1);
             if (masked_tile) {
               const int qq = qi * kTile + g * 64 + c * 32 + i;
-              const bool masked = (diag && key > qq) || qq >= p.T;
-              pr[e] = masked ? 0.f : pv;
-              ds[e] = masked ? 0.f : dsv;
-            } else {
-              pr[e] = pv;
-              ds[e] = dsv;
+              if ((diag && key > qq) || qq >= p.T) p0 = d0 = 0.f;
+              if ((diag && key > qq + 1) || qq + 1 >= p.T) p1 = d1 = 0.f;
             }
+            pp[i >> 1] = pack_bf16(p0, p1);
+            dd[i >> 1] = pack_bf16(d0, d1);
           }
-          pp[2 * i4] = pack_bf16(pr[0], pr[1]);
-          pp[2 * i4 + 1] = pack_bf16(pr[2], pr[3]);
-          dd[2 * i4] = pack_bf16(ds[0], ds[1]);
-          dd[2 * i4 + 1] = pack_bf16(ds[2], ds[3]);
         }
         // The previous tile's MMAs read P^T / dS^T smem and wrote dQ: wait once,
         // flush that dQ half, then overwrite this half of P^T / dS^T.
@@ -652,9 +666,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   if (threadIdx.x == 0) HB_TRACE(2);
 }
 
-// D[b, h, t] = sum_d dO[b*T+t, h*64+d] * O[b*T+t, h*64+d]   (fp32)
+// dvec[b, h, t] = -scale * D,  D = sum_d dO[b*T+t, h*64+d] * O[b*T+t, h*64+d]   (fp32)
 __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long ld_o, const __nv_bfloat16* __restrict__ dO,
-                                     long ld_do, float* __restrict__ dvec, int B, int T, int nh, int Tpad) {
+                                     long ld_do, float* __restrict__ dvec, int B, int T, int nh, int Tpad,
+                                     float scale) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
   if (i >= (long)B * T * nh) return;
   const int h = i % nh;
@@ -671,7 +686,7 @@ __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long l
 #pragma unroll
     for (int q = 0; q < 8; ++q) s += __bfloat162float(xe[q]) * __bfloat162float(ye[q]);
   }
-  dvec[((long)b * nh + h) * Tpad + t] = s;
+  dvec[((long)b * nh + h) * Tpad + t] = -scale * s;
 }
 
 // dqkv[:, h*64 + d] = bf16(dq_acc)
@@ -725,7 +740,7 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   }
   const int Hs = nh * kD;
   const long rows = (long)B * T;
-  attn_bwd_dvec_kernel<<<(rows * nh + 255) / 256, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad);
+  attn_bwd_dvec_kernel<<<(rows * nh + 255) / 256, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, 0.125f);
   HB_CUDA_CHECK(cudaGetLastError());
   HB_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * Hs, s));
   AttnParams p{};

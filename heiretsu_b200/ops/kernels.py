@@ -116,7 +116,11 @@ def f32_to_bf16(x: torch.Tensor, y: Optional[torch.Tensor] = None) -> torch.Tens
 # Attention (head_dim 64, causal)
 # ---------------------------------------------------------------------------
 def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torch.Tensor] = None):
-    """qkv bf16 [B*T, 3*nh*64] -> (y bf16 [B*T, nh*64], lse fp32 [B, nh, Tpad])."""
+    """qkv bf16 [B*T, 3*nh*64] -> (y bf16 [B*T, nh*64], nlse fp32 [B, nh, Tpad]).
+
+    nlse = -log2(sum_k 2^(s_k * log2(e) / 8)) per query row: the negated
+    log2-domain log-sum-exp, kept in the form the backward kernel consumes.
+    Natural-log LSE = -nlse * ln(2)."""
     Tpad = (T + 127) // 128 * 128
     if out is None:
         out = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.bfloat16)
