@@ -26,8 +26,9 @@
 //   row) turns its half into P^T and dS^T = P^T (dP^T - D) * scale in smem,
 //   then dV += P^T dO_i, dK += dS^T Q_i and dQ_i = dS K (the same smem tiles
 //   serve as K-major or MN-major operands); dQ_i is added to an fp32
-//   accumulator with vector atomics. The next tile's first half is computed
-//   while the second half of the current one is still in its softmax.
+//   accumulator by bulk tensor reduce-adds (one 32x32 block per warp).
+//   The next tile's first half is computed while the second half of the
+//   current one is still in its softmax.
 #include <cuda_bf16.h>
 
 #include "common.cuh"
@@ -388,6 +389,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_group0();  // every dQ reduce has landed
+    __syncwarp();
     tc_fence_before();
   }
   __syncthreads();
@@ -404,11 +407,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
 constexpr int BWD_STAGE = 2 * kTileBytes + 2048;  // Q_i, dO_i, lse_i (512 B), D_i (512 B), padded to 1 KB multiple
 constexpr int BWD_STAGES = 2;
 constexpr int BWD_THREADS = 320;
-constexpr int BWD_SMEM = 2 * kTileBytes /*K,V*/ + BWD_STAGES * BWD_STAGE + 4 * kTileBytes /*P^T, dS^T*/ + 1024;
+constexpr int BWD_DQ_STG = 8 * 4096;  // per softmax warp: 32 query rows x 32 fp32 dQ columns, 128B-swizzled
+constexpr int BWD_SMEM = 2 * kTileBytes /*K,V*/ + BWD_STAGES * BWD_STAGE + 4 * kTileBytes /*P^T, dS^T*/ +
+                         BWD_DQ_STG + 1024;
 
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
-                    AttnParams p) {
+                    const __grid_constant__ CUtensorMap tm_dq, AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
   uint8_t* smem = reinterpret_cast<uint8_t*>((reinterpret_cast<uintptr_t>(smem_raw) + 1023) & ~uintptr_t(1023));
   uint8_t* sK = smem;
@@ -416,6 +421,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   uint8_t* sStage = smem + 2 * kTileBytes;
   uint8_t* sP = sStage + BWD_STAGES * BWD_STAGE;
   uint8_t* sDS = sP + 2 * kTileBytes;
+  uint8_t* sDQ = sDS + 2 * kTileBytes;
   __shared__ uint64_t bar_kv, bar_full[BWD_STAGES], bar_empty[BWD_STAGES], bar_h[2], bar_p[2], bar_mma, bar_done;
   __shared__ uint32_t tmem_slot;
 
@@ -547,16 +553,24 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const int key = kt * kTile + r;
     bool ok = true;
+    // dQ rows of this warp (32 queries x 32 columns) leave through one bulk
+    // tensor reduce-add into the fp32 accumulator (the add happens in L2).
+    uint8_t* dq_stg = sDQ + (warp - 2) * 4096;
     auto flush_dq = [&](int qi) {
       tc_fence_after();
-      const int qrow = qi * kTile + r;
       float v[32];
       tmem_ld32(tDQ + g * 32 + lane_off, v);
-      if (qrow < p.T) {
-        float4* dst = reinterpret_cast<float4*>(p.dq_acc + ((long)b * p.T + qrow) * p.Hs + h * kD + g * 32);
+      if (lane == 0) bulk_wait_group_read0();  // the previous reduce has read the staging tile
+      __syncwarp();
 #pragma unroll
-        for (int q4 = 0; q4 < 8; ++q4)
-          atomicAdd(dst + q4, make_float4(v[4 * q4], v[4 * q4 + 1], v[4 * q4 + 2], v[4 * q4 + 3]));
+      for (int j = 0; j < 8; ++j)
+        *reinterpret_cast<float4*>(dq_stg + lane * 128 + ((j ^ (lane & 7)) << 4)) =
+            make_float4(v[4 * j], v[4 * j + 1], v[4 * j + 2], v[4 * j + 3]);
+      fence_proxy_async_smem();
+      __syncwarp();
+      if (lane == 0) {
+        tma_reduce_add_3d(&tm_dq, dq_stg, h * kD + g * 32, qi * kTile + sub * 32, b);
+        bulk_commit_group();
       }
     };
     for (int ii = 0; ii < n_i && ok; ++ii) {
@@ -656,6 +670,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         }
       }
     }
+    if (lane == 0) bulk_wait_group0();  // every dQ reduce has landed
+    __syncwarp();
     tc_fence_before();
   }
   __syncthreads();
@@ -752,8 +768,14 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   p.trace = g_attn_trace;
   const CUtensorMap tq = qkv_map(qkv, B, T, ld_qkv, 3 * Hs);
   const CUtensorMap td = qkv_map(dO, B, T, ld_do, Hs);
+  // dQ accumulator as {Hs, T, B} fp32: 32x32 reduce boxes never cross into the next sequence.
+  const uint64_t qdims[3] = {static_cast<uint64_t>(Hs), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
+  const uint64_t qstr[2] = {static_cast<uint64_t>(Hs) * 4, static_cast<uint64_t>(Hs) * 4 * T};
+  const uint32_t qbox[3] = {32, 32, 1};
+  const CUtensorMap tdq =
+      make_tmap(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
   const int n_t = (T + kTile - 1) / kTile;
-  attn_bwd_kernel<<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, p);
+  attn_bwd_kernel<<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
   HB_CUDA_CHECK(cudaGetLastError());
   attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
   HB_CUDA_CHECK(cudaGetLastError());
