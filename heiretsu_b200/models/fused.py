@@ -44,8 +44,6 @@ def fused_supported(cfg, topo=None) -> Tuple[bool, str]:
         return False, "fused path runs without dropout (dropout > 0 uses the plain path)"
     if cfg.num_experts > 0 and topo is not None and getattr(topo, "ep", 1) > 8:
         return False, "fused expert parallelism exchanges partials over NVLink within one node (ep <= 8)"
-    if topo is not None and getattr(topo, "tp", 1) > 1 and getattr(topo, "pp", 1) > 1:
-        return False, "tensor x pipeline parallelism uses the plain path"
     return True, ""
 
 

@@ -79,6 +79,17 @@ class StageModule(nn.Module):
             self.wte.weight = self.lm_head.weight
         init_gpt_weights(self, cfg.n_layer)
         self.fused = False
+        self.topo = topo
+
+    # Fused tensor parallelism keeps the residual stream token-sharded: each
+    # TP rank holds B/tp whole sequences, and the stage boundary is that shard
+    # (sent to the same TP rank of the next stage, 1/tp of the dense bytes).
+    def _tp_fused(self, t: torch.Tensor) -> bool:
+        return self.fused and self.tp > 1 and t.is_cuda
+
+    def boundary_batch(self, B: int) -> int:
+        """Sequences per boundary tensor on this rank for a micro-batch of B."""
+        return B // self.tp if self.fused and self.tp > 1 else B
 
     def embed(self, idx: torch.Tensor) -> torch.Tensor:
         B, T = idx.shape
@@ -86,10 +97,24 @@ class StageModule(nn.Module):
             raise ValueError(f"Sequence length {T} > block_size {self.cfg.block_size}")
         if self.fused and idx.is_cuda:
             from ..models.fused import embed_fused
+            if self._tp_fused(idx):
+                from ..models.fused_tp import tp_shard_rows
+                r0, Ms = tp_shard_rows(self.topo, B, T)
+                idx = idx.reshape(-1)[r0:r0 + Ms].view(Ms // T, T)
             return embed_fused(self.wte.weight, self.wpe.weight, idx)
         return self.wte(idx) + self.wpe(torch.arange(T, device=idx.device))[None]
 
     def forward_blocks(self, x: torch.Tensor) -> Tuple[torch.Tensor, torch.Tensor]:
+        if self._tp_fused(x):
+            from ..models.fused_tp import blocks_fused_tp, tp_supported
+            Bs, T, H = x.shape
+            ok, why = tp_supported(self.cfg, self.topo, Bs * self.tp, T)
+            if not ok:
+                raise ValueError(f"fused tensor parallelism: {why}")
+            xs = x.reshape(Bs * T, H)
+            xs = xs if xs.dtype == torch.float32 else xs.float()
+            out, aux = blocks_fused_tp(self.blocks, xs, self.cfg, self.topo, Bs * self.tp, T)
+            return out.view(Bs, T, H), aux / self.tp  # shard aux losses / tp sum to the mean
         if self.fused and x.is_cuda:
             from ..models.fused import blocks_fused
             return blocks_fused(self.blocks, x, self.cfg)
@@ -102,6 +127,14 @@ class StageModule(nn.Module):
     def forward_head(self, x: torch.Tensor, targets: Optional[torch.Tensor]):
         if self.fused and x.is_cuda:
             from ..models.fused import head_fused
+            if self._tp_fused(x):
+                # this shard's mean loss / tp: the sum over the TP group is the dense mean
+                Bs, T, _ = x.shape
+                from ..models.fused_tp import tp_shard_rows
+                r0, Ms = tp_shard_rows(self.topo, Bs * self.tp, T)
+                tgt = targets.reshape(-1)[r0:r0 + Ms].view(Bs, T) if targets is not None else None
+                _, loss = head_fused(self.ln_f, self.lm_head.weight, x, tgt, self.cfg.vocab_size, want_logits=False)
+                return None, (loss / self.tp if loss is not None else None)
             return head_fused(self.ln_f, self.lm_head.weight, x, targets, self.cfg.vocab_size)
         x = self.ln_f(x)
         logits = self.lm_head(x)
@@ -161,7 +194,7 @@ class GPipeEngine:
     # -- schedule -------------------------------------------------------------
     def _run_forward(self, loader, micro_batches, device, use_amp, amp_dtype, batch_size, state, keep_graph):
         cfg = self.stage.cfg
-        B, S, H = batch_size, cfg.block_size, cfg.n_embed
+        B, S, H = self.stage.boundary_batch(batch_size), cfg.block_size, cfg.n_embed
         pending_recv = self._recv_fwd(0, B, S, H, device) if not self.is_first else None
         sends = []
         for m in range(micro_batches):

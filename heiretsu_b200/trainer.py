@@ -329,6 +329,8 @@ class Engine:
                                                           use_amp=self.use_amp, amp_dtype=self.amp_dtype,
                                                           scaler=self.scaler, batch_size=args.batch_size,
                                                           aux_loss_coef=args.aux_loss_coef)
+            if self.fused and topo.tp > 1 and loss_scalar is not None and dist.is_initialized():
+                dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.tp_group)  # shard losses / tp
         else:
             aux = torch.zeros((), device=self.device)
             loss_sum = torch.zeros((), device=self.device)
@@ -409,6 +411,8 @@ class Engine:
             if self.use_pipeline:
                 l = self.pipe.forward_only(loader, self.args.grad_accum_steps, self.device, self.use_amp,
                                            self.amp_dtype, loader.B)
+                if l is not None and self.fused and self.topo.tp > 1 and dist.is_initialized():
+                    dist.all_reduce(l, group=self.topo.tp_group)  # shard losses / tp sum to the mean
                 if l is not None and self.topo.dp_group is not None and dist.is_initialized():
                     dist.all_reduce(l, group=self.topo.dp_group)
                     l = l / self.topo.dp
