@@ -56,6 +56,8 @@ def parse():
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true", help="skip the profiler-based kernel count")
+    ap.add_argument("--overlap-dp", type=int, default=0, choices=[0, 1],
+                    help="reduce DP gradients block by block during the last backward (ours)")
     return ap.parse_args()
 
 
@@ -186,7 +188,7 @@ def run_ours(args, world, rank, dev):
         "--batch_size", str(MICRO_BATCH), "--block_size", str(SEQ), "--grad_accum_steps", str(ACCUM),
         "--n_layer", "12", "--n_head", "12", "--n_embed", "768", "--dropout", "0", "--amp", "bf16",
         "--learning_rate", "3e-4", "--weight_decay", "0.1", "--grad_clip", "1.0", "--dp", str(world),
-        "--engine", "fused"])
+        "--engine", "fused", "--overlap_dp", str(args.overlap_dp)])
     topo = init_topology(dp=world)
     torch.manual_seed(1337)
     cfg = GPTConfig(**MODEL, dropout=0.0)

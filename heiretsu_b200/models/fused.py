@@ -129,6 +129,16 @@ def _ln_scratch(M: int, H: int, device) -> torch.Tensor:
     return torch.empty(rows * 2 * H, device=device, dtype=torch.float32)
 
 
+# Called after each block's backward has been issued (data-parallel gradient
+# reduction overlapped with the rest of backward); None when not armed.
+_BLOCK_DONE_HOOK = None
+
+
+def set_block_done_hook(fn) -> None:
+    global _BLOCK_DONE_HOOK
+    _BLOCK_DONE_HOOK = fn
+
+
 def _is_moe(blk) -> bool:
     return hasattr(blk, "moe")
 
@@ -169,6 +179,8 @@ class _Body(torch.autograd.Function):
             else:
                 _mlp_bwd(blk, sm, dres, dres16, ws)
             _attn_bwd(blk, sa, dres, dres16, B, T, ws)
+            if _BLOCK_DONE_HOOK is not None:
+                _BLOCK_DONE_HOOK(blk)
         ctx.saved = None
         return dres, None, None, None
 

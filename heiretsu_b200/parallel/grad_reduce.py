@@ -8,6 +8,18 @@ group in a few large contiguous buckets. Backends:
 * ``p2p``: the fused sm_100a kernel of heiretsu_b200/csrc/comm.cu, which reads
   the peers' buckets over NVLink, sums them with the 1/dp scale applied in the
   same pass and writes the result back to every peer (no staging copies).
+
+Overlap with backward (p2p): ``arm()`` before the last micro-batch's
+backward installs a per-block hook in the fused backward. When a block's
+backward has been issued, its parameters' gradient ranges are final, so an
+event is recorded and a side stream reduces those ranges while the main
+stream continues with the next block. The side-stream kernel runs at 2 warps
+per CTA, small enough to sit beside the persistent GEMM / attention CTAs.
+``finish()`` reduces whatever was not covered (embeddings, final norm) and
+joins the side stream. Every rank issues the same reductions in the same
+order, which the kernels' epoch-tagged barriers require. All of it is
+capturable in a CUDA graph (the side stream forks from and joins the
+capture stream through events).
 """
 from __future__ import annotations
 
@@ -39,6 +51,82 @@ class FlatGradReducer:
         self.symm = getattr(flat, "grad_symm", None)
         if self.backend == "p2p" and self.symm is None:
             self.backend = "nccl"
+        self._side = None
+        self._armed = False
+        self._done: List[Tuple[int, int]] = []
+        self._range_cache = {}
+
+    # -- overlap with backward ----------------------------------------------
+    def can_overlap(self) -> bool:
+        return self.world > 1 and self.backend == "p2p" and self.flat.device.type == "cuda"
+
+    def _ranges_of(self, module) -> List[Tuple[int, int]]:
+        """Contiguous flat-buffer ranges [start, end) holding module's parameter gradients."""
+        key = id(module)
+        if key not in self._range_cache:
+            index = {id(p): i for i, p in enumerate(self.flat.params)}
+            spans = []
+            for p in module.parameters():
+                i = index.get(id(p))
+                if i is not None:
+                    off = self.flat.offsets[i]
+                    spans.append((off, off + (p.numel() + 127) // 128 * 128))
+            spans.sort()
+            merged: List[Tuple[int, int]] = []
+            for a, b in spans:
+                if merged and merged[-1][1] == a:
+                    merged[-1] = (merged[-1][0], b)
+                else:
+                    merged.append((a, b))
+            self._range_cache[key] = merged
+        return self._range_cache[key]
+
+    def arm(self) -> None:
+        """Reduce each block's gradients during the coming backward pass."""
+        if not self.can_overlap():
+            return
+        from ..models import fused as F
+        if self._side is None:
+            self._side = torch.cuda.Stream(device=self.flat.device)
+        self._done = []
+        self._armed = True
+        F.set_block_done_hook(self._on_block_done)
+
+    def _on_block_done(self, blk) -> None:
+        ranges = self._ranges_of(blk)
+        if not ranges:
+            return
+        ev = torch.cuda.Event()
+        ev.record()
+        self._side.wait_event(ev)
+        with torch.cuda.stream(self._side):
+            for a, b in ranges:
+                self.symm.sum_range(a, b - a, 1.0 / self.world, threads=64)
+        self._done.extend(ranges)
+
+    def finish(self) -> None:
+        """After backward: reduce what the overlap did not cover and join the side stream."""
+        if not self._armed:
+            self.reduce()
+            return
+        from ..models import fused as F
+        F.set_block_done_hook(None)
+        self._armed = False
+        done = sorted(self._done)
+        rest, pos = [], 0
+        for a, b in done:
+            if a > pos:
+                rest.append((pos, a))
+            pos = max(pos, b)
+        if pos < self.flat.numel:
+            rest.append((pos, self.flat.numel))
+        ev = torch.cuda.Event()
+        ev.record()
+        self._side.wait_event(ev)
+        with torch.cuda.stream(self._side):
+            for a, b in rest:
+                self.symm.sum_range(a, b - a, 1.0 / self.world)
+        torch.cuda.current_stream().wait_stream(self._side)
 
     def reduce(self) -> None:
         if self.world == 1:

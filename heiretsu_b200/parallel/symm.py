@@ -65,12 +65,15 @@ class SymmetricBuffer:
         """Device-side barrier of the group (bounded wait), ordered on the current stream."""
         load().group_barrier(self.ptrs, self.signal_ptrs, self.rank, self.counter)
 
-    def sum_range(self, start_elem: int, n_elem: int, scale: float = 1.0) -> None:
-        """In place over the group: fp32 elements [start, start+n) <- scale * sum over ranks (NVLink, one kernel)."""
+    def sum_range(self, start_elem: int, n_elem: int, scale: float = 1.0, threads: int = 512) -> None:
+        """In place over the group: fp32 elements [start, start+n) <- scale * sum over ranks (NVLink, one kernel).
+
+        ``threads`` = 64 gives a footprint small enough to run beside compute kernels."""
         if self.world == 1 or n_elem == 0:
             return
         off = start_elem * 4
-        load().dp_allreduce([p + off for p in self.ptrs], self.signal_ptrs, self.rank, n_elem, scale, self.counter)
+        load().dp_allreduce([p + off for p in self.ptrs], self.signal_ptrs, self.rank, n_elem, scale, self.counter,
+                            threads)
 
 
 def check_comm_status(device: int) -> None:

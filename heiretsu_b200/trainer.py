@@ -110,6 +110,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--watchdog_s", type=float, default=300.0,
                    help="multi-process runs: abort when a peer announces a failure or makes no progress "
                         "for this many seconds (0 = off)")
+    p.add_argument("--overlap_dp", type=int, default=0, choices=[0, 1],
+                   help="reduce data-parallel gradients block by block during the last backward (fused path); "
+                        "off by default: on GPT-2 small the co-running reduction slowed backward more than it hid")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
     return p
@@ -239,6 +242,9 @@ class Engine:
         if topo.dp > 1 and self.fused:
             from .parallel.grad_reduce import FlatGradReducer
             self.reducer = FlatGradReducer(self.flat, topo.dp_group, topo)
+        # DP reduction overlapped with the last micro-batch's backward (fused, non-TP blocks).
+        self.overlap_dp = (self.reducer is not None and self.reducer.can_overlap() and topo.tp == 1
+                           and not self.use_pipeline and bool(getattr(args, "overlap_dp", 0)))
         if self.use_pipeline:
             bd = torch.float32 if args.pp_boundary_dtype == "fp32" else torch.bfloat16
             self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd)
@@ -300,15 +306,17 @@ class Engine:
         accum = self.args.grad_accum_steps
         aux = torch.zeros((), device=self.device)
         loss_sum = torch.zeros((), device=self.device)
-        for _ in range(accum):
+        for i in range(accum):
             x, y = loader.next_batch(self.device)
             _, loss, aux_mb = self.forward_module(x, y, return_logits=False)
+            if i == accum - 1 and self.reducer is not None and self.overlap_dp:
+                self.reducer.arm()  # reduce each block's gradients while backward continues
             ((loss + aux_mb) / accum).backward()
             aux = aux + aux_mb.detach().float()
             loss_sum = loss_sum + loss.detach().float()
-        self.tp_sync_grads()
         if self.reducer is not None:
-            self.reducer.reduce()
+            self.reducer.finish()
+        self.tp_sync_grads()
         self.optimizer.step_device()
         self.optimizer.zero_grad()
         return loss_sum / accum, aux
