@@ -54,6 +54,9 @@ __device__ __forceinline__ bool group_barrier(const PeerTable& pt, int rank, int
           break;
         }
       }
+      // A peer is at most one call ahead (same call sequence on every rank);
+      // further ahead means the ranks issued different collectives.
+      if (ok_sh && !HB_DCHECK(static_cast<int32_t>(ld_acquire_sys(slot) - val) < 8, status, 200 + p)) ok_sh = 0;
     }
   }
   __syncthreads();

@@ -36,6 +36,16 @@ __device__ __forceinline__ void record_error(int* status, int code, int where) {
   }
 }
 
+// Debug-build invariant checks (compile with -DHB_DEBUG): evaluate to the
+// condition; a violated check records kBadArg with its site in the status
+// word, and the caller skips the access. Release builds compile them out.
+#ifdef HB_DEBUG
+#define HB_DCHECK(cond, status, site) \
+  ((cond) ? true : (::hb::record_error((status), ::hb::kBadArg, (site)), false))
+#else
+#define HB_DCHECK(cond, status, site) true
+#endif
+
 __device__ __forceinline__ uint64_t globaltimer_ns() {
   uint64_t t;
   asm volatile("mov.u64 %0, %%globaltimer;" : "=l"(t));

@@ -129,19 +129,22 @@ __global__ void __launch_bounds__(1024) moe_positions_kernel(const int* __restri
 
 // Gather rows into the permuted matrix: one warp per slot.
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ pos, int NK, int K,
-                                  int H, __nv_bfloat16* __restrict__ xp, const int* __restrict__ off, int e0, int e1) {
+                                  int H, __nv_bfloat16* __restrict__ xp, const int* __restrict__ off, int e0, int e1,
+                                  int cap, int* status) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= NK) return;
   const int lo = off[e0], r = pos[i];
   if (r < lo || r >= off[e1]) return;  // routed to an expert outside this rank's window
+  if (!HB_DCHECK(r - lo < cap, status, 300)) return;
   const uint4* src = reinterpret_cast<const uint4*>(x + (long)(i / K) * H);
   uint4* dst = reinterpret_cast<uint4*>(xp + (long)(r - lo) * H);
   for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
 }
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const int* __restrict__ pos,
                                    const float* __restrict__ topw, const float* __restrict__ resid, int N, int K,
-                                   int H, float* __restrict__ out, const int* __restrict__ off, int e0, int e1) {
+                                   int H, float* __restrict__ out, const int* __restrict__ off, int e0, int e1,
+                                   int cap, int* status) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= N) return;
@@ -151,6 +154,7 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const i
     for (int k = 0; k < K; ++k) {
       const int r = pos[t * K + k];
       if (r < lo || r >= hi) continue;
+      if (!HB_DCHECK(r - lo < cap, status, 301)) continue;
       const float wk = topw[(long)t * K + k];
       const uint2 raw = *reinterpret_cast<const uint2*>(yp + (long)(r - lo) * H + j);
       const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
@@ -166,15 +170,15 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const i
 __global__ void moe_combine_bwd_kernel(const float* __restrict__ dy, const __nv_bfloat16* __restrict__ yp,
                                        const int* __restrict__ pos, const float* __restrict__ topw, int N, int K,
                                        int H, __nv_bfloat16* __restrict__ dyp, float* __restrict__ dw,
-                                       const int* __restrict__ off, int e0, int e1) {
+                                       const int* __restrict__ off, int e0, int e1, int cap, int* status) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= N) return;
   const int lo = off[e0], hi = off[e1];
   for (int k = 0; k < K; ++k) {
     const int r = pos[t * K + k];
-    if (r < lo || r >= hi) {  // another rank's expert: its weight gradient comes from that rank
-      if (lane == 0) dw[(long)t * K + k] = 0.f;
+    if (r < lo || r >= hi || !HB_DCHECK(r - lo < cap, status, 302)) {  // another rank's expert:
+      if (lane == 0) dw[(long)t * K + k] = 0.f;                           // its gradient comes from there
       continue;
     }
     const float wk = topw[(long)t * K + k];
@@ -195,7 +199,8 @@ __global__ void moe_combine_bwd_kernel(const float* __restrict__ dy, const __nv_
   }
 }
 __global__ void moe_unpermute_kernel(const float* __restrict__ dxp, const int* __restrict__ pos, int N, int K, int H,
-                                     float* __restrict__ dx, const int* __restrict__ off, int e0, int e1) {
+                                     float* __restrict__ dx, const int* __restrict__ off, int e0, int e1, int cap,
+                                     int* status) {
   const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (t >= N) return;
@@ -204,7 +209,7 @@ __global__ void moe_unpermute_kernel(const float* __restrict__ dxp, const int* _
     float4 acc = make_float4(0.f, 0.f, 0.f, 0.f);
     for (int k = 0; k < K; ++k) {
       const int r = pos[t * K + k];
-      if (r < lo || r >= hi) continue;
+      if (r < lo || r >= hi || !HB_DCHECK(r - lo < cap, status, 303)) continue;
       const float4 v = *reinterpret_cast<const float4*>(dxp + (long)(r - lo) * H + j);
       acc.x += v.x;
       acc.y += v.y;
@@ -275,27 +280,29 @@ void moe_route_launch(const __nv_bfloat16* x, const float* wg, int N, int H, int
 }
 
 void moe_gather_launch(const __nv_bfloat16* x, const int* pos, int N, int K, int H, __nv_bfloat16* xp,
-                       const int* off, int e0, int e1, cudaStream_t s) {
-  moe_gather_kernel<<<(N * K * 32 + 255) / 256, 256, 0, s>>>(x, pos, N * K, K, H, xp, off, e0, e1);
+                       const int* off, int e0, int e1, int cap, int* status, cudaStream_t s) {
+  moe_gather_kernel<<<(N * K * 32 + 255) / 256, 256, 0, s>>>(x, pos, N * K, K, H, xp, off, e0, e1, cap, status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void moe_combine_launch(const __nv_bfloat16* yp, const int* pos, const float* topw, const float* resid, int N, int K,
-                        int H, float* out, const int* off, int e0, int e1, cudaStream_t s) {
-  moe_combine_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(yp, pos, topw, resid, N, K, H, out, off, e0, e1);
+                        int H, float* out, const int* off, int e0, int e1, int cap, int* status, cudaStream_t s) {
+  moe_combine_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(yp, pos, topw, resid, N, K, H, out, off, e0, e1, cap,
+                                                          status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void moe_combine_bwd_launch(const float* dy, const __nv_bfloat16* yp, const int* pos, const float* topw, int N,
-                            int K, int H, __nv_bfloat16* dyp, float* dw, const int* off, int e0, int e1,
-                            cudaStream_t s) {
-  moe_combine_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dy, yp, pos, topw, N, K, H, dyp, dw, off, e0, e1);
+                            int K, int H, __nv_bfloat16* dyp, float* dw, const int* off, int e0, int e1, int cap,
+                            int* status, cudaStream_t s) {
+  moe_combine_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dy, yp, pos, topw, N, K, H, dyp, dw, off, e0, e1, cap,
+                                                              status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void moe_unpermute_launch(const float* dxp, const int* pos, int N, int K, int H, float* dx, const int* off, int e0,
-                          int e1, cudaStream_t s) {
-  moe_unpermute_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dxp, pos, N, K, H, dx, off, e0, e1);
+                          int e1, int cap, int* status, cudaStream_t s) {
+  moe_unpermute_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dxp, pos, N, K, H, dx, off, e0, e1, cap, status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

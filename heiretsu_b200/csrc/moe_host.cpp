@@ -11,13 +11,14 @@ namespace hb {
 
 void moe_route_launch(const __nv_bfloat16*, const float*, int, int, int, int, float, float*, int*, float*, int*, float*,
                       int*, float*, int*, cudaStream_t);
-void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, const int*, int, int,
-                       cudaStream_t);
+void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, const int*, int, int, int,
+                       int*, cudaStream_t);
 void moe_combine_launch(const __nv_bfloat16*, const int*, const float*, const float*, int, int, int, float*,
-                        const int*, int, int, cudaStream_t);
+                        const int*, int, int, int, int*, cudaStream_t);
 void moe_combine_bwd_launch(const float*, const __nv_bfloat16*, const int*, const float*, int, int, int,
-                            __nv_bfloat16*, float*, const int*, int, int, cudaStream_t);
-void moe_unpermute_launch(const float*, const int*, int, int, int, float*, const int*, int, int, cudaStream_t);
+                            __nv_bfloat16*, float*, const int*, int, int, int, int*, cudaStream_t);
+void moe_unpermute_launch(const float*, const int*, int, int, int, float*, const int*, int, int, int, int*,
+                          cudaStream_t);
 void moe_local_offsets_launch(const int*, int, int, int*, cudaStream_t);
 void moe_router_bwd_launch(const float*, const int*, const float*, const float*, const float*, const int*, float, int,
                            int, int, int, const float*, __nv_bfloat16*, long, float*, cudaStream_t);
@@ -70,7 +71,7 @@ void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tenso
   check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(x.device());
   moe_gather_launch(P<__nv_bfloat16>(x), P<int>(pos), x.size(0), K, x.size(1), P<__nv_bfloat16>(xp), P<int>(off),
-                    e0, e1, S());
+                    e0, e1, xp.size(0), device_status_ptr(x.get_device()), S());
 }
 
 void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
@@ -87,7 +88,7 @@ void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& 
   c10::cuda::CUDAGuard g(yp.device());
   const int N = out.size(0), H = out.size(1), K = topw.size(1);
   moe_combine_launch(P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), r, N, K, H, P<float>(out), P<int>(off), e0,
-                     e1, S());
+                     e1, yp.size(0), device_status_ptr(yp.get_device()), S());
 }
 
 void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
@@ -97,7 +98,8 @@ void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tenso
   c10::cuda::CUDAGuard g(dy.device());
   const int N = dy.size(0), H = dy.size(1), K = topw.size(1);
   moe_combine_bwd_launch(P<float>(dy), P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), N, K, H,
-                         P<__nv_bfloat16>(dyp), P<float>(dw), P<int>(off), e0, e1, S());
+                         P<__nv_bfloat16>(dyp), P<float>(dw), P<int>(off), e0, e1, yp.size(0),
+                         device_status_ptr(dy.get_device()), S());
 }
 
 void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx, const at::Tensor& off,
@@ -107,7 +109,7 @@ void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::
   check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(dx.device());
   moe_unpermute_launch(P<float>(dxp), P<int>(pos), dx.size(0), K, dx.size(1), P<float>(dx), P<int>(off), e0, e1,
-                       S());
+                       dxp.size(0), device_status_ptr(dx.get_device()), S());
 }
 
 void moe_local_offsets(const at::Tensor& off, int64_t e0, int64_t n, at::Tensor& out) {

@@ -29,6 +29,7 @@ from typing import List, Optional, Tuple
 import torch
 
 from ..ops import gemm as G
+from ..utils.profiling import nvtx
 from ..ops import kernels as K
 
 LN_EPS = 1e-5
@@ -151,13 +152,15 @@ class _Body(torch.autograd.Function):
         keep = x.requires_grad
         saved: List = []
         aux_total = torch.zeros((), device=x.device, dtype=torch.float32)
-        for blk in blocks:
-            x, sa = _attn_fwd(blk, x, B, T, keep)
-            if _is_moe(blk):
-                x, aux, sm = moe_sublayer_fwd(blk, None, x, keep)
-                aux_total = aux_total + aux
-            else:
-                x, sm = _mlp_fwd(blk, x, keep)
+        for i, blk in enumerate(blocks):
+            with nvtx(f"block{i}.attn.fwd"):
+                x, sa = _attn_fwd(blk, x, B, T, keep)
+            with nvtx(f"block{i}.mlp.fwd"):
+                if _is_moe(blk):
+                    x, aux, sm = moe_sublayer_fwd(blk, None, x, keep)
+                    aux_total = aux_total + aux
+                else:
+                    x, sm = _mlp_fwd(blk, x, keep)
             saved.append((sa, sm))
         ctx.blocks, ctx.saved, ctx.B, ctx.T = blocks, saved, B, T
         return x, aux_total
@@ -173,12 +176,15 @@ class _Body(torch.autograd.Function):
         ws = {"ln_scratch": _ln_scratch(M, H, dres.device)}
         if daux is None:
             daux = torch.zeros((), device=dres.device)
-        for blk, (sa, sm) in zip(reversed(ctx.blocks), reversed(ctx.saved)):
-            if _is_moe(blk):
-                moe_sublayer_bwd(blk, None, sm, dres, dres16, daux, ws["ln_scratch"])
-            else:
-                _mlp_bwd(blk, sm, dres, dres16, ws)
-            _attn_bwd(blk, sa, dres, dres16, B, T, ws)
+        n = len(ctx.blocks)
+        for j, (blk, (sa, sm)) in enumerate(zip(reversed(ctx.blocks), reversed(ctx.saved))):
+            with nvtx(f"block{n - 1 - j}.mlp.bwd"):
+                if _is_moe(blk):
+                    moe_sublayer_bwd(blk, None, sm, dres, dres16, daux, ws["ln_scratch"])
+                else:
+                    _mlp_bwd(blk, sm, dres, dres16, ws)
+            with nvtx(f"block{n - 1 - j}.attn.bwd"):
+                _attn_bwd(blk, sa, dres, dres16, B, T, ws)
             if _BLOCK_DONE_HOOK is not None:
                 _BLOCK_DONE_HOOK(blk)
         ctx.saved = None

@@ -110,6 +110,8 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--watchdog_s", type=float, default=300.0,
                    help="multi-process runs: abort when a peer announces a failure or makes no progress "
                         "for this many seconds (0 = off)")
+    p.add_argument("--device_timing", type=int, default=1, choices=[0, 1],
+                   help="time each step with CUDA events and log device tokens/s (max over ranks)")
     p.add_argument("--overlap_dp", type=int, default=0, choices=[0, 1],
                    help="reduce data-parallel gradients block by block during the last backward (fused path); "
                         "off by default: on GPT-2 small the co-running reduction slowed backward more than it hid")
@@ -544,24 +546,38 @@ def main(argv=None) -> None:
 
 
 def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0) -> None:
+    from .utils.profiling import RegionTimer
+
     is_main = topo.is_main
     tokens_per_step = args.batch_size * args.block_size * args.grad_accum_steps
     last = time.time()
     log_every = args.log_interval or max(1, args.eval_interval // 10)
+    timer = RegionTimer(enabled=bool(args.device_timing) and engine.device.type == "cuda")
+    timed_steps = 0
     for step in range(1, args.max_iters + 1):
         if wd is not None:
             wd.check()  # a failed peer is noticed here, before this step launches anything
-        loss_scalar, aux = engine.train_step(train_loader)
+        with timer.region("step"):
+            loss_scalar, aux = engine.train_step(train_loader)
+        timed_steps += 1
         if wd is not None:
             wd.beat(step)
         now = time.time()
         dt = now - last
         last = now
         eff = tokens_per_step / dt if dt > 0 else float("inf")
-        if is_main and (step % log_every == 0 or step == 1):
-            aux_str = f" | aux_loss {aux.item():.4f}" if args.num_experts > 0 else ""
-            ls = f"{loss_scalar.item():.4f}" if loss_scalar is not None else "n/a"
-            print(f"step {step:6d} | train_loss (mean micro) {ls}{aux_str} | eff_tok/s {eff:,.0f}")
+        if step % log_every == 0 or step == 1:
+            dev_str = ""
+            if timer.enabled:
+                # every rank takes part in the max over ranks; all log on the same steps
+                step_ms = timer.summary().get("step", 0.0) / max(1, timed_steps)
+                timed_steps = 0
+                if step_ms > 0:
+                    dev_str = f" | dev_tok/s {topo.dp * tokens_per_step / (step_ms / 1e3):,.0f} ({step_ms:.2f} ms)"
+            if is_main:
+                aux_str = f" | aux_loss {aux.item():.4f}" if args.num_experts > 0 else ""
+                ls = f"{loss_scalar.item():.4f}" if loss_scalar is not None else "n/a"
+                print(f"step {step:6d} | train_loss (mean micro) {ls}{aux_str} | eff_tok/s {eff:,.0f}{dev_str}")
         if is_main and run:
             log = {"train/loss_mean_micro": float(loss_scalar.item()) if loss_scalar is not None else float("nan"),
                    "opt/lr": float(engine.optimizer.param_groups[0]["lr"]), "speed/eff_tokens_per_sec": eff,

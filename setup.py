@@ -1,6 +1,7 @@
 """Build the heiretsu_b200 native extension in-tree for B200 (sm_100a).
 
     python setup.py build_ext --inplace
+    HB_DEBUG=1 python setup.py build_ext --inplace     # with device-side invariant checks
 
 produces heiretsu_b200/_C*.so next to the Python sources. Kernel files
 (*.cu) are torch-free and compile in parallel; *.cpp files hold the
@@ -24,6 +25,10 @@ NVCC_FLAGS = [
     "-U__CUDA_NO_BFLOAT16_CONVERSIONS__", "-U__CUDA_NO_HALF2_OPERATORS__",
 ]
 CXX_FLAGS = ["-O2", "-std=c++17"]
+if os.environ.get("HB_DEBUG", "0") == "1":
+    # Kernels check invariants the host cannot see (MoE row positions within
+    # the staging capacity, barrier epochs) and record failures in the status word.
+    NVCC_FLAGS.append("-DHB_DEBUG")
 
 
 def sources():

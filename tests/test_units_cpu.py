@@ -146,3 +146,56 @@ def test_cpu_trainer_runs_and_loss_drops(tmp_path):
           "--block_size", "32", "--batch_size", "4", "--max_iters", "3", "--eval_interval", "3", "--eval_iters", "1",
           "--dropout", "0", "--save_interval", "3", "--out_dir", str(tmp_path)])
     assert (tmp_path / "ckpt_0000003.pt").exists()
+
+
+def test_region_timer_and_nvtx_cpu():
+    import time
+
+    from heiretsu_b200.utils.profiling import RegionTimer, nvtx, tokens_per_second
+
+    t = RegionTimer()
+    for _ in range(3):
+        with t.region("a"), nvtx("a"):
+            time.sleep(0.002)
+    with t.region("b"):
+        pass
+    s = t.summary()
+    assert set(s) == {"a", "b"} and s["a"] >= 5.0 and s["b"] >= 0.0
+    assert t.summary() == {}  # reset after a summary
+    assert abs(tokens_per_second(1000, 500.0) - 2000.0) < 1e-9
+    assert RegionTimer(enabled=False).summary() == {}
+
+
+def _timer_max_worker(rank, world):
+    from heiretsu_b200.utils.profiling import RegionTimer
+
+    t = RegionTimer()
+    t._add("step", 10.0 * (rank + 1))
+    return t.summary()["step"]
+
+
+def test_region_timer_max_over_ranks():
+    from dist_util import run_ranks
+
+    assert run_ranks(_timer_max_worker, 2) == [20.0, 20.0]
+
+
+def test_roofline_fractions(tmp_path):
+    import json
+
+    from heiretsu_b200.utils.roofline import fractions, fused_target_ms, load_peaks, render
+
+    fb = load_peaks(str(tmp_path / "absent.json"))
+    assert fb.label == "of fallback" and fb.hbm_gbs == 6650.0
+    p = tmp_path / "peaks.json"
+    p.write_text(json.dumps({"hbm_gbs": 7000.0, "bf16_tflops": {"value": 1600.0}, "bf16_tflops_sustained": 1450.0}))
+    pk = load_peaks(str(p))
+    assert pk.label == "of measured" and pk.bf16_tflops == 1600.0 and pk.hbm_gbs == 7000.0
+    rows = fractions([{"op": "gemm", "name": "x", "ms": 1.0, "tflops": 800.0, "ref_tflops": 1200.0},
+                      {"op": "layernorm", "name": "bwd", "ms": 0.05, "gbs": 3500.0}], pk)
+    assert abs(rows[0]["frac"] - 0.5) < 1e-12 and abs(rows[0]["ref_frac"] - 0.75) < 1e-12
+    assert abs(rows[1]["frac"] - 0.5) < 1e-12
+    assert "of measured" in render(rows)
+    # 1 TFLOP at 1.6 PFLOP/s = 0.625 ms < 770 MB at 770 GB/s = 1 ms: the link bounds it
+    assert abs(fused_target_ms(1e12, 770e6, pk) - 1.0) < 1e-9
+    assert abs(fused_target_ms(3.2e12, 770e6, pk) - 2.0) < 1e-9
