@@ -32,6 +32,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "dropout.cuh"
 #include "host_utils.h"
 
 namespace hb {
@@ -49,6 +50,10 @@ struct AttnParams {
   float scale_log2;         // scale * log2(e)
   int* status;
   uint64_t* trace;          // optional phase timestamps [grid][kTraceSlots] (nullptr: off)
+  // Dropout on the attention probabilities (DROP instantiations only): mask
+  // element ((b * nh_total + h0 + h) * T + q) * T + k.
+  DropoutArgs drop;
+  int h0, nh_total;
 };
 
 // Phase tracing: with a trace buffer set, the kernels stamp %globaltimer at
@@ -106,9 +111,10 @@ __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 
 // uses three-input max over independent chains and is taken on raw scores
 // (the scale is positive); exponent arguments and row sums are computed on
 // fp32 pairs (one f32x2 instruction for two columns).
-template <bool DIAG>
+template <bool DIAG, bool DROP>
 __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
-                                              float scale_log2, float& m, float& l) {
+                                              float scale_log2, float& m, float& l, uint32_t dkey, uint64_t pair_row,
+                                              uint32_t dthresh, float dscale) {
   float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
@@ -153,7 +159,13 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
           if (key0 + c * 32 + i > q) p0 = 0.f;
           if (key0 + c * 32 + i + 1 > q) p1 = 0.f;
         }
-        sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));
+        sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));  // normaliser: undropped
+        if (DROP) {
+          float m0, m1;
+          dropout_pair(dropout_bits(dkey, pair_row + ((key0 + c * 32 + i) >> 1)), dthresh, dscale, m0, m1);
+          p0 *= m0;
+          p1 *= m1;
+        }
         pk[i >> 1] = pack_bf16(p0, p1);
       }
 #pragma unroll
@@ -186,6 +198,7 @@ __device__ __forceinline__ void accumulate_o(uint64_t (&o)[32], uint32_t tO, flo
   }
 }
 
+template <bool DROP>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -337,6 +350,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       const uint32_t tS = tmem + g * 256, tO0 = tmem + g * 256 + 128;
       uint8_t* myP = sP + g * 2 * kTileBytes;
       float m = -INFINITY, l = 0.f, alpha_prev = 0.f;
+      uint32_t dkey = 0;
+      uint64_t pair_row = 0;
+      if (DROP) {
+        dkey = dropout_key(*p.drop.seed, p.drop.site);
+        pair_row = ((((uint64_t)b * p.nh_total + p.h0 + h) * p.T + q) * p.T) >> 1;
+      }
       uint64_t o[32];  // output row as 32 column pairs
 #pragma unroll
       for (int i = 0; i < 32; ++i) o[i] = f2_pack(0.f, 0.f);
@@ -354,9 +373,11 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           break;
         }
         if (lane == 0 && sub == 0 && j < 8) HB_TRACE(16 + 24 * g + j);
-        const float alpha = (j == my_qt)
-                                ? softmax_tile<true>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l)
-                                : softmax_tile<false>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l);
+        const float alpha =
+            (j == my_qt) ? softmax_tile<true, DROP>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
+                                                    pair_row, p.drop.thresh, p.drop.scale)
+                         : softmax_tile<false, DROP>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
+                                                     pair_row, p.drop.thresh, p.drop.scale);
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
@@ -411,6 +432,7 @@ constexpr int BWD_DQ_STG = 8 * 4096;  // per softmax warp: 32 query rows x 32 fp
 constexpr int BWD_SMEM = 2 * kTileBytes /*K,V*/ + BWD_STAGES * BWD_STAGE + 4 * kTileBytes /*P^T, dS^T*/ +
                          BWD_DQ_STG + 1024;
 
+template <bool DROP>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, AttnParams p) {
@@ -553,6 +575,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
     const int key = kt * kTile + r;
     bool ok = true;
+    uint32_t dkey = 0;
+    uint64_t drop_bh = 0;  // (b * nh_total + h0 + h) * T: first query row of this head
+    if (DROP) {
+      dkey = dropout_key(*p.drop.seed, p.drop.site);
+      drop_bh = ((uint64_t)b * p.nh_total + p.h0 + h) * p.T;
+    }
     // dQ rows of this warp (32 queries x 32 columns) leave through one bulk
     // tensor reduce-add into the fp32 accumulator (the add happens in L2).
     uint8_t* dq_stg = sDQ + (warp - 2) * 4096;
@@ -601,6 +629,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         tmem_pin_regs(dr);
         uint32_t pp[16], dd[16];
         const uint64_t sl2 = f2_pack(p.scale_log2, p.scale_log2), sc2 = f2_pack(p.scale, p.scale);
+        // dropout: this thread's key is fixed; element (query qq, key) lives in
+        // pair (row_qq + key) / 2 and takes the half selected by key's parity
+        const uint64_t q_first = (uint64_t)qi * kTile + g * 64 + c * 32;
 #pragma unroll
         for (int i4 = 0; i4 < 8; ++i4) {
           // staged per query column: -lse (log2 domain) and -scale * D
@@ -614,10 +645,26 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             float t0, t1;
             f2_unpack(f2_fma(f2_pack(__uint_as_float(sr[i]), __uint_as_float(sr[i + 1])), sl2, nl), t0, t1);
             float p0 = fast_exp2(t0), p1 = fast_exp2(t1);  // P = 2^(s * scale * log2 e - lse)
+            uint64_t dp2 = f2_pack(__uint_as_float(dr[i]), __uint_as_float(dr[i + 1]));
+            float z0 = 1.f, z1 = 1.f;
+            if (DROP) {  // dP = Z * dO V^T;  dV operand P * Z
+              const uint64_t e0 = (drop_bh + q_first + i) * (uint64_t)p.T + key;
+              const uint64_t e1 = e0 + p.T;
+              const uint32_t b0 = dropout_bits(dkey, e0 >> 1), b1 = dropout_bits(dkey, e1 >> 1);
+              const uint32_t u0 = (key & 1) ? (b0 >> 16) : (b0 & 0xFFFFu);
+              const uint32_t u1 = (key & 1) ? (b1 >> 16) : (b1 & 0xFFFFu);
+              z0 = u0 >= p.drop.thresh ? p.drop.scale : 0.f;
+              z1 = u1 >= p.drop.thresh ? p.drop.scale : 0.f;
+              dp2 = f2_mul(dp2, f2_pack(z0, z1));
+            }
             // dS = P * (dP * scale - D * scale)
-            const uint64_t u = f2_fma(f2_pack(__uint_as_float(dr[i]), __uint_as_float(dr[i + 1])), sc2, nd);
+            const uint64_t u = f2_fma(dp2, sc2, nd);
             float d0, d1;
             f2_unpack(f2_mul(u, f2_pack(p0, p1)), d0, d1);
+            if (DROP) {
+              p0 *= z0;
+              p1 *= z1;
+            }
             if (masked_tile) {
               const int qq = qi * kTile + g * 64 + c * 32 + i;
               if ((diag && key > qq) || qq >= p.T) p0 = d0 = 0.f;
@@ -727,13 +774,19 @@ static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
 }
 
 void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, long ld_out, float* lse, int B,
-                     int T, int nh, int Tpad, int* status, cudaStream_t s) {
+                     int T, int nh, int Tpad, const DropoutArgs& drop, int h0, int nh_total, int* status,
+                     cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+    HB_CUDA_CHECK(
+        cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
     attr = true;
   }
   AttnParams p{};
+  p.drop = drop;
+  p.h0 = h0;
+  p.nh_total = nh_total;
   p.B = B, p.T = T, p.nh = nh, p.Hs = nh * kD, p.out = out, p.ld_out = ld_out, p.lse = lse, p.Tpad = Tpad;
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
@@ -742,16 +795,23 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
-  attn_fwd_kernel<<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
+  if (drop.thresh != 0) {
+    attn_fwd_kernel<true><<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
+  } else {
+    attn_fwd_kernel<false><<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
+  }
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16* o, long ld_o,
                      const __nv_bfloat16* dO, long ld_do, const float* lse, float* dvec, float* dq_acc,
-                     __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, int* status, cudaStream_t s) {
+                     __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, const DropoutArgs& drop,
+                     int h0, int nh_total, int* status, cudaStream_t s) {
   static bool attr = false;
   if (!attr) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
+    HB_CUDA_CHECK(
+        cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
+    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
     attr = true;
   }
   const int Hs = nh * kD;
@@ -762,6 +822,9 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   AttnParams p{};
   p.B = B, p.T = T, p.nh = nh, p.Hs = Hs, p.out = dqkv, p.ld_out = ld_dqkv, p.lse = const_cast<float*>(lse);
   p.Tpad = Tpad, p.dvec = dvec, p.dq_acc = dq_acc;
+  p.drop = drop;
+  p.h0 = h0;
+  p.nh_total = nh_total;
   p.scale = 0.125f;
   p.scale_log2 = 0.125f * 1.4426950408889634f;
   p.status = status;
@@ -775,7 +838,11 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   const CUtensorMap tdq =
       make_tmap(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
   const int n_t = (T + kTile - 1) / kTile;
-  attn_bwd_kernel<<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
+  if (drop.thresh != 0) {
+    attn_bwd_kernel<true><<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
+  } else {
+    attn_bwd_kernel<false><<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
+  }
   HB_CUDA_CHECK(cudaGetLastError());
   attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
   HB_CUDA_CHECK(cudaGetLastError());

@@ -13,7 +13,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ag_src") = std::vector<uint64_t>{}, py::arg("ag_flags") = py::none(), py::arg("ag_rank") = 0,
         py::arg("ag_rows") = 0, py::arg("rs_dst") = std::vector<uint64_t>{}, py::arg("rs_rank") = 0,
         py::arg("rs_rows") = 0, py::arg("grp_mode") = 0, py::arg("grp_off") = py::none(), py::arg("grp_n") = 0,
-        py::arg("grp_b_off") = 0, py::arg("grp_c_off") = 0);
+        py::arg("grp_b_off") = 0, py::arg("grp_c_off") = 0, py::arg("drop_seed") = py::none(),
+        py::arg("drop_site") = 0, py::arg("drop_p") = 0.0, py::arg("drop_row0") = 0);
   m.def("layernorm_fwd", &hb::layernorm_fwd);
   m.def("layernorm_bwd_scratch_rows", &hb::layernorm_bwd_scratch_rows);
   m.def("layernorm_bwd", &hb::layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
@@ -31,8 +32,14 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("adamw_step", &hb::adamw_step);
   m.def("f32_to_bf16", &hb::f32_to_bf16);
   m.def("attention_set_trace", &hb::attention_set_trace);
-  m.def("attention_fwd", &hb::attention_fwd);
-  m.def("attention_bwd", &hb::attention_bwd);
+  m.def("attention_fwd", &hb::attention_fwd, py::arg("qkv"), py::arg("B"), py::arg("T"), py::arg("nh"), py::arg("out"),
+        py::arg("lse"), py::arg("drop_seed") = py::none(), py::arg("drop_site") = 0, py::arg("drop_p") = 0.0,
+        py::arg("h0") = 0, py::arg("nh_total") = 0);
+  m.def("dropout_bf16", &hb::dropout_bf16);
+  m.def("attention_bwd", &hb::attention_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
+        py::arg("B"), py::arg("T"), py::arg("nh"), py::arg("dvec"), py::arg("dq_acc"), py::arg("dqkv"),
+        py::arg("drop_seed") = py::none(), py::arg("drop_site") = 0, py::arg("drop_p") = 0.0, py::arg("h0") = 0,
+        py::arg("nh_total") = 0);
   m.def("raw_malloc", &hb::raw_malloc);
   m.def("raw_free", &hb::raw_free);
   m.def("tensor_from_ptr", &hb::tensor_from_ptr);

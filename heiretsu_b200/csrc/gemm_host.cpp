@@ -1,6 +1,7 @@
 // Torch-facing entry point of the tcgen05 GEMM: validates tensors, builds
 // the TMA descriptors and picks the instantiation (gemm_inst_*.cu).
 #include <ATen/cuda/CUDAContext.h>
+#include <cmath>
 #include <cstdlib>
 #include <c10/cuda/CUDAGuard.h>
 #include <torch/extension.h>
@@ -44,7 +45,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& resid, int64_t block_n, const std::vector<uint64_t>& ag_src,
           const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
           const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows, int64_t grp_mode,
-          const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off) {
+          const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off,
+          const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: tensors must be on CUDA");
   TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: operands must be bf16");
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D tensors expected");
@@ -90,6 +92,20 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
                 "gemm: fp32 resid tensor required");
     p.resid = resid->data_ptr<float>();
     p.ldr = resid->stride(0);
+  }
+  p.drop = DropoutArgs{nullptr, 0, 0, 1.f, 0};
+  if (drop_p > 0.0) {
+    TORCH_CHECK(epi == kEpiF32Resid, "gemm: dropout is fused into the residual epilogue only");
+    TORCH_CHECK(drop_p < 1.0 && drop_seed && drop_seed->defined() && drop_seed->is_cuda() &&
+                    drop_seed->scalar_type() == at::kInt && drop_seed->numel() >= 1,
+                "gemm: dropout needs 0 < p < 1 and an int32 device seed");
+    TORCH_CHECK(N % 2 == 0, "gemm: dropout pairs columns (N must be even)");
+    p.drop.seed = reinterpret_cast<const uint32_t*>(drop_seed->data_ptr<int>());
+    p.drop.site = static_cast<uint32_t>(drop_site);
+    p.drop.thresh = static_cast<uint32_t>(std::lround(drop_p * 65536.0));
+    p.drop.scale = static_cast<float>(1.0 / (1.0 - drop_p));
+    p.drop.row0 = static_cast<long>(drop_row0);
+    if (p.drop.thresh == 0) p.drop.seed = nullptr;
   }
   // Rasterisation: CTAs in flight share tiles of the larger operand; the
   // smaller one is re-read from L2.

@@ -25,6 +25,7 @@
 #include "common.cuh"
 #include "host_utils.h"
 #include "gemm_params.h"
+#include "dropout.cuh"
 
 namespace hb {
 
@@ -193,11 +194,37 @@ __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, 
   }
 }
 
+// Residual dropout of one 32-column chunk of this thread's row:
+// v = mask * (v + bias), mask from the counter-based hash of the element index.
+__device__ __forceinline__ void epi_bias_dropout(const GemmParams& p, uint32_t key, int row, int n0, float (&v)[32]) {
+  if (p.bias != nullptr) {
+#pragma unroll
+    for (int j = 0; j < 32; j += 4) {
+      if (n0 + j < p.N) {
+        const float4 b = __ldg(reinterpret_cast<const float4*>(p.bias + n0 + j));
+        v[j] += b.x;
+        v[j + 1] += b.y;
+        v[j + 2] += b.z;
+        v[j + 3] += b.w;
+      }
+    }
+  }
+  const uint64_t pair0 = ((uint64_t)(p.drop.row0 + row) * (uint64_t)p.N + (uint64_t)n0) >> 1;
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    float m0, m1;
+    dropout_pair(dropout_bits(key, pair0 + j), p.drop.thresh, p.drop.scale, m0, m1);
+    v[2 * j] *= m0;
+    v[2 * j + 1] *= m1;
+  }
+}
+
 // Step 2: bias, activation and the stores of one 32x32 chunk into C.
 template <int EPI>
 __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_base, int n0, float (&v)[32],
-                                           uint8_t* stg, int lane) {
-  if (p.bias != nullptr && (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
+                                           uint8_t* stg, int lane, bool bias_done = false) {
+  if (!bias_done && p.bias != nullptr &&
+      (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       if (n0 + j < p.N) {
@@ -249,8 +276,10 @@ __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_b
 // The caller has waited for the previous bulk copies to finish reading `stg`.
 template <int EPI>
 __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmX,
-                                               int row, int n0, float (&v)[32], uint8_t* stg, int lane) {
-  if (p.bias != nullptr && (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
+                                               int row, int n0, float (&v)[32], uint8_t* stg, int lane,
+                                               bool bias_done = false) {
+  if (!bias_done && p.bias != nullptr &&
+      (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       if (n0 + j < p.N) {
@@ -543,6 +572,8 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     const int c0 = (eid >> 2) * CH;
     uint8_t* stg = smem + Cfg::STG_OFFSET + eid * kStgBytes;
     if (p.ag_world > 1) ag_copy_units(p, blockIdx.x * kEpiWarps + eid, gridDim.x * kEpiWarps, lane);
+    uint32_t drop_key = 0;
+    if (EPI == kEpiF32Resid && p.drop.thresh != 0) drop_key = dropout_key(*p.drop.seed, p.drop.site);
     int local = 0;
     for (int t = blockIdx.x; t < num_tiles; t += gridDim.x, ++local) {
       const int acc = local & 1;
@@ -581,12 +612,19 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
           }
+          bool bias_done = false;
+          if constexpr (EPI == kEpiF32Resid) {
+            if (p.drop.thresh != 0) {  // C = R + dropout(acc + bias)
+              epi_bias_dropout(p, drop_key, m_base + lane, n0, v);
+              bias_done = true;
+            }
+          }
           if (reads) epi_apply_operand<EPI>(v, stg, pre, lane);
           if (reads && c + 1 < CH && n0 + 32 < p.N) epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
           if (tma) {
-            epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane);
+            epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane, bias_done);
           } else {
-            epi_finish<EPI>(p, C, m_base, n0, v, stg, lane);
+            epi_finish<EPI>(p, C, m_base, n0, v, stg, lane, bias_done);
           }
         }
       }

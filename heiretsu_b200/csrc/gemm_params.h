@@ -1,6 +1,8 @@
 // Parameters and epilogue codes of the tcgen05 GEMM (shared by host and device code).
 #pragma once
 
+#include "dropout_args.h"
+
 namespace hb {
 
 enum GemmEpi : int {
@@ -8,7 +10,7 @@ enum GemmEpi : int {
   kEpiBf16Gelu = 1,   // AUX bf16 = acc + bias ; C bf16 = gelu(acc + bias)
   kEpiF32 = 2,        // C f32 = acc (+ bias)
   kEpiF32Acc = 3,     // C f32 += acc
-  kEpiF32Resid = 4,   // C f32 = R f32 + acc (+ bias)     (C may alias R)
+  kEpiF32Resid = 4,   // C f32 = R f32 + dropout(acc (+ bias))     (C may alias R; dropout optional)
   kEpiBf16Dgelu = 5,  // C bf16 = acc * gelu'(AUX)
   kEpiF32Atomic = 6,  // C f32 += acc with vector atomics (split-K partial sums)
 };
@@ -66,6 +68,10 @@ struct GemmParams {
   // accumulating epilogues) through the C / AUX tensor maps. 0 = per-lane
   // global stores (always the case for reduce-scatter peer outputs).
   int tma_epi;
+
+  // Residual dropout of the F32Resid epilogue (thresh 0 = off):
+  // C = R + mask * (acc + bias), mask element (drop.row0 + row) * N + col.
+  DropoutArgs drop;
 };
 
 }  // namespace hb

@@ -9,6 +9,7 @@
 #include <cuda_bf16.h>
 
 #include "common.cuh"
+#include "dropout.cuh"
 #include "host_utils.h"
 
 namespace hb {
@@ -367,6 +368,31 @@ void ln_bwd_launch(const float* dy, const float* x, const float* mean, const flo
                                                                           dy_src_stride));
   HB_CUDA_CHECK(cudaGetLastError());
   reduce_rows_kernel<<<(2 * H + 31) / 32, 256, 0, s>>>(part, num_ctas, 2 * H, dgamma, dbeta, H);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+// out = bf16(g * mask): 4 elements (2 mask pairs) per thread.
+__global__ void dropout_bf16_kernel(const float* __restrict__ g, __nv_bfloat16* __restrict__ out, long M, int H,
+                                    DropoutArgs d) {
+  const uint32_t key = dropout_key(*d.seed, d.site);
+  const long n4 = M * (long)H / 4;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n4; i += (long)gridDim.x * blockDim.x) {
+    const long e = 4 * i;
+    const long row = e / H, col = e % H;
+    const uint64_t pair = ((uint64_t)(d.row0 + row) * (uint64_t)H + (uint64_t)col) >> 1;
+    float m0, m1, m2, m3;
+    dropout_pair(dropout_bits(key, pair), d.thresh, d.scale, m0, m1);
+    dropout_pair(dropout_bits(key, pair + 1), d.thresh, d.scale, m2, m3);
+    const float4 v = reinterpret_cast<const float4*>(g)[i];
+    reinterpret_cast<uint2*>(out)[i] = make_uint2(pack_bf16(v.x * m0, v.y * m1), pack_bf16(v.z * m2, v.w * m3));
+  }
+}
+
+void dropout_bf16_launch(const float* g, __nv_bfloat16* out, long M, int H, const DropoutArgs& d, cudaStream_t s) {
+  const long n4 = M * (long)H / 4;
+  if (n4 == 0) return;
+  const int blocks = (int)std::min<long>((n4 + 255) / 256, 4L * num_sms(current_device()));
+  dropout_bf16_kernel<<<blocks, 256, 0, s>>>(g, out, M, H, d);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -10,7 +10,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& resid, int64_t block_n, const std::vector<uint64_t>& ag_src,
           const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
           const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows, int64_t grp_mode,
-          const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off);
+          const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off,
+          const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0);
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, at::Tensor& y, at::Tensor& mean,
                    at::Tensor& rstd, double eps);
@@ -37,9 +38,15 @@ void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor
                 const c10::optional<at::Tensor>& p16, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
 void f32_to_bf16(const at::Tensor& x, at::Tensor& y);
 void attention_set_trace(const c10::optional<at::Tensor>& trace);
-void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse);
+void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse,
+                   const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
+                   int64_t nh_total);
+void dropout_bf16(const at::Tensor& g, at::Tensor& out, const at::Tensor& seed, int64_t site, double p,
+                  int64_t row0);
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
-                   int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv);
+                   int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv,
+                   const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
+                   int64_t nh_total);
 uint64_t raw_malloc(int64_t bytes);
 void raw_free(uint64_t ptr);
 at::Tensor tensor_from_ptr(uint64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device);

@@ -1,6 +1,7 @@
 // Torch-facing entry points of the non-GEMM kernels: argument validation,
 // stream selection, then a call into the raw launchers in the .cu files.
 #include <ATen/cuda/CUDAContext.h>
+#include <cmath>
 #include <c10/cuda/CUDAGuard.h>
 #include <cuda_bf16.h>
 #include <torch/extension.h>
@@ -8,6 +9,7 @@
 #include <initializer_list>
 
 #include "host_utils.h"
+#include "dropout_args.h"
 #include "ops.h"
 
 namespace hb {
@@ -33,10 +35,28 @@ void clip_coef_launch(const float*, float, float*, float*, cudaStream_t);
 void adamw_launch(float*, const float*, float*, float*, __nv_bfloat16*, long, const void*, const float*,
                   cudaStream_t);
 void f32_to_bf16_launch(const float*, __nv_bfloat16*, long, cudaStream_t);
-void attn_fwd_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int, int*,
-                     cudaStream_t);
+void attn_fwd_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int,
+                     const DropoutArgs&, int, int, int*, cudaStream_t);
 void attn_bwd_launch(const __nv_bfloat16*, long, const __nv_bfloat16*, long, const __nv_bfloat16*, long,
-                     const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, int*, cudaStream_t);
+                     const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, const DropoutArgs&, int,
+                     int, int*, cudaStream_t);
+void dropout_bf16_launch(const float*, __nv_bfloat16*, long, int, const DropoutArgs&, cudaStream_t);
+
+// Dropout site arguments from a device seed tensor (int32 scalar) and a rate p (0 = off).
+static DropoutArgs make_dropout(const c10::optional<at::Tensor>& seed, int64_t site, double p, int64_t row0) {
+  DropoutArgs d{nullptr, 0, 0, 1.f, 0};
+  if (p <= 0.0) return d;
+  TORCH_CHECK(p < 1.0 && seed && seed->defined() && seed->is_cuda() && seed->scalar_type() == at::kInt &&
+                  seed->numel() >= 1,
+              "dropout needs 0 < p < 1 and an int32 device seed");
+  d.seed = reinterpret_cast<const uint32_t*>(seed->data_ptr<int>());
+  d.site = static_cast<uint32_t>(site);
+  d.thresh = static_cast<uint32_t>(std::lround(p * 65536.0));
+  d.scale = static_cast<float>(1.0 / (1.0 - p));
+  d.row0 = static_cast<long>(row0);
+  if (d.thresh == 0) d.seed = nullptr;
+  return d;
+}
 
 #define CHECK_CUDA(t) TORCH_CHECK((t).is_cuda(), #t " must be a CUDA tensor")
 #define CHECK_DT(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has the wrong dtype")
@@ -233,7 +253,9 @@ void attention_set_trace(const c10::optional<at::Tensor>& trace) {
   }
 }
 
-void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse) {
+void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse,
+                   const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
+                   int64_t nh_total) {
   CHECK_CUDA(qkv);
   CHECK_DT(qkv, at::kBFloat16);
   CHECK_ROWS(qkv);
@@ -244,12 +266,17 @@ void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::
   const int64_t Tpad = (T + 127) / 128 * 128;
   TORCH_CHECK(lse.numel() >= B * nh * Tpad && lse.scalar_type() == at::kFloat, "attention_fwd: lse [B, nh, Tpad]");
   c10::cuda::CUDAGuard g(qkv.device());
+  TORCH_CHECK(drop_p <= 0.0 || T % 2 == 0, "attention dropout pairs keys (T must be even)");
+  const DropoutArgs d = make_dropout(drop_seed, drop_site, drop_p, 0);
   attn_fwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<float>(lse), B,
-                  T, nh, Tpad, device_status_ptr(qkv.get_device()), stream());
+                  T, nh, Tpad, d, static_cast<int>(h0), static_cast<int>(nh_total > 0 ? nh_total : nh),
+                  device_status_ptr(qkv.get_device()), stream());
 }
 
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
-                   int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv) {
+                   int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv,
+                   const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
+                   int64_t nh_total) {
   CHECK_CUDA(qkv);
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&qkv, &out, &dout, &dqkv}) {
     TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 && t->stride(0) % 8 == 0,
@@ -261,8 +288,24 @@ void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tenso
   c10::cuda::CUDAGuard g(qkv.device());
   attn_bwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0),
                   ptr<__nv_bfloat16>(dout), dout.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc),
-                  ptr<__nv_bfloat16>(dqkv), dqkv.stride(0), B, T, nh, Tpad, device_status_ptr(qkv.get_device()),
-                  stream());
+                  ptr<__nv_bfloat16>(dqkv), dqkv.stride(0), B, T, nh, Tpad,
+                  make_dropout(drop_seed, drop_site, drop_p, 0), static_cast<int>(h0),
+                  static_cast<int>(nh_total > 0 ? nh_total : nh), device_status_ptr(qkv.get_device()), stream());
+}
+
+// out (bf16) = g * mask for a residual dropout site: the gradient reaching
+// the sub-layer's output projection (element (row0 + row) * H + col).
+void dropout_bf16(const at::Tensor& g, at::Tensor& out, const at::Tensor& seed, int64_t site, double p,
+                  int64_t row0) {
+  CHECK_CUDA(g);
+  TORCH_CHECK(g.scalar_type() == at::kFloat && g.is_contiguous() && g.dim() == 2, "dropout_bf16: g fp32 [M, H]");
+  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.sizes() == g.sizes(),
+              "dropout_bf16: out bf16 like g");
+  TORCH_CHECK(g.size(1) % 4 == 0, "dropout_bf16: H % 4 == 0");
+  const DropoutArgs d = make_dropout(seed, site, p, row0);
+  TORCH_CHECK(d.seed != nullptr, "dropout_bf16: p must be > 0");
+  c10::cuda::CUDAGuard guard(g.device());
+  dropout_bf16_launch(ptr<float>(g), ptr<__nv_bfloat16>(out), g.size(0), static_cast<int>(g.size(1)), d, stream());
 }
 
 }  // namespace hb

@@ -41,8 +41,10 @@ def fused_supported(cfg, topo=None) -> Tuple[bool, str]:
         return False, "fused attention needs head_dim == 64"
     if cfg.n_embed % 128:
         return False, "fused path needs n_embed % 128 == 0"
-    if cfg.dropout > 0:
-        return False, "fused path runs without dropout (dropout > 0 uses the plain path)"
+    if cfg.dropout > 0 and topo is not None and getattr(topo, "tp", 1) > 1:
+        return False, "fused tensor parallelism runs without dropout (dropout > 0 with tp > 1 uses the plain path)"
+    if cfg.dropout > 0 and cfg.n_embed % 4:
+        return False, "fused dropout needs n_embed % 4 == 0"
     if cfg.num_experts > 0 and topo is not None and getattr(topo, "ep", 1) > 8:
         return False, "fused expert parallelism exchanges partials over NVLink within one node (ep <= 8)"
     return True, ""
@@ -73,32 +75,51 @@ def embed_fused(wte: torch.nn.Parameter, wpe: torch.nn.Parameter, idx: torch.Ten
 
 
 # ---------------------------------------------------------------------------
+# Dropout (training only): block i uses sites 4i (attention probabilities),
+# 4i+1 (attention output residual) and 4i+2 (MLP output residual), as the
+# reference applies dropout (gpt_model.py:53-54, :79, :96). Every forward
+# takes a snapshot of the step's device seed and then advances it, so each
+# micro-batch and each graph replay draws fresh masks, and the backward
+# recomputes exactly the forward's masks from the snapshot.
+def _dropout_of(blk):
+    """(seed snapshot tensor, layer index, p) of a block in a training forward, else None."""
+    d = getattr(blk, "_hb_drop_now", None)
+    return d if (d is not None and blk.training) else None
+
+
 def _attn_fwd(blk, x: torch.Tensor, B: int, T: int, keep: bool):
-    """Attention sub-layer: x fp32 [M, H] -> x1 = x + c_proj(attn(c_attn(ln_1(x))))."""
+    """Attention sub-layer: x fp32 [M, H] -> x1 = x + drop(c_proj(attn(c_attn(ln_1(x)))))."""
     attn = blk.attn
+    d = _dropout_of(blk)
     xn, m1, r1 = K.layernorm_fwd(x, blk.ln_1.weight, blk.ln_1.bias, LN_EPS)
     qkv = G.linear_fwd(xn, attn.c_attn.weight.w16, attn.c_attn.bias)
-    y, lse = K.attention_fwd(qkv, B, T, attn.nh_tp)
-    x1 = G.linear_fwd_resid(y, attn.c_proj.weight.w16, attn.c_proj.bias, x)
-    return x1, ((x, xn, m1, r1, qkv, y, lse) if keep else None)
+    adrop = (d[0], 4 * d[1], d[2], 0, attn.nh_tp) if d else None
+    y, lse = K.attention_fwd(qkv, B, T, attn.nh_tp, drop=adrop)
+    x1 = G.linear_fwd_resid(y, attn.c_proj.weight.w16, attn.c_proj.bias, x,
+                            drop=(d[0], 4 * d[1] + 1, d[2], 0) if d else None)
+    return x1, ((x, xn, m1, r1, qkv, y, lse, d) if keep else None)
 
 
 def _mlp_fwd(blk, x1: torch.Tensor, keep: bool):
-    """Dense MLP sub-layer: x2 = x1 + c_proj(gelu(c_fc(ln_2(x1))))."""
+    """Dense MLP sub-layer: x2 = x1 + drop(c_proj(gelu(c_fc(ln_2(x1)))))."""
     mlp = blk.mlp
+    d = _dropout_of(blk)
     xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
     h, pre = G.linear_fwd_gelu(xn2, mlp.c_fc.weight.w16, mlp.c_fc.bias)
-    x2 = G.linear_fwd_resid(h, mlp.c_proj.weight.w16, mlp.c_proj.bias, x1)
-    return x2, ((x1, xn2, m2, r2, pre, h) if keep else None)
+    x2 = G.linear_fwd_resid(h, mlp.c_proj.weight.w16, mlp.c_proj.bias, x1,
+                            drop=(d[0], 4 * d[1] + 2, d[2], 0) if d else None)
+    return x2, ((x1, xn2, m2, r2, pre, h, d) if keep else None)
 
 
 def _mlp_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, ws: dict):
     """In place: dres (fp32) / dres16 (bf16) go from d(x2) to d(x1)."""
     mlp = blk.mlp
-    x1, xn2, m2, r2, pre, h = saved
-    dpre = G.linear_dgrad(dres16, mlp.c_proj.weight.w16, gelu_pre=pre)
-    G.linear_wgrad(dres16, h, out=mlp.c_proj.weight.main_grad, accumulate=True)
-    K.colsum_bf16(dres16, mlp.c_proj.bias.main_grad)
+    x1, xn2, m2, r2, pre, h, d = saved
+    dout16 = K.dropout_bf16(dres, d[0], 4 * d[1] + 2, d[2]) if d else dres16  # gradient at c_proj's output
+    dpre = G.linear_dgrad(dout16, mlp.c_proj.weight.w16, gelu_pre=pre)
+    G.linear_wgrad(dout16, h, out=mlp.c_proj.weight.main_grad, accumulate=True)
+    K.colsum_bf16(dout16, mlp.c_proj.bias.main_grad)
+    del dout16
     dxn2 = G.linear_dgrad(dpre, mlp.c_fc.weight.w16, f32=True)
     G.linear_wgrad(dpre, xn2, out=mlp.c_fc.weight.main_grad, accumulate=True)
     K.colsum_bf16(dpre, mlp.c_fc.bias.main_grad)
@@ -110,11 +131,14 @@ def _mlp_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, ws: dict):
 def _attn_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: int, T: int, ws: dict):
     """In place: dres / dres16 go from d(x1) to d(x)."""
     attn = blk.attn
-    x, xn, m1, r1, qkv, y, lse = saved
-    dy = G.linear_dgrad(dres16, attn.c_proj.weight.w16)
-    G.linear_wgrad(dres16, y, out=attn.c_proj.weight.main_grad, accumulate=True)
-    K.colsum_bf16(dres16, attn.c_proj.bias.main_grad)
-    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, attn.nh_tp)
+    x, xn, m1, r1, qkv, y, lse, d = saved
+    dout16 = K.dropout_bf16(dres, d[0], 4 * d[1] + 1, d[2]) if d else dres16  # gradient at c_proj's output
+    dy = G.linear_dgrad(dout16, attn.c_proj.weight.w16)
+    G.linear_wgrad(dout16, y, out=attn.c_proj.weight.main_grad, accumulate=True)
+    K.colsum_bf16(dout16, attn.c_proj.bias.main_grad)
+    del dout16
+    adrop = (d[0], 4 * d[1], d[2], 0, attn.nh_tp) if d else None
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, attn.nh_tp, drop=adrop)
     del dy
     G.linear_wgrad(dqkv, xn, out=attn.c_attn.weight.main_grad, accumulate=True)
     K.colsum_bf16(dqkv, attn.c_attn.bias.main_grad)
@@ -128,6 +152,23 @@ def _ln_scratch(M: int, H: int, device) -> torch.Tensor:
     from ..ops._C import load
     rows = load().layernorm_bwd_scratch_rows(M)
     return torch.empty(rows * 2 * H, device=device, dtype=torch.float32)
+
+
+def _snapshot_dropout_seeds(blocks) -> None:
+    """Give every block of this forward the current device seed (one copy),
+    then advance the seed for the next forward."""
+    seeds = {}
+    for blk in blocks:
+        cfg = getattr(blk, "_hb_dropout", None)  # (seed tensor, layer index, p)
+        if cfg is None or not blk.training:
+            blk._hb_drop_now = None
+            continue
+        seed, layer, p = cfg
+        if id(seed) not in seeds:
+            seeds[id(seed)] = (seed, seed.clone())
+        blk._hb_drop_now = (seeds[id(seed)][1], layer, p)
+    for seed, _ in seeds.values():
+        seed.add_(1)
 
 
 # Called after each block's backward has been issued (data-parallel gradient
@@ -152,6 +193,7 @@ class _Body(torch.autograd.Function):
         keep = x.requires_grad
         saved: List = []
         aux_total = torch.zeros((), device=x.device, dtype=torch.float32)
+        _snapshot_dropout_seeds(blocks)
         for i, blk in enumerate(blocks):
             with nvtx(f"block{i}.attn.fwd"):
                 x, sa = _attn_fwd(blk, x, B, T, keep)

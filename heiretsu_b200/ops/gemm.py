@@ -28,18 +28,21 @@ def _bn(n: int) -> int:
     return 256 if n >= 2048 else 128
 
 
-def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None, grp=None):
+def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None, grp=None,
+         drop=None):
     """D = A.B^T-style GEMM (see module doc). ``ag = (src_ptrs, flags, rank, rows)`` turns on
     the in-kernel all-gather of A's token shards; ``rs = (dst_ptrs, rank, rows)`` stores each
     output tile into its token owner's receive slot (reduce-scatter epilogue);
-    ``grp = (mode, offsets, n_groups, b_off, c_off)`` runs an expert-grouped GEMM."""
+    ``grp = (mode, offsets, n_groups, b_off, c_off)`` runs an expert-grouped GEMM;
+    ``drop = (seed_tensor, site, p, row0)`` applies residual dropout in the F32Resid epilogue."""
     ag_src, ag_flags, ag_rank, ag_rows = ag if ag is not None else ([], None, 0, 0)
     rs_dst, rs_rank, rs_rows = rs if rs is not None else ([], 0, 0)
     g_mode, g_off, g_n, g_b, g_c = grp if grp is not None else (0, None, 0, 0, 0)
+    d_seed, d_site, d_p, d_row0 = drop if drop is not None else (None, 0, 0.0, 0)
     load().gemm(a, b, c, int(n), int(epi), bool(a_mn), bool(b_mn), bias, aux, resid,
                 int(block_n if block_n is not None else _bn(n)), list(ag_src), ag_flags, int(ag_rank),
                 int(ag_rows), list(rs_dst), int(rs_rank), int(rs_rows), int(g_mode), g_off, int(g_n), int(g_b),
-                int(g_c))
+                int(g_c), d_seed, int(d_site), float(d_p), int(d_row0))
     return c
 
 
@@ -64,12 +67,12 @@ def linear_fwd_gelu(x, w, bias, *, out=None, pre=None):
     return out, pre
 
 
-def linear_fwd_resid(x, w, bias, resid, *, out=None):
-    """fp32 out = resid + x @ w^T + bias (out may be resid itself)."""
+def linear_fwd_resid(x, w, bias, resid, *, out=None, drop=None):
+    """fp32 out = resid + dropout(x @ w^T + bias) (out may be resid itself; ``drop`` as in gemm)."""
     N = w.shape[0]
     if out is None:
         out = torch.empty_like(resid)
-    return gemm(x, w, out, N, EPI_F32_RESID, False, False, bias=bias, resid=resid)
+    return gemm(x, w, out, N, EPI_F32_RESID, False, False, bias=bias, resid=resid, drop=drop)
 
 
 def linear_dgrad(dy, w, *, out=None, gelu_pre=None, f32=False):

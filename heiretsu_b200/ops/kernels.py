@@ -115,26 +115,42 @@ def f32_to_bf16(x: torch.Tensor, y: Optional[torch.Tensor] = None) -> torch.Tens
 # ---------------------------------------------------------------------------
 # Attention (head_dim 64, causal)
 # ---------------------------------------------------------------------------
-def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torch.Tensor] = None):
+def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torch.Tensor] = None, drop=None):
     """qkv bf16 [B*T, 3*nh*64] -> (y bf16 [B*T, nh*64], nlse fp32 [B, nh, Tpad]).
 
     nlse = -log2(sum_k 2^(s_k * log2(e) / 8)) per query row: the negated
     log2-domain log-sum-exp, kept in the form the backward kernel consumes.
-    Natural-log LSE = -nlse * ln(2)."""
+    Natural-log LSE = -nlse * ln(2).
+
+    ``drop = (seed_tensor, site, p, h0, nh_total)`` applies dropout to the
+    attention probabilities (mask of heads h0 .. h0+nh-1 of nh_total; see
+    ops/dropout_ref.py); the backward must get the same ``drop``."""
     Tpad = (T + 127) // 128 * 128
     if out is None:
         out = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.bfloat16)
     lse = torch.empty(B, nh, Tpad, device=qkv.device, dtype=torch.float32)
-    _ext().attention_fwd(qkv, B, T, nh, out, lse)
+    d_seed, d_site, d_p, h0, nht = drop if drop is not None else (None, 0, 0.0, 0, 0)
+    _ext().attention_fwd(qkv, B, T, nh, out, lse, d_seed, int(d_site), float(d_p), int(h0), int(nht))
     return out, lse
 
 
-def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv: Optional[torch.Tensor] = None):
+def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv: Optional[torch.Tensor] = None, drop=None):
     """Returns dqkv bf16 [B*T, 3*nh*64] (columns [dQ | dK | dV])."""
     Tpad = (T + 127) // 128 * 128
     if dqkv is None:
         dqkv = torch.empty(B * T, 3 * nh * 64, device=qkv.device, dtype=torch.bfloat16)
     dvec = torch.empty(B, nh, Tpad, device=qkv.device, dtype=torch.float32)
     dq_acc = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.float32)
-    _ext().attention_bwd(qkv, out, dout, lse, B, T, nh, dvec, dq_acc, dqkv)
+    d_seed, d_site, d_p, h0, nht = drop if drop is not None else (None, 0, 0.0, 0, 0)
+    _ext().attention_bwd(qkv, out, dout, lse, B, T, nh, dvec, dq_acc, dqkv, d_seed, int(d_site), float(d_p), int(h0),
+                         int(nht))
     return dqkv
+
+
+def dropout_bf16(g: torch.Tensor, seed: torch.Tensor, site: int, p: float, row0: int = 0,
+                 out: Optional[torch.Tensor] = None) -> torch.Tensor:
+    """bf16(g * mask) for residual dropout site ``site`` (g fp32 [M, H])."""
+    if out is None:
+        out = torch.empty(g.shape, device=g.device, dtype=torch.bfloat16)
+    _ext().dropout_bf16(g, out, seed, int(site), float(p), int(row0))
+    return out

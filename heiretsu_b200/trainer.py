@@ -210,6 +210,19 @@ class Engine:
         if self.fused:
             from .ops._C import load as _load
             _load()  # fail loudly if the extension is missing
+        self.dropout_seed = None
+        if self.fused and cfg.dropout > 0:
+            # Device seed of the fused dropout masks: different per DP / PP rank
+            # (like the reference's per-rank torch seeds, train.py:318-328), equal
+            # across TP / EP ranks, whose replicated computations must stay identical.
+            base = (args.seed * 1000003 + topo.dp_rank * 7919 + topo.pp_rank * 104729) & 0x7FFFFFFF
+            self.dropout_seed = torch.tensor([base], dtype=torch.int32, device=device)
+            if self.use_pipeline:
+                blocks = [(self.module.block_start + i, b) for i, b in enumerate(self.module.blocks)]
+            else:
+                blocks = list(enumerate(self.module.tr.h))
+            for layer, blk in blocks:
+                blk._hb_dropout = (self.dropout_seed, layer, float(cfg.dropout))
         self.mp_group = mp_group_of(topo)
         if self.fused:
             from .optim import FusedAdamW

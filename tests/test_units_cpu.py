@@ -199,3 +199,26 @@ def test_roofline_fractions(tmp_path):
     # 1 TFLOP at 1.6 PFLOP/s = 0.625 ms < 770 MB at 770 GB/s = 1 ms: the link bounds it
     assert abs(fused_target_ms(1e12, 770e6, pk) - 1.0) < 1e-9
     assert abs(fused_target_ms(3.2e12, 770e6, pk) - 2.0) < 1e-9
+
+
+def test_dropout_reference_hash():
+    import torch
+
+    from heiretsu_b200.ops.dropout_ref import lowbias32, residual_mask
+
+    def py_lowbias32(x):
+        x &= 0xFFFFFFFF
+        x ^= x >> 16
+        x = (x * 0x7FEB352D) & 0xFFFFFFFF
+        x ^= x >> 15
+        x = (x * 0x846CA68B) & 0xFFFFFFFF
+        x ^= x >> 16
+        return x
+
+    vals = [0, 1, 2, 12345, 0xFFFFFFFF, 0x80000000, 987654321]
+    assert lowbias32(torch.tensor(vals, dtype=torch.int64)).tolist() == [py_lowbias32(v) for v in vals]
+    m = residual_mask(7, 3, 256, 128, 0.2)
+    assert set(torch.unique(m).tolist()) == {0.0, 1.25}
+    assert abs((m == 0).double().mean().item() - 0.2) < 0.01
+    assert not torch.equal(m, residual_mask(8, 3, 256, 128, 0.2))  # seed changes the mask
+    assert not torch.equal(m, residual_mask(7, 4, 256, 128, 0.2))  # so does the site
