@@ -20,6 +20,12 @@ void gemm_launch_128_nn(int, const CUtensorMap&, const CUtensorMap&, const CUten
                         const GemmParams&, cudaStream_t);
 void gemm_launch_256_kk(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
                         const GemmParams&, cudaStream_t);
+void gemm_launch_192_kk(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_192_kn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
+void gemm_launch_192_nn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
+                        const GemmParams&, cudaStream_t);
 void gemm_launch_256_kn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
                         const GemmParams&, cudaStream_t);
 void gemm_launch_256_nn(int, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&, const CUtensorMap&,
@@ -65,7 +71,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   TORCH_CHECK(c.scalar_type() == (out_bf16 ? at::kBFloat16 : at::kFloat), "gemm: wrong output dtype for epilogue");
   if (M == 0 || N == 0) return;
   if (K == 0) TORCH_CHECK(false, "gemm: K == 0 not supported");
-  const int BN = (block_n == 256) ? 256 : 128;
+  const int BN = (block_n == 256) ? 256 : (block_n == 192 ? 192 : 128);
 
   GemmParams p{};
   p.M = M;
@@ -222,6 +228,10 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
     if (!a_mn && !b_mn) gemm_launch_256_kk(e, ta, tb, tc, tx, p, s);
     else if (!a_mn) gemm_launch_256_kn(e, ta, tb, tc, tx, p, s);
     else gemm_launch_256_nn(e, ta, tb, tc, tx, p, s);
+  } else if (BN == 192) {
+    if (!a_mn && !b_mn) gemm_launch_192_kk(e, ta, tb, tc, tx, p, s);
+    else if (!a_mn) gemm_launch_192_kn(e, ta, tb, tc, tx, p, s);
+    else gemm_launch_192_nn(e, ta, tb, tc, tx, p, s);
   } else {
     if (!a_mn && !b_mn) gemm_launch_128_kk(e, ta, tb, tc, tx, p, s);
     else if (!a_mn) gemm_launch_128_kn(e, ta, tb, tc, tx, p, s);

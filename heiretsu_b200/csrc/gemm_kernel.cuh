@@ -40,8 +40,9 @@ struct GemmCfg {
   static constexpr int A_BYTES = BM * BK * 2;
   static constexpr int B_BYTES = BN * BK * 2;
   static constexpr int STAGE_BYTES = A_BYTES + B_BYTES;
-  static constexpr int STAGES = (BN >= 256) ? 4 : 6;
-  static constexpr int TMEM_COLS = 2 * BN;
+  static constexpr int STAGES = (BN >= 192) ? 4 : 6;
+  // two accumulators of BN columns; TMEM is allocated in powers of two
+  static constexpr int TMEM_COLS = (2 * BN <= 256) ? 256 : 512;
   static constexpr int STG_OFFSET = STAGES * STAGE_BYTES;  // per-warp epilogue staging tiles
   static constexpr int SMEM_BYTES = STAGES * STAGE_BYTES + kEpiWarps * kStgBytes + 1024 /*align*/ + 256 /*barriers*/;
 };

@@ -21,7 +21,7 @@ SHAPES = [(256, 256, 128), (8192, 2304, 768), (300, 200, 136), (128, 50304, 768)
 
 
 @pytest.mark.parametrize("M,N,K", SHAPES)
-@pytest.mark.parametrize("bn", [128, 256])
+@pytest.mark.parametrize("bn", [128, 192, 256])
 def test_fwd_bias(M, N, K, bn):
     g, check = _ops()
     torch.manual_seed(0)
