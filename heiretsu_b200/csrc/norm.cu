@@ -298,6 +298,48 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
   }
 }
 
+// Wide variant (N % 8 == 0, 16-byte aligned rows): each lane sums 8 columns
+// (one 16-byte load per row), a CTA covers 256 columns, and every warp keeps
+// 8 row loads in flight; warps combine through shared memory, then one
+// atomic per column per CTA.
+__global__ void __launch_bounds__(256) colsum_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, long ld, int M,
+                                                               int N, int rows_per_cta, float* __restrict__ out) {
+  __shared__ float red[8][256 + 8];
+  const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
+  const int c0 = blockIdx.x * 256 + lane * 8;
+  const int r0 = blockIdx.y * rows_per_cta;
+  const int r1 = min(M, r0 + rows_per_cta);
+  float acc[8] = {0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f, 0.f};
+  if (c0 < N) {
+    int r = r0 + warp;
+    for (; r + 7 * 8 < r1; r += 64) {
+      uint4 v[8];
+#pragma unroll
+      for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const uint4*>(in + (long)(r + 8 * u) * ld + c0));
+#pragma unroll
+      for (int u = 0; u < 8; ++u) {
+        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[u]);
+#pragma unroll
+        for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]);
+      }
+    }
+    for (; r < r1; r += 8) {
+      const uint4 v = __ldg(reinterpret_cast<const uint4*>(in + (long)r * ld + c0));
+      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+#pragma unroll
+      for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]);
+    }
+  }
+#pragma unroll
+  for (int j = 0; j < 8; ++j) red[warp][lane * 8 + j] = acc[j];
+  __syncthreads();
+  float sum = 0.f;
+#pragma unroll
+  for (int q = 0; q < 8; ++q) sum += red[q][threadIdx.x];
+  const int cc = blockIdx.x * 256 + threadIdx.x;
+  if (cc < N) atomicAdd(out + cc, sum);
+}
+
 // ----------------------------------------------------------------------------
 // Host launchers (raw pointers; the torch-facing checks live in ops_host.cpp)
 // ----------------------------------------------------------------------------
@@ -398,6 +440,13 @@ void dropout_bf16_launch(const float* g, __nv_bfloat16* out, long M, int H, cons
 
 void colsum_bf16_launch(const __nv_bfloat16* in, long ld, int M, int N, float* out, cudaStream_t s) {
   if (M == 0 || N == 0) return;
+  if (N % 8 == 0 && ld % 8 == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0) {
+    const int rows_per_cta = 64;
+    dim3 grid((N + 255) / 256, (M + rows_per_cta - 1) / rows_per_cta);
+    colsum_bf16_wide_kernel<<<grid, 256, 0, s>>>(in, ld, M, N, rows_per_cta, out);
+    HB_CUDA_CHECK(cudaGetLastError());
+    return;
+  }
   const int rows_per_cta = 256;
   dim3 grid((N + 63) / 64, (M + rows_per_cta - 1) / rows_per_cta);
   colsum_bf16_kernel<<<grid, 256, 0, s>>>(in, ld, M, N, rows_per_cta, out);

@@ -182,6 +182,12 @@ def bench_norm(flush):
     db = torch.zeros(H, device="cuda")
     t = time_fn(lambda: K.layernorm_bwd(dy, x, mean, rstd, w, dres, dres, d16, dg, db), flush=flush)
     rows.append(dict(op="layernorm", name="bwd", ms=t, gbs=(M * H * 18) / t / 1e6))
+    # bias gradients: column sums of the bf16 output gradients (dqkv width)
+    g16 = torch.randn(M, 3 * H, device="cuda").bfloat16()
+    acc = torch.zeros(3 * H, device="cuda")
+    t = time_fn(lambda: K.colsum_bf16(g16, acc), flush=flush)
+    tr = time_fn(lambda: g16.float().sum(0), flush=flush)
+    rows.append(dict(op="colsum", name=f"{M}x{3 * H}", ms=t, ref_ms=tr, gbs=(M * 3 * H * 2) / t / 1e6))
     return rows
 
 
