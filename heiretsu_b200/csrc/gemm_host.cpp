@@ -135,11 +135,14 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
     p.grp_b_off = static_cast<int>(grp_b_off);
     p.grp_c_off = static_cast<int>(grp_c_off);
   }
-  // Only outputs smaller than one wave are split: for larger ones the atomic
-  // traffic (splits x M x N x 4 bytes through L2) costs more than the tail wave.
+  // Outputs smaller than one wave are split; larger outputs only when K is
+  // long (>= 64 k-blocks per split, e.g. the lm_head dgrad over the vocabulary),
+  // where the splits' bulk fp32 reduce-adds (splits x M x N x 4 bytes through
+  // L2) are small next to the tail wave they remove.
   const int sms_dev = num_sms(a.get_device());
   const long tiles_mn = (long)((M + 127) / 128) * ((N + BN - 1) / BN);
-  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 8 && tiles_mn < sms_dev && ag_src.empty() &&
+  const int min_kb_per_split = (tiles_mn < sms_dev) ? 4 : 64;
+  if ((epi == kEpiF32 || epi == kEpiF32Acc) && num_kb >= 2 * min_kb_per_split && ag_src.empty() &&
       rs_dst.empty() && grp_mode == 0) {
     const int sms = sms_dev;
     const long tiles = tiles_mn;
@@ -150,7 +153,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
     };
     int best = 1;
     double best_eff = eff(1);
-    for (int sp = 2; sp <= 16 && num_kb / sp >= 4; ++sp) {
+    for (int sp = 2; sp <= 16 && num_kb / sp >= min_kb_per_split; ++sp) {
       const double e = eff(sp);
       if (e > best_eff + 0.08) {
         best = sp;

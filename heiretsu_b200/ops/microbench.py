@@ -3,8 +3,10 @@ counterparts on the GPT-2 shapes (M = 8 x 1024 tokens).
 
     python -m heiretsu_b200.ops.microbench [--only gemm] [--shape fc_gelu] [--reps 20 --warmup 5] [--json out.json]
 
-Timing: CUDA events on the launching stream, warm-up first, L2 flushed by
-writing a 256 MB buffer before every timed launch, median of the repeats.
+Timing: CUDA events around CUDA-graph replays of the op (host launch work
+excluded, as in the graph-replayed training step), warm-up first, L2
+flushed by writing a 256 MB buffer before every timed replay, median of the
+repeats. PyTorch / cuBLAS references are timed the same way.
 """
 from __future__ import annotations
 
@@ -23,12 +25,24 @@ REPS, WARMUP = 20, 5
 SHAPE = None
 
 
-def time_fn(fn, reps=None, warmup=None, flush=None):
+def time_fn(fn, reps=None, warmup=None, flush=None, graph=True):
+    """Median device time of fn. With graph=True (default) fn is captured in a
+    CUDA graph and the replays are timed, so host-side launch work (argument
+    checks, tensor-map encoding) is not counted -- the training step replays a
+    graph too. Both our kernels and the PyTorch references are timed this way."""
     reps = REPS if reps is None else reps
     warmup = WARMUP if warmup is None else warmup
     for _ in range(warmup):
         fn()
     torch.cuda.synchronize()
+    run = fn
+    if graph:
+        g = torch.cuda.CUDAGraph()
+        with torch.cuda.graph(g):
+            fn()
+        run = g.replay
+        run()
+        torch.cuda.synchronize()
     times = []
     for _ in range(reps):
         if flush is not None:
@@ -36,7 +50,7 @@ def time_fn(fn, reps=None, warmup=None, flush=None):
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()
-        fn()
+        run()
         e.record()
         torch.cuda.synchronize()
         times.append(s.elapsed_time(e))
@@ -153,7 +167,8 @@ def bench_attention(flush):
     qg, kg, vg = (x.detach().requires_grad_(True) for x in (q, k, v))
     o = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
     g = torch.randn_like(o)
-    tr = time_fn(lambda: torch.autograd.grad(o, (qg, kg, vg), g, retain_graph=True), flush=flush)
+    # (autograd runs on its own threads and cannot be graph-captured; timed eagerly)
+    tr = time_fn(lambda: torch.autograd.grad(o, (qg, kg, vg), g, retain_graph=True), flush=flush, graph=False)
     rows.append(dict(op="attention", name="bwd", ms=t, ref_ms=tr, tflops=2.5 * fwd_flops / t / 1e9,
                      ref_tflops=2.5 * fwd_flops / tr / 1e9))
     check_status()
