@@ -47,9 +47,14 @@ def _worker_tp_dp(rank, world, dp, tp, moe, ep):
     # every DP rank gets its own batch; the dense oracle sees their concatenation
     xs = [_batch(100 + d) for d in range(dp)]
     x, y = xs[topo.dp_rank]
-    full_x = torch.cat([a for a, _ in xs])
-    full_y = torch.cat([b for _, b in xs])
-    full_state, dense_grads, dense_loss = _dense_grads(cfg_kw, full_x, full_y)
+    # Dense oracle: the mean over DP ranks of the dense model on each rank's
+    # batch (the MoE aux loss is per rank, as in the reference, and is not
+    # linear in the token statistics, so it differs from the aux loss of the
+    # concatenated batch).
+    per = [_dense_grads(cfg_kw, bx, by) for bx, by in xs]
+    full_state = per[0][0]
+    dense_grads = {k: sum(g[k] for _, g, _ in per) / dp for k in per[0][1]}
+    dense_loss = sum(l for _, _, l in per) / dp
     model = GPT(GPTConfig(**cfg_kw), topo=topo)
     load_from_full(model, full_state, topo.tp_rank, topo.tp)
     _, loss, aux = model(x, y)
@@ -69,7 +74,7 @@ def _worker_tp_dp(rank, world, dp, tp, moe, ep):
 
 
 @pytest.mark.parametrize("dp,tp,moe,ep", [(2, 1, False, 1), (1, 2, False, 1), (2, 2, False, 1), (1, 1, True, 2),
-                                          (1, 2, True, 2)])
+                                          (1, 2, True, 2), (2, 2, True, 2)])  # last: the 8-rank MoE 4-D layout
 def test_parallel_matches_dense(dp, tp, moe, ep):
     world = dp * tp * ep
     res = run_ranks(_worker_tp_dp, world, dp, tp, moe, ep)
