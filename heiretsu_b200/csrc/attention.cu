@@ -776,12 +776,13 @@ static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
 void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, long ld_out, float* lse, int B,
                      int T, int nh, int Tpad, const DropoutArgs& drop, int h0, int nh_total, int* status,
                      cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64] = {};  // the shared-memory opt-in is per device
+  const int dev = current_device();
+  if (!attr[dev]) {
     HB_CUDA_CHECK(
         cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
     HB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
-    attr = true;
+    attr[dev] = true;
   }
   AttnParams p{};
   p.drop = drop;
@@ -807,12 +808,13 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
                      const __nv_bfloat16* dO, long ld_do, const float* lse, float* dvec, float* dq_acc,
                      __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, const DropoutArgs& drop,
                      int h0, int nh_total, int* status, cudaStream_t s) {
-  static bool attr = false;
-  if (!attr) {
+  static bool attr[64] = {};  // the shared-memory opt-in is per device
+  const int dev = current_device();
+  if (!attr[dev]) {
     HB_CUDA_CHECK(
         cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
     HB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
-    attr = true;
+    attr[dev] = true;
   }
   const int Hs = nh * kD;
   const long rows = (long)B * T;

@@ -35,6 +35,18 @@ from .flat import FlatParams
 BUCKET_ELEMS = 32 * 1024 * 1024  # 128 MB fp32 per bucket
 
 
+def uncovered_ranges(done: List[Tuple[int, int]], n: int) -> List[Tuple[int, int]]:
+    """The parts of [0, n) not covered by the (possibly overlapping) ranges in ``done``."""
+    rest, pos = [], 0
+    for a, b in sorted(done):
+        if a > pos:
+            rest.append((pos, a))
+        pos = max(pos, b)
+    if pos < n:
+        rest.append((pos, n))
+    return rest
+
+
 class FlatGradReducer:
     def __init__(self, flat: FlatParams, group: Optional[dist.ProcessGroup], topo=None,
                  backend: Optional[str] = None, bucket_elems: int = BUCKET_ELEMS):
@@ -112,14 +124,7 @@ class FlatGradReducer:
         from ..models import fused as F
         F.set_block_done_hook(None)
         self._armed = False
-        done = sorted(self._done)
-        rest, pos = [], 0
-        for a, b in done:
-            if a > pos:
-                rest.append((pos, a))
-            pos = max(pos, b)
-        if pos < self.flat.numel:
-            rest.append((pos, self.flat.numel))
+        rest = uncovered_ranges(self._done, self.flat.numel)
         ev = torch.cuda.Event()
         ev.record()
         self._side.wait_event(ev)

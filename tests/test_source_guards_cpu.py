@@ -42,7 +42,7 @@ def test_no_forbidden_constructs():
 
 
 def test_every_device_spin_is_bounded():
-    """Every mbarrier / flag wait loop in the kernels carries a time budget."""
+    """Every mbarrier / flag wait loop in the kernels carries a time limit."""
     offenders = []
     checked = 0
     for path in _sources():

@@ -222,3 +222,87 @@ def test_dropout_reference_hash():
     assert abs((m == 0).double().mean().item() - 0.2) < 0.01
     assert not torch.equal(m, residual_mask(8, 3, 256, 128, 0.2))  # seed changes the mask
     assert not torch.equal(m, residual_mask(7, 4, 256, 128, 0.2))  # so does the site
+
+
+def test_uncovered_ranges():
+    from heiretsu_b200.parallel.grad_reduce import uncovered_ranges
+
+    assert uncovered_ranges([], 10) == [(0, 10)]
+    assert uncovered_ranges([(2, 4), (6, 8)], 10) == [(0, 2), (4, 6), (8, 10)]
+    assert uncovered_ranges([(0, 5), (3, 10)], 10) == []
+    assert uncovered_ranges([(6, 8), (0, 2)], 8) == [(2, 6)]
+
+
+def test_flat_params_grouping_and_block_ranges():
+    import torch
+
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.models.gpt import GPT
+    from heiretsu_b200.parallel.flat import ALIGN, FlatParams
+    from heiretsu_b200.parallel.grad_reduce import FlatGradReducer
+
+    cfg = GPTConfig(block_size=16, vocab_size=64, n_layer=2, n_head=2, n_embed=32, num_experts=4, top_k=2,
+                    moe_freq=2)
+    torch.manual_seed(0)
+    m = GPT(cfg)
+    before = {n: p.detach().clone() for n, p in m.named_parameters()}
+    # three classes: expert weights (weight 1, summed over TP), LayerNorms (0.5, summed), the rest (0.5, not)
+    weight_of = lambda n, p: 1.0 if ".experts." in n else 0.5
+    tp_sum_of = lambda n, p: ".experts." in n or ".ln_" in n
+    flat = FlatParams(m, torch.device("cpu"), weight_of=weight_of, tp_sum_of=tp_sum_of)
+    assert [(w, t) for (_, _, w), t in zip(flat.ranges, flat.tp_sum)] == [(0.5, False), (0.5, True), (1.0, True)]
+    for (a, b, w), t in zip(flat.ranges, flat.tp_sum):
+        for n, p, off in zip(flat.names, flat.params, flat.offsets):
+            if a <= off < b:
+                assert weight_of(n, p) == w and tp_sum_of(n, p) == t
+                assert off % ALIGN == 0
+    for n, p in m.named_parameters():  # values survive the move into the flat buffer
+        assert torch.equal(p.detach(), before[n])
+    # the experts of the MoE layer are stored back to back (one grouped-GEMM weight matrix)
+    ex = m.tr.h[1].moe.expert_group.experts
+    w1, g1 = flat.stacked([e.w1.weight for e in ex])
+    assert w1.shape == (4 * ex[0].w1.weight.shape[0], ex[0].w1.weight.shape[1])
+    assert torch.equal(w1[: ex[0].w1.weight.shape[0]], ex[0].w1.weight.detach().bfloat16())
+
+    # per-block gradient ranges of the overlapped reducer: sorted, disjoint, covering every parameter
+    red = FlatGradReducer.__new__(FlatGradReducer)
+    red.flat, red._range_cache = flat, {}
+    for blk in m.tr.h:
+        rs = red._ranges_of(blk)
+        assert rs == sorted(rs) and all(a < b for a, b in rs)
+        assert all(b1 <= a2 for (_, b1), (a2, _) in zip(rs, rs[1:]))
+        idx = {id(p): i for i, p in enumerate(flat.params)}
+        for p in blk.parameters():
+            off = flat.offsets[idx[id(p)]]
+            assert any(a <= off and off + p.numel() <= b for a, b in rs)
+
+
+def test_dropout_seed_snapshots():
+    import torch
+
+    from heiretsu_b200.models.fused import _dropout_of, _snapshot_dropout_seeds
+
+    class Blk(torch.nn.Module):
+        pass
+
+    seed = torch.tensor([41], dtype=torch.int32)
+    blocks = [Blk(), Blk(), Blk()]
+    for i, b in enumerate(blocks[:2]):
+        b._hb_dropout = (seed, i, 0.1)
+    _snapshot_dropout_seeds(blocks)
+    assert int(seed.item()) == 42  # advanced once per forward, not per block
+    d0, d1 = _dropout_of(blocks[0]), _dropout_of(blocks[1])
+    assert d0[0] is d1[0] and int(d0[0].item()) == 41 and (d0[1], d1[1]) == (0, 1)
+    assert _dropout_of(blocks[2]) is None  # no dropout configured
+    for b in blocks:
+        b.eval()
+    _snapshot_dropout_seeds(blocks)
+    assert int(seed.item()) == 42 and all(_dropout_of(b) is None for b in blocks)  # eval: off, no advance
+
+
+def test_gemm_tile_width_policy():
+    from heiretsu_b200.ops import gemm as g
+
+    assert g._bn(50304) == 256 and g._bn(2304) == 256 and g._bn(768) == 128 and g._bn(136) == 128
+    assert g._bn_f32_out(768) == 192 and g._bn_f32_out(1536) == 192
+    assert g._bn_f32_out(384) == 128 and g._bn_f32_out(3072) == 256 and g._bn_f32_out(1000) == 128
