@@ -484,11 +484,21 @@ def main(argv=None) -> None:
                     aux_loss_coef=args.aux_loss_coef)
     engine = Engine(args, topo, device, cfg)
     module = engine.module
+    start_step = 1
+    resume_side = None
     if args.resume:
         obj = load_checkpoint(module, args.resume)
         engine.after_load()
+        start_step = int(obj.get("step", 0)) + 1
+        from .utils.ckpt import sidecar_path
+        side = sidecar_path(args.resume)
+        if os.path.exists(side):
+            resume_side = torch.load(side, map_location="cpu", weights_only=False)
+            opt_state = resume_side.get("optimizer", resume_side)
+            engine.optimizer.load_state_dict(opt_state)
         if rank == 0:
-            print(f"[resume] loaded {args.resume} (step {obj.get('step')})")
+            print(f"[resume] loaded {args.resume} (step {obj.get('step')})"
+                  f"{'; optimizer, RNG and data position from ' + side if resume_side else ''}")
     n_params = sum(p.numel() for p in module.parameters())
     if rank == 0:
         print(f"[model] parameters: {n_params:,} ({n_params / 1e6:.1f}M) | engine="
@@ -518,6 +528,14 @@ def main(argv=None) -> None:
         val_loader = RandomBatchLoader(args.data_dir, "val", args.batch_size, args.block_size, args.num_val_chunks,
                                        seed=args.seed + 999, rank=0, dp_rank=0, dp_size=1, log_rank=rank)
 
+    if resume_side is not None:
+        from .utils.ckpt import set_rng_state
+        if "rng" in resume_side:
+            set_rng_state(resume_side["rng"])
+        if "train_loader" in resume_side and hasattr(train_loader, "load_state_dict"):
+            train_loader.load_state_dict(resume_side["train_loader"])
+        if "dropout_seed" in resume_side and engine.dropout_seed is not None:
+            engine.dropout_seed.fill_(int(resume_side["dropout_seed"]))
     is_main = topo.is_main
     if is_main:
         print(f"device={device} | world_size={topo.world_size} | dp={topo.dp} ep={topo.ep} tp={topo.tp} "
@@ -537,7 +555,7 @@ def main(argv=None) -> None:
         from .utils.fault import StepWatchdog, default_store
         wd = StepWatchdog(default_store(), dist.get_rank(), dist.get_world_size(), timeout_s=args.watchdog_s)
     try:
-        _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0)
+        _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0, start_step)
     except BaseException as e:
         if wd is not None:
             wd.mark_failed(f"{type(e).__name__}: {e}")
@@ -558,7 +576,7 @@ def main(argv=None) -> None:
         cleanup()
 
 
-def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0) -> None:
+def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0, start_step=1) -> None:
     from .utils.profiling import RegionTimer
 
     is_main = topo.is_main
@@ -567,7 +585,7 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
     log_every = args.log_interval or max(1, args.eval_interval // 10)
     timer = RegionTimer(enabled=bool(args.device_timing) and engine.device.type == "cuda")
     timed_steps = 0
-    for step in range(1, args.max_iters + 1):
+    for step in range(start_step, args.max_iters + 1):
         if wd is not None:
             wd.check()  # a failed peer is noticed here, before this step launches anything
         with timer.region("step"):
@@ -579,7 +597,7 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
         dt = now - last
         last = now
         eff = tokens_per_step / dt if dt > 0 else float("inf")
-        if step % log_every == 0 or step == 1:
+        if step % log_every == 0 or step == start_step:
             dev_str = ""
             if timer.enabled:
                 # every rank takes part in the max over ranks; all log on the same steps
@@ -607,8 +625,13 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
                 if run:
                     wandb.log({"eval/loss": ev, "step": step}, step=step)
         if args.save_interval and step % args.save_interval == 0:
-            save_checkpoint(module, cfg, step, topo, args.out_dir,
-                            optimizer_state=engine.optimizer.state_dict() if engine.fused else None)
+            from .utils.ckpt import rng_state
+            side = {"optimizer": engine.optimizer.state_dict(), "rng": rng_state()}
+            if engine.dropout_seed is not None:  # fused dropout masks continue where they stopped
+                side["dropout_seed"] = int(engine.dropout_seed.item())
+            if hasattr(train_loader, "state_dict"):
+                side["train_loader"] = train_loader.state_dict()
+            save_checkpoint(module, cfg, step, topo, args.out_dir, optimizer_state=side)
 
 
 def expert_load_metrics(module) -> dict:

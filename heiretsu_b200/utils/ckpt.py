@@ -37,8 +37,35 @@ def save_checkpoint(module: torch.nn.Module, cfg, step: int, topo, out_dir: str 
     path = os.path.join(out_dir, ckpt_name(step, topo))
     torch.save(obj, path)
     if optimizer_state is not None:
-        torch.save(optimizer_state, os.path.join(out_dir, "optim_" + ckpt_name(step, topo)[len("ckpt_"):]))
+        torch.save(optimizer_state, sidecar_path(path))
     return path
+
+
+def sidecar_path(ckpt_path: str) -> str:
+    """``.../ckpt_X.pt`` -> ``.../optim_X.pt`` (optimizer / RNG / data-position state)."""
+    d, b = os.path.split(ckpt_path)
+    return os.path.join(d, "optim_" + (b[len("ckpt_"):] if b.startswith("ckpt_") else b))
+
+
+def rng_state() -> dict:
+    import random
+
+    import numpy as np
+    st = {"python": random.getstate(), "numpy": np.random.get_state(), "torch": torch.get_rng_state()}
+    if torch.cuda.is_available() and torch.cuda.is_initialized():
+        st["cuda"] = torch.cuda.get_rng_state()
+    return st
+
+
+def set_rng_state(st: dict) -> None:
+    import random
+
+    import numpy as np
+    random.setstate(st["python"])
+    np.random.set_state(st["numpy"])
+    torch.set_rng_state(st["torch"])
+    if "cuda" in st and torch.cuda.is_available():
+        torch.cuda.set_rng_state(st["cuda"])
 
 
 def load_checkpoint(module: torch.nn.Module, path: str, strict: bool = True) -> dict:

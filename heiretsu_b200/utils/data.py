@@ -81,6 +81,13 @@ class RandomBatchLoader:
         nb = self.pin and torch.device(device).type == "cuda"
         return x.to(device, non_blocking=nb), y.to(device, non_blocking=nb)
 
+    # data position for exact resume (the state of the sampling RNG)
+    def state_dict(self) -> dict:
+        return {"rng": self.rng.getstate()}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.rng.setstate(sd["rng"])
+
 
 class SyntheticLoader:
     """Uniform-random token ids; y is x shifted by one within a (T+1)-token draw.
@@ -121,6 +128,12 @@ class SyntheticLoader:
         ev.record()
         self._events[slot] = ev
         return dev_xy[0], dev_xy[1]
+
+    def state_dict(self) -> dict:
+        return {"gen": self.gen.get_state()}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.gen.set_state(sd["gen"])
 
 
 def write_synthetic_bins(data_dir: str, vocab_size: int = 50257, train_tokens: int = 8_000_000,
