@@ -617,6 +617,12 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
             if args.num_experts > 0:
                 log["train/aux_loss"] = float(aux.item())
                 log.update(expert_load_metrics(module))
+                counts = expert_counts(module)
+                if counts is not None and hasattr(wandb, "Table"):
+                    table = wandb.Table(data=[[f"E{i}", float(c)] for i, c in enumerate(counts.tolist())],
+                                        columns=["Expert", "Tokens"])
+                    log["expert_load/distribution"] = wandb.plot.bar(table, "Expert", "Tokens",
+                                                                     title=f"Expert Load (step {step})")
             wandb.log(log, step=step)
         if step % args.eval_interval == 0 or step == args.max_iters:
             ev = engine.estimate_loss(val_loader, args.eval_iters)
@@ -634,14 +640,20 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
             save_checkpoint(module, cfg, step, topo, args.out_dir, optimizer_state=side)
 
 
-def expert_load_metrics(module) -> dict:
-    """Per-expert token counts summed over MoE layers (reference train.py:359-370, :478-499)."""
+def expert_counts(module):
+    """Per-expert token counts [E] summed over the MoE layers, or None (reference train.py:359-370)."""
     from .models.moe import MoELayer
 
     total = None
     for m in module.modules():
         if isinstance(m, MoELayer) and m._expert_counts is not None:
             total = m._expert_counts.float().clone() if total is None else total + m._expert_counts.float()
+    return total
+
+
+def expert_load_metrics(module) -> dict:
+    """Expert-load scalars of the reference's wandb log (train.py:478-494)."""
+    total = expert_counts(module)
     if total is None:
         return {}
     out = {}
