@@ -306,3 +306,24 @@ def test_gemm_tile_width_policy():
     assert g._bn(50304) == 256 and g._bn(2304) == 256 and g._bn(768) == 128 and g._bn(136) == 128
     assert g._bn_f32_out(768) == 192 and g._bn_f32_out(1536) == 192
     assert g._bn_f32_out(384) == 128 and g._bn_f32_out(3072) == 256 and g._bn_f32_out(1000) == 128
+
+
+def test_commbench_work_and_roofline():
+    from heiretsu_b200.parallel import commbench as C
+    from heiretsu_b200.utils.roofline import Peaks
+
+    # reduce-scatter + all-gather moves 2 (N-1)/N of the buffer per GPU and direction
+    assert C.dp_reduce_bytes(1000, 8) == 2 * 7 / 8 * 4000
+    assert C.dp_reduce_bytes(1000, 2) == 4000
+    f, b = C.tp_ag_gemm_work(8192, 3072, 1024, 4)
+    assert f == 2 * 8192 * 768 * 1024 and b == 0.75 * 8192 * 1024 * 2
+    f, b = C.tp_gemm_rs_work(8192, 1024, 4096, 4)
+    assert f == 2 * 8192 * 1024 * 1024 and b == 0.75 * 8192 * 1024 * 2
+    assert C.ep_combine_bytes(8192, 768, 2) == 8192 * 768 * 4
+    peaks = Peaks(6650.0, 1590.0, 1400.0, "of fallback")
+    rows = C.attach_roofline([dict(case="dp_reduce", shape="x", ms=2.0, ref_ms=4.0, flops=0.0,
+                                   nvlink_bytes=770e9 * 1e-3)], peaks)
+    r = rows[0]
+    assert abs(r["target_ms"] - 1.0) < 1e-9 and abs(r["frac"] - 0.5) < 1e-9 and abs(r["ref_frac"] - 0.25) < 1e-9
+    assert abs(r["nvlink_gbs"] - 385.0) < 1e-6
+    assert "of fallback" in r["label"] and "| dp_reduce |" in C.table(rows)
