@@ -90,6 +90,7 @@ def _full_key(local_key: str, module) -> str:
     """Map a key of a GPT / StageModule shard to the dense GPT's key."""
     from ..parallel.pipeline import StageModule
 
+    orig = local_key  # submodule lookups use the shard's own names
     if isinstance(module, StageModule):
         if local_key.startswith("blocks."):
             rest = local_key[len("blocks."):]
@@ -100,7 +101,7 @@ def _full_key(local_key: str, module) -> str:
     if ".moe.expert_group.experts." in local_key:
         pre, rest = local_key.split(".moe.expert_group.experts.", 1)
         j, tail = rest.split(".", 1)
-        group = module.get_submodule(f"{local_key.split('.moe.')[0]}.moe.expert_group")
+        group = module.get_submodule(f"{orig.split('.moe.')[0]}.moe.expert_group")
         local_key = f"{pre}.moe.expert_group.experts.{group.ep_rank * group.num_local_experts + int(j)}.{tail}"
     return local_key
 

@@ -74,7 +74,8 @@ def _worker_tp_dp(rank, world, dp, tp, moe, ep):
 
 
 @pytest.mark.parametrize("dp,tp,moe,ep", [(2, 1, False, 1), (1, 2, False, 1), (2, 2, False, 1), (1, 1, True, 2),
-                                          (1, 2, True, 2), (2, 2, True, 2)])  # last: the 8-rank MoE 4-D layout
+                                          (1, 2, True, 2), (2, 2, True, 2),  # the 8-rank MoE 4-D layout
+                                          (4, 1, False, 1), (1, 4, False, 1), (2, 1, True, 4)])
 def test_parallel_matches_dense(dp, tp, moe, ep):
     world = dp * tp * ep
     res = run_ranks(_worker_tp_dp, world, dp, tp, moe, ep)
@@ -83,14 +84,19 @@ def test_parallel_matches_dense(dp, tp, moe, ep):
         assert gerr < 1e-5, (rank, gerr, worst)
 
 
-def _worker_pp(rank, world, pp, tp, accum):
+def _worker_pp(rank, world, pp, tp, accum, dp=1, ep=1, moe=False):
+    import torch.distributed as dist
+
     from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.parallel.dp import average_gradients
     from heiretsu_b200.parallel.pipeline import GPipeEngine, StageModule
     from heiretsu_b200.topo import init_topology
-    from heiretsu_b200.utils.ckpt import load_from_full
+    from heiretsu_b200.utils.ckpt import load_from_full, shard_from_full
 
-    topo = init_topology(dp=1, tp=tp, pp=pp)
-    batches = [_batch(200 + m) for m in range(accum)]
+    cfg_kw = dict(CFG, **(dict(num_experts=4, top_k=2, moe_freq=2) if moe else {}))
+    topo = init_topology(dp=dp, ep=ep, tp=tp, pp=pp)
+    per_dp = [[_batch(200 + 10 * d + m) for m in range(accum)] for d in range(dp)]
+    batches = per_dp[topo.dp_rank]
 
     class L:
         B = 4
@@ -103,21 +109,28 @@ def _worker_pp(rank, world, pp, tp, accum):
             self.i += 1
             return b
 
-    # dense oracle: mean over microbatches of (loss)/accum accumulated
-    dense = _dense(CFG)
-    full_state = dense.state_dict()
-    tot = 0.0
-    for x, y in batches:
-        _, l, a = dense(x, y)
-        ((l + a) / accum).backward()
-        tot += l.item() / accum
-    stage = StageModule(GPTConfig(**CFG), topo, topo.pp_rank, topo.pp)
+    # Dense oracle: for each DP rank, the mean over its microbatches of loss
+    # (+ aux) accumulated; gradients and losses then averaged over DP ranks.
+    grads, tot = None, 0.0
+    for d in range(dp):
+        dense = _dense(cfg_kw)
+        full_state = dense.state_dict()
+        for x, y in per_dp[d]:
+            _, l, a = dense(x, y)
+            ((l + a) / accum).backward()
+            tot += l.item() / accum / dp
+        g = {n: p.grad.clone() / dp for n, p in dense.named_parameters()}
+        grads = g if grads is None else {k: grads[k] + g[k] for k in g}
+    stage = StageModule(GPTConfig(**cfg_kw), topo, topo.pp_rank, topo.pp)
     load_from_full(stage, full_state, topo.tp_rank, topo.tp)
     eng = GPipeEngine(stage, topo)
     loss, _ = eng.forward_backward(L(), accum, torch.device("cpu"), False, torch.bfloat16, None, 4)
-    from heiretsu_b200.utils.ckpt import shard_from_full
-    dgrads = {n: p.grad for n, p in dense.named_parameters()}
-    expect = shard_from_full(stage, {**full_state, **dgrads}, topo.tp_rank, topo.tp)
+    average_gradients(stage, topo.dp_group)
+    if loss is not None and topo.dp_group is not None:
+        loss = loss.detach().clone()
+        dist.all_reduce(loss, group=topo.dp_group)
+        loss /= topo.dp
+    expect = shard_from_full(stage, {**full_state, **grads}, topo.tp_rank, topo.tp)
     errs = []
     for n, p in stage.named_parameters():
         e = expect[n]
@@ -129,13 +142,15 @@ def _worker_pp(rank, world, pp, tp, accum):
         out["wte_grad"] = stage.wte.weight.grad.clone()
     if stage.is_last:
         out["head_grad"] = stage.lm_head.weight.grad.clone()
-    out["tied_dense"] = dgrads["tr.wte.weight"].clone()
+    out["tied_dense"] = grads["tr.wte.weight"].clone()
     return out
 
 
-@pytest.mark.parametrize("pp,tp", [(2, 1), (2, 2)])
-def test_pipeline_matches_dense(pp, tp):
-    res = run_ranks(_worker_pp, pp * tp, pp, tp, 2)
+# Layouts of the reference suite (tests/run_full_suite.sh:35-65): pp, tp, dp, ep, moe.
+@pytest.mark.parametrize("pp,tp,dp,ep,moe", [(2, 1, 1, 1, False), (2, 2, 1, 1, False), (4, 1, 1, 1, False),
+                                             (2, 1, 2, 1, False), (2, 2, 2, 1, False), (2, 2, 1, 2, True)])
+def test_pipeline_matches_dense(pp, tp, dp, ep, moe):
+    res = run_ranks(_worker_pp, pp * tp * dp * ep, pp, tp, 2, dp, ep, moe)
     for r in res:
         assert r["loss_err"] < 1e-5
         assert r["gerr"] < 1e-5
