@@ -158,3 +158,78 @@ def test_pipeline_matches_dense(pp, tp, dp, ep, moe):
     last = [r for r in res if "head_grad" in r][0]
     tied = first["wte_grad"] + last["head_grad"]
     assert (tied - first["tied_dense"]).abs().max().item() < 1e-5
+
+
+def _worker_curve(rank, world, dp, tp, pp, accum, steps):
+    """Five optimizer steps of the training engine (AdamW, global-norm clip) on
+    this layout; returns the logged losses and those of a single-process dense
+    engine fed the concatenation of the DP ranks' micro-batches."""
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.topo import init_topology
+    from heiretsu_b200.trainer import Engine, build_argparser
+    from heiretsu_b200.utils.ckpt import load_from_full
+
+    cfg = GPTConfig(**CFG)
+    flags = ["--batch_size", "4", "--block_size", "32", "--grad_accum_steps", str(accum), "--n_layer", "4",
+             "--n_head", "4", "--n_embed", "32", "--learning_rate", "3e-3", "--grad_clip", "0.5",
+             "--engine", "plain", "--amp", "none", "--device", "cpu"]
+    data = {(s, m, d): _batch(1000 + 97 * s + 13 * m + d) for s in range(steps) for m in range(accum)
+            for d in range(dp)}
+
+    class Feed:
+        def __init__(self, dps):
+            self.dps, self.i = dps, 0
+            self.B = 4 * len(dps)
+
+        def next_batch(self, device):
+            s, m = divmod(self.i, accum)
+            self.i += 1
+            xs = [data[(s, m, d)] for d in self.dps]
+            return torch.cat([x for x, _ in xs]), torch.cat([y for _, y in xs])
+
+    full_state = _dense(CFG).state_dict()
+    # dense single-process reference on the concatenated DP batches
+    eargs = build_argparser().parse_args(flags + ["--dp", "1"])
+    ref = Engine(eargs, _single_topo(), torch.device("cpu"), cfg)
+    load_from_full(ref.module, full_state)
+    if pp > 1:
+        # Pipeline stages keep separate embedding and lm_head copies (the reference's
+        # GPipe layout, pipeline.py:36-143), so the oracle unties them too.
+        m = ref.module
+        m.lm_head.weight = torch.nn.Parameter(m.tr.wte.weight.detach().clone())
+        ref.optimizer = torch.optim.AdamW(m.parameters(), lr=eargs.learning_rate, betas=tuple(eargs.betas),
+                                          weight_decay=eargs.weight_decay)
+    feed = Feed(list(range(dp)))
+    ref_losses = [float(ref.train_step(feed)[0]) for _ in range(steps)]
+
+    topo = init_topology(dp=dp, tp=tp, pp=pp)
+    args = build_argparser().parse_args(flags + ["--dp", str(dp), "--tp", str(tp), "--pp", str(pp)])
+    eng = Engine(args, topo, torch.device("cpu"), cfg)
+    load_from_full(eng.module, full_state, topo.tp_rank, topo.tp)
+    feed = Feed([topo.dp_rank])
+    losses = []
+    for _ in range(steps):
+        loss, _ = eng.train_step(feed)
+        losses.append(None if loss is None else float(loss))
+    return losses, ref_losses
+
+
+def _single_topo():
+    from heiretsu_b200.topo import Topology
+
+    return Topology(dp=1, ep=1, tp=1, pp=1, rank=0, world_size=1, dp_rank=0, ep_rank=0, pp_rank=0, tp_rank=0,
+                    tp_group=None, pp_group=None, ep_group=None, dp_group=None)
+
+
+@pytest.mark.parametrize("dp,tp,pp", [(2, 2, 1), (1, 2, 2), (2, 1, 2)])
+def test_five_step_loss_curve_matches_dense(dp, tp, pp):
+    res = run_ranks(_worker_curve, dp * tp * pp, dp, tp, pp, 2, 5)
+    checked = 0
+    for losses, ref in res:
+        assert ref[-1] < ref[0]
+        if losses[0] is None:  # pipeline stages before the last log no loss
+            continue
+        checked += 1
+        for a, b in zip(losses, ref):
+            assert abs(a - b) < 1e-4, (losses, ref)
+    assert checked >= 1
