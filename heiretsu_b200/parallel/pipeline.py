@@ -13,6 +13,11 @@ Differences, all deliberate:
 * Communication overlaps compute: the receive for microbatch m+1 is posted
   before microbatch m is computed, sends are not waited for until the end of
   the phase, and waits are stream waits (``Work.wait``), not host blocks.
+* Optional tied embeddings across stages (``TiedEmbeddings``, off by
+  default): the first stage's ``wte`` and the last stage's ``lm_head`` start
+  equal and their gradients are summed between the two stages every step, so
+  the pipeline model is the tied dense GPT. The reference unties them
+  (pipeline.py:75-92), which stays the default.
 """
 from __future__ import annotations
 
@@ -26,6 +31,54 @@ import torch.nn.functional as F
 
 from ..config import GPTConfig
 from ..topo import rank_from_coords
+
+
+def embedding_group(topo):
+    """(group, first-stage rank) of this rank's {first stage, last stage} pair with the
+    same (dp, ep, tp) coordinates, or None on a middle stage. Every rank creates every
+    pair's group, in the same order (torch.distributed.new_group requires it)."""
+    mine = None
+    for d in range(topo.dp):
+        for e in range(topo.ep):
+            for t in range(topo.tp):
+                pair = [rank_from_coords(d, e, p, t, topo.dp, topo.ep, topo.tp, topo.pp) for p in (0, topo.pp - 1)]
+                g = dist.new_group(ranks=pair)
+                if topo.rank in pair:
+                    mine = (g, pair[0])
+    return mine
+
+
+class TiedEmbeddings:
+    """Keeps the first stage's ``wte.weight`` and the last stage's ``lm_head.weight``
+    identical: ``sync_weights`` copies the first stage's table to the last stage (start,
+    checkpoint load) and ``reduce_grads`` sums the two gradients in place on both (before
+    clipping and the optimizer), so both copies take the same AdamW step."""
+
+    def __init__(self, stage: "StageModule", topo):
+        if topo.pp < 2:
+            raise ValueError("tied pipeline embeddings need pp >= 2")
+        got = embedding_group(topo)
+        self.group, self.src = got if got is not None else (None, None)
+        self.param = None
+        if stage.is_first:
+            self.param = stage.wte.weight
+        elif stage.is_last:
+            self.param = stage.lm_head.weight
+
+    def sync_weights(self) -> None:
+        if self.group is not None:
+            with torch.no_grad():
+                dist.broadcast(self.param.data, src=self.src, group=self.group)
+
+    def reduce_grads(self) -> None:
+        if self.group is None:
+            return
+        g = getattr(self.param, "main_grad", None)
+        if g is None:
+            g = self.param.grad
+        if g is None:
+            g = self.param.grad = torch.zeros_like(self.param)
+        dist.all_reduce(g, op=dist.ReduceOp.SUM, group=self.group)
 
 
 def _partition_layers(n_layer: int, pp: int) -> List[Tuple[int, int]]:

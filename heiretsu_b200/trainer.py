@@ -103,6 +103,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--engine", type=str, default="auto", choices=["auto", "fused", "plain"])
     p.add_argument("--clip_mode", type=str, default="global", choices=["global", "local"])
     p.add_argument("--pp_boundary_dtype", type=str, default="fp32", choices=["fp32", "bf16"])
+    p.add_argument("--pp_tie_embeddings", type=int, default=0, choices=[0, 1],
+                   help="pp > 1: keep the first stage's wte and the last stage's lm_head equal (gradients summed "
+                        "between the two stages), i.e. the tied dense GPT; 0 = the reference's untied stages")
     p.add_argument("--resume", type=str, default=None, help="checkpoint file to load before training")
     p.add_argument("--out_dir", type=str, default=".")
     p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
@@ -144,11 +147,15 @@ def mp_group_of(topo):
     return groups[topo.dp_rank]
 
 
-def replication_weight(topo):
-    """Norm weight of each parameter: 1 / (number of model-parallel ranks holding a copy)."""
+def replication_weight(topo, tied_pp: bool = False):
+    """Norm weight of each parameter: 1 / (number of model-parallel ranks holding a copy).
+    With tied pipeline embeddings the first stage's wte and the last stage's lm_head are
+    one parameter held twice."""
 
     def fn(name: str, p) -> float:
         w = 1.0
+        if tied_pp and topo.pp > 1 and name in ("wte.weight", "lm_head.weight"):
+            w /= 2
         tp_sharded = getattr(p, "tp_sharded", False)
         expert = ".experts." in name
         if topo.tp > 1 and not tp_sharded:
@@ -197,6 +204,11 @@ class Engine:
             self.module = GPT(cfg, topo=topo)
         mark_tp_sharded(self.module)
         self.module.to(device)
+        self.tied = None
+        if self.use_pipeline and getattr(args, "pp_tie_embeddings", 0):
+            from .parallel.pipeline import TiedEmbeddings
+            self.tied = TiedEmbeddings(self.module, topo)
+            self.tied.sync_weights()
         self.amp = args.amp if device.type == "cuda" else "none"
         from .models.fused import fused_supported
 
@@ -229,7 +241,7 @@ class Engine:
             from .parallel.flat import FlatParams
 
             use_p2p = topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
-            self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo),
+            self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo, self.tied is not None),
                                    grad_group=topo.dp_group if use_p2p else None,
                                    tp_group=topo.tp_group if topo.tp > 1 else None,
                                    tp_sum_of=lambda n, p: topo.tp > 1 and not getattr(p, "tp_sharded", False))
@@ -391,6 +403,8 @@ class Engine:
 
     def sync_and_step(self) -> None:
         args = self.args
+        if self.tied is not None:
+            self.tied.reduce_grads()
         if self.fused:
             self.tp_sync_grads()
             if self.reducer is not None:
@@ -415,7 +429,7 @@ class Engine:
         if self.args.clip_mode == "local" or self.mp_group is None:
             torch.nn.utils.clip_grad_norm_(params, max_norm)
             return
-        wfn = replication_weight(self.topo)
+        wfn = replication_weight(self.topo, self.tied is not None)
         names = {id(p): n for n, p in self.module.named_parameters()}
         tot = torch.zeros((), device=self.device)
         for p in params:
@@ -453,6 +467,8 @@ class Engine:
         return sum(losses) / len(losses) if losses else None
 
     def after_load(self) -> None:
+        if self.tied is not None:
+            self.tied.sync_weights()
         if self.flat is not None:
             self.flat.refresh_bf16()
 

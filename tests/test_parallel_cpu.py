@@ -160,7 +160,7 @@ def test_pipeline_matches_dense(pp, tp, dp, ep, moe):
     assert (tied - first["tied_dense"]).abs().max().item() < 1e-5
 
 
-def _worker_curve(rank, world, dp, tp, pp, accum, steps):
+def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0):
     """Five optimizer steps of the training engine (AdamW, global-norm clip) on
     this layout; returns the logged losses and those of a single-process dense
     engine fed the concatenation of the DP ranks' micro-batches."""
@@ -192,7 +192,7 @@ def _worker_curve(rank, world, dp, tp, pp, accum, steps):
     eargs = build_argparser().parse_args(flags + ["--dp", "1"])
     ref = Engine(eargs, _single_topo(), torch.device("cpu"), cfg)
     load_from_full(ref.module, full_state)
-    if pp > 1:
+    if pp > 1 and not tie:
         # Pipeline stages keep separate embedding and lm_head copies (the reference's
         # GPipe layout, pipeline.py:36-143), so the oracle unties them too.
         m = ref.module
@@ -203,9 +203,14 @@ def _worker_curve(rank, world, dp, tp, pp, accum, steps):
     ref_losses = [float(ref.train_step(feed)[0]) for _ in range(steps)]
 
     topo = init_topology(dp=dp, tp=tp, pp=pp)
-    args = build_argparser().parse_args(flags + ["--dp", str(dp), "--tp", str(tp), "--pp", str(pp)])
+    args = build_argparser().parse_args(flags + ["--dp", str(dp), "--tp", str(tp), "--pp", str(pp),
+                                                 "--pp_tie_embeddings", str(tie)])
     eng = Engine(args, topo, torch.device("cpu"), cfg)
     load_from_full(eng.module, full_state, topo.tp_rank, topo.tp)
+    if tie and eng.module.is_last:
+        with torch.no_grad():
+            eng.module.lm_head.weight.normal_()  # after_load must restore it from the first stage
+    eng.after_load()
     feed = Feed([topo.dp_rank])
     losses = []
     for _ in range(steps):
@@ -221,9 +226,11 @@ def _single_topo():
                     tp_group=None, pp_group=None, ep_group=None, dp_group=None)
 
 
-@pytest.mark.parametrize("dp,tp,pp", [(2, 2, 1), (1, 2, 2), (2, 1, 2)])
-def test_five_step_loss_curve_matches_dense(dp, tp, pp):
-    res = run_ranks(_worker_curve, dp * tp * pp, dp, tp, pp, 2, 5)
+@pytest.mark.parametrize("dp,tp,pp,tie", [(2, 2, 1, 0), (1, 2, 2, 0), (2, 1, 2, 0), (1, 2, 2, 1), (2, 1, 2, 1)])
+def test_five_step_loss_curve_matches_dense(dp, tp, pp, tie):
+    """Untied pipeline stages (the reference's layout) follow an untied dense model;
+    with --pp_tie_embeddings 1 they follow the tied dense GPT itself."""
+    res = run_ranks(_worker_curve, dp * tp * pp, dp, tp, pp, 2, 5, tie)
     checked = 0
     for losses, ref in res:
         assert ref[-1] < ref[0]
