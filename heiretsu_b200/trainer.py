@@ -205,6 +205,7 @@ class Engine:
         mark_tp_sharded(self.module)
         self.module.to(device)
         self.tied = None
+        self.skipped_steps = 0  # plain engine: steps skipped for a non-finite gradient norm
         if self.use_pipeline and getattr(args, "pp_tie_embeddings", 0):
             from .parallel.pipeline import TiedEmbeddings
             self.tied = TiedEmbeddings(self.module, topo)
@@ -415,8 +416,14 @@ class Engine:
         if self.scaler is not None and self.scaler.is_enabled():
             self.scaler.unscale_(self.optimizer)
         average_gradients(self.module, self.topo.dp_group)
-        if args.grad_clip > 0:
-            self.clip_plain(args.grad_clip)
+        if args.grad_clip > 0 and not self.clip_plain(args.grad_clip):
+            # Non-finite global norm (clip_mode global): every rank of the job sees it
+            # (the DP average and the model-parallel norm sum carry it), so all skip.
+            self.skipped_steps += 1
+            if self.scaler is not None and self.scaler.is_enabled():
+                self.scaler.update(self.scaler.get_scale() * self.scaler.get_backoff_factor())
+            self.optimizer.zero_grad(set_to_none=True)
+            return
         if self.scaler is not None and self.scaler.is_enabled():
             self.scaler.step(self.optimizer)
             self.scaler.update()
@@ -424,20 +431,31 @@ class Engine:
             self.optimizer.step()
         self.optimizer.zero_grad(set_to_none=True)
 
-    def clip_plain(self, max_norm: float) -> None:
+    def clip_plain(self, max_norm: float) -> bool:
+        """Clip the gradients to ``max_norm``. Returns False when the global norm is not
+        finite (clip_mode global): the caller then skips the step on every rank, as the
+        fused optimizer does and as GradScaler does for an fp16 overflow (the reference
+        clips NaN gradients into the weights, train.py:446, and its GradScaler decides per
+        rank). clip_mode local keeps the reference's per-shard clip and never skips."""
         params = [p for p in self.module.parameters() if p.grad is not None]
-        if self.args.clip_mode == "local" or self.mp_group is None:
+        if self.args.clip_mode == "local":
             torch.nn.utils.clip_grad_norm_(params, max_norm)
-            return
+            return True
+        if self.mp_group is None:
+            norm = torch.nn.utils.clip_grad_norm_(params, max_norm)
+            return bool(torch.isfinite(norm))
         wfn = replication_weight(self.topo, self.tied is not None)
         names = {id(p): n for n, p in self.module.named_parameters()}
         tot = torch.zeros((), device=self.device)
         for p in params:
             tot = tot + wfn(names[id(p)], p) * p.grad.detach().float().pow(2).sum()
         dist.all_reduce(tot, group=self.mp_group)
+        if not bool(torch.isfinite(tot)):
+            return False
         coef = torch.clamp(max_norm / (tot.sqrt() + 1e-6), max=1.0)
         for p in params:
             p.grad.detach().mul_(coef.to(p.grad.dtype))
+        return True
 
     # -- eval -----------------------------------------------------------------
     @torch.no_grad()

@@ -163,3 +163,68 @@ def test_trainer_stops_on_peer_failure():
     # rank 0 either sees the announcement before its next step, or its
     # in-flight all-reduce errors when rank 1's connections close.
     assert status == "ok" and out[0] in ("peer_failure", "raised"), res[0]
+
+
+def _nonfinite(rank, world, tp, clip_mode):
+    import torch
+
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.topo import init_topology
+    from heiretsu_b200.trainer import Engine, build_argparser
+
+    dp = world // tp
+    topo = init_topology(dp=dp, tp=tp)
+    args = build_argparser().parse_args([
+        "--batch_size", "2", "--block_size", "16", "--n_layer", "2", "--n_head", "2", "--n_embed", "16",
+        "--dp", str(dp), "--tp", str(tp), "--engine", "plain", "--device", "cpu", "--learning_rate", "1e-2",
+        "--clip_mode", clip_mode])
+    torch.manual_seed(0)
+    eng = Engine(args, topo, torch.device("cpu"), GPTConfig(block_size=16, vocab_size=64, n_layer=2, n_head=2,
+                                                            n_embed=16, dropout=0.0))
+    poison = [False]
+    w = eng.module.tr.h[0].mlp.c_fc.weight
+    if rank == world - 1:  # one rank's gradient turns NaN (injected on the host)
+        w.register_hook(lambda g: g * float("nan") if poison[0] else g)
+
+    class Feed:
+        B = 2
+
+        def __init__(self):
+            self.g = torch.Generator().manual_seed(5 + topo.dp_rank)
+
+        def next_batch(self, device):
+            return (torch.randint(0, 64, (2, 16), generator=self.g), torch.randint(0, 64, (2, 16), generator=self.g))
+
+    feed = Feed()
+    snap = lambda: [p.detach().clone() for p in eng.module.parameters()]
+    same = lambda a, b: all(torch.equal(x, y) for x, y in zip(a, b))
+    s0 = snap()
+    eng.train_step(feed)
+    s1 = snap()
+    poison[0] = True
+    eng.train_step(feed)
+    s2 = snap()
+    poison[0] = False
+    eng.train_step(feed)
+    s3 = snap()
+    finite = all(bool(torch.isfinite(p).all()) for p in s3)
+    return dict(moved1=not same(s0, s1), skipped2=same(s1, s2), moved3=not same(s2, s3), finite=finite,
+                skipped=eng.skipped_steps)
+
+
+@pytest.mark.parametrize("tp", [1, 2])
+def test_nonfinite_gradient_skips_the_step_on_every_rank(tp):
+    """A NaN in one rank's gradient reaches every rank through the DP average and
+    the model-parallel norm; every rank skips that step and training continues."""
+    res = run_ranks_raw(_nonfinite, 4, tp, "global")
+    for status, out in res:
+        assert status == "ok", out
+        assert out == dict(moved1=True, skipped2=True, moved3=True, finite=True, skipped=1), out
+
+
+def test_nonfinite_gradient_with_local_clip_follows_the_reference():
+    """clip_mode local reproduces the reference (train.py:446): the NaN reaches the weights."""
+    res = run_ranks_raw(_nonfinite, 2, 1, "local")
+    for status, out in res:
+        assert status == "ok", out
+        assert out["skipped"] == 0 and not out["finite"]

@@ -129,6 +129,37 @@ def test_adamw_matches_torch():
         assert torch.allclose(b.w16.float(), b, atol=1e-2, rtol=1e-2), n
 
 
+def test_adamw_skips_a_nonfinite_step():
+    """A NaN anywhere in the flat gradient makes the clip coefficient NaN, and the
+    AdamW kernel then leaves weights, moments and the bf16 shadow untouched."""
+    from heiretsu_b200.optim import FusedAdamW
+    from heiretsu_b200.parallel.flat import FlatParams
+
+    torch.manual_seed(5)
+    m = torch.nn.Sequential(torch.nn.Linear(64, 96), torch.nn.LayerNorm(96), torch.nn.Linear(96, 40)).cuda()
+    flat = FlatParams(m, torch.device("cuda"))
+    opt = FusedAdamW(flat, lr=1e-2, betas=(0.9, 0.95), weight_decay=0.1, max_grad_norm=1.0)
+
+    def step(poison):
+        flat.grad.normal_()
+        if poison:
+            flat.grad[flat.grad.numel() // 3] = float("nan")
+        opt.step()
+        opt.zero_grad()
+        torch.cuda.synchronize()
+
+    step(False)
+    before = (flat.data.clone(), opt.m.clone(), opt.v.clone(), flat.data16.clone())
+    step(True)
+    check()
+    assert torch.isnan(opt.coef).item()
+    after = (flat.data, opt.m, opt.v, flat.data16)
+    assert all(torch.equal(a, b) for a, b in zip(before, after))
+    step(False)
+    check()
+    assert not torch.equal(before[0], flat.data) and bool(torch.isfinite(flat.data).all())
+
+
 @pytest.mark.parametrize("B,T,nh", [(2, 256, 2), (1, 1024, 4), (2, 200, 3), (8, 1024, 12)])
 def test_attention_fwd_bwd(B, T, nh):
     torch.manual_seed(5)
