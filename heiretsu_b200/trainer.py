@@ -24,6 +24,7 @@ pipeline boundary has one declared dtype.
 from __future__ import annotations
 
 import argparse
+import contextlib
 import math
 import os
 import random
@@ -115,6 +116,10 @@ def build_argparser() -> argparse.ArgumentParser:
                         "for this many seconds (0 = off)")
     p.add_argument("--device_timing", type=int, default=1, choices=[0, 1],
                    help="time each step with CUDA events and log device tokens/s (max over ranks)")
+    p.add_argument("--region_timing_interval", type=int, default=0,
+                   help="every N steps run the step eagerly with device timers around forward+backward, the tied "
+                        "embedding sum, the TP gradient sum, the DP reduction and the optimizer; log them (max over "
+                        "ranks). 0 = off")
     p.add_argument("--overlap_dp", type=int, default=0, choices=[0, 1],
                    help="reduce data-parallel gradients block by block during the last backward (fused path); "
                         "off by default: on GPT-2 small the co-running reduction slowed backward more than it hid")
@@ -206,6 +211,7 @@ class Engine:
         self.module.to(device)
         self.tied = None
         self.skipped_steps = 0  # plain engine: steps skipped for a non-finite gradient norm
+        self.regions = None  # RegionTimer of an instrumented eager step (REGIONS), else None
         if self.use_pipeline and getattr(args, "pp_tie_embeddings", 0):
             from .parallel.pipeline import TiedEmbeddings
             self.tied = TiedEmbeddings(self.module, topo)
@@ -357,7 +363,35 @@ class Engine:
         self._static = None
         self._static_out = None
 
+    # Regions of an instrumented step, entered by every rank in this order.
+    REGIONS = ("fwd_bwd", "tied_emb", "tp_sync", "dp_reduce", "optimizer")
+
+    def _region(self, name: str):
+        return self.regions.region(name) if self.regions is not None else contextlib.nullcontext()
+
+    def timed_regions_step(self, loader, timer) -> tuple:
+        """One eager optimizer step (the kernels a captured step replays) with device
+        timers around each region in REGIONS; returns the step's (loss, aux)."""
+        self.regions = timer
+        try:
+            return self._eager_step(loader)
+        finally:
+            self.regions = None
+
     def _eager_step(self, loader) -> tuple:
+        topo = self.topo
+        with self._region("fwd_bwd"):
+            loss_scalar, aux = self._forward_backward(loader)
+        if loss_scalar is not None and topo.dp_group is not None and dist.is_initialized():
+            dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            loss_scalar = loss_scalar / topo.dp
+        if aux is not None and topo.dp_group is not None and dist.is_initialized():
+            dist.all_reduce(aux, op=dist.ReduceOp.SUM, group=topo.dp_group)
+            aux = aux / topo.dp
+        self.sync_and_step()
+        return loss_scalar, aux
+
+    def _forward_backward(self, loader) -> tuple:
         args, topo = self.args, self.topo
         accum = args.grad_accum_steps
         if self.use_pipeline:
@@ -385,13 +419,6 @@ class Engine:
             loss_scalar = loss_sum / accum
             if self.fused and topo.tp > 1 and dist.is_initialized():
                 dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.tp_group)
-        if loss_scalar is not None and topo.dp_group is not None and dist.is_initialized():
-            dist.all_reduce(loss_scalar, op=dist.ReduceOp.SUM, group=topo.dp_group)
-            loss_scalar = loss_scalar / topo.dp
-        if aux is not None and topo.dp_group is not None and dist.is_initialized():
-            dist.all_reduce(aux, op=dist.ReduceOp.SUM, group=topo.dp_group)
-            aux = aux / topo.dp
-        self.sync_and_step()
         return loss_scalar, aux
 
     def tp_sync_grads(self) -> None:
@@ -404,32 +431,40 @@ class Engine:
 
     def sync_and_step(self) -> None:
         args = self.args
-        if self.tied is not None:
-            self.tied.reduce_grads()
+        with self._region("tied_emb"):
+            if self.tied is not None:
+                self.tied.reduce_grads()
         if self.fused:
-            self.tp_sync_grads()
-            if self.reducer is not None:
-                self.reducer.reduce()
-            self.optimizer.step()
-            self.optimizer.zero_grad()
+            with self._region("tp_sync"):
+                self.tp_sync_grads()
+            with self._region("dp_reduce"):
+                if self.reducer is not None:
+                    self.reducer.reduce()
+            with self._region("optimizer"):
+                self.optimizer.step()
+                self.optimizer.zero_grad()
             return
         if self.scaler is not None and self.scaler.is_enabled():
             self.scaler.unscale_(self.optimizer)
-        average_gradients(self.module, self.topo.dp_group)
-        if args.grad_clip > 0 and not self.clip_plain(args.grad_clip):
-            # Non-finite global norm (clip_mode global): every rank of the job sees it
-            # (the DP average and the model-parallel norm sum carry it), so all skip.
-            self.skipped_steps += 1
+        with self._region("tp_sync"):
+            pass  # the plain path sums TP gradients inside autograd (column-parallel backward)
+        with self._region("dp_reduce"):
+            average_gradients(self.module, self.topo.dp_group)
+        with self._region("optimizer"):
+            if args.grad_clip > 0 and not self.clip_plain(args.grad_clip):
+                # Non-finite global norm (clip_mode global): every rank of the job sees it
+                # (the DP average and the model-parallel norm sum carry it), so all skip.
+                self.skipped_steps += 1
+                if self.scaler is not None and self.scaler.is_enabled():
+                    self.scaler.update(self.scaler.get_scale() * self.scaler.get_backoff_factor())
+                self.optimizer.zero_grad(set_to_none=True)
+                return
             if self.scaler is not None and self.scaler.is_enabled():
-                self.scaler.update(self.scaler.get_scale() * self.scaler.get_backoff_factor())
+                self.scaler.step(self.optimizer)
+                self.scaler.update()
+            else:
+                self.optimizer.step()
             self.optimizer.zero_grad(set_to_none=True)
-            return
-        if self.scaler is not None and self.scaler.is_enabled():
-            self.scaler.step(self.optimizer)
-            self.scaler.update()
-        else:
-            self.optimizer.step()
-        self.optimizer.zero_grad(set_to_none=True)
 
     def clip_plain(self, max_norm: float) -> bool:
         """Clip the gradients to ``max_norm``. Returns False when the global norm is not
@@ -622,9 +657,19 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
     for step in range(start_step, args.max_iters + 1):
         if wd is not None:
             wd.check()  # a failed peer is noticed here, before this step launches anything
-        with timer.region("step"):
-            loss_scalar, aux = engine.train_step(train_loader)
-        timed_steps += 1
+        region_ms = None
+        if args.region_timing_interval > 0 and step % args.region_timing_interval == 0:
+            # Instrumented eager step (kept out of the dev_tok/s figure); every rank takes part.
+            regions = RegionTimer(enabled=True)
+            loss_scalar, aux = engine.timed_regions_step(train_loader, regions)
+            region_ms = regions.summary()
+            if is_main:
+                print(f"step {step:6d} | regions (ms, max over ranks) "
+                      + " | ".join(f"{k} {v:.3f}" for k, v in region_ms.items()))
+        else:
+            with timer.region("step"):
+                loss_scalar, aux = engine.train_step(train_loader)
+            timed_steps += 1
         if wd is not None:
             wd.beat(step)
         now = time.time()
@@ -648,6 +693,8 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
                    "opt/lr": float(engine.optimizer.param_groups[0]["lr"]), "speed/eff_tokens_per_sec": eff,
                    "amp/enabled": int(engine.amp != "none"), "amp/mode": args.amp,
                    "accum/steps": args.grad_accum_steps, "step": step}
+            if region_ms:
+                log.update({f"time/{k}_ms": v for k, v in region_ms.items()})
             if args.num_experts > 0:
                 log["train/aux_loss"] = float(aux.item())
                 log.update(expert_load_metrics(module))

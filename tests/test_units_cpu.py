@@ -327,3 +327,16 @@ def test_commbench_work_and_roofline():
     assert abs(r["target_ms"] - 1.0) < 1e-9 and abs(r["frac"] - 0.5) < 1e-9 and abs(r["ref_frac"] - 0.25) < 1e-9
     assert abs(r["nvlink_gbs"] - 385.0) < 1e-6
     assert "of fallback" in r["label"] and "| dp_reduce |" in C.table(rows)
+
+
+def test_region_timing_step(tmp_path, capsys):
+    from heiretsu_b200.trainer import Engine, main
+
+    main(["--device", "cpu", "--synthetic_data", "--n_layer", "2", "--n_head", "2", "--n_embed", "32",
+          "--block_size", "32", "--batch_size", "4", "--max_iters", "4", "--eval_interval", "100",
+          "--eval_iters", "1", "--dropout", "0", "--log_interval", "1", "--region_timing_interval", "2",
+          "--out_dir", str(tmp_path)])
+    lines = [l for l in capsys.readouterr().out.splitlines() if "regions (ms" in l]
+    assert len(lines) == 2 and lines[0].startswith("step      2") and lines[1].startswith("step      4")
+    for name in Engine.REGIONS:
+        assert f"| {name} " in lines[0] or f") {name} " in lines[0], lines[0]
