@@ -160,7 +160,7 @@ def test_pipeline_matches_dense(pp, tp, dp, ep, moe):
     assert (tied - first["tied_dense"]).abs().max().item() < 1e-5
 
 
-def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0):
+def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0, ep=1, moe=False):
     """Five optimizer steps of the training engine (AdamW, global-norm clip) on
     this layout; returns the logged losses and those of a single-process dense
     engine fed the concatenation of the DP ranks' micro-batches."""
@@ -169,10 +169,14 @@ def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0):
     from heiretsu_b200.trainer import Engine, build_argparser
     from heiretsu_b200.utils.ckpt import load_from_full
 
-    cfg = GPTConfig(**CFG)
+    moe_kw = dict(num_experts=4, top_k=2, moe_freq=2) if moe else {}
+    cfg_kw = dict(CFG, **moe_kw)
+    cfg = GPTConfig(**cfg_kw)
     flags = ["--batch_size", "4", "--block_size", "32", "--grad_accum_steps", str(accum), "--n_layer", "4",
              "--n_head", "4", "--n_embed", "32", "--learning_rate", "3e-3", "--grad_clip", "0.5",
              "--engine", "plain", "--amp", "none", "--device", "cpu"]
+    for k, v in moe_kw.items():
+        flags += [f"--{k}", str(v)]
     data = {(s, m, d): _batch(1000 + 97 * s + 13 * m + d) for s in range(steps) for m in range(accum)
             for d in range(dp)}
 
@@ -187,7 +191,7 @@ def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0):
             xs = [data[(s, m, d)] for d in self.dps]
             return torch.cat([x for x, _ in xs]), torch.cat([y for _, y in xs])
 
-    full_state = _dense(CFG).state_dict()
+    full_state = _dense(cfg_kw).state_dict()
     # dense single-process reference on the concatenated DP batches
     eargs = build_argparser().parse_args(flags + ["--dp", "1"])
     ref = Engine(eargs, _single_topo(), torch.device("cpu"), cfg)
@@ -202,8 +206,8 @@ def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0):
     feed = Feed(list(range(dp)))
     ref_losses = [float(ref.train_step(feed)[0]) for _ in range(steps)]
 
-    topo = init_topology(dp=dp, tp=tp, pp=pp)
-    args = build_argparser().parse_args(flags + ["--dp", str(dp), "--tp", str(tp), "--pp", str(pp),
+    topo = init_topology(dp=dp, ep=ep, tp=tp, pp=pp)
+    args = build_argparser().parse_args(flags + ["--dp", str(dp), "--ep", str(ep), "--tp", str(tp), "--pp", str(pp),
                                                  "--pp_tie_embeddings", str(tie)])
     eng = Engine(args, topo, torch.device("cpu"), cfg)
     load_from_full(eng.module, full_state, topo.tp_rank, topo.tp)
@@ -226,11 +230,16 @@ def _single_topo():
                     tp_group=None, pp_group=None, ep_group=None, dp_group=None)
 
 
-@pytest.mark.parametrize("dp,tp,pp,tie", [(2, 2, 1, 0), (1, 2, 2, 0), (2, 1, 2, 0), (1, 2, 2, 1), (2, 1, 2, 1)])
-def test_five_step_loss_curve_matches_dense(dp, tp, pp, tie):
+@pytest.mark.parametrize("dp,tp,pp,tie,ep,moe", [(2, 2, 1, 0, 1, False), (1, 2, 2, 0, 1, False),
+                                                  (2, 1, 2, 0, 1, False), (1, 2, 2, 1, 1, False),
+                                                  (2, 1, 2, 1, 1, False), (1, 1, 1, 0, 2, True),
+                                                  (1, 2, 1, 0, 2, True), (1, 1, 2, 0, 2, True)])
+def test_five_step_loss_curve_matches_dense(dp, tp, pp, tie, ep, moe):
     """Untied pipeline stages (the reference's layout) follow an untied dense model;
-    with --pp_tie_embeddings 1 they follow the tied dense GPT itself."""
-    res = run_ranks(_worker_curve, dp * tp * pp, dp, tp, pp, 2, 5, tie)
+    with --pp_tie_embeddings 1 they follow the tied dense GPT itself. Expert-parallel
+    ranks of one replica see the same tokens, so an EP run (dp = 1) follows the
+    single-process MoE model."""
+    res = run_ranks(_worker_curve, dp * tp * pp * ep, dp, tp, pp, 2, 5, tie, ep, moe)
     checked = 0
     for losses, ref in res:
         assert ref[-1] < ref[0]
