@@ -42,7 +42,7 @@ from .models.gpt import GPT
 from .parallel.dp import average_gradients
 from .parallel.pipeline import GPipeEngine, StageModule
 from .topo import cleanup, init_topology
-from .utils.ckpt import load_checkpoint, save_checkpoint
+from .utils.ckpt import save_checkpoint
 from .utils.data import RandomBatchLoader, SyntheticLoader
 
 try:  # optional, as in the reference
@@ -556,18 +556,28 @@ def main(argv=None) -> None:
     start_step = 1
     resume_side = None
     if args.resume:
-        obj = load_checkpoint(module, args.resume)
+        from .utils.ckpt import load_for_resume, load_rank_state, sidecar_path
+        info = load_for_resume(module, args.resume, topo)
         engine.after_load()
-        start_step = int(obj.get("step", 0)) + 1
-        from .utils.ckpt import sidecar_path
-        side = sidecar_path(args.resume)
-        if os.path.exists(side):
-            resume_side = torch.load(side, map_location="cpu", weights_only=False)
-            opt_state = resume_side.get("optimizer", resume_side)
-            engine.optimizer.load_state_dict(opt_state)
+        start_step = info["step"] + 1
+        restored = []
+        if info["same_layout"]:
+            side = sidecar_path(info["file"])
+            if os.path.exists(side):
+                side_obj = torch.load(side, map_location="cpu", weights_only=False)
+                engine.optimizer.load_state_dict(side_obj.get("optimizer", side_obj))
+                restored.append("optimizer")
+                if topo.dp == 1:
+                    resume_side = side_obj  # files without per-rank state: RNG / data position of dp rank 0
+            st = load_rank_state(info["file"], info["step"], topo)
+            if st is not None:
+                resume_side = st
+            if resume_side is not None and "rng" in resume_side:
+                restored.append("RNG and data position")
         if rank == 0:
-            print(f"[resume] loaded {args.resume} (step {obj.get('step')})"
-                  f"{'; optimizer, RNG and data position from ' + side if resume_side else ''}")
+            how = "its own shard" if info["same_layout"] else "the merged shards of another TP/PP/EP layout"
+            print(f"[resume] step {info['step']} from {args.resume} ({how})"
+                  f"{'; ' + ', '.join(restored) if restored else '; weights only, the optimizer restarts'}")
     n_params = sum(p.numel() for p in module.parameters())
     if rank == 0:
         print(f"[model] parameters: {n_params:,} ({n_params / 1e6:.1f}M) | engine="
@@ -719,6 +729,9 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
             if hasattr(train_loader, "state_dict"):
                 side["train_loader"] = train_loader.state_dict()
             save_checkpoint(module, cfg, step, topo, args.out_dir, optimizer_state=side)
+            from .utils.ckpt import save_rank_state  # every rank: its own RNG and data position
+            save_rank_state(args.out_dir, step, topo, {k: side[k] for k in ("rng", "train_loader", "dropout_seed")
+                                                       if k in side})
 
 
 def expert_counts(module):

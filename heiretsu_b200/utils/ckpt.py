@@ -4,13 +4,20 @@ Model files are byte-compatible with the reference:
 ``{"model": state_dict, "cfg": asdict(GPTConfig), "step": int}`` and, when
 sharded, a ``"topo"`` dict; names ``ckpt_{step:07d}.pt`` (tp=pp=ep=1) or
 ``ckpt_{step:07d}_pp{p}_ep{e}_tp{t}.pt``. Optimizer state goes to a separate
-``optim_{...}.pt`` sidecar so the model files stay unchanged.
+``optim_{...}.pt`` sidecar so the model files stay unchanged, and each rank's
+RNG states and data position to ``rstate_{step:07d}_r{rank}.pt``.
+
+Resume (``load_for_resume``) takes any file of a step. With the same TP / PP /
+EP layout every rank loads its own shard; with another layout all shards of
+the step are merged into the dense GPT state dict (``merge_shards``) and
+re-sliced for the new layout (weights only: the optimizer restarts).
 """
 from __future__ import annotations
 
 import os
+import re
 from dataclasses import asdict
-from typing import Optional
+from typing import Dict, List, Optional, Tuple
 
 import torch
 
@@ -68,14 +75,74 @@ def set_rng_state(st: dict) -> None:
         torch.cuda.set_rng_state(st["cuda"])
 
 
+def _strip_compile_prefix(sd: dict) -> dict:
+    # torch.compile-wrapped reference models prefix keys with `_orig_mod.`.
+    return {k[len("_orig_mod."):] if k.startswith("_orig_mod.") else k: v for k, v in sd.items()}
+
+
 def load_checkpoint(module: torch.nn.Module, path: str, strict: bool = True) -> dict:
     obj = torch.load(path, map_location="cpu", weights_only=False)
-    sd = obj["model"]
-    # torch.compile-wrapped reference models prefix keys with `_orig_mod.`.
-    sd = {k[len("_orig_mod."):] if k.startswith("_orig_mod.") else k: v for k, v in sd.items()}
     with torch.no_grad():
-        module.load_state_dict(sd, strict=strict)
+        module.load_state_dict(_strip_compile_prefix(obj["model"]), strict=strict)
     return obj
+
+
+# ---------------------------------------------------------------------------
+# Files of one checkpoint step; per-rank state
+# ---------------------------------------------------------------------------
+_CKPT_RE = re.compile(r"^ckpt_(\d{7})(?:_pp(\d+)_ep(\d+)_tp(\d+))?\.pt$")
+
+
+def step_files(path: str) -> List[str]:
+    """Every file of the checkpoint step that ``path`` belongs to: the dense file, or all
+    ``ckpt_{step}_pp*_ep*_tp*.pt`` shards beside it."""
+    d, b = os.path.split(path)
+    m = _CKPT_RE.match(b)
+    if m is None or m.group(2) is None:
+        return [path]
+    out = []
+    for f in sorted(os.listdir(d or ".")):
+        mm = _CKPT_RE.match(f)
+        if mm is not None and mm.group(1) == m.group(1) and mm.group(2) is not None:
+            out.append(os.path.join(d, f))
+    return out
+
+
+def own_shard_path(path: str, topo) -> str:
+    """The file of ``path``'s step holding this rank's (pp, ep, tp) shard."""
+    d, b = os.path.split(path)
+    m = _CKPT_RE.match(b)
+    if m is None:
+        return path
+    return os.path.join(d, ckpt_name(int(m.group(1)), topo))
+
+
+def ckpt_layout(obj: dict) -> Tuple[int, int, int]:
+    """(tp, pp, ep) a checkpoint was written with ((1, 1, 1) for a dense file)."""
+    t = obj.get("topo")
+    return (1, 1, 1) if t is None else (int(t["tp"]), int(t["pp"]), int(t["ep"]))
+
+
+def rank_state_path(out_dir: str, step: int, rank: int) -> str:
+    return os.path.join(out_dir, f"rstate_{step:07d}_r{rank}.pt")
+
+
+def save_rank_state(out_dir: str, step: int, topo, state: dict) -> str:
+    """Per-rank resume state (RNG states, data position, ...), tagged with the layout."""
+    path = rank_state_path(out_dir, step, topo.rank)
+    torch.save({**state, "layout": [topo.dp, topo.ep, topo.tp, topo.pp]}, path)
+    return path
+
+
+def load_rank_state(ckpt_path: str, step: int, topo) -> Optional[dict]:
+    """This rank's state file written beside ``ckpt_path`` by a run of the same layout, or None."""
+    path = rank_state_path(os.path.dirname(ckpt_path), step, topo.rank)
+    if not os.path.exists(path):
+        return None
+    st = torch.load(path, map_location="cpu", weights_only=False)
+    if list(st.get("layout", [])) != [topo.dp, topo.ep, topo.tp, topo.pp]:
+        return None
+    return st
 
 
 # ---------------------------------------------------------------------------
@@ -91,6 +158,8 @@ def _full_key(local_key: str, module) -> str:
     from ..parallel.pipeline import StageModule
 
     orig = local_key  # submodule lookups use the shard's own names
+    if not isinstance(module, StageModule) and local_key == "lm_head.weight":
+        return "tr.wte.weight"  # one tied table: a state from untied pipeline stages gives its embedding
     if isinstance(module, StageModule):
         if local_key.startswith("blocks."):
             rest = local_key[len("blocks."):]
@@ -143,3 +212,108 @@ def load_from_full(module, full_state: dict, tp_rank: int = 0, tp: int = 1) -> N
     sd = shard_from_full(module, full_state, tp_rank, tp)
     with torch.no_grad():
         module.load_state_dict(sd, strict=True)
+
+
+# ---------------------------------------------------------------------------
+# Shards -> dense state dict (topology changes, dense export)
+# ---------------------------------------------------------------------------
+def _tp_kind(full_key: str) -> Optional[str]:
+    """How a dense GPT key is split over TP ranks (tp_linear.py:87-312 layouts)."""
+    if ".attn.c_attn." in full_key:
+        return "qkv"
+    if ".mlp.c_fc." in full_key:
+        return "col"
+    if full_key.endswith((".attn.c_proj.weight", ".mlp.c_proj.weight")):
+        return "row"
+    return None  # replicated over TP (LayerNorms, embeddings, row biases, router, experts)
+
+
+def merge_shards(objs: List[dict]) -> Dict[str, torch.Tensor]:
+    """Dense GPT state dict from every shard file of one checkpoint step (as loaded by
+    torch.load). Pipeline stages keep their own embedding tables: ``tr.wte.weight`` comes
+    from the first stage and ``lm_head.weight`` from the last (equal unless the stages
+    were trained untied)."""
+    from ..parallel.pipeline import _partition_layers
+
+    cfg = objs[0]["cfg"]
+    n_layer, n_exp = int(cfg["n_layer"]), int(cfg.get("num_experts", 0) or 0)
+    parts: Dict[str, Dict[int, torch.Tensor]] = {}
+    tp_of: Dict[str, int] = {}
+    for obj in objs:
+        t = obj.get("topo") or dict(tp=1, pp=1, ep=1, tp_rank=0, pp_rank=0, ep_rank=0)
+        tp, pp, ep = int(t["tp"]), int(t["pp"]), int(t["ep"])
+        start = _partition_layers(n_layer, pp)[int(t["pp_rank"])][0]
+        for key, v in _strip_compile_prefix(obj["model"]).items():
+            fk = key
+            if pp > 1:
+                if fk.startswith("blocks."):
+                    i, tail = fk[len("blocks."):].split(".", 1)
+                    fk = f"tr.h.{start + int(i)}.{tail}"
+                elif fk.startswith(("wte.", "wpe.", "ln_f.")):
+                    fk = "tr." + fk
+            if ".moe.expert_group.experts." in fk:
+                pre, rest = fk.split(".moe.expert_group.experts.", 1)
+                j, tail = rest.split(".", 1)
+                fk = f"{pre}.moe.expert_group.experts.{int(t['ep_rank']) * (n_exp // ep) + int(j)}.{tail}"
+            parts.setdefault(fk, {})[int(t["tp_rank"])] = v
+            tp_of[fk] = tp
+    full: Dict[str, torch.Tensor] = {}
+    for fk, by_rank in parts.items():
+        kind, tp = _tp_kind(fk), tp_of[fk]
+        if kind is None or tp == 1:
+            full[fk] = next(iter(by_rank.values())).clone()
+            continue
+        if sorted(by_rank) != list(range(tp)):
+            raise ValueError(f"checkpoint shards incomplete for {fk}: tp ranks {sorted(by_rank)} of {tp}")
+        shards = [by_rank[r] for r in range(tp)]
+        if kind == "qkv":
+            per = shards[0].shape[0] // 3
+            full[fk] = torch.cat([s[i * per:(i + 1) * per] for i in range(3) for s in shards])
+        elif kind == "col":
+            full[fk] = torch.cat(shards, 0)
+        else:
+            full[fk] = torch.cat(shards, 1)
+    if "lm_head.weight" not in full and "tr.wte.weight" in full:
+        full["lm_head.weight"] = full["tr.wte.weight"]
+    return full
+
+
+def load_for_resume(module, path: str, topo) -> dict:
+    """Load the checkpoint step that ``path`` belongs to into this rank's module.
+
+    Returns ``{"step", "same_layout", "file"}``; ``file`` is the shard this rank read
+    (same layout) or ``path``."""
+    head = torch.load(path, map_location="cpu", weights_only=False)
+    layout = ckpt_layout(head)
+    if layout == (topo.tp, topo.pp, topo.ep):
+        own = own_shard_path(path, topo) if layout != (1, 1, 1) else path
+        obj = head if os.path.abspath(own) == os.path.abspath(path) else \
+            torch.load(own, map_location="cpu", weights_only=False)
+        with torch.no_grad():
+            module.load_state_dict(_strip_compile_prefix(obj["model"]), strict=True)
+        return {"step": int(obj.get("step", 0)), "same_layout": True, "file": own}
+    objs = [head if os.path.abspath(f) == os.path.abspath(path) else
+            torch.load(f, map_location="cpu", weights_only=False) for f in step_files(path)]
+    load_from_full(module, merge_shards(objs), topo.tp_rank, topo.tp)
+    return {"step": int(head.get("step", 0)), "same_layout": False, "file": path}
+
+
+def main(argv=None) -> None:
+    """python -m heiretsu_b200.utils.ckpt merge OUT.pt CKPT  (any file of the step):
+    writes the dense checkpoint ``{"model", "cfg", "step"}`` of a sharded step."""
+    import argparse
+
+    ap = argparse.ArgumentParser(description="checkpoint tools")
+    sub = ap.add_subparsers(dest="cmd", required=True)
+    mg = sub.add_parser("merge", help="merge the shards of one step into a dense checkpoint")
+    mg.add_argument("out")
+    mg.add_argument("ckpt")
+    a = ap.parse_args(argv)
+    objs = [torch.load(f, map_location="cpu", weights_only=False) for f in step_files(a.ckpt)]
+    full = merge_shards(objs)
+    torch.save({"model": full, "cfg": objs[0]["cfg"], "step": objs[0].get("step", 0)}, a.out)
+    print(f"merged {len(objs)} file(s) -> {a.out} ({len(full)} tensors)")
+
+
+if __name__ == "__main__":
+    main()
