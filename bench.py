@@ -32,7 +32,9 @@ samples and every throttle reason seen active.
 The ``e2e`` number is the same metric through the public training API
 (``Engine.train_step`` with a host data loader): each step copies its input
 tokens host->device from pinned memory and reads the loss back to the host,
-timed on the host clock (max over ranks).
+timed on the host clock (max over ranks). The loss of step i is copied
+asynchronously and read once step i+1 is queued (``ScalarReader``; the last
+one before the clock stops), on both arms.
 
 ``--impl reference`` runs the unmodified reference implementation installed
 in baseline/_ref through its own modules (GPT or StageModule + GPipeEngine,
@@ -454,6 +456,41 @@ def run_reference(args, w: Workload, layout, world, rank, dev):
     return eng, (lambda: train_step(dl)), make_loader, "zzz-no-own-kernels"
 
 
+class _PinnedReader:
+    """The reference arm's copy of the deferred read-back (that arm imports nothing of
+    this framework): async copy into pinned memory + event, read one step later."""
+
+    def __init__(self):
+        self.q = []
+        self.slots = [torch.empty((), dtype=torch.float32, pin_memory=True) for _ in range(2)]
+        self.i = 0
+
+    def push(self, t):
+        h = self.slots[self.i % 2]
+        self.i += 1
+        h.copy_(t.detach().float(), non_blocking=True)
+        ev = torch.cuda.Event()
+        ev.record()
+        self.q.append((h, ev))
+
+    def pop(self):
+        h, ev = self.q.pop(0)
+        ev.synchronize()
+        return float(h)
+
+    def __len__(self):
+        return len(self.q)
+
+
+def _scalar_reader(impl: str):
+    """Deferred loss read-back of the e2e loop (same pattern on both arms)."""
+    if impl == "reference":
+        return _PinnedReader()
+    sys.path.insert(0, ROOT)
+    from heiretsu_b200.trainer import ScalarReader
+    return ScalarReader(depth=2)
+
+
 def main():
     args = parse()
     w = WORKLOADS[args.config]
@@ -490,12 +527,18 @@ def main():
         for _ in range(2):
             l, a = eng.train_step(loader)
             float((l if l is not None else a).item())
+        reader = _scalar_reader(args.impl)
         barrier_sync(world)
         t0 = time.perf_counter()
         for _ in range(args.steps):
             l, a = eng.train_step(loader)
-            # device -> host read of the step's loss (pipeline stages before the last hold the aux loss)
-            float((l if l is not None else a).item())
+            # device -> host read of every step's loss (pipeline stages before the last hold the aux
+            # loss): copied asynchronously, read once the next step is queued, the last one below
+            reader.push(l if l is not None else a)
+            if len(reader) > 1:
+                reader.pop()
+        while len(reader):
+            reader.pop()
         barrier_sync(world)
         e2e_s = max_over_ranks((time.perf_counter() - t0) / args.steps, world)
         e2e = {"value": tokens / e2e_s, "unit": "tokens/s", "h2d_bytes_per_step": h2d, "d2h_bytes_per_step": 4,

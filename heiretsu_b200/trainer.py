@@ -184,6 +184,45 @@ def mark_tp_sharded(module: torch.nn.Module) -> None:
             m.weight.tp_sharded = True
 
 
+class ScalarReader:
+    """Reads each step's device scalar (loss) back to the host one step late.
+
+    ``push`` starts an asynchronous copy into a pinned host slot and records an
+    event; ``pop`` waits for the oldest copy and returns its value. Pushing step
+    i+1 before popping step i keeps the next step queued on the GPU while the
+    host waits, so reading every loss costs no idle gap between steps."""
+
+    def __init__(self, depth: int = 2):
+        self.depth = depth
+        self._slots = None
+        self._queue = []  # (slot index, event or None)
+        self._i = 0
+
+    def push(self, t: torch.Tensor) -> None:
+        if len(self._queue) >= self.depth:
+            raise RuntimeError("ScalarReader: pop before pushing more than `depth` values")
+        if self._slots is None:
+            pin = t.is_cuda
+            self._slots = [torch.empty((), dtype=torch.float32, pin_memory=pin) for _ in range(self.depth)]
+        slot = self._i % self.depth
+        self._i += 1
+        self._slots[slot].copy_(t.detach().float(), non_blocking=t.is_cuda)
+        ev = None
+        if t.is_cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+        self._queue.append((slot, ev))
+
+    def pop(self) -> float:
+        slot, ev = self._queue.pop(0)
+        if ev is not None:
+            ev.synchronize()
+        return float(self._slots[slot])
+
+    def __len__(self) -> int:
+        return len(self._queue)
+
+
 class _ListLoader:
     """Serves a fixed list of device batches in order (graph capture / replay)."""
 

@@ -118,3 +118,24 @@ def test_reference_config_accepts_every_workload():
     for w in bench.WORKLOADS.values():
         cfg = ref.gpt_model.GPTConfig(**w.model_kwargs(), dropout=0.0)
         assert cfg.n_layer == w.model["n_layer"] and cfg.num_experts == w.model.get("num_experts", 0)
+
+
+def test_scalar_reader_returns_every_value_in_order():
+    import torch
+
+    from heiretsu_b200.trainer import ScalarReader
+
+    r = ScalarReader(depth=2)
+    out = []
+    for i in range(5):
+        r.push(torch.tensor(float(i)))
+        if len(r) > 1:
+            out.append(r.pop())
+    while len(r):
+        out.append(r.pop())
+    assert out == [0.0, 1.0, 2.0, 3.0, 4.0]
+    r.push(torch.tensor(1.0))
+    r.push(torch.tensor(2.0))
+    import pytest
+    with pytest.raises(RuntimeError):
+        r.push(torch.tensor(3.0))
