@@ -10,8 +10,10 @@ One step = sum-of-squares reductions (one per replication class) ->
 optional all-reduce of the squared norm over the model-parallel group ->
 clip coefficient -> one AdamW kernel that also refreshes the bf16 GEMM
 shadow. Within one node the model-parallel sum runs over NVLink in a
-kernel, so the whole step stays inside one captured CUDA graph. No host synchronisation: the coefficient stays on the device, and a
-non-finite norm (fp16 overflow) skips the update inside the kernel.
+kernel, so the whole step stays inside one captured CUDA graph. No host
+synchronisation: the per-step hyper-parameters are uploaded asynchronously
+from pinned memory, the coefficient stays on the device, and a non-finite norm
+(fp16 overflow) skips the update inside the kernel.
 """
 from __future__ import annotations
 
@@ -48,6 +50,10 @@ class FusedAdamW:
         self.coef = torch.ones((), device=dev, dtype=torch.float32)
         self.grad_scale = 1.0
         self.param_groups = [{"lr": lr}]  # logging compatibility with torch optimizers
+        # Pinned staging slots of the hyper-parameter upload; a slot is rewritten only
+        # after the event behind its previous copy completed.
+        self._stage = [torch.empty(8, dtype=torch.float32, pin_memory=dev.type == "cuda") for _ in range(2)]
+        self._stage_ev = [None, None]
 
     def compute_grad_norm(self) -> torch.Tensor:
         """Global L2 norm of the gradients (device tensor), each replicated parameter counted once."""
@@ -77,11 +83,22 @@ class FusedAdamW:
         self.step_count += 1
         lr = self.param_groups[0]["lr"]
         b1, b2 = self.betas
-        # A fresh pageable host tensor: the copy is staged before copy_ returns,
-        # so the host may run ahead without overwriting an in-flight source.
-        h = torch.tensor([lr, b1, b2, self.eps, self.wd, 1.0 - b1 ** self.step_count,
-                          math.sqrt(1.0 - b2 ** self.step_count), self.grad_scale], dtype=torch.float32)
-        self.hyper.copy_(h)
+        vals = [lr, b1, b2, self.eps, self.wd, 1.0 - b1 ** self.step_count, math.sqrt(1.0 - b2 ** self.step_count),
+                self.grad_scale]
+        # Asynchronous upload from a pinned slot: a blocking copy from pageable memory would
+        # synchronise the stream, and the GPU would idle while the host launches the next step.
+        i = self.step_count % 2
+        if self._stage_ev[i] is not None:
+            self._stage_ev[i].synchronize()
+        slot = self._stage[i]
+        for j, v in enumerate(vals):
+            slot[j] = v
+        cuda = self.hyper.is_cuda
+        self.hyper.copy_(slot, non_blocking=cuda)
+        if cuda:
+            ev = torch.cuda.Event()
+            ev.record()
+            self._stage_ev[i] = ev
 
     def step_device(self) -> None:
         """Device part of a step (no host synchronisation; graph-capturable)."""

@@ -340,3 +340,21 @@ def test_region_timing_step(tmp_path, capsys):
     assert len(lines) == 2 and lines[0].startswith("step      2") and lines[1].startswith("step      4")
     for name in Engine.REGIONS:
         assert f"| {name} " in lines[0] or f") {name} " in lines[0], lines[0]
+
+
+def test_fused_adamw_hyper_upload_values():
+    """prepare_step writes [lr, b1, b2, eps, wd, 1-b1^t, sqrt(1-b2^t), grad_scale] for step t
+    through its staging slots (host part only; the kernels need a GPU)."""
+    import math
+    import types
+
+    import torch
+
+    from heiretsu_b200.optim import FusedAdamW
+
+    flat = types.SimpleNamespace(device=torch.device("cpu"), data=torch.zeros(16), grad=torch.zeros(16), ranges=[])
+    opt = FusedAdamW(flat, lr=2e-3, betas=(0.8, 0.9), eps=1e-7, weight_decay=0.05)
+    for t in (1, 2, 3):
+        opt.prepare_step()
+        want = torch.tensor([2e-3, 0.8, 0.9, 1e-7, 0.05, 1 - 0.8 ** t, math.sqrt(1 - 0.9 ** t), 1.0])
+        assert torch.allclose(opt.hyper, want), (t, opt.hyper)
