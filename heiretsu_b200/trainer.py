@@ -123,6 +123,10 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--overlap_dp", type=int, default=0, choices=[0, 1],
                    help="reduce data-parallel gradients block by block during the last backward (fused path); "
                         "off by default: on GPT-2 small the co-running reduction slowed backward more than it hid")
+    p.add_argument("--lr_schedule", type=str, default="constant", choices=["constant", "cosine"],
+                   help="constant (the reference) or linear warmup then cosine decay to --min_lr at --max_iters")
+    p.add_argument("--warmup_iters", type=int, default=0)
+    p.add_argument("--min_lr", type=float, default=0.0)
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
     return p
@@ -182,6 +186,21 @@ def mark_tp_sharded(module: torch.nn.Module) -> None:
                 m.bias.tp_sharded = True
         elif isinstance(m, RowParallelLinear):
             m.weight.tp_sharded = True
+
+
+def lr_at(step: int, args) -> float:
+    """Learning rate of optimizer step ``step`` (1-based). ``constant``: --learning_rate.
+    ``cosine``: linear warmup over --warmup_iters steps, then cosine decay from
+    --learning_rate to --min_lr at --max_iters."""
+    lr = args.learning_rate
+    if getattr(args, "lr_schedule", "constant") == "constant":
+        return lr
+    warm = max(0, int(args.warmup_iters))
+    if step <= warm:
+        return lr * step / warm
+    span = max(1, args.max_iters - warm)
+    frac = min(1.0, (step - warm) / span)
+    return args.min_lr + 0.5 * (lr - args.min_lr) * (1.0 + math.cos(math.pi * frac))
 
 
 class ScalarReader:
@@ -704,6 +723,9 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
     timer = RegionTimer(enabled=bool(args.device_timing) and engine.device.type == "cuda")
     timed_steps = 0
     for step in range(start_step, args.max_iters + 1):
+        if args.lr_schedule != "constant":
+            for g in engine.optimizer.param_groups:
+                g["lr"] = lr_at(step, args)  # read by the next step (graph replays included)
         if wd is not None:
             wd.check()  # a failed peer is noticed here, before this step launches anything
         region_ms = None
@@ -736,7 +758,9 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
             if is_main:
                 aux_str = f" | aux_loss {aux.item():.4f}" if args.num_experts > 0 else ""
                 ls = f"{loss_scalar.item():.4f}" if loss_scalar is not None else "n/a"
-                print(f"step {step:6d} | train_loss (mean micro) {ls}{aux_str} | eff_tok/s {eff:,.0f}{dev_str}")
+                lr_str = (f" | lr {engine.optimizer.param_groups[0]['lr']:.3e}"
+                          if args.lr_schedule != "constant" else "")
+                print(f"step {step:6d} | train_loss (mean micro) {ls}{aux_str} | eff_tok/s {eff:,.0f}{dev_str}{lr_str}")
         if is_main and run:
             log = {"train/loss_mean_micro": float(loss_scalar.item()) if loss_scalar is not None else float("nan"),
                    "opt/lr": float(engine.optimizer.param_groups[0]["lr"]), "speed/eff_tokens_per_sec": eff,

@@ -358,3 +358,23 @@ def test_fused_adamw_hyper_upload_values():
         opt.prepare_step()
         want = torch.tensor([2e-3, 0.8, 0.9, 1e-7, 0.05, 1 - 0.8 ** t, math.sqrt(1 - 0.9 ** t), 1.0])
         assert torch.allclose(opt.hyper, want), (t, opt.hyper)
+
+
+def test_lr_schedule(capsys, tmp_path):
+    import math
+
+    from heiretsu_b200.trainer import build_argparser, lr_at, main
+
+    a = build_argparser().parse_args(["--learning_rate", "1e-3", "--lr_schedule", "cosine", "--warmup_iters", "4",
+                                      "--min_lr", "1e-4", "--max_iters", "14"])
+    assert lr_at(1, a) == 2.5e-4 and lr_at(4, a) == 1e-3
+    assert abs(lr_at(9, a) - (1e-4 + 0.5 * 9e-4 * (1 + math.cos(math.pi * 0.5)))) < 1e-12
+    assert abs(lr_at(14, a) - 1e-4) < 1e-12
+    c = build_argparser().parse_args(["--learning_rate", "1e-3"])
+    assert lr_at(7, c) == 1e-3  # the reference's constant rate by default
+    main(["--device", "cpu", "--synthetic_data", "--n_layer", "1", "--n_head", "2", "--n_embed", "32",
+          "--block_size", "16", "--batch_size", "2", "--max_iters", "3", "--eval_interval", "100", "--eval_iters",
+          "1", "--log_interval", "1", "--learning_rate", "1e-3", "--lr_schedule", "cosine", "--warmup_iters", "2",
+          "--out_dir", str(tmp_path)])
+    lrs = [l.split("| lr ")[1] for l in capsys.readouterr().out.splitlines() if "| lr " in l]
+    assert lrs == ["5.000e-04", "1.000e-03", "0.000e+00"], lrs
