@@ -112,6 +112,28 @@ class FusedAdamW:
     def zero_grad(self, set_to_none: bool = True) -> None:
         self.flat.zero_grad()
 
+    def moments_by_name(self) -> dict:
+        """AdamW state keyed by parameter name (host copies): ``{"format": "by_name",
+        "step", "m": {name: tensor}, "v": {name: tensor}}``. Shaped like the parameters,
+        so checkpoint tools can merge and re-slice it like the weights."""
+        f = self.flat
+        m, v = {}, {}
+        for name, off, p in zip(f.names, f.offsets, f.params):
+            n = p.numel()
+            m[name] = self.m[off:off + n].view(p.shape).detach().cpu()
+            v[name] = self.v[off:off + n].view(p.shape).detach().cpu()
+        return {"format": "by_name", "step": self.step_count, "m": m, "v": v}
+
+    def load_moments_by_name(self, st: dict) -> None:
+        f = self.flat
+        with torch.no_grad():
+            for name, off, p in zip(f.names, f.offsets, f.params):
+                n = p.numel()
+                if name in st["m"]:
+                    self.m[off:off + n].copy_(st["m"][name].reshape(-1))
+                    self.v[off:off + n].copy_(st["v"][name].reshape(-1))
+        self.step_count = int(st["step"])
+
     def state_dict(self) -> dict:
         return {"m": self.m.cpu(), "v": self.v.cpu(), "step": self.step_count, "lr": self.param_groups[0]["lr"],
                 "betas": self.betas, "eps": self.eps, "weight_decay": self.wd, "names": list(self.flat.names)}

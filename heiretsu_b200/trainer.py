@@ -577,6 +577,38 @@ class Engine:
         self.module.train()
         return sum(losses) / len(losses) if losses else None
 
+    # -- optimizer state by parameter name (checkpoints) ------------------------
+    def optimizer_state(self) -> dict:
+        """AdamW moments keyed by parameter name, for either engine (see FusedAdamW.moments_by_name)."""
+        if self.fused:
+            return self.optimizer.moments_by_name()
+        m, v, step = {}, {}, 0
+        for name, p in self.module.named_parameters():
+            st = self.optimizer.state.get(p)
+            if st and "exp_avg" in st:
+                m[name], v[name] = st["exp_avg"].detach().cpu(), st["exp_avg_sq"].detach().cpu()
+                step = int(st["step"])
+        out = {"format": "by_name", "step": step, "m": m, "v": v}
+        if self.scaler is not None and self.scaler.is_enabled():
+            out["scaler"] = self.scaler.state_dict()
+        return out
+
+    def load_optimizer_state(self, st: dict) -> None:
+        """Inverse of ``optimizer_state``; also accepts an optimizer's own ``state_dict()``."""
+        if st.get("format") != "by_name":
+            self.optimizer.load_state_dict(st)
+            return
+        if self.fused:
+            self.optimizer.load_moments_by_name(st)
+            return
+        for name, p in self.module.named_parameters():
+            if name in st["m"]:
+                self.optimizer.state[p] = {"step": torch.tensor(float(st["step"])),
+                                           "exp_avg": st["m"][name].to(p.device, p.dtype).clone(),
+                                           "exp_avg_sq": st["v"][name].to(p.device, p.dtype).clone()}
+        if "scaler" in st and self.scaler is not None and self.scaler.is_enabled():
+            self.scaler.load_state_dict(st["scaler"])
+
     def after_load(self) -> None:
         if self.tied is not None:
             self.tied.sync_weights()
@@ -614,7 +646,8 @@ def main(argv=None) -> None:
     start_step = 1
     resume_side = None
     if args.resume:
-        from .utils.ckpt import load_for_resume, load_rank_state, sidecar_path
+        from .utils.ckpt import (find_rank_state, load_for_resume, merged_optimizer_moments, reslice_moments,
+                                 sidecar_path)
         info = load_for_resume(module, args.resume, topo)
         engine.after_load()
         start_step = info["step"] + 1
@@ -623,15 +656,21 @@ def main(argv=None) -> None:
             side = sidecar_path(info["file"])
             if os.path.exists(side):
                 side_obj = torch.load(side, map_location="cpu", weights_only=False)
-                engine.optimizer.load_state_dict(side_obj.get("optimizer", side_obj))
+                engine.load_optimizer_state(side_obj.get("optimizer", side_obj))
                 restored.append("optimizer")
                 if topo.dp == 1:
                     resume_side = side_obj  # files without per-rank state: RNG / data position of dp rank 0
-            st = load_rank_state(info["file"], info["step"], topo)
-            if st is not None:
-                resume_side = st
-            if resume_side is not None and "rng" in resume_side:
-                restored.append("RNG and data position")
+        else:
+            moments = merged_optimizer_moments(args.resume, info["headers"])
+            if moments is not None:
+                engine.load_optimizer_state(reslice_moments(module, info["full"], moments, topo.tp_rank, topo.tp))
+                restored.append("optimizer (merged and re-sliced)")
+        st, exact = find_rank_state(info["file"], info["step"], topo)
+        if st is not None:
+            resume_side = st
+        if resume_side is not None and "rng" in resume_side:
+            restored.append("RNG and data position" + ("" if exact or info["same_layout"] else
+                                                       " (of the same DP rank)"))
         if rank == 0:
             how = "its own shard" if info["same_layout"] else "the merged shards of another TP/PP/EP layout"
             print(f"[resume] step {info['step']} from {args.resume} ({how})"
@@ -786,7 +825,7 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
                     wandb.log({"eval/loss": ev, "step": step}, step=step)
         if args.save_interval and step % args.save_interval == 0:
             from .utils.ckpt import rng_state
-            side = {"optimizer": engine.optimizer.state_dict(), "rng": rng_state()}
+            side = {"optimizer": engine.optimizer_state(), "rng": rng_state()}
             if engine.dropout_seed is not None:  # fused dropout masks continue where they stopped
                 side["dropout_seed"] = int(engine.dropout_seed.item())
             if hasattr(train_loader, "state_dict"):

@@ -275,6 +275,8 @@ def merge_shards(objs: List[dict]) -> Dict[str, torch.Tensor]:
             full[fk] = torch.cat(shards, 1)
     if "lm_head.weight" not in full and "tr.wte.weight" in full:
         full["lm_head.weight"] = full["tr.wte.weight"]
+    if "tr.wte.weight" not in full and "lm_head.weight" in full:
+        full["tr.wte.weight"] = full["lm_head.weight"]
     return full
 
 
@@ -294,8 +296,64 @@ def load_for_resume(module, path: str, topo) -> dict:
         return {"step": int(obj.get("step", 0)), "same_layout": True, "file": own}
     objs = [head if os.path.abspath(f) == os.path.abspath(path) else
             torch.load(f, map_location="cpu", weights_only=False) for f in step_files(path)]
-    load_from_full(module, merge_shards(objs), topo.tp_rank, topo.tp)
-    return {"step": int(head.get("step", 0)), "same_layout": False, "file": path}
+    full = merge_shards(objs)
+    load_from_full(module, full, topo.tp_rank, topo.tp)
+    return {"step": int(head.get("step", 0)), "same_layout": False, "file": path, "full": full,
+            "headers": [{"cfg": o["cfg"], "topo": o.get("topo")} for o in objs]}
+
+
+def merged_optimizer_moments(path: str, headers: List[dict]) -> Optional[dict]:
+    """Dense AdamW moments of the step ``path`` belongs to, merged from every shard's
+    sidecar written in the by-name format (``{"step", "m", "v"}`` keyed like the dense
+    GPT state dict), or None when a sidecar is missing or in another format."""
+    files = step_files(path)
+    sides = []
+    for f in files:
+        sp = sidecar_path(f)
+        if not os.path.exists(sp):
+            return None
+        st = torch.load(sp, map_location="cpu", weights_only=False).get("optimizer", {})
+        if st.get("format") != "by_name":
+            return None
+        sides.append(st)
+    out = {"step": int(sides[0]["step"])}
+    for key in ("m", "v"):
+        out[key] = merge_shards([{"model": st[key], **h} for st, h in zip(sides, headers)])
+    return out
+
+
+def reslice_moments(module, full_weights: dict, moments: dict, tp_rank: int, tp: int) -> dict:
+    """This rank's by-name optimizer state from dense moments (parameters without
+    moments start at zero)."""
+    out = {"format": "by_name", "step": moments["step"]}
+    names = {n for n, _ in module.named_parameters()}
+    for key in ("m", "v"):
+        dense = {k: moments[key].get(k, torch.zeros_like(w)) for k, w in full_weights.items()}
+        local = shard_from_full(module, dense, tp_rank, tp)
+        out[key] = {k: v for k, v in local.items() if k in names}
+    return out
+
+
+def find_rank_state(ckpt_path: str, step: int, topo) -> Tuple[Optional[dict], bool]:
+    """(state, exact): this rank's own state file of the same layout (exact), or else,
+    when the checkpoint's run had the same DP degree, the file of its rank with this
+    rank's dp_rank and all other coordinates 0 (same data stream), or (None, False)."""
+    st = load_rank_state(ckpt_path, step, topo)
+    if st is not None:
+        return st, True
+    from ..topo import rank_from_coords
+    d = os.path.dirname(ckpt_path)
+    probe = rank_state_path(d, step, 0)
+    if not os.path.exists(probe):
+        return None, False
+    lay = torch.load(probe, map_location="cpu", weights_only=False).get("layout")
+    if not lay or int(lay[0]) != topo.dp:
+        return None, False
+    dp, ep, tp, pp = (int(x) for x in lay)
+    path = rank_state_path(d, step, rank_from_coords(topo.dp_rank, 0, 0, 0, dp, ep, tp, pp))
+    if not os.path.exists(path):
+        return None, False
+    return torch.load(path, map_location="cpu", weights_only=False), False
 
 
 def main(argv=None) -> None:

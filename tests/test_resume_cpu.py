@@ -169,3 +169,46 @@ def test_merge_and_resume_on_another_layout(tmp_path):
     assert info["same_layout"] and info["step"] == 5
     for k, v in dense.items():
         assert torch.equal(m.state_dict()[k], v), k
+
+
+def _main_plain(rank, world, out_dir, extra):
+    from heiretsu_b200.trainer import main
+
+    main(["--device", "cpu", "--dist_backend", "gloo", "--synthetic_data", "--n_layer", "4", "--n_head", "2",
+          "--n_embed", "32", "--block_size", "16", "--batch_size", "2", "--grad_accum_steps", "2", "--dropout", "0",
+          "--eval_interval", "1000", "--eval_iters", "1", "--out_dir", out_dir, "--seed", "3", "--learning_rate",
+          "3e-3", "--pg_timeout_s", "60"] + extra)
+
+
+def test_resume_on_another_layout_continues_the_run(tmp_path):
+    """A tied tp2 x pp2 run saved at step 2, resumed by one dense process (weights, AdamW
+    moments merged from the four shard sidecars and re-sliced, data position of dp rank
+    0), reaches the tp2 x pp2 run's own step-4 weights; a weights-only resume does not."""
+    from dist_util import run_ranks_raw
+
+    from heiretsu_b200.trainer import main
+    from heiretsu_b200.utils.ckpt import merge_shards, step_files
+
+    a, b, c = tmp_path / "a", tmp_path / "b", tmp_path / "c"
+    for d in (a, b, c):
+        d.mkdir()
+    lay = ["--tp", "2", "--pp", "2", "--pp_tie_embeddings", "1"]
+    res = run_ranks_raw(_main_plain, 4, str(a), lay + ["--max_iters", "4", "--save_interval", "2"], init=False,
+                        timeout=300)
+    assert all(st == "ok" for st, _ in res), res
+    shard2 = os.fspath(a / "ckpt_0000002_pp1_ep0_tp1.pt")
+    single = ["--device", "cpu", "--synthetic_data", "--n_layer", "4", "--n_head", "2", "--n_embed", "32",
+              "--block_size", "16", "--batch_size", "2", "--grad_accum_steps", "2", "--dropout", "0",
+              "--eval_interval", "1000", "--eval_iters", "1", "--seed", "3", "--learning_rate", "3e-3",
+              "--max_iters", "4", "--save_interval", "4", "--resume", shard2]
+    main(single + ["--out_dir", str(b)])
+    ref = merge_shards([torch.load(f, weights_only=False) for f in step_files(os.fspath(a / "ckpt_0000004_pp0_ep0_tp0.pt"))])
+    got = torch.load(b / "ckpt_0000004.pt", weights_only=False)["model"]
+    err = max((got[k] - ref[k]).abs().max().item() for k in ref)
+    assert err < 2e-5, err
+    for f in step_files(shard2):  # weights only: the optimizer restarts
+        os.remove(os.path.join(os.path.dirname(f), "optim_" + os.path.basename(f)[len("ckpt_"):]))
+    main(single + ["--out_dir", str(c)])
+    got_c = torch.load(c / "ckpt_0000004.pt", weights_only=False)["model"]
+    err_c = max((got_c[k] - ref[k]).abs().max().item() for k in ref)
+    assert err_c > 50 * max(err, 1e-7), (err, err_c)
