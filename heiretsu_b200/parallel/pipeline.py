@@ -1,9 +1,17 @@
-"""GPipe pipeline parallelism (fill / drain) with NCCL point-to-point.
+"""Pipeline parallelism with NCCL point-to-point: GPipe (fill / drain) and 1F1B.
 
-Same stage partition, parameter names and schedule as the reference
+Same stage partition, parameter names and default schedule as the reference
 (pipeline.py:19-340): contiguous balanced layer ranges; the first stage owns
 ``wte``/``wpe``, the last ``ln_f``/``lm_head`` (tied only when both live on
 the same stage); all M forwards, then all M backwards in reverse.
+
+``schedule="1f1b"`` (an addition; the reference lists it as future work,
+README.md:131) runs the one-forward-one-backward schedule of PipeDream-Flush
+(Narayanan et al., 2021): stage s runs min(pp - s - 1, M) warm-up forwards,
+then alternates one forward and one backward, then drains the remaining
+backwards. It computes the same gradients as GPipe (micro-batch gradients
+are summed in another order) while stage s keeps at most pp - s micro-batches
+of activations instead of M.
 
 Differences, all deliberate:
 
@@ -208,7 +216,12 @@ class PipelineState:
 class GPipeEngine:
     """Fill/drain schedule over the stages of one pipeline group."""
 
-    def __init__(self, stage: StageModule, topo, boundary_dtype: torch.dtype = torch.float32):
+    def __init__(self, stage: StageModule, topo, boundary_dtype: torch.dtype = torch.float32,
+                 schedule: str = "gpipe"):
+        if schedule not in ("gpipe", "1f1b"):
+            raise ValueError(f"unknown pipeline schedule {schedule!r} (gpipe | 1f1b)")
+        self.schedule = schedule
+        self.max_inflight = 0  # most micro-batches whose activations were held at once (last step)
         self.stage, self.topo = stage, topo
         self.pp_rank, self.pp_size = topo.pp_rank, topo.pp
         self.is_first, self.is_last = stage.is_first, stage.is_last
@@ -245,29 +258,38 @@ class GPipeEngine:
         return buf, self._irecv(buf, self.prev_rank, self._fwd_tag(m))
 
     # -- schedule -------------------------------------------------------------
+    def _forward_micro(self, loader, device, use_amp, amp_dtype, recv_x):
+        """Forward of one micro-batch on this stage: (stage output, loss on the last stage | None, aux)."""
+        idx, targets = loader.next_batch(device)
+        if not self.is_last:
+            targets = None
+        ctx = torch.autocast(device_type=device.type, dtype=amp_dtype, enabled=use_amp and not self.stage.fused)
+        with ctx:
+            x = self.stage.embed(idx) if self.is_first else recv_x
+            x, aux = self.stage.forward_blocks(x)
+            loss = self.stage.forward_head(x, targets)[1] if self.is_last else None
+        return x, loss, aux
+
+    def _as_input(self, buf: torch.Tensor, keep_graph: bool) -> torch.Tensor:
+        x = buf.to(torch.float32) if buf.dtype != torch.float32 else buf
+        if keep_graph:
+            x.requires_grad_(True)
+        return x
+
     def _run_forward(self, loader, micro_batches, device, use_amp, amp_dtype, batch_size, state, keep_graph):
         cfg = self.stage.cfg
         B, S, H = self.stage.boundary_batch(batch_size), cfg.block_size, cfg.n_embed
         pending_recv = self._recv_fwd(0, B, S, H, device) if not self.is_first else None
         sends = []
         for m in range(micro_batches):
-            idx, targets = loader.next_batch(device)
-            if not self.is_last:
-                targets = None
             recv_x = None
             if not self.is_first:
                 buf, works = pending_recv
                 self._wait(works)
                 if m + 1 < micro_batches:
                     pending_recv = self._recv_fwd(m + 1, B, S, H, device)
-                recv_x = buf.to(torch.float32) if buf.dtype != torch.float32 else buf
-                if keep_graph:
-                    recv_x.requires_grad_(True)
-            ctx = torch.autocast(device_type=device.type, dtype=amp_dtype, enabled=use_amp and not self.stage.fused)
-            with ctx:
-                x = self.stage.embed(idx) if self.is_first else recv_x
-                x, aux = self.stage.forward_blocks(x)
-                loss = self.stage.forward_head(x, targets)[1] if self.is_last else None
+                recv_x = self._as_input(buf, keep_graph)
+            x, loss, aux = self._forward_micro(loader, device, use_amp, amp_dtype, recv_x)
             if not self.is_last:
                 out = x.detach().to(self.boundary_dtype)
                 sends.append((out, self._isend(out, self.next_rank, self._fwd_tag(m))))
@@ -280,11 +302,29 @@ class GPipeEngine:
             state.aux_losses.append(aux)
         for _, works in sends:
             self._wait(works)
+        if keep_graph:
+            self.max_inflight = micro_batches
+
+    def _backward_micro(self, boundary, loss, aux, grad, micro_batches, scaler) -> None:
+        """Backward of one micro-batch: the last stage from (loss + aux) / M, the others
+        from the gradient of their output (plus their own aux / M)."""
+        scaled = scaler is not None and scaler.is_enabled()
+        if self.is_last:
+            loss_mb = (loss + aux) / micro_batches
+            (scaler.scale(loss_mb) if scaled else loss_mb).backward()
+        elif aux.requires_grad:
+            a = aux / micro_batches
+            torch.autograd.backward([boundary, scaler.scale(a) if scaled else a], [grad, None])
+        else:
+            boundary.backward(grad)
 
     def forward_backward(self, loader, micro_batches: int, device: torch.device, use_amp: bool,
                          amp_dtype: torch.dtype, scaler=None, batch_size: int = 1,
                          aux_loss_coef: float = 0.01) -> Tuple[Optional[torch.Tensor], torch.Tensor]:
         """One optimizer step's worth of forward and backward; returns (mean loss on the last stage | None, aux)."""
+        if self.schedule == "1f1b":
+            return self._forward_backward_1f1b(loader, micro_batches, device, use_amp, amp_dtype, scaler,
+                                               batch_size)
         state = PipelineState()
         self._run_forward(loader, micro_batches, device, use_amp, amp_dtype, batch_size, state, keep_graph=True)
         total_aux = (torch.stack([a.detach().float() for a in state.aux_losses]).sum()
@@ -298,28 +338,18 @@ class GPipeEngine:
             g0 = torch.empty_like(state.boundaries[micro_batches - 1], dtype=self.boundary_dtype)
             pending = (g0, self._irecv(g0, self.next_rank, self._bwd_tag(micro_batches - 1)))
         for m in reversed(range(micro_batches)):
-            aux = state.aux_losses[m]
+            grad, boundary, loss = None, None, None
             if self.is_last:
-                loss_mb = (state.losses[m] + aux) / micro_batches
-                if scaler is not None and scaler.is_enabled():
-                    scaler.scale(loss_mb).backward()
-                else:
-                    loss_mb.backward()
+                loss = state.losses[m]
             else:
                 gbuf, works = pending
                 self._wait(works)
                 if m > 0:
                     nxt = torch.empty_like(state.boundaries[m - 1], dtype=self.boundary_dtype)
                     pending = (nxt, self._irecv(nxt, self.next_rank, self._bwd_tag(m - 1)))
-                grad = gbuf.to(state.boundaries[m].dtype)
-                if aux.requires_grad:
-                    if scaler is not None and scaler.is_enabled():
-                        torch.autograd.backward([state.boundaries[m], scaler.scale(aux / micro_batches)],
-                                                [grad, None])
-                    else:
-                        torch.autograd.backward([state.boundaries[m], aux / micro_batches], [grad, None])
-                else:
-                    state.boundaries[m].backward(grad)
+                boundary = state.boundaries[m]
+                grad = gbuf.to(boundary.dtype)
+            self._backward_micro(boundary, loss, state.aux_losses[m], grad, micro_batches, scaler)
             if not self.is_first:
                 gin = state.recv_inputs[m].grad.to(self.boundary_dtype)
                 sends.append((gin, self._isend(gin, self.prev_rank, self._bwd_tag(m))))
@@ -329,6 +359,103 @@ class GPipeEngine:
         if self.is_last and state.losses:
             with torch.no_grad():
                 return torch.stack([l.detach().float() for l in state.losses]).mean(), total_aux.detach()
+        return None, total_aux.detach()
+
+    # -- 1F1B -------------------------------------------------------------------
+    def _batch_p2p(self, ops: list) -> list:
+        """Post the point-to-point ops of one step as one batch (one NCCL group): a send
+        and a receive in opposite directions between two stages then cannot wait on each
+        other, whatever order the two ranks reach them in."""
+        return dist.batch_isend_irecv(ops) if ops else []
+
+    def _forward_backward_1f1b(self, loader, M: int, device, use_amp, amp_dtype, scaler, batch_size):
+        """PipeDream-Flush 1F1B. Per stage s with W = min(pp - s - 1, M): W forwards, then
+        M - W rounds of (forward m + W, backward m), then the last W backwards, all in
+        micro-batch order. Between stages s and s + 1 the two ranks post matching batches:
+        a send of an activation together with the receive of a gradient on one side, the
+        send of that gradient together with the receive of the next activation on the other.
+        """
+        cfg = self.stage.cfg
+        B, S, H = self.stage.boundary_batch(batch_size), cfg.block_size, cfg.n_embed
+        warm = min(self.pp_size - self.pp_rank - 1, M)
+        steady = M - warm
+        P2P = dist.P2POp
+        held = []  # FIFO of (recv_x, boundary, loss, aux) for forwards whose backward is pending
+        keep = []  # tensors whose sends are in flight, with their works
+        losses, auxes = [], []
+        self.max_inflight = 0
+
+        def new_act():
+            return torch.empty((B, S, H), device=device, dtype=self.boundary_dtype)
+
+        def recv_act(m):
+            buf = new_act()
+            self._wait(self._batch_p2p([P2P(dist.irecv, buf, self.prev_rank, tag=self._fwd_tag(m))]))
+            return buf
+
+        def forward(m, buf):
+            recv_x = self._as_input(buf, True) if buf is not None else None
+            x, loss, aux = self._forward_micro(loader, device, use_amp, amp_dtype, recv_x)
+            held.append((recv_x, x, loss, aux))
+            self.max_inflight = max(self.max_inflight, len(held))
+            auxes.append(aux.detach().float())
+            if loss is not None:
+                losses.append(loss.detach().float())
+            return None if self.is_last else x.detach().to(self.boundary_dtype)
+
+        def backward(grad_buf):
+            recv_x, x, loss, aux = held.pop(0)
+            grad = grad_buf.to(x.dtype) if grad_buf is not None else None
+            self._backward_micro(x, loss, aux, grad, M, scaler)
+            return None if self.is_first else recv_x.grad.to(self.boundary_dtype)
+
+        def send(t, peer, tag):
+            keep.append((t, self._batch_p2p([P2P(dist.isend, t, peer, tag=tag)])))
+
+        # warm-up forwards
+        for m in range(warm):
+            out = forward(m, None if self.is_first else recv_act(m))
+            send(out, self.next_rank, self._fwd_tag(m))
+        # steady state: one forward, one backward
+        buf = recv_act(warm) if steady > 0 and not self.is_first else None
+        for i in range(steady):
+            f = warm + i
+            out = forward(f, buf)
+            gbuf = None
+            if not self.is_last:
+                gbuf = torch.empty_like(out)
+                works = self._batch_p2p([P2P(dist.isend, out, self.next_rank, tag=self._fwd_tag(f)),
+                                         P2P(dist.irecv, gbuf, self.next_rank, tag=self._bwd_tag(i))])
+                self._wait(works)
+                keep.append((out, []))
+            gin = backward(gbuf)
+            if self.is_first:
+                buf = None
+            elif i == steady - 1:
+                send(gin, self.prev_rank, self._bwd_tag(i))
+            else:
+                buf = new_act()
+                works = self._batch_p2p([P2P(dist.isend, gin, self.prev_rank, tag=self._bwd_tag(i)),
+                                         P2P(dist.irecv, buf, self.prev_rank, tag=self._fwd_tag(f + 1))])
+                self._wait(works)
+                keep.append((gin, []))
+        # drain: the remaining backwards
+        for b in range(steady, M):
+            gbuf = None
+            if not self.is_last:
+                gbuf = new_act()
+                self._wait(self._batch_p2p([P2P(dist.irecv, gbuf, self.next_rank, tag=self._bwd_tag(b))]))
+            gin = backward(gbuf)
+            if not self.is_first:
+                send(gin, self.prev_rank, self._bwd_tag(b))
+        for _, works in keep:
+            self._wait(works)
+
+        total_aux = torch.stack(auxes).sum() if auxes else torch.zeros((), device=device)
+        if self.pp_size > 1 and dist.is_initialized() and self.topo.pp_group is not None:
+            dist.all_reduce(total_aux, op=dist.ReduceOp.SUM, group=self.topo.pp_group)
+        if self.is_last and losses:
+            return torch.stack(losses).mean(), total_aux.detach()
         return None, total_aux.detach()
 
     @torch.no_grad()

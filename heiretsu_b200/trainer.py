@@ -104,6 +104,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--engine", type=str, default="auto", choices=["auto", "fused", "plain"])
     p.add_argument("--clip_mode", type=str, default="global", choices=["global", "local"])
     p.add_argument("--pp_boundary_dtype", type=str, default="fp32", choices=["fp32", "bf16"])
+    p.add_argument("--pp_schedule", type=str, default="gpipe", choices=["gpipe", "1f1b"],
+                   help="pp > 1: gpipe (the reference: all forwards, then all backwards) or 1f1b (one forward, "
+                        "one backward; stage s holds at most pp - s micro-batches of activations)")
     p.add_argument("--pp_tie_embeddings", type=int, default=0, choices=[0, 1],
                    help="pp > 1: keep the first stage's wte and the last stage's lm_head equal (gradients summed "
                         "between the two stages), i.e. the tied dense GPT; 0 = the reference's untied stages")
@@ -339,7 +342,8 @@ class Engine:
                            and not self.use_pipeline and bool(getattr(args, "overlap_dp", 0)))
         if self.use_pipeline:
             bd = torch.float32 if args.pp_boundary_dtype == "fp32" else torch.bfloat16
-            self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd)
+            self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd,
+                                    schedule=getattr(args, "pp_schedule", "gpipe"))
         # CUDA-graph replay of the whole fused step (forward, backward, DP
         # reduction, clipping, AdamW) once shapes are known; the first
         # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).

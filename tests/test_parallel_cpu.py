@@ -84,7 +84,7 @@ def test_parallel_matches_dense(dp, tp, moe, ep):
         assert gerr < 1e-5, (rank, gerr, worst)
 
 
-def _worker_pp(rank, world, pp, tp, accum, dp=1, ep=1, moe=False):
+def _worker_pp(rank, world, pp, tp, accum, dp=1, ep=1, moe=False, schedule="gpipe"):
     import torch.distributed as dist
 
     from heiretsu_b200.config import GPTConfig
@@ -123,7 +123,7 @@ def _worker_pp(rank, world, pp, tp, accum, dp=1, ep=1, moe=False):
         grads = g if grads is None else {k: grads[k] + g[k] for k in g}
     stage = StageModule(GPTConfig(**cfg_kw), topo, topo.pp_rank, topo.pp)
     load_from_full(stage, full_state, topo.tp_rank, topo.tp)
-    eng = GPipeEngine(stage, topo)
+    eng = GPipeEngine(stage, topo, schedule=schedule)
     loss, _ = eng.forward_backward(L(), accum, torch.device("cpu"), False, torch.bfloat16, None, 4)
     average_gradients(stage, topo.dp_group)
     if loss is not None and topo.dp_group is not None:
@@ -143,6 +143,7 @@ def _worker_pp(rank, world, pp, tp, accum, dp=1, ep=1, moe=False):
     if stage.is_last:
         out["head_grad"] = stage.lm_head.weight.grad.clone()
     out["tied_dense"] = grads["tr.wte.weight"].clone()
+    out["stage"], out["inflight"] = topo.pp_rank, eng.max_inflight
     return out
 
 
@@ -160,7 +161,24 @@ def test_pipeline_matches_dense(pp, tp, dp, ep, moe):
     assert (tied - first["tied_dense"]).abs().max().item() < 1e-5
 
 
-def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0, ep=1, moe=False):
+@pytest.mark.parametrize("pp,tp,dp,ep,moe,accum", [(2, 1, 1, 1, False, 4), (4, 1, 1, 1, False, 6),
+                                                   (4, 1, 1, 1, False, 2), (2, 2, 1, 1, False, 3),
+                                                   (2, 1, 2, 1, False, 4), (2, 1, 1, 2, True, 4)])
+def test_1f1b_matches_dense(pp, tp, dp, ep, moe, accum):
+    """The 1F1B schedule gives the dense model's loss and gradients (also with fewer
+    micro-batches than stages), and stage s never holds more than pp - s micro-batches
+    of activations (GPipe holds all of them)."""
+    res = run_ranks(_worker_pp, pp * tp * dp * ep, pp, tp, accum, dp, ep, moe, "1f1b")
+    for r in res:
+        assert r["loss_err"] < 1e-5
+        assert r["gerr"] < 1e-5
+        assert r["inflight"] == min(pp - r["stage"], accum), r
+    first = [r for r in res if "wte_grad" in r][0]
+    last = [r for r in res if "head_grad" in r][0]
+    assert ((first["wte_grad"] + last["head_grad"]) - first["tied_dense"]).abs().max().item() < 1e-5
+
+
+def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0, ep=1, moe=False, extra=()):
     """Five optimizer steps of the training engine (AdamW, global-norm clip) on
     this layout; returns the logged losses and those of a single-process dense
     engine fed the concatenation of the DP ranks' micro-batches."""
@@ -208,7 +226,7 @@ def _worker_curve(rank, world, dp, tp, pp, accum, steps, tie=0, ep=1, moe=False)
 
     topo = init_topology(dp=dp, ep=ep, tp=tp, pp=pp)
     args = build_argparser().parse_args(flags + ["--dp", str(dp), "--ep", str(ep), "--tp", str(tp), "--pp", str(pp),
-                                                 "--pp_tie_embeddings", str(tie)])
+                                                 "--pp_tie_embeddings", str(tie)] + list(extra))
     eng = Engine(args, topo, torch.device("cpu"), cfg)
     load_from_full(eng.module, full_state, topo.tp_rank, topo.tp)
     if tie and eng.module.is_last:
@@ -244,6 +262,21 @@ def test_five_step_loss_curve_matches_dense(dp, tp, pp, tie, ep, moe):
     for losses, ref in res:
         assert ref[-1] < ref[0]
         if losses[0] is None:  # pipeline stages before the last log no loss
+            continue
+        checked += 1
+        for a, b in zip(losses, ref):
+            assert abs(a - b) < 1e-4, (losses, ref)
+    assert checked >= 1
+
+
+@pytest.mark.parametrize("dp,tp,pp,tie", [(1, 2, 2, 1), (2, 1, 2, 0)])
+def test_1f1b_training_follows_dense(dp, tp, pp, tie):
+    """--pp_schedule 1f1b through the trainer: five AdamW steps with clipping follow the
+    single-process loss curve (four micro-batches, so the steady state is exercised)."""
+    res = run_ranks(_worker_curve, dp * tp * pp, dp, tp, pp, 4, 5, tie, 1, False, ("--pp_schedule", "1f1b"))
+    checked = 0
+    for losses, ref in res:
+        if losses[0] is None:
             continue
         checked += 1
         for a, b in zip(losses, ref):
