@@ -22,6 +22,7 @@ from typing import Optional, Tuple
 
 import torch
 import torch.nn as nn
+import torch.utils.checkpoint
 import torch.nn.functional as F
 
 from ..config import GPTConfig, make_moe_config
@@ -125,6 +126,26 @@ def make_block(cfg: GPTConfig, layer_idx: int, tp_group=None, tp_rank: int = 0, 
     return BlockTP(cfg, tp_group, tp_rank, tp_world_size)
 
 
+def run_blocks(blocks, x: torch.Tensor, recompute: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Plain-path block loop: x through every block, returning (x, summed aux loss).
+
+    ``recompute`` (activation checkpointing, absent from the reference, whose
+    README.md:127 lists it as future work) keeps only each block's input during a
+    training forward and re-runs the block in backward (non-reentrant
+    ``torch.utils.checkpoint``, which restores the RNG and autocast state, so the
+    dropout masks and the bf16 casts are the forward's). Collectives inside a block
+    (TP all-reduces, EP all-to-alls) are re-issued in the same order on every rank.
+    """
+    aux_total = torch.zeros((), device=x.device, dtype=x.dtype)
+    for blk in blocks:
+        if recompute and blk.training and torch.is_grad_enabled():
+            x, aux = torch.utils.checkpoint.checkpoint(blk, x, use_reentrant=False)
+        else:
+            x, aux = blk(x)
+        aux_total = aux_total + aux
+    return x, aux_total
+
+
 def init_gpt_weights(module: nn.Module, n_layer: int) -> None:
     """NanoGPT init: N(0, 0.02) everywhere, c_proj std scaled by (2L)^-0.5, zero biases.
 
@@ -169,6 +190,7 @@ class GPT(nn.Module):
         self.tr.wte.weight = self.lm_head.weight  # weight tying
         init_gpt_weights(self, cfg.n_layer)
         self.fused = False  # set by heiretsu_b200.models.fused.enable_fused
+        self.recompute = False  # activation checkpointing of the plain path (run_blocks)
 
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None, return_logits: bool = True):
         B, T = idx.shape
@@ -179,10 +201,7 @@ class GPT(nn.Module):
             return gpt_forward_fused(self, idx, targets, return_logits=return_logits)
         pos = torch.arange(T, device=idx.device)
         x = self.tr.wte(idx) + self.tr.wpe(pos)[None]
-        aux_total = torch.zeros((), device=x.device, dtype=x.dtype)
-        for blk in self.tr.h:
-            x, aux = blk(x)
-            aux_total = aux_total + aux
+        x, aux_total = run_blocks(self.tr.h, x, self.recompute)
         x = self.tr.ln_f(x)
         logits = self.lm_head(x)
         loss = None

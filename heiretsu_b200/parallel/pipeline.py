@@ -140,6 +140,7 @@ class StageModule(nn.Module):
             self.wte.weight = self.lm_head.weight
         init_gpt_weights(self, cfg.n_layer)
         self.fused = False
+        self.recompute = False  # activation checkpointing of the plain path (models.gpt.run_blocks)
         self.topo = topo
 
     # Fused tensor parallelism keeps the residual stream token-sharded: each
@@ -179,11 +180,8 @@ class StageModule(nn.Module):
         if self.fused and x.is_cuda:
             from ..models.fused import blocks_fused
             return blocks_fused(self.blocks, x, self.cfg)
-        aux = torch.zeros((), device=x.device, dtype=x.dtype)
-        for blk in self.blocks:
-            x, a = blk(x)
-            aux = aux + a
-        return x, aux
+        from ..models.gpt import run_blocks
+        return run_blocks(self.blocks, x, self.recompute)
 
     def forward_head(self, x: torch.Tensor, targets: Optional[torch.Tensor]):
         if self.fused and x.is_cuda:

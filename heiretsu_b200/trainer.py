@@ -130,6 +130,8 @@ def build_argparser() -> argparse.ArgumentParser:
                    help="constant (the reference) or linear warmup then cosine decay to --min_lr at --max_iters")
     p.add_argument("--warmup_iters", type=int, default=0)
     p.add_argument("--min_lr", type=float, default=0.0)
+    p.add_argument("--activation_checkpointing", type=int, default=0, choices=[0, 1],
+                   help="plain engine: keep only each block's input and recompute the block in backward")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
     return p
@@ -290,6 +292,11 @@ class Engine:
         if self.fused:
             from .ops._C import load as _load
             _load()  # fail loudly if the extension is missing
+        if getattr(args, "activation_checkpointing", 0):
+            if self.fused:
+                raise ValueError("--activation_checkpointing runs on the plain engine (--engine plain); the fused "
+                                 "engine keeps every block's activations")
+            self.module.recompute = True
         self.dropout_seed = None
         if self.fused and cfg.dropout > 0:
             # Device seed of the fused dropout masks: different per DP / PP rank
