@@ -130,6 +130,8 @@ def build_argparser() -> argparse.ArgumentParser:
                    help="constant (the reference) or linear warmup then cosine decay to --min_lr at --max_iters")
     p.add_argument("--warmup_iters", type=int, default=0)
     p.add_argument("--min_lr", type=float, default=0.0)
+    p.add_argument("--zero_stage", type=int, default=0, choices=[0, 1],
+                   help="plain engine: 1 = shard the AdamW moments over the DP group (ZeRO stage 1)")
     p.add_argument("--activation_checkpointing", type=int, default=0, choices=[0, 1],
                    help="plain engine: keep only each block's input and recompute the block in backward")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
@@ -292,6 +294,9 @@ class Engine:
         if self.fused:
             from .ops._C import load as _load
             _load()  # fail loudly if the extension is missing
+        if getattr(args, "zero_stage", 0) and self.fused:
+            raise ValueError("--zero_stage 1 runs on the plain engine (--engine plain); the fused engine keeps "
+                             "full AdamW moments in its flat buffers")
         if getattr(args, "activation_checkpointing", 0):
             if self.fused:
                 raise ValueError("--activation_checkpointing runs on the plain engine (--engine plain); the fused "
@@ -330,6 +335,13 @@ class Engine:
                                         weight_decay=args.weight_decay, max_grad_norm=args.grad_clip,
                                         mp_group=clip_group, mp_symm=mp_symm)
             self.scaler = None
+        elif getattr(args, "zero_stage", 0):
+            from .parallel.zero import ZeroAdamW
+
+            self.flat = None
+            self.optimizer = ZeroAdamW(self.module.named_parameters(), topo.dp_group, lr=args.learning_rate,
+                                       betas=tuple(args.betas), weight_decay=args.weight_decay)
+            self.scaler = torch.amp.GradScaler("cuda", enabled=(self.amp == "fp16"))
         else:
             self.flat = None
             self.optimizer = torch.optim.AdamW(self.module.parameters(), lr=args.learning_rate,
@@ -593,6 +605,11 @@ class Engine:
         """AdamW moments keyed by parameter name, for either engine (see FusedAdamW.moments_by_name)."""
         if self.fused:
             return self.optimizer.moments_by_name()
+        if hasattr(self.optimizer, "moments_by_name"):  # ZeroAdamW: gathers the DP shards (collective)
+            out = self.optimizer.moments_by_name()
+            if self.scaler is not None and self.scaler.is_enabled():
+                out["scaler"] = self.scaler.state_dict()
+            return out
         m, v, step = {}, {}, 0
         for name, p in self.module.named_parameters():
             st = self.optimizer.state.get(p)
@@ -609,8 +626,10 @@ class Engine:
         if st.get("format") != "by_name":
             self.optimizer.load_state_dict(st)
             return
-        if self.fused:
+        if self.fused or hasattr(self.optimizer, "load_moments_by_name"):
             self.optimizer.load_moments_by_name(st)
+            if not self.fused and "scaler" in st and self.scaler is not None and self.scaler.is_enabled():
+                self.scaler.load_state_dict(st["scaler"])
             return
         for name, p in self.module.named_parameters():
             if name in st["m"]:
