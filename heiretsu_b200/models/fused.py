@@ -47,6 +47,13 @@ def fused_supported(cfg, topo=None) -> Tuple[bool, str]:
         return False, "fused dropout needs n_embed % 4 == 0"
     if cfg.num_experts > 0 and topo is not None and getattr(topo, "ep", 1) > 8:
         return False, "fused expert parallelism exchanges partials over NVLink within one node (ep <= 8)"
+    if topo is not None and hasattr(topo, "on_one_node"):
+        # Fused TP and EP exchange through CUDA IPC peer mappings, which exist only between
+        # GPUs of one node; a group that spans nodes runs the plain (NCCL) path.
+        if topo.tp > 1 and not topo.on_one_node(topo.tp_ranks):
+            return False, "fused tensor parallelism needs each TP group on one node (this one spans nodes)"
+        if cfg.num_experts > 0 and topo.ep > 1 and not topo.on_one_node(topo.ep_ranks):
+            return False, "fused expert parallelism needs each EP group on one node (this one spans nodes)"
     return True, ""
 
 

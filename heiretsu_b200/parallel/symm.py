@@ -10,6 +10,7 @@ barriers.
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional
 
 import torch
@@ -41,6 +42,10 @@ class SymmetricBuffer:
         self.world = dist.get_world_size(group)
         if self.world > 8:
             raise ValueError("symmetric buffers support at most 8 ranks per group (one NVSwitch node)")
+        per_node = int(os.environ.get("LOCAL_WORLD_SIZE", dist.get_world_size()) or dist.get_world_size())
+        if len({r // per_node for r in dist.get_process_group_ranks(group)}) > 1:
+            raise ValueError("symmetric buffers map peers through CUDA IPC, which needs every rank of the group "
+                             "on one node; this group spans nodes")
         self.device = device
         self.nbytes = nbytes
         with torch.cuda.device(device):

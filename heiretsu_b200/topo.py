@@ -15,6 +15,8 @@ from dataclasses import dataclass, field
 from datetime import timedelta
 from typing import List, Optional, Tuple
 
+import os
+
 import torch.distributed as dist
 
 
@@ -39,6 +41,22 @@ class Topology:
     pp_ranks: List[int] = field(default_factory=list)
     ep_ranks: List[int] = field(default_factory=list)
     dp_ranks: List[int] = field(default_factory=list)
+    # Processes per node (torchrun's LOCAL_WORLD_SIZE; torchrun numbers ranks node
+    # by node); 0 = every rank on one node.
+    local_world: int = 0
+
+    def node_of(self, rank: int) -> int:
+        return rank // (self.local_world or self.world_size or 1)
+
+    def on_one_node(self, ranks) -> bool:
+        """Whether these global ranks share one node, i.e. one NVLink/NVSwitch domain in
+        which CUDA IPC peer mappings work (the fused collectives need that)."""
+        return len({self.node_of(r) for r in ranks}) <= 1
+
+    def model_parallel_ranks(self) -> List[int]:
+        """Global ranks of this rank's model-parallel replica (same dp_rank)."""
+        per = self.ep * self.pp * self.tp
+        return list(range(self.dp_rank * per, (self.dp_rank + 1) * per))
 
     @property
     def is_distributed(self) -> bool:
@@ -132,7 +150,15 @@ def init_topology(dp: int, ep: int = 1, tp: int = 1, pp: int = 1, timeout: Optio
     return Topology(dp=dp, ep=ep, tp=tp, pp=pp, rank=rank, world_size=world, dp_rank=dp_rank, ep_rank=ep_rank,
                     pp_rank=pp_rank, tp_rank=tp_rank, tp_group=tp_group, pp_group=pp_group, ep_group=ep_group,
                     dp_group=dp_group, tp_ranks=mem["tp"], pp_ranks=mem["pp"], ep_ranks=mem["ep"],
-                    dp_ranks=mem["dp"])
+                    dp_ranks=mem["dp"], local_world=local_world_size(world))
+
+
+def local_world_size(world: int) -> int:
+    """Ranks per node from torchrun's LOCAL_WORLD_SIZE (default: all ``world`` ranks on one node)."""
+    n = int(os.environ.get("LOCAL_WORLD_SIZE", world) or world)
+    if n <= 0 or world % n:
+        raise ValueError(f"LOCAL_WORLD_SIZE {n} does not divide the world size {world}")
+    return n
 
 
 def cleanup() -> None:

@@ -25,6 +25,7 @@ from __future__ import annotations
 
 import argparse
 import contextlib
+import json
 import math
 import os
 import random
@@ -136,7 +137,94 @@ def build_argparser() -> argparse.ArgumentParser:
                    help="plain engine: keep only each block's input and recompute the block in backward")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
+    p.add_argument("--config_file", type=str, default=None,
+                   help="YAML, TOML or JSON file of flag values (keys = flag names without dashes); flags given on "
+                        "the command line override it")
+    p.add_argument("--save_config", type=str, default=None,
+                   help="write the resolved flags to this YAML/TOML/JSON file (by extension) and continue")
     return p
+
+
+def _load_config_file(path: str) -> dict:
+    ext = os.path.splitext(path)[1].lower()
+    if ext in (".yaml", ".yml"):
+        import yaml
+        with open(path) as f:
+            data = yaml.safe_load(f) or {}
+    elif ext == ".toml":
+        import tomllib
+        with open(path, "rb") as f:
+            data = tomllib.load(f)
+    elif ext == ".json":
+        with open(path) as f:
+            data = json.load(f)
+    else:
+        raise ValueError(f"--config_file {path}: extension must be .yaml, .yml, .toml or .json")
+    if not isinstance(data, dict):
+        raise ValueError(f"--config_file {path}: top level must be a mapping of flag names to values")
+    return data
+
+
+def _coerce(action, key: str, value):
+    """A config-file value as argparse would have produced it from the command line."""
+    if isinstance(action, (argparse._StoreTrueAction, argparse._StoreFalseAction)):
+        if not isinstance(value, bool):
+            raise ValueError(f"config key {key!r}: expected true/false, got {value!r}")
+        return value
+    if action.nargs is not None and action.nargs not in ("?",):
+        if not isinstance(value, (list, tuple)):
+            raise ValueError(f"config key {key!r}: expected a list, got {value!r}")
+        if isinstance(action.nargs, int) and len(value) != action.nargs:
+            raise ValueError(f"config key {key!r}: expected {action.nargs} values, got {len(value)}")
+        out = [action.type(v) if action.type is not None and v is not None else v for v in value]
+        vals = out
+    else:
+        out = action.type(value) if (action.type is not None and value is not None) else value
+        vals = [out]
+    if action.choices is not None:
+        for v in vals:
+            if v not in action.choices:
+                raise ValueError(f"config key {key!r}: {v!r} is not one of {list(action.choices)}")
+    return tuple(out) if isinstance(out, list) and isinstance(action.default, tuple) else out
+
+
+def parse_args(argv=None) -> argparse.Namespace:
+    """Command-line flags, with defaults taken from ``--config_file`` when given.
+
+    Precedence: command line > config file > built-in defaults. Unknown keys in
+    the file are an error, so a typo cannot silently fall back to a default."""
+    p = build_argparser()
+    pre, _ = p.parse_known_args(argv)
+    if pre.config_file:
+        data = _load_config_file(pre.config_file)
+        actions = {a.dest: a for a in p._actions if a.dest != "help"}
+        unknown = sorted(k for k in data if k.replace("-", "_") not in actions)
+        if unknown:
+            raise ValueError(f"--config_file {pre.config_file}: unknown keys {unknown}")
+        p.set_defaults(**{k.replace("-", "_"): _coerce(actions[k.replace("-", "_")], k, v) for k, v in data.items()
+                          if k.replace("-", "_") not in ("config_file", "save_config")})
+    args = p.parse_args(argv)
+    if args.save_config:
+        save_config(args, args.save_config)
+    return args
+
+
+def save_config(args: argparse.Namespace, path: str) -> None:
+    data = {k: (list(v) if isinstance(v, tuple) else v) for k, v in vars(args).items()
+            if k not in ("config_file", "save_config")}
+    ext = os.path.splitext(path)[1].lower()
+    with open(path, "w") as f:
+        if ext in (".yaml", ".yml"):
+            import yaml
+            yaml.safe_dump(data, f, sort_keys=False)
+        elif ext == ".json":
+            json.dump(data, f, indent=1)
+        elif ext == ".toml":
+            for k, v in data.items():  # flat keys: str, int, float, bool, list; None is left out
+                if v is not None:
+                    f.write(f"{k} = {json.dumps(v)}\n")
+        else:
+            raise ValueError(f"--save_config {path}: extension must be .yaml, .yml, .toml or .json")
 
 
 def pick_device(arg: str):
@@ -150,6 +238,10 @@ def pick_device(arg: str):
         lr = int(os.environ.get("LOCAL_RANK", "0")) if dev.index is None else dev.index
         return torch.device("cuda", lr), lr
     return dev, 0
+
+
+def on_one_node(topo, ranks) -> bool:
+    return topo.on_one_node(ranks) if hasattr(topo, "on_one_node") else True
 
 
 def mp_group_of(topo):
@@ -320,7 +412,10 @@ class Engine:
             from .optim import FusedAdamW
             from .parallel.flat import FlatParams
 
-            use_p2p = topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
+            # The DP reduction runs over NVLink peer memory when the DP group is on one node,
+            # else (a multi-node job) as NCCL all-reduces.
+            use_p2p = (topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
+                       and on_one_node(topo, topo.dp_ranks))
             self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo, self.tied is not None),
                                    grad_group=topo.dp_group if use_p2p else None,
                                    tp_group=topo.tp_group if topo.tp > 1 else None,
@@ -328,7 +423,7 @@ class Engine:
             self.module.fused = True
             clip_group = self.mp_group if args.clip_mode == "global" else None
             mp_symm = None
-            if clip_group is not None and device.type == "cuda":
+            if clip_group is not None and device.type == "cuda" and on_one_node(topo, topo.model_parallel_ranks()):
                 from .parallel.symm import SymmetricBuffer
                 mp_symm = SymmetricBuffer(clip_group, 16, device)
             self.optimizer = FusedAdamW(self.flat, lr=args.learning_rate, betas=args.betas,
@@ -647,7 +742,7 @@ class Engine:
 
 
 def main(argv=None) -> None:
-    args = build_argparser().parse_args(argv)
+    args = parse_args(argv)
     world_env = int(os.environ.get("WORLD_SIZE", "1"))
     distributed = world_env > 1
     device, local_rank = pick_device(args.device)
@@ -709,6 +804,12 @@ def main(argv=None) -> None:
     if rank == 0:
         print(f"[model] parameters: {n_params:,} ({n_params / 1e6:.1f}M) | engine="
               f"{'fused' if engine.fused else 'plain'}")
+        per_node = topo.local_world or topo.world_size
+        if topo.world_size > per_node:
+            dp_how = ("NVLink peer memory" if engine.reducer is not None and engine.reducer.backend == "p2p"
+                      else "NCCL all-reduce")
+            print(f"[nodes] {topo.world_size // per_node} nodes x {per_node} ranks | DP gradient reduction: "
+                  f"{dp_how}")
         if args.num_experts > 0:
             nm = sum(1 for i in range(args.n_layer) if cfg.is_moe_layer(i))
             print(f"[MoE] num_experts={args.num_experts}, top_k={args.top_k}, moe_layers={nm}/{args.n_layer}, "

@@ -5,78 +5,92 @@
 #   DP=8 bash run_train.sh
 #   DP=2 TP=2 PP=2 N_LAYER=36 N_HEAD=20 N_EMBED=1280 bash run_train.sh
 #   SYNTHETIC=1 MAX_ITERS=50 bash run_train.sh      # no dataset needed
+#   CONFIG_FILE=run.yaml bash run_train.sh          # flag values from a YAML/TOML/JSON file
+# Multi-node: run the same command on every node with NNODES, NODE_RANK and a
+# MASTER_ADDR that all nodes reach (node 0's address), e.g. on two 8-GPU nodes
+#   NNODES=2 NODE_RANK=0 MASTER_ADDR=10.0.0.1 DP=16 bash run_train.sh   # node 0
+#   NNODES=2 NODE_RANK=1 MASTER_ADDR=10.0.0.1 DP=16 bash run_train.sh   # node 1
+# Ranks are numbered node by node, so TP (innermost), then PP and EP groups
+# stay inside a node when tp*pp*ep divides the GPUs per node; the fused TP/EP
+# collectives use NVLink peer memory and need that. DP groups may span nodes:
+# their gradient reduction then runs as NCCL all-reduces (over the inter-node
+# network, e.g. InfiniBand with GPUDirect RDMA when NCCL finds it).
 set -euo pipefail
 
+# Topology and launch (always from the environment: the launcher needs the world size).
 DP=${DP:-4}
 TP=${TP:-1}
 PP=${PP:-1}
 EP=${EP:-1}
-
-NUM_EXPERTS=${NUM_EXPERTS:-0}
-TOP_K=${TOP_K:-2}
-MOE_FREQ=${MOE_FREQ:-2}
-AUX_LOSS_COEF=${AUX_LOSS_COEF:-0.01}
-
-N_LAYER=${N_LAYER:-24}
-N_HEAD=${N_HEAD:-16}
-N_EMBED=${N_EMBED:-1024}
-DROPOUT=${DROPOUT:-0.1}
-
-BATCH_SIZE=${BATCH_SIZE:-8}
-BLOCK_SIZE=${BLOCK_SIZE:-1024}
-GRAD_ACCUM=${GRAD_ACCUM:-4}
-MAX_ITERS=${MAX_ITERS:-50000}
-LEARNING_RATE=${LEARNING_RATE:-3e-4}
-WEIGHT_DECAY=${WEIGHT_DECAY:-0.1}
-GRAD_CLIP=${GRAD_CLIP:-1.0}
-AMP=${AMP:-bf16}
-ENGINE=${ENGINE:-auto}
-DEVICE=${DEVICE:-auto}
-DIST_BACKEND=${DIST_BACKEND:-nccl}
-
-EVAL_INTERVAL=${EVAL_INTERVAL:-500}
-EVAL_ITERS=${EVAL_ITERS:-100}
-SAVE_INTERVAL=${SAVE_INTERVAL:-5000}
-SAVE_PATH=${SAVE_PATH:-./checkpoints}
-DATA_DIR=${DATA_DIR:-data/fineweb10B}
-SYNTHETIC=${SYNTHETIC:-0}
-RESUME=${RESUME:-}
-
-WANDB=${WANDB:-0}
-WANDB_PROJECT=${WANDB_PROJECT:-heiretsu-fineweb}
-WANDB_MODE=${WANDB_MODE:-online}
-RUN_NAME=${RUN_NAME:-"heiretsu-$(date +%Y%m%d_%H%M%S)"}
-
 MASTER_ADDR=${MASTER_ADDR:-127.0.0.1}
 MASTER_PORT=${MASTER_PORT:-29500}
+NNODES=${NNODES:-1}
+NODE_RANK=${NODE_RANK:-0}
+CONFIG_FILE=${CONFIG_FILE:-}
 # Upper bound on the whole job; process-group timeouts end a stuck collective long before.
 JOB_TIMEOUT=${JOB_TIMEOUT:-0}
+SAVE_PATH=${SAVE_PATH:-./checkpoints}
+SYNTHETIC=${SYNTHETIC:-0}
+RESUME=${RESUME:-}
+NUM_EXPERTS=${NUM_EXPERTS:-0}
+WANDB=${WANDB:-0}
+
+# Run settings: "flag ENV_VAR default". Without CONFIG_FILE every flag is passed
+# (the env var or its preset default); with CONFIG_FILE only the env vars that
+# are set are passed, so everything else comes from the file.
+SPEC=(
+  "--data_dir DATA_DIR data/fineweb10B"
+  "--batch_size BATCH_SIZE 8"
+  "--block_size BLOCK_SIZE 1024"
+  "--n_layer N_LAYER 24"
+  "--n_head N_HEAD 16"
+  "--n_embed N_EMBED 1024"
+  "--dropout DROPOUT 0.1"
+  "--max_iters MAX_ITERS 50000"
+  "--learning_rate LEARNING_RATE 3e-4"
+  "--weight_decay WEIGHT_DECAY 0.1"
+  "--grad_clip GRAD_CLIP 1.0"
+  "--grad_accum_steps GRAD_ACCUM 4"
+  "--amp AMP bf16"
+  "--engine ENGINE auto"
+  "--device DEVICE auto"
+  "--dist_backend DIST_BACKEND nccl"
+  "--eval_interval EVAL_INTERVAL 500"
+  "--eval_iters EVAL_ITERS 100"
+  "--save_interval SAVE_INTERVAL 5000"
+  "--run_name RUN_NAME heiretsu-$(date +%Y%m%d_%H%M%S)"
+  "--seed SEED 1337"
+)
+ARGS=(--dp "${DP}" --tp "${TP}" --pp "${PP}" --ep "${EP}" --out_dir "${SAVE_PATH}")
+for row in "${SPEC[@]}"; do
+  read -r flag var def <<< "${row}"
+  if [[ -n "${!var:-}" ]]; then
+    ARGS+=("${flag}" "${!var}")
+  elif [[ -z ${CONFIG_FILE} ]]; then
+    ARGS+=("${flag}" "${def}")
+  fi
+done
+if [[ ${NUM_EXPERTS} -gt 0 ]]; then
+  ARGS+=(--num_experts "${NUM_EXPERTS}" --top_k "${TOP_K:-2}" --moe_freq "${MOE_FREQ:-2}"
+         --aux_loss_coef "${AUX_LOSS_COEF:-0.01}")
+fi
+[[ ${SYNTHETIC} != 0 ]] && ARGS+=(--synthetic_data)
+[[ -n ${RESUME} ]] && ARGS+=(--resume "${RESUME}")
+[[ -n ${CONFIG_FILE} ]] && ARGS+=(--config_file "${CONFIG_FILE}")
+[[ ${WANDB} != 0 ]] && ARGS+=(--wandb --wandb_project "${WANDB_PROJECT:-heiretsu-fineweb}"
+                              --wandb_mode "${WANDB_MODE:-online}")
 
 WORLD_SIZE=$((DP * TP * PP * EP))
-echo "run ${RUN_NAME}: dp=${DP} tp=${TP} pp=${PP} ep=${EP} (world ${WORLD_SIZE}); ${N_LAYER}L ${N_HEAD}H ${N_EMBED}D;" \
-     "micro-batch ${BATCH_SIZE} x ${BLOCK_SIZE}, accum ${GRAD_ACCUM}, global batch $((BATCH_SIZE * GRAD_ACCUM * DP))"
-
-EXTRA=()
-if [[ ${NUM_EXPERTS} -gt 0 ]]; then
-  EXTRA+=(--num_experts "${NUM_EXPERTS}" --top_k "${TOP_K}" --moe_freq "${MOE_FREQ}" --aux_loss_coef "${AUX_LOSS_COEF}")
+if (( WORLD_SIZE % NNODES != 0 )); then
+  echo "world size ${WORLD_SIZE} (dp*tp*pp*ep) is not a multiple of NNODES=${NNODES}" >&2; exit 2
 fi
-[[ ${SYNTHETIC} != 0 ]] && EXTRA+=(--synthetic_data)
-[[ -n ${RESUME} ]] && EXTRA+=(--resume "${RESUME}")
-[[ ${WANDB} != 0 ]] && EXTRA+=(--wandb --wandb_project "${WANDB_PROJECT}" --wandb_mode "${WANDB_MODE}")
+NPROC_PER_NODE=$((WORLD_SIZE / NNODES))
+echo "launch: dp=${DP} tp=${TP} pp=${PP} ep=${EP} (world ${WORLD_SIZE}, ${NNODES} node(s) x ${NPROC_PER_NODE});" \
+     "train.py ${ARGS[*]}"
 
 mkdir -p "${SAVE_PATH}"
 cd "$(dirname "$0")"
-LAUNCH=(python -m torch.distributed.run --nnodes=1 --nproc-per-node="${WORLD_SIZE}"
-        --master-addr "${MASTER_ADDR}" --master-port "${MASTER_PORT}")
+LAUNCH=(python -m torch.distributed.run --nnodes="${NNODES}" --node-rank="${NODE_RANK}"
+        --nproc-per-node="${NPROC_PER_NODE}" --master-addr "${MASTER_ADDR}" --master-port "${MASTER_PORT}")
 if [[ ${JOB_TIMEOUT} -gt 0 ]]; then LAUNCH=(timeout -k 60 "${JOB_TIMEOUT}" "${LAUNCH[@]}"); fi
-exec "${LAUNCH[@]}" train.py \
-  --data_dir "${DATA_DIR}" \
-  --batch_size "${BATCH_SIZE}" --block_size "${BLOCK_SIZE}" \
-  --n_layer "${N_LAYER}" --n_head "${N_HEAD}" --n_embed "${N_EMBED}" --dropout "${DROPOUT}" \
-  --max_iters "${MAX_ITERS}" --learning_rate "${LEARNING_RATE}" --weight_decay "${WEIGHT_DECAY}" \
-  --grad_clip "${GRAD_CLIP}" --grad_accum_steps "${GRAD_ACCUM}" --amp "${AMP}" --engine "${ENGINE}" \
-  --dp "${DP}" --tp "${TP}" --pp "${PP}" --ep "${EP}" --device "${DEVICE}" --dist_backend "${DIST_BACKEND}" \
-  --eval_interval "${EVAL_INTERVAL}" --eval_iters "${EVAL_ITERS}" \
-  --save_interval "${SAVE_INTERVAL}" --out_dir "${SAVE_PATH}" \
-  --run_name "${RUN_NAME}" --seed 1337 \
-  "${EXTRA[@]}"
+exec "${LAUNCH[@]}" train.py "${ARGS[@]}"

@@ -25,3 +25,25 @@ def test_run_train_sh_dp2_cpu(tmp_path):
     assert "training finished." in r.stdout
     assert "[eval] step 3" in r.stdout
     assert sorted(p.name for p in tmp_path.glob("ckpt_*.pt")), list(tmp_path.iterdir())
+
+
+def test_run_train_sh_two_nodes_cpu(tmp_path):
+    """NNODES=2: the same launcher command on two 'nodes' (two torchrun agents on this host,
+    one gloo rank each) forms one dp2 job; run settings come from a CONFIG_FILE."""
+    cfg = tmp_path / "run.yaml"
+    cfg.write_text("n_layer: 1\nn_head: 2\nn_embed: 32\nblock_size: 16\nbatch_size: 2\nmax_iters: 3\n"
+                   "eval_interval: 3\neval_iters: 1\ndropout: 0.0\nsynthetic_data: true\n")
+    base = dict(os.environ, DP="2", NNODES="2", DEVICE="cpu", DIST_BACKEND="gloo", AMP="none", GRAD_ACCUM="1",
+                SAVE_INTERVAL="3", SAVE_PATH=str(tmp_path), MASTER_PORT=str(_port()), JOB_TIMEOUT="240",
+                OMP_NUM_THREADS="1", CONFIG_FILE=str(cfg),
+                # launcher defaults that the file must override: command-line values only come from the file
+                N_LAYER="", N_HEAD="", N_EMBED="", BLOCK_SIZE="", BATCH_SIZE="", MAX_ITERS="", EVAL_INTERVAL="",
+                EVAL_ITERS="", DROPOUT="")
+    procs = [subprocess.Popen(["bash", os.path.join(ROOT, "run_train.sh")], cwd=ROOT,
+                              env=dict(base, NODE_RANK=str(n)), stdout=subprocess.PIPE, stderr=subprocess.PIPE,
+                              text=True) for n in range(2)]
+    outs = [p.communicate(timeout=300) for p in procs]
+    for p, (out, err) in zip(procs, outs):
+        assert p.returncode == 0, (out[-2000:], err[-3000:])
+    assert "training finished." in outs[0][0]
+    assert "[eval] step 3" in outs[0][0]

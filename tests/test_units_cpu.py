@@ -378,3 +378,45 @@ def test_lr_schedule(capsys, tmp_path):
           "--out_dir", str(tmp_path)])
     lrs = [l.split("| lr ")[1] for l in capsys.readouterr().out.splitlines() if "| lr " in l]
     assert lrs == ["5.000e-04", "1.000e-03", "0.000e+00"], lrs
+
+
+def test_node_locality_of_groups(monkeypatch):
+    """Ranks are numbered node by node (torchrun): on two 8-GPU nodes, TP/EP/PP groups of a
+    dp2 x ep2 x tp2 x pp2 job stay on one node, its DP groups span both; the fused path is
+    kept only for groups on one node (CUDA IPC peer mappings), DP falls back to NCCL."""
+    from heiretsu_b200.config import GPTConfig
+    from heiretsu_b200.models.fused import fused_supported
+    from heiretsu_b200.topo import Topology, coords_from_rank, group_members, local_world_size
+
+    def topo(rank, dp, ep, tp, pp, per_node):
+        d, e, p, t = coords_from_rank(rank, dp, ep, tp, pp)
+        m = group_members(dp, ep, tp, pp, rank)
+        return Topology(dp=dp, ep=ep, tp=tp, pp=pp, rank=rank, world_size=dp * ep * tp * pp, dp_rank=d, ep_rank=e,
+                        pp_rank=p, tp_rank=t, tp_group=None, pp_group=None, ep_group=None, dp_group=None,
+                        tp_ranks=m["tp"], pp_ranks=m["pp"], ep_ranks=m["ep"], dp_ranks=m["dp"],
+                        local_world=per_node)
+
+    moe = GPTConfig(block_size=64, vocab_size=128, n_layer=2, n_head=2, n_embed=128, dropout=0.0, num_experts=4)
+    for r in range(16):
+        t = topo(r, 2, 2, 2, 2, 8)
+        assert t.on_one_node(t.tp_ranks) and t.on_one_node(t.ep_ranks) and t.on_one_node(t.pp_ranks)
+        assert not t.on_one_node(t.dp_ranks)
+        assert t.on_one_node(t.model_parallel_ranks())
+        assert fused_supported(moe, t)[0]
+    # tp4 over nodes of 2 GPUs: the TP group spans nodes -> plain path
+    t = topo(0, 1, 1, 4, 1, 2)
+    ok, why = fused_supported(moe, t)
+    assert not ok and "spans nodes" in why
+    t = topo(0, 1, 4, 1, 1, 2)
+    ok, why = fused_supported(moe, t)
+    assert not ok and "EP group" in why
+    # single node: local_world 0 (unset) means everything is on one node
+    t = topo(3, 8, 1, 1, 1, 0)
+    assert t.on_one_node(t.dp_ranks)
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "8")
+    assert local_world_size(16) == 8
+    monkeypatch.setenv("LOCAL_WORLD_SIZE", "3")
+    with pytest.raises(ValueError):
+        local_world_size(16)
+    monkeypatch.delenv("LOCAL_WORLD_SIZE")
+    assert local_world_size(4) == 4
