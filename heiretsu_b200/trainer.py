@@ -884,7 +884,7 @@ def main(argv=None) -> None:
 
 
 def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0, start_step=1) -> None:
-    from .utils.profiling import RegionTimer
+    from .utils.profiling import RegionTimer, rank_spread
 
     is_main = topo.is_main
     tokens_per_step = args.batch_size * args.block_size * args.grad_accum_steps
@@ -899,6 +899,7 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
         if wd is not None:
             wd.check()  # a failed peer is noticed here, before this step launches anything
         region_ms = None
+        spread = None  # per-rank device step times of a logging step (multi-rank runs)
         if args.region_timing_interval > 0 and step % args.region_timing_interval == 0:
             # Instrumented eager step (kept out of the dev_tok/s figure); every rank takes part.
             regions = RegionTimer(enabled=True)
@@ -920,11 +921,16 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
         if step % log_every == 0 or step == start_step:
             dev_str = ""
             if timer.enabled:
-                # every rank takes part in the max over ranks; all log on the same steps
-                step_ms = timer.summary().get("step", 0.0) / max(1, timed_steps)
+                # every rank takes part in the gather; all log on the same steps
+                per_rank = [t / max(1, timed_steps) for t in timer.per_rank().get("step", [0.0])]
+                step_ms = max(per_rank)
                 timed_steps = 0
                 if step_ms > 0:
                     dev_str = f" | dev_tok/s {topo.dp * tokens_per_step / (step_ms / 1e3):,.0f} ({step_ms:.2f} ms)"
+                    if len(per_rank) > 1:
+                        spread = rank_spread(per_rank)
+                        dev_str += (f" | rank ms {spread['min']:.2f}..{spread['max']:.2f} "
+                                    f"(slowest r{int(spread['slowest'])})")
             if is_main:
                 aux_str = f" | aux_loss {aux.item():.4f}" if args.num_experts > 0 else ""
                 ls = f"{loss_scalar.item():.4f}" if loss_scalar is not None else "n/a"
@@ -938,6 +944,10 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
                    "accum/steps": args.grad_accum_steps, "step": step}
             if region_ms:
                 log.update({f"time/{k}_ms": v for k, v in region_ms.items()})
+            if spread:
+                log.update({"speed/rank_step_ms_min": spread["min"], "speed/rank_step_ms_median": spread["median"],
+                            "speed/rank_step_ms_max": spread["max"], "speed/slowest_rank": int(spread["slowest"]),
+                            "speed/rank_imbalance": spread["imbalance"]})
             if args.num_experts > 0:
                 log["train/aux_loss"] = float(aux.item())
                 log.update(expert_load_metrics(module))

@@ -100,5 +100,36 @@ class RegionTimer:
         return out
 
 
+    def per_rank(self, group=None, reset: bool = True) -> Dict[str, List[float]]:
+        """Per-region total ms of every rank of ``group`` (one all-gather), in group-rank
+        order: the spread shows a straggler that the max alone hides.
+
+        Every rank of the group must call this with the same region names."""
+        self.collect()
+        names = list(self.totals)
+        vals = torch.tensor([self.totals[n] for n in names], dtype=torch.float64)
+        rows = [vals]
+        if dist.is_initialized() and names:
+            dev = torch.device("cuda", torch.cuda.current_device()) if dist.get_backend(group) == "nccl" \
+                else torch.device("cpu")
+            v = vals.to(dev)
+            parts = [torch.empty_like(v) for _ in range(dist.get_world_size(group))]
+            dist.all_gather(parts, v, group=group)
+            rows = [x.cpu() for x in parts]
+        out = {n: [float(r[i]) for r in rows] for i, n in enumerate(names)}
+        if reset:
+            self.totals.clear()
+            self.counts.clear()
+        return out
+
+
+def rank_spread(per_rank_ms: List[float]) -> Dict[str, float]:
+    """min / median / max of per-rank times, the slowest rank and max/min (imbalance)."""
+    srt = sorted(per_rank_ms)
+    lo, hi = srt[0], srt[-1]
+    return {"min": lo, "median": srt[len(srt) // 2], "max": hi, "slowest": float(per_rank_ms.index(hi)),
+            "imbalance": hi / lo if lo > 0 else float("inf")}
+
+
 def tokens_per_second(tokens_per_step_all_ranks: int, step_ms: Optional[float]) -> Optional[float]:
     return None if not step_ms else tokens_per_step_all_ranks / (step_ms / 1e3)

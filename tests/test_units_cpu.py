@@ -180,6 +180,25 @@ def test_region_timer_max_over_ranks():
     assert run_ranks(_timer_max_worker, 2) == [20.0, 20.0]
 
 
+def _timer_per_rank_worker(rank, world):
+    from heiretsu_b200.utils.profiling import RegionTimer, rank_spread
+
+    t = RegionTimer()
+    t._add("step", [12.0, 30.0, 10.0][rank])
+    pr = t.per_rank()["step"]
+    return pr, rank_spread(pr)
+
+
+def test_region_timer_per_rank_spread():
+    """Per-rank step times (all-gather) and their spread: the straggler is named."""
+    from dist_util import run_ranks
+
+    for pr, sp in run_ranks(_timer_per_rank_worker, 3):
+        assert pr == [12.0, 30.0, 10.0]
+        assert sp["min"] == 10.0 and sp["max"] == 30.0 and sp["median"] == 12.0 and sp["slowest"] == 1.0
+        assert abs(sp["imbalance"] - 3.0) < 1e-12
+
+
 def test_roofline_fractions(tmp_path):
     import json
 
