@@ -203,6 +203,54 @@ class StageModule(nn.Module):
         return logits, loss
 
 
+def one_f_one_b_plan(stage: int, pp: int, M: int) -> List[tuple]:
+    """The 1F1B (PipeDream-Flush) step list of one stage.
+
+    With W = min(pp - stage - 1, M): W warm-up forwards, then M - W rounds of one
+    forward (micro-batch W + i) and one backward (micro-batch i), then the last W
+    backwards; forwards and backwards each in micro-batch order. Steps:
+    ``("fwd", m)``, ``("bwd", m)``; receives that the next step waits for,
+    ``("recv_act", m)`` from the previous stage and ``("recv_grad", m)`` from the next;
+    sends, ``("send_act", m)`` to the next stage and ``("send_grad", m)`` to the previous;
+    and two batched pairs, ``("send_act+recv_grad", f, b)`` with the next stage and
+    ``("send_grad+recv_act", b, f)`` with the previous one. A pair is one NCCL group,
+    posted when both neighbours reach the matching pair, so transfers in opposite
+    directions between two stages never wait on each other (NCCL runs each rank's
+    point-to-point groups in order; ``tests/test_parallel_cpu.py`` checks the plans of
+    all stages against that rule).
+    """
+    first, last = stage == 0, stage == pp - 1
+    warm = min(pp - stage - 1, M)
+    steady = M - warm
+    plan: List[tuple] = []
+    for m in range(warm):
+        if not first:
+            plan.append(("recv_act", m))
+        plan.append(("fwd", m))
+        plan.append(("send_act", m))
+    if steady > 0 and not first:
+        plan.append(("recv_act", warm))
+    for i in range(steady):
+        f = warm + i
+        plan.append(("fwd", f))
+        if not last:
+            plan.append(("send_act+recv_grad", f, i))
+        plan.append(("bwd", i))
+        if first:
+            continue
+        if i == steady - 1:
+            plan.append(("send_grad", i))
+        else:
+            plan.append(("send_grad+recv_act", i, f + 1))
+    for b in range(steady, M):
+        if not last:
+            plan.append(("recv_grad", b))
+        plan.append(("bwd", b))
+        if not first:
+            plan.append(("send_grad", b))
+    return plan
+
+
 @dataclass
 class PipelineState:
     boundaries: List[torch.Tensor] = field(default_factory=list)
@@ -367,85 +415,64 @@ class GPipeEngine:
         return dist.batch_isend_irecv(ops) if ops else []
 
     def _forward_backward_1f1b(self, loader, M: int, device, use_amp, amp_dtype, scaler, batch_size):
-        """PipeDream-Flush 1F1B. Per stage s with W = min(pp - s - 1, M): W forwards, then
-        M - W rounds of (forward m + W, backward m), then the last W backwards, all in
-        micro-batch order. Between stages s and s + 1 the two ranks post matching batches:
-        a send of an activation together with the receive of a gradient on one side, the
-        send of that gradient together with the receive of the next activation on the other.
-        """
+        """Runs ``one_f_one_b_plan`` for this stage (see there for the schedule)."""
         cfg = self.stage.cfg
         B, S, H = self.stage.boundary_batch(batch_size), cfg.block_size, cfg.n_embed
-        warm = min(self.pp_size - self.pp_rank - 1, M)
-        steady = M - warm
         P2P = dist.P2POp
         held = []  # FIFO of (recv_x, boundary, loss, aux) for forwards whose backward is pending
-        keep = []  # tensors whose sends are in flight, with their works
+        keep = []  # tensors of sends in flight, with their works
         losses, auxes = [], []
         self.max_inflight = 0
+        act = None   # the received input of the next forward
+        out = None   # the output of the last forward, to send
+        gbuf = None  # the received gradient of the next backward
+        gin = None   # the input gradient of the last backward, to send
 
-        def new_act():
+        def new_buf():
             return torch.empty((B, S, H), device=device, dtype=self.boundary_dtype)
 
-        def recv_act(m):
-            buf = new_act()
-            self._wait(self._batch_p2p([P2P(dist.irecv, buf, self.prev_rank, tag=self._fwd_tag(m))]))
-            return buf
-
-        def forward(m, buf):
-            recv_x = self._as_input(buf, True) if buf is not None else None
-            x, loss, aux = self._forward_micro(loader, device, use_amp, amp_dtype, recv_x)
-            held.append((recv_x, x, loss, aux))
-            self.max_inflight = max(self.max_inflight, len(held))
-            auxes.append(aux.detach().float())
-            if loss is not None:
-                losses.append(loss.detach().float())
-            return None if self.is_last else x.detach().to(self.boundary_dtype)
-
-        def backward(grad_buf):
-            recv_x, x, loss, aux = held.pop(0)
-            grad = grad_buf.to(x.dtype) if grad_buf is not None else None
-            self._backward_micro(x, loss, aux, grad, M, scaler)
-            return None if self.is_first else recv_x.grad.to(self.boundary_dtype)
-
-        def send(t, peer, tag):
-            keep.append((t, self._batch_p2p([P2P(dist.isend, t, peer, tag=tag)])))
-
-        # warm-up forwards
-        for m in range(warm):
-            out = forward(m, None if self.is_first else recv_act(m))
-            send(out, self.next_rank, self._fwd_tag(m))
-        # steady state: one forward, one backward
-        buf = recv_act(warm) if steady > 0 and not self.is_first else None
-        for i in range(steady):
-            f = warm + i
-            out = forward(f, buf)
-            gbuf = None
-            if not self.is_last:
-                gbuf = torch.empty_like(out)
-                works = self._batch_p2p([P2P(dist.isend, out, self.next_rank, tag=self._fwd_tag(f)),
-                                         P2P(dist.irecv, gbuf, self.next_rank, tag=self._bwd_tag(i))])
-                self._wait(works)
+        for step in one_f_one_b_plan(self.pp_rank, self.pp_size, M):
+            kind = step[0]
+            if kind == "fwd":
+                recv_x = self._as_input(act, True) if act is not None else None
+                act = None
+                x, loss, aux = self._forward_micro(loader, device, use_amp, amp_dtype, recv_x)
+                held.append((recv_x, x, loss, aux))
+                self.max_inflight = max(self.max_inflight, len(held))
+                auxes.append(aux.detach().float())
+                if loss is not None:
+                    losses.append(loss.detach().float())
+                out = None if self.is_last else x.detach().to(self.boundary_dtype)
+            elif kind == "bwd":
+                recv_x, x, loss, aux = held.pop(0)
+                grad = gbuf.to(x.dtype) if gbuf is not None else None
+                gbuf = None
+                self._backward_micro(x, loss, aux, grad, M, scaler)
+                gin = None if self.is_first else recv_x.grad.to(self.boundary_dtype)
+            elif kind == "recv_act":
+                act = new_buf()
+                self._wait(self._batch_p2p([P2P(dist.irecv, act, self.prev_rank, tag=self._fwd_tag(step[1]))]))
+            elif kind == "recv_grad":
+                gbuf = new_buf()
+                self._wait(self._batch_p2p([P2P(dist.irecv, gbuf, self.next_rank, tag=self._bwd_tag(step[1]))]))
+            elif kind == "send_act":
+                keep.append((out, self._batch_p2p([P2P(dist.isend, out, self.next_rank,
+                                                       tag=self._fwd_tag(step[1]))])))
+            elif kind == "send_grad":
+                keep.append((gin, self._batch_p2p([P2P(dist.isend, gin, self.prev_rank,
+                                                       tag=self._bwd_tag(step[1]))])))
+            elif kind == "send_act+recv_grad":
+                gbuf = new_buf()
+                self._wait(self._batch_p2p([P2P(dist.isend, out, self.next_rank, tag=self._fwd_tag(step[1])),
+                                            P2P(dist.irecv, gbuf, self.next_rank, tag=self._bwd_tag(step[2]))]))
                 keep.append((out, []))
-            gin = backward(gbuf)
-            if self.is_first:
-                buf = None
-            elif i == steady - 1:
-                send(gin, self.prev_rank, self._bwd_tag(i))
-            else:
-                buf = new_act()
-                works = self._batch_p2p([P2P(dist.isend, gin, self.prev_rank, tag=self._bwd_tag(i)),
-                                         P2P(dist.irecv, buf, self.prev_rank, tag=self._fwd_tag(f + 1))])
-                self._wait(works)
+            elif kind == "send_grad+recv_act":
+                act = new_buf()
+                self._wait(self._batch_p2p([P2P(dist.isend, gin, self.prev_rank, tag=self._bwd_tag(step[1])),
+                                            P2P(dist.irecv, act, self.prev_rank, tag=self._fwd_tag(step[2]))]))
                 keep.append((gin, []))
-        # drain: the remaining backwards
-        for b in range(steady, M):
-            gbuf = None
-            if not self.is_last:
-                gbuf = new_act()
-                self._wait(self._batch_p2p([P2P(dist.irecv, gbuf, self.next_rank, tag=self._bwd_tag(b))]))
-            gin = backward(gbuf)
-            if not self.is_first:
-                send(gin, self.prev_rank, self._bwd_tag(b))
+            else:
+                raise AssertionError(kind)
         for _, works in keep:
             self._wait(works)
 

@@ -282,3 +282,70 @@ def test_1f1b_training_follows_dense(dp, tp, pp, tie):
         for a, b in zip(losses, ref):
             assert abs(a - b) < 1e-4, (losses, ref)
     assert checked >= 1
+
+
+def _ops(stage, step):
+    """(peer stage, direction, kind, micro-batch) of each transfer of a 1F1B plan step."""
+    k = step[0]
+    if k == "recv_act":
+        return [(stage - 1, "recv", "act", step[1])]
+    if k == "recv_grad":
+        return [(stage + 1, "recv", "grad", step[1])]
+    if k == "send_act":
+        return [(stage + 1, "send", "act", step[1])]
+    if k == "send_grad":
+        return [(stage - 1, "send", "grad", step[1])]
+    if k == "send_act+recv_grad":
+        return [(stage + 1, "send", "act", step[1]), (stage + 1, "recv", "grad", step[2])]
+    if k == "send_grad+recv_act":
+        return [(stage - 1, "send", "grad", step[1]), (stage - 1, "recv", "act", step[2])]
+    return None  # compute
+
+
+@pytest.mark.parametrize("pp", range(1, 9))
+def test_1f1b_plans_cannot_deadlock(pp):
+    """Simulate every stage's 1F1B plan under NCCL's rule (a rank runs its point-to-point
+    groups in order; a group ends once every transfer's counterpart is posted by the peer)
+    for M = 1..12 micro-batches: every plan runs to the end, sends and receives pair up in
+    order on every link, and stage s never holds more than pp - s forwards."""
+    from heiretsu_b200.parallel.pipeline import one_f_one_b_plan
+
+    for M in range(1, 13):
+        plans = [one_f_one_b_plan(s, pp, M) for s in range(pp)]
+        pos = [0] * pp
+        while True:
+            moved = False
+            current = [plans[s][pos[s]] if pos[s] < len(plans[s]) else None for s in range(pp)]
+            posted = [set() for _ in range(pp)]
+            for s, st in enumerate(current):
+                for op in (_ops(s, st) or []) if st is not None else []:
+                    posted[s].add(op)
+            for s, st in enumerate(current):
+                if st is None:
+                    continue
+                ops = _ops(s, st)
+                done = ops is None or all(
+                    (s, "recv" if d == "send" else "send", kind, m) in posted[peer] for peer, d, kind, m in ops)
+                if done:
+                    pos[s] += 1
+                    moved = True
+            if not moved:
+                break
+        assert pos == [len(p) for p in plans], (pp, M, pos)
+        for s, plan in enumerate(plans):
+            f = [st[1] for st in plan if st[0] == "fwd"]
+            b = [st[1] for st in plan if st[0] == "bwd"]
+            assert f == list(range(M)) and b == list(range(M))
+            held = peak = 0
+            for st in plan:
+                held += {"fwd": 1, "bwd": -1}.get(st[0], 0)
+                peak = max(peak, held)
+            assert peak == min(pp - s, M)
+            for kind, d, nb in (("act", "send", s + 1), ("grad", "send", s - 1), ("act", "recv", s - 1),
+                                ("grad", "recv", s + 1)):
+                seq = [m for st in plan for peer, dd, k, m in (_ops(s, st) or []) if k == kind and dd == d]
+                assert seq == sorted(seq)
+                if 0 <= nb < pp:
+                    other = [m for st in plans[nb] for peer, dd, k, m in (_ops(nb, st) or [])
+                             if k == kind and dd != d]
+                    assert seq == other, (s, kind, d)
