@@ -111,7 +111,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--pp_tie_embeddings", type=int, default=0, choices=[0, 1],
                    help="pp > 1: keep the first stage's wte and the last stage's lm_head equal (gradients summed "
                         "between the two stages), i.e. the tied dense GPT; 0 = the reference's untied stages")
-    p.add_argument("--resume", type=str, default=None, help="checkpoint file to load before training")
+    p.add_argument("--resume", type=str, default=None,
+                   help="checkpoint file to load before training; 'auto' = the newest complete step in --out_dir "
+                        "(or a fresh start), for jobs restarted after a failure")
     p.add_argument("--out_dir", type=str, default=".")
     p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
     p.add_argument("--log_interval", type=int, default=None)
@@ -770,6 +772,15 @@ def main(argv=None) -> None:
     module = engine.module
     start_step = 1
     resume_side = None
+    if args.resume == "auto":
+        # Restart after a failure (torchrun --max-restarts): the newest step every rank
+        # finished writing, or a fresh start when there is none.
+        from .utils.ckpt import latest_complete_checkpoint
+        found = latest_complete_checkpoint(args.out_dir, topo)
+        if rank == 0:
+            print(f"[resume] auto: {found}" if found else f"[resume] auto: no complete checkpoint in "
+                                                           f"{args.out_dir}; starting from step 1")
+        args.resume = found
     if args.resume:
         from .utils.ckpt import (find_rank_state, load_for_resume, merged_optimizer_moments, reslice_moments,
                                  sidecar_path)
@@ -860,7 +871,11 @@ def main(argv=None) -> None:
     wd = None
     if distributed and args.watchdog_s > 0:
         from .utils.fault import StepWatchdog, default_store
-        wd = StepWatchdog(default_store(), dist.get_rank(), dist.get_world_size(), timeout_s=args.watchdog_s)
+        # Keys of one attempt only: a restarted job (torchrun --max-restarts) must not read the
+        # failure that ended the previous attempt.
+        attempt = os.environ.get("TORCHELASTIC_RESTART_COUNT", "0")
+        wd = StepWatchdog(default_store(), dist.get_rank(), dist.get_world_size(), timeout_s=args.watchdog_s,
+                          prefix=f"hb_watchdog/attempt{attempt}")
     try:
         _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0, start_step)
     except BaseException as e:
@@ -883,6 +898,18 @@ def main(argv=None) -> None:
         cleanup()
 
 
+def injected_failure():
+    """Host-side fault injection for recovery tests: ``HB_INJECT_FAILURE=<rank>:<step>``
+    makes that rank raise at the start of that step, in the first attempt of a job only
+    (TORCHELASTIC_RESTART_COUNT unset or 0), so a restarted job runs through. Nothing
+    on a GPU is involved: the rank leaves between steps, with no kernel in flight."""
+    spec = os.environ.get("HB_INJECT_FAILURE")
+    if not spec or os.environ.get("TORCHELASTIC_RESTART_COUNT", "0") != "0":
+        return None
+    r, _, k = spec.partition(":")
+    return int(r), int(k)
+
+
 def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, wd, t0, start_step=1) -> None:
     from .utils.profiling import RegionTimer, rank_spread
 
@@ -892,12 +919,15 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
     log_every = args.log_interval or max(1, args.eval_interval // 10)
     timer = RegionTimer(enabled=bool(args.device_timing) and engine.device.type == "cuda")
     timed_steps = 0
+    inject = injected_failure()
     for step in range(start_step, args.max_iters + 1):
         if args.lr_schedule != "constant":
             for g in engine.optimizer.param_groups:
                 g["lr"] = lr_at(step, args)  # read by the next step (graph replays included)
         if wd is not None:
             wd.check()  # a failed peer is noticed here, before this step launches anything
+        if inject is not None and inject == (topo.rank, step):
+            raise RuntimeError(f"injected failure: rank {topo.rank} at step {step} (HB_INJECT_FAILURE)")
         region_ms = None
         spread = None  # per-rank device step times of a logging step (multi-rank runs)
         if args.region_timing_interval > 0 and step % args.region_timing_interval == 0:
@@ -975,6 +1005,11 @@ def _train_loop(args, engine, module, cfg, topo, train_loader, val_loader, run, 
             from .utils.ckpt import save_rank_state  # every rank: its own RNG and data position
             save_rank_state(args.out_dir, step, topo, {k: side[k] for k in ("rng", "train_loader", "dropout_seed")
                                                        if k in side})
+            if dist.is_initialized() and topo.world_size > 1:
+                dist.barrier()  # every rank's files of this step are on disk
+            if topo.rank == 0:
+                from .utils.ckpt import mark_step_complete
+                mark_step_complete(args.out_dir, step, topo)
 
 
 def expert_counts(module):

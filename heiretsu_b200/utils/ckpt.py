@@ -14,6 +14,7 @@ re-sliced for the new layout (weights only: the optimizer restarts).
 """
 from __future__ import annotations
 
+import json
 import os
 import re
 from dataclasses import asdict
@@ -125,6 +126,47 @@ def ckpt_layout(obj: dict) -> Tuple[int, int, int]:
 
 def rank_state_path(out_dir: str, step: int, rank: int) -> str:
     return os.path.join(out_dir, f"rstate_{step:07d}_r{rank}.pt")
+
+
+def done_marker_path(out_dir: str, step: int) -> str:
+    return os.path.join(out_dir, f"ckpt_{step:07d}.done")
+
+
+def mark_step_complete(out_dir: str, step: int, topo) -> str:
+    """Written by rank 0 once every rank has finished writing step ``step`` (the caller
+    holds a barrier first): a crash in the middle of a save leaves no marker, so
+    ``latest_complete_checkpoint`` never picks a half-written step."""
+    path = done_marker_path(out_dir, step)
+    tmp = path + ".tmp"
+    with open(tmp, "w") as f:
+        json.dump({"step": step, "layout": [topo.dp, topo.ep, topo.tp, topo.pp],
+                   "file": ckpt_name(step, topo)}, f)
+    os.replace(tmp, path)
+    return path
+
+
+def latest_complete_checkpoint(out_dir: str, topo) -> Optional[str]:
+    """A checkpoint file of the newest step in ``out_dir`` with a completion marker, or
+    None. The file is this rank's own shard when the layout is unchanged, else any
+    shard of the step (``load_for_resume`` takes any file of a step)."""
+    if not os.path.isdir(out_dir):
+        return None
+    steps = []
+    for name in os.listdir(out_dir):
+        if name.startswith("ckpt_") and name.endswith(".done"):
+            try:
+                steps.append(int(name[len("ckpt_"):-len(".done")]))
+            except ValueError:
+                continue
+    for step in sorted(steps, reverse=True):
+        own = os.path.join(out_dir, ckpt_name(step, topo))
+        if os.path.exists(own):
+            return own
+        with open(done_marker_path(out_dir, step)) as f:
+            other = os.path.join(out_dir, json.load(f)["file"])
+        if os.path.exists(other):
+            return other
+    return None
 
 
 def save_rank_state(out_dir: str, step: int, topo, state: dict) -> str:

@@ -27,11 +27,15 @@ MASTER_PORT=${MASTER_PORT:-29500}
 NNODES=${NNODES:-1}
 NODE_RANK=${NODE_RANK:-0}
 CONFIG_FILE=${CONFIG_FILE:-}
+# Restarts of the whole worker group after a rank fails (torchrun --max-restarts);
+# with restarts the job resumes from its newest complete checkpoint (RESUME=auto).
+MAX_RESTARTS=${MAX_RESTARTS:-0}
 # Upper bound on the whole job; process-group timeouts end a stuck collective long before.
 JOB_TIMEOUT=${JOB_TIMEOUT:-0}
 SAVE_PATH=${SAVE_PATH:-./checkpoints}
 SYNTHETIC=${SYNTHETIC:-0}
 RESUME=${RESUME:-}
+if [[ ${MAX_RESTARTS} -gt 0 && -z ${RESUME} ]]; then RESUME=auto; fi
 NUM_EXPERTS=${NUM_EXPERTS:-0}
 WANDB=${WANDB:-0}
 
@@ -91,6 +95,7 @@ echo "launch: dp=${DP} tp=${TP} pp=${PP} ep=${EP} (world ${WORLD_SIZE}, ${NNODES
 mkdir -p "${SAVE_PATH}"
 cd "$(dirname "$0")"
 LAUNCH=(python -m torch.distributed.run --nnodes="${NNODES}" --node-rank="${NODE_RANK}"
-        --nproc-per-node="${NPROC_PER_NODE}" --master-addr "${MASTER_ADDR}" --master-port "${MASTER_PORT}")
+        --nproc-per-node="${NPROC_PER_NODE}" --master-addr "${MASTER_ADDR}" --master-port "${MASTER_PORT}"
+        --max-restarts="${MAX_RESTARTS}")
 if [[ ${JOB_TIMEOUT} -gt 0 ]]; then LAUNCH=(timeout -k 60 "${JOB_TIMEOUT}" "${LAUNCH[@]}"); fi
 exec "${LAUNCH[@]}" train.py "${ARGS[@]}"

@@ -47,3 +47,34 @@ def test_run_train_sh_two_nodes_cpu(tmp_path):
         assert p.returncode == 0, (out[-2000:], err[-3000:])
     assert "training finished." in outs[0][0]
     assert "[eval] step 3" in outs[0][0]
+
+
+def test_restart_after_failure_resumes_exactly(tmp_path):
+    """MAX_RESTARTS=1: rank 1 raises at step 5 (host-side injection, after the step-4
+    checkpoint); torchrun restarts both ranks, which resume from the newest complete
+    checkpoint (RESUME=auto) and finish; the step-6 weights equal an uninterrupted run's."""
+    import torch
+
+    def run(out, **extra):
+        env = dict(os.environ, DP="2", SYNTHETIC="1", DEVICE="cpu", DIST_BACKEND="gloo", AMP="none", N_LAYER="1",
+                   N_HEAD="2", N_EMBED="32", BLOCK_SIZE="16", BATCH_SIZE="2", GRAD_ACCUM="2", MAX_ITERS="6",
+                   EVAL_INTERVAL="100", EVAL_ITERS="1", SAVE_INTERVAL="2", SAVE_PATH=str(out), DROPOUT="0.1",
+                   MASTER_PORT=str(_port()), JOB_TIMEOUT="280", OMP_NUM_THREADS="1", **extra)
+        return subprocess.run(["bash", os.path.join(ROOT, "run_train.sh")], cwd=ROOT, env=env, capture_output=True,
+                              text=True, timeout=300)
+
+    clean = run(tmp_path / "clean")
+    assert clean.returncode == 0, (clean.stdout[-2000:], clean.stderr[-3000:])
+    hit = run(tmp_path / "hit", MAX_RESTARTS="1", HB_INJECT_FAILURE="1:5")
+    assert hit.returncode == 0, (hit.stdout[-2000:], hit.stderr[-3000:])
+    assert "injected failure: rank 1 at step 5" in hit.stderr
+    assert "[resume] auto: no complete checkpoint" in hit.stdout  # the first attempt starts fresh
+    assert "[resume] step 4 from" in hit.stdout
+    assert "training finished." in hit.stdout
+    assert sorted(p.name for p in (tmp_path / "hit").glob("*.done")) == [
+        "ckpt_0000002.done", "ckpt_0000004.done", "ckpt_0000006.done"]
+    a = torch.load(tmp_path / "clean" / "ckpt_0000006.pt", weights_only=False)["model"]
+    b = torch.load(tmp_path / "hit" / "ckpt_0000006.pt", weights_only=False)["model"]
+    assert a.keys() == b.keys()
+    for k in a:
+        assert torch.equal(a[k], b[k]), k
