@@ -234,6 +234,8 @@ def pick_device(arg: str):
         if torch.cuda.is_available():
             lr = int(os.environ.get("LOCAL_RANK", "0"))
             return torch.device("cuda", lr), lr
+        if getattr(torch.backends, "mps", None) is not None and torch.backends.mps.is_available():
+            return torch.device("mps"), 0  # the reference's order: cuda, then mps, then cpu (train.py:233-243)
         return torch.device("cpu"), 0
     dev = torch.device(arg)
     if dev.type == "cuda":
