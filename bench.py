@@ -103,6 +103,11 @@ WORKLOADS = {w.name: w for w in [
 ]}
 
 
+# CPU single-process sanity configuration (fp32, host-timed): 4L/4H/128d, T=256,
+# vocab 50257, micro-batch 8, 50 AdamW iterations at lr 6e-4.
+CPU_SANITY = dict(n_layer=4, n_head=4, n_embed=128, block_size=256, vocab_size=VOCAB, batch=8, lr=6e-4)
+
+
 def parallelism_name(layout) -> str:
     dp, ep, tp, pp = layout
     parts = [f"dp{dp}"] + [f"{k}{v}" for k, v in (("ep", ep), ("tp", tp), ("pp", pp)) if v > 1]
@@ -115,8 +120,9 @@ def parse():
     ap.add_argument("--steps", type=int, default=10)
     ap.add_argument("--warmup", type=int, default=3)
     ap.add_argument("--impl", default="ours", choices=["ours", "reference"])
-    ap.add_argument("--config", default="gpt2s_dp", choices=sorted(WORKLOADS),
-                    help="workload (default: GPT-2 small, pure data parallel)")
+    ap.add_argument("--config", default="gpt2s_dp", choices=sorted(WORKLOADS) + ["cpu_sanity"],
+                    help="workload (default: GPT-2 small, pure data parallel; cpu_sanity: the fp32 CPU "
+                         "configuration, one process, host-timed)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true", help="skip the profiler-based kernel count")
     ap.add_argument("--overlap-dp", type=int, default=0, choices=[0, 1],
@@ -491,8 +497,91 @@ def _scalar_reader(impl: str):
     return ScalarReader(depth=2)
 
 
+def cpu_batches(seed: int, n: int):
+    """n (x, y) batches of the CPU configuration: int64 ids uniform in [0, V), y = x shifted by one."""
+    g = torch.Generator().manual_seed(seed)
+    B, T = CPU_SANITY["batch"], CPU_SANITY["block_size"]
+    out = []
+    for _ in range(n):
+        ids = torch.randint(0, VOCAB, (B, T + 1), generator=g)
+        out.append((ids[:, :-1].contiguous(), ids[:, 1:].contiguous()))
+    return out
+
+
+def run_cpu_sanity(args) -> dict:
+    """One process on the host CPU, fp32: ``steps`` timed optimizer steps after ``warmup``
+    (host clock, perf_counter), through each implementation's own training step."""
+    c = CPU_SANITY
+    batches = cpu_batches(1234, args.warmup + args.steps)
+    it = iter(batches)
+
+    class Feed:
+        B = c["batch"]
+
+        def next_batch(self, device):
+            return next(it)
+
+    feed = Feed()
+    if args.impl == "ours":
+        sys.path.insert(0, ROOT)
+        from heiretsu_b200.config import GPTConfig
+        from heiretsu_b200.topo import init_topology
+        from heiretsu_b200.trainer import Engine, build_argparser
+        flags = ["--device", "cpu", "--amp", "none", "--engine", "plain", "--batch_size", str(c["batch"]),
+                 "--block_size", str(c["block_size"]), "--n_layer", str(c["n_layer"]), "--n_head", str(c["n_head"]),
+                 "--n_embed", str(c["n_embed"]), "--dropout", "0", "--learning_rate", str(c["lr"])]
+        targs = build_argparser().parse_args(flags)
+        torch.manual_seed(1337)
+        cfg = GPTConfig(n_layer=c["n_layer"], n_head=c["n_head"], n_embed=c["n_embed"], block_size=c["block_size"],
+                        vocab_size=VOCAB, dropout=0.0)
+        eng = Engine(targs, init_topology(dp=1), torch.device("cpu"), cfg)
+        step = lambda: eng.train_step(feed)
+    else:
+        ref = os.path.join(ROOT, "baseline", "_ref")
+        if not os.path.exists(os.path.join(ref, "gpt_model.py")):
+            return {"impl": "reference", "unavailable": "reference not installed in baseline/_ref"}
+        sys.path.insert(0, ref)
+        import gpt_model  # noqa: E402  (reference modules, unmodified)
+        import topo as rtopo
+        tpo = rtopo.init_topology(dp=1)
+        torch.manual_seed(1337)
+        model = gpt_model.GPT(gpt_model.GPTConfig(n_layer=c["n_layer"], n_head=c["n_head"], n_embed=c["n_embed"],
+                                                  block_size=c["block_size"], vocab_size=VOCAB, dropout=0.0),
+                              topo=tpo)
+        opt = torch.optim.AdamW(model.parameters(), lr=c["lr"], betas=(0.9, 0.95), weight_decay=0.1)
+
+        def step():  # reference train.py:400-453 with --amp none, accumulation 1, one process
+            x, y = feed.next_batch(None)
+            _, loss, aux = model(x, y)
+            (loss + aux).backward()
+            torch.nn.utils.clip_grad_norm_(model.parameters(), 1.0)
+            opt.step()
+            opt.zero_grad(set_to_none=True)
+            return loss.detach(), aux
+    for _ in range(args.warmup):
+        step()
+    t0 = time.perf_counter()
+    last = None
+    for _ in range(args.steps):
+        last = step()
+    loss = float(last[0])  # the last step's loss read back (inside the timed region)
+    dt = (time.perf_counter() - t0) / args.steps
+    tokens = c["batch"] * c["block_size"]
+    return {"metric": METRIC.replace("device-timed, max over ranks", "host-timed, CPU"), "value": tokens / dt,
+            "unit": "tokens/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,
+            "higher_is_better": True, "scaling": "weak", "vs_baseline": None, "dtype": "fp32",
+            "data": "synthetic uniform-random GPT-2 token ids (targets = inputs shifted by one), random-init weights",
+            "config": {"model": "GPT 4L/4H/128d, vocab 50257", "global_batch": c["batch"], "seq_len": c["block_size"],
+                       "parallelism": "cpu", "optimizer": f"AdamW lr {c['lr']} + clip 1.0",
+                       "threads": torch.get_num_threads(), "name": "cpu_sanity"},
+            "final_loss": loss, "gpu_launches": 0, "impl": args.impl}
+
+
 def main():
     args = parse()
+    if args.config == "cpu_sanity":
+        print(json.dumps(run_cpu_sanity(args)))
+        return
     w = WORKLOADS[args.config]
     world, rank, local, dev = setup()
     layout = w.layout(world)

@@ -146,6 +146,73 @@ def run_blocks(blocks, x: torch.Tensor, recompute: bool = False) -> Tuple[torch.
     return x, aux_total
 
 
+class _HeadCE(torch.autograd.Function):
+    """lm_head projection + mean cross-entropy in one autograd node (plain path, no autocast).
+
+    Forward: logits = x W^T, per-row log-sum-exp, loss = mean over rows whose
+    target is not ``ignore_index`` of (lse - logit[target]) (NaN when no row
+    counts, like ``F.cross_entropy``). Backward turns the saved logits buffer
+    into the gradient in place, (softmax - onehot) * dloss / n, and runs the two
+    GEMMs. Both directions go through the rows in blocks of about 16 MB of
+    logits: each block's GEMM output is reduced (forward) or turned into its
+    gradient and consumed by its two GEMMs (backward) while it is still in
+    cache, so the [N, V] buffer crosses DRAM about three times per step, against
+    about ten for ``F.cross_entropy`` on materialised logits (log-softmax copy,
+    zero-filled one-hot gradient, softmax-backward buffer). The graph can be
+    differentiated once (the buffer is consumed).
+    """
+
+    BLOCK_BYTES = 16 << 20
+
+    @staticmethod
+    def _blocks(n_rows: int, n_cols: int, esz: int):
+        step = max(16, _HeadCE.BLOCK_BYTES // max(1, n_cols * esz))
+        return [(r, min(n_rows, r + step)) for r in range(0, n_rows, step)]
+
+    @staticmethod
+    def forward(ctx, x, w, targets, ignore_index: int):
+        N, V = x.shape[0], w.shape[0]
+        logits = torch.empty(N, V, dtype=x.dtype, device=x.device)
+        lse = torch.empty(N, dtype=x.dtype, device=x.device)
+        wt = w.t()
+        for a, b in _HeadCE._blocks(N, V, x.element_size()):
+            blk = logits[a:b]
+            torch.mm(x[a:b], wt, out=blk)
+            m = blk.amax(dim=1, keepdim=True)
+            lse[a:b] = (blk - m).exp_().sum(dim=1).log_().add_(m.squeeze(1))
+        valid = targets != ignore_index
+        tgt = torch.where(valid, targets, torch.zeros_like(targets))
+        picked = logits.gather(1, tgt[:, None]).squeeze(1)
+        n = valid.sum().to(x.dtype)
+        loss = torch.where(valid, lse - picked, torch.zeros_like(lse)).sum() / n
+        ctx.save_for_backward(x, w, logits, lse, tgt, valid, n)
+        ctx.consumed = False
+        return loss
+
+    @staticmethod
+    def backward(ctx, dloss):
+        if ctx.consumed:
+            raise RuntimeError("the fused lm_head/cross-entropy graph can be differentiated only once")
+        ctx.consumed = True
+        x, w, g, lse, tgt, valid, n = ctx.saved_tensors
+        scale = torch.where(valid, dloss / n, torch.zeros_like(lse))
+        dx = torch.empty_like(x)
+        dw = torch.zeros_like(w)
+        for a, b in _HeadCE._blocks(g.shape[0], g.shape[1], g.element_size()):
+            gb = g[a:b]
+            gb.sub_(lse[a:b, None]).exp_().mul_(scale[a:b, None])
+            gb.scatter_add_(1, tgt[a:b, None], -scale[a:b, None])
+            torch.mm(gb, w, out=dx[a:b])
+            dw.addmm_(gb.t(), x[a:b])
+        return dx, dw, None, None
+
+
+def head_cross_entropy(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor,
+                       ignore_index: int = -100) -> torch.Tensor:
+    """Mean cross-entropy of ``x @ w.T`` against ``targets`` without keeping the logits."""
+    return _HeadCE.apply(x.reshape(-1, x.size(-1)), w, targets.reshape(-1), ignore_index)
+
+
 def init_gpt_weights(module: nn.Module, n_layer: int) -> None:
     """NanoGPT init: N(0, 0.02) everywhere, c_proj std scaled by (2L)^-0.5, zero biases.
 
@@ -203,6 +270,8 @@ class GPT(nn.Module):
         x = self.tr.wte(idx) + self.tr.wpe(pos)[None]
         x, aux_total = run_blocks(self.tr.h, x, self.recompute)
         x = self.tr.ln_f(x)
+        if targets is not None and not return_logits and not torch.is_autocast_enabled(x.device.type):
+            return None, head_cross_entropy(x, self.lm_head.weight, targets), aux_total
         logits = self.lm_head(x)
         loss = None
         if targets is not None:

@@ -183,7 +183,7 @@ class StageModule(nn.Module):
         from ..models.gpt import run_blocks
         return run_blocks(self.blocks, x, self.recompute)
 
-    def forward_head(self, x: torch.Tensor, targets: Optional[torch.Tensor]):
+    def forward_head(self, x: torch.Tensor, targets: Optional[torch.Tensor], want_logits: bool = True):
         if self.fused and x.is_cuda:
             from ..models.fused import head_fused
             if self._tp_fused(x):
@@ -196,6 +196,9 @@ class StageModule(nn.Module):
                 return None, (loss / self.tp if loss is not None else None)
             return head_fused(self.ln_f, self.lm_head.weight, x, targets, self.cfg.vocab_size)
         x = self.ln_f(x)
+        if targets is not None and not want_logits and not torch.is_autocast_enabled(x.device.type):
+            from ..models.gpt import head_cross_entropy
+            return None, head_cross_entropy(x, self.lm_head.weight, targets)
         logits = self.lm_head(x)
         loss = None
         if targets is not None:
@@ -267,6 +270,10 @@ class GPipeEngine:
         if schedule not in ("gpipe", "1f1b"):
             raise ValueError(f"unknown pipeline schedule {schedule!r} (gpipe | 1f1b)")
         self.schedule = schedule
+        # Plain (non-fused) last stage: lm_head + cross-entropy without keeping the logits
+        # (models.gpt.head_cross_entropy). Off by default, so that scripts written for the
+        # reference's GPipeEngine get its exact numerics; the trainer turns it on.
+        self.fused_head = False
         self.max_inflight = 0  # most micro-batches whose activations were held at once (last step)
         self.stage, self.topo = stage, topo
         self.pp_rank, self.pp_size = topo.pp_rank, topo.pp
@@ -313,7 +320,7 @@ class GPipeEngine:
         with ctx:
             x = self.stage.embed(idx) if self.is_first else recv_x
             x, aux = self.stage.forward_blocks(x)
-            loss = self.stage.forward_head(x, targets)[1] if self.is_last else None
+            loss = self.stage.forward_head(x, targets, want_logits=not self.fused_head)[1] if self.is_last else None
         return x, loss, aux
 
     def _as_input(self, buf: torch.Tensor, keep_graph: bool) -> torch.Tensor:

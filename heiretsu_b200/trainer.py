@@ -443,8 +443,12 @@ class Engine:
             self.scaler = torch.amp.GradScaler("cuda", enabled=(self.amp == "fp16"))
         else:
             self.flat = None
+            # torch's single-kernel AdamW (same update as the reference's default AdamW,
+            # one pass over each parameter instead of one op per moment and parameter)
+            fused_ok = device.type in ("cpu", "cuda")
             self.optimizer = torch.optim.AdamW(self.module.parameters(), lr=args.learning_rate,
-                                               betas=tuple(args.betas), weight_decay=args.weight_decay)
+                                               betas=tuple(args.betas), weight_decay=args.weight_decay,
+                                               fused=fused_ok or None)
             self.scaler = torch.amp.GradScaler("cuda", enabled=(self.amp == "fp16"))
         self.amp_dtype = torch.float16 if self.amp == "fp16" else torch.bfloat16
         self.use_amp = self.amp in ("fp16", "bf16") and not self.fused
@@ -462,6 +466,7 @@ class Engine:
             bd = torch.float32 if args.pp_boundary_dtype == "fp32" else torch.bfloat16
             self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd,
                                     schedule=getattr(args, "pp_schedule", "gpipe"))
+            self.pipe.fused_head = True
         # CUDA-graph replay of the whole fused step (forward, backward, DP
         # reduction, clipping, AdamW) once shapes are known; the first
         # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).
@@ -587,8 +592,7 @@ class Engine:
             for _ in range(accum):
                 x, y = loader.next_batch(self.device)
                 with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype, enabled=self.use_amp):
-                    _, loss, aux_mb = self.forward_module(x, y, return_logits=False) if self.fused else \
-                        self.forward_module(x, y)
+                    _, loss, aux_mb = self.forward_module(x, y, return_logits=False)
                     combined = (loss + aux_mb) / accum
                 aux = aux + aux_mb.detach().float()
                 loss_sum = loss_sum + loss.detach().float()
@@ -758,6 +762,9 @@ def main(argv=None) -> None:
         kw = {"timeout": timedelta(seconds=args.pg_timeout_s)}
         if args.dist_backend == "nccl":
             kw["device_id"] = device
+        store = attempt_store(kw["timeout"])
+        if store is not None:
+            kw.update(store=store, rank=int(os.environ["RANK"]), world_size=world_env)
         dist.init_process_group(backend=args.dist_backend, **kw)
     topo = init_topology(dp=args.dp, ep=args.ep, tp=args.tp, pp=args.pp,
                          timeout=timedelta(seconds=args.pg_timeout_s))
@@ -898,6 +905,24 @@ def main(argv=None) -> None:
     engine.close()
     if distributed and dist.is_initialized():
         cleanup()
+
+
+def attempt_store(timeout):
+    """The rendezvous store of a restarted torchrun attempt, under a key prefix of its own.
+
+    torchrun keeps its store across restarts of the worker group, and process
+    groups publish their addresses under fixed keys: a rank of attempt n could
+    read the address of a dead rank of an earlier attempt and fail to connect.
+    From the first restart on (TORCHELASTIC_RESTART_COUNT > 0) every key goes under
+    ``hb_attempt<n>/``; the first attempt uses the plain env:// rendezvous."""
+    attempt = int(os.environ.get("TORCHELASTIC_RESTART_COUNT", "0") or 0)
+    if attempt == 0:
+        return None
+    agent = os.environ.get("TORCHELASTIC_USE_AGENT_STORE") == "True"
+    rank = int(os.environ["RANK"])
+    base = dist.TCPStore(os.environ["MASTER_ADDR"], int(os.environ["MASTER_PORT"]),
+                         int(os.environ["WORLD_SIZE"]), is_master=(not agent and rank == 0), timeout=timeout)
+    return dist.PrefixStore(f"hb_attempt{attempt}", base)
 
 
 def injected_failure():

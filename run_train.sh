@@ -94,8 +94,14 @@ echo "launch: dp=${DP} tp=${TP} pp=${PP} ep=${EP} (world ${WORLD_SIZE}, ${NNODES
 
 mkdir -p "${SAVE_PATH}"
 cd "$(dirname "$0")"
-LAUNCH=(python -m torch.distributed.run --nnodes="${NNODES}" --node-rank="${NODE_RANK}"
-        --nproc-per-node="${NPROC_PER_NODE}" --master-addr "${MASTER_ADDR}" --master-port "${MASTER_PORT}"
+if [[ ${MAX_RESTARTS} -gt 0 ]]; then
+  # Elastic rendezvous: every restart gets a fresh store, so no rank of a new attempt
+  # reads addresses that ranks of the failed attempt published.
+  RDZV=(--rdzv-backend=c10d --rdzv-endpoint="${MASTER_ADDR}:${MASTER_PORT}" --rdzv-id="${RUN_NAME:-heiretsu}"
         --max-restarts="${MAX_RESTARTS}")
+else
+  RDZV=(--node-rank="${NODE_RANK}" --master-addr "${MASTER_ADDR}" --master-port "${MASTER_PORT}")
+fi
+LAUNCH=(python -m torch.distributed.run --nnodes="${NNODES}" --nproc-per-node="${NPROC_PER_NODE}" "${RDZV[@]}")
 if [[ ${JOB_TIMEOUT} -gt 0 ]]; then LAUNCH=(timeout -k 60 "${JOB_TIMEOUT}" "${LAUNCH[@]}"); fi
 exec "${LAUNCH[@]}" train.py "${ARGS[@]}"

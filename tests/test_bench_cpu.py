@@ -139,3 +139,28 @@ def test_scalar_reader_returns_every_value_in_order():
     import pytest
     with pytest.raises(RuntimeError):
         r.push(torch.tensor(3.0))
+
+
+def test_cpu_sanity_config_both_arms():
+    """bench.py --config cpu_sanity: both implementations print the JSON line, train the same
+    model on the same batches and reach the same loss (fp32, one process)."""
+    import json
+    import subprocess
+
+    from oracle import have_reference
+
+    out = {}
+    for impl in ("ours", "reference"):
+        r = subprocess.run([sys.executable, os.path.join(ROOT, "bench.py"), "--config", "cpu_sanity", "--impl", impl,
+                            "--steps", "2", "--warmup", "1"], capture_output=True, text=True, timeout=600,
+                           env=dict(os.environ, OMP_NUM_THREADS="2"))
+        assert r.returncode == 0, r.stderr[-3000:]
+        out[impl] = json.loads(r.stdout.strip().splitlines()[-1])
+    o = out["ours"]
+    assert o["unit"] == "tokens/s" and o["value"] > 0 and o["dtype"] == "fp32" and o["n_gpus"] == 0
+    assert o["config"]["seq_len"] == 256 and o["config"]["global_batch"] == 8
+    ref = out["reference"]
+    if "unavailable" in ref:
+        assert not have_reference()
+        return
+    assert abs(o["final_loss"] - ref["final_loss"]) < 1e-4

@@ -73,17 +73,21 @@ def _worker_zero(rank, world, dp, tp):
 
 @pytest.mark.parametrize("dp,tp", [(2, 1), (2, 2), (4, 1)])
 def test_zero1_same_steps_sharded_state_and_resume(dp, tp):
+    """Against the plain engine's full AdamW (torch's fused kernel, whose rounding differs
+    from the element-wise formula in the last bits: within 1e-5 over four steps at lr
+    3e-3). The resumed run starts from weights that the full AdamW produced, so it is
+    held to the same bound."""
     res = run_ranks(_worker_zero, dp * tp, dp, tp)
     for r in res:
         for a, b in zip(r["lp"], r["lz"]):
-            assert abs(a - b) < 1e-6, (r["lp"], r["lz"])
-        assert r["perr"] < 1e-6
-        assert r["merr"] < 1e-6
+            assert abs(a - b) < 1e-5, (r["lp"], r["lz"])
+        assert r["perr"] < 1e-5
+        assert r["merr"] < 1e-5
         assert r["steps"] == 4
         assert r["bytes"] == 8 * -(-r["n"] // dp)  # 1/dp of the fp32 moments
         for a, b in zip(r["lr"], r["lz"][2:]):
-            assert abs(a - b) < 1e-6
-        assert r["rerr"] < 1e-6
+            assert abs(a - b) < 1e-5
+        assert r["rerr"] < 1e-5
 
 
 @pytest.mark.parametrize("dp,tp,pp", [(2, 1, 2), (2, 2, 1)])
