@@ -466,7 +466,7 @@ class Engine:
             bd = torch.float32 if args.pp_boundary_dtype == "fp32" else torch.bfloat16
             self.pipe = GPipeEngine(self.module, topo, boundary_dtype=bd,
                                     schedule=getattr(args, "pp_schedule", "gpipe"))
-            self.pipe.fused_head = True
+            self.pipe.fused_head = not args.compile
         # CUDA-graph replay of the whole fused step (forward, backward, DP
         # reduction, clipping, AdamW) once shapes are known; the first
         # GRAPH_WARMUP steps run eagerly (they also initialise lazy state).
@@ -592,7 +592,10 @@ class Engine:
             for _ in range(accum):
                 x, y = loader.next_batch(self.device)
                 with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype, enabled=self.use_amp):
-                    _, loss, aux_mb = self.forward_module(x, y, return_logits=False)
+                    # the plain path's one-node lm_head + cross-entropy is an eager optimisation;
+                    # a torch.compile'd module gets the logits path to trace instead
+                    _, loss, aux_mb = self.forward_module(x, y, return_logits=bool(self.args.compile)
+                                                          and not self.fused)
                     combined = (loss + aux_mb) / accum
                 aux = aux + aux_mb.detach().float()
                 loss_sum = loss_sum + loss.detach().float()
