@@ -401,6 +401,11 @@ def run_reference(args, w: Workload, layout, world, rank, dev):
     cfg = gpt_model.GPTConfig(**w.model_kwargs(), dropout=0.0)
     aux_coef = float(w.model.get("aux_loss_coef", 0.01))
     if pp > 1:
+        # The reference's pipeline cannot run under bf16 autocast: the sender's boundary is
+        # the fp32 residual stream while the receiver allocates a bf16 buffer
+        # (pipeline.py:217-247), so each transfer sends twice the bytes the peer expects
+        # (gloo on CPU rejects it: "Received data size doesn't match expected size"; NCCL
+        # gets mismatched counts). Its pipeline therefore runs in fp32, its only working mode.
         from pipeline import GPipeEngine, StageModule
         module = StageModule(cfg, tpo, tpo.pp_rank, tpo.pp).to(dev)
         pipe = GPipeEngine(module, tpo)
@@ -416,7 +421,7 @@ def run_reference(args, w: Workload, layout, world, rank, dev):
     def train_step(loader):
         # reference train.py:400-453 with --amp bf16 (no GradScaler)
         if pipe is not None:
-            loss_scalar, total_aux = pipe.forward_backward(loader, micro_batches=w.accum, device=dev, use_amp=True,
+            loss_scalar, total_aux = pipe.forward_backward(loader, micro_batches=w.accum, device=dev, use_amp=False,
                                                            amp_dtype=torch.bfloat16, scaler=None, batch_size=w.micro,
                                                            aux_loss_coef=aux_coef)
         else:
@@ -444,6 +449,10 @@ def run_reference(args, w: Workload, layout, world, rank, dev):
 
     eng = Eng()
     eng.train_step = train_step
+    if pipe is not None:
+        eng.dtype = "fp32"
+        eng.note = ("reference pipeline in fp32: with bf16 autocast it sends an fp32 boundary into a bf16 "
+                    "receive buffer (pipeline.py:217-247)")
 
     def make_loader():
         import train as rtrain  # reference train.py (main() is guarded)
@@ -637,7 +646,8 @@ def main():
         rec = {"metric": METRIC, "value": value, "unit": "tokens/s", "n_gpus": world, "steps": args.steps,
                "warmup": max(3, args.warmup), "ms_per_step": ms, "higher_is_better": True,
                "scaling": "weak" if (args.config == "gpt2s_dp" or dp > 1) else "strong",
-               "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None, "dtype": "bf16",
+               "vs_baseline": (value / BASELINE_VALUE) if BASELINE_VALUE else None,
+               "dtype": getattr(eng, "dtype", "bf16"),
                "data": "synthetic uniform-random GPT-2 token ids, random-init weights",
                "config": {"model": w.desc, "global_batch": dp * w.micro * w.accum,
                           "micro_batch": w.micro, "grad_accum_steps": w.accum, "seq_len": SEQ,
@@ -647,6 +657,8 @@ def main():
                "impl": args.impl}
         if args.config != "gpt2s_dp":
             rec["config"]["name"] = args.config
+        if getattr(eng, "note", None):
+            rec["note"] = eng.note
         print(json.dumps(rec))
     if hasattr(eng, "close"):
         eng.close()  # the captured graph must be released before the process group
