@@ -264,7 +264,10 @@ class _Head(torch.autograd.Function):
             ctx.mark_non_differentiable(logits_out) if logits_out is not None else None
             return torch.zeros((), device=x.device), logits_out
         loss, lse, _ = K.cross_entropy_fwd(logits, V, targets)
-        ctx.save_for_backward(x, xn, mean, rstd, logits, lse, targets)
+        # rows the mean runs over (targets equal to ignore_index count for nothing, as in
+        # F.cross_entropy): the gradient scale is dloss / n_valid, like the forward's mean
+        n_valid = (targets != -100).sum().float().clamp_min_(1.0).reshape(1)
+        ctx.save_for_backward(x, xn, mean, rstd, logits, lse, targets, n_valid)
         ctx.ln_w, ctx.ln_b, ctx.wte, ctx.V = ln_w, ln_b, wte, V
         if logits_out is not None:
             ctx.mark_non_differentiable(logits_out)
@@ -272,10 +275,10 @@ class _Head(torch.autograd.Function):
 
     @staticmethod
     def backward(ctx, dloss, _dlogits):
-        x, xn, mean, rstd, logits, lse, targets = ctx.saved_tensors
+        x, xn, mean, rstd, logits, lse, targets, n_valid = ctx.saved_tensors
         V = ctx.V
         M, H = x.shape
-        dl = K.cross_entropy_bwd_(logits, V, targets, lse, dloss.reshape(1).float().contiguous(), 1.0 / M)
+        dl = K.cross_entropy_bwd_(logits, V, targets, lse, (dloss.reshape(1).float() / n_valid).contiguous(), 1.0)
         dlv = dl[:, :V]
         dxn = G.linear_dgrad(dlv, ctx.wte.w16, f32=True)
         G.linear_wgrad(dl, xn, out=ctx.wte.main_grad, accumulate=True, n_rows=V)

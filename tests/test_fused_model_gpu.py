@@ -48,6 +48,33 @@ def test_fused_loss_and_grads(n_layer, n_embed, n_head, V, T):
     assert not bad, bad
 
 
+def test_fused_grads_with_ignored_targets():
+    """Targets equal to -100 (F.cross_entropy's ignore_index) count for nothing: the
+    loss and the gradients are means over the remaining rows only."""
+    from heiretsu_b200.ops._C import check_status
+
+    cfg, ref, fz, flat = _models()
+    g = torch.Generator(device="cuda").manual_seed(2)
+    x = torch.randint(0, 1000, (2, 256), device="cuda", generator=g)
+    y = torch.randint(0, 1000, (2, 256), device="cuda", generator=g)
+    y[0, :100] = -100
+    _, loss_r, _ = ref(x, y)
+    loss_r.backward()
+    _, loss_f, _ = fz(x, y, return_logits=False)
+    loss_f.backward()
+    torch.cuda.synchronize()
+    check_status()
+    assert abs(loss_f.item() - loss_r.item()) < 2e-2, (loss_f.item(), loss_r.item())
+    rp = dict(ref.named_parameters())
+    bad = []
+    for n, p in fz.named_parameters():
+        gr, gf = rp[n].grad, p.main_grad
+        rel = (gf - gr).norm().item() / (gr.norm().item() + 1e-8)
+        if rel > 5e-2:
+            bad.append((n, rel))
+    assert not bad, bad
+
+
 def test_fused_logits_match():
     cfg, ref, fz, flat = _models()
     x = torch.randint(0, 1000, (2, 256), device="cuda")
