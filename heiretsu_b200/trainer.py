@@ -206,7 +206,7 @@ def parse_args(argv=None) -> argparse.Namespace:
         p.set_defaults(**{k.replace("-", "_"): _coerce(actions[k.replace("-", "_")], k, v) for k, v in data.items()
                           if k.replace("-", "_") not in ("config_file", "save_config")})
     args = p.parse_args(argv)
-    if args.save_config:
+    if args.save_config and int(os.environ.get("RANK", "0")) == 0:  # one writer in a multi-process job
         save_config(args, args.save_config)
     return args
 
