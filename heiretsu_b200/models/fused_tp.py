@@ -21,6 +21,15 @@ gathered activations kept from forward. Parameters replicated over TP
 (LayerNorms, row-parallel biases, embeddings) accumulate token-shard partial
 gradients, summed over the group once per step (``tp_sync_grads``).
 
+Dropout (opt-in, ``--fused_tp_dropout 1``) uses the masks of the single-GPU
+fused path, indexed by global head and global token row, so every TP rank
+draws distinct masks from the one seed: the attention kernels take the
+rank's first head (h0 = tp_rank * heads per rank), and a residual site sums
+the partial outputs with the bias, keeps bf16(mask * sum) and adds it to the
+fp32 residual shard (token rows from tp_rank * Ms). Backward masks the
+residual-gradient shard into the gather source before the all-gather GEMM,
+so both the weight gradient and the bias column sum see the masked gradient.
+
 Ordering between ranks uses device barriers (bounded waits) on the TP group:
 before every gather (sources written) and after every scatter (partials
 delivered); gather sources alternate between two buffers so a rank never
@@ -51,6 +60,12 @@ class TPComm:
         self.recv16 = SymmetricBuffer(g, self.tp * Ms * H * 2, device)
         self.recv32 = SymmetricBuffer(g, self.tp * Ms * H * 4, device)
         self.flags = torch.zeros(self.tp * Ms // 128 + 1, dtype=torch.int32, device=device)
+        self.zero32 = None  # [Ms, H] fp32 zeros: the residual input of a dropout site's partial sum
+
+    def zeros(self) -> torch.Tensor:
+        if self.zero32 is None:
+            self.zero32 = torch.zeros(self.Ms, self.H, dtype=torch.float32, device=self.src[0].device)
+        return self.zero32
 
     def barrier(self) -> None:
         self.src[0].barrier()
@@ -88,14 +103,30 @@ def _empty(*shape, dtype=torch.bfloat16, device=None):
     return torch.empty(*shape, dtype=dtype, device=device)
 
 
+def _resid_dropout(comm: TPComm, x_s: torch.Tensor, bias, d, site: int) -> torch.Tensor:
+    """x_s + bf16(mask * (sum of the TP partial outputs + bias)): a residual dropout site on the
+    token shard (global token rows from tp_rank * Ms, so the mask is the single-GPU one)."""
+    t = torch.empty_like(x_s)
+    K.resid_sum_ln(comm.zeros(), comm.recv16_all(), comm.tp, bias, t)
+    kept = K.dropout_bf16(t, d[0], site, d[2], row0=comm.rank * comm.Ms)
+    return x_s + kept.float()
+
+
+def _attn_drop(attn, comm: TPComm, d):
+    return (d[0], 4 * d[1], d[2], comm.rank * attn.nh_tp, attn.nh_tp * comm.tp) if d else None
+
+
 def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: bool):
     """x_s: fp32 residual token shard [Ms, H] -> next residual shard; returns (x2_s, aux | None, saved)."""
+    from .fused import _dropout_of
+
     attn, mlp = blk.attn, getattr(blk, "mlp", None)
     tp, Ms, H = comm.tp, comm.Ms, comm.H
     M = tp * Ms
     dev = x_s.device
     nh = attn.nh_tp
     ext = _ext()
+    d = _dropout_of(blk)  # (seed snapshot, layer, p) in a training forward with dropout, else None
     # LN1 -> gather source 0
     xn_s = comm.src_view(0)
     m1 = _empty(Ms, dtype=torch.float32, device=dev)
@@ -107,7 +138,7 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
     qkv = _empty(M, n_qkv, device=dev)
     G.gemm(xn_full, attn.c_attn.weight.w16, qkv, n_qkv, G.EPI_BF16, False, False, bias=attn.c_attn.bias,
            ag=comm.ag(0))
-    y, lse = K.attention_fwd(qkv, B, T, nh)
+    y, lse = K.attention_fwd(qkv, B, T, nh, drop=_attn_drop(attn, comm, d))
     G.gemm(y, attn.c_proj.weight.w16, comm.recv16_all(), H, G.EPI_BF16, False, False, rs=comm.rs16())
     comm.barrier()
     x1_s = _empty(Ms, H, dtype=torch.float32, device=dev)
@@ -115,15 +146,22 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
         # MoE sub-layer on this rank's tokens: no TP communication (experts are TP-replicated).
         from .fused_moe import moe_sublayer_fwd
 
-        K.resid_sum_ln(x_s, comm.recv16_all(), tp, attn.c_proj.bias, x1_s)
+        if d:
+            x1_s = _resid_dropout(comm, x_s, attn.c_proj.bias, d, 4 * d[1] + 1)
+        else:
+            K.resid_sum_ln(x_s, comm.recv16_all(), tp, attn.c_proj.bias, x1_s)
         x2_s, aux, sm = moe_sublayer_fwd(blk, None, x1_s, keep)
-        saved = ((x_s, m1, r1, xn_full, qkv, y, lse), sm) if keep else None
+        saved = ((x_s, m1, r1, xn_full, qkv, y, lse), sm, d) if keep else None
         return x2_s, aux, saved
     xn2_s = comm.src_view(1)
     m2 = _empty(Ms, dtype=torch.float32, device=dev)
     r2 = _empty(Ms, dtype=torch.float32, device=dev)
-    K.resid_sum_ln(x_s, comm.recv16_all(), tp, attn.c_proj.bias, x1_s, blk.ln_2.weight, blk.ln_2.bias, xn2_s, m2,
-                   r2, LN_EPS)
+    if d:
+        x1_s = _resid_dropout(comm, x_s, attn.c_proj.bias, d, 4 * d[1] + 1)
+        ext.layernorm_fwd(x1_s, blk.ln_2.weight, blk.ln_2.bias, xn2_s, m2, r2, LN_EPS)
+    else:
+        K.resid_sum_ln(x_s, comm.recv16_all(), tp, attn.c_proj.bias, x1_s, blk.ln_2.weight, blk.ln_2.bias, xn2_s,
+                       m2, r2, LN_EPS)
     comm.barrier()
     xn2_full = _empty(M, H, device=dev)
     n_fc = mlp.c_fc.out_per_partition
@@ -133,9 +171,12 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
            ag=comm.ag(1))
     G.gemm(h, mlp.c_proj.weight.w16, comm.recv16_all(), H, G.EPI_BF16, False, False, rs=comm.rs16())
     comm.barrier()
-    x2_s = _empty(Ms, H, dtype=torch.float32, device=dev)
-    K.resid_sum_ln(x1_s, comm.recv16_all(), tp, mlp.c_proj.bias, x2_s)
-    saved = ((x_s, m1, r1, xn_full, qkv, y, lse), (x1_s, m2, r2, xn2_full, pre, h)) if keep else None
+    if d:
+        x2_s = _resid_dropout(comm, x1_s, mlp.c_proj.bias, d, 4 * d[1] + 2)
+    else:
+        x2_s = _empty(Ms, H, dtype=torch.float32, device=dev)
+        K.resid_sum_ln(x1_s, comm.recv16_all(), tp, mlp.c_proj.bias, x2_s)
+    saved = ((x_s, m1, r1, xn_full, qkv, y, lse), (x1_s, m2, r2, xn2_full, pre, h), d) if keep else None
     return x2_s, None, saved
 
 
@@ -148,16 +189,18 @@ def tp_block_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
     M = tp * Ms
     dev = dres.device
     nh = attn.nh_tp
-    (x_s, m1, r1, xn_full, qkv, y, lse), sm = saved
+    (x_s, m1, r1, xn_full, qkv, y, lse), sm, d = saved
     if hasattr(blk, "moe"):
         from .fused_moe import moe_sublayer_bwd
 
         k = 1 - k
         moe_sublayer_bwd(blk, None, sm, dres, comm.src_view(k), daux, ln_scratch)
-        return _tp_attn_bwd(blk, comm, (x_s, m1, r1, xn_full, qkv, y, lse), dres, k, B, T, ln_scratch)
+        return _tp_attn_bwd(blk, comm, (x_s, m1, r1, xn_full, qkv, y, lse), dres, k, B, T, ln_scratch, d)
     x1_s, m2, r2, xn2_full, pre, h = sm
     n_fc = mlp.c_fc.out_per_partition
-    # --- MLP: x2 = x1 + RS(c_proj(gelu(c_fc(AG(ln_2(x1))))))
+    # --- MLP: x2 = x1 + drop(RS(c_proj(gelu(c_fc(AG(ln_2(x1)))))))
+    if d:  # the gathered gradient of c_proj's output is the masked residual gradient
+        K.dropout_bf16(dres, d[0], 4 * d[1] + 2, d[2], row0=comm.rank * Ms, out=comm.src_view(k))
     comm.barrier()
     dx2_full = _empty(M, H, device=dev)
     dpre = _empty(M, n_fc, device=dev)
@@ -172,24 +215,26 @@ def tp_block_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
     k = 1 - k
     K.layernorm_bwd(comm.recv32_all(), x1_s, m2, r2, blk.ln_2.weight, dres, dres, comm.src_view(k),
                     blk.ln_2.weight.main_grad, blk.ln_2.bias.main_grad, scratch=ln_scratch, dy_srcs=tp)
-    return _tp_attn_bwd(blk, comm, (x_s, m1, r1, xn_full, qkv, y, lse), dres, k, B, T, ln_scratch)
+    return _tp_attn_bwd(blk, comm, (x_s, m1, r1, xn_full, qkv, y, lse), dres, k, B, T, ln_scratch, d)
 
 
-def _tp_attn_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T: int, ln_scratch) -> int:
-    """Attention sub-layer backward: x1 = x + RS(c_proj(attn(c_attn(AG(ln_1(x))))))."""
+def _tp_attn_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T: int, ln_scratch, d=None) -> int:
+    """Attention sub-layer backward: x1 = x + drop(RS(c_proj(attn(c_attn(AG(ln_1(x)))))))."""
     attn = blk.attn
     tp, Ms, H = comm.tp, comm.Ms, comm.H
     M = tp * Ms
     dev = dres.device
     nh = attn.nh_tp
     x_s, m1, r1, xn_full, qkv, y, lse = saved
+    if d:
+        K.dropout_bf16(dres, d[0], 4 * d[1] + 1, d[2], row0=comm.rank * Ms, out=comm.src_view(k))
     comm.barrier()
     dx1_full = _empty(M, H, device=dev)
     dy = _empty(M, attn.h_tp, device=dev)
     G.gemm(dx1_full, attn.c_proj.weight.w16, dy, attn.h_tp, G.EPI_BF16, False, True, ag=comm.ag(k))
     G.linear_wgrad(dx1_full, y, out=attn.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(comm.src_view(k), attn.c_proj.bias.main_grad)
-    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, nh)
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, nh, drop=_attn_drop(attn, comm, d))
     del dy, dx1_full
     G.linear_wgrad(dqkv, xn_full, out=attn.c_attn.weight.main_grad, accumulate=True)
     K.colsum_bf16(dqkv, attn.c_attn.bias.main_grad)
@@ -205,9 +250,12 @@ def _tp_attn_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
 class _TPBody(torch.autograd.Function):
     @staticmethod
     def forward(ctx, x_s, blocks, comm, B, T):
+        from .fused import _snapshot_dropout_seeds
+
         keep = x_s.requires_grad
         saved = []
         aux_total = torch.zeros((), device=x_s.device, dtype=torch.float32)
+        _snapshot_dropout_seeds(blocks)
         comm.barrier()
         for blk in blocks:
             x_s, aux, s = tp_block_fwd(blk, comm, x_s, B, T, keep)

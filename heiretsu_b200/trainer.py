@@ -137,6 +137,9 @@ def build_argparser() -> argparse.ArgumentParser:
                    help="plain engine: 1 = shard the AdamW moments over the DP group (ZeRO stage 1)")
     p.add_argument("--activation_checkpointing", type=int, default=0, choices=[0, 1],
                    help="plain engine: keep only each block's input and recompute the block in backward")
+    p.add_argument("--fused_tp_dropout", type=int, default=0, choices=[0, 1],
+                   help="run tp > 1 with dropout > 0 on the fused engine (masks applied around the in-kernel "
+                        "reduce-scatter and all-gather); 0 = such runs use the plain engine")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
     p.add_argument("--config_file", type=str, default=None,
@@ -380,7 +383,7 @@ class Engine:
         self.amp = args.amp if device.type == "cuda" else "none"
         from .models.fused import fused_supported
 
-        ok, why = fused_supported(cfg, topo)
+        ok, why = fused_supported(cfg, topo, tp_dropout=bool(getattr(args, "fused_tp_dropout", 0)))
         want = args.engine
         if want == "fused" and not ok:
             raise ValueError(f"--engine fused: {why}")

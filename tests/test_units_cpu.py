@@ -439,3 +439,17 @@ def test_node_locality_of_groups(monkeypatch):
         local_world_size(16)
     monkeypatch.delenv("LOCAL_WORLD_SIZE")
     assert local_world_size(4) == 4
+
+
+def test_fused_tp_dropout_is_opt_in():
+    """tp > 1 with dropout runs the fused engine only with --fused_tp_dropout 1."""
+    import types
+
+    from heiretsu_b200.models.fused import fused_supported
+
+    cfg = GPTConfig(block_size=256, vocab_size=1000, n_layer=2, n_head=4, n_embed=256, dropout=0.1)
+    topo = types.SimpleNamespace(dp=1, ep=1, tp=2, pp=1)
+    ok, why = fused_supported(cfg, topo)
+    assert not ok and "--fused_tp_dropout" in why
+    assert fused_supported(cfg, topo, tp_dropout=True)[0]
+    assert fused_supported(cfg, types.SimpleNamespace(dp=2, ep=1, tp=1, pp=1))[0]  # DP with dropout: fused
