@@ -114,6 +114,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--resume", type=str, default=None,
                    help="checkpoint file to load before training; 'auto' = the newest complete step in --out_dir "
                         "(or a fresh start), for jobs restarted after a failure")
+    p.add_argument("--init_from", type=str, default=None,
+                   help="start a new run from the weights of this checkpoint file (any shard of a step, any "
+                        "layout); the optimizer and the step count start fresh")
     p.add_argument("--out_dir", type=str, default=".")
     p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
     p.add_argument("--log_interval", type=int, default=None)
@@ -787,6 +790,16 @@ def main(argv=None) -> None:
     module = engine.module
     start_step = 1
     resume_side = None
+    if args.init_from and args.resume:
+        raise ValueError("--init_from starts a new run from a checkpoint's weights; --resume continues one")
+    if args.init_from:
+        # New run from trained weights (fine-tuning, a changed schedule): weights only, on any
+        # TP/PP/EP layout; optimizer, RNG, data position and step numbering start fresh.
+        from .utils.ckpt import load_for_resume
+        info = load_for_resume(module, args.init_from, topo)
+        engine.after_load()
+        if rank == 0:
+            print(f"[init_from] weights of step {info['step']} from {args.init_from}; starting at step 1")
     if args.resume == "auto":
         # Restart after a failure (torchrun --max-restarts): the newest step every rank
         # finished writing, or a fresh start when there is none.

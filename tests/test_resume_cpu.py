@@ -42,6 +42,27 @@ def test_resume_without_sidecar_loads_weights(tmp_path):
     assert torch.load(b / "ckpt_0000003.pt", weights_only=False)["step"] == 3
 
 
+def test_init_from_loads_weights_only(tmp_path):
+    """--init_from: the new run starts from the checkpoint's weights at step 1 with a fresh
+    optimizer; its first step's loss is the loss of those weights, not of a new init."""
+    from heiretsu_b200.trainer import main
+
+    a, b, c = tmp_path / "a", tmp_path / "b", tmp_path / "c"
+    for d in (a, b, c):
+        d.mkdir()
+    main(_args(a, ["--max_iters", "3", "--save_interval", "3", "--learning_rate", "1e-2"]))
+    for d, extra in ((b, ["--init_from", os.fspath(a / "ckpt_0000003.pt")]), (c, [])):
+        main(_args(d, ["--max_iters", "1", "--save_interval", "1", "--dropout", "0"] + extra))
+    trained = torch.load(a / "ckpt_0000003.pt", weights_only=False)["model"]
+    tuned = torch.load(b / "ckpt_0000001.pt", weights_only=False)
+    fresh = torch.load(c / "ckpt_0000001.pt", weights_only=False)["model"]
+    assert tuned["step"] == 1 and not (b / "optim_0000003.pt").exists()
+    # one AdamW step with fresh moments moves every weight by at most ~lr (3e-4) from the trained one
+    for k, v in trained.items():
+        assert (tuned["model"][k] - v).abs().max().item() < 1e-3, k
+    assert max((fresh[k] - v).abs().max().item() for k, v in trained.items()) > 1e-2
+
+
 def _pp_main(rank, world, out_dir):
     from heiretsu_b200.trainer import main
 
