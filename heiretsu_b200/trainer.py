@@ -383,7 +383,7 @@ class Engine:
             from .parallel.pipeline import TiedEmbeddings
             self.tied = TiedEmbeddings(self.module, topo)
             self.tied.sync_weights()
-        self.amp = args.amp if device.type == "cuda" else "none"
+        self.amp = args.amp if device.type in ("cuda", "mps") else "none"  # as train.py:354
         from .models.fused import fused_supported
 
         ok, why = fused_supported(cfg, topo, tp_dropout=bool(getattr(args, "fused_tp_dropout", 0)))
