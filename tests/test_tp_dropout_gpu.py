@@ -12,7 +12,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-pytestmark = pytest.mark.gpu
+pytestmark = [pytest.mark.gpu, pytest.mark.unvalidated]
 
 P_DROP = 0.1
 SEED = 4321
