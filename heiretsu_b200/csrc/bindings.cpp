@@ -24,6 +24,8 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("colsum_bf16", &hb::colsum_bf16);
   m.def("cross_entropy_fwd", &hb::cross_entropy_fwd);
   m.def("cross_entropy_bwd", &hb::cross_entropy_bwd);
+  m.def("cross_entropy_fused", &hb::cross_entropy_fused);
+  m.def("cross_entropy_rescale", &hb::cross_entropy_rescale);
   m.def("embedding_fwd", &hb::embedding_fwd);
   m.def("embedding_bwd", &hb::embedding_bwd);
   m.def("sumsq_scratch_size", &hb::sumsq_scratch_size);

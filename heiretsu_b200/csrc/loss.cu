@@ -117,6 +117,98 @@ __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __res
   }
 }
 
+// Forward and gradient in one pass per row (selected by HB_CE_FUSED=1 on the
+// host side): the log-sum-exp pass reads the row from DRAM, and the gradient
+// pass that follows in the same CTA re-reads it while it is still in L2
+// (a 50304-wide bf16 row is 100 KB; the CTAs in flight hold a few tens of MB),
+// so the logits cross DRAM once each way instead of read twice and written
+// once. The gradient is scaled by *scale_ptr, which the caller computes before
+// the launch (the expected upstream gradient over the number of counted rows);
+// ce_rescale_kernel corrects it in backward when the actual upstream gradient
+// differs. The target logit is read before the row is overwritten.
+__global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __restrict__ logits, long ld, int V,
+                                                              int Vp, const int64_t* __restrict__ targets,
+                                                              int ignore_index, float* __restrict__ lse_out,
+                                                              float* __restrict__ loss_rows,
+                                                              const float* __restrict__ scale_ptr) {
+  __shared__ float sh[32];
+  const long row = blockIdx.x;
+  __nv_bfloat16* lr = logits + row * ld;
+  const int64_t t = targets[row];
+  const bool counted = (t != ignore_index);
+  const float target_logit = (threadIdx.x == 0 && counted) ? __bfloat162float(lr[t]) : 0.f;
+  float m = -INFINITY, s = 0.f;
+  const int nchunk = V >> 3;
+  for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
+    const uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float v[8];
+    float cm = -INFINITY;
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      v[q] = __bfloat162float(e[q]);
+      cm = fmaxf(cm, v[q]);
+    }
+    const float nm = fmaxf(m, cm);
+    float acc = s * __expf(m - nm);
+#pragma unroll
+    for (int q = 0; q < 8; ++q) acc += __expf(v[q] - nm);
+    m = nm;
+    s = acc;
+  }
+  for (int j = nchunk * 8 + threadIdx.x; j < V; j += CE_THREADS) {
+    const float v = __bfloat162float(lr[j]);
+    const float nm = fmaxf(m, v);
+    s = s * __expf(m - nm) + __expf(v - nm);
+    m = nm;
+  }
+  // block reductions end with a barrier: every thread has finished reading the
+  // row (and thread 0 its target logit) before any gradient is written below
+  const float gm = block_reduce_max<CE_THREADS>(m, sh);
+  const float gs = block_reduce_sum<CE_THREADS>((m == -INFINITY) ? 0.f : s * __expf(m - gm), sh);
+  const float lse = gm + __logf(gs);
+  if (threadIdx.x == 0) {
+    lse_out[row] = lse;
+    loss_rows[row] = counted ? lse - target_logit : 0.f;
+  }
+  const float scale = counted ? *scale_ptr : 0.f;
+  const int nchunk_p = Vp >> 3;
+  for (int c = threadIdx.x; c < nchunk_p; c += CE_THREADS) {
+    uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
+    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float g[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) {
+      const int j = c * 8 + q;
+      g[q] = (j < V) ? (__expf(__bfloat162float(e[q]) - lse) - (j == t ? 1.f : 0.f)) * scale : 0.f;
+    }
+    *reinterpret_cast<uint4*>(lr + c * 8) =
+        make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+  }
+}
+
+// g *= actual / expected over [M, Vp] bf16 (row stride ld); every CTA returns at
+// once when the two device scalars are equal (the usual case).
+__global__ void __launch_bounds__(256) ce_rescale_kernel(__nv_bfloat16* __restrict__ g, long ld, int M, int Vp,
+                                                         const float* __restrict__ actual,
+                                                         const float* __restrict__ expected) {
+  const float a = *actual, e = *expected;
+  if (a == e) return;
+  const float r = a / e;
+  const long per_row = Vp >> 3;
+  const long n = (long)M * per_row;
+  for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
+    const long row = i / per_row, c = i % per_row;
+    uint4* ptr = reinterpret_cast<uint4*>(g + row * ld + c * 8);
+    uint4 raw = *ptr;
+    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    float v[8];
+#pragma unroll
+    for (int q = 0; q < 8; ++q) v[q] = __bfloat162float(x[q]) * r;
+    *ptr = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+  }
+}
+
 // out[0] (+)= mean over rows of loss_rows (rows with ignore_index excluded from the count).
 __global__ void __launch_bounds__(1024) mean_loss_kernel(const float* __restrict__ loss_rows,
                                                          const int64_t* __restrict__ targets, int M,
@@ -143,6 +235,26 @@ void ce_fwd_launch(const __nv_bfloat16* logits, long ld, int M, int V, const int
   ce_fwd_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, targets, ignore_index, lse, loss_rows);
   HB_CUDA_CHECK(cudaGetLastError());
   mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, count);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_fused_launch(__nv_bfloat16* logits, long ld, int M, int V, int Vp, const int64_t* targets, int ignore_index,
+                     float* lse, float* loss_rows, float* loss_mean, const float* scale_ptr, cudaStream_t s) {
+  if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
+  if (M == 0) return;
+  ce_fused_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets, ignore_index, lse, loss_rows, scale_ptr);
+  HB_CUDA_CHECK(cudaGetLastError());
+  mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, nullptr);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void ce_rescale_launch(__nv_bfloat16* g, long ld, int M, int Vp, const float* actual, const float* expected,
+                       cudaStream_t s) {
+  if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
+  if (M == 0) return;
+  const long n = (long)M * (Vp >> 3);
+  const int blocks = (int)std::min<long>((n + 255) / 256, 4L * num_sms(current_device()));
+  ce_rescale_kernel<<<blocks, 256, 0, s>>>(g, ld, M, Vp, actual, expected);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

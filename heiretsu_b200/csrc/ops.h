@@ -28,6 +28,9 @@ void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& ta
                        at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean);
 void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                        const at::Tensor& lse, const c10::optional<at::Tensor>& scale, double scale_mul);
+void cross_entropy_fused(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                         at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean, const at::Tensor& scale);
+void cross_entropy_rescale(at::Tensor& g, const at::Tensor& actual, const at::Tensor& expected);
 void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const at::Tensor& wpe, at::Tensor& out);
 void embedding_bwd(const at::Tensor& idx, const at::Tensor& dx, const c10::optional<at::Tensor>& dwte,
                    const c10::optional<at::Tensor>& dwpe);

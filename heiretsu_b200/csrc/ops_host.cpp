@@ -27,6 +27,9 @@ void ce_fwd_launch(const __nv_bfloat16*, long, int, int, const int64_t*, int, fl
                    cudaStream_t);
 void ce_bwd_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, const float*, const float*, float,
                    cudaStream_t);
+void ce_fused_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, float*, float*, float*, const float*,
+                     cudaStream_t);
+void ce_rescale_launch(__nv_bfloat16*, long, int, int, const float*, const float*, cudaStream_t);
 void embed_fwd_launch(const int64_t*, const float*, const float*, float*, int, int, int, cudaStream_t);
 void embed_bwd_launch(const int64_t*, const float*, float*, float*, int, int, int, cudaStream_t);
 int sumsq_num_parts(int device);
@@ -164,6 +167,31 @@ void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets,
   const float* sp = (scale && scale->defined()) ? ptr<float>(*scale) : nullptr;
   ce_bwd_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, logits.size(1),
                 ptr<int64_t>(targets), ignore_index, ptr<float>(lse), sp, static_cast<float>(scale_mul), stream());
+}
+
+void cross_entropy_fused(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                         at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean, const at::Tensor& scale) {
+  CHECK_CUDA(logits);
+  CHECK_DT(logits, at::kBFloat16);
+  CHECK_ROWS(logits);
+  CHECK_DT(targets, at::kLong);
+  CHECK_CONTIG(targets);
+  CHECK_DT(scale, at::kFloat);
+  c10::cuda::CUDAGuard g(logits.device());
+  ce_fused_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, logits.size(1),
+                  ptr<int64_t>(targets), ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean),
+                  ptr<float>(scale), stream());
+}
+
+void cross_entropy_rescale(at::Tensor& g, const at::Tensor& actual, const at::Tensor& expected) {
+  CHECK_CUDA(g);
+  CHECK_DT(g, at::kBFloat16);
+  CHECK_ROWS(g);
+  CHECK_DT(actual, at::kFloat);
+  CHECK_DT(expected, at::kFloat);
+  c10::cuda::CUDAGuard gd(g.device());
+  ce_rescale_launch(ptr<__nv_bfloat16>(g), g.stride(0), g.size(0), g.size(1), ptr<float>(actual),
+                    ptr<float>(expected), stream());
 }
 
 void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const at::Tensor& wpe, at::Tensor& out) {

@@ -24,6 +24,7 @@ LayerNorm statistics -- the same precision split as the reference under
 """
 from __future__ import annotations
 
+import os
 from typing import List, Optional, Tuple
 
 import torch
@@ -255,9 +256,14 @@ def blocks_fused(blocks, x: torch.Tensor, cfg) -> Tuple[torch.Tensor, torch.Tens
 
 
 # ---------------------------------------------------------------------------
+# Single-pass cross-entropy (forward and gradient in one kernel while each logit
+# row is in L2), off until measured on the GPU; HB_CE_FUSED=1 selects it.
+CE_FUSED = os.environ.get("HB_CE_FUSED", "0") == "1"
+
+
 class _Head(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, ln_w, ln_b, wte, targets, V, want_logits):
+    def forward(ctx, x, ln_w, ln_b, wte, targets, V, want_logits, grad_hint=1.0):
         M, H = x.shape
         Vp = _vpad(V)
         xn, mean, rstd = K.layernorm_fwd(x, ln_w, ln_b, LN_EPS)
@@ -267,10 +273,18 @@ class _Head(torch.autograd.Function):
         if targets is None:
             ctx.mark_non_differentiable(logits_out) if logits_out is not None else None
             return torch.zeros((), device=x.device), logits_out
-        loss, lse, _ = K.cross_entropy_fwd(logits, V, targets)
         # rows the mean runs over (targets equal to ignore_index count for nothing, as in
         # F.cross_entropy): the gradient scale is dloss / n_valid, like the forward's mean
         n_valid = (targets != -100).sum().float().clamp_min_(1.0).reshape(1)
+        ctx.ce_fused = CE_FUSED and not want_logits
+        if ctx.ce_fused:
+            # the gradient is written now, scaled for the upstream gradient the caller expects
+            # (grad_hint); backward corrects it only if the actual one differs
+            expected = torch.full((1,), float(grad_hint), device=x.device, dtype=torch.float32)
+            loss, lse = K.cross_entropy_fused_(logits, V, targets, (expected / n_valid).contiguous())
+            n_valid = expected
+        else:
+            loss, lse, _ = K.cross_entropy_fwd(logits, V, targets)
         ctx.save_for_backward(x, xn, mean, rstd, logits, lse, targets, n_valid)
         ctx.ln_w, ctx.ln_b, ctx.wte, ctx.V = ln_w, ln_b, wte, V
         if logits_out is not None:
@@ -282,7 +296,10 @@ class _Head(torch.autograd.Function):
         x, xn, mean, rstd, logits, lse, targets, n_valid = ctx.saved_tensors
         V = ctx.V
         M, H = x.shape
-        dl = K.cross_entropy_bwd_(logits, V, targets, lse, (dloss.reshape(1).float() / n_valid).contiguous(), 1.0)
+        if ctx.ce_fused:  # n_valid holds the expected upstream gradient here
+            dl = K.cross_entropy_rescale_(logits, dloss.reshape(1).float().contiguous(), n_valid)
+        else:
+            dl = K.cross_entropy_bwd_(logits, V, targets, lse, (dloss.reshape(1).float() / n_valid).contiguous(), 1.0)
         dlv = dl[:, :V]
         dxn = G.linear_dgrad(dlv, ctx.wte.w16, f32=True)
         G.linear_wgrad(dl, xn, out=ctx.wte.main_grad, accumulate=True, n_rows=V)
@@ -290,18 +307,18 @@ class _Head(torch.autograd.Function):
         dx16 = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
         zero = torch.zeros_like(x)
         K.layernorm_bwd(dxn, x, mean, rstd, ctx.ln_w, zero, dx, dx16, ctx.ln_w.main_grad, ctx.ln_b.main_grad)
-        return dx, None, None, None, None, None, None
+        return dx, None, None, None, None, None, None, None
 
 
 def head_fused(ln_f, wte: torch.nn.Parameter, x: torch.Tensor, targets: Optional[torch.Tensor], V: int,
-               want_logits: bool = True):
+               want_logits: bool = True, grad_hint: float = 1.0):
     """ln_f -> lm_head (tied to wte) -> cross-entropy. Returns (logits fp32 | None, loss | None)."""
     B, T, H = x.shape
     x2 = x.reshape(B * T, H)
     if x2.dtype != torch.float32:
         x2 = x2.float()
     t = targets.reshape(-1).contiguous() if targets is not None else None
-    loss, logits = _Head.apply(x2.contiguous(), ln_f.weight, ln_f.bias, wte, t, V, want_logits)
+    loss, logits = _Head.apply(x2.contiguous(), ln_f.weight, ln_f.bias, wte, t, V, want_logits, grad_hint)
     if logits is not None:
         logits = logits.view(B, T, V)
     return logits, (loss if targets is not None else None)
@@ -315,7 +332,7 @@ def gpt_forward_fused(model, idx: torch.Tensor, targets: Optional[torch.Tensor],
     x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx)
     x, aux = blocks_fused(model.tr.h, x, cfg)
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x, targets, cfg.vocab_size,
-                              want_logits=return_logits)
+                              want_logits=return_logits, grad_hint=getattr(model, "loss_grad_hint", 1.0))
     return logits, loss, aux
 
 
@@ -338,7 +355,7 @@ def _gpt_forward_fused_tp(model, idx, targets):
     x, aux = blocks_fused_tp(model.tr.h, x.reshape(Ms, -1), cfg, topo, B, T)
     tgt = targets.reshape(-1)[r0:r0 + Ms].view(Bs, T) if targets is not None else None
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x.view(Bs, T, -1), tgt, cfg.vocab_size,
-                              want_logits=False)
+                              want_logits=False, grad_hint=getattr(model, "loss_grad_hint", 1.0) / topo.tp)
     # Each TP rank routes only its token shard; the shard aux losses / tp sum to
     # the mean over shards (the dense aux uses all tokens at once).
     return None, (loss / topo.tp if loss is not None else None), aux / topo.tp

@@ -66,6 +66,24 @@ def cross_entropy_fwd(logits: torch.Tensor, V: int, targets: torch.Tensor, ignor
     return mean, lse, rows
 
 
+def cross_entropy_fused_(logits: torch.Tensor, V: int, targets: torch.Tensor, scale: torch.Tensor,
+                         ignore_index: int = -100):
+    """Forward and gradient in one pass: returns (mean loss, lse) and leaves
+    (softmax - onehot) * scale in ``logits`` (columns >= V zeroed); ``scale`` fp32 [1]."""
+    M = logits.shape[0]
+    lse = torch.empty(M, device=logits.device, dtype=torch.float32)
+    rows = torch.empty(M, device=logits.device, dtype=torch.float32)
+    mean = torch.empty((), device=logits.device, dtype=torch.float32)
+    _ext().cross_entropy_fused(logits, V, targets, ignore_index, lse, rows, mean, scale)
+    return mean, lse
+
+
+def cross_entropy_rescale_(g: torch.Tensor, actual: torch.Tensor, expected: torch.Tensor) -> torch.Tensor:
+    """In place g *= actual / expected (fp32 [1] device scalars); nothing happens when equal."""
+    _ext().cross_entropy_rescale(g, actual, expected)
+    return g
+
+
 def cross_entropy_bwd_(logits, V, targets, lse, scale: Optional[torch.Tensor], scale_mul: float,
                        ignore_index: int = -100) -> torch.Tensor:
     """In place: logits <- (softmax - onehot) * scale * scale_mul (columns >= V zeroed)."""

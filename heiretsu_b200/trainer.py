@@ -431,6 +431,8 @@ class Engine:
                                    tp_group=topo.tp_group if topo.tp > 1 else None,
                                    tp_sum_of=lambda n, p: topo.tp > 1 and not getattr(p, "tp_sharded", False))
             self.module.fused = True
+            # upstream gradient of the data loss in a training step: (loss + aux) / accumulation
+            self.module.loss_grad_hint = 1.0 / args.grad_accum_steps
             clip_group = self.mp_group if args.clip_mode == "global" else None
             mp_symm = None
             if clip_group is not None and device.type == "cuda" and on_one_node(topo, topo.model_parallel_ranks()):
