@@ -706,7 +706,8 @@ class Engine:
             else:
                 x, y = loader.next_batch(self.device)
                 with torch.autocast(device_type=self.device.type, dtype=self.amp_dtype, enabled=self.use_amp):
-                    _, loss, _ = self.forward_module(x, y)
+                    # the loss only: no [tokens, vocab] logits copy
+                    _, loss, _ = self.forward_module(x, y, return_logits=bool(self.args.compile) and not self.fused)
                 if self.fused and self.topo.tp > 1 and dist.is_initialized():
                     loss = loss.detach().clone()
                     dist.all_reduce(loss, group=self.topo.tp_group)  # shard losses / tp sum to the mean
