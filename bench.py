@@ -125,6 +125,8 @@ def parse():
                          "configuration, one process, host-timed)")
     ap.add_argument("--no-e2e", action="store_true")
     ap.add_argument("--no-launch-count", action="store_true", help="skip the profiler-based kernel count")
+    ap.add_argument("--profile-ops", action="store_true",
+                    help="cpu_sanity: print torch.profiler's per-op table of the timed steps to stderr")
     ap.add_argument("--overlap-dp", type=int, default=0, choices=[0, 1],
                     help="reduce DP gradients block by block during the last backward (ours)")
     return ap.parse_args()
@@ -569,12 +571,20 @@ def run_cpu_sanity(args) -> dict:
             return loss.detach(), aux
     for _ in range(args.warmup):
         step()
+    prof = None
+    if getattr(args, "profile_ops", False):
+        from torch.profiler import ProfilerActivity, profile
+        prof = profile(activities=[ProfilerActivity.CPU])
+        prof.__enter__()
     t0 = time.perf_counter()
     last = None
     for _ in range(args.steps):
         last = step()
     loss = float(last[0])  # the last step's loss read back (inside the timed region)
     dt = (time.perf_counter() - t0) / args.steps
+    if prof is not None:
+        prof.__exit__(None, None, None)
+        print(prof.key_averages().table(sort_by="self_cpu_time_total", row_limit=15), file=sys.stderr)
     tokens = c["batch"] * c["block_size"]
     return {"metric": METRIC.replace("device-timed, max over ranks", "host-timed, CPU"), "value": tokens / dt,
             "unit": "tokens/s", "n_gpus": 0, "steps": args.steps, "warmup": args.warmup, "ms_per_step": dt * 1e3,

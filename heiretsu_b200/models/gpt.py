@@ -153,7 +153,7 @@ class _HeadCE(torch.autograd.Function):
     target is not ``ignore_index`` of (lse - logit[target]) (NaN when no row
     counts, like ``F.cross_entropy``). Backward turns the saved logits buffer
     into the gradient in place, (softmax - onehot) * dloss / n, and runs the two
-    GEMMs. Both directions go through the rows in blocks of about 16 MB of
+    GEMMs. Both directions go through the rows in blocks of about 32 MB of
     logits: each block's GEMM output is reduced (forward) or turned into its
     gradient and consumed by its two GEMMs (backward) while it is still in
     cache, so the [N, V] buffer crosses DRAM about three times per step, against
@@ -162,7 +162,7 @@ class _HeadCE(torch.autograd.Function):
     differentiated once (the buffer is consumed).
     """
 
-    BLOCK_BYTES = 16 << 20
+    BLOCK_BYTES = 32 << 20
 
     @staticmethod
     def _blocks(n_rows: int, n_cols: int, esz: int):
