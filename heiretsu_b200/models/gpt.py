@@ -170,9 +170,16 @@ class _HeadCE(torch.autograd.Function):
         return [(r, min(n_rows, r + step)) for r in range(0, n_rows, step)]
 
     @staticmethod
-    def forward(ctx, x, w, targets, ignore_index: int):
+    def forward(ctx, x, w, targets, ignore_index: int, pool):
         N, V = x.shape[0], w.shape[0]
-        logits = torch.empty(N, V, dtype=x.dtype, device=x.device)
+        logits = None
+        while pool:  # a buffer a finished backward handed back (no fresh pages to fault in)
+            cand = pool.pop()
+            if cand.shape == (N, V) and cand.dtype == x.dtype and cand.device == x.device:
+                logits = cand
+                break
+        if logits is None:
+            logits = torch.empty(N, V, dtype=x.dtype, device=x.device)
         lse = torch.empty(N, dtype=x.dtype, device=x.device)
         wt = w.t()
         for a, b in _HeadCE._blocks(N, V, x.element_size()):
@@ -187,6 +194,7 @@ class _HeadCE(torch.autograd.Function):
         loss = torch.where(valid, lse - picked, torch.zeros_like(lse)).sum() / n
         ctx.save_for_backward(x, w, logits, lse, tgt, valid, n)
         ctx.consumed = False
+        ctx.pool = pool
         return loss
 
     @staticmethod
@@ -204,13 +212,20 @@ class _HeadCE(torch.autograd.Function):
             gb.scatter_add_(1, tgt[a:b, None], -scale[a:b, None])
             torch.mm(gb, w, out=dx[a:b])
             dw.addmm_(gb.t(), x[a:b])
-        return dx, dw, None, None
+        if ctx.pool is not None:
+            ctx.pool.append(g)  # nothing else refers to the buffer: the next forward may reuse it
+        return dx, dw, None, None, None
 
 
-def head_cross_entropy(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor,
-                       ignore_index: int = -100) -> torch.Tensor:
-    """Mean cross-entropy of ``x @ w.T`` against ``targets`` without keeping the logits."""
-    return _HeadCE.apply(x.reshape(-1, x.size(-1)), w, targets.reshape(-1), ignore_index)
+def head_cross_entropy(x: torch.Tensor, w: torch.Tensor, targets: torch.Tensor, ignore_index: int = -100,
+                       pool: Optional[list] = None) -> torch.Tensor:
+    """Mean cross-entropy of ``x @ w.T`` against ``targets`` without keeping the logits.
+
+    ``pool``: a list the caller keeps; each backward puts its [N, V] buffer there and
+    the next forward of the same shape takes it back, so steps stop allocating (and
+    page-faulting in) a fresh logits buffer. Pipelines with several forwards in flight
+    simply hold several buffers."""
+    return _HeadCE.apply(x.reshape(-1, x.size(-1)), w, targets.reshape(-1), ignore_index, pool)
 
 
 def init_gpt_weights(module: nn.Module, n_layer: int) -> None:
@@ -258,6 +273,7 @@ class GPT(nn.Module):
         init_gpt_weights(self, cfg.n_layer)
         self.fused = False  # set by heiretsu_b200.models.fused.enable_fused
         self.recompute = False  # activation checkpointing of the plain path (run_blocks)
+        self._head_pool: list = []  # logits buffers reused by head_cross_entropy
 
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None, return_logits: bool = True):
         B, T = idx.shape
@@ -271,7 +287,7 @@ class GPT(nn.Module):
         x, aux_total = run_blocks(self.tr.h, x, self.recompute)
         x = self.tr.ln_f(x)
         if targets is not None and not return_logits and not torch.is_autocast_enabled(x.device.type):
-            return None, head_cross_entropy(x, self.lm_head.weight, targets), aux_total
+            return None, head_cross_entropy(x, self.lm_head.weight, targets, pool=self._head_pool), aux_total
         logits = self.lm_head(x)
         loss = None
         if targets is not None:

@@ -141,6 +141,7 @@ class StageModule(nn.Module):
         init_gpt_weights(self, cfg.n_layer)
         self.fused = False
         self.recompute = False  # activation checkpointing of the plain path (models.gpt.run_blocks)
+        self._head_pool: list = []  # logits buffers reused by head_cross_entropy
         self.topo = topo
 
     # Fused tensor parallelism keeps the residual stream token-sharded: each
@@ -200,7 +201,7 @@ class StageModule(nn.Module):
         x = self.ln_f(x)
         if targets is not None and not want_logits and not torch.is_autocast_enabled(x.device.type):
             from ..models.gpt import head_cross_entropy
-            return None, head_cross_entropy(x, self.lm_head.weight, targets)
+            return None, head_cross_entropy(x, self.lm_head.weight, targets, pool=self._head_pool)
         logits = self.lm_head(x)
         loss = None
         if targets is not None:

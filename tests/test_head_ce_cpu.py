@@ -54,3 +54,46 @@ def test_gpt_forward_without_logits_matches():
     assert abs(l1.item() - l2.item()) < 1e-6
     for n, p in m.named_parameters():
         assert torch.allclose(g1[n], p.grad, atol=1e-6, rtol=1e-5), n
+
+
+def test_head_ce_buffer_pool():
+    """Backward hands its logits buffer to the pool and the next forward takes it; two
+    forwards in flight (a pipeline) hold two buffers; every result stays exact."""
+    g = torch.Generator().manual_seed(4)
+    N, H, V = 32, 16, 300
+    w = torch.randn(V, H, generator=g, dtype=torch.float64, requires_grad=True)
+    pool = []
+
+    def ref(x, t):
+        w.grad = None
+        xr = x.detach().clone().requires_grad_(True)
+        F.cross_entropy((xr @ w.t()), t).backward()
+        return xr.grad, w.grad.clone()
+
+    xs = [torch.randn(N, H, generator=g, dtype=torch.float64, requires_grad=True) for _ in range(4)]
+    ts = [torch.randint(0, V, (N,), generator=g) for _ in range(4)]
+    expect = [ref(x, t) for x, t in zip(xs, ts)]
+    w.grad = None
+    l0 = head_cross_entropy(xs[0], w, ts[0], pool=pool)
+    l0.backward()
+    assert len(pool) == 1
+    buf = pool[0].data_ptr()
+    gw0 = w.grad.clone()
+    w.grad = None
+    l1 = head_cross_entropy(xs[1], w, ts[1], pool=pool)
+    assert not pool  # taken back
+    l1.backward()
+    assert pool[0].data_ptr() == buf
+    gw1 = w.grad.clone()
+    w.grad = None
+    l2 = head_cross_entropy(xs[2], w, ts[2], pool=pool)  # two in flight: the second one allocates
+    l3 = head_cross_entropy(xs[3], w, ts[3], pool=pool)
+    l3.backward()
+    gw3 = w.grad.clone()
+    w.grad = None
+    l2.backward()
+    gw2 = w.grad.clone()
+    assert len(pool) == 2
+    for i, gw in enumerate([gw0, gw1, gw2, gw3]):
+        assert torch.allclose(xs[i].grad, expect[i][0], rtol=1e-10, atol=1e-12), i
+        assert torch.allclose(gw, expect[i][1], rtol=1e-10, atol=1e-12), i
