@@ -165,7 +165,9 @@ class _HeadCE(torch.autograd.Function):
     BLOCK_BYTES = 32 << 20
 
     @staticmethod
-    def _blocks(n_rows: int, n_cols: int, esz: int):
+    def _blocks(n_rows: int, n_cols: int, esz: int, cuda: bool = False):
+        if cuda:  # one block: whole-matrix GEMMs suit a GPU, and its L2 is not the working set here
+            return [(0, n_rows)]
         step = max(16, _HeadCE.BLOCK_BYTES // max(1, n_cols * esz))
         return [(r, min(n_rows, r + step)) for r in range(0, n_rows, step)]
 
@@ -182,7 +184,7 @@ class _HeadCE(torch.autograd.Function):
             logits = torch.empty(N, V, dtype=x.dtype, device=x.device)
         lse = torch.empty(N, dtype=x.dtype, device=x.device)
         wt = w.t()
-        for a, b in _HeadCE._blocks(N, V, x.element_size()):
+        for a, b in _HeadCE._blocks(N, V, x.element_size(), x.is_cuda):
             blk = logits[a:b]
             torch.mm(x[a:b], wt, out=blk)
             m = blk.amax(dim=1, keepdim=True)
@@ -206,7 +208,7 @@ class _HeadCE(torch.autograd.Function):
         scale = torch.where(valid, dloss / n, torch.zeros_like(lse))
         dx = torch.empty_like(x)
         dw = torch.zeros_like(w)
-        for a, b in _HeadCE._blocks(g.shape[0], g.shape[1], g.element_size()):
+        for a, b in _HeadCE._blocks(g.shape[0], g.shape[1], g.element_size(), g.is_cuda):
             gb = g[a:b]
             gb.sub_(lse[a:b, None]).exp_().mul_(scale[a:b, None])
             gb.scatter_add_(1, tgt[a:b, None], -scale[a:b, None])
