@@ -7,6 +7,7 @@
 // row; each lane keeps its share of the row in registers as float4, so the
 // row is read from HBM once and written once.
 #include <cuda_bf16.h>
+#include <cstdlib>
 
 #include "common.cuh"
 #include "dropout.cuh"
@@ -151,7 +152,16 @@ __global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restri
 //   part fp32 [gridDim.x, 2, H]        per-CTA partial dgamma (row 0) and dbeta (row 1)
 // Per-CTA partials are accumulated with shared-memory atomics (no per-thread
 // accumulators), which keeps registers low enough for 3 CTAs per SM.
-template <int V4>
+//
+// HOIST (selected by HB_LN_BWD_HOIST=1 until measured): the incoming residual
+// gradient of a row is loaded in one batch after the row's reductions and
+// before any of its outputs is stored. Without it, each dres_in load follows
+// the previous element's dres store, and since dres may alias dres_in the
+// compiler must keep that order: V4 dependent DRAM round trips per row. The
+// batch reuses the normalised-input registers, which are dead by then, so the
+// register count stays the same; the arithmetic is unchanged (same fused
+// multiply-add per element).
+template <int V4, bool HOIST>
 __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                                         const float* __restrict__ mean, const float* __restrict__ rstd,
                                                         const float* __restrict__ w, const float* dres_in,
@@ -212,17 +222,45 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const float* __restrict_
     const float4* rin = reinterpret_cast<const float4*>(dres_in + (long)r * H);
     float4* rout = reinterpret_cast<float4*>(dres + (long)r * H);
     uint2* r16 = reinterpret_cast<uint2*>(dres16 + (long)r * H);
+    if constexpr (HOIST) {
 #pragma unroll
-    for (int i = 0; i < V4; ++i) {
-      const int j = lane + 32 * i;
-      if (j < H4) {
-        float4 o = rin[j];
-        o.x += rs * (dv[i].x - m1 - xv[i].x * m2);
-        o.y += rs * (dv[i].y - m1 - xv[i].y * m2);
-        o.z += rs * (dv[i].z - m1 - xv[i].z * m2);
-        o.w += rs * (dv[i].w - m1 - xv[i].w * m2);
-        rout[j] = o;
-        r16[j] = make_uint2(pack_bf16(o.x, o.y), pack_bf16(o.z, o.w));
+      for (int i = 0; i < V4; ++i) {  // per-element term; the normalised input is dead after this
+        dv[i].x = dv[i].x - m1 - xv[i].x * m2;
+        dv[i].y = dv[i].y - m1 - xv[i].y * m2;
+        dv[i].z = dv[i].z - m1 - xv[i].z * m2;
+        dv[i].w = dv[i].w - m1 - xv[i].w * m2;
+      }
+#pragma unroll
+      for (int i = 0; i < V4; ++i) {  // every load of the row before any store of it
+        const int j = lane + 32 * i;
+        xv[i] = (j < H4) ? rin[j] : make_float4(0.f, 0.f, 0.f, 0.f);
+      }
+#pragma unroll
+      for (int i = 0; i < V4; ++i) {
+        const int j = lane + 32 * i;
+        if (j < H4) {
+          float4 o;
+          o.x = fmaf(rs, dv[i].x, xv[i].x);
+          o.y = fmaf(rs, dv[i].y, xv[i].y);
+          o.z = fmaf(rs, dv[i].z, xv[i].z);
+          o.w = fmaf(rs, dv[i].w, xv[i].w);
+          rout[j] = o;
+          r16[j] = make_uint2(pack_bf16(o.x, o.y), pack_bf16(o.z, o.w));
+        }
+      }
+    } else {
+#pragma unroll
+      for (int i = 0; i < V4; ++i) {
+        const int j = lane + 32 * i;
+        if (j < H4) {
+          float4 o = rin[j];
+          o.x += rs * (dv[i].x - m1 - xv[i].x * m2);
+          o.y += rs * (dv[i].y - m1 - xv[i].y * m2);
+          o.z += rs * (dv[i].z - m1 - xv[i].z * m2);
+          o.w += rs * (dv[i].w - m1 - xv[i].w * m2);
+          rout[j] = o;
+          r16[j] = make_uint2(pack_bf16(o.x, o.y), pack_bf16(o.z, o.w));
+        }
       }
     }
   }
@@ -394,20 +432,35 @@ void ln_bwd_launch(const float* dy, const float* x, const float* mean, const flo
                    const float* dres_in, float* dres, __nv_bfloat16* dres16, float* part, int num_ctas,
                    float* dgamma, float* dbeta, int M, int H, int dy_srcs, long dy_src_stride, cudaStream_t s) {
   if (M == 0) return;
+  static const bool hoist = [] {
+    const char* e = std::getenv("HB_LN_BWD_HOIST");
+    return e != nullptr && e[0] == '1';
+  }();
   const size_t smem = (size_t)LN_BWD_WARPS * 2 * H * sizeof(float);
   if (smem > 48 * 1024) {
-    static bool attr_set[64][17] = {};
+    static bool attr_set[64][17][2] = {};
     const int dev = current_device();
     const int v = ln_v4(H);
-    if (!attr_set[dev][v]) {
-      HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<kV>,
-                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
-      attr_set[dev][v] = true;
+    if (!attr_set[dev][v][hoist]) {
+      if (hoist) {
+        HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<kV, true>,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
+      } else {
+        HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<kV, false>,
+                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
+      }
+      attr_set[dev][v][hoist] = true;
     }
   }
-  HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
-                                                                          dres16, part, M, H, dy_srcs,
-                                                                          dy_src_stride));
+  if (hoist) {
+    HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV, true><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
+                                                                                  dres16, part, M, H, dy_srcs,
+                                                                                  dy_src_stride));
+  } else {
+    HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV, false><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
+                                                                                   dres16, part, M, H, dy_srcs,
+                                                                                   dy_src_stride));
+  }
   HB_CUDA_CHECK(cudaGetLastError());
   reduce_rows_kernel<<<(2 * H + 31) / 32, 256, 0, s>>>(part, num_ctas, 2 * H, dgamma, dbeta, H);
   HB_CUDA_CHECK(cudaGetLastError());
