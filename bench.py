@@ -19,6 +19,9 @@ same timing; tokens/s counts dp * micro-batch * T * accumulation per step):
                      ep2 x tp2 at 4, dp2 x ep2 x tp2 at 8
   gpt2l_dp2_tp2_pp2  GPT-2 large (36L/20H/1280d), GPipe with 8 micro-batches
                      of 4; pp2 at 2 GPUs, tp2 x pp2 at 4, dp2 x tp2 x pp2 at 8
+  cpu_sanity         GPT 4L/4H/128d, T=256, vocab 50257, micro-batch 8, fp32, one
+                     process on the host CPU (host-timed; --profile-ops prints the
+                     per-op table)
 
 Timing: W untimed warm-up steps; then a barrier and cuda.synchronize, CUDA
 events around exactly K optimizer steps on the launching stream, synchronize
