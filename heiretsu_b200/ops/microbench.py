@@ -206,7 +206,31 @@ def bench_norm(flush):
     return rows
 
 
-EXTRA_BENCHES = {"attention": bench_attention, "norm": bench_norm}
+def bench_ce(flush):
+    """Cross-entropy over [8192, 50304] bf16 logits: forward + in-place gradient as two
+    kernels (ref_ms) against the single-pass kernel (ms). gbs counts the single pass's
+    bytes (one read and one write of the logits)."""
+    from . import kernels as K
+    from ._C import check_status
+
+    M, V, Vp = 8192, 50257, 50304
+    logits = torch.zeros(M, Vp, device="cuda", dtype=torch.bfloat16)
+    logits[:, :V] = torch.randn(M, V, device="cuda").bfloat16()
+    t = torch.randint(0, V, (M,), device="cuda")
+    scale = torch.full((1,), 1.0 / M, device="cuda")
+
+    def two():
+        _, lse, _ = K.cross_entropy_fwd(logits, V, t)
+        K.cross_entropy_bwd_(logits, V, t, lse, scale, 1.0)
+
+    tr = time_fn(two, flush=flush)
+    ts = time_fn(lambda: K.cross_entropy_fused_(logits, V, t, scale), flush=flush)
+    check_status()
+    return [dict(op="cross_entropy", name=f"{M}x{Vp} single pass vs two kernels", ms=ts, ref_ms=tr,
+                 gbs=2 * M * Vp * 2 / ts / 1e6)]
+
+
+EXTRA_BENCHES = {"attention": bench_attention, "norm": bench_norm, "ce": bench_ce}
 
 
 def main(argv=None):
