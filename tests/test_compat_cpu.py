@@ -72,6 +72,12 @@ CASES = [
     ("grad_parity.py", 2, ["--backend", "gloo", "--pp", "2"]),
     ("boundary_push.py", 4, ["--backend", "gloo", "--dp", "2", "--tp", "2", "--steps", "2", "--micro_batches", "2"]),
     ("boundary_push.py", 2, ["--backend", "gloo", "--pp", "2", "--steps", "2", "--micro_batches", "2"]),
+    # the 4-rank dense layouts of the reference's own suite (tests/run_full_suite.sh:35-42)
+    ("parallel_sanity.py", 4, ["--backend", "gloo", "--dp", "4"]),
+    ("parallel_sanity.py", 4, ["--backend", "gloo", "--tp", "4"]),
+    ("parallel_sanity.py", 4, ["--backend", "gloo", "--pp", "4"]),
+    ("parallel_sanity.py", 4, ["--backend", "gloo", "--dp", "2", "--pp", "2"]),
+    ("grad_parity.py", 4, ["--backend", "gloo", "--dp", "2", "--tp", "2"]),
 ]
 
 
