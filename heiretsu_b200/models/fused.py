@@ -197,9 +197,30 @@ def _is_moe(blk) -> bool:
     return hasattr(blk, "moe")
 
 
+class _Recompute:
+    """Saved state of a dense block run without keeping its activations: the block's
+    input and the dropout snapshot its forward used (backward reruns the forward)."""
+
+    def __init__(self, x_in, drop_now):
+        self.x_in, self.drop_now = x_in, drop_now
+
+
+def _rerun_dense(blk, r: "_Recompute", B: int, T: int):
+    """The (attention, MLP) saved tuples of a dense block, recomputed from its input
+    with the forward's dropout masks (a pure function of the saved seed snapshot)."""
+    prev = getattr(blk, "_hb_drop_now", None)
+    blk._hb_drop_now = r.drop_now
+    try:
+        x1, sa = _attn_fwd(blk, r.x_in, B, T, True)
+        _, sm = _mlp_fwd(blk, x1, True)
+    finally:
+        blk._hb_drop_now = prev
+    return sa, sm
+
+
 class _Body(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, blocks, B, T):
+    def forward(ctx, x, blocks, B, T, recompute=False):
         from .fused_moe import moe_sublayer_fwd
 
         keep = x.requires_grad
@@ -207,15 +228,18 @@ class _Body(torch.autograd.Function):
         aux_total = torch.zeros((), device=x.device, dtype=torch.float32)
         _snapshot_dropout_seeds(blocks)
         for i, blk in enumerate(blocks):
+            # activation checkpointing: a dense block keeps only its input (MoE blocks keep all)
+            rerun = keep and recompute and not _is_moe(blk)
+            x_in = x
             with nvtx(f"block{i}.attn.fwd"):
-                x, sa = _attn_fwd(blk, x, B, T, keep)
+                x, sa = _attn_fwd(blk, x, B, T, keep and not rerun)
             with nvtx(f"block{i}.mlp.fwd"):
                 if _is_moe(blk):
                     x, aux, sm = moe_sublayer_fwd(blk, None, x, keep)
                     aux_total = aux_total + aux
                 else:
-                    x, sm = _mlp_fwd(blk, x, keep)
-            saved.append((sa, sm))
+                    x, sm = _mlp_fwd(blk, x, keep and not rerun)
+            saved.append(_Recompute(x_in, getattr(blk, "_hb_drop_now", None)) if rerun else (sa, sm))
         ctx.blocks, ctx.saved, ctx.B, ctx.T = blocks, saved, B, T
         return x, aux_total
 
@@ -231,7 +255,11 @@ class _Body(torch.autograd.Function):
         if daux is None:
             daux = torch.zeros((), device=dres.device)
         n = len(ctx.blocks)
-        for j, (blk, (sa, sm)) in enumerate(zip(reversed(ctx.blocks), reversed(ctx.saved))):
+        for j, (blk, st) in enumerate(zip(reversed(ctx.blocks), reversed(ctx.saved))):
+            if isinstance(st, _Recompute):
+                with nvtx(f"block{n - 1 - j}.recompute"):
+                    st = _rerun_dense(blk, st, B, T)
+            sa, sm = st
             with nvtx(f"block{n - 1 - j}.mlp.bwd"):
                 if _is_moe(blk):
                     moe_sublayer_bwd(blk, None, sm, dres, dres16, daux, ws["ln_scratch"])
@@ -242,16 +270,17 @@ class _Body(torch.autograd.Function):
             if _BLOCK_DONE_HOOK is not None:
                 _BLOCK_DONE_HOOK(blk)
         ctx.saved = None
-        return dres, None, None, None
+        return dres, None, None, None, None
 
 
-def blocks_fused(blocks, x: torch.Tensor, cfg) -> Tuple[torch.Tensor, torch.Tensor]:
-    """Run a list of blocks (dense or MoE) on x [B, T, H]; returns (fp32 x, summed MoE aux loss)."""
+def blocks_fused(blocks, x: torch.Tensor, cfg, recompute: bool = False) -> Tuple[torch.Tensor, torch.Tensor]:
+    """Run a list of blocks (dense or MoE) on x [B, T, H]; returns (fp32 x, summed MoE aux loss).
+    ``recompute``: dense blocks keep only their input and rerun their forward in backward."""
     B, T, H = x.shape
     x2 = x.reshape(B * T, H)
     if x2.dtype != torch.float32:
         x2 = x2.float()
-    out, aux = _Body.apply(x2.contiguous(), list(blocks), B, T)
+    out, aux = _Body.apply(x2.contiguous(), list(blocks), B, T, bool(recompute))
     return out.view(B, T, H), aux
 
 
@@ -330,7 +359,7 @@ def gpt_forward_fused(model, idx: torch.Tensor, targets: Optional[torch.Tensor],
     if topo is not None and getattr(topo, "tp", 1) > 1:
         return _gpt_forward_fused_tp(model, idx, targets)
     x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx)
-    x, aux = blocks_fused(model.tr.h, x, cfg)
+    x, aux = blocks_fused(model.tr.h, x, cfg, recompute=getattr(model, "recompute", False))
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x, targets, cfg.vocab_size,
                               want_logits=return_logits, grad_hint=getattr(model, "loss_grad_hint", 1.0))
     return logits, loss, aux

@@ -180,7 +180,7 @@ class StageModule(nn.Module):
             return out.view(Bs, T, H), aux / self.tp  # shard aux losses / tp sum to the mean
         if self.fused and x.is_cuda:
             from ..models.fused import blocks_fused
-            return blocks_fused(self.blocks, x, self.cfg)
+            return blocks_fused(self.blocks, x, self.cfg, recompute=self.recompute)
         from ..models.gpt import run_blocks
         return run_blocks(self.blocks, x, self.recompute)
 

@@ -139,7 +139,8 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--zero_stage", type=int, default=0, choices=[0, 1],
                    help="plain engine: 1 = shard the AdamW moments over the DP group (ZeRO stage 1)")
     p.add_argument("--activation_checkpointing", type=int, default=0, choices=[0, 1],
-                   help="plain engine: keep only each block's input and recompute the block in backward")
+                   help="keep only each block's input and recompute the block in backward (plain engine; fused "
+                        "engine without TP: dense blocks, not yet run on GPUs)")
     p.add_argument("--fused_tp_dropout", type=int, default=0, choices=[0, 1],
                    help="run tp > 1 with dropout > 0 on the fused engine (masks applied around the in-kernel "
                         "reduce-scatter and all-gather); 0 = such runs use the plain engine")
@@ -400,10 +401,10 @@ class Engine:
             raise ValueError("--zero_stage 1 runs on the plain engine (--engine plain); the fused engine keeps "
                              "full AdamW moments in its flat buffers")
         if getattr(args, "activation_checkpointing", 0):
-            if self.fused:
-                raise ValueError("--activation_checkpointing runs on the plain engine (--engine plain); the fused "
-                                 "engine keeps every block's activations")
-            self.module.recompute = True
+            if self.fused and topo.tp > 1:
+                raise ValueError("--activation_checkpointing: the fused tensor-parallel blocks keep their "
+                                 "activations; use --engine plain or tp 1")
+            self.module.recompute = True  # plain: torch.utils.checkpoint; fused: dense blocks rerun in backward
         self.dropout_seed = None
         if self.fused and cfg.dropout > 0:
             # Device seed of the fused dropout masks: different per DP / PP rank
