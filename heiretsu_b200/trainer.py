@@ -394,6 +394,10 @@ class Engine:
         if want == "fused" and (device.type != "cuda" or self.amp != "bf16"):
             raise ValueError("--engine fused needs --device cuda and --amp bf16")
         self.fused = (want in ("auto", "fused")) and ok and device.type == "cuda" and self.amp == "bf16"
+        # why an automatic choice ended on the plain engine (logged at start)
+        self.plain_reason = None
+        if not self.fused and want == "auto" and device.type == "cuda":
+            self.plain_reason = why if not ok else "the fused engine runs with --amp bf16"
         if self.fused:
             from .ops._C import load as _load
             _load()  # fail loudly if the extension is missing
@@ -847,6 +851,8 @@ def main(argv=None) -> None:
     if rank == 0:
         print(f"[model] parameters: {n_params:,} ({n_params / 1e6:.1f}M) | engine="
               f"{'fused' if engine.fused else 'plain'}")
+        if engine.plain_reason:
+            print(f"[engine] plain: {engine.plain_reason}")
         per_node = topo.local_world or topo.world_size
         if topo.world_size > per_node:
             dp_how = ("NVLink peer memory" if engine.reducer is not None and engine.reducer.backend == "p2p"
