@@ -1,0 +1,271 @@
+"""PyTorch stand-ins for the sm_100a kernel wrappers, for CPU tests of the fused
+engine's host orchestration.
+
+The fused path (models/fused.py) is Python that sequences kernel calls, saves
+tensors between forward and backward, and (with activation checkpointing)
+reruns forwards. Its kernels run only on a B200, but its sequencing can be
+checked on the CPU: ``emulate(monkeypatch)`` replaces every wrapper in
+``heiretsu_b200.ops.kernels`` and ``heiretsu_b200.ops.gemm`` that the single-GPU
+fused path calls with an fp32 PyTorch restatement of the same contract (same
+argument conventions, same in-place outputs, the same dropout masks through
+``ops/dropout_ref.py``). The kernels themselves are tested against fp32
+oracles on the GPU; these stand-ins test only the code around them.
+"""
+from __future__ import annotations
+
+import math
+
+import torch
+import torch.nn.functional as F
+
+from heiretsu_b200.ops import dropout_ref as DR
+
+
+def _seed(t) -> int:
+    return int(t.reshape(-1)[0].item())
+
+
+def _gelu(x):
+    return F.gelu(x, approximate="tanh")
+
+
+def _gelu_grad(x):
+    x = x.detach().requires_grad_(True)
+    with torch.enable_grad():
+        y = _gelu(x)
+        (g,) = torch.autograd.grad(y.sum(), x)
+    return g
+
+
+# ---- GEMM -------------------------------------------------------------------
+def linear_fwd(x, w, bias=None, *, out=None, n=None):
+    N = int(n if n is not None else w.shape[0])
+    y = x.float() @ w.float().t()
+    if bias is not None:
+        y = y + bias.float()
+    if N > y.shape[1]:
+        y = F.pad(y, (0, N - y.shape[1]))
+    y = y.bfloat16()
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def linear_fwd_gelu(x, w, bias, *, out=None, pre=None):
+    p = x.float() @ w.float().t() + bias.float()
+    return _gelu(p).bfloat16(), p.bfloat16()
+
+
+def linear_fwd_resid(x, w, bias, resid, *, out=None, drop=None):
+    y = x.float() @ w.float().t() + bias.float()
+    if drop is not None:
+        seed, site, p, row0 = drop
+        y = y * DR.residual_mask(_seed(seed), site, y.shape[0], y.shape[1], p, row0).float()
+    r = resid + y
+    if out is not None:
+        out.copy_(r)
+        return out
+    return r
+
+
+def linear_dgrad(dy, w, *, out=None, gelu_pre=None, f32=False):
+    d = dy.float() @ w.float()
+    if gelu_pre is not None:
+        return (d * _gelu_grad(gelu_pre.float())).bfloat16()
+    return d if f32 else d.bfloat16()
+
+
+def linear_wgrad(dy, x, *, out=None, accumulate=False, n_rows=None):
+    N = int(n_rows if n_rows is not None else dy.shape[1])
+    g = dy[:, :N].float().t() @ x.float()
+    if out is None:
+        return g
+    if accumulate:
+        out.add_(g)
+    else:
+        out.copy_(g)
+    return out
+
+
+def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None, grp=None,
+         drop=None):
+    """Only the plain bf16 C = A B^T form (the lm_head) is used on the single-GPU path."""
+    assert epi == 0 and not a_mn and not b_mn and ag is None and rs is None and grp is None
+    y = a.float() @ b.float().t()
+    c[:, :y.shape[1]].copy_(y.bfloat16())
+    if c.shape[1] > y.shape[1]:
+        c[:, y.shape[1]:].zero_()
+    return c
+
+
+# ---- LayerNorm, dropout, conversions ------------------------------------------
+def layernorm_fwd(x, w, b, eps=1e-5):
+    mean = x.mean(-1)
+    rstd = torch.rsqrt(x.var(-1, unbiased=False) + eps)
+    y = (x - mean[:, None]) * rstd[:, None] * w + b
+    return y.bfloat16(), mean, rstd
+
+
+def layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dgamma, dbeta, scratch=None, dy_srcs=1):
+    H = x.shape[-1]
+    g = dy.float().reshape(dy_srcs, -1, H).sum(0) if dy_srcs > 1 else dy.float()
+    xh = (x - mean[:, None]) * rstd[:, None]
+    dgamma.add_((g * xh).sum(0))
+    dbeta.add_(g.sum(0))
+    gw = g * w
+    dx = rstd[:, None] * (gw - gw.mean(-1, keepdim=True) - xh * (gw * xh).mean(-1, keepdim=True))
+    new = dres_in + dx
+    dres.copy_(new)
+    dres16.copy_(new.bfloat16())
+
+
+def dropout_bf16(g, seed, site, p, row0=0, out=None):
+    m = DR.residual_mask(_seed(seed), site, g.shape[0], g.shape[1], p, row0).float()
+    y = (g.float() * m).bfloat16()
+    if out is not None:
+        out.copy_(y)
+        return out
+    return y
+
+
+def f32_to_bf16(x, out=None):
+    if out is None:
+        return x.bfloat16()
+    out.copy_(x)
+    return out
+
+
+def colsum_bf16(x, out):
+    out.add_(x.float().sum(0))
+
+
+# ---- attention ------------------------------------------------------------------
+def _qkv(qkv, B, T, nh):
+    q, k, v = qkv.float().view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4).unbind(0)
+    return q, k, v
+
+
+def _attn(q, k, v, T, drop, B, nh):
+    s = (q @ k.transpose(-1, -2)) / 8.0
+    s = s.masked_fill(torch.ones(T, T, dtype=torch.bool).triu(1), float("-inf"))
+    p = torch.softmax(s, -1)
+    if drop is not None:
+        seed, site, pr, h0, nht = drop
+        p = p * DR.attention_mask(_seed(seed), site, B, nh, T, pr, h0, nht).float()
+    return p @ v
+
+
+def attention_fwd(qkv, B, T, nh, out=None, drop=None):
+    q, k, v = _qkv(qkv, B, T, nh)
+    y = _attn(q, k, v, T, drop, B, nh).transpose(1, 2).reshape(B * T, nh * 64)
+    lse = torch.zeros(B, nh, (T + 127) // 128 * 128)
+    return y.bfloat16(), lse
+
+
+def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv=None, drop=None):
+    q, k, v = (t.detach().requires_grad_(True) for t in _qkv(qkv, B, T, nh))
+    with torch.enable_grad():
+        y = _attn(q, k, v, T, drop, B, nh).transpose(1, 2).reshape(B * T, nh * 64)
+        dq, dk, dv = torch.autograd.grad(y, (q, k, v), dout.float())
+    d = torch.stack([dq, dk, dv]).permute(1, 3, 0, 2, 4).reshape(B * T, 3 * nh * 64)
+    return d.bfloat16()
+
+
+# ---- loss, embedding, optimizer ------------------------------------------------
+def cross_entropy_fwd(logits, V, targets, ignore_index=-100):
+    lf = logits[:, :V].float()
+    lse = torch.logsumexp(lf, -1)
+    valid = targets != ignore_index
+    t = torch.where(valid, targets, torch.zeros_like(targets))
+    rows = torch.where(valid, lse - lf.gather(1, t[:, None]).squeeze(1), torch.zeros_like(lse))
+    mean = rows.sum() / valid.sum().clamp_min(1)
+    return mean, lse, rows
+
+
+def cross_entropy_bwd_(logits, V, targets, lse, scale, scale_mul, ignore_index=-100):
+    lf = logits[:, :V].float()
+    valid = targets != ignore_index
+    s = (scale.reshape(-1)[0] if scale is not None else 1.0) * scale_mul
+    g = torch.exp(lf - lse[:, None])
+    t = torch.where(valid, targets, torch.zeros_like(targets))
+    g.scatter_add_(1, t[:, None], -torch.ones(g.shape[0], 1))
+    g = g * torch.where(valid, s, torch.zeros_like(lse))[:, None]
+    logits.zero_()
+    logits[:, :V].copy_(g.bfloat16())
+    return logits
+
+
+def cross_entropy_fused_(logits, V, targets, scale, ignore_index=-100):
+    mean, lse, _ = cross_entropy_fwd(logits, V, targets, ignore_index)
+    cross_entropy_bwd_(logits, V, targets, lse, scale, 1.0, ignore_index)
+    return mean, lse
+
+
+def cross_entropy_rescale_(g, actual, expected):
+    if not torch.equal(actual, expected):
+        g.copy_((g.float() * (actual / expected)).bfloat16())
+    return g
+
+
+def embedding_fwd(idx, wte, wpe):
+    B, T = idx.shape
+    return (wte[idx] + wpe[:T][None]).reshape(B * T, -1)
+
+
+def embedding_bwd(idx, dx, dwte, dwpe):
+    B, T = idx.shape
+    d = dx.reshape(B, T, -1)
+    if dwte is not None:
+        dwte.index_add_(0, idx.reshape(-1), d.reshape(B * T, -1))
+    if dwpe is not None:
+        dwpe[:T].add_(d.sum(0))
+
+
+def sumsq(x, out, weight=1.0, accumulate=False):
+    v = weight * x.float().pow(2).sum()
+    if accumulate:
+        out.add_(v)
+    else:
+        out.copy_(v)
+
+
+def clip_coef(norm2, max_norm, coef, norm=None):
+    n = norm2.sqrt()
+    if norm is not None:
+        norm.copy_(n)
+    c = torch.clamp(max_norm / (n + 1e-6), max=1.0) if max_norm > 0 else torch.ones(())
+    coef.copy_(torch.where(torch.isfinite(n), c, torch.full((), float("nan"))))
+
+
+def adamw_step(p, g, m, v, p16, hyper, coef):
+    lr, b1, b2, eps, wd, bc1, bc2s, gs = hyper.tolist()
+    c = float(coef)
+    if not math.isfinite(c):
+        return
+    gg = g * c / gs
+    p.mul_(1 - lr * wd)
+    m.mul_(b1).add_(gg, alpha=1 - b1)
+    v.mul_(b2).addcmul_(gg, gg, value=1 - b2)
+    p.addcdiv_(m, (v.sqrt() / bc2s).add_(eps), value=-lr / bc1)
+    if p16 is not None:
+        p16.copy_(p)
+
+
+KERNELS = ["layernorm_fwd", "layernorm_bwd", "dropout_bf16", "f32_to_bf16", "colsum_bf16", "attention_fwd",
+           "attention_bwd", "cross_entropy_fwd", "cross_entropy_bwd_", "cross_entropy_fused_",
+           "cross_entropy_rescale_", "embedding_fwd", "embedding_bwd", "sumsq", "clip_coef", "adamw_step"]
+GEMMS = ["linear_fwd", "linear_fwd_gelu", "linear_fwd_resid", "linear_dgrad", "linear_wgrad", "gemm"]
+
+
+def emulate(monkeypatch) -> None:
+    import heiretsu_b200.models.fused as FZ
+    from heiretsu_b200.ops import gemm as G
+    from heiretsu_b200.ops import kernels as K
+
+    mod = globals()
+    for name in KERNELS:
+        monkeypatch.setattr(K, name, mod[name])
+    for name in GEMMS:
+        monkeypatch.setattr(G, name, mod[name])
+    monkeypatch.setattr(FZ, "_ln_scratch", lambda M, H, device: torch.empty(0))

@@ -1,0 +1,119 @@
+"""The fused engine's host orchestration on the CPU, with the kernel wrappers
+replaced by PyTorch stand-ins (tests/fused_emulation.py): forward/backward
+sequencing and saved tensors against the plain model, activation
+checkpointing (rerun forwards with the saved dropout snapshot), the
+single-pass cross-entropy with its backward correction, and rows whose
+target is ignored. The kernels themselves are covered by the GPU tests."""
+import pytest
+import torch
+
+from fused_emulation import emulate
+
+from heiretsu_b200.config import GPTConfig
+from heiretsu_b200.models.gpt import GPT
+
+CFG = dict(block_size=64, vocab_size=200, n_layer=3, n_head=2, n_embed=128)
+
+
+def _fused(dropout=0.0, recompute=False):
+    from heiretsu_b200.parallel.flat import FlatParams
+
+    torch.manual_seed(0)
+    m = GPT(GPTConfig(**CFG, dropout=dropout))
+    flat = FlatParams(m, torch.device("cpu"))
+    m.fused = True
+    m.recompute = recompute
+    if dropout > 0:
+        seed = torch.tensor([77], dtype=torch.int32)
+        for layer, blk in enumerate(m.tr.h):
+            blk._hb_dropout = (seed, layer, dropout)
+    return m, flat
+
+
+def _step(m, x, y, upstream=1.0):
+    from heiretsu_b200.models.fused import gpt_forward_fused
+
+    _, loss, _ = gpt_forward_fused(m, x, y, return_logits=False)
+    (upstream * loss).backward()
+    return loss.item(), {n: p.main_grad.clone() for n, p in m.named_parameters()}
+
+
+def _batch(ignore=False):
+    g = torch.Generator().manual_seed(5)
+    x = torch.randint(0, 200, (2, 64), generator=g)
+    y = torch.randint(0, 200, (2, 64), generator=g)
+    if ignore:
+        y[1, :20] = -100
+    return x, y
+
+
+def _close(a, b, tol):
+    for n in a:
+        assert (a[n] - b[n]).norm().item() <= tol * (b[n].norm().item() + 1e-8), n
+
+
+@pytest.mark.parametrize("ignore", [False, True])
+def test_emulated_fused_path_matches_the_plain_model(monkeypatch, ignore):
+    emulate(monkeypatch)
+    x, y = _batch(ignore)
+    m, flat = _fused()
+    loss_f, grads_f = _step(m, x, y)
+    torch.manual_seed(0)
+    plain = GPT(GPTConfig(**CFG, dropout=0.0))
+    _, loss_p, _ = plain(x, y)
+    loss_p.backward()
+    assert abs(loss_f - loss_p.item()) < 2e-2
+    _close(grads_f, {n: p.grad for n, p in plain.named_parameters()}, 5e-2)
+
+
+@pytest.mark.parametrize("dropout", [0.0, 0.2])
+def test_emulated_recompute_gives_the_same_gradients(monkeypatch, dropout):
+    emulate(monkeypatch)
+    x, y = _batch()
+    l0, g0 = _step(_fused(dropout)[0], x, y)
+    m1, flat1 = _fused(dropout, recompute=True)
+    l1, g1 = _step(m1, x, y)
+    assert l0 == l1
+    _close(g1, g0, 1e-6)
+    if dropout:  # the masks were really applied: a run without dropout differs
+        _, gn = _step(_fused(0.0)[0], x, y)
+        assert any((gn[n] - g0[n]).norm() > 1e-3 * g0[n].norm() for n in g0)
+
+
+@pytest.mark.parametrize("upstream", [1.0, 0.5])
+@pytest.mark.parametrize("ignore", [False, True])
+def test_emulated_single_pass_cross_entropy(monkeypatch, upstream, ignore):
+    import heiretsu_b200.models.fused as FZ
+
+    emulate(monkeypatch)
+    x, y = _batch(ignore)
+    l0, g0 = _step(_fused()[0], x, y, upstream)
+    monkeypatch.setattr(FZ, "CE_FUSED", True)
+    m1, flat1 = _fused()
+    l1, g1 = _step(m1, x, y, upstream)  # grad_hint 1.0: upstream 0.5 goes through the correction
+    assert abs(l0 - l1) < 1e-6
+    _close(g1, g0, 1e-2)
+
+
+def test_emulated_grad_hint_skips_the_correction(monkeypatch):
+    """With the hint equal to the upstream gradient (1 / accumulation in the trainer), the
+    backward correction is a no-op and the gradients equal the two-kernel path's."""
+    import heiretsu_b200.models.fused as FZ
+
+    emulate(monkeypatch)
+    calls = []
+    real = FZ.K.cross_entropy_rescale_
+
+    def spy(g, actual, expected):
+        calls.append(bool(torch.equal(actual, expected)))
+        return real(g, actual, expected)
+
+    monkeypatch.setattr(FZ.K, "cross_entropy_rescale_", spy)
+    x, y = _batch()
+    l0, g0 = _step(_fused()[0], x, y, 0.5)
+    monkeypatch.setattr(FZ, "CE_FUSED", True)
+    m1, flat1 = _fused()
+    m1.loss_grad_hint = 0.5
+    l1, g1 = _step(m1, x, y, 0.5)
+    assert calls == [True]
+    _close(g1, g0, 1e-2)
