@@ -269,3 +269,132 @@ def emulate(monkeypatch) -> None:
     for name in GEMMS:
         monkeypatch.setattr(G, name, mod[name])
     monkeypatch.setattr(FZ, "_ln_scratch", lambda M, H, device: torch.empty(0))
+
+
+# ---- fused tensor parallelism (gloo ranks) -----------------------------------------
+class FakeTPComm:
+    """Stand-in of models/fused_tp.TPComm on gloo ranks: the same buffers as local
+    tensors; the in-kernel all-gather and reduce-scatter of the GEMM become
+    all_gather calls in ``tp_gemm``; barriers are no-ops (gloo calls block)."""
+
+    def __init__(self, topo, Ms, H):
+        self.tp, self.rank, self.Ms, self.H, self.group = topo.tp, topo.tp_rank, Ms, H, topo.tp_group
+        self.src = [torch.zeros(Ms, H, dtype=torch.bfloat16) for _ in range(2)]
+        self.r16 = torch.zeros(self.tp * Ms, H, dtype=torch.bfloat16)
+        self.r32 = torch.zeros(self.tp * Ms, H, dtype=torch.float32)
+        self.zero32 = None
+
+    def barrier(self):
+        pass
+
+    def zeros(self):
+        if self.zero32 is None:
+            self.zero32 = torch.zeros(self.Ms, self.H)
+        return self.zero32
+
+    def src_view(self, i):
+        return self.src[i]
+
+    def recv16_all(self):
+        return self.r16
+
+    def recv32_all(self):
+        return self.r32
+
+    def ag(self, i):
+        return ("ag", i, self)
+
+    def rs16(self):
+        return ("rs", self)
+
+    def rs32(self):
+        return ("rs", self)
+
+
+def _all_gather(t, group):
+    import torch.distributed as dist
+
+    parts = [torch.empty_like(t) for _ in range(dist.get_world_size(group))]
+    dist.all_gather(parts, t.contiguous(), group=group)
+    return parts
+
+
+def tp_gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None,
+            grp=None, drop=None):
+    """The GEMM forms of the fused TP path: C = A B^T (b_mn False) or A B (b_mn True), with
+    bias, GELU (pre-activation to ``aux``) or dGELU (times GELU'(aux)) epilogues, an
+    all-gather of A's token shards (``ag``) and a reduce-scatter of C into the owners'
+    receive slots (``rs``)."""
+    assert grp is None and drop is None and not a_mn
+    if ag is not None:
+        _, i, comm = ag
+        a.copy_(torch.cat(_all_gather(comm.src[i], comm.group)))
+    y = a.float() @ (b.float() if b_mn else b.float().t())
+    if bias is not None:
+        y = y + bias.float()
+    if epi == 1:
+        aux.copy_(y.bfloat16())
+        y = _gelu(y)
+    elif epi == 5:
+        y = y * _gelu_grad(aux.float())
+    if rs is not None:
+        _, comm = rs
+        out = y.to(c.dtype)
+        for src, part in enumerate(_all_gather(out, comm.group)):
+            c[src * comm.Ms:(src + 1) * comm.Ms].copy_(part[comm.rank * comm.Ms:(comm.rank + 1) * comm.Ms])
+        return c
+    c[:, :y.shape[1]].copy_(y.to(c.dtype))
+    return c
+
+
+def resid_sum_ln(x, parts, nsrc, bias, x_new, w=None, b=None, y=None, mean=None, rstd=None, eps=1e-5):
+    Ms = x.shape[0]
+    s = x + parts.float().reshape(nsrc, Ms, -1).sum(0) + bias
+    x_new.copy_(s)
+    if w is not None:
+        yy, mm, rr = layernorm_fwd(s, w, b, eps)
+        y.copy_(yy)
+        mean.copy_(mm)
+        rstd.copy_(rr)
+
+
+class _FakeExt:
+    @staticmethod
+    def layernorm_fwd(x, w, b, y, mean, rstd, eps):
+        yy, mm, rr = layernorm_fwd(x, w, b, eps)
+        y.copy_(yy)
+        mean.copy_(mm)
+        rstd.copy_(rr)
+
+    @staticmethod
+    def layernorm_bwd_scratch_rows(M):
+        return 1
+
+
+def emulate_tp(setattr_fn) -> None:
+    """Everything ``emulate`` replaces, plus the TP communication layer and GEMM forms.
+    ``setattr_fn(obj, name, value)`` installs a replacement (monkeypatch.setattr or a
+    plain setattr in a spawned rank)."""
+    import heiretsu_b200.models.fused as FZ
+    import heiretsu_b200.models.fused_tp as FT
+    from heiretsu_b200.ops import gemm as G
+    from heiretsu_b200.ops import kernels as K
+
+    mod = globals()
+    for name in KERNELS:
+        setattr_fn(K, name, mod[name])
+    for name in GEMMS:
+        setattr_fn(G, name, mod[name])
+    setattr_fn(G, "gemm", tp_gemm)
+    setattr_fn(K, "resid_sum_ln", resid_sum_ln)
+    setattr_fn(FZ, "_ln_scratch", lambda M, H, device: torch.empty(0))
+    setattr_fn(FT, "_ext", lambda: _FakeExt)
+    comms = {}
+
+    def get_comm(topo, Ms, H, device):
+        key = (id(topo.tp_group), Ms, H)
+        if key not in comms:
+            comms[key] = FakeTPComm(topo, Ms, H)
+        return comms[key]
+
+    setattr_fn(FT, "get_comm", get_comm)

@@ -117,3 +117,69 @@ def test_emulated_grad_hint_skips_the_correction(monkeypatch):
     l1, g1 = _step(m1, x, y, 0.5)
     assert calls == [True]
     _close(g1, g0, 1e-2)
+
+
+def _worker_tp(rank, world, dropout):
+    import torch.distributed as dist
+
+    from fused_emulation import emulate_tp
+
+    from heiretsu_b200.models.fused import gpt_forward_fused
+    from heiretsu_b200.parallel.flat import FlatParams
+    from heiretsu_b200.topo import init_topology
+    from heiretsu_b200.trainer import mark_tp_sharded
+    from heiretsu_b200.utils.ckpt import load_from_full, shard_from_full
+
+    emulate_tp(setattr)
+    topo = init_topology(dp=1, tp=world)
+    cfg = GPTConfig(**dict(CFG, n_layer=2), dropout=dropout)
+    g = torch.Generator().manual_seed(9)
+    x = torch.randint(0, 200, (4, 64), generator=g)
+    y = torch.randint(0, 200, (4, 64), generator=g)
+
+    def with_dropout(m):
+        if dropout > 0:
+            seed = torch.tensor([31], dtype=torch.int32)
+            for layer, blk in enumerate(m.tr.h):
+                blk._hb_dropout = (seed, layer, dropout)
+
+    torch.manual_seed(0)
+    one = GPT(cfg)
+    full = {k: v.detach().clone() for k, v in one.state_dict().items()}
+    f1 = FlatParams(one, torch.device("cpu"))
+    one.fused = True
+    with_dropout(one)
+    _, l1, _ = gpt_forward_fused(one, x, y, return_logits=False)
+    l1.backward()
+    g1 = {n: p.main_grad.clone() for n, p in one.named_parameters()}
+
+    model = GPT(cfg, topo=topo)
+    load_from_full(model, full, topo.tp_rank, topo.tp)
+    mark_tp_sharded(model)
+    flat = FlatParams(model, torch.device("cpu"))
+    model.fused = True
+    with_dropout(model)
+    _, ls, _ = gpt_forward_fused(model, x, y, return_logits=False)
+    ls.backward()
+    for p in model.parameters():  # token-shard partials of TP-replicated parameters
+        if not getattr(p, "tp_sharded", False):
+            dist.all_reduce(p.main_grad, group=topo.tp_group)
+    lt = ls.detach().clone()
+    dist.all_reduce(lt, group=topo.tp_group)
+    expect = shard_from_full(model, {**full, **g1}, topo.tp_rank, topo.tp)
+    worst = max(((p.main_grad - expect[n]).norm() / (expect[n].norm() + 1e-8)).item()
+                for n, p in model.named_parameters())
+    del f1, flat
+    return abs(lt.item() - l1.item()), worst
+
+
+@pytest.mark.parametrize("dropout", [0.0, 0.2])
+def test_emulated_fused_tp_matches_one_process(dropout):
+    """Fused TP orchestration on 2 gloo ranks (all-gather / reduce-scatter GEMM forms
+    emulated) against the one-process fused run: with dropout the masks must be the
+    single-GPU ones (global head and token-row indices) for the two to agree."""
+    from dist_util import run_ranks
+
+    for dloss, worst in run_ranks(_worker_tp, 2, dropout):
+        assert dloss < 2e-2, dloss
+        assert worst < 5e-2, worst
