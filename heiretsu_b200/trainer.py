@@ -117,6 +117,8 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--init_from", type=str, default=None,
                    help="start a new run from the weights of this checkpoint file (any shard of a step, any "
                         "layout); the optimizer and the step count start fresh")
+    p.add_argument("--eval_only", action="store_true",
+                   help="evaluate the (loaded) weights on --eval_iters validation batches and exit")
     p.add_argument("--out_dir", type=str, default=".")
     p.add_argument("--pg_timeout_s", type=float, default=600.0, help="process-group collective timeout")
     p.add_argument("--log_interval", type=int, default=None)
@@ -904,6 +906,18 @@ def main(argv=None) -> None:
     elif is_main and args.wandb and not WANDB_AVAILABLE:
         print("wandb not available; proceeding without external logging.")
 
+    if args.eval_only:
+        # evaluate the weights as loaded (--init_from / --resume) and stop: every rank takes part
+        ev = engine.estimate_loss(val_loader, args.eval_iters)
+        if is_main and ev is not None:
+            print(f"[eval_only] eval_loss {ev:.4f} over {args.eval_iters} batches")
+            if run:
+                wandb.log({"eval/loss": ev})
+                run.finish()
+        engine.close()
+        if distributed and dist.is_initialized():
+            cleanup()
+        return
     module.train()
     t0 = time.time()
     wd = None

@@ -63,6 +63,25 @@ def test_init_from_loads_weights_only(tmp_path):
     assert max((fresh[k] - v).abs().max().item() for k, v in trained.items()) > 1e-2
 
 
+def test_eval_only_reports_the_loaded_weights(tmp_path, capsys):
+    """--eval_only with --init_from prints the evaluation of the checkpoint's weights and trains nothing."""
+    import re
+
+    from heiretsu_b200.trainer import main
+
+    a = tmp_path / "a"
+    a.mkdir()
+    main(_args(a, ["--max_iters", "4", "--save_interval", "4", "--eval_interval", "4", "--eval_iters", "3",
+                   "--learning_rate", "1e-2"]))
+    out = capsys.readouterr().out
+    trained = float(re.search(r"\[eval\] step 4 \| eval_loss ([0-9.]+)", out).group(1))
+    main(_args(tmp_path, ["--eval_only", "--eval_iters", "3", "--init_from", os.fspath(a / "ckpt_0000004.pt")]))
+    out = capsys.readouterr().out
+    got = float(re.search(r"\[eval_only\] eval_loss ([0-9.]+)", out).group(1))
+    assert abs(got - trained) < 1e-3, (got, trained)
+    assert not list(tmp_path.glob("ckpt_*.pt"))
+
+
 def _pp_main(rank, world, out_dir):
     from heiretsu_b200.trainer import main
 
