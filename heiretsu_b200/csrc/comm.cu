@@ -149,6 +149,9 @@ void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<ui
                          long n, float scale, uint32_t* counter, int* status, int threads, cudaStream_t s) {
   const int world = static_cast<int>(data.size());
   if (n % 4 != 0) throw std::runtime_error("dp_allreduce: element count must be a multiple of 4");
+  // float4 peer loads and stores: an unaligned range start would fault the GPU.
+  for (uint64_t ptr : data)
+    if (ptr % 16) throw std::runtime_error("dp_allreduce: peer ranges must start 16-byte aligned");
   const PeerTable t = make_table(data, signal);
   const long n4 = n / 4;
   const long chunk4 = (n4 + world - 1) / world;

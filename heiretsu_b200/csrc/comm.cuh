@@ -28,9 +28,16 @@ struct PeerTable {
 // Per-block barrier across the group. Called by all threads of the block.
 // `counter` is this rank's per-block epoch array (device memory, local).
 // Returns false (after recording an error) if a peer did not arrive in time.
+//
+// The block-wide __syncthreads() before thread 0's system fence is what
+// makes the release cover the stores of EVERY warp of the block (the fence
+// is cumulative over what the CTA barrier ordered before it), not only
+// thread 0's own: a barrier that follows a data phase ("results delivered")
+// must not signal while other warps are still writing into peers' buffers.
 __device__ __forceinline__ bool group_barrier(const PeerTable& pt, int rank, int world, uint32_t* counter,
                                               uint32_t phase_tag, int* status) {
   __shared__ int ok_sh;
+  __syncthreads();
   if (threadIdx.x == 0) {
     ok_sh = 1;
     const uint32_t epoch = counter[blockIdx.x] + 1;  // advanced once per call, after both barriers

@@ -76,6 +76,9 @@ class SymmetricBuffer:
         ``threads`` = 64 gives a footprint small enough to run beside compute kernels."""
         if self.world == 1 or n_elem == 0:
             return
+        if start_elem % 4 or n_elem % 4:
+            raise ValueError(f"sum_range: start ({start_elem}) and count ({n_elem}) must be multiples of 4 "
+                             "(the kernel moves float4 vectors)")
         off = start_elem * 4
         load().dp_allreduce([p + off for p in self.ptrs], self.signal_ptrs, self.rank, n_elem, scale, self.counter,
                             threads)
