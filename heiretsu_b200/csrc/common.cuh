@@ -333,17 +333,27 @@ __host__ __device__ constexpr uint32_t make_idesc_f16(int M, int N, bool a_mn, b
 // Evaluated through the identity 1 + tanh(u) = 2 sigmoid(2u), so
 //   gelu(x) = x * s,  s = 1 / (1 + 2^(-2u log2 e)).
 // The exponential is one ex2.approx; the reciprocal stays off the
-// transcendental unit (which the epilogue's bf16 conversions also use):
-// an integer-subtraction initial estimate (exponent negation, the classic
-// fast-reciprocal bit trick with constant 0x7EF311C7: |rel err| < 5.1% for
-// d in [1, 2^64]) refined by two Newton steps r <- r (2 - d r), giving
-// |rel err| < 7e-6 -- far below bf16 resolution. The exponent is clamped at
-// 64 so d stays finite; gelu -> x * 2^-64 ~ 0 there.
+// transcendental unit (which the epilogue's bf16 conversions also use): an
+// initial estimate by integer subtraction on the float's bit pattern,
+// refined by two Newton steps r <- r (2 - d r).
+//
+// The seed constant, derived here: write d = 2^E (1 + m), m in [0, 1), and
+// K = 0x7E800000 + c * 2^23 (0x7E800000 is exponent field 253). Then
+// K - bits(d) decodes to 2^(-E-1) (1 + c - m) when m <= c, and, after the
+// borrow from the exponent field, to 2^(-E-2) (2 + c - m) when m > c. So
+//   r d = (1 + c - m)(1 + m) / 2   or   (2 + c - m)(1 + m) / 4.
+// The largest |r d - 1| is (1 - c)/2 (at m = 0 and m -> 1) or
+// (1 + c/2)^2 / 2 - 1 (the peak at m = c/2). Equal ripple gives
+// c^2 + 8c - 8 = 0, c = 2 sqrt(6) - 4, K = 0x7E800000 + round(c * 2^23)
+// = 0x7EF311C3, and a seed error of at most (5 - 2 sqrt(6)) / 2 < 5.06%
+// (the same in every binade). Each Newton step squares the relative error:
+// < 2.6e-3, then < 7e-6 -- far below bf16 resolution. The exponent is
+// clamped at 64 so d stays finite; gelu -> x * 2^-64 ~ 0 there.
 __device__ __forceinline__ float sigmoid_2u(float u) {
   float e;
   asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(e) : "f"(fminf(-2.8853900817779268f * u, 64.f)));  // -2 log2(e) u
   const float d = 1.f + e;
-  float r = __int_as_float(0x7EF311C7 - __float_as_int(d));
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(d));
   r = r * fmaf(-d, r, 2.f);
   r = r * fmaf(-d, r, 2.f);
   return r;

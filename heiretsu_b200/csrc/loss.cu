@@ -309,6 +309,8 @@ extern "C" int hb_cross_entropy_fwd_noalloc(const void* logits, long ld, int M, 
                                             int ignore_index, float* lse, float* loss_mean, cudaStream_t stream) {
   if (logits == nullptr || targets == nullptr || lse == nullptr || loss_mean == nullptr) return HB_NOALLOC_ERR_ARG;
   if (M < 0 || V <= 0 || ld < V || ld % 8 != 0) return HB_NOALLOC_ERR_ARG;
+  // Rows are read with 16-byte vector loads: the first row must start 16-byte aligned.
+  if (reinterpret_cast<uintptr_t>(logits) % 16 != 0) return HB_NOALLOC_ERR_ARG;
   if (M > HB_CE_NOALLOC_MAX_ROWS) return HB_NOALLOC_ERR_TOO_LARGE;
   if (M == 0) return HB_NOALLOC_OK;
   float* rows = nullptr;

@@ -24,6 +24,8 @@
 //   each call overwrites the rows it uses before reading them. Calls that
 //   overlap on the GPU (for example on two streams) race on it: order them
 //   on one stream or with events.
+// * M == 0 returns HB_NOALLOC_OK, launches nothing and leaves lse and
+//   *loss_mean untouched (they keep whatever the caller put there).
 // * Kernels are enqueued on `stream`; the call returns without synchronising.
 #pragma once
 
@@ -33,7 +35,7 @@
 #define HB_CE_NOALLOC_MAX_ROWS 65536
 
 #define HB_NOALLOC_OK 0
-#define HB_NOALLOC_ERR_ARG 1        // null pointer, bad V / ld / M
+#define HB_NOALLOC_ERR_ARG 1        // null pointer, bad V / ld / M, logits not 16-byte aligned
 #define HB_NOALLOC_ERR_TOO_LARGE 2  // M > HB_CE_NOALLOC_MAX_ROWS
 #define HB_NOALLOC_ERR_CUDA 3       // a CUDA runtime call failed
 
@@ -41,7 +43,7 @@
 extern "C" {
 #endif
 
-// logits: bf16 [M, ld] (row stride ld elements, ld % 8 == 0, ld >= V), device memory
+// logits: bf16 [M, ld] (row stride ld elements, ld % 8 == 0, ld >= V), device memory, 16-byte aligned
 // targets: int64 [M] class ids (ignore_index rows contribute no loss), device memory
 // lse: fp32 [M] output, device memory; loss_mean: fp32 [1] output, device memory
 int hb_cross_entropy_fwd_noalloc(const void* logits, long ld, int M, int V, const int64_t* targets, int ignore_index,

@@ -36,18 +36,17 @@ from ..ops import kernels as K
 LN_EPS = 1e-5
 
 
-def fused_supported(cfg, topo=None, tp_dropout: bool = False) -> Tuple[bool, str]:
+def fused_supported(cfg, topo=None, tp_dropout: bool = True) -> Tuple[bool, str]:
     """Whether the fused path covers this configuration (else the plain path runs).
 
-    ``tp_dropout`` opts in to dropout on the fused tensor-parallel path
-    (``models/fused_tp.py``; ``--fused_tp_dropout 1``)."""
+    ``tp_dropout`` = False sends tensor-parallel runs with dropout to the plain
+    path (``--fused_tp_dropout 0``); by default they run fused (``models/fused_tp.py``)."""
     if cfg.n_embed % cfg.n_head or cfg.n_embed // cfg.n_head != 64:
         return False, "fused attention needs head_dim == 64"
     if cfg.n_embed % 128:
         return False, "fused path needs n_embed % 128 == 0"
     if cfg.dropout > 0 and topo is not None and getattr(topo, "tp", 1) > 1 and not tp_dropout:
-        return False, ("fused tensor parallelism with dropout is opt-in (--fused_tp_dropout 1); dropout > 0 with "
-                       "tp > 1 uses the plain path")
+        return False, "fused tensor parallelism with dropout is switched off (--fused_tp_dropout 0)"
     if cfg.dropout > 0 and cfg.n_embed % 4:
         return False, "fused dropout needs n_embed % 4 == 0"
     if cfg.num_experts > 0 and topo is not None and getattr(topo, "ep", 1) > 8:

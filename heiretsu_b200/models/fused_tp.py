@@ -21,7 +21,7 @@ gathered activations kept from forward. Parameters replicated over TP
 (LayerNorms, row-parallel biases, embeddings) accumulate token-shard partial
 gradients, summed over the group once per step (``tp_sync_grads``).
 
-Dropout (opt-in, ``--fused_tp_dropout 1``) uses the masks of the single-GPU
+Dropout (on by default; ``--fused_tp_dropout 0`` sends such runs to the plain engine) uses the masks of the single-GPU
 fused path, indexed by global head and global token row, so every TP rank
 draws distinct masks from the one seed: the attention kernels take the
 rank's first head (h0 = tp_rank * heads per rank), and a residual site sums

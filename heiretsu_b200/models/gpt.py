@@ -40,9 +40,11 @@ class AttentionTP(nn.Module):
         if cfg.n_embed % cfg.n_head:
             raise ValueError("n_embed must be divisible by n_head")
         if cfg.n_embed % tp_world_size:
-            raise ValueError(f"n_embed {cfg.n_embed} not divisible by tp {tp_world_size}")
+            raise ValueError(f"n_embed = {cfg.n_embed} does not split evenly over "
+                             f"{tp_world_size} tensor-parallel ranks")
         if cfg.n_head % tp_world_size:
-            raise ValueError(f"n_head {cfg.n_head} not divisible by tp {tp_world_size}")
+            raise ValueError(f"n_head = {cfg.n_head} does not split evenly over "
+                             f"{tp_world_size} tensor-parallel ranks")
         self.n_embed, self.n_head = cfg.n_embed, cfg.n_head
         self.tp_world_size, self.tp_rank, self.tp_group = tp_world_size, tp_rank, tp_group
         self.nh_tp = cfg.n_head // tp_world_size
@@ -280,7 +282,7 @@ class GPT(nn.Module):
     def forward(self, idx: torch.Tensor, targets: Optional[torch.Tensor] = None, return_logits: bool = True):
         B, T = idx.shape
         if T > self.cfg.block_size:
-            raise ValueError(f"Sequence length {T} > block_size {self.cfg.block_size}")
+            raise ValueError(f"input of {T} positions exceeds the model's block_size of {self.cfg.block_size}")
         if self.fused and idx.is_cuda:
             from .fused import gpt_forward_fused
             return gpt_forward_fused(self, idx, targets, return_logits=return_logits)

@@ -92,9 +92,9 @@ class TiedEmbeddings:
 def _partition_layers(n_layer: int, pp: int) -> List[Tuple[int, int]]:
     """Balanced contiguous [start, end) layer ranges; earlier stages take the remainder."""
     if pp <= 0:
-        raise ValueError("pp must be >= 1")
+        raise ValueError(f"pipeline degree {pp}: at least one stage is needed")
     if pp > n_layer:
-        raise ValueError(f"pp {pp} > n_layer {n_layer} (would create empty stages)")
+        raise ValueError(f"{pp} pipeline stages cannot split {n_layer} blocks: every stage needs a block")
     base, rem = divmod(n_layer, pp)
     out, start = [], 0
     for i in range(pp):
@@ -157,7 +157,7 @@ class StageModule(nn.Module):
     def embed(self, idx: torch.Tensor) -> torch.Tensor:
         B, T = idx.shape
         if T > self.cfg.block_size:
-            raise ValueError(f"Sequence length {T} > block_size {self.cfg.block_size}")
+            raise ValueError(f"input of {T} positions exceeds the model's block_size of {self.cfg.block_size}")
         if self.fused and idx.is_cuda:
             from ..models.fused import embed_fused
             if self._tp_fused(idx):

@@ -95,7 +95,8 @@ class ColumnParallelLinear(_TPLinearBase):
         super().__init__()
         self._setup(tp_group, tp_rank, tp_world_size)
         if out_features % self.tp_world_size:
-            raise ValueError(f"out_features {out_features} not divisible by tp {self.tp_world_size}")
+            raise ValueError(f"out_features = {out_features} does not split evenly over "
+                             f"{self.tp_world_size} tensor-parallel ranks")
         self.in_features, self.out_features = in_features, out_features
         self.out_per_partition = out_features // self.tp_world_size
         self.weight = nn.Parameter(torch.empty(self.out_per_partition, in_features))
@@ -126,7 +127,8 @@ class ColumnParallelLinearQKV(_TPLinearBase):
         super().__init__()
         self._setup(tp_group, tp_rank, tp_world_size)
         if out_features % self.tp_world_size:
-            raise ValueError(f"out_features {out_features} not divisible by tp {self.tp_world_size}")
+            raise ValueError(f"out_features = {out_features} does not split evenly over "
+                             f"{self.tp_world_size} tensor-parallel ranks")
         self.in_features, self.out_features = in_features, out_features
         self.out_per_partition = out_features // self.tp_world_size
         self.weight = nn.Parameter(torch.empty(3 * self.out_per_partition, in_features))
@@ -162,7 +164,8 @@ class RowParallelLinear(_TPLinearBase):
         super().__init__()
         self._setup(tp_group, tp_rank, tp_world_size)
         if in_features % self.tp_world_size:
-            raise ValueError(f"in_features {in_features} not divisible by tp {self.tp_world_size}")
+            raise ValueError(f"in_features = {in_features} does not split evenly over "
+                             f"{self.tp_world_size} tensor-parallel ranks")
         self.in_features, self.out_features = in_features, out_features
         self.in_per_partition = in_features // self.tp_world_size
         self.weight = nn.Parameter(torch.empty(out_features, self.in_per_partition))

@@ -119,7 +119,8 @@ def build_groups(dp: int, ep: int, tp: int, pp: int, timeout: Optional[timedelta
         return None, None, None, None
     world = dist.get_world_size()
     if world != dp * ep * tp * pp:
-        raise ValueError(f"world_size={world} must equal dp*ep*tp*pp={dp * ep * tp * pp}")
+        raise ValueError(f"{world} processes cannot form a dp{dp} x ep{ep} x tp{tp} x pp{pp} layout "
+                         f"({dp * ep * tp * pp} ranks)")
     rank = dist.get_rank()
     mine = {}
     kw = {} if timeout is None else {"timeout": timeout}
@@ -143,7 +144,8 @@ def init_topology(dp: int, ep: int = 1, tp: int = 1, pp: int = 1, timeout: Optio
         if world == 1:
             dp = ep = tp = pp = 1
         else:
-            raise ValueError(f"world_size {world} != dp*ep*tp*pp {dp * ep * tp * pp}")
+            raise ValueError(f"layout dp{dp} x ep{ep} x tp{tp} x pp{pp} needs {dp * ep * tp * pp} processes, "
+                             f"the job has {world}")
     dp_rank, ep_rank, pp_rank, tp_rank = coords_from_rank(rank, dp, ep, tp, pp)
     tp_group, pp_group, ep_group, dp_group = build_groups(dp, ep, tp, pp, timeout)
     mem = group_members(dp, ep, tp, pp, rank)

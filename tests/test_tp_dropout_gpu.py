@@ -1,4 +1,4 @@
-"""Fused tensor parallelism with dropout (--fused_tp_dropout 1) against the
+"""Fused tensor parallelism with dropout (the default; --fused_tp_dropout 0 turns it off) against the
 single-GPU fused model with dropout. Both draw their masks from the same seed,
 indexed by global head and token row, so the two runs drop the same elements:
 loss and gradients must agree within the bf16 tolerance of the plain TP test.
@@ -12,7 +12,7 @@ import pytest
 import torch
 import torch.multiprocessing as mp
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unvalidated]
+pytestmark = pytest.mark.gpu
 
 P_DROP = 0.1
 SEED = 4321
@@ -54,7 +54,7 @@ def _worker(rank, world, port, q):
 
         topo = init_topology(dp=1, tp=world)
         cfg = GPTConfig(block_size=256, vocab_size=1000, n_layer=2, n_head=4, n_embed=256, dropout=P_DROP)
-        assert not fused_supported(cfg, topo)[0] and fused_supported(cfg, topo, tp_dropout=True)[0]
+        assert fused_supported(cfg, topo)[0] and not fused_supported(cfg, topo, tp_dropout=False)[0]
         g = torch.Generator(device=dev).manual_seed(5)
         x = torch.randint(0, 1000, (2, 256), device=dev, generator=g)
         y = torch.randint(0, 1000, (2, 256), device=dev, generator=g)

@@ -441,15 +441,39 @@ def test_node_locality_of_groups(monkeypatch):
     assert local_world_size(4) == 4
 
 
-def test_fused_tp_dropout_is_opt_in():
-    """tp > 1 with dropout runs the fused engine only with --fused_tp_dropout 1."""
+def test_fused_tp_dropout_is_default():
+    """tp > 1 with dropout runs the fused engine unless --fused_tp_dropout 0."""
     import types
 
     from heiretsu_b200.models.fused import fused_supported
+    from heiretsu_b200.trainer import build_argparser
 
     cfg = GPTConfig(block_size=256, vocab_size=1000, n_layer=2, n_head=4, n_embed=256, dropout=0.1)
     topo = types.SimpleNamespace(dp=1, ep=1, tp=2, pp=1)
-    ok, why = fused_supported(cfg, topo)
-    assert not ok and "--fused_tp_dropout" in why
-    assert fused_supported(cfg, topo, tp_dropout=True)[0]
+    assert fused_supported(cfg, topo)[0]
+    ok, why = fused_supported(cfg, topo, tp_dropout=False)
+    assert not ok and "--fused_tp_dropout 0" in why
+    assert build_argparser().parse_args([]).fused_tp_dropout == 1
     assert fused_supported(cfg, types.SimpleNamespace(dp=2, ep=1, tp=1, pp=1))[0]  # DP with dropout: fused
+
+
+def test_gelu_reciprocal_seed_constant():
+    """The epilogue's reciprocal seed K - bits(d): K is the equal-ripple constant
+    0x7E800000 + round((2 sqrt 6 - 4) 2^23), and its seed error over a whole binade
+    (every fp32 mantissa) stays below (5 - 2 sqrt 6) / 2 plus rounding."""
+    import math
+    import re
+
+    import numpy as np
+
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "heiretsu_b200", "csrc", "common.cuh")).read()
+    k = int(re.search(r"__int_as_float\((0x[0-9A-Fa-f]+) - __float_as_int\(d\)\)", src).group(1), 16)
+    c = 2 * math.sqrt(6) - 4
+    assert k == 0x7E800000 + round(c * 2 ** 23)
+    bits = (np.int64(127) << 23) | np.arange(2 ** 23, dtype=np.int64)
+    d = bits.astype(np.int32).view(np.float32).astype(np.float64)
+    r = (np.int64(k) - bits).astype(np.int32).view(np.float32).astype(np.float64)
+    seed_err = np.abs(r * d - 1).max()
+    assert seed_err <= (5 - 2 * math.sqrt(6)) / 2 + 1e-6
+    assert seed_err ** 4 < 7e-6  # two Newton steps square the error twice

@@ -1,8 +1,10 @@
 """The allocation-free cross-entropy entry point, called through its C symbol.
 
-It must match the regular entry point (the torch binding) on two calls in a
-row; the second call reuses the file-scope scratch left by the first.
-Collected last on purpose, so a failure here never hides another test.
+It exists for callers that cannot allocate device memory (an allocator's
+out-of-memory handler, a C/C++ host that owns every allocation). It must match
+the regular entry point (the torch binding) and an fp32 PyTorch log-sum-exp on
+two calls in a row; the second call reuses the file-scope scratch left by the
+first. Collected last on purpose, so a failure here never hides another test.
 """
 import ctypes
 
@@ -48,6 +50,12 @@ def test_noalloc_matches_regular_entry_point_twice():
         torch.cuda.synchronize()
         assert torch.allclose(lse, ref_lse, atol=1e-5, rtol=1e-5), call
         assert abs(loss.item() - ref_loss.item()) <= 1e-5 * max(1.0, abs(ref_loss.item())), call
+        # fp32 PyTorch oracle of the same op on the same bf16 logits
+        x = logits[:, :V].float()
+        want_lse = torch.logsumexp(x, dim=1)
+        want_loss = (want_lse - x.gather(1, t[:, None]).squeeze(1)).mean()
+        assert torch.allclose(lse, want_lse, atol=1e-4, rtol=1e-5), (call, (lse - want_lse).abs().max().item())
+        assert abs(loss.item() - want_loss.item()) <= 1e-4 * max(1.0, abs(want_loss.item())), call
 
 
 def test_noalloc_rejects_too_many_rows():
@@ -56,3 +64,19 @@ def test_noalloc_rejects_too_many_rows():
     rc = fn(dummy.data_ptr(), 128, 65537, 128, dummy.data_ptr(), -100, dummy.data_ptr(), dummy.data_ptr(),
             torch.cuda.current_stream().cuda_stream)
     assert rc == 2
+
+
+def test_noalloc_rejects_unaligned_logits_and_leaves_outputs_for_zero_rows():
+    fn = _symbol()
+    stream = torch.cuda.current_stream().cuda_stream
+    logits, t = _inputs(16, 256, 2)
+    lse = torch.full((16,), 7.0, device="cuda")
+    loss = torch.full((1,), 7.0, device="cuda")
+    # a row start 2 bytes into the buffer: rejected before any launch
+    rc = fn(logits.data_ptr() + 2, logits.stride(0), 16, 256, t.data_ptr(), -100, lse.data_ptr(), loss.data_ptr(),
+            stream)
+    assert rc == 1
+    rc = fn(logits.data_ptr(), logits.stride(0), 0, 256, t.data_ptr(), -100, lse.data_ptr(), loss.data_ptr(), stream)
+    assert rc == 0
+    torch.cuda.synchronize()
+    assert loss.item() == 7.0 and bool((lse == 7.0).all())
