@@ -117,8 +117,8 @@ __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __res
   }
 }
 
-// Forward and gradient in one pass per row (selected by HB_CE_FUSED=1 on the
-// host side): the log-sum-exp pass reads the row from DRAM, and the gradient
+// Forward and gradient in one pass per row (the model's default; HB_CE_FUSED=0
+// on the host side selects the two-kernel pair): the log-sum-exp pass reads the row from DRAM, and the gradient
 // pass that follows in the same CTA re-reads it while it is still in L2
 // (a 50304-wide bf16 row is 100 KB; the CTAs in flight hold a few tens of MB),
 // so the logits cross DRAM once each way instead of read twice and written

@@ -5,7 +5,9 @@ counterparts on the GPT-2 shapes (M = 8 x 1024 tokens).
 
 Timing: CUDA events around CUDA-graph replays of the op (host launch work
 excluded, as in the graph-replayed training step), warm-up first, L2
-flushed by writing a 256 MB buffer before every timed replay, median of the
+flushed before every timed replay by READING a 256 MB buffer (a flush that
+writes leaves ~126 MB of dirty lines whose write-back the timed kernel would
+pay, about 20 us on a B200), median of the
 repeats. PyTorch / cuBLAS references are timed the same way.
 """
 from __future__ import annotations
@@ -17,8 +19,20 @@ import statistics
 import torch
 
 
+class _Flush:
+    """Evicts the timed op's data from L2 without dirtying it: a sum over 256 MB
+    (written once here, only read afterwards) into a preallocated scalar."""
+
+    def __init__(self):
+        self.buf = torch.zeros(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+        self.out = torch.empty((), dtype=torch.float32, device="cuda")
+
+    def __call__(self):
+        torch.sum(self.buf, dim=0, out=self.out)
+
+
 def _flush_buf():
-    return torch.empty(256 * 1024 * 1024 // 4, dtype=torch.float32, device="cuda")
+    return _Flush()
 
 
 REPS, WARMUP = 20, 5
@@ -46,7 +60,7 @@ def time_fn(fn, reps=None, warmup=None, flush=None, graph=True):
     times = []
     for _ in range(reps):
         if flush is not None:
-            flush.zero_()
+            flush()
         s = torch.cuda.Event(enable_timing=True)
         e = torch.cuda.Event(enable_timing=True)
         s.record()

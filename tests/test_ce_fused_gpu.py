@@ -1,4 +1,4 @@
-"""Single-pass cross-entropy (HB_CE_FUSED=1): one kernel writes the loss terms
+"""Single-pass cross-entropy (the default; HB_CE_FUSED=0 selects two kernels): one kernel writes the loss terms
 and the gradient while each logit row is in L2. It must equal the two-kernel
 path (forward, then the in-place gradient), also with ignored targets, and the
 backward correction must rescale the gradient when the upstream gradient is not
@@ -52,6 +52,7 @@ def test_fused_model_with_single_pass_ce(upstream):
     x = torch.randint(0, 1000, (2, 256), device="cuda", generator=gx)
     y = torch.randint(0, 1000, (2, 256), device="cuda", generator=gx)
     grads, losses = [], []
+    default = FZ.CE_FUSED
     for single in (False, True):
         torch.manual_seed(0)
         m = GPT(cfg).cuda()
@@ -62,7 +63,7 @@ def test_fused_model_with_single_pass_ce(upstream):
             _, loss, _ = m(x, y, return_logits=False)  # grad_hint 1.0: upstream 0.5 takes the correction
             (upstream * loss).backward()
         finally:
-            FZ.CE_FUSED = False
+            FZ.CE_FUSED = default
         torch.cuda.synchronize()
         losses.append(loss.item())
         grads.append({n: p.main_grad.clone() for n, p in m.named_parameters()})

@@ -87,6 +87,7 @@ def test_emulated_single_pass_cross_entropy(monkeypatch, upstream, ignore):
 
     emulate(monkeypatch)
     x, y = _batch(ignore)
+    monkeypatch.setattr(FZ, "CE_FUSED", False)  # the two-kernel path as the reference
     l0, g0 = _step(_fused()[0], x, y, upstream)
     monkeypatch.setattr(FZ, "CE_FUSED", True)
     m1, flat1 = _fused()
@@ -110,6 +111,7 @@ def test_emulated_grad_hint_skips_the_correction(monkeypatch):
 
     monkeypatch.setattr(FZ.K, "cross_entropy_rescale_", spy)
     x, y = _batch()
+    monkeypatch.setattr(FZ, "CE_FUSED", False)  # the two-kernel path as the reference
     l0, g0 = _step(_fused()[0], x, y, 0.5)
     monkeypatch.setattr(FZ, "CE_FUSED", True)
     m1, flat1 = _fused()

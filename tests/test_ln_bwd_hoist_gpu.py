@@ -1,6 +1,6 @@
 """LayerNorm backward with the residual-gradient loads batched ahead of the
-stores (HB_LN_BWD_HOIST=1) gives bit-identical outputs to the default
-ordering, in place (dres aliasing dres_in) and out of place, at the model's
+stores (the default; HB_LN_BWD_HOIST=0 selects the plain order) gives
+bit-identical outputs to the plain ordering, in place (dres aliasing dres_in) and out of place, at the model's
 widths. The switch is read once per process, so each setting runs in a child
 process that writes its outputs to a file."""
 import os

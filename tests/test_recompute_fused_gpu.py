@@ -5,7 +5,7 @@ saved state between forward and backward must shrink."""
 import pytest
 import torch
 
-pytestmark = [pytest.mark.gpu, pytest.mark.unvalidated]
+pytestmark = pytest.mark.gpu
 
 
 @pytest.mark.parametrize("dropout", [0.0, 0.1])
