@@ -31,67 +31,16 @@
 //   current one is still in its softmax.
 #include <cuda_bf16.h>
 
-#include "common.cuh"
-#include "dropout.cuh"
+#include <stdexcept>
+
+#include "attention_common.cuh"
 #include "host_utils.h"
 
 namespace hb {
 
-struct AttnParams {
-  int B, T, nh, Hs;         // Hs = nh * 64 (this rank's heads)
-  __nv_bfloat16* out;       // forward: y [B*T, ld_out]; backward: dqkv [B*T, ld_out]
-  long ld_out;
-  float* lse;               // [B, nh, Tpad] NEGATED log2-domain LSE of the scaled scores (-lse, the
-                            // form the backward's fma consumes)
-  int Tpad;
-  const float* dvec;        // backward: -scale * D, D = rowsum(dO * O) [B, nh, Tpad]
-  float* dq_acc;            // backward: fp32 dQ accumulator [B*T, Hs]
-  float scale;              // 1/sqrt(64)
-  float scale_log2;         // scale * log2(e)
-  int* status;
-  uint64_t* trace;          // optional phase timestamps [grid][kTraceSlots] (nullptr: off)
-  // Dropout on the attention probabilities (DROP instantiations only): mask
-  // element ((b * nh_total + h0 + h) * T + q) * T + k.
-  DropoutArgs drop;
-  int h0, nh_total;
-};
-
-// Phase tracing: with a trace buffer set, the kernels stamp %globaltimer at
-// their pipeline hand-offs (slot layout documented at each kernel), which
-// turns "where does a tile's time go" into a measurement. Off by default;
-// one predicated branch per hand-off when off.
-constexpr int kTraceSlots = 80;
-static uint64_t* g_attn_trace = nullptr;
-#define HB_TRACE(slot)                                                                \
-  do {                                                                                \
-    if (p.trace != nullptr && (slot) < kTraceSlots)                                   \
-      p.trace[(long)blockIdx.x * kTraceSlots + (slot)] = globaltimer_ns();            \
-  } while (0)
-
-__device__ __forceinline__ void bulk_load(void* smem_dst, const void* gsrc, uint32_t bytes, uint64_t* bar) {
-  asm volatile(
-      "cp.async.bulk.shared::cluster.global.mbarrier::complete_tx::bytes [%0], [%1], %2, [%3];" ::"r"(
-          smem_u32(smem_dst)),
-      "l"(reinterpret_cast<uint64_t>(gsrc)), "r"(bytes), "r"(smem_u32(bar))
-      : "memory");
-}
-
-// Byte offset of 16-byte chunk `c16` (0..15 over 128 bf16 columns) of row `r`
-// in a K-major 128-byte-swizzled tile of 128 rows x 128 bf16 (two 16 KB atoms).
-__device__ __forceinline__ uint32_t sw128_off(int r, int c16) {
-  return (c16 >> 3) * 16384 + r * 128 + (((c16 & 7) ^ (r & 7)) << 4);
-}
-
-constexpr int kTile = 128;
 constexpr int kD = 64;
 constexpr int kTileBytes = kTile * kD * 2;  // 16 KB
-
-// exp2 on the special-function unit (PTX ex2.approx, flush-to-zero).
-__device__ __forceinline__ float fast_exp2(float x) {
-  float y;
-  asm("ex2.approx.ftz.f32 %0, %1;" : "=f"(y) : "f"(x));
-  return y;
-}
+static uint64_t* g_attn_trace = nullptr;
 
 // ============================================================================
 // Forward
@@ -729,7 +678,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   if (threadIdx.x == 0) HB_TRACE(2);
 }
 
-// dvec[b, h, t] = -scale * D,  D = sum_d dO[b*T+t, h*64+d] * O[b*T+t, h*64+d]   (fp32)
+// dvec[b, h, t] = -scale * D,  D = sum_d dO[b*T+t, h*DH+d] * O[b*T+t, h*DH+d]   (fp32)
+template <int DH>
 __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long ld_o, const __nv_bfloat16* __restrict__ dO,
                                      long ld_do, float* __restrict__ dvec, int B, int T, int nh, int Tpad,
                                      float scale) {
@@ -738,11 +688,11 @@ __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long l
   const int h = i % nh;
   const long row = i / nh;
   const int b = row / T, t = row % T;
-  const uint4* a = reinterpret_cast<const uint4*>(o + row * ld_o + h * kD);
-  const uint4* g = reinterpret_cast<const uint4*>(dO + row * ld_do + h * kD);
+  const uint4* a = reinterpret_cast<const uint4*>(o + row * ld_o + h * DH);
+  const uint4* g = reinterpret_cast<const uint4*>(dO + row * ld_do + h * DH);
   float s = 0.f;
 #pragma unroll
-  for (int k = 0; k < 8; ++k) {
+  for (int k = 0; k < DH / 8; ++k) {
     const uint4 x = a[k], y = g[k];
     const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&x);
     const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&y);
@@ -752,7 +702,7 @@ __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long l
   dvec[((long)b * nh + h) * Tpad + t] = -scale * s;
 }
 
-// dqkv[:, h*64 + d] = bf16(dq_acc)
+// dqkv[:, c] = bf16(dq_acc[:, c]) for the Q columns c < Hs
 __global__ void attn_bwd_dq_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, long ld,
                                    long rows, int Hs) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -765,16 +715,42 @@ __global__ void attn_bwd_dq_kernel(const float* __restrict__ dq_acc, __nv_bfloat
   *reinterpret_cast<uint2*>(dqkv + row * ld + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
 }
 
+// Backward pre-pass of every head width: dvec = -scale * rowsum(dO * O) and a
+// zeroed fp32 dQ accumulator.
+void attn_bwd_prepass(const __nv_bfloat16* o, long ld_o, const __nv_bfloat16* dO, long ld_do, float* dvec,
+                      float* dq_acc, int B, int T, int nh, int dh, int Tpad, float scale, cudaStream_t s) {
+  const long rows = (long)B * T;
+  const unsigned grid = static_cast<unsigned>((rows * nh + 255) / 256);
+  if (dh == 64) {
+    attn_bwd_dvec_kernel<64><<<grid, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, scale);
+  } else if (dh == 128) {
+    attn_bwd_dvec_kernel<128><<<grid, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, scale);
+  } else {
+    throw std::runtime_error("attention backward: head_dim must be 64 or 128 here");
+  }
+  HB_CUDA_CHECK(cudaGetLastError());
+  HB_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * nh * dh, s));
+}
+
+// dQ accumulator -> bf16 Q columns of dqkv.
+void attn_bwd_dq_finish(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, long rows, int Hs, cudaStream_t s) {
+  attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
 // ----------------------------------------------------------------------------
-static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
+CUtensorMap attn_seq_map(const void* base, int B, int T, long ld, int cols, int box_rows) {
   const uint64_t dims[3] = {static_cast<uint64_t>(cols), static_cast<uint64_t>(T), static_cast<uint64_t>(B)};
   const uint64_t strides[2] = {static_cast<uint64_t>(ld) * 2, static_cast<uint64_t>(ld) * 2 * T};
-  const uint32_t box[3] = {64, 128, 1};
+  const uint32_t box[3] = {64, static_cast<uint32_t>(box_rows), 1};
   return make_tmap_bf16(3, base, dims, strides, box, CU_TENSOR_MAP_SWIZZLE_128B);
+}
+static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
+  return attn_seq_map(base, B, T, ld, cols, 128);
 }
 
 void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, long ld_out, float* lse, int B,
-                     int T, int nh, int Tpad, const DropoutArgs& drop, int h0, int nh_total, int* status,
+                     int T, int nh, int Tpad, float scale, const DropoutArgs& drop, int h0, int nh_total, int* status,
                      cudaStream_t s) {
   static bool attr[64] = {};  // the shared-memory opt-in is per device
   const int dev = current_device();
@@ -789,8 +765,8 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   p.h0 = h0;
   p.nh_total = nh_total;
   p.B = B, p.T = T, p.nh = nh, p.Hs = nh * kD, p.out = out, p.ld_out = ld_out, p.lse = lse, p.Tpad = Tpad;
-  p.scale = 0.125f;
-  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   p.trace = g_attn_trace;
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
@@ -806,8 +782,8 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
 
 void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16* o, long ld_o,
                      const __nv_bfloat16* dO, long ld_do, const float* lse, float* dvec, float* dq_acc,
-                     __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, const DropoutArgs& drop,
-                     int h0, int nh_total, int* status, cudaStream_t s) {
+                     __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, float scale,
+                     const DropoutArgs& drop, int h0, int nh_total, int* status, cudaStream_t s) {
   static bool attr[64] = {};  // the shared-memory opt-in is per device
   const int dev = current_device();
   if (!attr[dev]) {
@@ -818,17 +794,15 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   }
   const int Hs = nh * kD;
   const long rows = (long)B * T;
-  attn_bwd_dvec_kernel<<<(rows * nh + 255) / 256, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, 0.125f);
-  HB_CUDA_CHECK(cudaGetLastError());
-  HB_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * Hs, s));
+  attn_bwd_prepass(o, ld_o, dO, ld_do, dvec, dq_acc, B, T, nh, kD, Tpad, scale, s);
   AttnParams p{};
   p.B = B, p.T = T, p.nh = nh, p.Hs = Hs, p.out = dqkv, p.ld_out = ld_dqkv, p.lse = const_cast<float*>(lse);
   p.Tpad = Tpad, p.dvec = dvec, p.dq_acc = dq_acc;
   p.drop = drop;
   p.h0 = h0;
   p.nh_total = nh_total;
-  p.scale = 0.125f;
-  p.scale_log2 = 0.125f * 1.4426950408889634f;
+  p.scale = scale;
+  p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   p.trace = g_attn_trace;
   const CUtensorMap tq = qkv_map(qkv, B, T, ld_qkv, 3 * Hs);
@@ -846,8 +820,7 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
     attn_bwd_kernel<false><<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
   }
   HB_CUDA_CHECK(cudaGetLastError());
-  attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
-  HB_CUDA_CHECK(cudaGetLastError());
+  attn_bwd_dq_finish(dq_acc, dqkv, ld_dqkv, rows, Hs, s);
 }
 
 // Trace buffer for the next attention launches (nullptr turns tracing off).

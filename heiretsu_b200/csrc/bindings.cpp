@@ -36,12 +36,12 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("attention_set_trace", &hb::attention_set_trace);
   m.def("attention_fwd", &hb::attention_fwd, py::arg("qkv"), py::arg("B"), py::arg("T"), py::arg("nh"), py::arg("out"),
         py::arg("lse"), py::arg("drop_seed") = py::none(), py::arg("drop_site") = 0, py::arg("drop_p") = 0.0,
-        py::arg("h0") = 0, py::arg("nh_total") = 0);
+        py::arg("h0") = 0, py::arg("nh_total") = 0, py::arg("head_dim") = 64);
   m.def("dropout_bf16", &hb::dropout_bf16);
   m.def("attention_bwd", &hb::attention_bwd, py::arg("qkv"), py::arg("out"), py::arg("dout"), py::arg("lse"),
         py::arg("B"), py::arg("T"), py::arg("nh"), py::arg("dvec"), py::arg("dq_acc"), py::arg("dqkv"),
         py::arg("drop_seed") = py::none(), py::arg("drop_site") = 0, py::arg("drop_p") = 0.0, py::arg("h0") = 0,
-        py::arg("nh_total") = 0);
+        py::arg("nh_total") = 0, py::arg("head_dim") = 64);
   m.def("raw_malloc", &hb::raw_malloc);
   m.def("raw_free", &hb::raw_free);
   m.def("tensor_from_ptr", &hb::tensor_from_ptr);

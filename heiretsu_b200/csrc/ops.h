@@ -43,13 +43,13 @@ void f32_to_bf16(const at::Tensor& x, at::Tensor& y);
 void attention_set_trace(const c10::optional<at::Tensor>& trace);
 void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse,
                    const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
-                   int64_t nh_total);
+                   int64_t nh_total, int64_t head_dim);
 void dropout_bf16(const at::Tensor& g, at::Tensor& out, const at::Tensor& seed, int64_t site, double p,
                   int64_t row0);
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
                    int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv,
                    const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
-                   int64_t nh_total);
+                   int64_t nh_total, int64_t head_dim);
 uint64_t raw_malloc(int64_t bytes);
 void raw_free(uint64_t ptr);
 at::Tensor tensor_from_ptr(uint64_t ptr, int64_t numel, at::ScalarType dtype, int64_t device);

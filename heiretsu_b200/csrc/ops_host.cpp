@@ -38,11 +38,18 @@ void clip_coef_launch(const float*, float, float*, float*, cudaStream_t);
 void adamw_launch(float*, const float*, float*, float*, __nv_bfloat16*, long, const void*, const float*,
                   cudaStream_t);
 void f32_to_bf16_launch(const float*, __nv_bfloat16*, long, cudaStream_t);
-void attn_fwd_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int,
+void attn_fwd_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int, float,
                      const DropoutArgs&, int, int, int*, cudaStream_t);
 void attn_bwd_launch(const __nv_bfloat16*, long, const __nv_bfloat16*, long, const __nv_bfloat16*, long,
-                     const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, const DropoutArgs&, int,
-                     int, int*, cudaStream_t);
+                     const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, float,
+                     const DropoutArgs&, int, int, int*, cudaStream_t);
+void attn_fwd_d128_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int, float,
+                          const DropoutArgs&, int, int, int*, cudaStream_t);
+void attn_bwd_d128_launch(const __nv_bfloat16*, long, const __nv_bfloat16*, long, const __nv_bfloat16*, long,
+                          const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, float,
+                          const DropoutArgs&, int, int, int*, cudaStream_t);
+void attn_pad_heads(const __nv_bfloat16*, long, __nv_bfloat16*, long, long, int, int, int, cudaStream_t);
+void attn_unpad_heads(const __nv_bfloat16*, long, __nv_bfloat16*, long, long, int, int, int, cudaStream_t);
 void dropout_bf16_launch(const float*, __nv_bfloat16*, long, int, const DropoutArgs&, cudaStream_t);
 
 // Dropout site arguments from a device seed tensor (int32 scalar) and a rate p (0 = off).
@@ -281,44 +288,99 @@ void attention_set_trace(const c10::optional<at::Tensor>& trace) {
   }
 }
 
+// Head widths: 64 and 128 run their own kernels; 16 and 32 run the 64-wide
+// kernels on zero-padded copies of the heads (see attention_d128.cu).
+static void check_head_dim(int64_t dh) {
+  TORCH_CHECK(dh == 16 || dh == 32 || dh == 64 || dh == 128, "attention: head_dim must be 16, 32, 64 or 128, got ",
+              dh);
+}
+
 void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::Tensor& out, at::Tensor& lse,
                    const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
-                   int64_t nh_total) {
+                   int64_t nh_total, int64_t head_dim) {
   CHECK_CUDA(qkv);
   CHECK_DT(qkv, at::kBFloat16);
   CHECK_ROWS(qkv);
   CHECK_DT(out, at::kBFloat16);
   CHECK_ROWS(out);
-  TORCH_CHECK(qkv.size(0) == B * T && qkv.size(1) == 3 * nh * 64, "attention_fwd: qkv must be [B*T, 3*nh*64]");
+  check_head_dim(head_dim);
+  TORCH_CHECK(qkv.size(0) == B * T && qkv.size(1) == 3 * nh * head_dim,
+              "attention_fwd: qkv must be [B*T, 3*nh*head_dim]");
+  TORCH_CHECK(out.size(0) == B * T && out.size(1) >= nh * head_dim, "attention_fwd: out must be [B*T, nh*head_dim]");
   TORCH_CHECK(qkv.stride(0) % 8 == 0 && out.stride(0) % 8 == 0, "attention_fwd: row strides must be 16B multiples");
   const int64_t Tpad = (T + 127) / 128 * 128;
   TORCH_CHECK(lse.numel() >= B * nh * Tpad && lse.scalar_type() == at::kFloat, "attention_fwd: lse [B, nh, Tpad]");
   c10::cuda::CUDAGuard g(qkv.device());
   TORCH_CHECK(drop_p <= 0.0 || T % 2 == 0, "attention dropout pairs keys (T must be even)");
   const DropoutArgs d = make_dropout(drop_seed, drop_site, drop_p, 0);
-  attn_fwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<float>(lse), B,
-                  T, nh, Tpad, d, static_cast<int>(h0), static_cast<int>(nh_total > 0 ? nh_total : nh),
-                  device_status_ptr(qkv.get_device()), stream());
+  const float scale = 1.f / std::sqrt(static_cast<float>(head_dim));
+  const int nht = static_cast<int>(nh_total > 0 ? nh_total : nh);
+  int* status = device_status_ptr(qkv.get_device());
+  if (head_dim == 128) {
+    attn_fwd_d128_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0),
+                         ptr<float>(lse), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+    return;
+  }
+  if (head_dim == 64) {
+    attn_fwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<float>(lse),
+                    B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+    return;
+  }
+  const long rows = B * T;
+  auto opts = qkv.options();
+  at::Tensor qkv_p = at::empty({rows, 3 * nh * 64}, opts), out_p = at::empty({rows, nh * 64}, opts);
+  attn_pad_heads(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), rows, 3, nh,
+                 head_dim, stream());
+  attn_fwd_launch(ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), ptr<__nv_bfloat16>(out_p), out_p.stride(0),
+                  ptr<float>(lse), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+  attn_unpad_heads(ptr<__nv_bfloat16>(out_p), out_p.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), rows, 1, nh,
+                   head_dim, stream());
 }
 
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
                    int64_t B, int64_t T, int64_t nh, at::Tensor& dvec, at::Tensor& dq_acc, at::Tensor& dqkv,
                    const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
-                   int64_t nh_total) {
+                   int64_t nh_total, int64_t head_dim) {
   CHECK_CUDA(qkv);
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&qkv, &out, &dout, &dqkv}) {
     TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 && t->stride(0) % 8 == 0,
                 "attention_bwd: bf16 2-D tensors with 16B-aligned rows expected");
   }
+  check_head_dim(head_dim);
+  TORCH_CHECK(qkv.size(1) == 3 * nh * head_dim && dqkv.size(1) >= 3 * nh * head_dim,
+              "attention_bwd: qkv / dqkv must be [B*T, 3*nh*head_dim]");
   const int64_t Tpad = (T + 127) / 128 * 128;
+  const int64_t dh_k = head_dim < 64 ? 64 : head_dim;  // width the kernels run at
   TORCH_CHECK(dvec.numel() >= B * nh * Tpad && lse.numel() >= B * nh * Tpad, "attention_bwd: lse/dvec size");
-  TORCH_CHECK(dq_acc.numel() >= B * T * nh * 64 && dq_acc.scalar_type() == at::kFloat, "attention_bwd: dq_acc");
+  TORCH_CHECK(dq_acc.numel() >= B * T * nh * dh_k && dq_acc.scalar_type() == at::kFloat, "attention_bwd: dq_acc");
   c10::cuda::CUDAGuard g(qkv.device());
-  attn_bwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0),
-                  ptr<__nv_bfloat16>(dout), dout.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc),
-                  ptr<__nv_bfloat16>(dqkv), dqkv.stride(0), B, T, nh, Tpad,
-                  make_dropout(drop_seed, drop_site, drop_p, 0), static_cast<int>(h0),
-                  static_cast<int>(nh_total > 0 ? nh_total : nh), device_status_ptr(qkv.get_device()), stream());
+  const DropoutArgs d = make_dropout(drop_seed, drop_site, drop_p, 0);
+  const float scale = 1.f / std::sqrt(static_cast<float>(head_dim));
+  const int nht = static_cast<int>(nh_total > 0 ? nh_total : nh);
+  int* status = device_status_ptr(qkv.get_device());
+  if (head_dim >= 64) {
+    auto launch = head_dim == 128 ? attn_bwd_d128_launch : attn_bwd_launch;
+    launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<__nv_bfloat16>(dout),
+           dout.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc), ptr<__nv_bfloat16>(dqkv),
+           dqkv.stride(0), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+    return;
+  }
+  const long rows = B * T;
+  auto opts = qkv.options();
+  at::Tensor qkv_p = at::empty({rows, 3 * nh * 64}, opts), out_p = at::empty({rows, nh * 64}, opts);
+  at::Tensor dout_p = at::empty({rows, nh * 64}, opts), dqkv_p = at::empty({rows, 3 * nh * 64}, opts);
+  attn_pad_heads(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), rows, 3, nh,
+                 head_dim, stream());
+  attn_pad_heads(ptr<__nv_bfloat16>(out), out.stride(0), ptr<__nv_bfloat16>(out_p), out_p.stride(0), rows, 1, nh,
+                 head_dim, stream());
+  attn_pad_heads(ptr<__nv_bfloat16>(dout), dout.stride(0), ptr<__nv_bfloat16>(dout_p), dout_p.stride(0), rows, 1, nh,
+                 head_dim, stream());
+  attn_bwd_launch(ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), ptr<__nv_bfloat16>(out_p), out_p.stride(0),
+                  ptr<__nv_bfloat16>(dout_p), dout_p.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc),
+                  ptr<__nv_bfloat16>(dqkv_p), dqkv_p.stride(0), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht,
+                  status, stream());
+  attn_unpad_heads(ptr<__nv_bfloat16>(dqkv_p), dqkv_p.stride(0), ptr<__nv_bfloat16>(dqkv), dqkv.stride(0), rows, 3,
+                   nh, head_dim, stream());
 }
 
 // out (bf16) = g * mask for a residual dropout site: the gradient reaching

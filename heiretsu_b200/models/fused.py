@@ -41,8 +41,8 @@ def fused_supported(cfg, topo=None, tp_dropout: bool = True) -> Tuple[bool, str]
 
     ``tp_dropout`` = False sends tensor-parallel runs with dropout to the plain
     path (``--fused_tp_dropout 0``); by default they run fused (``models/fused_tp.py``)."""
-    if cfg.n_embed % cfg.n_head or cfg.n_embed // cfg.n_head != 64:
-        return False, "fused attention needs head_dim == 64"
+    if cfg.n_embed % cfg.n_head or cfg.n_embed // cfg.n_head not in (16, 32, 64, 128):
+        return False, "fused attention needs head_dim 16, 32, 64 or 128"
     if cfg.n_embed % 128:
         return False, "fused path needs n_embed % 128 == 0"
     if cfg.dropout > 0 and topo is not None and getattr(topo, "tp", 1) > 1 and not tp_dropout:
@@ -105,7 +105,7 @@ def _attn_fwd(blk, x: torch.Tensor, B: int, T: int, keep: bool):
     xn, m1, r1 = K.layernorm_fwd(x, blk.ln_1.weight, blk.ln_1.bias, LN_EPS)
     qkv = G.linear_fwd(xn, attn.c_attn.weight.w16, attn.c_attn.bias)
     adrop = (d[0], 4 * d[1], d[2], 0, attn.nh_tp) if d else None
-    y, lse = K.attention_fwd(qkv, B, T, attn.nh_tp, drop=adrop)
+    y, lse = K.attention_fwd(qkv, B, T, attn.nh_tp, drop=adrop, head_dim=attn.dh)
     x1 = G.linear_fwd_resid(y, attn.c_proj.weight.w16, attn.c_proj.bias, x,
                             drop=(d[0], 4 * d[1] + 1, d[2], 0) if d else None)
     return x1, ((x, xn, m1, r1, qkv, y, lse, d) if keep else None)
@@ -149,7 +149,7 @@ def _attn_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: int, T: i
     K.colsum_bf16(dout16, attn.c_proj.bias.main_grad)
     del dout16
     adrop = (d[0], 4 * d[1], d[2], 0, attn.nh_tp) if d else None
-    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, attn.nh_tp, drop=adrop)
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, attn.nh_tp, drop=adrop, head_dim=attn.dh)
     del dy
     G.linear_wgrad(dqkv, xn, out=attn.c_attn.weight.main_grad, accumulate=True)
     K.colsum_bf16(dqkv, attn.c_attn.bias.main_grad)

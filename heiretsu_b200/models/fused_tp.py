@@ -138,7 +138,7 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
     qkv = _empty(M, n_qkv, device=dev)
     G.gemm(xn_full, attn.c_attn.weight.w16, qkv, n_qkv, G.EPI_BF16, False, False, bias=attn.c_attn.bias,
            ag=comm.ag(0))
-    y, lse = K.attention_fwd(qkv, B, T, nh, drop=_attn_drop(attn, comm, d))
+    y, lse = K.attention_fwd(qkv, B, T, nh, drop=_attn_drop(attn, comm, d), head_dim=attn.dh)
     G.gemm(y, attn.c_proj.weight.w16, comm.recv16_all(), H, G.EPI_BF16, False, False, rs=comm.rs16())
     comm.barrier()
     x1_s = _empty(Ms, H, dtype=torch.float32, device=dev)
@@ -234,7 +234,7 @@ def _tp_attn_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
     G.gemm(dx1_full, attn.c_proj.weight.w16, dy, attn.h_tp, G.EPI_BF16, False, True, ag=comm.ag(k))
     G.linear_wgrad(dx1_full, y, out=attn.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(comm.src_view(k), attn.c_proj.bias.main_grad)
-    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, nh, drop=_attn_drop(attn, comm, d))
+    dqkv = K.attention_bwd(qkv, y, dy, lse, B, T, nh, drop=_attn_drop(attn, comm, d), head_dim=attn.dh)
     del dy, dx1_full
     G.linear_wgrad(dqkv, xn_full, out=attn.c_attn.weight.main_grad, accumulate=True)
     K.colsum_bf16(dqkv, attn.c_attn.bias.main_grad)

@@ -131,12 +131,13 @@ def f32_to_bf16(x: torch.Tensor, y: Optional[torch.Tensor] = None) -> torch.Tens
 
 
 # ---------------------------------------------------------------------------
-# Attention (head_dim 64, causal)
+# Attention (causal; head_dim 16, 32, 64 or 128)
 # ---------------------------------------------------------------------------
-def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torch.Tensor] = None, drop=None):
-    """qkv bf16 [B*T, 3*nh*64] -> (y bf16 [B*T, nh*64], nlse fp32 [B, nh, Tpad]).
+def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torch.Tensor] = None, drop=None,
+                  head_dim: int = 64):
+    """qkv bf16 [B*T, 3*nh*dh] -> (y bf16 [B*T, nh*dh], nlse fp32 [B, nh, Tpad]), dh = head_dim.
 
-    nlse = -log2(sum_k 2^(s_k * log2(e) / 8)) per query row: the negated
+    nlse = -log2(sum_k 2^(s_k * log2(e) / sqrt(dh))) per query row: the negated
     log2-domain log-sum-exp, kept in the form the backward kernel consumes.
     Natural-log LSE = -nlse * ln(2).
 
@@ -145,23 +146,24 @@ def attention_fwd(qkv: torch.Tensor, B: int, T: int, nh: int, out: Optional[torc
     ops/dropout_ref.py); the backward must get the same ``drop``."""
     Tpad = (T + 127) // 128 * 128
     if out is None:
-        out = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.bfloat16)
+        out = torch.empty(B * T, nh * head_dim, device=qkv.device, dtype=torch.bfloat16)
     lse = torch.empty(B, nh, Tpad, device=qkv.device, dtype=torch.float32)
     d_seed, d_site, d_p, h0, nht = drop if drop is not None else (None, 0, 0.0, 0, 0)
-    _ext().attention_fwd(qkv, B, T, nh, out, lse, d_seed, int(d_site), float(d_p), int(h0), int(nht))
+    _ext().attention_fwd(qkv, B, T, nh, out, lse, d_seed, int(d_site), float(d_p), int(h0), int(nht), int(head_dim))
     return out, lse
 
 
-def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv: Optional[torch.Tensor] = None, drop=None):
-    """Returns dqkv bf16 [B*T, 3*nh*64] (columns [dQ | dK | dV])."""
+def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv: Optional[torch.Tensor] = None, drop=None,
+                  head_dim: int = 64):
+    """Returns dqkv bf16 [B*T, 3*nh*dh] (columns [dQ | dK | dV])."""
     Tpad = (T + 127) // 128 * 128
     if dqkv is None:
-        dqkv = torch.empty(B * T, 3 * nh * 64, device=qkv.device, dtype=torch.bfloat16)
+        dqkv = torch.empty(B * T, 3 * nh * head_dim, device=qkv.device, dtype=torch.bfloat16)
     dvec = torch.empty(B, nh, Tpad, device=qkv.device, dtype=torch.float32)
-    dq_acc = torch.empty(B * T, nh * 64, device=qkv.device, dtype=torch.float32)
+    dq_acc = torch.empty(B * T, nh * max(head_dim, 64), device=qkv.device, dtype=torch.float32)
     d_seed, d_site, d_p, h0, nht = drop if drop is not None else (None, 0, 0.0, 0, 0)
     _ext().attention_bwd(qkv, out, dout, lse, B, T, nh, dvec, dq_acc, dqkv, d_seed, int(d_site), float(d_p), int(h0),
-                         int(nht))
+                         int(nht), int(head_dim))
     return dqkv
 
 

@@ -158,33 +158,34 @@ def bench_gemm(flush):
 
 
 def bench_attention(flush):
-    """Causal attention fwd / bwd, GPT-2 small shape (B=8, T=1024, 12 heads of 64) vs torch SDPA."""
+    """Causal attention fwd / bwd vs torch SDPA on the same box: GPT-2 small's heads
+    (B=8, T=1024, 12 heads of 64) and the reference's default model's (6 heads of 128)."""
     import torch.nn.functional as F
 
     from . import kernels as K
     from ._C import check_status
 
-    B, T, nh = 8, 1024, 12
-    H = nh * 64
-    qkv = torch.randn(B * T, 3 * H, device="cuda", dtype=torch.bfloat16)
-    y, lse = K.attention_fwd(qkv, B, T, nh)
-    dy = torch.randn_like(y)
-    q, k, v = qkv.view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4).unbind(0)
-    q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
-    fwd_flops = 4.0 * B * nh * T * T * 64 / 2
     rows = []
-    t = time_fn(lambda: K.attention_fwd(qkv, B, T, nh, out=y), flush=flush)
-    tr = time_fn(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), flush=flush)
-    rows.append(dict(op="attention", name="fwd", ms=t, ref_ms=tr, tflops=fwd_flops / t / 1e9,
-                     ref_tflops=fwd_flops / tr / 1e9))
-    t = time_fn(lambda: K.attention_bwd(qkv, y, dy, lse, B, T, nh), flush=flush)
-    qg, kg, vg = (x.detach().requires_grad_(True) for x in (q, k, v))
-    o = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
-    g = torch.randn_like(o)
-    # (autograd runs on its own threads and cannot be graph-captured; timed eagerly)
-    tr = time_fn(lambda: torch.autograd.grad(o, (qg, kg, vg), g, retain_graph=True), flush=flush, graph=False)
-    rows.append(dict(op="attention", name="bwd", ms=t, ref_ms=tr, tflops=2.5 * fwd_flops / t / 1e9,
-                     ref_tflops=2.5 * fwd_flops / tr / 1e9))
+    for tag, B, T, nh, dh in (("", 8, 1024, 12, 64), ("_d128", 8, 1024, 6, 128)):
+        H = nh * dh
+        qkv = torch.randn(B * T, 3 * H, device="cuda", dtype=torch.bfloat16)
+        y, lse = K.attention_fwd(qkv, B, T, nh, head_dim=dh)
+        dy = torch.randn_like(y)
+        q, k, v = qkv.view(B, T, 3, nh, dh).permute(2, 0, 3, 1, 4).unbind(0)
+        q, k, v = q.contiguous(), k.contiguous(), v.contiguous()
+        fwd_flops = 4.0 * B * nh * T * T * dh / 2
+        t = time_fn(lambda: K.attention_fwd(qkv, B, T, nh, out=y, head_dim=dh), flush=flush)
+        tr = time_fn(lambda: F.scaled_dot_product_attention(q, k, v, is_causal=True), flush=flush)
+        rows.append(dict(op="attention", name="fwd" + tag, ms=t, ref_ms=tr, tflops=fwd_flops / t / 1e9,
+                         ref_tflops=fwd_flops / tr / 1e9))
+        t = time_fn(lambda: K.attention_bwd(qkv, y, dy, lse, B, T, nh, head_dim=dh), flush=flush)
+        qg, kg, vg = (x.detach().requires_grad_(True) for x in (q, k, v))
+        o = F.scaled_dot_product_attention(qg, kg, vg, is_causal=True)
+        g = torch.randn_like(o)
+        # (autograd runs on its own threads and cannot be graph-captured; timed eagerly)
+        tr = time_fn(lambda: torch.autograd.grad(o, (qg, kg, vg), g, retain_graph=True), flush=flush, graph=False)
+        rows.append(dict(op="attention", name="bwd" + tag, ms=t, ref_ms=tr, tflops=2.5 * fwd_flops / t / 1e9,
+                         ref_tflops=2.5 * fwd_flops / tr / 1e9))
     check_status()
     return rows
 

@@ -141,13 +141,13 @@ def colsum_bf16(x, out):
 
 
 # ---- attention ------------------------------------------------------------------
-def _qkv(qkv, B, T, nh):
-    q, k, v = qkv.float().view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4).unbind(0)
+def _qkv(qkv, B, T, nh, dh=64):
+    q, k, v = qkv.float().view(B, T, 3, nh, dh).permute(2, 0, 3, 1, 4).unbind(0)
     return q, k, v
 
 
 def _attn(q, k, v, T, drop, B, nh):
-    s = (q @ k.transpose(-1, -2)) / 8.0
+    s = (q @ k.transpose(-1, -2)) / (q.shape[-1] ** 0.5)
     s = s.masked_fill(torch.ones(T, T, dtype=torch.bool).triu(1), float("-inf"))
     p = torch.softmax(s, -1)
     if drop is not None:
@@ -156,19 +156,19 @@ def _attn(q, k, v, T, drop, B, nh):
     return p @ v
 
 
-def attention_fwd(qkv, B, T, nh, out=None, drop=None):
-    q, k, v = _qkv(qkv, B, T, nh)
-    y = _attn(q, k, v, T, drop, B, nh).transpose(1, 2).reshape(B * T, nh * 64)
+def attention_fwd(qkv, B, T, nh, out=None, drop=None, head_dim=64):
+    q, k, v = _qkv(qkv, B, T, nh, head_dim)
+    y = _attn(q, k, v, T, drop, B, nh).transpose(1, 2).reshape(B * T, nh * head_dim)
     lse = torch.zeros(B, nh, (T + 127) // 128 * 128)
     return y.bfloat16(), lse
 
 
-def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv=None, drop=None):
-    q, k, v = (t.detach().requires_grad_(True) for t in _qkv(qkv, B, T, nh))
+def attention_bwd(qkv, out, dout, lse, B, T, nh, dqkv=None, drop=None, head_dim=64):
+    q, k, v = (t.detach().requires_grad_(True) for t in _qkv(qkv, B, T, nh, head_dim))
     with torch.enable_grad():
-        y = _attn(q, k, v, T, drop, B, nh).transpose(1, 2).reshape(B * T, nh * 64)
+        y = _attn(q, k, v, T, drop, B, nh).transpose(1, 2).reshape(B * T, nh * head_dim)
         dq, dk, dv = torch.autograd.grad(y, (q, k, v), dout.float())
-    d = torch.stack([dq, dk, dv]).permute(1, 3, 0, 2, 4).reshape(B * T, 3 * nh * 64)
+    d = torch.stack([dq, dk, dv]).permute(1, 3, 0, 2, 4).reshape(B * T, 3 * nh * head_dim)
     return d.bfloat16()
 
 
