@@ -60,7 +60,7 @@ __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 
 // uses three-input max over independent chains and is taken on raw scores
 // (the scale is positive); exponent arguments and row sums are computed on
 // fp32 pairs (one f32x2 instruction for two columns).
-template <bool DIAG, bool DROP>
+template <bool DIAG, bool DROP, bool F16>
 __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
                                               float scale_log2, float& m, float& l, uint32_t dkey, uint64_t pair_row,
                                               uint32_t dthresh, float dscale) {
@@ -115,7 +115,7 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
           p0 *= m0;
           p1 *= m1;
         }
-        pk[i >> 1] = pack_bf16(p0, p1);
+        pk[i >> 1] = pack16<F16>(p0, p1);
       }
 #pragma unroll
       for (int g = 0; g < 4; ++g)
@@ -147,7 +147,7 @@ __device__ __forceinline__ void accumulate_o(uint64_t (&o)[32], uint32_t tO, flo
   }
 }
 
-template <bool DROP>
+template <bool DROP, bool F16>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -226,8 +226,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idS = make_idesc_f16(128, 128, false, false, true);
-      constexpr uint32_t idO = make_idesc_f16(128, 64, false, true, true);
+      constexpr uint32_t idS = make_idesc_f16(128, 128, false, false, !F16);
+      constexpr uint32_t idO = make_idesc_f16(128, 64, false, true, !F16);
       bool ok = mbar_wait(&bar_q, 0, p.status, 21);
       HB_TRACE(1);
       auto item = [&](int idx, uint32_t& addr) -> bool {
@@ -323,9 +323,9 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         }
         if (lane == 0 && sub == 0 && j < 8) HB_TRACE(16 + 24 * g + j);
         const float alpha =
-            (j == my_qt) ? softmax_tile<true, DROP>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
+            (j == my_qt) ? softmax_tile<true, DROP, F16>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
                                                     pair_row, p.drop.thresh, p.drop.scale)
-                         : softmax_tile<false, DROP>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
+                         : softmax_tile<false, DROP, F16>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
                                                      pair_row, p.drop.thresh, p.drop.scale);
         fence_proxy_async_smem();
         tc_fence_before();
@@ -349,7 +349,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
           for (int i = 0; i < 32; ++i) {
             float a0, a1;
             f2_unpack(f2_mul(o[i], inv2), a0, a1);
-            w[i] = pack_bf16(a0, a1);
+            w[i] = pack16<F16>(a0, a1);
           }
           __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD;
 #pragma unroll
@@ -381,7 +381,7 @@ constexpr int BWD_DQ_STG = 8 * 4096;  // per softmax warp: 32 query rows x 32 fp
 constexpr int BWD_SMEM = 2 * kTileBytes /*K,V*/ + BWD_STAGES * BWD_STAGE + 4 * kTileBytes /*P^T, dS^T*/ +
                          BWD_DQ_STG + 1024;
 
-template <bool DROP>
+template <bool DROP, bool F16>
 __global__ void __launch_bounds__(BWD_THREADS, 1)
     attn_bwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, const __grid_constant__ CUtensorMap tm_do,
                     const __grid_constant__ CUtensorMap tm_dq, AttnParams p) {
@@ -451,9 +451,9 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idH = make_idesc_f16(128, 64, false, false, true);   // S^T / dP^T halves
-      constexpr uint32_t idKM = make_idesc_f16(128, 64, false, true, true);   // dV, dK
-      constexpr uint32_t idQ = make_idesc_f16(128, 64, true, true, true);     // dQ
+      constexpr uint32_t idH = make_idesc_f16(128, 64, false, false, !F16);   // S^T / dP^T halves
+      constexpr uint32_t idKM = make_idesc_f16(128, 64, false, true, !F16);   // dV, dK
+      constexpr uint32_t idQ = make_idesc_f16(128, 64, true, true, !F16);     // dQ
       const uint32_t ka = smem_u32(sK), va = smem_u32(sV), pa = smem_u32(sP), dsa = smem_u32(sDS);
       auto stage_ready = [&](int ii) -> bool {
         if (!mbar_wait(&bar_full[ii % BWD_STAGES], (ii / BWD_STAGES) & 1, p.status, 41)) return false;
@@ -619,8 +619,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
               if ((diag && key > qq) || qq >= p.T) p0 = d0 = 0.f;
               if ((diag && key > qq + 1) || qq + 1 >= p.T) p1 = d1 = 0.f;
             }
-            pp[i >> 1] = pack_bf16(p0, p1);
-            dd[i >> 1] = pack_bf16(d0, d1);
+            pp[i >> 1] = pack16<F16>(p0, p1);
+            dd[i >> 1] = pack16<F16>(d0, d1);
           }
         }
         // The previous tile's MMAs read P^T / dS^T smem and wrote dQ: wait once,
@@ -661,8 +661,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 #pragma unroll
           for (int q8 = 0; q8 < 4; ++q8)
             *reinterpret_cast<uint4*>(dst + q8 * 8) =
-                make_uint4(pack_bf16(v[q8 * 8 + 0], v[q8 * 8 + 1]), pack_bf16(v[q8 * 8 + 2], v[q8 * 8 + 3]),
-                           pack_bf16(v[q8 * 8 + 4], v[q8 * 8 + 5]), pack_bf16(v[q8 * 8 + 6], v[q8 * 8 + 7]));
+                make_uint4(pack16<F16>(v[q8 * 8 + 0], v[q8 * 8 + 1]), pack16<F16>(v[q8 * 8 + 2], v[q8 * 8 + 3]),
+                           pack16<F16>(v[q8 * 8 + 4], v[q8 * 8 + 5]), pack16<F16>(v[q8 * 8 + 6], v[q8 * 8 + 7]));
         }
       }
     }
@@ -679,7 +679,7 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
 }
 
 // dvec[b, h, t] = -scale * D,  D = sum_d dO[b*T+t, h*DH+d] * O[b*T+t, h*DH+d]   (fp32)
-template <int DH>
+template <int DH, bool F16>
 __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long ld_o, const __nv_bfloat16* __restrict__ dO,
                                      long ld_do, float* __restrict__ dvec, int B, int T, int nh, int Tpad,
                                      float scale) {
@@ -694,15 +694,15 @@ __global__ void attn_bwd_dvec_kernel(const __nv_bfloat16* __restrict__ o, long l
 #pragma unroll
   for (int k = 0; k < DH / 8; ++k) {
     const uint4 x = a[k], y = g[k];
-    const __nv_bfloat16* xe = reinterpret_cast<const __nv_bfloat16*>(&x);
-    const __nv_bfloat16* ye = reinterpret_cast<const __nv_bfloat16*>(&y);
+    const uint32_t xw[4] = {x.x, x.y, x.z, x.w}, yw[4] = {y.x, y.y, y.z, y.w};
 #pragma unroll
-    for (int q = 0; q < 8; ++q) s += __bfloat162float(xe[q]) * __bfloat162float(ye[q]);
+    for (int q = 0; q < 4; ++q) s += lo16<F16>(xw[q]) * lo16<F16>(yw[q]) + hi16<F16>(xw[q]) * hi16<F16>(yw[q]);
   }
   dvec[((long)b * nh + h) * Tpad + t] = -scale * s;
 }
 
-// dqkv[:, c] = bf16(dq_acc[:, c]) for the Q columns c < Hs
+// dqkv[:, c] = 16-bit(dq_acc[:, c]) for the Q columns c < Hs
+template <bool F16>
 __global__ void attn_bwd_dq_kernel(const float* __restrict__ dq_acc, __nv_bfloat16* __restrict__ dqkv, long ld,
                                    long rows, int Hs) {
   const long i = (long)blockIdx.x * blockDim.x + threadIdx.x;
@@ -712,29 +712,28 @@ __global__ void attn_bwd_dq_kernel(const float* __restrict__ dq_acc, __nv_bfloat
   const long row = e / Hs;
   const int c = e % Hs;
   const float4 v = reinterpret_cast<const float4*>(dq_acc)[i];
-  *reinterpret_cast<uint2*>(dqkv + row * ld + c) = make_uint2(pack_bf16(v.x, v.y), pack_bf16(v.z, v.w));
+  *reinterpret_cast<uint2*>(dqkv + row * ld + c) = make_uint2(pack16<F16>(v.x, v.y), pack16<F16>(v.z, v.w));
 }
 
 // Backward pre-pass of every head width: dvec = -scale * rowsum(dO * O) and a
 // zeroed fp32 dQ accumulator.
 void attn_bwd_prepass(const __nv_bfloat16* o, long ld_o, const __nv_bfloat16* dO, long ld_do, float* dvec,
-                      float* dq_acc, int B, int T, int nh, int dh, int Tpad, float scale, cudaStream_t s) {
+                      float* dq_acc, int B, int T, int nh, int dh, int Tpad, float scale, bool f16, cudaStream_t s) {
   const long rows = (long)B * T;
   const unsigned grid = static_cast<unsigned>((rows * nh + 255) / 256);
-  if (dh == 64) {
-    attn_bwd_dvec_kernel<64><<<grid, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, scale);
-  } else if (dh == 128) {
-    attn_bwd_dvec_kernel<128><<<grid, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, scale);
-  } else {
-    throw std::runtime_error("attention backward: head_dim must be 64 or 128 here");
-  }
+  auto kern = dh == 64 ? (f16 ? attn_bwd_dvec_kernel<64, true> : attn_bwd_dvec_kernel<64, false>)
+                       : (f16 ? attn_bwd_dvec_kernel<128, true> : attn_bwd_dvec_kernel<128, false>);
+  if (dh != 64 && dh != 128) throw std::runtime_error("attention backward: head_dim must be 64 or 128 here");
+  kern<<<grid, 256, 0, s>>>(o, ld_o, dO, ld_do, dvec, B, T, nh, Tpad, scale);
   HB_CUDA_CHECK(cudaGetLastError());
   HB_CUDA_CHECK(cudaMemsetAsync(dq_acc, 0, sizeof(float) * rows * nh * dh, s));
 }
 
 // dQ accumulator -> bf16 Q columns of dqkv.
-void attn_bwd_dq_finish(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, long rows, int Hs, cudaStream_t s) {
-  attn_bwd_dq_kernel<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
+void attn_bwd_dq_finish(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, long rows, int Hs, bool f16,
+                        cudaStream_t s) {
+  auto kern = f16 ? attn_bwd_dq_kernel<true> : attn_bwd_dq_kernel<false>;
+  kern<<<(rows * Hs / 4 + 255) / 256, 256, 0, s>>>(dq_acc, dqkv, ld_dqkv, rows, Hs);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -749,15 +748,21 @@ static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
   return attn_seq_map(base, B, T, ld, cols, 128);
 }
 
+// The four (dropout, 16-bit format) instantiations of a kernel template.
+#define HB_ATTN_PICK(kern, drop_on, f16)                                                     \
+  ((drop_on) ? ((f16) ? kern<true, true> : kern<true, false>)                                \
+             : ((f16) ? kern<false, true> : kern<false, false>))
+
 void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, long ld_out, float* lse, int B,
                      int T, int nh, int Tpad, float scale, const DropoutArgs& drop, int h0, int nh_total, int* status,
-                     cudaStream_t s) {
+                     bool f16, cudaStream_t s) {
   static bool attr[64] = {};  // the shared-memory opt-in is per device
   const int dev = current_device();
   if (!attr[dev]) {
-    HB_CUDA_CHECK(
-        cudaFuncSetAttribute(attn_fwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+    for (int d = 0; d < 2; ++d)
+      for (int h = 0; h < 2; ++h)
+        HB_CUDA_CHECK(cudaFuncSetAttribute(HB_ATTN_PICK(attn_fwd_kernel, d, h),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
     attr[dev] = true;
   }
   AttnParams p{};
@@ -772,29 +777,26 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
-  if (drop.thresh != 0) {
-    attn_fwd_kernel<true><<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
-  } else {
-    attn_fwd_kernel<false><<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
-  }
+  HB_ATTN_PICK(attn_fwd_kernel, drop.thresh != 0, f16)<<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16* o, long ld_o,
                      const __nv_bfloat16* dO, long ld_do, const float* lse, float* dvec, float* dq_acc,
                      __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, float scale,
-                     const DropoutArgs& drop, int h0, int nh_total, int* status, cudaStream_t s) {
+                     const DropoutArgs& drop, int h0, int nh_total, int* status, bool f16, cudaStream_t s) {
   static bool attr[64] = {};  // the shared-memory opt-in is per device
   const int dev = current_device();
   if (!attr[dev]) {
-    HB_CUDA_CHECK(
-        cudaFuncSetAttribute(attn_bwd_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
+    for (int d = 0; d < 2; ++d)
+      for (int h = 0; h < 2; ++h)
+        HB_CUDA_CHECK(cudaFuncSetAttribute(HB_ATTN_PICK(attn_bwd_kernel, d, h),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, BWD_SMEM));
     attr[dev] = true;
   }
   const int Hs = nh * kD;
   const long rows = (long)B * T;
-  attn_bwd_prepass(o, ld_o, dO, ld_do, dvec, dq_acc, B, T, nh, kD, Tpad, scale, s);
+  attn_bwd_prepass(o, ld_o, dO, ld_do, dvec, dq_acc, B, T, nh, kD, Tpad, scale, f16, s);
   AttnParams p{};
   p.B = B, p.T = T, p.nh = nh, p.Hs = Hs, p.out = dqkv, p.ld_out = ld_dqkv, p.lse = const_cast<float*>(lse);
   p.Tpad = Tpad, p.dvec = dvec, p.dq_acc = dq_acc;
@@ -814,13 +816,9 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   const CUtensorMap tdq =
       make_tmap(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
   const int n_t = (T + kTile - 1) / kTile;
-  if (drop.thresh != 0) {
-    attn_bwd_kernel<true><<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
-  } else {
-    attn_bwd_kernel<false><<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
-  }
+  HB_ATTN_PICK(attn_bwd_kernel, drop.thresh != 0, f16)<<<B * nh * n_t, BWD_THREADS, BWD_SMEM, s>>>(tq, td, tdq, p);
   HB_CUDA_CHECK(cudaGetLastError());
-  attn_bwd_dq_finish(dq_acc, dqkv, ld_dqkv, rows, Hs, s);
+  attn_bwd_dq_finish(dq_acc, dqkv, ld_dqkv, rows, Hs, f16, s);
 }
 
 // Trace buffer for the next attention launches (nullptr turns tracing off).

@@ -66,7 +66,7 @@ __device__ __forceinline__ int v_item(int j, int n) { return (j == n - 1) ? 2 * 
 // over columns [64g, 64g+64), written as bf16 into P's atom g. Updates the
 // running max m and this half's partial row sum l; returns the rescale factor
 // of the previous output accumulator.
-template <bool DIAG, bool DROP>
+template <bool DIAG, bool DROP, bool F16>
 __device__ __forceinline__ float softmax_half(uint32_t tS, uint32_t lane_off, uint8_t* sP, int g, int row, int key0,
                                               int q, float scale_log2, float& m, float& l, uint32_t dkey,
                                               uint64_t pair_row, uint32_t dthresh, float dscale) {
@@ -119,7 +119,7 @@ __device__ __forceinline__ float softmax_half(uint32_t tS, uint32_t lane_off, ui
         p0 *= m0;
         p1 *= m1;
       }
-      pk[i >> 1] = pack_bf16(p0, p1);
+      pk[i >> 1] = pack16<F16>(p0, p1);
     }
 #pragma unroll
     for (int q4 = 0; q4 < 4; ++q4)
@@ -158,7 +158,7 @@ __device__ __forceinline__ void named_bar_sync(int id, int threads) {
 // ============================================================================
 // Forward
 // ============================================================================
-template <bool DROP>
+template <bool DROP, bool F16>
 __global__ void __launch_bounds__(d128::THREADS, 1)
     attn_fwd_d128_kernel(const __grid_constant__ CUtensorMap tm_qkv, AttnParams p) {
   using namespace d128;
@@ -232,8 +232,8 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idS = make_idesc_f16(128, 128, false, false, true);
-      constexpr uint32_t idO = make_idesc_f16(128, 64, false, true, true);
+      constexpr uint32_t idS = make_idesc_f16(128, 128, false, false, !F16);
+      constexpr uint32_t idO = make_idesc_f16(128, 64, false, true, !F16);
       bool ok = mbar_wait(&bar_q, 0, p.status, 61);
       auto item = [&](int idx, uint32_t& addr) -> bool {
         const int slot = idx % FWD_SLOTS;
@@ -324,9 +324,9 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
       }
       const uint32_t tS = tmem + (j & 1) * 128;
       const float alpha =
-          (j == qt) ? softmax_half<true, DROP>(tS, lane_off, sP, g, row, j * kTile, q, p.scale_log2, m, l, dkey,
+          (j == qt) ? softmax_half<true, DROP, F16>(tS, lane_off, sP, g, row, j * kTile, q, p.scale_log2, m, l, dkey,
                                                pair_row, p.drop.thresh, p.drop.scale)
-                    : softmax_half<false, DROP>(tS, lane_off, sP, g, row, j * kTile, q, p.scale_log2, m, l, dkey,
+                    : softmax_half<false, DROP, F16>(tS, lane_off, sP, g, row, j * kTile, q, p.scale_log2, m, l, dkey,
                                                 pair_row, p.drop.thresh, p.drop.scale);
       fence_proxy_async_smem();
       tc_fence_before();
@@ -357,7 +357,7 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
       for (int i = 0; i < 32; ++i) {
         float a0, a1;
         f2_unpack(f2_mul(o[i], inv2), a0, a1);
-        w[i] = pack_bf16(a0, a1);
+        w[i] = pack16<F16>(a0, a1);
       }
       __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD + g * 64;
 #pragma unroll
@@ -389,7 +389,7 @@ constexpr int OFF_LD = OFF_DST + 2 * kSub;                   // [stage][lse 64 |
 constexpr int BWD_SMEM = OFF_LD + BWD_STAGES * 512 + 1024;
 }  // namespace d128
 
-template <bool DROP>
+template <bool DROP, bool F16>
 __global__ void __launch_bounds__(d128::THREADS, 1)
     attn_bwd_d128_kernel(const __grid_constant__ CUtensorMap tm_kv, const __grid_constant__ CUtensorMap tm_q,
                          const __grid_constant__ CUtensorMap tm_do, const __grid_constant__ CUtensorMap tm_dq,
@@ -463,9 +463,9 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idH = make_idesc_f16(128, 64, false, false, true);   // S^T, dP^T
-      constexpr uint32_t idKV = make_idesc_f16(128, 128, false, true, true);  // dV, dK
-      constexpr uint32_t idQ = make_idesc_f16(128, 64, true, true, true);     // dQ^T
+      constexpr uint32_t idH = make_idesc_f16(128, 64, false, false, !F16);   // S^T, dP^T
+      constexpr uint32_t idKV = make_idesc_f16(128, 128, false, true, !F16);  // dV, dK
+      constexpr uint32_t idQ = make_idesc_f16(128, 64, true, true, !F16);     // dQ^T
       const uint32_t ka = smem_u32(smem), va = smem_u32(smem + OFF_V);
       auto stage_ready = [&](int j) -> bool {
         if (!mbar_wait(&bar_full[j % BWD_STAGES], (j / BWD_STAGES) & 1, p.status, 71)) return false;
@@ -604,8 +604,8 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
               if (key > qq || qq >= p.T) p0 = d0 = 0.f;
               if (key > qq + 1 || qq + 1 >= p.T) p1 = d1 = 0.f;
             }
-            pp[i >> 1] = pack_bf16(p0, p1);
-            dd[i >> 1] = pack_bf16(d0, d1);
+            pp[i >> 1] = pack16<F16>(p0, p1);
+            dd[i >> 1] = pack16<F16>(d0, d1);
           }
         }
 #pragma unroll
@@ -664,8 +664,8 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
 #pragma unroll
             for (int q8 = 0; q8 < 4; ++q8)
               *reinterpret_cast<uint4*>(dst + q8 * 8) =
-                  make_uint4(pack_bf16(v[q8 * 8 + 0], v[q8 * 8 + 1]), pack_bf16(v[q8 * 8 + 2], v[q8 * 8 + 3]),
-                             pack_bf16(v[q8 * 8 + 4], v[q8 * 8 + 5]), pack_bf16(v[q8 * 8 + 6], v[q8 * 8 + 7]));
+                  make_uint4(pack16<F16>(v[q8 * 8 + 0], v[q8 * 8 + 1]), pack16<F16>(v[q8 * 8 + 2], v[q8 * 8 + 3]),
+                             pack16<F16>(v[q8 * 8 + 4], v[q8 * 8 + 5]), pack16<F16>(v[q8 * 8 + 6], v[q8 * 8 + 7]));
           }
         }
       }
@@ -685,8 +685,14 @@ __global__ void __launch_bounds__(d128::THREADS, 1)
 // Host side
 // ----------------------------------------------------------------------------
 void attn_bwd_prepass(const __nv_bfloat16* o, long ld_o, const __nv_bfloat16* dO, long ld_do, float* dvec,
-                      float* dq_acc, int B, int T, int nh, int dh, int Tpad, float scale, cudaStream_t s);
-void attn_bwd_dq_finish(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, long rows, int Hs, cudaStream_t s);
+                      float* dq_acc, int B, int T, int nh, int dh, int Tpad, float scale, bool f16, cudaStream_t s);
+void attn_bwd_dq_finish(const float* dq_acc, __nv_bfloat16* dqkv, long ld_dqkv, long rows, int Hs, bool f16,
+                        cudaStream_t s);
+
+// The four (dropout, 16-bit format) instantiations of a kernel template.
+#define HB_ATTN128_PICK(kern, drop_on, f16)                                                  \
+  ((drop_on) ? ((f16) ? kern<true, true> : kern<true, false>)                                \
+             : ((f16) ? kern<false, true> : kern<false, false>))
 
 static AttnParams d128_params(int B, int T, int nh, int Tpad, float scale, const DropoutArgs& drop, int h0,
                               int nh_total, int* status) {
@@ -704,44 +710,41 @@ static AttnParams d128_params(int B, int T, int nh, int Tpad, float scale, const
 
 void attn_fwd_d128_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, long ld_out, float* lse, int B,
                           int T, int nh, int Tpad, float scale, const DropoutArgs& drop, int h0, int nh_total,
-                          int* status, cudaStream_t s) {
+                          int* status, bool f16, cudaStream_t s) {
   static bool attr[64] = {};  // the shared-memory opt-in is per device
   const int dev = current_device();
   if (!attr[dev]) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_d128_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       d128::FWD_SMEM));
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_fwd_d128_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       d128::FWD_SMEM));
+    for (int d = 0; d < 2; ++d)
+      for (int h = 0; h < 2; ++h)
+        HB_CUDA_CHECK(cudaFuncSetAttribute(HB_ATTN128_PICK(attn_fwd_d128_kernel, d, h),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, d128::FWD_SMEM));
     attr[dev] = true;
   }
   AttnParams p = d128_params(B, T, nh, Tpad, scale, drop, h0, nh_total, status);
   p.out = out, p.ld_out = ld_out, p.lse = lse;
   const CUtensorMap tm = attn_seq_map(qkv, B, T, ld_qkv, 3 * p.Hs, 128);
   const int n_qt = (T + kTile - 1) / kTile;
-  if (drop.thresh != 0) {
-    attn_fwd_d128_kernel<true><<<B * nh * n_qt, d128::THREADS, d128::FWD_SMEM, s>>>(tm, p);
-  } else {
-    attn_fwd_d128_kernel<false><<<B * nh * n_qt, d128::THREADS, d128::FWD_SMEM, s>>>(tm, p);
-  }
+  HB_ATTN128_PICK(attn_fwd_d128_kernel, drop.thresh != 0, f16)<<<B * nh * n_qt, d128::THREADS, d128::FWD_SMEM, s>>>(
+      tm, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void attn_bwd_d128_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16* o, long ld_o,
                           const __nv_bfloat16* dO, long ld_do, const float* lse, float* dvec, float* dq_acc,
                           __nv_bfloat16* dqkv, long ld_dqkv, int B, int T, int nh, int Tpad, float scale,
-                          const DropoutArgs& drop, int h0, int nh_total, int* status, cudaStream_t s) {
+                          const DropoutArgs& drop, int h0, int nh_total, int* status, bool f16, cudaStream_t s) {
   static bool attr[64] = {};
   const int dev = current_device();
   if (!attr[dev]) {
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_d128_kernel<false>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       d128::BWD_SMEM));
-    HB_CUDA_CHECK(cudaFuncSetAttribute(attn_bwd_d128_kernel<true>, cudaFuncAttributeMaxDynamicSharedMemorySize,
-                                       d128::BWD_SMEM));
+    for (int d = 0; d < 2; ++d)
+      for (int h = 0; h < 2; ++h)
+        HB_CUDA_CHECK(cudaFuncSetAttribute(HB_ATTN128_PICK(attn_bwd_d128_kernel, d, h),
+                                           cudaFuncAttributeMaxDynamicSharedMemorySize, d128::BWD_SMEM));
     attr[dev] = true;
   }
   const int Hs = nh * d128::kD;
   const long rows = (long)B * T;
-  attn_bwd_prepass(o, ld_o, dO, ld_do, dvec, dq_acc, B, T, nh, d128::kD, Tpad, scale, s);
+  attn_bwd_prepass(o, ld_o, dO, ld_do, dvec, dq_acc, B, T, nh, d128::kD, Tpad, scale, f16, s);
   AttnParams p = d128_params(B, T, nh, Tpad, scale, drop, h0, nh_total, status);
   p.out = dqkv, p.ld_out = ld_dqkv, p.lse = const_cast<float*>(lse), p.dvec = dvec, p.dq_acc = dq_acc;
   const CUtensorMap tkv = attn_seq_map(qkv, B, T, ld_qkv, 3 * Hs, 128);
@@ -754,13 +757,10 @@ void attn_bwd_d128_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bflo
   const CUtensorMap tdq =
       make_tmap(CU_TENSOR_MAP_DATA_TYPE_FLOAT32, 3, dq_acc, qdims, qstr, qbox, CU_TENSOR_MAP_SWIZZLE_128B);
   const int n_t = (T + kTile - 1) / kTile;
-  if (drop.thresh != 0) {
-    attn_bwd_d128_kernel<true><<<B * nh * n_t, d128::THREADS, d128::BWD_SMEM, s>>>(tkv, tq, td, tdq, p);
-  } else {
-    attn_bwd_d128_kernel<false><<<B * nh * n_t, d128::THREADS, d128::BWD_SMEM, s>>>(tkv, tq, td, tdq, p);
-  }
+  HB_ATTN128_PICK(attn_bwd_d128_kernel, drop.thresh != 0, f16)<<<B * nh * n_t, d128::THREADS, d128::BWD_SMEM, s>>>(
+      tkv, tq, td, tdq, p);
   HB_CUDA_CHECK(cudaGetLastError());
-  attn_bwd_dq_finish(dq_acc, dqkv, ld_dqkv, rows, Hs, s);
+  attn_bwd_dq_finish(dq_acc, dqkv, ld_dqkv, rows, Hs, f16, s);
 }
 
 // ----------------------------------------------------------------------------

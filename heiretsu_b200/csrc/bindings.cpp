@@ -30,7 +30,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("embedding_bwd", &hb::embedding_bwd);
   m.def("sumsq_scratch_size", &hb::sumsq_scratch_size);
   m.def("sumsq", &hb::sumsq);
-  m.def("clip_coef", &hb::clip_coef);
+  m.def("clip_coef", &hb::clip_coef, py::arg("norm2"), py::arg("max_norm"), py::arg("coef"), py::arg("norm") = py::none(),
+        py::arg("loss_scale") = py::none());
+  m.def("loss_scale_update", &hb::loss_scale_update);
   m.def("adamw_step", &hb::adamw_step);
   m.def("f32_to_bf16", &hb::f32_to_bf16);
   m.def("attention_set_trace", &hb::attention_set_trace);

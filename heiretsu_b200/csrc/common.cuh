@@ -412,6 +412,54 @@ __device__ __forceinline__ uint32_t pack_bf16(float a, float b) {
   __nv_bfloat162 v = __floats2bfloat162_rn(a, b);
   return *reinterpret_cast<uint32_t*>(&v);
 }
+__device__ __forceinline__ uint32_t pack_f16(float a, float b) {
+  __half2 v = __floats2half2_rn(a, b);
+  return *reinterpret_cast<uint32_t*>(&v);
+}
+
+// 16-bit storage formats. Activations and weight shadows are bf16 under
+// --amp bf16 and fp16 under --amp fp16; kernels take the format as a template
+// argument (F16) or, where one compiled kernel serves both, as a flag.
+template <bool F16>
+__device__ __forceinline__ uint32_t pack16(float a, float b) {
+  return F16 ? pack_f16(a, b) : pack_bf16(a, b);
+}
+__device__ __forceinline__ uint32_t pack16(float a, float b, bool f16) {
+  return f16 ? pack_f16(a, b) : pack_bf16(a, b);
+}
+// Low / high element of a packed pair as fp32.
+template <bool F16>
+__device__ __forceinline__ float lo16(uint32_t w) {
+  if constexpr (F16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w & 0xFFFFu)));
+  } else {
+    return __uint_as_float(w << 16);
+  }
+}
+template <bool F16>
+__device__ __forceinline__ float hi16(uint32_t w) {
+  if constexpr (F16) {
+    return __half2float(__ushort_as_half(static_cast<unsigned short>(w >> 16)));
+  } else {
+    return __uint_as_float(w & 0xFFFF0000u);
+  }
+}
+template <bool F16>
+__device__ __forceinline__ float to_f32(uint16_t v) {
+  if constexpr (F16) {
+    return __half2float(__ushort_as_half(v));
+  } else {
+    return __uint_as_float(static_cast<uint32_t>(v) << 16);
+  }
+}
+template <bool F16>
+__device__ __forceinline__ uint16_t from_f32(float x) {
+  if constexpr (F16) {
+    return __half_as_ushort(__float2half_rn(x));
+  } else {
+    return __bfloat16_as_ushort(__float2bfloat16_rn(x));
+  }
+}
 
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll

@@ -127,16 +127,46 @@ void sumsq_launch(const float* x, long n, float* part, int nparts, float weight,
 
 // coef[0] = min(1, max_norm / (sqrt(norm2) + 1e-6)) (torch clip_grad_norm_ semantics);
 // with a non-finite norm the step is skipped by AdamW (coef = NaN sentinel).
-__global__ void clip_coef_kernel(const float* norm2, float max_norm, float* coef, float* norm_out) {
-  const float nrm = sqrtf(norm2[0]);
+// With a loss scale S (fp16, `lscale` != nullptr) the gradients hold S * g:
+// the norm is unscaled first (the order of GradScaler.unscale_ then
+// clip_grad_norm_), and 1/S is folded into the coefficient AdamW applies.
+__global__ void clip_coef_kernel(const float* norm2, float max_norm, float* coef, float* norm_out,
+                                 const float* lscale) {
+  const float inv_s = lscale ? 1.f / lscale[0] : 1.f;
+  const float nrm = sqrtf(norm2[0]) * inv_s;
   if (norm_out) norm_out[0] = nrm;
   float c = 1.f;
   if (max_norm > 0.f) c = fminf(1.f, max_norm / (nrm + 1e-6f));
-  coef[0] = isfinite(nrm) ? c : NAN;
+  coef[0] = isfinite(nrm) ? c * inv_s : NAN;
 }
 
-void clip_coef_launch(const float* norm2, float max_norm, float* coef, float* norm_out, cudaStream_t s) {
-  clip_coef_kernel<<<1, 1, 0, s>>>(norm2, max_norm, coef, norm_out);
+void clip_coef_launch(const float* norm2, float max_norm, float* coef, float* norm_out, const float* lscale,
+                      cudaStream_t s) {
+  clip_coef_kernel<<<1, 1, 0, s>>>(norm2, max_norm, coef, norm_out, lscale);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+// Dynamic loss scale (fp16), torch.cuda.amp.GradScaler's rule kept on the
+// device: state = {scale, steps since the last non-finite step}. After a
+// skipped step (coef NaN) the scale is multiplied by `backoff` and the count
+// restarts; after `interval` finite steps in a row it is multiplied by `growth`.
+__global__ void loss_scale_update_kernel(const float* coef, float* state, float growth, float backoff,
+                                         int interval) {
+  if (isnan(coef[0])) {
+    state[0] *= backoff;
+    state[1] = 0.f;
+  } else {
+    state[1] += 1.f;
+    if (state[1] >= static_cast<float>(interval)) {
+      state[0] *= growth;
+      state[1] = 0.f;
+    }
+  }
+}
+
+void loss_scale_update_launch(const float* coef, float* state, float growth, float backoff, int interval,
+                              cudaStream_t s) {
+  loss_scale_update_kernel<<<1, 1, 0, s>>>(coef, state, growth, backoff, interval);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -153,6 +183,7 @@ struct AdamHyper {
   float lr, beta1, beta2, eps, wd, bc1, bc2_sqrt, gscale;
 };
 
+template <bool F16>
 __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const float* __restrict__ g,
                                                     float* __restrict__ m, float* __restrict__ v,
                                                     __nv_bfloat16* __restrict__ p16, long n,
@@ -185,7 +216,7 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
     reinterpret_cast<float4*>(m)[i] = mm;
     reinterpret_cast<float4*>(v)[i] = vv;
     if (p16) {
-      reinterpret_cast<uint2*>(p16)[i] = make_uint2(pack_bf16(pp.x, pp.y), pack_bf16(pp.z, pp.w));
+      reinterpret_cast<uint2*>(p16)[i] = make_uint2(pack16<F16>(pp.x, pp.y), pack16<F16>(pp.z, pp.w));
     }
   }
   for (long i = n4 * 4 + (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x) {
@@ -193,27 +224,29 @@ __global__ void __launch_bounds__(256) adamw_kernel(float* __restrict__ p, const
     m[i] = h.beta1 * m[i] + (1.f - h.beta1) * gq;
     v[i] = h.beta2 * v[i] + (1.f - h.beta2) * gq * gq;
     p[i] = p[i] * decay - step * m[i] / (sqrtf(v[i]) / h.bc2_sqrt + h.eps);
-    if (p16) p16[i] = __float2bfloat16_rn(p[i]);
+    if (p16) reinterpret_cast<uint16_t*>(p16)[i] = from_f32<F16>(p[i]);
   }
 }
 
 void adamw_launch(float* p, const float* g, float* m, float* v, __nv_bfloat16* p16, long n, const void* hyper,
-                  const float* coef, cudaStream_t s) {
+                  const float* coef, bool f16, cudaStream_t s) {
   if (n == 0) return;
   const int grid = 4 * num_sms(current_device());
-  adamw_kernel<<<grid, 256, 0, s>>>(p, g, m, v, p16, n, reinterpret_cast<const AdamHyper*>(hyper), coef);
+  (f16 ? adamw_kernel<true> : adamw_kernel<false>)<<<grid, 256, 0, s>>>(
+      p, g, m, v, p16, n, reinterpret_cast<const AdamHyper*>(hyper), coef);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-// Plain fp32 -> bf16 copy (refresh of the GEMM weight shadow after a load).
+// Plain fp32 -> 16-bit copy (refresh of the GEMM weight shadow after a load).
+template <bool F16>
 __global__ void f32_to_bf16_kernel(const float* __restrict__ x, __nv_bfloat16* __restrict__ y, long n) {
   for (long i = (long)blockIdx.x * blockDim.x + threadIdx.x; i < n; i += (long)gridDim.x * blockDim.x)
-    y[i] = __float2bfloat16_rn(x[i]);
+    reinterpret_cast<uint16_t*>(y)[i] = from_f32<F16>(x[i]);
 }
 
-void f32_to_bf16_launch(const float* x, __nv_bfloat16* y, long n, cudaStream_t s) {
+void f32_to_bf16_launch(const float* x, __nv_bfloat16* y, long n, bool f16, cudaStream_t s) {
   if (n == 0) return;
-  f32_to_bf16_kernel<<<4 * num_sms(current_device()), 256, 0, s>>>(x, y, n);
+  (f16 ? f32_to_bf16_kernel<true> : f32_to_bf16_kernel<false>)<<<4 * num_sms(current_device()), 256, 0, s>>>(x, y, n);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

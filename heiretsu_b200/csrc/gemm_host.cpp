@@ -42,6 +42,7 @@ static bool tma_epilogue_enabled() {
   return on;
 }
 
+// (The map's element type is bf16 for either 16-bit format: loads copy bits.)
 static CUtensorMap operand_map(const at::Tensor& t, int box_rows) {
   return make_tmap_2d_bf16(t.data_ptr(), t.size(1), t.size(0), t.stride(0) * 2, 64, box_rows);
 }
@@ -54,7 +55,10 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off,
           const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: tensors must be on CUDA");
-  TORCH_CHECK(a.scalar_type() == at::kBFloat16 && b.scalar_type() == at::kBFloat16, "gemm: operands must be bf16");
+  const bool f16 = a.scalar_type() == at::kHalf;
+  TORCH_CHECK((a.scalar_type() == at::kBFloat16 || f16) && b.scalar_type() == a.scalar_type(),
+              "gemm: operands must be both bf16 or both fp16");
+  const at::ScalarType t16 = a.scalar_type();
   TORCH_CHECK(a.dim() == 2 && b.dim() == 2 && c.dim() == 2, "gemm: 2-D tensors expected");
   TORCH_CHECK(a.stride(1) == 1 && b.stride(1) == 1 && c.stride(1) == 1, "gemm: inner dim must be contiguous");
   TORCH_CHECK(a.stride(0) % 8 == 0 && b.stride(0) % 8 == 0, "gemm: row strides must be multiples of 16 bytes");
@@ -68,7 +72,8 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   TORCH_CHECK(grp_mode == 1 || (b_mn ? b.size(1) : b.size(0)) <= N, "gemm: B has more rows than N");
   TORCH_CHECK(c.size(0) >= M && c.size(1) >= N, "gemm: output too small");
   const bool out_bf16 = (epi == kEpiBf16 || epi == kEpiBf16Gelu || epi == kEpiBf16Dgelu);
-  TORCH_CHECK(c.scalar_type() == (out_bf16 ? at::kBFloat16 : at::kFloat), "gemm: wrong output dtype for epilogue");
+  TORCH_CHECK(c.scalar_type() == (out_bf16 ? t16 : at::kFloat),
+              "gemm: wrong output dtype for epilogue (16-bit outputs take the operands' format)");
   if (M == 0 || N == 0) return;
   if (K == 0) TORCH_CHECK(false, "gemm: K == 0 not supported");
   const int BN = (block_n == 256) ? 256 : (block_n == 192 ? 192 : 128);
@@ -80,15 +85,16 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   p.C = c.data_ptr();
   p.ldc = c.stride(0);
   p.status = device_status_ptr(a.get_device());
+  p.f16 = f16 ? 1 : 0;
   if (bias && bias->defined()) {
     TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() >= N && N % 4 == 0,
                 "gemm: bias must be fp32 contiguous with >= N elements");
     p.bias = bias->data_ptr<float>();
   }
   if (epi == kEpiBf16Gelu || epi == kEpiBf16Dgelu) {
-    TORCH_CHECK(aux && aux->defined() && aux->scalar_type() == at::kBFloat16 && aux->stride(1) == 1 &&
+    TORCH_CHECK(aux && aux->defined() && aux->scalar_type() == t16 && aux->stride(1) == 1 &&
                     aux->stride(0) % 8 == 0,
-                "gemm: bf16 aux tensor required");
+                "gemm: 16-bit aux tensor (the operands' format) required");
     p.aux = aux->data_ptr();
     p.ldaux = aux->stride(0);
   }
@@ -215,12 +221,13 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
       const uint64_t cdims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(c_rows)};
       const uint64_t cstr[1] = {static_cast<uint64_t>(c.stride(0) * esz)};
       const uint32_t box[2] = {32, 32};
-      tc = make_tmap(c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, c.data_ptr(),
-                     cdims, cstr, box, c_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
+      const CUtensorMapDataType t16map = f16 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT16 : CU_TENSOR_MAP_DATA_TYPE_BFLOAT16;
+      tc = make_tmap(c_f32 ? CU_TENSOR_MAP_DATA_TYPE_FLOAT32 : t16map, 2, c.data_ptr(), cdims, cstr, box,
+                     c_f32 ? CU_TENSOR_MAP_SWIZZLE_128B : CU_TENSOR_MAP_SWIZZLE_64B);
       if (epi == kEpiBf16Gelu) {
         const uint64_t xdims[2] = {static_cast<uint64_t>(N), static_cast<uint64_t>(M)};
         const uint64_t xstr[1] = {static_cast<uint64_t>(p.ldaux * 2)};
-        tx = make_tmap(CU_TENSOR_MAP_DATA_TYPE_BFLOAT16, 2, p.aux, xdims, xstr, box, CU_TENSOR_MAP_SWIZZLE_64B);
+        tx = make_tmap(t16map, 2, p.aux, xdims, xstr, box, CU_TENSOR_MAP_SWIZZLE_64B);
       }
       p.tma_epi = 1;
     }

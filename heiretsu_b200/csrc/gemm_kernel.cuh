@@ -133,12 +133,40 @@ __device__ __forceinline__ void stg_atomic_add(const uint8_t* stg, float* dst, l
 }
 
 // Row-per-thread write of 32 values into this thread's staging row.
-__device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float (&v)[32]) {
+template <bool F16>
+__device__ __forceinline__ void stg_put16(uint8_t* stg, int lane, const float (&v)[32]) {
 #pragma unroll
   for (int g = 0; g < 4; ++g)
     *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
-        make_uint4(pack_bf16(v[8 * g], v[8 * g + 1]), pack_bf16(v[8 * g + 2], v[8 * g + 3]),
-                   pack_bf16(v[8 * g + 4], v[8 * g + 5]), pack_bf16(v[8 * g + 6], v[8 * g + 7]));
+        make_uint4(pack16<F16>(v[8 * g], v[8 * g + 1]), pack16<F16>(v[8 * g + 2], v[8 * g + 3]),
+                   pack16<F16>(v[8 * g + 4], v[8 * g + 5]), pack16<F16>(v[8 * g + 6], v[8 * g + 7]));
+}
+__device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float (&v)[32], bool f16) {
+  if (f16) {
+    stg_put16<true>(stg, lane, v);
+  } else {
+    stg_put16<false>(stg, lane, v);
+  }
+}
+
+// GELU epilogue core: pk <- the 16-bit pre-activation pairs; v <- GELU of those
+// rounded values (so backward differentiates exactly what forward applied).
+template <bool F16>
+__device__ __forceinline__ void gelu_chunk16(float (&v)[32], uint32_t (&pk)[16]) {
+#pragma unroll
+  for (int j = 0; j < 16; ++j) pk[j] = pack16<F16>(v[2 * j], v[2 * j + 1]);
+#pragma unroll
+  for (int j = 0; j < 16; ++j) {
+    v[2 * j] = gelu_tanh(lo16<F16>(pk[j]));
+    v[2 * j + 1] = gelu_tanh(hi16<F16>(pk[j]));
+  }
+}
+__device__ __forceinline__ void gelu_chunk(float (&v)[32], uint32_t (&pk)[16], bool f16) {
+  if (f16) {
+    gelu_chunk16<true>(v, pk);
+  } else {
+    gelu_chunk16<false>(v, pk);
+  }
 }
 __device__ __forceinline__ void stg_put_f32(uint8_t* stg, int lane, const float (&v)[32]) {
 #pragma unroll
@@ -167,7 +195,8 @@ __device__ __forceinline__ void epi_prefetch(const GemmParams& p, const void* C,
 
 // Step 1: combine the prefetched operand with the accumulator row (frees `pre`).
 template <int EPI>
-__device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, const uint4 (&pre)[8], int lane) {
+__device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, const uint4 (&pre)[8], int lane,
+                                                  bool f16) {
   if constexpr (EPI == kEpiF32Resid || EPI == kEpiF32Acc) {
     stg_fill<true>(stg, pre, lane);
     __syncwarp();
@@ -187,9 +216,20 @@ __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, 
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const uint4 raw = *reinterpret_cast<const uint4*>(stg + stg_off<false>(lane, g));
-      const __nv_bfloat16* pb = reinterpret_cast<const __nv_bfloat16*>(&raw);
+      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+      if (f16) {
 #pragma unroll
-      for (int q = 0; q < 8; ++q) v[8 * g + q] *= gelu_tanh_grad(__bfloat162float(pb[q]));
+        for (int q = 0; q < 4; ++q) {
+          v[8 * g + 2 * q] *= gelu_tanh_grad(lo16<true>(w[q]));
+          v[8 * g + 2 * q + 1] *= gelu_tanh_grad(hi16<true>(w[q]));
+        }
+      } else {
+#pragma unroll
+        for (int q = 0; q < 4; ++q) {
+          v[8 * g + 2 * q] *= gelu_tanh_grad(lo16<false>(w[q]));
+          v[8 * g + 2 * q + 1] *= gelu_tanh_grad(hi16<false>(w[q]));
+        }
+      }
     }
     __syncwarp();
   }
@@ -238,11 +278,10 @@ __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_b
     }
   }
   if constexpr (EPI == kEpiBf16Gelu) {
-    // Pre-activation (rounded to bf16) goes to AUX; GELU of that rounded value
-    // goes to C, so backward differentiates exactly what forward applied.
+    // Pre-activation (rounded to the 16-bit format) goes to AUX; GELU of that
+    // rounded value goes to C, so backward differentiates exactly what forward applied.
     uint32_t pk[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+    gelu_chunk(v, pk, p.f16 != 0);
 #pragma unroll
     for (int g = 0; g < 4; ++g)
       *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
@@ -250,14 +289,9 @@ __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_b
     __syncwarp();
     stg_store<false>(stg, p.aux, p.ldaux, m_base, n0, p.M, p.N, lane);
     __syncwarp();
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {  // unpack the rounded values (bit moves, no conversion)
-      v[2 * j] = gelu_tanh(__uint_as_float(pk[j] << 16));
-      v[2 * j + 1] = gelu_tanh(__uint_as_float(pk[j] & 0xffff0000u));
-    }
   }
   if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiBf16Dgelu) {
-    stg_put_bf16(stg, lane, v);
+    stg_put_bf16(stg, lane, v, p.f16 != 0);
     __syncwarp();
     stg_store<false>(stg, C, p.ldc, m_base, n0, p.M, p.N, lane);
   } else if constexpr (EPI == kEpiF32Atomic) {
@@ -293,21 +327,15 @@ __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtens
     }
   }
   if constexpr (EPI == kEpiBf16Gelu) {
-    // pre-activation (bf16) -> first 2 KB of the staging tile; GELU of the
+    // pre-activation (16-bit) -> first 2 KB of the staging tile; GELU of the
     // rounded value -> second 2 KB; two stores.
     uint32_t pk[16];
-#pragma unroll
-    for (int j = 0; j < 16; ++j) pk[j] = pack_bf16(v[2 * j], v[2 * j + 1]);
+    gelu_chunk(v, pk, p.f16 != 0);
 #pragma unroll
     for (int g = 0; g < 4; ++g)
       *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
           make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-#pragma unroll
-    for (int j = 0; j < 16; ++j) {
-      v[2 * j] = gelu_tanh(__uint_as_float(pk[j] << 16));
-      v[2 * j + 1] = gelu_tanh(__uint_as_float(pk[j] & 0xffff0000u));
-    }
-    stg_put_bf16(stg + 2048, lane, v);
+    stg_put_bf16(stg + 2048, lane, v, p.f16 != 0);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
@@ -316,7 +344,7 @@ __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtens
       bulk_commit_group();
     }
   } else if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Dgelu) {
-    stg_put_bf16(stg, lane, v);
+    stg_put_bf16(stg, lane, v, p.f16 != 0);
     fence_proxy_async_smem();
     __syncwarp();
     if (lane == 0) {
@@ -527,7 +555,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
     }
   } else if (warp == 1) {
     if (elect_one()) {
-      constexpr uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN, true);
+      const uint32_t idesc = make_idesc_f16(BM, BN, A_MN, B_MN, p.f16 == 0);
       int stage = 0;
       uint32_t phase = 0;
       int local = 0;
@@ -620,7 +648,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               bias_done = true;
             }
           }
-          if (reads) epi_apply_operand<EPI>(v, stg, pre, lane);
+          if (reads) epi_apply_operand<EPI>(v, stg, pre, lane, p.f16 != 0);
           if (reads && c + 1 < CH && n0 + 32 < p.N) epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
           if (tma) {
             epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane, bias_done);

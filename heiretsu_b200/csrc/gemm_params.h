@@ -6,6 +6,7 @@
 namespace hb {
 
 enum GemmEpi : int {
+  // "Bf16" epilogues write the 16-bit format of the operands (bf16 or fp16, GemmParams::f16).
   kEpiBf16 = 0,       // C bf16 = acc (+ bias)
   kEpiBf16Gelu = 1,   // AUX bf16 = acc + bias ; C bf16 = gelu(acc + bias)
   kEpiF32 = 2,        // C f32 = acc (+ bias)
@@ -68,6 +69,9 @@ struct GemmParams {
   // accumulating epilogues) through the C / AUX tensor maps. 0 = per-lane
   // global stores (always the case for reduce-scatter peer outputs).
   int tma_epi;
+
+  // 16-bit format of A, B and of the 16-bit outputs / AUX: 0 bf16, 1 fp16.
+  int f16;
 
   // Residual dropout of the F32Resid epilogue (thresh 0 = off):
   // C = R + mask * (acc + bias), mask element (drop.row0 + row) * N + col.

@@ -50,6 +50,7 @@ __device__ __forceinline__ float block_reduce_sum(float v, float* sh) {
 constexpr int CE_THREADS = 512;
 
 // One CTA per row. Online (max, sum-exp) per thread over 8-element chunks.
+template <bool F16>
 __global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16* __restrict__ logits, long ld, int V,
                                                             const int64_t* __restrict__ targets, int ignore_index,
                                                             float* __restrict__ lse_out,
@@ -61,12 +62,12 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16*
   const int nchunk = V >> 3;  // full 8-wide chunks
   for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
     const uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&raw);
     float v[8];
     float cm = -INFINITY;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      v[q] = __bfloat162float(e[q]);
+      v[q] = to_f32<F16>(e[q]);
       cm = fmaxf(cm, v[q]);
     }
     const float nm = fmaxf(m, cm);
@@ -77,7 +78,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16*
     s = acc;
   }
   for (int j = nchunk * 8 + threadIdx.x; j < V; j += CE_THREADS) {
-    const float v = __bfloat162float(lr[j]);
+    const float v = to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[j]);
     const float nm = fmaxf(m, v);
     s = s * __expf(m - nm) + __expf(v - nm);
     m = nm;
@@ -88,11 +89,12 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16*
     const float lse = gm + __logf(gs);
     lse_out[row] = lse;
     const int64_t t = targets[row];
-    loss_rows[row] = (t == ignore_index) ? 0.f : lse - __bfloat162float(lr[t]);
+    loss_rows[row] = (t == ignore_index) ? 0.f : lse - to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[t]);
   }
 }
 
 // In-place gradient: l_j <- (exp(l_j - lse) - [j == t]) * scale; j in [V, Vp) -> 0.
+template <bool F16>
 __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __restrict__ logits, long ld, int V,
                                                             int Vp, const int64_t* __restrict__ targets,
                                                             int ignore_index, const float* __restrict__ lse_in,
@@ -105,15 +107,15 @@ __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __res
   const int nchunk = Vp >> 3;
   for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
     uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&raw);
     float g[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int j = c * 8 + q;
-      g[q] = (j < V) ? (__expf(__bfloat162float(e[q]) - lse) - (j == t ? 1.f : 0.f)) * scale : 0.f;
+      g[q] = (j < V) ? (__expf(to_f32<F16>(e[q]) - lse) - (j == t ? 1.f : 0.f)) * scale : 0.f;
     }
     *reinterpret_cast<uint4*>(lr + c * 8) =
-        make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+        make_uint4(pack16<F16>(g[0], g[1]), pack16<F16>(g[2], g[3]), pack16<F16>(g[4], g[5]), pack16<F16>(g[6], g[7]));
   }
 }
 
@@ -126,6 +128,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __res
 // the launch (the expected upstream gradient over the number of counted rows);
 // ce_rescale_kernel corrects it in backward when the actual upstream gradient
 // differs. The target logit is read before the row is overwritten.
+template <bool F16>
 __global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __restrict__ logits, long ld, int V,
                                                               int Vp, const int64_t* __restrict__ targets,
                                                               int ignore_index, float* __restrict__ lse_out,
@@ -136,17 +139,17 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __r
   __nv_bfloat16* lr = logits + row * ld;
   const int64_t t = targets[row];
   const bool counted = (t != ignore_index);
-  const float target_logit = (threadIdx.x == 0 && counted) ? __bfloat162float(lr[t]) : 0.f;
+  const float target_logit = (threadIdx.x == 0 && counted) ? to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[t]) : 0.f;
   float m = -INFINITY, s = 0.f;
   const int nchunk = V >> 3;
   for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
     const uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&raw);
     float v[8];
     float cm = -INFINITY;
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
-      v[q] = __bfloat162float(e[q]);
+      v[q] = to_f32<F16>(e[q]);
       cm = fmaxf(cm, v[q]);
     }
     const float nm = fmaxf(m, cm);
@@ -157,7 +160,7 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __r
     s = acc;
   }
   for (int j = nchunk * 8 + threadIdx.x; j < V; j += CE_THREADS) {
-    const float v = __bfloat162float(lr[j]);
+    const float v = to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[j]);
     const float nm = fmaxf(m, v);
     s = s * __expf(m - nm) + __expf(v - nm);
     m = nm;
@@ -175,20 +178,21 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __r
   const int nchunk_p = Vp >> 3;
   for (int c = threadIdx.x; c < nchunk_p; c += CE_THREADS) {
     uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
-    const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const uint16_t* e = reinterpret_cast<const uint16_t*>(&raw);
     float g[8];
 #pragma unroll
     for (int q = 0; q < 8; ++q) {
       const int j = c * 8 + q;
-      g[q] = (j < V) ? (__expf(__bfloat162float(e[q]) - lse) - (j == t ? 1.f : 0.f)) * scale : 0.f;
+      g[q] = (j < V) ? (__expf(to_f32<F16>(e[q]) - lse) - (j == t ? 1.f : 0.f)) * scale : 0.f;
     }
     *reinterpret_cast<uint4*>(lr + c * 8) =
-        make_uint4(pack_bf16(g[0], g[1]), pack_bf16(g[2], g[3]), pack_bf16(g[4], g[5]), pack_bf16(g[6], g[7]));
+        make_uint4(pack16<F16>(g[0], g[1]), pack16<F16>(g[2], g[3]), pack16<F16>(g[4], g[5]), pack16<F16>(g[6], g[7]));
   }
 }
 
 // g *= actual / expected over [M, Vp] bf16 (row stride ld); every CTA returns at
 // once when the two device scalars are equal (the usual case).
+template <bool F16>
 __global__ void __launch_bounds__(256) ce_rescale_kernel(__nv_bfloat16* __restrict__ g, long ld, int M, int Vp,
                                                          const float* __restrict__ actual,
                                                          const float* __restrict__ expected) {
@@ -201,11 +205,11 @@ __global__ void __launch_bounds__(256) ce_rescale_kernel(__nv_bfloat16* __restri
     const long row = i / per_row, c = i % per_row;
     uint4* ptr = reinterpret_cast<uint4*>(g + row * ld + c * 8);
     uint4 raw = *ptr;
-    const __nv_bfloat16* x = reinterpret_cast<const __nv_bfloat16*>(&raw);
+    const uint16_t* x = reinterpret_cast<const uint16_t*>(&raw);
     float v[8];
 #pragma unroll
-    for (int q = 0; q < 8; ++q) v[q] = __bfloat162float(x[q]) * r;
-    *ptr = make_uint4(pack_bf16(v[0], v[1]), pack_bf16(v[2], v[3]), pack_bf16(v[4], v[5]), pack_bf16(v[6], v[7]));
+    for (int q = 0; q < 8; ++q) v[q] = to_f32<F16>(x[q]) * r;
+    *ptr = make_uint4(pack16<F16>(v[0], v[1]), pack16<F16>(v[2], v[3]), pack16<F16>(v[4], v[5]), pack16<F16>(v[6], v[7]));
   }
 }
 
@@ -229,40 +233,45 @@ __global__ void __launch_bounds__(1024) mean_loss_kernel(const float* __restrict
 }
 
 void ce_fwd_launch(const __nv_bfloat16* logits, long ld, int M, int V, const int64_t* targets, int ignore_index,
-                   float* lse, float* loss_rows, float* loss_mean, float* count, cudaStream_t s) {
+                   float* lse, float* loss_rows, float* loss_mean, float* count, bool f16, cudaStream_t s) {
   if (ld % 8 != 0) throw std::runtime_error("cross_entropy: logits row stride must be a multiple of 8");
   if (M == 0) return;
-  ce_fwd_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, targets, ignore_index, lse, loss_rows);
+  (f16 ? ce_fwd_kernel<true> : ce_fwd_kernel<false>)<<<M, CE_THREADS, 0, s>>>(logits, ld, V, targets, ignore_index, lse,
+                                                                             loss_rows);
   HB_CUDA_CHECK(cudaGetLastError());
   mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, count);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void ce_fused_launch(__nv_bfloat16* logits, long ld, int M, int V, int Vp, const int64_t* targets, int ignore_index,
-                     float* lse, float* loss_rows, float* loss_mean, const float* scale_ptr, cudaStream_t s) {
+                     float* lse, float* loss_rows, float* loss_mean, const float* scale_ptr, bool f16,
+                     cudaStream_t s) {
   if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
   if (M == 0) return;
-  ce_fused_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets, ignore_index, lse, loss_rows, scale_ptr);
+  (f16 ? ce_fused_kernel<true> : ce_fused_kernel<false>)<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets,
+                                                                                 ignore_index, lse, loss_rows,
+                                                                                 scale_ptr);
   HB_CUDA_CHECK(cudaGetLastError());
   mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, nullptr);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void ce_rescale_launch(__nv_bfloat16* g, long ld, int M, int Vp, const float* actual, const float* expected,
-                       cudaStream_t s) {
+                       bool f16, cudaStream_t s) {
   if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
   if (M == 0) return;
   const long n = (long)M * (Vp >> 3);
   const int blocks = (int)std::min<long>((n + 255) / 256, 4L * num_sms(current_device()));
-  ce_rescale_kernel<<<blocks, 256, 0, s>>>(g, ld, M, Vp, actual, expected);
+  (f16 ? ce_rescale_kernel<true> : ce_rescale_kernel<false>)<<<blocks, 256, 0, s>>>(g, ld, M, Vp, actual, expected);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void ce_bwd_launch(__nv_bfloat16* logits, long ld, int M, int V, int Vp, const int64_t* targets, int ignore_index,
-                   const float* lse, const float* scale_ptr, float scale_mul, cudaStream_t s) {
+                   const float* lse, const float* scale_ptr, float scale_mul, bool f16, cudaStream_t s) {
   if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
   if (M == 0) return;
-  ce_bwd_kernel<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets, ignore_index, lse, scale_ptr, scale_mul);
+  (f16 ? ce_bwd_kernel<true> : ce_bwd_kernel<false>)<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets, ignore_index,
+                                                                             lse, scale_ptr, scale_mul);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -316,7 +325,7 @@ extern "C" int hb_cross_entropy_fwd_noalloc(const void* logits, long ld, int M, 
   float* rows = nullptr;
   const int rc = ce_noalloc_scratch(&rows);
   if (rc != HB_NOALLOC_OK) return rc;
-  hb::ce_fwd_kernel<<<M, hb::CE_THREADS, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, targets,
+  hb::ce_fwd_kernel<false><<<M, hb::CE_THREADS, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, targets,
                                                       ignore_index, lse, rows);
   if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_ERR_CUDA;
   hb::mean_loss_kernel<<<1, 1024, 0, stream>>>(rows, targets, M, ignore_index, loss_mean, nullptr);

@@ -23,6 +23,7 @@ constexpr int kMaxTopK = 8;
 constexpr int kPad = 128;
 
 // One warp per token: logits = x . Wg^T (fp32), softmax, top-k, renormalise.
+template <bool F16>
 __global__ void moe_router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const float* __restrict__ wg, int N,
                                       int H, int E, int K, float* __restrict__ probs, int* __restrict__ topi,
                                       float* __restrict__ topw, int* __restrict__ counts,
@@ -34,8 +35,8 @@ __global__ void moe_router_fwd_kernel(const __nv_bfloat16* __restrict__ x, const
   const __nv_bfloat16* xr = x + (long)t * H;
   for (int e = 0; e < E; ++e) logit[e] = 0.f;
   for (int j = lane * 2; j < H; j += 64) {
-    const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(xr + j);
-    const float a = __bfloat162float(v.x), b = __bfloat162float(v.y);
+    const uint32_t v = *reinterpret_cast<const uint32_t*>(xr + j);
+    const float a = lo16<F16>(v), b = hi16<F16>(v);
     for (int e = 0; e < E; ++e) logit[e] += a * wg[(long)e * H + j] + b * wg[(long)e * H + j + 1];
   }
   float mx = -INFINITY;
@@ -141,6 +142,7 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int
   uint4* dst = reinterpret_cast<uint4*>(xp + (long)(r - lo) * H);
   for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
 }
+template <bool F16>
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const int* __restrict__ pos,
                                    const float* __restrict__ topw, const float* __restrict__ resid, int N, int K,
                                    int H, float* __restrict__ out, const int* __restrict__ off, int e0, int e1,
@@ -157,16 +159,15 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const i
       if (!HB_DCHECK(r - lo < cap, status, 301)) continue;
       const float wk = topw[(long)t * K + k];
       const uint2 raw = *reinterpret_cast<const uint2*>(yp + (long)(r - lo) * H + j);
-      const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-      acc.x += wk * __bfloat162float(a.x);
-      acc.y += wk * __bfloat162float(a.y);
-      acc.z += wk * __bfloat162float(b.x);
-      acc.w += wk * __bfloat162float(b.y);
+      acc.x += wk * lo16<F16>(raw.x);
+      acc.y += wk * hi16<F16>(raw.x);
+      acc.z += wk * lo16<F16>(raw.y);
+      acc.w += wk * hi16<F16>(raw.y);
     }
     *reinterpret_cast<float4*>(out + (long)t * H + j) = acc;
   }
 }
+template <bool F16>
 __global__ void moe_combine_bwd_kernel(const float* __restrict__ dy, const __nv_bfloat16* __restrict__ yp,
                                        const int* __restrict__ pos, const float* __restrict__ topw, int N, int K,
                                        int H, __nv_bfloat16* __restrict__ dyp, float* __restrict__ dw,
@@ -187,12 +188,9 @@ __global__ void moe_combine_bwd_kernel(const float* __restrict__ dy, const __nv_
     for (int j = lane * 4; j < H; j += 128) {
       const float4 g = *reinterpret_cast<const float4*>(dy + (long)t * H + j);
       const uint2 raw = *reinterpret_cast<const uint2*>(yp + row * H + j);
-      const __nv_bfloat162 a = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-      const __nv_bfloat162 b = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-      dot += g.x * __bfloat162float(a.x) + g.y * __bfloat162float(a.y) + g.z * __bfloat162float(b.x) +
-             g.w * __bfloat162float(b.y);
+      dot += g.x * lo16<F16>(raw.x) + g.y * hi16<F16>(raw.x) + g.z * lo16<F16>(raw.y) + g.w * hi16<F16>(raw.y);
       *reinterpret_cast<uint2*>(dyp + row * H + j) =
-          make_uint2(pack_bf16(wk * g.x, wk * g.y), pack_bf16(wk * g.z, wk * g.w));
+          make_uint2(pack16<F16>(wk * g.x, wk * g.y), pack16<F16>(wk * g.z, wk * g.w));
     }
     dot = warp_sum(dot);
     if (lane == 0) dw[(long)t * K + k] = dot;
@@ -228,8 +226,9 @@ __global__ void moe_local_offsets_kernel(const int* __restrict__ off, int e0, in
 
 // Router backward, one warp per token. Upstream: dw (gradient of the
 // renormalised top-k weights) and daux (gradient of the aux loss). Produces
-// dlogits (bf16 [N, E], for the gate weight gradient GEMM) and adds
+// dlogits (16-bit [N, E], for the gate weight gradient GEMM) and adds
 // dlogits . Wg to dx (fp32).
+template <bool F16>
 __global__ void moe_router_bwd_kernel(const float* __restrict__ probs, const int* __restrict__ topi,
                                       const float* __restrict__ topw, const float* __restrict__ dw,
                                       const float* __restrict__ daux, const int* __restrict__ counts, float coef,
@@ -256,7 +255,7 @@ __global__ void moe_router_bwd_kernel(const float* __restrict__ probs, const int
   for (int e = 0; e < E; ++e) pdp += p[e] * dp[e];
   float dl[kMaxExperts];
   for (int e = 0; e < E; ++e) dl[e] = p[e] * (dp[e] - pdp);
-  for (int e = lane; e < E; e += 32) dlogits[(long)t * ld_dl + e] = __float2bfloat16_rn(dl[e]);
+  for (int e = lane; e < E; e += 32) reinterpret_cast<uint16_t*>(dlogits)[(long)t * ld_dl + e] = from_f32<F16>(dl[e]);
   for (int j = lane; j < H; j += 32) {
     float acc = 0.f;
     for (int e = 0; e < E; ++e) acc += dl[e] * wg[(long)e * H + j];
@@ -266,12 +265,13 @@ __global__ void moe_router_bwd_kernel(const float* __restrict__ probs, const int
 
 // ---------------------------------------------------------------------------
 void moe_route_launch(const __nv_bfloat16* x, const float* wg, int N, int H, int E, int K, float coef, float* probs,
-                      int* topi, float* topw, int* counts, float* probsum, int* off, float* aux, int* pos,
+                      int* topi, float* topw, int* counts, float* probsum, int* off, float* aux, int* pos, bool f16,
                       cudaStream_t s) {
   if (E > kMaxExperts || K > kMaxTopK || K > E || H % 8) throw std::runtime_error("moe: unsupported E / K / H");
   HB_CUDA_CHECK(cudaMemsetAsync(counts, 0, sizeof(int) * E, s));
   HB_CUDA_CHECK(cudaMemsetAsync(probsum, 0, sizeof(float) * E, s));
-  moe_router_fwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(x, wg, N, H, E, K, probs, topi, topw, counts, probsum);
+  (f16 ? moe_router_fwd_kernel<true> : moe_router_fwd_kernel<false>)<<<(N * 32 + 255) / 256, 256, 0, s>>>(
+      x, wg, N, H, E, K, probs, topi, topw, counts, probsum);
   HB_CUDA_CHECK(cudaGetLastError());
   moe_offsets_kernel<<<1, 32, 0, s>>>(counts, probsum, E, N, K, coef, off, aux);
   HB_CUDA_CHECK(cudaGetLastError());
@@ -286,17 +286,18 @@ void moe_gather_launch(const __nv_bfloat16* x, const int* pos, int N, int K, int
 }
 
 void moe_combine_launch(const __nv_bfloat16* yp, const int* pos, const float* topw, const float* resid, int N, int K,
-                        int H, float* out, const int* off, int e0, int e1, int cap, int* status, cudaStream_t s) {
-  moe_combine_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(yp, pos, topw, resid, N, K, H, out, off, e0, e1, cap,
-                                                          status);
+                        int H, float* out, const int* off, int e0, int e1, int cap, int* status, bool f16,
+                        cudaStream_t s) {
+  (f16 ? moe_combine_kernel<true> : moe_combine_kernel<false>)<<<(N * 32 + 255) / 256, 256, 0, s>>>(
+      yp, pos, topw, resid, N, K, H, out, off, e0, e1, cap, status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void moe_combine_bwd_launch(const float* dy, const __nv_bfloat16* yp, const int* pos, const float* topw, int N,
                             int K, int H, __nv_bfloat16* dyp, float* dw, const int* off, int e0, int e1, int cap,
-                            int* status, cudaStream_t s) {
-  moe_combine_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dy, yp, pos, topw, N, K, H, dyp, dw, off, e0, e1, cap,
-                                                              status);
+                            int* status, bool f16, cudaStream_t s) {
+  (f16 ? moe_combine_bwd_kernel<true> : moe_combine_bwd_kernel<false>)<<<(N * 32 + 255) / 256, 256, 0, s>>>(
+      dy, yp, pos, topw, N, K, H, dyp, dw, off, e0, e1, cap, status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -314,9 +315,9 @@ void moe_local_offsets_launch(const int* off, int e0, int n, int* out, cudaStrea
 
 void moe_router_bwd_launch(const float* probs, const int* topi, const float* topw, const float* dw, const float* daux,
                            const int* counts, float coef, int N, int H, int E, int K, const float* wg,
-                           __nv_bfloat16* dlogits, long ld_dl, float* dx, cudaStream_t s) {
-  moe_router_bwd_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(probs, topi, topw, dw, daux, counts, coef, N, H, E, K,
-                                                              wg, dlogits, ld_dl, dx);
+                           __nv_bfloat16* dlogits, long ld_dl, float* dx, bool f16, cudaStream_t s) {
+  (f16 ? moe_router_bwd_kernel<true> : moe_router_bwd_kernel<false>)<<<(N * 32 + 255) / 256, 256, 0, s>>>(
+      probs, topi, topw, dw, daux, counts, coef, N, H, E, K, wg, dlogits, ld_dl, dx);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

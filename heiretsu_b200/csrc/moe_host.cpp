@@ -10,18 +10,18 @@
 namespace hb {
 
 void moe_route_launch(const __nv_bfloat16*, const float*, int, int, int, int, float, float*, int*, float*, int*, float*,
-                      int*, float*, int*, cudaStream_t);
+                      int*, float*, int*, bool, cudaStream_t);
 void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, const int*, int, int, int,
                        int*, cudaStream_t);
 void moe_combine_launch(const __nv_bfloat16*, const int*, const float*, const float*, int, int, int, float*,
-                        const int*, int, int, int, int*, cudaStream_t);
+                        const int*, int, int, int, int*, bool, cudaStream_t);
 void moe_combine_bwd_launch(const float*, const __nv_bfloat16*, const int*, const float*, int, int, int,
-                            __nv_bfloat16*, float*, const int*, int, int, int, int*, cudaStream_t);
+                            __nv_bfloat16*, float*, const int*, int, int, int, int*, bool, cudaStream_t);
 void moe_unpermute_launch(const float*, const int*, int, int, int, float*, const int*, int, int, int, int*,
                           cudaStream_t);
 void moe_local_offsets_launch(const int*, int, int, int*, cudaStream_t);
 void moe_router_bwd_launch(const float*, const int*, const float*, const float*, const float*, const int*, float, int,
-                           int, int, int, const float*, __nv_bfloat16*, long, float*, cudaStream_t);
+                           int, int, int, const float*, __nv_bfloat16*, long, float*, bool, cudaStream_t);
 
 template <typename T>
 static T* P(const at::Tensor& t) {
@@ -39,7 +39,8 @@ static void check_f32(const at::Tensor& t, const char* what) {
 void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef, at::Tensor& probs, at::Tensor& topi,
                at::Tensor& topw, at::Tensor& counts, at::Tensor& probsum, at::Tensor& off, at::Tensor& aux,
                at::Tensor& pos) {
-  TORCH_CHECK(x.is_cuda() && x.scalar_type() == at::kBFloat16 && x.is_contiguous(), "moe_route: x bf16 [N, H]");
+  TORCH_CHECK(x.is_cuda() && (x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf) && x.is_contiguous(),
+              "moe_route: x bf16 or fp16 [N, H]");
   check_f32(wg, "moe_route: gate weight [E, H]");
   check_f32(probs, "moe_route: probs");
   check_i32(topi, "moe_route: topi");
@@ -53,7 +54,7 @@ void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef
               "moe_route: shape mismatch");
   moe_route_launch(P<__nv_bfloat16>(x), P<float>(wg), N, H, E, K, static_cast<float>(coef), P<float>(probs),
                    P<int>(topi), P<float>(topw), P<int>(counts), P<float>(probsum), P<int>(off), P<float>(aux),
-                   P<int>(pos), S());
+                   P<int>(pos), x.scalar_type() == at::kHalf, S());
 }
 
 // Expert window [e0, e1): only rows of padded expert segments e0 .. e1-1 take
@@ -66,8 +67,9 @@ static void check_window(const at::Tensor& off, int64_t e0, int64_t e1) {
 
 void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp, const at::Tensor& off,
                 int64_t e0, int64_t e1) {
-  TORCH_CHECK(x.scalar_type() == at::kBFloat16 && xp.scalar_type() == at::kBFloat16 && x.size(1) == xp.size(1),
-              "moe_gather: bf16 [N, H] -> [R, H]");
+  TORCH_CHECK((x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf) &&
+                  xp.scalar_type() == x.scalar_type() && x.size(1) == xp.size(1),
+              "moe_gather: 16-bit [N, H] -> [R, H] of one format");
   check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(x.device());
   moe_gather_launch(P<__nv_bfloat16>(x), P<int>(pos), x.size(0), K, x.size(1), P<__nv_bfloat16>(xp), P<int>(off),
@@ -88,7 +90,7 @@ void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& 
   c10::cuda::CUDAGuard g(yp.device());
   const int N = out.size(0), H = out.size(1), K = topw.size(1);
   moe_combine_launch(P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), r, N, K, H, P<float>(out), P<int>(off), e0,
-                     e1, yp.size(0), device_status_ptr(yp.get_device()), S());
+                     e1, yp.size(0), device_status_ptr(yp.get_device()), yp.scalar_type() == at::kHalf, S());
 }
 
 void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
@@ -99,7 +101,7 @@ void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tenso
   const int N = dy.size(0), H = dy.size(1), K = topw.size(1);
   moe_combine_bwd_launch(P<float>(dy), P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), N, K, H,
                          P<__nv_bfloat16>(dyp), P<float>(dw), P<int>(off), e0, e1, yp.size(0),
-                         device_status_ptr(dy.get_device()), S());
+                         device_status_ptr(dy.get_device()), yp.scalar_type() == at::kHalf, S());
 }
 
 void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::Tensor& dx, const at::Tensor& off,
@@ -128,7 +130,7 @@ void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::T
   const int N = probs.size(0), E = probs.size(1), K = topi.size(1), H = wg.size(1);
   moe_router_bwd_launch(P<float>(probs), P<int>(topi), P<float>(topw), P<float>(dw), P<float>(daux), P<int>(counts),
                         static_cast<float>(coef), N, H, E, K, P<float>(wg), P<__nv_bfloat16>(dlogits),
-                        dlogits.stride(0), P<float>(dx), S());
+                        dlogits.stride(0), P<float>(dx), dlogits.scalar_type() == at::kHalf, S());
 }
 
 }  // namespace hb

@@ -25,7 +25,7 @@ namespace hb {
 constexpr int LN_ROWS_PER_CTA = 8;   // forward: 8 warps, one row each
 constexpr int LN_BWD_WARPS = 8;
 
-template <int V4>
+template <int V4, bool F16>
 __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x, const float* __restrict__ w,
                                                      const float* __restrict__ b, __nv_bfloat16* __restrict__ y,
                                                      float* __restrict__ mean_out, float* __restrict__ rstd_out,
@@ -66,7 +66,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
       const float o1 = (v[i].y - mu) * rstd * ww.y + bb.y;
       const float o2 = (v[i].z - mu) * rstd * ww.z + bb.z;
       const float o3 = (v[i].w - mu) * rstd * ww.w + bb.w;
-      yr[j] = make_uint2(pack_bf16(o0, o1), pack_bf16(o2, o3));
+      yr[j] = make_uint2(pack16<F16>(o0, o1), pack16<F16>(o2, o3));
     }
   }
   if (lane == 0) {
@@ -78,7 +78,7 @@ __global__ void __launch_bounds__(256) ln_fwd_kernel(const float* __restrict__ x
 // Reduce-scatter consumer: x_new = x + sum_s parts[s] + bias (fp32 residual
 // shard), and, if w != nullptr, y = LN(x_new) in bf16 with its statistics.
 // parts: `nsrc` bf16 slots of [M, H] at stride `src_stride` elements.
-template <int V4>
+template <int V4, bool F16>
 __global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restrict__ x,
                                                            const __nv_bfloat16* __restrict__ parts, int nsrc,
                                                            long src_stride, const float* __restrict__ bias,
@@ -104,12 +104,10 @@ __global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restri
       a.w += bb.w;
       for (int q = 0; q < nsrc; ++q) {
         const uint2 raw = reinterpret_cast<const uint2*>(parts + q * src_stride + (long)row * H)[j];
-        const __nv_bfloat162 lo = *reinterpret_cast<const __nv_bfloat162*>(&raw.x);
-        const __nv_bfloat162 hi = *reinterpret_cast<const __nv_bfloat162*>(&raw.y);
-        a.x += __bfloat162float(lo.x);
-        a.y += __bfloat162float(lo.y);
-        a.z += __bfloat162float(hi.x);
-        a.w += __bfloat162float(hi.y);
+        a.x += lo16<F16>(raw.x);
+        a.y += hi16<F16>(raw.x);
+        a.z += lo16<F16>(raw.y);
+        a.w += hi16<F16>(raw.y);
       }
       v[i] = a;
       reinterpret_cast<float4*>(x_new + (long)row * H)[j] = a;
@@ -136,8 +134,8 @@ __global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restri
     const int j = lane + 32 * i;
     if (j < H4) {
       const float4 ww = reinterpret_cast<const float4*>(w)[j], bb = reinterpret_cast<const float4*>(b)[j];
-      yr[j] = make_uint2(pack_bf16((v[i].x - mu) * rstd * ww.x + bb.x, (v[i].y - mu) * rstd * ww.y + bb.y),
-                         pack_bf16((v[i].z - mu) * rstd * ww.z + bb.z, (v[i].w - mu) * rstd * ww.w + bb.w));
+      yr[j] = make_uint2(pack16<F16>((v[i].x - mu) * rstd * ww.x + bb.x, (v[i].y - mu) * rstd * ww.y + bb.y),
+                         pack16<F16>((v[i].z - mu) * rstd * ww.z + bb.z, (v[i].w - mu) * rstd * ww.w + bb.w));
     }
   }
   if (lane == 0) {
@@ -161,7 +159,7 @@ __global__ void __launch_bounds__(256) resid_sum_ln_kernel(const float* __restri
 // batch reuses the normalised-input registers, which are dead by then, so the
 // register count stays the same; the arithmetic is unchanged (same fused
 // multiply-add per element).
-template <int V4, bool HOIST>
+template <int V4, bool HOIST, bool F16>
 __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const float* __restrict__ dy, const float* __restrict__ x,
                                                         const float* __restrict__ mean, const float* __restrict__ rstd,
                                                         const float* __restrict__ w, const float* dres_in,
@@ -245,7 +243,7 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const float* __restrict_
           o.z = fmaf(rs, dv[i].z, xv[i].z);
           o.w = fmaf(rs, dv[i].w, xv[i].w);
           rout[j] = o;
-          r16[j] = make_uint2(pack_bf16(o.x, o.y), pack_bf16(o.z, o.w));
+          r16[j] = make_uint2(pack16<F16>(o.x, o.y), pack16<F16>(o.z, o.w));
         }
       }
     } else {
@@ -259,7 +257,7 @@ __global__ void __launch_bounds__(256, 2) ln_bwd_kernel(const float* __restrict_
           o.z += rs * (dv[i].z - m1 - xv[i].z * m2);
           o.w += rs * (dv[i].w - m1 - xv[i].w * m2);
           rout[j] = o;
-          r16[j] = make_uint2(pack_bf16(o.x, o.y), pack_bf16(o.z, o.w));
+          r16[j] = make_uint2(pack16<F16>(o.x, o.y), pack16<F16>(o.z, o.w));
         }
       }
     }
@@ -309,6 +307,7 @@ __global__ void __launch_bounds__(256) reduce_rows_kernel(const float* __restric
 
 // Column sums of a bf16 matrix: out[c] += sum_r in[r, c]. Block = 8 warps
 // covering 64 columns (2 per lane) and `rows_per_cta` rows.
+template <bool F16>
 __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* __restrict__ in, long ld, int M,
                                                           int N, int rows_per_cta, float* __restrict__ out) {
   __shared__ float red[8][64];
@@ -319,9 +318,9 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
   float a0 = 0.f, a1 = 0.f;
   if (c < N) {
     for (int r = r0 + warp; r < r1; r += 8) {
-      const __nv_bfloat162 v = *reinterpret_cast<const __nv_bfloat162*>(in + (long)r * ld + c);
-      a0 += __bfloat162float(v.x);
-      a1 += __bfloat162float(v.y);
+      const uint32_t v = *reinterpret_cast<const uint32_t*>(in + (long)r * ld + c);
+      a0 += lo16<F16>(v);
+      a1 += hi16<F16>(v);
     }
   }
   red[warp][lane * 2] = a0;
@@ -340,6 +339,7 @@ __global__ void __launch_bounds__(256) colsum_bf16_kernel(const __nv_bfloat16* _
 // (one 16-byte load per row), a CTA covers 256 columns, and every warp keeps
 // 8 row loads in flight; warps combine through shared memory, then one
 // atomic per column per CTA.
+template <bool F16>
 __global__ void __launch_bounds__(256) colsum_bf16_wide_kernel(const __nv_bfloat16* __restrict__ in, long ld, int M,
                                                                int N, int rows_per_cta, float* __restrict__ out) {
   __shared__ float red[8][256 + 8];
@@ -356,16 +356,16 @@ __global__ void __launch_bounds__(256) colsum_bf16_wide_kernel(const __nv_bfloat
       for (int u = 0; u < 8; ++u) v[u] = __ldg(reinterpret_cast<const uint4*>(in + (long)(r + 8 * u) * ld + c0));
 #pragma unroll
       for (int u = 0; u < 8; ++u) {
-        const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v[u]);
+        const uint16_t* e = reinterpret_cast<const uint16_t*>(&v[u]);
 #pragma unroll
-        for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]);
+        for (int j = 0; j < 8; ++j) acc[j] += to_f32<F16>(e[j]);
       }
     }
     for (; r < r1; r += 8) {
       const uint4 v = __ldg(reinterpret_cast<const uint4*>(in + (long)r * ld + c0));
-      const __nv_bfloat16* e = reinterpret_cast<const __nv_bfloat16*>(&v);
+      const uint16_t* e = reinterpret_cast<const uint16_t*>(&v);
 #pragma unroll
-      for (int j = 0; j < 8; ++j) acc[j] += __bfloat162float(e[j]);
+      for (int j = 0; j < 8; ++j) acc[j] += to_f32<F16>(e[j]);
     }
   }
 #pragma unroll
@@ -404,20 +404,29 @@ static int ln_v4(int H) {
 }
 
 void ln_fwd_launch(const float* x, const float* w, const float* b, __nv_bfloat16* y, float* mean, float* rstd,
-                   int M, int H, float eps, cudaStream_t s) {
+                   int M, int H, float eps, bool f16, cudaStream_t s) {
   if (M == 0) return;
   const int blocks = (M + LN_ROWS_PER_CTA - 1) / LN_ROWS_PER_CTA;
-  HB_LN_DISPATCH(ln_v4(H), ln_fwd_kernel<kV><<<blocks, 256, 0, s>>>(x, w, b, y, mean, rstd, M, H, eps));
+  if (f16) {
+    HB_LN_DISPATCH(ln_v4(H), ln_fwd_kernel<kV, true><<<blocks, 256, 0, s>>>(x, w, b, y, mean, rstd, M, H, eps));
+  } else {
+    HB_LN_DISPATCH(ln_v4(H), ln_fwd_kernel<kV, false><<<blocks, 256, 0, s>>>(x, w, b, y, mean, rstd, M, H, eps));
+  }
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
 void resid_sum_ln_launch(const float* x, const __nv_bfloat16* parts, int nsrc, long src_stride, const float* bias,
                          float* x_new, const float* w, const float* b, __nv_bfloat16* y, float* mean, float* rstd,
-                         int M, int H, float eps, cudaStream_t s) {
+                         int M, int H, float eps, bool f16, cudaStream_t s) {
   if (M == 0) return;
   const int blocks = (M + LN_ROWS_PER_CTA - 1) / LN_ROWS_PER_CTA;
-  HB_LN_DISPATCH(ln_v4(H), resid_sum_ln_kernel<kV><<<blocks, 256, 0, s>>>(x, parts, nsrc, src_stride, bias, x_new, w,
-                                                                           b, y, mean, rstd, M, H, eps));
+  if (f16) {
+    HB_LN_DISPATCH(ln_v4(H), resid_sum_ln_kernel<kV, true><<<blocks, 256, 0, s>>>(
+                                 x, parts, nsrc, src_stride, bias, x_new, w, b, y, mean, rstd, M, H, eps));
+  } else {
+    HB_LN_DISPATCH(ln_v4(H), resid_sum_ln_kernel<kV, false><<<blocks, 256, 0, s>>>(
+                                 x, parts, nsrc, src_stride, bias, x_new, w, b, y, mean, rstd, M, H, eps));
+  }
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -430,7 +439,8 @@ int ln_bwd_num_ctas(int M, int device) {
 
 void ln_bwd_launch(const float* dy, const float* x, const float* mean, const float* rstd, const float* w,
                    const float* dres_in, float* dres, __nv_bfloat16* dres16, float* part, int num_ctas,
-                   float* dgamma, float* dbeta, int M, int H, int dy_srcs, long dy_src_stride, cudaStream_t s) {
+                   float* dgamma, float* dbeta, int M, int H, int dy_srcs, long dy_src_stride, bool f16,
+                   cudaStream_t s) {
   if (M == 0) return;
   static const bool hoist = [] {
     // measured on a B200 at 8192 x 768: 34.8 us hoisted, 42.2 us in the plain order
@@ -438,36 +448,31 @@ void ln_bwd_launch(const float* dy, const float* x, const float* mean, const flo
     return e == nullptr || e[0] != '0';
   }();
   const size_t smem = (size_t)LN_BWD_WARPS * 2 * H * sizeof(float);
+  // The four (hoist, 16-bit format) instantiations at width kV.
+#define HB_LN_BWD_KERNEL(kV) \
+  (hoist ? (f16 ? ln_bwd_kernel<kV, true, true> : ln_bwd_kernel<kV, true, false>) \
+         : (f16 ? ln_bwd_kernel<kV, false, true> : ln_bwd_kernel<kV, false, false>))
   if (smem > 48 * 1024) {
-    static bool attr_set[64][17][2] = {};
+    static bool attr_set[64][17][2][2] = {};
     const int dev = current_device();
     const int v = ln_v4(H);
-    if (!attr_set[dev][v][hoist]) {
-      if (hoist) {
-        HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<kV, true>,
-                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
-      } else {
-        HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(ln_bwd_kernel<kV, false>,
-                                                             cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
-      }
-      attr_set[dev][v][hoist] = true;
+    if (!attr_set[dev][v][hoist][f16]) {
+      HB_LN_DISPATCH(v, HB_CUDA_CHECK(cudaFuncSetAttribute(HB_LN_BWD_KERNEL(kV),
+                                                           cudaFuncAttributeMaxDynamicSharedMemorySize, (int)smem)));
+      attr_set[dev][v][hoist][f16] = true;
     }
   }
-  if (hoist) {
-    HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV, true><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
-                                                                                  dres16, part, M, H, dy_srcs,
-                                                                                  dy_src_stride));
-  } else {
-    HB_LN_DISPATCH(ln_v4(H), ln_bwd_kernel<kV, false><<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
-                                                                                   dres16, part, M, H, dy_srcs,
-                                                                                   dy_src_stride));
-  }
+  HB_LN_DISPATCH(ln_v4(H), HB_LN_BWD_KERNEL(kV)<<<num_ctas, 256, smem, s>>>(dy, x, mean, rstd, w, dres_in, dres,
+                                                                            dres16, part, M, H, dy_srcs,
+                                                                            dy_src_stride));
+#undef HB_LN_BWD_KERNEL
   HB_CUDA_CHECK(cudaGetLastError());
   reduce_rows_kernel<<<(2 * H + 31) / 32, 256, 0, s>>>(part, num_ctas, 2 * H, dgamma, dbeta, H);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-// out = bf16(g * mask): 4 elements (2 mask pairs) per thread.
+// out = 16-bit(g * mask): 4 elements (2 mask pairs) per thread.
+template <bool F16>
 __global__ void dropout_bf16_kernel(const float* __restrict__ g, __nv_bfloat16* __restrict__ out, long M, int H,
                                     DropoutArgs d) {
   const uint32_t key = dropout_key(*d.seed, d.site);
@@ -480,30 +485,32 @@ __global__ void dropout_bf16_kernel(const float* __restrict__ g, __nv_bfloat16* 
     dropout_pair(dropout_bits(key, pair), d.thresh, d.scale, m0, m1);
     dropout_pair(dropout_bits(key, pair + 1), d.thresh, d.scale, m2, m3);
     const float4 v = reinterpret_cast<const float4*>(g)[i];
-    reinterpret_cast<uint2*>(out)[i] = make_uint2(pack_bf16(v.x * m0, v.y * m1), pack_bf16(v.z * m2, v.w * m3));
+    reinterpret_cast<uint2*>(out)[i] = make_uint2(pack16<F16>(v.x * m0, v.y * m1), pack16<F16>(v.z * m2, v.w * m3));
   }
 }
 
-void dropout_bf16_launch(const float* g, __nv_bfloat16* out, long M, int H, const DropoutArgs& d, cudaStream_t s) {
+void dropout_bf16_launch(const float* g, __nv_bfloat16* out, long M, int H, const DropoutArgs& d, bool f16,
+                         cudaStream_t s) {
   const long n4 = M * (long)H / 4;
   if (n4 == 0) return;
   const int blocks = (int)std::min<long>((n4 + 255) / 256, 4L * num_sms(current_device()));
-  dropout_bf16_kernel<<<blocks, 256, 0, s>>>(g, out, M, H, d);
+  (f16 ? dropout_bf16_kernel<true> : dropout_bf16_kernel<false>)<<<blocks, 256, 0, s>>>(g, out, M, H, d);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-void colsum_bf16_launch(const __nv_bfloat16* in, long ld, int M, int N, float* out, cudaStream_t s) {
+void colsum_bf16_launch(const __nv_bfloat16* in, long ld, int M, int N, float* out, bool f16, cudaStream_t s) {
   if (M == 0 || N == 0) return;
   if (N % 8 == 0 && ld % 8 == 0 && reinterpret_cast<uintptr_t>(in) % 16 == 0) {
     const int rows_per_cta = 64;
     dim3 grid((N + 255) / 256, (M + rows_per_cta - 1) / rows_per_cta);
-    colsum_bf16_wide_kernel<<<grid, 256, 0, s>>>(in, ld, M, N, rows_per_cta, out);
+    (f16 ? colsum_bf16_wide_kernel<true> : colsum_bf16_wide_kernel<false>)<<<grid, 256, 0, s>>>(in, ld, M, N,
+                                                                                               rows_per_cta, out);
     HB_CUDA_CHECK(cudaGetLastError());
     return;
   }
   const int rows_per_cta = 256;
   dim3 grid((N + 63) / 64, (M + rows_per_cta - 1) / rows_per_cta);
-  colsum_bf16_kernel<<<grid, 256, 0, s>>>(in, ld, M, N, rows_per_cta, out);
+  (f16 ? colsum_bf16_kernel<true> : colsum_bf16_kernel<false>)<<<grid, 256, 0, s>>>(in, ld, M, N, rows_per_cta, out);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

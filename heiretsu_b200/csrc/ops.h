@@ -36,7 +36,9 @@ void embedding_bwd(const at::Tensor& idx, const at::Tensor& dx, const c10::optio
                    const c10::optional<at::Tensor>& dwpe);
 int64_t sumsq_scratch_size();
 void sumsq(const at::Tensor& x, at::Tensor& scratch, double weight, at::Tensor& out, bool accumulate);
-void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm);
+void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm,
+               const c10::optional<at::Tensor>& loss_scale);
+void loss_scale_update(const at::Tensor& coef, at::Tensor& state, double growth, double backoff, int64_t interval);
 void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
                 const c10::optional<at::Tensor>& p16, const at::Tensor& hyper, const c10::optional<at::Tensor>& coef);
 void f32_to_bf16(const at::Tensor& x, at::Tensor& y);

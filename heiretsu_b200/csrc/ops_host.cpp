@@ -15,42 +15,45 @@
 namespace hb {
 
 // launchers (norm.cu, loss.cu, embed_optim.cu, attention.cu)
-void ln_fwd_launch(const float*, const float*, const float*, __nv_bfloat16*, float*, float*, int, int, float,
+void ln_fwd_launch(const float*, const float*, const float*, __nv_bfloat16*, float*, float*, int, int, float, bool,
                    cudaStream_t);
 int ln_bwd_num_ctas(int M, int device);
 void ln_bwd_launch(const float*, const float*, const float*, const float*, const float*, const float*, float*,
-                   __nv_bfloat16*, float*, int, float*, float*, int, int, int, long, cudaStream_t);
+                   __nv_bfloat16*, float*, int, float*, float*, int, int, int, long, bool, cudaStream_t);
 void resid_sum_ln_launch(const float*, const __nv_bfloat16*, int, long, const float*, float*, const float*,
-                         const float*, __nv_bfloat16*, float*, float*, int, int, float, cudaStream_t);
-void colsum_bf16_launch(const __nv_bfloat16*, long, int, int, float*, cudaStream_t);
-void ce_fwd_launch(const __nv_bfloat16*, long, int, int, const int64_t*, int, float*, float*, float*, float*,
+                         const float*, __nv_bfloat16*, float*, float*, int, int, float, bool, cudaStream_t);
+void colsum_bf16_launch(const __nv_bfloat16*, long, int, int, float*, bool, cudaStream_t);
+void ce_fwd_launch(const __nv_bfloat16*, long, int, int, const int64_t*, int, float*, float*, float*, float*, bool,
                    cudaStream_t);
-void ce_bwd_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, const float*, const float*, float,
+void ce_bwd_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, const float*, const float*, float, bool,
                    cudaStream_t);
 void ce_fused_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, float*, float*, float*, const float*,
-                     cudaStream_t);
-void ce_rescale_launch(__nv_bfloat16*, long, int, int, const float*, const float*, cudaStream_t);
+                     bool, cudaStream_t);
+void ce_rescale_launch(__nv_bfloat16*, long, int, int, const float*, const float*, bool, cudaStream_t);
 void embed_fwd_launch(const int64_t*, const float*, const float*, float*, int, int, int, cudaStream_t);
 void embed_bwd_launch(const int64_t*, const float*, float*, float*, int, int, int, cudaStream_t);
 int sumsq_num_parts(int device);
 void sumsq_launch(const float*, long, float*, int, float, float*, bool, cudaStream_t);
-void clip_coef_launch(const float*, float, float*, float*, cudaStream_t);
-void adamw_launch(float*, const float*, float*, float*, __nv_bfloat16*, long, const void*, const float*,
+void clip_coef_launch(const float*, float, float*, float*, const float*, cudaStream_t);
+void loss_scale_update_launch(const float*, float*, float, float, int, cudaStream_t);
+void adamw_launch(float*, const float*, float*, float*, __nv_bfloat16*, long, const void*, const float*, bool,
                   cudaStream_t);
-void f32_to_bf16_launch(const float*, __nv_bfloat16*, long, cudaStream_t);
+void f32_to_bf16_launch(const float*, __nv_bfloat16*, long, bool, cudaStream_t);
+// (16-bit tensors travel as __nv_bfloat16 pointers; the bool before the stream
+// says whether they hold fp16.)
 void attn_fwd_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int, float,
-                     const DropoutArgs&, int, int, int*, cudaStream_t);
+                     const DropoutArgs&, int, int, int*, bool, cudaStream_t);
 void attn_bwd_launch(const __nv_bfloat16*, long, const __nv_bfloat16*, long, const __nv_bfloat16*, long,
                      const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, float,
-                     const DropoutArgs&, int, int, int*, cudaStream_t);
+                     const DropoutArgs&, int, int, int*, bool, cudaStream_t);
 void attn_fwd_d128_launch(const __nv_bfloat16*, long, __nv_bfloat16*, long, float*, int, int, int, int, float,
-                          const DropoutArgs&, int, int, int*, cudaStream_t);
+                          const DropoutArgs&, int, int, int*, bool, cudaStream_t);
 void attn_bwd_d128_launch(const __nv_bfloat16*, long, const __nv_bfloat16*, long, const __nv_bfloat16*, long,
                           const float*, float*, float*, __nv_bfloat16*, long, int, int, int, int, float,
-                          const DropoutArgs&, int, int, int*, cudaStream_t);
+                          const DropoutArgs&, int, int, int*, bool, cudaStream_t);
 void attn_pad_heads(const __nv_bfloat16*, long, __nv_bfloat16*, long, long, int, int, int, cudaStream_t);
 void attn_unpad_heads(const __nv_bfloat16*, long, __nv_bfloat16*, long, long, int, int, int, cudaStream_t);
-void dropout_bf16_launch(const float*, __nv_bfloat16*, long, int, const DropoutArgs&, cudaStream_t);
+void dropout_bf16_launch(const float*, __nv_bfloat16*, long, int, const DropoutArgs&, bool, cudaStream_t);
 
 // Dropout site arguments from a device seed tensor (int32 scalar) and a rate p (0 = off).
 static DropoutArgs make_dropout(const c10::optional<at::Tensor>& seed, int64_t site, double p, int64_t row0) {
@@ -73,6 +76,14 @@ static DropoutArgs make_dropout(const c10::optional<at::Tensor>& seed, int64_t s
 #define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
 #define CHECK_ROWS(t) TORCH_CHECK((t).dim() == 2 && (t).stride(1) == 1, #t " must be 2-D with contiguous rows")
 
+// Data pointer of a bf16 or fp16 tensor as the kernels' 16-bit element pointer
+// (kernels take the format as a flag: is_f16).
+static __nv_bfloat16* raw16(const at::Tensor& t) {
+  TORCH_CHECK(t.scalar_type() == at::kBFloat16 || t.scalar_type() == at::kHalf, "expected a bf16 or fp16 tensor");
+  return reinterpret_cast<__nv_bfloat16*>(t.data_ptr());
+}
+static bool is_f16(const at::Tensor& t) { return t.scalar_type() == at::kHalf; }
+
 static cudaStream_t stream() { return at::cuda::getCurrentCUDAStream(); }
 template <typename T>
 static T* ptr(const at::Tensor& t) {
@@ -86,13 +97,12 @@ void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b
   CHECK_CONTIG(x);
   CHECK_DT(w, at::kFloat);
   CHECK_DT(b, at::kFloat);
-  CHECK_DT(y, at::kBFloat16);
   CHECK_CONTIG(y);
   c10::cuda::CUDAGuard g(x.device());
   const int H = x.size(-1);
   const int M = x.numel() / H;
-  ln_fwd_launch(ptr<float>(x), ptr<float>(w), ptr<float>(b), ptr<__nv_bfloat16>(y), ptr<float>(mean),
-                ptr<float>(rstd), M, H, static_cast<float>(eps), stream());
+  ln_fwd_launch(ptr<float>(x), ptr<float>(w), ptr<float>(b), raw16(y), ptr<float>(mean), ptr<float>(rstd), M, H,
+                static_cast<float>(eps), is_f16(y), stream());
 }
 
 int64_t layernorm_bwd_scratch_rows(int64_t M) { return ln_bwd_num_ctas(static_cast<int>(M), current_device()); }
@@ -109,7 +119,6 @@ void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   CHECK_CONTIG(dres);
   CHECK_DT(dres_in, at::kFloat);
   CHECK_CONTIG(dres_in);
-  CHECK_DT(dres16, at::kBFloat16);
   CHECK_CONTIG(dres16);
   CHECK_DT(scratch, at::kFloat);
   c10::cuda::CUDAGuard g(x.device());
@@ -119,8 +128,8 @@ void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   TORCH_CHECK(scratch.numel() >= (int64_t)ctas * 2 * H, "layernorm_bwd: scratch too small");
   TORCH_CHECK(dy_srcs >= 1 && dy.numel() >= dy_srcs * (int64_t)M * H, "layernorm_bwd: dy holds dy_srcs slots of [M, H]");
   ln_bwd_launch(ptr<float>(dy), ptr<float>(x), ptr<float>(mean), ptr<float>(rstd), ptr<float>(w),
-                ptr<float>(dres_in), ptr<float>(dres), ptr<__nv_bfloat16>(dres16), ptr<float>(scratch), ctas,
-                ptr<float>(dgamma), ptr<float>(dbeta), M, H, static_cast<int>(dy_srcs), (long)M * H, stream());
+                ptr<float>(dres_in), ptr<float>(dres), raw16(dres16), ptr<float>(scratch), ctas, ptr<float>(dgamma),
+                ptr<float>(dbeta), M, H, static_cast<int>(dy_srcs), (long)M * H, is_f16(dres16), stream());
 }
 
 void resid_sum_ln(const at::Tensor& x, const at::Tensor& parts, int64_t nsrc, const at::Tensor& bias,
@@ -130,75 +139,70 @@ void resid_sum_ln(const at::Tensor& x, const at::Tensor& parts, int64_t nsrc, co
   CHECK_CUDA(x);
   CHECK_DT(x, at::kFloat);
   CHECK_CONTIG(x);
-  CHECK_DT(parts, at::kBFloat16);
   CHECK_DT(x_new, at::kFloat);
   const int H = x.size(-1);
   const int M = x.numel() / H;
   TORCH_CHECK(parts.numel() >= nsrc * (int64_t)M * H, "resid_sum_ln: parts holds nsrc slots of [M, H]");
   const bool ln = w && w->defined();
   c10::cuda::CUDAGuard g(x.device());
-  resid_sum_ln_launch(ptr<float>(x), ptr<__nv_bfloat16>(parts), static_cast<int>(nsrc), (long)M * H, ptr<float>(bias),
+  TORCH_CHECK(!ln || y->scalar_type() == parts.scalar_type(), "resid_sum_ln: y and parts share one 16-bit format");
+  resid_sum_ln_launch(ptr<float>(x), raw16(parts), static_cast<int>(nsrc), (long)M * H, ptr<float>(bias),
                       ptr<float>(x_new), ln ? ptr<float>(*w) : nullptr, ln ? ptr<float>(*b) : nullptr,
-                      ln ? ptr<__nv_bfloat16>(*y) : nullptr, ln ? ptr<float>(*mean) : nullptr,
-                      ln ? ptr<float>(*rstd) : nullptr, M, H, static_cast<float>(eps), stream());
+                      ln ? raw16(*y) : nullptr, ln ? ptr<float>(*mean) : nullptr, ln ? ptr<float>(*rstd) : nullptr, M,
+                      H, static_cast<float>(eps), is_f16(parts), stream());
 }
 
 void colsum_bf16(const at::Tensor& x, at::Tensor& out) {
   CHECK_CUDA(x);
-  CHECK_DT(x, at::kBFloat16);
   CHECK_ROWS(x);
   CHECK_DT(out, at::kFloat);
   TORCH_CHECK(x.size(1) % 2 == 0 && x.stride(0) % 2 == 0, "colsum_bf16: even column count required");
   c10::cuda::CUDAGuard g(x.device());
-  colsum_bf16_launch(ptr<__nv_bfloat16>(x), x.stride(0), x.size(0), x.size(1), ptr<float>(out), stream());
+  colsum_bf16_launch(raw16(x), x.stride(0), x.size(0), x.size(1), ptr<float>(out), is_f16(x), stream());
 }
 
 void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                        at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean) {
   CHECK_CUDA(logits);
-  CHECK_DT(logits, at::kBFloat16);
   CHECK_ROWS(logits);
   CHECK_DT(targets, at::kLong);
   CHECK_CONTIG(targets);
   c10::cuda::CUDAGuard g(logits.device());
-  ce_fwd_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, ptr<int64_t>(targets),
-                ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), nullptr, stream());
+  ce_fwd_launch(raw16(logits), logits.stride(0), logits.size(0), V, ptr<int64_t>(targets), ignore_index,
+                ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), nullptr, is_f16(logits), stream());
 }
 
 void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                        const at::Tensor& lse, const c10::optional<at::Tensor>& scale, double scale_mul) {
   CHECK_CUDA(logits);
-  CHECK_DT(logits, at::kBFloat16);
   CHECK_ROWS(logits);
   c10::cuda::CUDAGuard g(logits.device());
   const float* sp = (scale && scale->defined()) ? ptr<float>(*scale) : nullptr;
-  ce_bwd_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, logits.size(1),
-                ptr<int64_t>(targets), ignore_index, ptr<float>(lse), sp, static_cast<float>(scale_mul), stream());
+  ce_bwd_launch(raw16(logits), logits.stride(0), logits.size(0), V, logits.size(1), ptr<int64_t>(targets),
+                ignore_index, ptr<float>(lse), sp, static_cast<float>(scale_mul), is_f16(logits), stream());
 }
 
 void cross_entropy_fused(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                          at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean, const at::Tensor& scale) {
   CHECK_CUDA(logits);
-  CHECK_DT(logits, at::kBFloat16);
   CHECK_ROWS(logits);
   CHECK_DT(targets, at::kLong);
   CHECK_CONTIG(targets);
   CHECK_DT(scale, at::kFloat);
   c10::cuda::CUDAGuard g(logits.device());
-  ce_fused_launch(ptr<__nv_bfloat16>(logits), logits.stride(0), logits.size(0), V, logits.size(1),
-                  ptr<int64_t>(targets), ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean),
-                  ptr<float>(scale), stream());
+  ce_fused_launch(raw16(logits), logits.stride(0), logits.size(0), V, logits.size(1), ptr<int64_t>(targets),
+                  ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), ptr<float>(scale),
+                  is_f16(logits), stream());
 }
 
 void cross_entropy_rescale(at::Tensor& g, const at::Tensor& actual, const at::Tensor& expected) {
   CHECK_CUDA(g);
-  CHECK_DT(g, at::kBFloat16);
   CHECK_ROWS(g);
   CHECK_DT(actual, at::kFloat);
   CHECK_DT(expected, at::kFloat);
   c10::cuda::CUDAGuard gd(g.device());
-  ce_rescale_launch(ptr<__nv_bfloat16>(g), g.stride(0), g.size(0), g.size(1), ptr<float>(actual),
-                    ptr<float>(expected), stream());
+  ce_rescale_launch(raw16(g), g.stride(0), g.size(0), g.size(1), ptr<float>(actual), ptr<float>(expected), is_f16(g),
+                    stream());
 }
 
 void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const at::Tensor& wpe, at::Tensor& out) {
@@ -239,10 +243,21 @@ void sumsq(const at::Tensor& x, at::Tensor& scratch, double weight, at::Tensor& 
                accumulate, stream());
 }
 
-void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm) {
+void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm,
+               const c10::optional<at::Tensor>& loss_scale) {
   c10::cuda::CUDAGuard g(norm2.device());
   clip_coef_launch(ptr<float>(norm2), static_cast<float>(max_norm), ptr<float>(coef),
-                   (norm && norm->defined()) ? ptr<float>(*norm) : nullptr, stream());
+                   (norm && norm->defined()) ? ptr<float>(*norm) : nullptr,
+                   (loss_scale && loss_scale->defined()) ? ptr<float>(*loss_scale) : nullptr, stream());
+}
+
+// state = {scale, finite steps in a row} (fp32 device tensor), updated after a step
+// whose coefficient (NaN = skipped) is `coef`.
+void loss_scale_update(const at::Tensor& coef, at::Tensor& state, double growth, double backoff, int64_t interval) {
+  TORCH_CHECK(state.is_cuda() && state.scalar_type() == at::kFloat && state.numel() >= 2, "loss_scale_update: state");
+  c10::cuda::CUDAGuard g(state.device());
+  loss_scale_update_launch(ptr<float>(coef), ptr<float>(state), static_cast<float>(growth),
+                           static_cast<float>(backoff), static_cast<int>(interval), stream());
 }
 
 void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor& v,
@@ -255,23 +270,24 @@ void adamw_step(at::Tensor& p, const at::Tensor& grad, at::Tensor& m, at::Tensor
   TORCH_CHECK(hyper.scalar_type() == at::kFloat && hyper.numel() >= 8 && hyper.is_cuda(), "adamw_step: hyper");
   c10::cuda::CUDAGuard g(p.device());
   __nv_bfloat16* p16p = nullptr;
+  bool f16 = false;
   if (p16 && p16->defined()) {
-    TORCH_CHECK(p16->scalar_type() == at::kBFloat16 && p16->numel() == p.numel() && p16->is_contiguous(), "p16");
-    p16p = ptr<__nv_bfloat16>(*p16);
+    TORCH_CHECK(p16->numel() == p.numel() && p16->is_contiguous(), "p16");
+    p16p = raw16(*p16);
+    f16 = is_f16(*p16);
   }
   adamw_launch(ptr<float>(p), ptr<float>(grad), ptr<float>(m), ptr<float>(v), p16p, p.numel(), hyper.data_ptr(),
-               (coef && coef->defined()) ? ptr<float>(*coef) : nullptr, stream());
+               (coef && coef->defined()) ? ptr<float>(*coef) : nullptr, f16, stream());
 }
 
 void f32_to_bf16(const at::Tensor& x, at::Tensor& y) {
   CHECK_CUDA(x);
   CHECK_DT(x, at::kFloat);
   CHECK_CONTIG(x);
-  CHECK_DT(y, at::kBFloat16);
   CHECK_CONTIG(y);
   TORCH_CHECK(x.numel() == y.numel(), "f32_to_bf16: size mismatch");
   c10::cuda::CUDAGuard g(x.device());
-  f32_to_bf16_launch(ptr<float>(x), ptr<__nv_bfloat16>(y), x.numel(), stream());
+  f32_to_bf16_launch(ptr<float>(x), raw16(y), x.numel(), is_f16(y), stream());
 }
 
 void attn_set_trace(uint64_t* trace);
@@ -299,11 +315,12 @@ void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::
                    const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
                    int64_t nh_total, int64_t head_dim) {
   CHECK_CUDA(qkv);
-  CHECK_DT(qkv, at::kBFloat16);
+  TORCH_CHECK(qkv.scalar_type() == at::kBFloat16 || qkv.scalar_type() == at::kHalf, "attention_fwd: bf16 or fp16 qkv");
   CHECK_ROWS(qkv);
-  CHECK_DT(out, at::kBFloat16);
+  CHECK_DT(out, qkv.scalar_type());
   CHECK_ROWS(out);
   check_head_dim(head_dim);
+  const bool f16 = qkv.scalar_type() == at::kHalf;
   TORCH_CHECK(qkv.size(0) == B * T && qkv.size(1) == 3 * nh * head_dim,
               "attention_fwd: qkv must be [B*T, 3*nh*head_dim]");
   TORCH_CHECK(out.size(0) == B * T && out.size(1) >= nh * head_dim, "attention_fwd: out must be [B*T, nh*head_dim]");
@@ -317,24 +334,22 @@ void attention_fwd(const at::Tensor& qkv, int64_t B, int64_t T, int64_t nh, at::
   const int nht = static_cast<int>(nh_total > 0 ? nh_total : nh);
   int* status = device_status_ptr(qkv.get_device());
   if (head_dim == 128) {
-    attn_fwd_d128_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0),
-                         ptr<float>(lse), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+    attn_fwd_d128_launch(raw16(qkv), qkv.stride(0), raw16(out), out.stride(0), ptr<float>(lse), B, T, nh, Tpad, scale,
+                         d, static_cast<int>(h0), nht, status, f16, stream());
     return;
   }
   if (head_dim == 64) {
-    attn_fwd_launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<float>(lse),
-                    B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+    attn_fwd_launch(raw16(qkv), qkv.stride(0), raw16(out), out.stride(0), ptr<float>(lse), B, T, nh, Tpad, scale, d,
+                    static_cast<int>(h0), nht, status, f16, stream());
     return;
   }
   const long rows = B * T;
   auto opts = qkv.options();
   at::Tensor qkv_p = at::empty({rows, 3 * nh * 64}, opts), out_p = at::empty({rows, nh * 64}, opts);
-  attn_pad_heads(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), rows, 3, nh,
-                 head_dim, stream());
-  attn_fwd_launch(ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), ptr<__nv_bfloat16>(out_p), out_p.stride(0),
-                  ptr<float>(lse), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
-  attn_unpad_heads(ptr<__nv_bfloat16>(out_p), out_p.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), rows, 1, nh,
-                   head_dim, stream());
+  attn_pad_heads(raw16(qkv), qkv.stride(0), raw16(qkv_p), qkv_p.stride(0), rows, 3, nh, head_dim, stream());
+  attn_fwd_launch(raw16(qkv_p), qkv_p.stride(0), raw16(out_p), out_p.stride(0), ptr<float>(lse), B, T, nh, Tpad, scale,
+                  d, static_cast<int>(h0), nht, status, f16, stream());
+  attn_unpad_heads(raw16(out_p), out_p.stride(0), raw16(out), out.stride(0), rows, 1, nh, head_dim, stream());
 }
 
 void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tensor& dout, const at::Tensor& lse,
@@ -342,9 +357,11 @@ void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tenso
                    const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t h0,
                    int64_t nh_total, int64_t head_dim) {
   CHECK_CUDA(qkv);
+  const bool f16 = qkv.scalar_type() == at::kHalf;
   for (const at::Tensor* t : std::initializer_list<const at::Tensor*>{&qkv, &out, &dout, &dqkv}) {
-    TORCH_CHECK(t->scalar_type() == at::kBFloat16 && t->dim() == 2 && t->stride(1) == 1 && t->stride(0) % 8 == 0,
-                "attention_bwd: bf16 2-D tensors with 16B-aligned rows expected");
+    TORCH_CHECK(t->scalar_type() == (f16 ? at::kHalf : at::kBFloat16) && t->dim() == 2 && t->stride(1) == 1 &&
+                    t->stride(0) % 8 == 0,
+                "attention_bwd: 2-D tensors of one 16-bit format with 16B-aligned rows expected");
   }
   check_head_dim(head_dim);
   TORCH_CHECK(qkv.size(1) == 3 * nh * head_dim && dqkv.size(1) >= 3 * nh * head_dim,
@@ -360,27 +377,22 @@ void attention_bwd(const at::Tensor& qkv, const at::Tensor& out, const at::Tenso
   int* status = device_status_ptr(qkv.get_device());
   if (head_dim >= 64) {
     auto launch = head_dim == 128 ? attn_bwd_d128_launch : attn_bwd_launch;
-    launch(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(out), out.stride(0), ptr<__nv_bfloat16>(dout),
-           dout.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc), ptr<__nv_bfloat16>(dqkv),
-           dqkv.stride(0), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht, status, stream());
+    launch(raw16(qkv), qkv.stride(0), raw16(out), out.stride(0), raw16(dout), dout.stride(0), ptr<float>(lse),
+           ptr<float>(dvec), ptr<float>(dq_acc), raw16(dqkv), dqkv.stride(0), B, T, nh, Tpad, scale, d,
+           static_cast<int>(h0), nht, status, f16, stream());
     return;
   }
   const long rows = B * T;
   auto opts = qkv.options();
   at::Tensor qkv_p = at::empty({rows, 3 * nh * 64}, opts), out_p = at::empty({rows, nh * 64}, opts);
   at::Tensor dout_p = at::empty({rows, nh * 64}, opts), dqkv_p = at::empty({rows, 3 * nh * 64}, opts);
-  attn_pad_heads(ptr<__nv_bfloat16>(qkv), qkv.stride(0), ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), rows, 3, nh,
-                 head_dim, stream());
-  attn_pad_heads(ptr<__nv_bfloat16>(out), out.stride(0), ptr<__nv_bfloat16>(out_p), out_p.stride(0), rows, 1, nh,
-                 head_dim, stream());
-  attn_pad_heads(ptr<__nv_bfloat16>(dout), dout.stride(0), ptr<__nv_bfloat16>(dout_p), dout_p.stride(0), rows, 1, nh,
-                 head_dim, stream());
-  attn_bwd_launch(ptr<__nv_bfloat16>(qkv_p), qkv_p.stride(0), ptr<__nv_bfloat16>(out_p), out_p.stride(0),
-                  ptr<__nv_bfloat16>(dout_p), dout_p.stride(0), ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc),
-                  ptr<__nv_bfloat16>(dqkv_p), dqkv_p.stride(0), B, T, nh, Tpad, scale, d, static_cast<int>(h0), nht,
-                  status, stream());
-  attn_unpad_heads(ptr<__nv_bfloat16>(dqkv_p), dqkv_p.stride(0), ptr<__nv_bfloat16>(dqkv), dqkv.stride(0), rows, 3,
-                   nh, head_dim, stream());
+  attn_pad_heads(raw16(qkv), qkv.stride(0), raw16(qkv_p), qkv_p.stride(0), rows, 3, nh, head_dim, stream());
+  attn_pad_heads(raw16(out), out.stride(0), raw16(out_p), out_p.stride(0), rows, 1, nh, head_dim, stream());
+  attn_pad_heads(raw16(dout), dout.stride(0), raw16(dout_p), dout_p.stride(0), rows, 1, nh, head_dim, stream());
+  attn_bwd_launch(raw16(qkv_p), qkv_p.stride(0), raw16(out_p), out_p.stride(0), raw16(dout_p), dout_p.stride(0),
+                  ptr<float>(lse), ptr<float>(dvec), ptr<float>(dq_acc), raw16(dqkv_p), dqkv_p.stride(0), B, T, nh, Tpad,
+                  scale, d, static_cast<int>(h0), nht, status, f16, stream());
+  attn_unpad_heads(raw16(dqkv_p), dqkv_p.stride(0), raw16(dqkv), dqkv.stride(0), rows, 3, nh, head_dim, stream());
 }
 
 // out (bf16) = g * mask for a residual dropout site: the gradient reaching
@@ -389,13 +401,14 @@ void dropout_bf16(const at::Tensor& g, at::Tensor& out, const at::Tensor& seed, 
                   int64_t row0) {
   CHECK_CUDA(g);
   TORCH_CHECK(g.scalar_type() == at::kFloat && g.is_contiguous() && g.dim() == 2, "dropout_bf16: g fp32 [M, H]");
-  TORCH_CHECK(out.scalar_type() == at::kBFloat16 && out.is_contiguous() && out.sizes() == g.sizes(),
-              "dropout_bf16: out bf16 like g");
+  TORCH_CHECK((out.scalar_type() == at::kBFloat16 || out.scalar_type() == at::kHalf) && out.is_contiguous() &&
+                  out.sizes() == g.sizes(),
+              "dropout_bf16: out 16-bit (bf16 or fp16) like g");
   TORCH_CHECK(g.size(1) % 4 == 0, "dropout_bf16: H % 4 == 0");
   const DropoutArgs d = make_dropout(seed, site, p, row0);
   TORCH_CHECK(d.seed != nullptr, "dropout_bf16: p must be > 0");
   c10::cuda::CUDAGuard guard(g.device());
-  dropout_bf16_launch(ptr<float>(g), ptr<__nv_bfloat16>(out), g.size(0), static_cast<int>(g.size(1)), d, stream());
+  dropout_bf16_launch(ptr<float>(g), raw16(out), g.size(0), static_cast<int>(g.size(1)), d, is_f16(out), stream());
 }
 
 }  // namespace hb

@@ -92,6 +92,12 @@ def embed_fused(wte: torch.nn.Parameter, wpe: torch.nn.Parameter, idx: torch.Ten
 # takes a snapshot of the step's device seed and then advances it, so each
 # micro-batch and each graph replay draws fresh masks, and the backward
 # recomputes exactly the forward's masks from the snapshot.
+def _dt(blk) -> torch.dtype:
+    """16-bit format of a block's activations: the format of its weight shadows
+    (bf16 under --amp bf16, fp16 under --amp fp16)."""
+    return blk.ln_1.weight.w16.dtype
+
+
 def _dropout_of(blk):
     """(seed snapshot tensor, layer index, p) of a block in a training forward, else None."""
     d = getattr(blk, "_hb_drop_now", None)
@@ -102,7 +108,7 @@ def _attn_fwd(blk, x: torch.Tensor, B: int, T: int, keep: bool):
     """Attention sub-layer: x fp32 [M, H] -> x1 = x + drop(c_proj(attn(c_attn(ln_1(x)))))."""
     attn = blk.attn
     d = _dropout_of(blk)
-    xn, m1, r1 = K.layernorm_fwd(x, blk.ln_1.weight, blk.ln_1.bias, LN_EPS)
+    xn, m1, r1 = K.layernorm_fwd(x, blk.ln_1.weight, blk.ln_1.bias, LN_EPS, dtype=_dt(blk))
     qkv = G.linear_fwd(xn, attn.c_attn.weight.w16, attn.c_attn.bias)
     adrop = (d[0], 4 * d[1], d[2], 0, attn.nh_tp) if d else None
     y, lse = K.attention_fwd(qkv, B, T, attn.nh_tp, drop=adrop, head_dim=attn.dh)
@@ -115,7 +121,7 @@ def _mlp_fwd(blk, x1: torch.Tensor, keep: bool):
     """Dense MLP sub-layer: x2 = x1 + drop(c_proj(gelu(c_fc(ln_2(x1)))))."""
     mlp = blk.mlp
     d = _dropout_of(blk)
-    xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
+    xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS, dtype=_dt(blk))
     h, pre = G.linear_fwd_gelu(xn2, mlp.c_fc.weight.w16, mlp.c_fc.bias)
     x2 = G.linear_fwd_resid(h, mlp.c_proj.weight.w16, mlp.c_proj.bias, x1,
                             drop=(d[0], 4 * d[1] + 2, d[2], 0) if d else None)
@@ -123,10 +129,11 @@ def _mlp_fwd(blk, x1: torch.Tensor, keep: bool):
 
 
 def _mlp_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, ws: dict):
-    """In place: dres (fp32) / dres16 (bf16) go from d(x2) to d(x1)."""
+    """In place: dres (fp32) / dres16 (16-bit) go from d(x2) to d(x1)."""
     mlp = blk.mlp
     x1, xn2, m2, r2, pre, h, d = saved
-    dout16 = K.dropout_bf16(dres, d[0], 4 * d[1] + 2, d[2]) if d else dres16  # gradient at c_proj's output
+    # gradient at c_proj's output
+    dout16 = K.dropout_bf16(dres, d[0], 4 * d[1] + 2, d[2], dtype=dres16.dtype) if d else dres16
     dpre = G.linear_dgrad(dout16, mlp.c_proj.weight.w16, gelu_pre=pre)
     G.linear_wgrad(dout16, h, out=mlp.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(dout16, mlp.c_proj.bias.main_grad)
@@ -143,7 +150,8 @@ def _attn_bwd(blk, saved, dres: torch.Tensor, dres16: torch.Tensor, B: int, T: i
     """In place: dres / dres16 go from d(x1) to d(x)."""
     attn = blk.attn
     x, xn, m1, r1, qkv, y, lse, d = saved
-    dout16 = K.dropout_bf16(dres, d[0], 4 * d[1] + 1, d[2]) if d else dres16  # gradient at c_proj's output
+    # gradient at c_proj's output
+    dout16 = K.dropout_bf16(dres, d[0], 4 * d[1] + 1, d[2], dtype=dres16.dtype) if d else dres16
     dy = G.linear_dgrad(dout16, attn.c_proj.weight.w16)
     G.linear_wgrad(dout16, y, out=attn.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(dout16, attn.c_proj.bias.main_grad)
@@ -248,7 +256,7 @@ class _Body(torch.autograd.Function):
 
         B, T = ctx.B, ctx.T
         dres = dx.contiguous().clone()
-        dres16 = K.f32_to_bf16(dres)
+        dres16 = K.f32_to_bf16(dres, dtype=_dt(ctx.blocks[0]))
         M, H = dres.shape
         ws = {"ln_scratch": _ln_scratch(M, H, dres.device)}
         if daux is None:
@@ -292,11 +300,12 @@ CE_FUSED = os.environ.get("HB_CE_FUSED", "1") == "1"
 
 class _Head(torch.autograd.Function):
     @staticmethod
-    def forward(ctx, x, ln_w, ln_b, wte, targets, V, want_logits, grad_hint=1.0):
+    def forward(ctx, x, ln_w, ln_b, wte, targets, V, want_logits, grad_hint=1.0, grad_scale=None):
         M, H = x.shape
         Vp = _vpad(V)
-        xn, mean, rstd = K.layernorm_fwd(x, ln_w, ln_b, LN_EPS)
-        logits = torch.empty(M, Vp, device=x.device, dtype=torch.bfloat16)
+        dt = wte.w16.dtype
+        xn, mean, rstd = K.layernorm_fwd(x, ln_w, ln_b, LN_EPS, dtype=dt)
+        logits = torch.empty(M, Vp, device=x.device, dtype=dt)
         G.gemm(xn, wte.w16, logits, Vp, G.EPI_BF16, False, False)
         logits_out = logits[:, :V].float() if want_logits else None
         if targets is None:
@@ -308,8 +317,11 @@ class _Head(torch.autograd.Function):
         ctx.ce_fused = CE_FUSED and not want_logits
         if ctx.ce_fused:
             # the gradient is written now, scaled for the upstream gradient the caller expects
-            # (grad_hint); backward corrects it only if the actual one differs
+            # (grad_hint, times the fp16 loss scale the caller multiplies the loss by);
+            # backward corrects it only if the actual one differs
             expected = torch.full((1,), float(grad_hint), device=x.device, dtype=torch.float32)
+            if grad_scale is not None:
+                expected = expected * grad_scale
             loss, lse = K.cross_entropy_fused_(logits, V, targets, (expected / n_valid).contiguous())
             n_valid = expected
         else:
@@ -333,21 +345,25 @@ class _Head(torch.autograd.Function):
         dxn = G.linear_dgrad(dlv, ctx.wte.w16, f32=True)
         G.linear_wgrad(dl, xn, out=ctx.wte.main_grad, accumulate=True, n_rows=V)
         dx = torch.empty_like(x)
-        dx16 = torch.empty(x.shape, device=x.device, dtype=torch.bfloat16)
+        dx16 = torch.empty(x.shape, device=x.device, dtype=xn.dtype)
         zero = torch.zeros_like(x)
         K.layernorm_bwd(dxn, x, mean, rstd, ctx.ln_w, zero, dx, dx16, ctx.ln_w.main_grad, ctx.ln_b.main_grad)
-        return dx, None, None, None, None, None, None, None
+        return dx, None, None, None, None, None, None, None, None
 
 
 def head_fused(ln_f, wte: torch.nn.Parameter, x: torch.Tensor, targets: Optional[torch.Tensor], V: int,
-               want_logits: bool = True, grad_hint: float = 1.0):
-    """ln_f -> lm_head (tied to wte) -> cross-entropy. Returns (logits fp32 | None, loss | None)."""
+               want_logits: bool = True, grad_hint: float = 1.0, grad_scale: Optional[torch.Tensor] = None):
+    """ln_f -> lm_head (tied to wte) -> cross-entropy. Returns (logits fp32 | None, loss | None).
+
+    ``grad_hint`` / ``grad_scale``: the upstream gradient the caller will send (a float,
+    times an optional device scalar such as the fp16 loss scale)."""
     B, T, H = x.shape
     x2 = x.reshape(B * T, H)
     if x2.dtype != torch.float32:
         x2 = x2.float()
     t = targets.reshape(-1).contiguous() if targets is not None else None
-    loss, logits = _Head.apply(x2.contiguous(), ln_f.weight, ln_f.bias, wte, t, V, want_logits, grad_hint)
+    loss, logits = _Head.apply(x2.contiguous(), ln_f.weight, ln_f.bias, wte, t, V, want_logits, grad_hint,
+                               grad_scale)
     if logits is not None:
         logits = logits.view(B, T, V)
     return logits, (loss if targets is not None else None)
@@ -361,7 +377,8 @@ def gpt_forward_fused(model, idx: torch.Tensor, targets: Optional[torch.Tensor],
     x = embed_fused(model.tr.wte.weight, model.tr.wpe.weight, idx)
     x, aux = blocks_fused(model.tr.h, x, cfg, recompute=getattr(model, "recompute", False))
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x, targets, cfg.vocab_size,
-                              want_logits=return_logits, grad_hint=getattr(model, "loss_grad_hint", 1.0))
+                              want_logits=return_logits, grad_hint=getattr(model, "loss_grad_hint", 1.0),
+                              grad_scale=getattr(model, "loss_grad_scale", None))
     return logits, loss, aux
 
 
@@ -384,7 +401,8 @@ def _gpt_forward_fused_tp(model, idx, targets):
     x, aux = blocks_fused_tp(model.tr.h, x.reshape(Ms, -1), cfg, topo, B, T)
     tgt = targets.reshape(-1)[r0:r0 + Ms].view(Bs, T) if targets is not None else None
     logits, loss = head_fused(model.tr.ln_f, model.lm_head.weight, x.view(Bs, T, -1), tgt, cfg.vocab_size,
-                              want_logits=False, grad_hint=getattr(model, "loss_grad_hint", 1.0) / topo.tp)
+                              want_logits=False, grad_hint=getattr(model, "loss_grad_hint", 1.0) / topo.tp,
+                              grad_scale=getattr(model, "loss_grad_scale", None))
     # Each TP rank routes only its token shard; the shard aux losses / tp sum to
     # the mean over shards (the dense aux uses all tokens at once).
     return None, (loss / topo.tp if loss is not None else None), aux / topo.tp

@@ -97,7 +97,7 @@ def _peer_sum(buf, addend, dst, n: int) -> None:
 
 
 def moe_route_and_experts(moe, xn2: torch.Tensor, flat=None):
-    """Router + permutation + the two grouped expert GEMMs for bf16 xn2 [N, H],
+    """Router + permutation + the two grouped expert GEMMs for 16-bit xn2 [N, H] (bf16 or fp16),
     over this rank's experts.
 
     Returns (aux, state) where state holds everything combine / backward need."""
@@ -127,13 +127,13 @@ def moe_route_and_experts(moe, xn2: torch.Tensor, flat=None):
         ext.moe_local_offsets(off, e0, El, off_l)
     # capacity of this rank's rows: every local segment padded to 128 rows
     R = (N * Kk + El * (PAD - 1) + PAD - 1) // PAD * PAD
-    xp = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
+    xp = torch.zeros(R, H, device=dev, dtype=xn2.dtype)
     ext.moe_gather(xn2, pos, Kk, xp, off, e0, e1)
     w1, _, w2, _ = _stacks(moe, flat)
-    hp = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
-    prep = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+    hp = torch.empty(R, I, device=dev, dtype=xn2.dtype)
+    prep = torch.empty(R, I, device=dev, dtype=xn2.dtype)
     G.gemm(xp, w1, hp, I, G.EPI_BF16_GELU, False, False, aux=prep, grp=(1, off_l, El, I, 0))
-    yp = torch.empty(R, H, device=dev, dtype=torch.bfloat16)
+    yp = torch.empty(R, H, device=dev, dtype=xn2.dtype)
     G.gemm(hp, w2, yp, H, G.EPI_BF16, False, False, grp=(1, off_l, El, H, 0))
     return aux, (probs, topi, topw, counts, off, off_l, pos, xp, hp, prep, yp)
 
@@ -175,9 +175,9 @@ def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: t
     else:
         dxn2_part = torch.empty(N, H, device=dev, dtype=torch.float32)
         dw = torch.empty(N, Kk, device=dev, dtype=torch.float32)
-    dyp = torch.zeros(R, H, device=dev, dtype=torch.bfloat16)
+    dyp = torch.zeros(R, H, device=dev, dtype=xn2.dtype)
     ext.moe_combine_bwd(dx_res, yp, pos, topw, dyp, dw, off, e0, e1)
-    dprep = torch.empty(R, I, device=dev, dtype=torch.bfloat16)
+    dprep = torch.empty(R, I, device=dev, dtype=xn2.dtype)
     G.gemm(dyp, w2, dprep, I, G.EPI_BF16_DGELU, False, True, aux=prep, grp=(1, off_l, El, H, 0))
     G.gemm(dyp, hp, g2, I, G.EPI_F32_ACC, True, True, grp=(2, off_l, El, 0, H))
     dxp = torch.empty(R, H, device=dev, dtype=torch.float32)
@@ -195,7 +195,7 @@ def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: t
     else:
         dxn2 = dxn2_part
     Ep = (E + 7) // 8 * 8  # row stride of the logits gradient: 16-byte aligned for TMA
-    dlog = torch.zeros(N, Ep, device=dev, dtype=torch.bfloat16)
+    dlog = torch.zeros(N, Ep, device=dev, dtype=xn2.dtype)
     ext.moe_router_bwd(probs, topi, topw, dw, daux.reshape(1).float().contiguous(), counts, moe.aux_loss_coef,
                        moe.router.gate.weight, dlog, dxn2)
     G.gemm(dlog[:, :E], xn2, moe.router.gate.weight.main_grad, H, G.EPI_F32_ACC, True, True)
@@ -205,7 +205,7 @@ def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: t
 def moe_sublayer_fwd(blk, flat, x1: torch.Tensor, keep: bool):
     """x1: fp32 residual [N, H] -> (x2 = x1 + MoE(ln_2(x1)) fp32, aux (0-d), saved)."""
     moe = blk.moe
-    xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS)
+    xn2, m2, r2 = K.layernorm_fwd(x1, blk.ln_2.weight, blk.ln_2.bias, LN_EPS, dtype=blk.ln_2.weight.w16.dtype)
     aux, state = moe_route_and_experts(moe, xn2, flat)
     x2 = moe_combine_fwd(moe, state, x1)
     saved = (x1, xn2, m2, r2, state) if keep else None

@@ -51,11 +51,12 @@ LN_EPS = 1e-5
 class TPComm:
     """Symmetric buffers and barriers of one TP group for one activation shape."""
 
-    def __init__(self, topo, Ms: int, H: int, device: torch.device):
+    def __init__(self, topo, Ms: int, H: int, device: torch.device, dtype: torch.dtype = torch.bfloat16):
         from ..parallel.symm import SymmetricBuffer
 
         g = topo.tp_group
         self.tp, self.rank, self.Ms, self.H = topo.tp, topo.tp_rank, Ms, H
+        self.dtype = dtype  # 16-bit format of the gathered / reduce-scattered activations
         self.src = [SymmetricBuffer(g, Ms * H * 2, device) for _ in range(2)]
         self.recv16 = SymmetricBuffer(g, self.tp * Ms * H * 2, device)
         self.recv32 = SymmetricBuffer(g, self.tp * Ms * H * 4, device)
@@ -71,10 +72,10 @@ class TPComm:
         self.src[0].barrier()
 
     def src_view(self, i: int) -> torch.Tensor:
-        return self.src[i].tensor(torch.bfloat16, self.Ms * self.H).view(self.Ms, self.H)
+        return self.src[i].tensor(self.dtype, self.Ms * self.H).view(self.Ms, self.H)
 
     def recv16_all(self) -> torch.Tensor:
-        return self.recv16.tensor(torch.bfloat16, self.tp * self.Ms * self.H).view(self.tp * self.Ms, self.H)
+        return self.recv16.tensor(self.dtype, self.tp * self.Ms * self.H).view(self.tp * self.Ms, self.H)
 
     def recv32_all(self) -> torch.Tensor:
         return self.recv32.tensor(torch.float32, self.tp * self.Ms * self.H).view(self.tp * self.Ms, self.H)
@@ -92,14 +93,14 @@ class TPComm:
 _COMMS = {}
 
 
-def get_comm(topo, Ms: int, H: int, device) -> TPComm:
-    key = (id(topo.tp_group), Ms, H, str(device))
+def get_comm(topo, Ms: int, H: int, device, dtype: torch.dtype = torch.bfloat16) -> TPComm:
+    key = (id(topo.tp_group), Ms, H, str(device), dtype)
     if key not in _COMMS:
-        _COMMS[key] = TPComm(topo, Ms, H, device)
+        _COMMS[key] = TPComm(topo, Ms, H, device, dtype)
     return _COMMS[key]
 
 
-def _empty(*shape, dtype=torch.bfloat16, device=None):
+def _empty(*shape, dtype, device=None):
     return torch.empty(*shape, dtype=dtype, device=device)
 
 
@@ -108,7 +109,7 @@ def _resid_dropout(comm: TPComm, x_s: torch.Tensor, bias, d, site: int) -> torch
     token shard (global token rows from tp_rank * Ms, so the mask is the single-GPU one)."""
     t = torch.empty_like(x_s)
     K.resid_sum_ln(comm.zeros(), comm.recv16_all(), comm.tp, bias, t)
-    kept = K.dropout_bf16(t, d[0], site, d[2], row0=comm.rank * comm.Ms)
+    kept = K.dropout_bf16(t, d[0], site, d[2], row0=comm.rank * comm.Ms, dtype=comm.dtype)
     return x_s + kept.float()
 
 
@@ -133,9 +134,9 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
     r1 = _empty(Ms, dtype=torch.float32, device=dev)
     ext.layernorm_fwd(x_s, blk.ln_1.weight, blk.ln_1.bias, xn_s, m1, r1, LN_EPS)
     comm.barrier()
-    xn_full = _empty(M, H, device=dev)
+    xn_full = _empty(M, H, dtype=comm.dtype, device=dev)
     n_qkv = 3 * attn.h_tp
-    qkv = _empty(M, n_qkv, device=dev)
+    qkv = _empty(M, n_qkv, dtype=comm.dtype, device=dev)
     G.gemm(xn_full, attn.c_attn.weight.w16, qkv, n_qkv, G.EPI_BF16, False, False, bias=attn.c_attn.bias,
            ag=comm.ag(0))
     y, lse = K.attention_fwd(qkv, B, T, nh, drop=_attn_drop(attn, comm, d), head_dim=attn.dh)
@@ -163,10 +164,10 @@ def tp_block_fwd(blk, comm: TPComm, x_s: torch.Tensor, B: int, T: int, keep: boo
         K.resid_sum_ln(x_s, comm.recv16_all(), tp, attn.c_proj.bias, x1_s, blk.ln_2.weight, blk.ln_2.bias, xn2_s,
                        m2, r2, LN_EPS)
     comm.barrier()
-    xn2_full = _empty(M, H, device=dev)
+    xn2_full = _empty(M, H, dtype=comm.dtype, device=dev)
     n_fc = mlp.c_fc.out_per_partition
-    h = _empty(M, n_fc, device=dev)
-    pre = _empty(M, n_fc, device=dev)
+    h = _empty(M, n_fc, dtype=comm.dtype, device=dev)
+    pre = _empty(M, n_fc, dtype=comm.dtype, device=dev)
     G.gemm(xn2_full, mlp.c_fc.weight.w16, h, n_fc, G.EPI_BF16_GELU, False, False, bias=mlp.c_fc.bias, aux=pre,
            ag=comm.ag(1))
     G.gemm(h, mlp.c_proj.weight.w16, comm.recv16_all(), H, G.EPI_BF16, False, False, rs=comm.rs16())
@@ -202,8 +203,8 @@ def tp_block_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
     if d:  # the gathered gradient of c_proj's output is the masked residual gradient
         K.dropout_bf16(dres, d[0], 4 * d[1] + 2, d[2], row0=comm.rank * Ms, out=comm.src_view(k))
     comm.barrier()
-    dx2_full = _empty(M, H, device=dev)
-    dpre = _empty(M, n_fc, device=dev)
+    dx2_full = _empty(M, H, dtype=comm.dtype, device=dev)
+    dpre = _empty(M, n_fc, dtype=comm.dtype, device=dev)
     G.gemm(dx2_full, mlp.c_proj.weight.w16, dpre, n_fc, G.EPI_BF16_DGELU, False, True, aux=pre, ag=comm.ag(k))
     G.linear_wgrad(dx2_full, h, out=mlp.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(comm.src_view(k), mlp.c_proj.bias.main_grad)  # token-shard partial; summed over TP per step
@@ -229,8 +230,8 @@ def _tp_attn_bwd(blk, comm: TPComm, saved, dres: torch.Tensor, k: int, B: int, T
     if d:
         K.dropout_bf16(dres, d[0], 4 * d[1] + 1, d[2], row0=comm.rank * Ms, out=comm.src_view(k))
     comm.barrier()
-    dx1_full = _empty(M, H, device=dev)
-    dy = _empty(M, attn.h_tp, device=dev)
+    dx1_full = _empty(M, H, dtype=comm.dtype, device=dev)
+    dy = _empty(M, attn.h_tp, dtype=comm.dtype, device=dev)
     G.gemm(dx1_full, attn.c_proj.weight.w16, dy, attn.h_tp, G.EPI_BF16, False, True, ag=comm.ag(k))
     G.linear_wgrad(dx1_full, y, out=attn.c_proj.weight.main_grad, accumulate=True)
     K.colsum_bf16(comm.src_view(k), attn.c_proj.bias.main_grad)
@@ -303,5 +304,5 @@ def tp_supported(cfg, topo, B: int, T: int) -> Tuple[bool, str]:
 
 def blocks_fused_tp(blocks, x_s: torch.Tensor, cfg, topo, B: int, T: int):
     """Returns (x_L token shard, aux loss of this shard's MoE layers)."""
-    comm = get_comm(topo, x_s.shape[0], x_s.shape[1], x_s.device)
+    comm = get_comm(topo, x_s.shape[0], x_s.shape[1], x_s.device, blocks[0].ln_1.weight.w16.dtype)
     return _TPBody.apply(x_s.contiguous(), list(blocks), comm, B, T)

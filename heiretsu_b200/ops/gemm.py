@@ -67,21 +67,21 @@ def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=N
 
 def linear_fwd(x: torch.Tensor, w: torch.Tensor, bias: Optional[torch.Tensor] = None, *,
                out: Optional[torch.Tensor] = None, n: Optional[int] = None) -> torch.Tensor:
-    """bf16 y = x @ w^T + bias. `n` may exceed w.shape[0] (rows beyond are zero)."""
+    """y = x @ w^T + bias in x's 16-bit format. `n` may exceed w.shape[0] (rows beyond are zero)."""
     M = x.shape[0]
     N = int(n if n is not None else w.shape[0])
     if out is None:
-        out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+        out = torch.empty(M, N, device=x.device, dtype=x.dtype)
     return gemm(x, w, out, N, EPI_BF16, False, False, bias=bias)
 
 
 def linear_fwd_gelu(x, w, bias, *, out=None, pre=None):
-    """Returns (gelu(x @ w^T + b), x @ w^T + b), both bf16."""
+    """Returns (gelu(x @ w^T + b), x @ w^T + b), both in x's 16-bit format."""
     M, N = x.shape[0], w.shape[0]
     if out is None:
-        out = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+        out = torch.empty(M, N, device=x.device, dtype=x.dtype)
     if pre is None:
-        pre = torch.empty(M, N, device=x.device, dtype=torch.bfloat16)
+        pre = torch.empty(M, N, device=x.device, dtype=x.dtype)
     gemm(x, w, out, N, EPI_BF16_GELU, False, False, bias=bias, aux=pre)
     return out, pre
 
@@ -99,9 +99,9 @@ def linear_dgrad(dy, w, *, out=None, gelu_pre=None, f32=False):
     """dx = dy @ w (w: [N, K]); with `gelu_pre`, dx *= gelu'(gelu_pre)."""
     M, K = dy.shape[0], w.shape[1]
     if gelu_pre is not None:
-        epi, dt = EPI_BF16_DGELU, torch.bfloat16
+        epi, dt = EPI_BF16_DGELU, dy.dtype
     else:
-        epi, dt = (EPI_F32, torch.float32) if f32 else (EPI_BF16, torch.bfloat16)
+        epi, dt = (EPI_F32, torch.float32) if f32 else (EPI_BF16, dy.dtype)
     if out is None:
         out = torch.empty(M, K, device=dy.device, dtype=dt)
     return gemm(dy, w, out, K, epi, False, True, aux=gelu_pre, block_n=_bn_f32_out(K) if epi == EPI_F32 else None)

@@ -8,8 +8,8 @@ counted once) rather than each shard's local norm.
 
 One step = sum-of-squares reductions (one per replication class) ->
 optional all-reduce of the squared norm over the model-parallel group ->
-clip coefficient -> one AdamW kernel that also refreshes the bf16 GEMM
-shadow. Within one node the model-parallel sum runs over NVLink in a
+clip coefficient -> one AdamW kernel that also refreshes the 16-bit GEMM
+shadow (bf16, or fp16 with a device loss scale: ``DeviceLossScaler``). Within one node the model-parallel sum runs over NVLink in a
 kernel, so the whole step stays inside one captured CUDA graph. No host
 synchronisation: the per-step hyper-parameters are uploaded asynchronously
 from pinned memory, the coefficient stays on the device, and a non-finite norm
@@ -27,14 +27,59 @@ from .ops import kernels as K
 from .parallel.flat import FlatParams
 
 
+class DeviceLossScaler:
+    """Dynamic loss scaling for fp16 with torch.cuda.amp.GradScaler's rule and
+    defaults (reference train.py:356, :436-452), kept on the device so a captured
+    step needs no host synchronisation: ``state`` = [scale, finite steps in a row].
+
+    ``scale(loss)`` multiplies by the device scale before backward; the optimizer
+    unscales inside its clip coefficient (``K.clip_coef(..., loss_scale)``), skips
+    a step whose gradient norm is not finite (the coefficient is NaN), and then
+    calls ``update_after(coef)``: backoff x0.5 after a skipped step, growth x2
+    after ``growth_interval`` finite steps in a row."""
+
+    def __init__(self, device, init_scale: float = 2.0 ** 16, growth_factor: float = 2.0,
+                 backoff_factor: float = 0.5, growth_interval: int = 2000):
+        self.state = torch.tensor([init_scale, 0.0], device=device, dtype=torch.float32)
+        self.growth_factor, self.backoff_factor, self.growth_interval = growth_factor, backoff_factor, growth_interval
+
+    @property
+    def scale_tensor(self) -> torch.Tensor:
+        """The scale as a 1-element device tensor (a view: replays read the current value)."""
+        return self.state[0:1]
+
+    def scale(self, t: torch.Tensor) -> torch.Tensor:
+        return t * self.state[0]
+
+    def is_enabled(self) -> bool:
+        return True
+
+    def get_scale(self) -> float:
+        return float(self.state[0].item())
+
+    def update_after(self, coef: torch.Tensor) -> None:
+        K.loss_scale_update(coef, self.state, self.growth_factor, self.backoff_factor, self.growth_interval)
+
+    # GradScaler's checkpoint keys, so either kind of run resumes the other's scale.
+    def state_dict(self) -> dict:
+        st = self.state.cpu()
+        return {"scale": float(st[0]), "growth_factor": self.growth_factor, "backoff_factor": self.backoff_factor,
+                "growth_interval": self.growth_interval, "_growth_tracker": int(st[1])}
+
+    def load_state_dict(self, sd: dict) -> None:
+        self.state.copy_(torch.tensor([float(sd["scale"]), float(sd.get("_growth_tracker", 0))]))
+
+
 class FusedAdamW:
     def __init__(self, flat: FlatParams, lr: float = 3e-4, betas=(0.9, 0.95), eps: float = 1e-8,
                  weight_decay: float = 0.1, max_grad_norm: float = 0.0, mp_group: Optional[dist.ProcessGroup] = None,
-                 mp_symm=None):
+                 mp_symm=None, scaler: Optional[DeviceLossScaler] = None):
         """``mp_symm``: optional peer-mapped buffer (>= 16 bytes) over ``mp_group``;
         with it the squared norm is summed over NVLink by a kernel (graph-capturable)
-        instead of an NCCL all-reduce."""
+        instead of an NCCL all-reduce. ``scaler``: the fp16 loss scale the gradients
+        carry (unscaled in the clip coefficient, updated after each step)."""
         self.flat = flat
+        self.scaler = scaler
         self.lr, self.betas, self.eps, self.wd = lr, tuple(betas), eps, weight_decay
         self.max_grad_norm = max_grad_norm
         self.mp_group = mp_group
@@ -72,7 +117,8 @@ class FusedAdamW:
             self.norm2.copy_(self._norm_slot[0])
         elif self.mp_group is not None and dist.is_initialized() and dist.get_world_size(self.mp_group) > 1:
             dist.all_reduce(self.norm2, group=self.mp_group)
-        K.clip_coef(self.norm2, self.max_grad_norm, self.coef, self.norm)
+        K.clip_coef(self.norm2, self.max_grad_norm, self.coef, self.norm,
+                    self.scaler.scale_tensor if self.scaler is not None else None)
         return self.norm
 
     def prepare_step(self) -> None:
@@ -104,6 +150,8 @@ class FusedAdamW:
         """Device part of a step (no host synchronisation; graph-capturable)."""
         self.compute_grad_norm()
         K.adamw_step(self.flat.data, self.flat.grad, self.m, self.v, self.flat.data16, self.hyper, self.coef)
+        if self.scaler is not None:
+            self.scaler.update_after(self.coef)
 
     def step(self) -> None:
         self.prepare_step()

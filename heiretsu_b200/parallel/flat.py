@@ -1,9 +1,9 @@
-"""Flat parameter / gradient / bf16-shadow buffers.
+"""Flat parameter / gradient / 16-bit-shadow buffers.
 
 All parameters of a module are moved into one fp32 buffer (each parameter
 becomes a view, so ``state_dict`` and the module code are unchanged), with
-a matching fp32 gradient buffer (``p.main_grad``) and a bf16 shadow
-(``p.w16``) that the GEMMs read. One flat layout means one AdamW kernel, one
+a matching fp32 gradient buffer (``p.main_grad``) and a 16-bit shadow
+(``p.w16``, bf16 or fp16) that the GEMMs read. One flat layout means one AdamW kernel, one
 gradient-norm reduction and large, contiguous DP reduction buckets.
 
 Parameters are grouped by how they are replicated across model-parallel
@@ -48,8 +48,11 @@ def _stack_experts(named: List[Tuple[str, torch.nn.Parameter]]) -> List[Tuple[st
 class FlatParams:
     def __init__(self, module: torch.nn.Module, device: torch.device,
                  weight_of: Optional[Callable[[str, torch.nn.Parameter], float]] = None, grad_group=None,
-                 tp_group=None, tp_sum_of: Optional[Callable[[str, torch.nn.Parameter], bool]] = None):
-        """``tp_sum_of(name, p)``: whether p's gradient is a per-token-shard partial
+                 tp_group=None, tp_sum_of: Optional[Callable[[str, torch.nn.Parameter], bool]] = None,
+                 dtype16: torch.dtype = torch.bfloat16):
+        """``dtype16``: format of the weight shadows and so of every activation of the
+        fused path (bf16, or fp16 for --amp fp16).
+        ``tp_sum_of(name, p)``: whether p's gradient is a per-token-shard partial
         that must be summed over the TP group (TP-replicated parameters under
         sequence-sharded TP). Parameters are grouped by (norm weight, tp_sum),
         and ``tp_sum[i]`` tells it for ``ranges[i]``."""
@@ -97,7 +100,7 @@ class FlatParams:
             self.grad = _load().tensor_from_ptr(raw, total, torch.float32, device.index)
         else:
             self.grad = torch.zeros(total, device=device, dtype=torch.float32)
-        self.data16 = torch.zeros(total, device=device, dtype=torch.bfloat16)
+        self.data16 = torch.zeros(total, device=device, dtype=dtype16)
         self.params: List[torch.nn.Parameter] = []
         self.names: List[str] = []
         self.offsets: List[int] = []
@@ -132,7 +135,7 @@ class FlatParams:
                 self.grad[off:off + n * len(params)].view(rows, cols))
 
     def refresh_bf16(self) -> None:
-        """Re-derive the bf16 shadow from the fp32 master (after init / checkpoint load)."""
+        """Re-derive the 16-bit shadow from the fp32 master (after init / checkpoint load)."""
         if self.device.type == "cuda":
             from ..ops.kernels import f32_to_bf16
             f32_to_bf16(self.data, self.data16)

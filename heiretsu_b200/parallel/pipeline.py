@@ -194,10 +194,12 @@ class StageModule(nn.Module):
                 r0, Ms = tp_shard_rows(self.topo, Bs * self.tp, T)
                 tgt = targets.reshape(-1)[r0:r0 + Ms].view(Bs, T) if targets is not None else None
                 _, loss = head_fused(self.ln_f, self.lm_head.weight, x, tgt, self.cfg.vocab_size, want_logits=False,
-                                     grad_hint=getattr(self, "loss_grad_hint", 1.0) / self.tp)
+                                     grad_hint=getattr(self, "loss_grad_hint", 1.0) / self.tp,
+                                     grad_scale=getattr(self, "loss_grad_scale", None))
                 return None, (loss / self.tp if loss is not None else None)
             return head_fused(self.ln_f, self.lm_head.weight, x, targets, self.cfg.vocab_size,
-                              want_logits=want_logits, grad_hint=getattr(self, "loss_grad_hint", 1.0))
+                              want_logits=want_logits, grad_hint=getattr(self, "loss_grad_hint", 1.0),
+                              grad_scale=getattr(self, "loss_grad_scale", None))
         x = self.ln_f(x)
         if targets is not None and not want_logits and not torch.is_autocast_enabled(x.device.type):
             from ..models.gpt import head_cross_entropy

@@ -393,13 +393,14 @@ class Engine:
         want = args.engine
         if want == "fused" and not ok:
             raise ValueError(f"--engine fused: {why}")
-        if want == "fused" and (device.type != "cuda" or self.amp != "bf16"):
-            raise ValueError("--engine fused needs --device cuda and --amp bf16")
-        self.fused = (want in ("auto", "fused")) and ok and device.type == "cuda" and self.amp == "bf16"
-        # why an automatic choice ended on the plain engine (logged at start)
+        if want == "fused" and (device.type != "cuda" or self.amp not in ("bf16", "fp16")):
+            raise ValueError("--engine fused needs --device cuda and --amp bf16 or fp16")
+        self.fused = (want in ("auto", "fused")) and ok and device.type == "cuda" and self.amp in ("bf16", "fp16")
+        # why an automatic choice ended on the plain engine (logged at start). --amp none
+        # stays on the plain engine: it is the fp32 mode that matches the reference to 1e-4.
         self.plain_reason = None
         if not self.fused and want == "auto" and device.type == "cuda":
-            self.plain_reason = why if not ok else "the fused engine runs with --amp bf16"
+            self.plain_reason = why if not ok else "--amp none runs the plain fp32 engine (the fused one is 16-bit)"
         if self.fused:
             from .ops._C import load as _load
             _load()  # fail loudly if the extension is missing
@@ -433,13 +434,21 @@ class Engine:
             # else (a multi-node job) as NCCL all-reduces.
             use_p2p = (topo.dp > 1 and os.environ.get("HB_DP_BACKEND", "p2p") == "p2p"
                        and on_one_node(topo, topo.dp_ranks))
+            from .optim import DeviceLossScaler
+
             self.flat = FlatParams(self.module, device, weight_of=replication_weight(topo, self.tied is not None),
                                    grad_group=topo.dp_group if use_p2p else None,
                                    tp_group=topo.tp_group if topo.tp > 1 else None,
-                                   tp_sum_of=lambda n, p: topo.tp > 1 and not getattr(p, "tp_sharded", False))
+                                   tp_sum_of=lambda n, p: topo.tp > 1 and not getattr(p, "tp_sharded", False),
+                                   dtype16=torch.float16 if self.amp == "fp16" else torch.bfloat16)
             self.module.fused = True
-            # upstream gradient of the data loss in a training step: (loss + aux) / accumulation
+            # fp16: activations and weight shadows in fp16, the loss scaled on the device
+            # (GradScaler's rule) and unscaled inside the optimizer's clip coefficient
+            fused_scaler = DeviceLossScaler(device) if self.amp == "fp16" else None
+            # upstream gradient of the data loss in a training step: (loss + aux) / accumulation,
+            # times the loss scale under fp16
             self.module.loss_grad_hint = 1.0 / args.grad_accum_steps
+            self.module.loss_grad_scale = fused_scaler.scale_tensor if fused_scaler is not None else None
             clip_group = self.mp_group if args.clip_mode == "global" else None
             mp_symm = None
             if clip_group is not None and device.type == "cuda" and on_one_node(topo, topo.model_parallel_ranks()):
@@ -447,8 +456,8 @@ class Engine:
                 mp_symm = SymmetricBuffer(clip_group, 16, device)
             self.optimizer = FusedAdamW(self.flat, lr=args.learning_rate, betas=args.betas,
                                         weight_decay=args.weight_decay, max_grad_norm=args.grad_clip,
-                                        mp_group=clip_group, mp_symm=mp_symm)
-            self.scaler = None
+                                        mp_group=clip_group, mp_symm=mp_symm, scaler=fused_scaler)
+            self.scaler = fused_scaler
         elif getattr(args, "zero_stage", 0):
             from .parallel.zero import ZeroAdamW
 
@@ -545,7 +554,8 @@ class Engine:
             _, loss, aux_mb = self.forward_module(x, y, return_logits=False)
             if i == accum - 1 and self.reducer is not None and self.overlap_dp:
                 self.reducer.arm()  # reduce each block's gradients while backward continues
-            ((loss + aux_mb) / accum).backward()
+            combined = (loss + aux_mb) / accum
+            (self.scaler.scale(combined) if self.scaler is not None else combined).backward()
             aux = aux + aux_mb.detach().float()
             loss_sum = loss_sum + loss.detach().float()
         if self.reducer is not None:
@@ -726,7 +736,10 @@ class Engine:
     def optimizer_state(self) -> dict:
         """AdamW moments keyed by parameter name, for either engine (see FusedAdamW.moments_by_name)."""
         if self.fused:
-            return self.optimizer.moments_by_name()
+            out = self.optimizer.moments_by_name()
+            if self.scaler is not None:  # fp16: the device loss scale
+                out["scaler"] = self.scaler.state_dict()
+            return out
         if hasattr(self.optimizer, "moments_by_name"):  # ZeroAdamW: gathers the DP shards (collective)
             out = self.optimizer.moments_by_name()
             if self.scaler is not None and self.scaler.is_enabled():
@@ -750,7 +763,7 @@ class Engine:
             return
         if self.fused or hasattr(self.optimizer, "load_moments_by_name"):
             self.optimizer.load_moments_by_name(st)
-            if not self.fused and "scaler" in st and self.scaler is not None and self.scaler.is_enabled():
+            if "scaler" in st and self.scaler is not None and self.scaler.is_enabled():
                 self.scaler.load_state_dict(st["scaler"])
             return
         for name, p in self.module.named_parameters():

@@ -45,7 +45,7 @@ def linear_fwd(x, w, bias=None, *, out=None, n=None):
         y = y + bias.float()
     if N > y.shape[1]:
         y = F.pad(y, (0, N - y.shape[1]))
-    y = y.bfloat16()
+    y = y.to(x.dtype)
     if out is not None:
         out.copy_(y)
         return out
@@ -53,8 +53,8 @@ def linear_fwd(x, w, bias=None, *, out=None, n=None):
 
 
 def linear_fwd_gelu(x, w, bias, *, out=None, pre=None):
-    p = x.float() @ w.float().t() + bias.float()
-    return _gelu(p).bfloat16(), p.bfloat16()
+    p = (x.float() @ w.float().t() + bias.float()).to(x.dtype).float()
+    return _gelu(p).to(x.dtype), p.to(x.dtype)
 
 
 def linear_fwd_resid(x, w, bias, resid, *, out=None, drop=None):
@@ -72,8 +72,8 @@ def linear_fwd_resid(x, w, bias, resid, *, out=None, drop=None):
 def linear_dgrad(dy, w, *, out=None, gelu_pre=None, f32=False):
     d = dy.float() @ w.float()
     if gelu_pre is not None:
-        return (d * _gelu_grad(gelu_pre.float())).bfloat16()
-    return d if f32 else d.bfloat16()
+        return (d * _gelu_grad(gelu_pre.float())).to(dy.dtype)
+    return d if f32 else d.to(dy.dtype)
 
 
 def linear_wgrad(dy, x, *, out=None, accumulate=False, n_rows=None):
@@ -93,18 +93,18 @@ def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=N
     """Only the plain bf16 C = A B^T form (the lm_head) is used on the single-GPU path."""
     assert epi == 0 and not a_mn and not b_mn and ag is None and rs is None and grp is None
     y = a.float() @ b.float().t()
-    c[:, :y.shape[1]].copy_(y.bfloat16())
+    c[:, :y.shape[1]].copy_(y.to(c.dtype))
     if c.shape[1] > y.shape[1]:
         c[:, y.shape[1]:].zero_()
     return c
 
 
 # ---- LayerNorm, dropout, conversions ------------------------------------------
-def layernorm_fwd(x, w, b, eps=1e-5):
+def layernorm_fwd(x, w, b, eps=1e-5, dtype=torch.bfloat16):
     mean = x.mean(-1)
     rstd = torch.rsqrt(x.var(-1, unbiased=False) + eps)
     y = (x - mean[:, None]) * rstd[:, None] * w + b
-    return y.bfloat16(), mean, rstd
+    return y.to(dtype), mean, rstd
 
 
 def layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dgamma, dbeta, scratch=None, dy_srcs=1):
@@ -117,21 +117,21 @@ def layernorm_bwd(dy, x, mean, rstd, w, dres_in, dres, dres16, dgamma, dbeta, sc
     dx = rstd[:, None] * (gw - gw.mean(-1, keepdim=True) - xh * (gw * xh).mean(-1, keepdim=True))
     new = dres_in + dx
     dres.copy_(new)
-    dres16.copy_(new.bfloat16())
+    dres16.copy_(new.to(dres16.dtype))
 
 
-def dropout_bf16(g, seed, site, p, row0=0, out=None):
+def dropout_bf16(g, seed, site, p, row0=0, out=None, dtype=torch.bfloat16):
     m = DR.residual_mask(_seed(seed), site, g.shape[0], g.shape[1], p, row0).float()
-    y = (g.float() * m).bfloat16()
+    y = (g.float() * m).to(out.dtype if out is not None else dtype)
     if out is not None:
         out.copy_(y)
         return out
     return y
 
 
-def f32_to_bf16(x, out=None):
+def f32_to_bf16(x, out=None, dtype=torch.bfloat16):
     if out is None:
-        return x.bfloat16()
+        return x.to(dtype)
     out.copy_(x)
     return out
 
@@ -230,12 +230,24 @@ def sumsq(x, out, weight=1.0, accumulate=False):
         out.copy_(v)
 
 
-def clip_coef(norm2, max_norm, coef, norm=None):
-    n = norm2.sqrt()
+def clip_coef(norm2, max_norm, coef, norm=None, loss_scale=None):
+    inv_s = 1.0 / loss_scale.reshape(-1)[0] if loss_scale is not None else torch.ones(())
+    n = norm2.sqrt() * inv_s
     if norm is not None:
         norm.copy_(n)
     c = torch.clamp(max_norm / (n + 1e-6), max=1.0) if max_norm > 0 else torch.ones(())
-    coef.copy_(torch.where(torch.isfinite(n), c, torch.full((), float("nan"))))
+    coef.copy_(torch.where(torch.isfinite(n), c * inv_s, torch.full((), float("nan"))))
+
+
+def loss_scale_update(coef, state, growth=2.0, backoff=0.5, interval=2000):
+    if math.isnan(float(coef)):
+        state[0] *= backoff
+        state[1] = 0.0
+    else:
+        state[1] += 1.0
+        if state[1] >= interval:
+            state[0] *= growth
+            state[1] = 0.0
 
 
 def adamw_step(p, g, m, v, p16, hyper, coef):
@@ -243,7 +255,7 @@ def adamw_step(p, g, m, v, p16, hyper, coef):
     c = float(coef)
     if not math.isfinite(c):
         return
-    gg = g * c / gs
+    gg = g * c * gs
     p.mul_(1 - lr * wd)
     m.mul_(b1).add_(gg, alpha=1 - b1)
     v.mul_(b2).addcmul_(gg, gg, value=1 - b2)
@@ -254,7 +266,8 @@ def adamw_step(p, g, m, v, p16, hyper, coef):
 
 KERNELS = ["layernorm_fwd", "layernorm_bwd", "dropout_bf16", "f32_to_bf16", "colsum_bf16", "attention_fwd",
            "attention_bwd", "cross_entropy_fwd", "cross_entropy_bwd_", "cross_entropy_fused_",
-           "cross_entropy_rescale_", "embedding_fwd", "embedding_bwd", "sumsq", "clip_coef", "adamw_step"]
+           "cross_entropy_rescale_", "embedding_fwd", "embedding_bwd", "sumsq", "clip_coef", "loss_scale_update",
+           "adamw_step"]
 GEMMS = ["linear_fwd", "linear_fwd_gelu", "linear_fwd_resid", "linear_dgrad", "linear_wgrad", "gemm"]
 
 
@@ -277,10 +290,11 @@ class FakeTPComm:
     tensors; the in-kernel all-gather and reduce-scatter of the GEMM become
     all_gather calls in ``tp_gemm``; barriers are no-ops (gloo calls block)."""
 
-    def __init__(self, topo, Ms, H):
+    def __init__(self, topo, Ms, H, dtype=torch.bfloat16):
         self.tp, self.rank, self.Ms, self.H, self.group = topo.tp, topo.tp_rank, Ms, H, topo.tp_group
-        self.src = [torch.zeros(Ms, H, dtype=torch.bfloat16) for _ in range(2)]
-        self.r16 = torch.zeros(self.tp * Ms, H, dtype=torch.bfloat16)
+        self.dtype = dtype
+        self.src = [torch.zeros(Ms, H, dtype=dtype) for _ in range(2)]
+        self.r16 = torch.zeros(self.tp * Ms, H, dtype=dtype)
         self.r32 = torch.zeros(self.tp * Ms, H, dtype=torch.float32)
         self.zero32 = None
 
@@ -391,10 +405,10 @@ def emulate_tp(setattr_fn) -> None:
     setattr_fn(FT, "_ext", lambda: _FakeExt)
     comms = {}
 
-    def get_comm(topo, Ms, H, device):
-        key = (id(topo.tp_group), Ms, H)
+    def get_comm(topo, Ms, H, device, dtype=torch.bfloat16):
+        key = (id(topo.tp_group), Ms, H, dtype)
         if key not in comms:
-            comms[key] = FakeTPComm(topo, Ms, H)
+            comms[key] = FakeTPComm(topo, Ms, H, dtype)
         return comms[key]
 
     setattr_fn(FT, "get_comm", get_comm)

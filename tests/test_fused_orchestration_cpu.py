@@ -185,3 +185,42 @@ def test_emulated_fused_tp_matches_one_process(dropout):
     for dloss, worst in run_ranks(_worker_tp, 2, dropout):
         assert dloss < 2e-2, dloss
         assert worst < 5e-2, worst
+
+
+def test_device_loss_scaler_rule(monkeypatch):
+    """fp16 loss scaling of the fused optimizer, with the kernels emulated: a scaled
+    gradient steps exactly like the unscaled one (1/S folded into the clip
+    coefficient), a non-finite gradient skips the step and halves S, and S doubles
+    after growth_interval finite steps in a row."""
+    import torch.nn as nn
+
+    from fused_emulation import emulate
+    from heiretsu_b200.optim import DeviceLossScaler, FusedAdamW
+    from heiretsu_b200.parallel.flat import FlatParams
+
+    emulate(monkeypatch)
+    torch.manual_seed(0)
+    ref_m, m = nn.Linear(8, 4), nn.Linear(8, 4)
+    m.load_state_dict(ref_m.state_dict())
+    f_ref = FlatParams(ref_m, torch.device("cpu"))
+    f = FlatParams(m, torch.device("cpu"))
+    opt_ref = FusedAdamW(f_ref, lr=1e-2, max_grad_norm=0.5)
+    sc = DeviceLossScaler(torch.device("cpu"), init_scale=1024.0, growth_interval=3)
+    opt = FusedAdamW(f, lr=1e-2, max_grad_norm=0.5, scaler=sc)
+    g = torch.randn(f.numel)
+    f_ref.grad.copy_(g)
+    f.grad.copy_(g * 1024.0)
+    opt_ref.step()
+    opt.step()
+    assert torch.allclose(f.data, f_ref.data, atol=1e-6)
+    assert sc.get_scale() == 1024.0
+    before = f.data.clone()
+    f.grad.fill_(float("inf"))
+    opt.step()
+    assert torch.equal(before, f.data) and sc.get_scale() == 512.0
+    for _ in range(3):
+        f.grad.copy_(g * sc.get_scale())
+        opt.step()
+    assert sc.get_scale() == 1024.0
+    st = sc.state_dict()
+    assert st["scale"] == 1024.0 and st["_growth_tracker"] == 0
