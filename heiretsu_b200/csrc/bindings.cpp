@@ -51,7 +51,7 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("ipc_open", &hb::ipc_open_py);
   m.def("ipc_close", &hb::ipc_close);
   m.def("dp_allreduce", &hb::dp_allreduce, py::arg("data"), py::arg("signal"), py::arg("rank"), py::arg("n"),
-        py::arg("scale"), py::arg("counter"), py::arg("threads") = 512);
+        py::arg("scale"), py::arg("counter"), py::arg("threads") = 512, py::arg("blocks") = 0);
   m.def("group_barrier", &hb::group_barrier);
   m.def("peer_sum", &hb::peer_sum);
   m.def("moe_route", &hb::moe_route);

@@ -146,7 +146,8 @@ static PeerTable make_table(const std::vector<uint64_t>& data, const std::vector
 int dp_allreduce_blocks(int device) { return num_sms(device); }
 
 void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
-                         long n, float scale, uint32_t* counter, int* status, int threads, cudaStream_t s) {
+                         long n, float scale, uint32_t* counter, int* status, int threads, int blocks_req,
+                         cudaStream_t s) {
   const int world = static_cast<int>(data.size());
   if (n % 4 != 0) throw std::runtime_error("dp_allreduce: element count must be a multiple of 4");
   // float4 peer loads and stores: an unaligned range start would fault the GPU.
@@ -155,11 +156,13 @@ void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<ui
   const PeerTable t = make_table(data, signal);
   const long n4 = n / 4;
   const long chunk4 = (n4 + world - 1) / world;
-  const int blocks = std::min(dp_allreduce_blocks(current_device()), kMaxSignalBlocks);
+  // blocks_req = 0: one CTA per SM. Every rank must pass the same block count
+  // for the same call (the barrier epochs are per block index).
+  const int blocks = std::min(blocks_req > 0 ? blocks_req : dp_allreduce_blocks(current_device()), kMaxSignalBlocks);
   // threads = 512: the whole GPU moves the data (reduction after backward).
   // threads = 64: a footprint of 2 warps and ~3K registers per SM, small
   // enough to sit beside a persistent GEMM / attention CTA, so the reduction
-  // runs underneath backward compute (still one CTA per SM for bandwidth).
+  // runs underneath backward compute; with few blocks it also stays off most SMs.
   if (threads != 512 && threads != 256 && threads != 128 && threads != 64)
     throw std::runtime_error("dp_allreduce: threads must be 64, 128, 256 or 512");
   dp_allreduce_kernel<<<blocks, threads, 0, s>>>(t, rank, world, n4, chunk4, scale, counter, status);

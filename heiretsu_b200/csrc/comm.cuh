@@ -55,6 +55,11 @@ __device__ __forceinline__ bool group_barrier(const PeerTable& pt, int rank, int
       const uint32_t* slot = mine + p * kMaxSignalBlocks + blockIdx.x;
       int spins = 0;
       while (static_cast<int32_t>(ld_acquire_sys(slot) - val) < 0) {
+        // Back off after a short spin: a rank that is ahead waits here while its
+        // peers finish their compute, and a tight poll in every CTA would take
+        // issue slots from the kernels that share the SMs (the overlapped DP
+        // reduction runs beside backward GEMMs and attention).
+        if (spins > 32) __nanosleep(128);
         if (((++spins) & 255) == 0 && globaltimer_ns() - t0 > HB_WAIT_TIMEOUT_NS) {
           record_error(status, kPeerTimeout, 100 + p);
           ok_sh = 0;

@@ -14,7 +14,7 @@ std::vector<uint8_t> ipc_handle(uint64_t ptr);
 uint64_t ipc_open(const std::vector<uint8_t>& handle);
 void ipc_close(uint64_t ptr);
 void dp_allreduce_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank, long n,
-                         float scale, uint32_t* counter, int* status, int threads, cudaStream_t s);
+                         float scale, uint32_t* counter, int* status, int threads, int blocks, cudaStream_t s);
 void group_barrier_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
                           uint32_t* counter, int* status, cudaStream_t s);
 void peer_sum_launch(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int rank,
@@ -47,13 +47,13 @@ uint64_t ipc_open_py(py::bytes handle) {
 }
 
 void dp_allreduce(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank, int64_t n,
-                  double scale, const at::Tensor& counter, int64_t threads) {
+                  double scale, const at::Tensor& counter, int64_t threads, int64_t blocks) {
   TORCH_CHECK(counter.is_cuda() && counter.scalar_type() == at::kInt && counter.numel() >= 1024,
               "dp_allreduce: counter must be int32 [>=1024] on the device");
   c10::cuda::CUDAGuard g(counter.device());
   dp_allreduce_launch(data, signal, static_cast<int>(rank), n, static_cast<float>(scale),
                       reinterpret_cast<uint32_t*>(counter.data_ptr()), device_status_ptr(counter.get_device()),
-                      static_cast<int>(threads), at::cuda::getCurrentCUDAStream());
+                      static_cast<int>(threads), static_cast<int>(blocks), at::cuda::getCurrentCUDAStream());
 }
 
 void group_barrier(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,

@@ -59,7 +59,7 @@ pybind11::bytes ipc_handle_py(uint64_t ptr);
 uint64_t ipc_open_py(pybind11::bytes handle);
 void ipc_close(uint64_t ptr);
 void dp_allreduce(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank, int64_t n,
-                  double scale, const at::Tensor& counter, int64_t threads);
+                  double scale, const at::Tensor& counter, int64_t threads, int64_t blocks);
 void group_barrier(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,
                    const at::Tensor& counter);
 void peer_sum(const std::vector<uint64_t>& data, const std::vector<uint64_t>& signal, int64_t rank,

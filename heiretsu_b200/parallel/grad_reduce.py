@@ -47,6 +47,10 @@ def uncovered_ranges(done: List[Tuple[int, int]], n: int) -> List[Tuple[int, int
     return rest
 
 
+# CTAs of each overlapped per-block reduction (HB_DP_OVERLAP_BLOCKS overrides).
+OVERLAP_BLOCKS = int(os.environ.get("HB_DP_OVERLAP_BLOCKS", "32"))
+
+
 class FlatGradReducer:
     def __init__(self, flat: FlatParams, group: Optional[dist.ProcessGroup], topo=None,
                  backend: Optional[str] = None, bucket_elems: int = BUCKET_ELEMS):
@@ -113,7 +117,9 @@ class FlatGradReducer:
         self._side.wait_event(ev)
         with torch.cuda.stream(self._side):
             for a, b in ranges:
-                self.symm.sum_range(a, b - a, 1.0 / self.world, threads=64)
+                # 2 warps x OVERLAP_BLOCKS CTAs: enough to keep NVLink busy for a block's
+                # gradients while leaving almost every SM to the backward kernels
+                self.symm.sum_range(a, b - a, 1.0 / self.world, threads=64, blocks=OVERLAP_BLOCKS)
         self._done.extend(ranges)
 
     def finish(self) -> None:

@@ -70,10 +70,11 @@ class SymmetricBuffer:
         """Device-side barrier of the group (bounded wait), ordered on the current stream."""
         load().group_barrier(self.ptrs, self.signal_ptrs, self.rank, self.counter)
 
-    def sum_range(self, start_elem: int, n_elem: int, scale: float = 1.0, threads: int = 512) -> None:
+    def sum_range(self, start_elem: int, n_elem: int, scale: float = 1.0, threads: int = 512, blocks: int = 0) -> None:
         """In place over the group: fp32 elements [start, start+n) <- scale * sum over ranks (NVLink, one kernel).
 
-        ``threads`` = 64 gives a footprint small enough to run beside compute kernels."""
+        ``threads`` = 64 gives a footprint small enough to run beside compute kernels;
+        ``blocks`` > 0 caps the grid (0: one CTA per SM). Every rank must pass the same values."""
         if self.world == 1 or n_elem == 0:
             return
         if start_elem % 4 or n_elem % 4:
@@ -81,7 +82,7 @@ class SymmetricBuffer:
                              "(the kernel moves float4 vectors)")
         off = start_elem * 4
         load().dp_allreduce([p + off for p in self.ptrs], self.signal_ptrs, self.rank, n_elem, scale, self.counter,
-                            threads)
+                            threads, blocks)
 
 
 def check_comm_status(device: int) -> None:
