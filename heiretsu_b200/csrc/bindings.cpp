@@ -14,7 +14,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
         py::arg("ag_rows") = 0, py::arg("rs_dst") = std::vector<uint64_t>{}, py::arg("rs_rank") = 0,
         py::arg("rs_rows") = 0, py::arg("grp_mode") = 0, py::arg("grp_off") = py::none(), py::arg("grp_n") = 0,
         py::arg("grp_b_off") = 0, py::arg("grp_c_off") = 0, py::arg("drop_seed") = py::none(),
-        py::arg("drop_site") = 0, py::arg("drop_p") = 0.0, py::arg("drop_row0") = 0);
+        py::arg("drop_site") = 0, py::arg("drop_p") = 0.0, py::arg("drop_row0") = 0,
+        py::arg("cmb_dst") = std::vector<uint64_t>{}, py::arg("cmb_inv") = py::none(), py::arg("cmb_w") = py::none(),
+        py::arg("cmb_k") = 0, py::arg("cmb_n") = 0);
   m.def("layernorm_fwd", &hb::layernorm_fwd);
   m.def("layernorm_bwd_scratch_rows", &hb::layernorm_bwd_scratch_rows);
   m.def("layernorm_bwd", &hb::layernorm_bwd, py::arg("dy"), py::arg("x"), py::arg("mean"), py::arg("rstd"),
@@ -55,7 +57,9 @@ PYBIND11_MODULE(TORCH_EXTENSION_NAME, m) {
   m.def("group_barrier", &hb::group_barrier);
   m.def("peer_sum", &hb::peer_sum);
   m.def("moe_route", &hb::moe_route);
-  m.def("moe_gather", &hb::moe_gather);
+  m.def("moe_gather", &hb::moe_gather, py::arg("x"), py::arg("pos"), py::arg("K"), py::arg("xp"), py::arg("off"),
+        py::arg("e0"), py::arg("e1"), py::arg("inv") = py::none());
+  m.def("moe_slots_reduce", &hb::moe_slots_reduce);
   m.def("moe_combine", &hb::moe_combine);
   m.def("moe_combine_bwd", &hb::moe_combine_bwd);
   m.def("moe_unpermute", &hb::moe_unpermute);

@@ -53,7 +53,9 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
           const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows, int64_t grp_mode,
           const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off,
-          const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0) {
+          const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0,
+          const std::vector<uint64_t>& cmb_dst, const c10::optional<at::Tensor>& cmb_inv,
+          const c10::optional<at::Tensor>& cmb_w, int64_t cmb_k, int64_t cmb_n) {
   TORCH_CHECK(a.is_cuda() && b.is_cuda() && c.is_cuda(), "gemm: tensors must be on CUDA");
   const bool f16 = a.scalar_type() == at::kHalf;
   TORCH_CHECK((a.scalar_type() == at::kBFloat16 || f16) && b.scalar_type() == a.scalar_type(),
@@ -190,6 +192,24 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
     p.ag_dst = a.data_ptr();
     p.ag_flags = ag_flags->data_ptr<int>();
     HB_CUDA_CHECK(cudaMemsetAsync(p.ag_flags, 0, sizeof(int) * (M / 128), at::cuda::getCurrentCUDAStream()));
+  }
+  if (!cmb_dst.empty()) {
+    TORCH_CHECK(grp_mode == 1 && epi == kEpiBf16 && cmb_dst.size() <= 8 && cmb_k >= 1 && cmb_n >= 1,
+                "gemm: the combine epilogue belongs to a row-grouped GEMM with a 16-bit output");
+    TORCH_CHECK(N % 32 == 0, "gemm: the combine epilogue stores whole 32-column chunks (N % 32 == 0)");
+    TORCH_CHECK(cmb_inv && cmb_inv->defined() && cmb_inv->scalar_type() == at::kInt && cmb_inv->is_cuda() &&
+                    cmb_inv->numel() >= M,
+                "gemm: combine needs int32 slot indices for every output row");
+    TORCH_CHECK(cmb_w && cmb_w->defined() && cmb_w->scalar_type() == at::kFloat && cmb_w->is_contiguous() &&
+                    cmb_w->numel() >= cmb_k * cmb_n,
+                "gemm: combine needs fp32 routing weights [tokens, K]");
+    for (uint64_t ptr : cmb_dst) TORCH_CHECK(ptr % 16 == 0, "gemm: combine slots must be 16-byte aligned");
+    p.cmb_world = static_cast<int>(cmb_dst.size());
+    p.cmb_K = static_cast<int>(cmb_k);
+    p.cmb_N = static_cast<int>(cmb_n);
+    p.cmb_inv = cmb_inv->data_ptr<int>();
+    p.cmb_w = cmb_w->data_ptr<float>();
+    for (size_t i = 0; i < cmb_dst.size(); ++i) p.cmb_dst[i] = reinterpret_cast<void*>(cmb_dst[i]);
   }
   if (!rs_dst.empty()) {
     TORCH_CHECK(rs_dst.size() <= 8 && rs_rows % 128 == 0 && (int64_t)rs_dst.size() * rs_rows == M,

@@ -235,32 +235,35 @@ __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, 
   }
 }
 
-// Bias of the epilogue, read once per tile: lane l holds the 4 bias values of
-// columns n_first + 4l .. 4l+3 of its warp's column range (zeros past N), loaded
-// before the tile's accumulator wait. Chunk c takes column j's value from lane
-// 8c + j/4 by warp shuffle, so the epilogue never waits on a global load.
-template <int EPI>
-constexpr bool epi_has_bias() {
-  return EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid;
-}
-__device__ __forceinline__ float4 bias_for_warp(const GemmParams& p, int n_first, int lane) {
-  const int col = n_first + 4 * lane;
-  if (p.bias == nullptr || col >= p.N) return make_float4(0.f, 0.f, 0.f, 0.f);
-  return __ldg(reinterpret_cast<const float4*>(p.bias + col));
-}
-__device__ __forceinline__ void add_bias_shfl(float (&v)[32], const float4& b4, int c) {
+// Expert-parallel combine: this thread's output row, scaled by its routing
+// weight, pushed into slot k, row t of every EP rank's receive buffer.
+__device__ __forceinline__ void epi_combine_push(const GemmParams& p, int row, int n0, const float (&v)[32]) {
+  if (row >= p.M) return;
+  const int inv = p.cmb_inv[row];
+  if (inv < 0) return;  // padding row of an expert segment
+  const float w = p.cmb_w[inv];
+  const int t = inv / p.cmb_K, k = inv - t * p.cmb_K;
+  uint32_t pk[16];
+  if (p.f16) {
 #pragma unroll
-  for (int j = 0; j < 32; ++j) {
-    const float comp = (j & 3) == 0 ? b4.x : ((j & 3) == 1 ? b4.y : ((j & 3) == 2 ? b4.z : b4.w));
-    v[j] += __shfl_sync(0xffffffffu, comp, c * 8 + (j >> 2));
+    for (int j = 0; j < 16; ++j) pk[j] = pack16<true>(w * v[2 * j], w * v[2 * j + 1]);
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) pk[j] = pack16<false>(w * v[2 * j], w * v[2 * j + 1]);
+  }
+  const long off = (((long)k * p.cmb_N + t) * p.N + n0) * 2;  // bytes
+#pragma unroll 1
+  for (int r = 0; r < p.cmb_world; ++r) {
+    uint4* d = reinterpret_cast<uint4*>(static_cast<uint8_t*>(p.cmb_dst[r]) + off);
+#pragma unroll
+    for (int q = 0; q < 4; ++q) d[q] = make_uint4(pk[4 * q], pk[4 * q + 1], pk[4 * q + 2], pk[4 * q + 3]);
   }
 }
 
 // Residual dropout of one 32-column chunk of this thread's row:
 // v = mask * (v + bias), mask from the counter-based hash of the element index.
-__device__ __forceinline__ void epi_bias_dropout(const GemmParams& p, uint32_t key, int row, int n0, float (&v)[32],
-                                                 bool bias_done) {
-  if (!bias_done && p.bias != nullptr) {
+__device__ __forceinline__ void epi_bias_dropout(const GemmParams& p, uint32_t key, int row, int n0, float (&v)[32]) {
+  if (p.bias != nullptr) {
 #pragma unroll
     for (int j = 0; j < 32; j += 4) {
       if (n0 + j < p.N) {
@@ -331,16 +334,10 @@ __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_b
 // Step 2, TMA form: bias / activation, stage the chunk, one lane issues the
 // bulk store (or reduce-add). `row` is the chunk's first row in the C map.
 // The caller has waited for the previous bulk copies to finish reading `stg`.
-// Waits for the previous chunk's bulk copies to have read `stg` (all lanes return after it).
-__device__ __forceinline__ void stg_wait_read(int lane) {
-  if (lane == 0) bulk_wait_group_read0();
-  __syncwarp();
-}
-
 template <int EPI>
 __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtensorMap* tmC, const CUtensorMap* tmX,
                                                int row, int n0, float (&v)[32], uint8_t* stg, int lane,
-                                               bool bias_done, bool wait_stg) {
+                                               bool bias_done = false) {
   if (!bias_done && p.bias != nullptr &&
       (EPI == kEpiBf16 || EPI == kEpiBf16Gelu || EPI == kEpiF32 || EPI == kEpiF32Resid)) {
 #pragma unroll
@@ -359,7 +356,6 @@ __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtens
     // rounded value -> second 2 KB; two stores.
     uint32_t pk[16];
     gelu_chunk(v, pk, p.f16 != 0);
-    if (wait_stg) stg_wait_read(lane);
 #pragma unroll
     for (int g = 0; g < 4; ++g)
       *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
@@ -373,7 +369,6 @@ __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtens
       bulk_commit_group();
     }
   } else if constexpr (EPI == kEpiBf16 || EPI == kEpiBf16Dgelu) {
-    if (wait_stg) stg_wait_read(lane);
     stg_put_bf16(stg, lane, v, p.f16 != 0);
     fence_proxy_async_smem();
     __syncwarp();
@@ -382,7 +377,6 @@ __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtens
       bulk_commit_group();
     }
   } else {
-    if (wait_stg) stg_wait_read(lane);
     stg_put_f32(stg, lane, v);
     fence_proxy_async_smem();
     __syncwarp();
@@ -659,8 +653,6 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
       uint4 pre[8];
       const int n_first = nb * BN + c0 * 32;
       if (reads && nkb_ > 0 && n_first < p.N) epi_prefetch<EPI>(p, C, m_base, n_first, lane, pre);
-      const bool has_bias = epi_has_bias<EPI>() && p.bias != nullptr;
-      const float4 bias4 = has_bias ? bias_for_warp(p, n_first, lane) : make_float4(0.f, 0.f, 0.f, 0.f);
       if (!mbar_wait(&tfull[acc], acc_phase, p.status, 4)) break;
       tc_fence_after();
       if (nkb_ > 0) {  // an empty expert segment accumulated nothing and stores nothing
@@ -670,31 +662,26 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
           if (n0 >= p.N) break;
           float v[32];
           tmem_ld32(tmem_base + (static_cast<uint32_t>(quarter * 32) << 16) + acc * BN + (c0 + c) * 32, v);
-          // The staging tile is reused: the previous chunk's bulk copies must have read
-          // it. Epilogues that stage an operand wait here; the others wait in
-          // epi_finish_tma right before their first staging write, so the copy engine
-          // reads the previous chunk while this one's bias / activation math runs.
-          if (tma && reads) {
+          if (tma) {  // the staging tile is reused: the previous bulk copies must have read it
             if (lane == 0) bulk_wait_group_read0();
             __syncwarp();
           }
           bool bias_done = false;
-          if (has_bias) {
-            add_bias_shfl(v, bias4, c);
-            bias_done = true;
-          }
           if constexpr (EPI == kEpiF32Resid) {
             if (p.drop.thresh != 0) {  // C = R + dropout(acc + bias)
-              epi_bias_dropout(p, drop_key, m_base + lane, n0, v, bias_done);
+              epi_bias_dropout(p, drop_key, m_base + lane, n0, v);
               bias_done = true;
             }
           }
           if (reads) epi_apply_operand<EPI>(v, stg, pre, lane, p.f16 != 0);
           if (reads && c + 1 < CH && n0 + 32 < p.N) epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
           if (tma) {
-            epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane, bias_done, !reads);
+            epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane, bias_done);
           } else {
             epi_finish<EPI>(p, C, m_base, n0, v, stg, lane, bias_done);
+          }
+          if constexpr (EPI == kEpiBf16) {
+            if (p.cmb_world > 0) epi_combine_push(p, m_base + lane, n0, v);
           }
         }
       }

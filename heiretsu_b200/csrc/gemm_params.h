@@ -73,6 +73,20 @@ struct GemmParams {
   // 16-bit format of A, B and of the 16-bit outputs / AUX: 0 bf16, 1 fp16.
   int f16;
 
+  // Expert-parallel combine epilogue (row-grouped GEMM with a 16-bit output;
+  // cmb_world = 0: off). Output row p of this rank's expert window holds the
+  // expert output of routing slot cmb_inv[p] = t * cmb_K + k (-1: padding row).
+  // Besides C, the epilogue stores 16-bit(cmb_w[t * cmb_K + k] * row) into row
+  // t of slot k of every EP rank's receive buffer cmb_dst[r] = [cmb_K][cmb_N][N]
+  // (peer stores over NVLink). Each (t, k) belongs to exactly one rank's
+  // experts, so every slot row is written once per call.
+  int cmb_world;
+  int cmb_K;
+  int cmb_N;
+  const int* cmb_inv;
+  const float* cmb_w;
+  void* cmb_dst[8];
+
   // Residual dropout of the F32Resid epilogue (thresh 0 = off):
   // C = R + mask * (acc + bias), mask element (drop.row0 + row) * N + col.
   DropoutArgs drop;

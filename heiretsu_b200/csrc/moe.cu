@@ -128,16 +128,19 @@ __global__ void __launch_bounds__(1024) moe_positions_kernel(const int* __restri
   }
 }
 
-// Gather rows into the permuted matrix: one warp per slot.
+// Gather rows into the permuted matrix: one warp per slot. With `inv`, also
+// records which routing slot (t * K + k) each window row holds (rows left at
+// -1 are segment padding); the expert-parallel combine epilogue reads it.
 __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int* __restrict__ pos, int NK, int K,
                                   int H, __nv_bfloat16* __restrict__ xp, const int* __restrict__ off, int e0, int e1,
-                                  int cap, int* status) {
+                                  int cap, int* status, int* __restrict__ inv) {
   const int i = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (i >= NK) return;
   const int lo = off[e0], r = pos[i];
   if (r < lo || r >= off[e1]) return;  // routed to an expert outside this rank's window
   if (!HB_DCHECK(r - lo < cap, status, 300)) return;
+  if (inv != nullptr && lane == 0) inv[r - lo] = i;
   const uint4* src = reinterpret_cast<const uint4*>(x + (long)(i / K) * H);
   uint4* dst = reinterpret_cast<uint4*>(xp + (long)(r - lo) * H);
   for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
@@ -218,6 +221,29 @@ __global__ void moe_unpermute_kernel(const float* __restrict__ dxp, const int* _
   }
 }
 
+// Expert-parallel combine, second half: out[t] = x[t] + sum_k slots[k][t]
+// (16-bit slots filled by every EP rank's combine epilogue, then a barrier).
+// Every rank adds the same values in the same order, so all replicas hold
+// identical results. One warp per token, 4 columns per lane per step.
+template <bool F16>
+__global__ void moe_slots_reduce_kernel(const float* __restrict__ x, const __nv_bfloat16* __restrict__ slots, int N,
+                                        int K, int H, float* __restrict__ out) {
+  const int t = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
+  const int lane = threadIdx.x & 31;
+  if (t >= N) return;
+  for (int j = lane * 4; j < H; j += 128) {
+    float4 acc = *reinterpret_cast<const float4*>(x + (long)t * H + j);
+    for (int k = 0; k < K; ++k) {
+      const uint2 raw = *reinterpret_cast<const uint2*>(slots + ((long)k * N + t) * H + j);
+      acc.x += lo16<F16>(raw.x);
+      acc.y += hi16<F16>(raw.x);
+      acc.z += lo16<F16>(raw.y);
+      acc.w += hi16<F16>(raw.y);
+    }
+    *reinterpret_cast<float4*>(out + (long)t * H + j) = acc;
+  }
+}
+
 // Offsets of the window's experts relative to its first row: out[i] = off[e0 + i] - off[e0], i = 0 .. n.
 __global__ void moe_local_offsets_kernel(const int* __restrict__ off, int e0, int n, int* __restrict__ out) {
   const int i = threadIdx.x;
@@ -280,8 +306,9 @@ void moe_route_launch(const __nv_bfloat16* x, const float* wg, int N, int H, int
 }
 
 void moe_gather_launch(const __nv_bfloat16* x, const int* pos, int N, int K, int H, __nv_bfloat16* xp,
-                       const int* off, int e0, int e1, int cap, int* status, cudaStream_t s) {
-  moe_gather_kernel<<<(N * K * 32 + 255) / 256, 256, 0, s>>>(x, pos, N * K, K, H, xp, off, e0, e1, cap, status);
+                       const int* off, int e0, int e1, int cap, int* status, int* inv, cudaStream_t s) {
+  if (inv != nullptr) HB_CUDA_CHECK(cudaMemsetAsync(inv, 0xFF, sizeof(int) * cap, s));  // -1: padding rows
+  moe_gather_kernel<<<(N * K * 32 + 255) / 256, 256, 0, s>>>(x, pos, N * K, K, H, xp, off, e0, e1, cap, status, inv);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
@@ -304,6 +331,14 @@ void moe_combine_bwd_launch(const float* dy, const __nv_bfloat16* yp, const int*
 void moe_unpermute_launch(const float* dxp, const int* pos, int N, int K, int H, float* dx, const int* off, int e0,
                           int e1, int cap, int* status, cudaStream_t s) {
   moe_unpermute_kernel<<<(N * 32 + 255) / 256, 256, 0, s>>>(dxp, pos, N, K, H, dx, off, e0, e1, cap, status);
+  HB_CUDA_CHECK(cudaGetLastError());
+}
+
+void moe_slots_reduce_launch(const float* x, const __nv_bfloat16* slots, int N, int K, int H, float* out, bool f16,
+                             cudaStream_t s) {
+  if (H % 4) throw std::runtime_error("moe_slots_reduce: H must be a multiple of 4");
+  (f16 ? moe_slots_reduce_kernel<true> : moe_slots_reduce_kernel<false>)<<<(N * 32 + 255) / 256, 256, 0, s>>>(
+      x, slots, N, K, H, out);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -12,7 +12,8 @@ namespace hb {
 void moe_route_launch(const __nv_bfloat16*, const float*, int, int, int, int, float, float*, int*, float*, int*, float*,
                       int*, float*, int*, bool, cudaStream_t);
 void moe_gather_launch(const __nv_bfloat16*, const int*, int, int, int, __nv_bfloat16*, const int*, int, int, int,
-                       int*, cudaStream_t);
+                       int*, int*, cudaStream_t);
+void moe_slots_reduce_launch(const float*, const __nv_bfloat16*, int, int, int, float*, bool, cudaStream_t);
 void moe_combine_launch(const __nv_bfloat16*, const int*, const float*, const float*, int, int, int, float*,
                         const int*, int, int, int, int*, bool, cudaStream_t);
 void moe_combine_bwd_launch(const float*, const __nv_bfloat16*, const int*, const float*, int, int, int,
@@ -66,14 +67,32 @@ static void check_window(const at::Tensor& off, int64_t e0, int64_t e1) {
 }
 
 void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp, const at::Tensor& off,
-                int64_t e0, int64_t e1) {
+                int64_t e0, int64_t e1, const c10::optional<at::Tensor>& inv) {
   TORCH_CHECK((x.scalar_type() == at::kBFloat16 || x.scalar_type() == at::kHalf) &&
                   xp.scalar_type() == x.scalar_type() && x.size(1) == xp.size(1),
               "moe_gather: 16-bit [N, H] -> [R, H] of one format");
   check_window(off, e0, e1);
   c10::cuda::CUDAGuard g(x.device());
+  int* inv_p = nullptr;
+  if (inv && inv->defined()) {
+    check_i32(*inv, "moe_gather: inv");
+    TORCH_CHECK(inv->numel() >= xp.size(0), "moe_gather: inv needs one entry per permuted row");
+    inv_p = P<int>(*inv);
+  }
   moe_gather_launch(P<__nv_bfloat16>(x), P<int>(pos), x.size(0), K, x.size(1), P<__nv_bfloat16>(xp), P<int>(off),
-                    e0, e1, xp.size(0), device_status_ptr(x.get_device()), S());
+                    e0, e1, xp.size(0), device_status_ptr(x.get_device()), inv_p, S());
+}
+
+// out = x + sum_k slots[k] (fp32 [N, H] out and x; 16-bit slots [K, N, H]).
+void moe_slots_reduce(const at::Tensor& x, const at::Tensor& slots, int64_t K, at::Tensor& out) {
+  check_f32(x, "moe_slots_reduce: x");
+  check_f32(out, "moe_slots_reduce: out");
+  TORCH_CHECK((slots.scalar_type() == at::kBFloat16 || slots.scalar_type() == at::kHalf) && slots.is_contiguous() &&
+                  slots.numel() >= K * x.numel(),
+              "moe_slots_reduce: slots 16-bit [K, N, H]");
+  c10::cuda::CUDAGuard g(x.device());
+  moe_slots_reduce_launch(P<float>(x), P<__nv_bfloat16>(slots), x.size(0), K, x.size(1), P<float>(out),
+                          slots.scalar_type() == at::kHalf, S());
 }
 
 void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,

@@ -11,7 +11,9 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
           const c10::optional<at::Tensor>& ag_flags, int64_t ag_rank, int64_t ag_rows,
           const std::vector<uint64_t>& rs_dst, int64_t rs_rank, int64_t rs_rows, int64_t grp_mode,
           const c10::optional<at::Tensor>& grp_off, int64_t grp_n, int64_t grp_b_off, int64_t grp_c_off,
-          const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0);
+          const c10::optional<at::Tensor>& drop_seed, int64_t drop_site, double drop_p, int64_t drop_row0,
+          const std::vector<uint64_t>& cmb_dst, const c10::optional<at::Tensor>& cmb_inv,
+          const c10::optional<at::Tensor>& cmb_w, int64_t cmb_k, int64_t cmb_n);
 
 void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b, at::Tensor& y, at::Tensor& mean,
                    at::Tensor& rstd, double eps);
@@ -68,7 +70,8 @@ void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef
                at::Tensor& topw, at::Tensor& counts, at::Tensor& probsum, at::Tensor& off, at::Tensor& aux,
                at::Tensor& pos);
 void moe_gather(const at::Tensor& x, const at::Tensor& pos, int64_t K, at::Tensor& xp, const at::Tensor& off,
-                int64_t e0, int64_t e1);
+                int64_t e0, int64_t e1, const c10::optional<at::Tensor>& inv);
+void moe_slots_reduce(const at::Tensor& x, const at::Tensor& slots, int64_t K, at::Tensor& out);
 void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& topw,
                  const c10::optional<at::Tensor>& resid, at::Tensor& out, const at::Tensor& off, int64_t e0,
                  int64_t e1);

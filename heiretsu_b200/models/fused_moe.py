@@ -22,16 +22,20 @@ tokens (the reference shards data by DP rank only, train.py:322), so no
 token ever has to travel: every EP rank routes all of its tokens (the router
 is replicated), gathers only the rows of its own experts (window
 [e0, e0 + E/ep) of the padded segments) and runs those experts once. The
-combine becomes a sum of per-rank partial outputs: each rank writes
-sum_{k: expert local} w_k y_k into a peer-mapped buffer, and one kernel waits
-on a bounded NVLink barrier and adds x + sum over ranks, in rank order, so
-every replica gets the same bits. In backward the combine needs no traffic
-(every partial receives the full gradient). The input gradients of the local
-experts and the routing-weight gradients of the local slots are summed the
-same way before the replicated router backward. Compared with the
-reference's two all-to-alls per layer (moe.py:349-386; every token sent once
-per EP rank), each token is processed once, and each rank reads
-(ep-1) x N x H fp32 of partials per layer in each direction.
+combine's exchange happens inside the second expert GEMM: its epilogue
+writes each output row, times the row's routing weight, as 16 bits into
+slot k, row t of every EP rank's peer-mapped slot buffer (the (token, k)
+of a row comes from the inverse map the gather records). Each (t, k) is
+owned by exactly one rank, so every slot row is written once. After one
+bounded NVLink barrier, every rank adds x + slot 0 + ... + slot K-1 in
+that order (moe_slots_reduce), so every replica gets the same bits. In
+backward the combine needs no traffic (every rank holds the full
+gradient). The input gradients of the local experts and the routing-weight
+gradients of the local slots are summed over NVLink (peer_sum) before the
+replicated router backward. Compared with the reference's two all-to-alls
+per layer (moe.py:349-386; every token sent once per EP rank), each token
+is processed once, and each rank sends (ep-1)/ep of its K x N x H 16-bit
+slot rows over NVLink from the GEMM epilogue, with no separate combine pass.
 """
 from __future__ import annotations
 
@@ -62,21 +66,33 @@ def _window(moe):
 
 
 class _EPBuffers:
-    """Peer-mapped partial buffers of one MoE layer over its EP group: one for
-    the forward combine (N x H) and one for the backward sums (N x H input
-    gradient + N x K routing-weight gradient). Each call site owns its buffer,
-    which is what makes one barrier per exchange sufficient."""
+    """Peer-mapped buffers of one MoE layer over its EP group: the forward
+    combine slots (K x N x H, 16-bit; slot k row t receives token t's k-th
+    expert output, scaled by its routing weight, from the rank that owns that
+    expert) and the backward sums (N x H input gradient + N x K routing-weight
+    gradient, fp32). Each call site owns its buffer, which is what makes one
+    barrier per exchange sufficient."""
 
-    def __init__(self, moe, N: int, H: int, K: int, device):
+    def __init__(self, moe, N: int, H: int, K: int, device, dtype: torch.dtype):
         from ..parallel.symm import SymmetricBuffer
-        self.N, self.H, self.K = N, H, K
+        self.N, self.H, self.K, self.dtype = N, H, K, dtype
         self.nb = (N * H + N * K + 3) // 4 * 4
-        self.fwd = SymmetricBuffer(moe.ep_group, N * H * 4, device)
+        # Two slot buffers used in turn by consecutive forwards: a rank that is one
+        # forward ahead (evaluation runs forwards back to back, with no backward
+        # barrier in between) writes the other buffer while a peer still reads.
+        self.slots = [SymmetricBuffer(moe.ep_group, K * N * H * 2, device) for _ in range(2)]
+        self.turn = 0
         self.bwd = SymmetricBuffer(moe.ep_group, self.nb * 4, device)
-        self.rank = self.fwd.rank
+        self.rank = self.bwd.rank
 
-    def fwd_partial(self) -> torch.Tensor:
-        return self.fwd.tensor(torch.float32, self.N * self.H).view(self.N, self.H)
+    def next_slots(self):
+        """The slot buffer of the coming forward."""
+        b = self.slots[self.turn]
+        self.turn ^= 1
+        return b
+
+    def slot_tensor(self, b) -> torch.Tensor:
+        return b.tensor(self.dtype, self.K * self.N * self.H).view(self.K, self.N, self.H)
 
     def bwd_parts(self):
         t = self.bwd.tensor(torch.float32, self.nb)
@@ -84,11 +100,11 @@ class _EPBuffers:
         return t, t[:NH].view(self.N, self.H), t[NH:NH + self.N * self.K].view(self.N, self.K)
 
 
-def _ep_buffers(moe, N: int, H: int, K: int, device) -> _EPBuffers:
+def _ep_buffers(moe, N: int, H: int, K: int, device, dtype: torch.dtype = torch.bfloat16) -> _EPBuffers:
     cache = moe.__dict__.setdefault("_hb_ep_buffers", {})
-    key = (N, H, K, str(device))
+    key = (N, H, K, str(device), dtype)
     if key not in cache:
-        cache[key] = _EPBuffers(moe, N, H, K, device)
+        cache[key] = _EPBuffers(moe, N, H, K, device, dtype)
     return cache[key]
 
 
@@ -128,13 +144,22 @@ def moe_route_and_experts(moe, xn2: torch.Tensor, flat=None):
     # capacity of this rank's rows: every local segment padded to 128 rows
     R = (N * Kk + El * (PAD - 1) + PAD - 1) // PAD * PAD
     xp = torch.zeros(R, H, device=dev, dtype=xn2.dtype)
-    ext.moe_gather(xn2, pos, Kk, xp, off, e0, e1)
+    ep = moe.ep_world_size
+    inv = torch.empty(R, device=dev, dtype=torch.int32) if ep > 1 else None
+    ext.moe_gather(xn2, pos, Kk, xp, off, e0, e1, inv)
     w1, _, w2, _ = _stacks(moe, flat)
     hp = torch.empty(R, I, device=dev, dtype=xn2.dtype)
     prep = torch.empty(R, I, device=dev, dtype=xn2.dtype)
     G.gemm(xp, w1, hp, I, G.EPI_BF16_GELU, False, False, aux=prep, grp=(1, off_l, El, I, 0))
     yp = torch.empty(R, H, device=dev, dtype=xn2.dtype)
-    G.gemm(hp, w2, yp, H, G.EPI_BF16, False, False, grp=(1, off_l, El, H, 0))
+    cmb = None
+    if ep > 1:
+        # the second expert GEMM also performs the combine's exchange: each output row,
+        # times its routing weight, goes straight into slot (k, t) of every EP rank
+        slots = _ep_buffers(moe, N, H, Kk, dev, xn2.dtype).next_slots()
+        cmb = (slots.ptrs, inv, topw, Kk, N)
+        moe._hb_slots_now = slots
+    G.gemm(hp, w2, yp, H, G.EPI_BF16, False, False, grp=(1, off_l, El, H, 0), cmb=cmb)
     return aux, (probs, topi, topw, counts, off, off_l, pos, xp, hp, prep, yp)
 
 
@@ -148,9 +173,10 @@ def moe_combine_fwd(moe, state, x1: torch.Tensor) -> torch.Tensor:
         ext.moe_combine(yp, pos, topw, x1, x2, off, e0, e1)
         return x2
     N, H = x1.shape
-    buf = _ep_buffers(moe, N, H, moe.top_k, x1.device)
-    ext.moe_combine(yp, pos, topw, None, buf.fwd_partial(), off, e0, e1)
-    _peer_sum(buf.fwd, x1, x2, N * H)
+    buf = _ep_buffers(moe, N, H, moe.top_k, x1.device, yp.dtype)
+    slots = moe._hb_slots_now  # the buffer the expert GEMM of this forward filled
+    slots.barrier()  # every rank's expert GEMM has written its slot rows
+    ext.moe_slots_reduce(x1, buf.slot_tensor(slots), moe.top_k, x2)
     return x2
 
 
@@ -170,7 +196,7 @@ def moe_experts_bwd(moe, xn2: torch.Tensor, state, dx_res: torch.Tensor, daux: t
     ep = moe.ep_world_size
     w1, g1, w2, g2 = _stacks(moe, flat)
     if ep > 1:
-        buf = _ep_buffers(moe, N, H, Kk, dev)
+        buf = _ep_buffers(moe, N, H, Kk, dev, xn2.dtype)
         whole, dxn2_part, dw = buf.bwd_parts()
     else:
         dxn2_part = torch.empty(N, H, device=dev, dtype=torch.float32)

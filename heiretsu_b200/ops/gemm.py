@@ -48,20 +48,23 @@ def _bn_f32_out(n: int) -> int:
 
 
 def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None, grp=None,
-         drop=None):
+         drop=None, cmb=None):
     """D = A.B^T-style GEMM (see module doc). ``ag = (src_ptrs, flags, rank, rows)`` turns on
     the in-kernel all-gather of A's token shards; ``rs = (dst_ptrs, rank, rows)`` stores each
     output tile into its token owner's receive slot (reduce-scatter epilogue);
     ``grp = (mode, offsets, n_groups, b_off, c_off)`` runs an expert-grouped GEMM;
-    ``drop = (seed_tensor, site, p, row0)`` applies residual dropout in the F32Resid epilogue."""
+    ``drop = (seed_tensor, site, p, row0)`` applies residual dropout in the F32Resid epilogue;
+    ``cmb = (slot_ptrs, inv, weights, K, tokens)`` adds the expert-parallel combine to a row-grouped
+    16-bit GEMM: each output row, times its routing weight, goes to slot (k, t) of every EP rank."""
     ag_src, ag_flags, ag_rank, ag_rows = ag if ag is not None else ([], None, 0, 0)
     rs_dst, rs_rank, rs_rows = rs if rs is not None else ([], 0, 0)
     g_mode, g_off, g_n, g_b, g_c = grp if grp is not None else (0, None, 0, 0, 0)
     d_seed, d_site, d_p, d_row0 = drop if drop is not None else (None, 0, 0.0, 0)
+    c_dst, c_inv, c_w, c_k, c_n = cmb if cmb is not None else ([], None, None, 0, 0)
     load().gemm(a, b, c, int(n), int(epi), bool(a_mn), bool(b_mn), bias, aux, resid,
                 int(block_n if block_n is not None else _bn(n)), list(ag_src), ag_flags, int(ag_rank),
                 int(ag_rows), list(rs_dst), int(rs_rank), int(rs_rows), int(g_mode), g_off, int(g_n), int(g_b),
-                int(g_c), d_seed, int(d_site), float(d_p), int(d_row0))
+                int(g_c), d_seed, int(d_site), float(d_p), int(d_row0), list(c_dst), c_inv, c_w, int(c_k), int(c_n))
     return c
 
 
