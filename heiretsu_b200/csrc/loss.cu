@@ -54,7 +54,7 @@ template <bool F16>
 __global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16* __restrict__ logits, long ld, int V,
                                                             const int64_t* __restrict__ targets, int ignore_index,
                                                             float* __restrict__ lse_out,
-                                                            float* __restrict__ loss_rows) {
+                                                            float* __restrict__ loss_rows, int* status) {
   __shared__ float sh[32];
   const long row = blockIdx.x;
   const __nv_bfloat16* lr = logits + row * ld;
@@ -89,7 +89,14 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fwd_kernel(const __nv_bfloat16*
     const float lse = gm + __logf(gs);
     lse_out[row] = lse;
     const int64_t t = targets[row];
-    loss_rows[row] = (t == ignore_index) ? 0.f : lse - to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[t]);
+    if (t == ignore_index) {
+      loss_rows[row] = 0.f;
+    } else if (t < 0 || t >= V) {  // no such class (F.cross_entropy rejects it): NaN row, status set
+      record_error(status, kBadArg, 400);
+      loss_rows[row] = NAN;
+    } else {
+      loss_rows[row] = lse - to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[t]);
+    }
   }
 }
 
@@ -102,7 +109,10 @@ __global__ void __launch_bounds__(CE_THREADS) ce_bwd_kernel(__nv_bfloat16* __res
   const long row = blockIdx.x;
   __nv_bfloat16* lr = logits + row * ld;
   const int64_t t = targets[row];
-  const float scale = (t == ignore_index) ? 0.f : scale_mul * (scale_ptr ? *scale_ptr : 1.f);
+  // an out-of-range target (already reported by the forward) poisons its row's gradient
+  const float scale = (t == ignore_index) ? 0.f
+                      : (t < 0 || t >= V) ? NAN
+                                          : scale_mul * (scale_ptr ? *scale_ptr : 1.f);
   const float lse = lse_in[row];
   const int nchunk = Vp >> 3;
   for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
@@ -133,13 +143,18 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __r
                                                               int Vp, const int64_t* __restrict__ targets,
                                                               int ignore_index, float* __restrict__ lse_out,
                                                               float* __restrict__ loss_rows,
-                                                              const float* __restrict__ scale_ptr) {
+                                                              const float* __restrict__ scale_ptr, int* status) {
   __shared__ float sh[32];
   const long row = blockIdx.x;
   __nv_bfloat16* lr = logits + row * ld;
   const int64_t t = targets[row];
   const bool counted = (t != ignore_index);
-  const float target_logit = (threadIdx.x == 0 && counted) ? to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[t]) : 0.f;
+  // A target outside [0, V) is no class (F.cross_entropy rejects it): its row's
+  // loss and gradient become NaN (so the step is skipped) and the status is set.
+  const bool bad = counted && (t < 0 || t >= V);
+  if (bad && threadIdx.x == 0) record_error(status, kBadArg, 401);
+  const float target_logit =
+      (threadIdx.x == 0 && counted && !bad) ? to_f32<F16>(reinterpret_cast<const uint16_t*>(lr)[t]) : 0.f;
   float m = -INFINITY, s = 0.f;
   const int nchunk = V >> 3;
   for (int c = threadIdx.x; c < nchunk; c += CE_THREADS) {
@@ -172,9 +187,9 @@ __global__ void __launch_bounds__(CE_THREADS) ce_fused_kernel(__nv_bfloat16* __r
   const float lse = gm + __logf(gs);
   if (threadIdx.x == 0) {
     lse_out[row] = lse;
-    loss_rows[row] = counted ? lse - target_logit : 0.f;
+    loss_rows[row] = bad ? NAN : (counted ? lse - target_logit : 0.f);
   }
-  const float scale = counted ? *scale_ptr : 0.f;
+  const float scale = bad ? NAN : (counted ? *scale_ptr : 0.f);
   const int nchunk_p = Vp >> 3;
   for (int c = threadIdx.x; c < nchunk_p; c += CE_THREADS) {
     uint4 raw = *reinterpret_cast<const uint4*>(lr + c * 8);
@@ -233,11 +248,12 @@ __global__ void __launch_bounds__(1024) mean_loss_kernel(const float* __restrict
 }
 
 void ce_fwd_launch(const __nv_bfloat16* logits, long ld, int M, int V, const int64_t* targets, int ignore_index,
-                   float* lse, float* loss_rows, float* loss_mean, float* count, bool f16, cudaStream_t s) {
+                   float* lse, float* loss_rows, float* loss_mean, float* count, bool f16, int* status,
+                   cudaStream_t s) {
   if (ld % 8 != 0) throw std::runtime_error("cross_entropy: logits row stride must be a multiple of 8");
   if (M == 0) return;
   (f16 ? ce_fwd_kernel<true> : ce_fwd_kernel<false>)<<<M, CE_THREADS, 0, s>>>(logits, ld, V, targets, ignore_index, lse,
-                                                                             loss_rows);
+                                                                             loss_rows, status);
   HB_CUDA_CHECK(cudaGetLastError());
   mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, count);
   HB_CUDA_CHECK(cudaGetLastError());
@@ -245,12 +261,12 @@ void ce_fwd_launch(const __nv_bfloat16* logits, long ld, int M, int V, const int
 
 void ce_fused_launch(__nv_bfloat16* logits, long ld, int M, int V, int Vp, const int64_t* targets, int ignore_index,
                      float* lse, float* loss_rows, float* loss_mean, const float* scale_ptr, bool f16,
-                     cudaStream_t s) {
+                     int* status, cudaStream_t s) {
   if (ld % 8 != 0 || Vp % 8 != 0) throw std::runtime_error("cross_entropy: Vp and row stride must be multiples of 8");
   if (M == 0) return;
   (f16 ? ce_fused_kernel<true> : ce_fused_kernel<false>)<<<M, CE_THREADS, 0, s>>>(logits, ld, V, Vp, targets,
                                                                                  ignore_index, lse, loss_rows,
-                                                                                 scale_ptr);
+                                                                                 scale_ptr, status);
   HB_CUDA_CHECK(cudaGetLastError());
   mean_loss_kernel<<<1, 1024, 0, s>>>(loss_rows, targets, M, ignore_index, loss_mean, nullptr);
   HB_CUDA_CHECK(cudaGetLastError());
@@ -326,7 +342,7 @@ extern "C" int hb_cross_entropy_fwd_noalloc(const void* logits, long ld, int M, 
   const int rc = ce_noalloc_scratch(&rows);
   if (rc != HB_NOALLOC_OK) return rc;
   hb::ce_fwd_kernel<false><<<M, hb::CE_THREADS, 0, stream>>>(static_cast<const __nv_bfloat16*>(logits), ld, V, targets,
-                                                      ignore_index, lse, rows);
+                                                             ignore_index, lse, rows, nullptr);
   if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_ERR_CUDA;
   hb::mean_loss_kernel<<<1, 1024, 0, stream>>>(rows, targets, M, ignore_index, loss_mean, nullptr);
   if (cudaGetLastError() != cudaSuccess) return HB_NOALLOC_ERR_CUDA;

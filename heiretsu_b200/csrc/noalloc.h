@@ -24,6 +24,8 @@
 //   each call overwrites the rows it uses before reading them. Calls that
 //   overlap on the GPU (for example on two streams) race on it: order them
 //   on one stream or with events.
+// * A target outside [0, V) that is not ignore_index is no class: that row's
+//   loss is NaN, so *loss_mean is NaN (this entry point has no status word).
 // * M == 0 returns HB_NOALLOC_OK, launches nothing and leaves lse and
 //   *loss_mean untouched (they keep whatever the caller put there).
 // * Kernels are enqueued on `stream`; the call returns without synchronising.

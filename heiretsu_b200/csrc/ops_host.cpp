@@ -24,11 +24,11 @@ void resid_sum_ln_launch(const float*, const __nv_bfloat16*, int, long, const fl
                          const float*, __nv_bfloat16*, float*, float*, int, int, float, bool, cudaStream_t);
 void colsum_bf16_launch(const __nv_bfloat16*, long, int, int, float*, bool, cudaStream_t);
 void ce_fwd_launch(const __nv_bfloat16*, long, int, int, const int64_t*, int, float*, float*, float*, float*, bool,
-                   cudaStream_t);
+                   int*, cudaStream_t);
 void ce_bwd_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, const float*, const float*, float, bool,
                    cudaStream_t);
 void ce_fused_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, float*, float*, float*, const float*,
-                     bool, cudaStream_t);
+                     bool, int*, cudaStream_t);
 void ce_rescale_launch(__nv_bfloat16*, long, int, int, const float*, const float*, bool, cudaStream_t);
 void embed_fwd_launch(const int64_t*, const float*, const float*, float*, int, int, int, cudaStream_t);
 void embed_bwd_launch(const int64_t*, const float*, float*, float*, int, int, int, cudaStream_t);
@@ -169,7 +169,8 @@ void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& ta
   CHECK_CONTIG(targets);
   c10::cuda::CUDAGuard g(logits.device());
   ce_fwd_launch(raw16(logits), logits.stride(0), logits.size(0), V, ptr<int64_t>(targets), ignore_index,
-                ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), nullptr, is_f16(logits), stream());
+                ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), nullptr, is_f16(logits),
+                device_status_ptr(logits.get_device()), stream());
 }
 
 void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
@@ -192,7 +193,7 @@ void cross_entropy_fused(at::Tensor& logits, int64_t V, const at::Tensor& target
   c10::cuda::CUDAGuard g(logits.device());
   ce_fused_launch(raw16(logits), logits.stride(0), logits.size(0), V, logits.size(1), ptr<int64_t>(targets),
                   ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), ptr<float>(scale),
-                  is_f16(logits), stream());
+                  is_f16(logits), device_status_ptr(logits.get_device()), stream());
 }
 
 void cross_entropy_rescale(at::Tensor& g, const at::Tensor& actual, const at::Tensor& expected) {

@@ -184,3 +184,31 @@ def test_attention_fwd_bwd(B, T, nh):
         e = (d[i] - g).abs().max().item()
         scale = g.abs().max().item()
         assert e <= 3e-2 * scale + 1e-3, (name, e, scale)
+
+
+@pytest.mark.parametrize("single_pass", [False, True])
+def test_cross_entropy_rejects_out_of_range_targets(single_pass):
+    """A target outside [0, V) (not ignore_index) is no class: the kernel reads no
+    logit for it, reports a bad argument in the status word, and makes that row's
+    loss NaN (and, in the single pass, its gradient), as F.cross_entropy refuses it."""
+    from heiretsu_b200.ops._C import check_status
+
+    torch.manual_seed(6)
+    M, V = 64, 1000
+    Vp = 1024
+    logits = torch.zeros(M, Vp, device="cuda", dtype=torch.bfloat16)
+    logits[:, :V] = torch.randn(M, V, device="cuda").bfloat16()
+    t = torch.randint(0, V, (M,), device="cuda")
+    t[5] = V + 3
+    if single_pass:
+        scale = torch.full((1,), 1.0 / M, device="cuda")
+        loss, _ = K().cross_entropy_fused_(logits, V, t, scale)
+    else:
+        loss, _, rows = K().cross_entropy_fwd(logits, V, t)
+        assert bool(torch.isnan(rows[5])) and bool(torch.isfinite(rows[:5]).all())
+    torch.cuda.synchronize()
+    assert bool(torch.isnan(loss))
+    with pytest.raises(RuntimeError, match="bad argument"):
+        check_status()
+    if single_pass:
+        assert bool(torch.isnan(logits[5].float()).any()) and bool(torch.isfinite(logits[4].float()).all())
