@@ -359,10 +359,48 @@ __device__ __forceinline__ float sigmoid_2u(float u) {
   return r;
 }
 
+// 2^x on the FMA / integer pipes, for x in [-125, 64] (clamped), to take part
+// of the exponentials off the transcendental unit (whose throughput the
+// epilogue's 16-bit conversions also use). Derived here:
+//   n = nearest integer to x: adding 1.5 * 2^23 (0x4B400000) leaves n in the
+//   low mantissa bits of t = x + 1.5 * 2^23, and t - 1.5 * 2^23 is n as a float;
+//   f = x - n lies in [-1/2, 1/2];
+//   2^f = e^(f ln 2) by its Taylor series to degree 5, coefficients (ln 2)^k / k!;
+//   the Lagrange remainder bounds the relative error: with |f ln 2| <= ln(2)/2,
+//   |R| / 2^f <= (ln(2)/2)^6 / 6! * e^(ln 2) < 5e-6;
+//   2^x = 2^f * 2^n: n is added to the exponent field of 2^f (which lies in
+//   [0.70, 1.42], so the result's exponent stays normal for n >= -125).
+__device__ __forceinline__ float exp2_fma(float x) {
+  x = fminf(fmaxf(x, -125.f), 64.f);
+  const float t = x + 12582912.f;
+  const float f = x - (t - 12582912.f);
+  float p = fmaf(f, 1.3333558146428443e-3f, 9.6181291076284772e-3f);  // (ln 2)^5/5!, (ln 2)^4/4!
+  p = fmaf(f, p, 5.5504108664821580e-2f);                             // (ln 2)^3/3!
+  p = fmaf(f, p, 2.4022650695910071e-1f);                             // (ln 2)^2/2!
+  p = fmaf(f, p, 6.9314718055994531e-1f);                             // ln 2
+  p = fmaf(f, p, 1.f);
+  return __int_as_float(__float_as_int(p) + ((__float_as_int(t) - 0x4B400000) << 23));
+}
+
+// sigmoid(2u) as sigmoid_2u, with the exponential from exp2_fma.
+__device__ __forceinline__ float sigmoid_2u_fma(float u) {
+  const float d = 1.f + exp2_fma(-2.8853900817779268f * u);
+  float r = __int_as_float(0x7EF311C3 - __float_as_int(d));
+  r = r * fmaf(-d, r, 2.f);
+  r = r * fmaf(-d, r, 2.f);
+  return r;
+}
+
 __device__ __forceinline__ float gelu_tanh(float x) {
   const float k0 = 0.7978845608028654f;  // sqrt(2/pi)
   const float k1 = 0.044715f;
   return x * sigmoid_2u(k0 * fmaf(k1 * x, x * x, x));
+}
+// The same function with its exponential on the FMA pipe (epilogues alternate the two).
+__device__ __forceinline__ float gelu_tanh_fma(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  return x * sigmoid_2u_fma(k0 * fmaf(k1 * x, x * x, x));
 }
 
 // d/dx gelu(x) = s + 2 x s (1 - s) du/dx,  du/dx = sqrt(2/pi) (1 + 3 * 0.044715 x^2)
@@ -372,6 +410,14 @@ __device__ __forceinline__ float gelu_tanh_grad(float x) {
   const float k1 = 0.044715f;
   const float x2 = x * x;
   const float s = sigmoid_2u(k0 * fmaf(k1 * x, x2, x));
+  const float du = k0 * fmaf(3.f * k1, x2, 1.f);
+  return fmaf(2.f * x * s * (1.f - s), du, s);
+}
+__device__ __forceinline__ float gelu_tanh_grad_fma(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float k1 = 0.044715f;
+  const float x2 = x * x;
+  const float s = sigmoid_2u_fma(k0 * fmaf(k1 * x, x2, x));
   const float du = k0 * fmaf(3.f * k1, x2, 1.f);
   return fmaf(2.f * x * s * (1.f - s), du, s);
 }

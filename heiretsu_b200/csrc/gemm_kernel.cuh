@@ -156,9 +156,9 @@ __device__ __forceinline__ void gelu_chunk16(float (&v)[32], uint32_t (&pk)[16])
 #pragma unroll
   for (int j = 0; j < 16; ++j) pk[j] = pack16<F16>(v[2 * j], v[2 * j + 1]);
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {
+  for (int j = 0; j < 16; ++j) {  // half the exponentials on the transcendental unit, half on the FMA pipe
     v[2 * j] = gelu_tanh(lo16<F16>(pk[j]));
-    v[2 * j + 1] = gelu_tanh(hi16<F16>(pk[j]));
+    v[2 * j + 1] = gelu_tanh_fma(hi16<F16>(pk[j]));
   }
 }
 __device__ __forceinline__ void gelu_chunk(float (&v)[32], uint32_t (&pk)[16], bool f16) {
@@ -221,13 +221,13 @@ __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, 
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           v[8 * g + 2 * q] *= gelu_tanh_grad(lo16<true>(w[q]));
-          v[8 * g + 2 * q + 1] *= gelu_tanh_grad(hi16<true>(w[q]));
+          v[8 * g + 2 * q + 1] *= gelu_tanh_grad_fma(hi16<true>(w[q]));
         }
       } else {
 #pragma unroll
         for (int q = 0; q < 4; ++q) {
           v[8 * g + 2 * q] *= gelu_tanh_grad(lo16<false>(w[q]));
-          v[8 * g + 2 * q + 1] *= gelu_tanh_grad(hi16<false>(w[q]));
+          v[8 * g + 2 * q + 1] *= gelu_tanh_grad_fma(hi16<false>(w[q]));
         }
       }
     }

@@ -477,3 +477,34 @@ def test_gelu_reciprocal_seed_constant():
     seed_err = np.abs(r * d - 1).max()
     assert seed_err <= (5 - 2 * math.sqrt(6)) / 2 + 1e-6
     assert seed_err ** 4 < 7e-6  # two Newton steps square the error twice
+
+
+def test_exp2_fma_derivation():
+    """exp2_fma (common.cuh), restated in numpy float32: nearest-integer split by the
+    1.5 * 2^23 shift, degree-5 Taylor series of 2^f on [-1/2, 1/2], exponent-field
+    scaling. Its coefficients are (ln 2)^k / k!, and its relative error stays under the
+    Lagrange remainder bound (ln(2)/2)^6 / 6! * 2 < 5e-6 plus float32 rounding."""
+    import math
+    import re
+
+    import numpy as np
+
+    src = open(os.path.join(os.path.dirname(os.path.dirname(os.path.abspath(__file__))),
+                            "heiretsu_b200", "csrc", "common.cuh")).read()
+    body = src[src.index("float exp2_fma(float x)"):src.index("sigmoid_2u_fma")]
+    coefs = [float(c) for c in re.findall(r"([0-9]\.[0-9]+e-?[0-9]+)f", body)]
+    want = [(math.log(2) ** k) / math.factorial(k) for k in (5, 4, 3, 2, 1)]
+    assert len(coefs) == 5 and all(abs(a - b) <= 1e-7 * b for a, b in zip(coefs, want))
+    f32 = np.float32
+    x = np.concatenate([np.linspace(-125, 64, 2_000_001, dtype=np.float64),
+                        np.random.default_rng(0).uniform(-125, 64, 200_000)]).astype(np.float32)
+    t = (x + f32(12582912.0)).astype(np.float32)
+    f = (x - (t - f32(12582912.0))).astype(np.float32)
+    p = np.float32(coefs[0])
+    for c in coefs[1:] + [1.0]:
+        p = (f.astype(np.float64) * p + c).astype(np.float32)  # one rounding per step, as fmaf
+    n = t.view(np.int32) - 0x4B400000
+    got = (p.view(np.int32) + (n << 23)).view(np.float32).astype(np.float64)
+    ref = np.exp2(x.astype(np.float64))
+    rel = np.abs(got - ref) / ref
+    assert rel.max() < 5e-6 + 4e-7, rel.max()
