@@ -403,6 +403,22 @@ __device__ __forceinline__ float gelu_tanh_fma(float x) {
   return x * sigmoid_2u_fma(k0 * fmaf(k1 * x, x * x, x));
 }
 
+// The same function through the hardware tanh approximation (tanh.approx.f32,
+// relative error about 2^-11, below the 16-bit outputs' rounding):
+//   gelu(x) = h + h t,  h = x / 2,  t = tanh(x (k0 + k0 k1 x^2)).
+__device__ __forceinline__ float tanh_approx(float u) {
+  float t;
+  asm("tanh.approx.f32 %0, %1;" : "=f"(t) : "f"(u));
+  return t;
+}
+__device__ __forceinline__ float gelu_tanh_mufu(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float k01 = 0.7978845608028654f * 0.044715f;
+  const float h = 0.5f * x;
+  const float t = tanh_approx(x * fmaf(k01, x * x, k0));
+  return fmaf(h, t, h);
+}
+
 // d/dx gelu(x) = s + 2 x s (1 - s) du/dx,  du/dx = sqrt(2/pi) (1 + 3 * 0.044715 x^2)
 // (product rule on x * sigmoid(2u); equals 0.5(1+t) + 0.5 x (1-t^2) du/dx with t = tanh u).
 __device__ __forceinline__ float gelu_tanh_grad(float x) {
@@ -420,6 +436,15 @@ __device__ __forceinline__ float gelu_tanh_grad_fma(float x) {
   const float s = sigmoid_2u_fma(k0 * fmaf(k1 * x, x2, x));
   const float du = k0 * fmaf(3.f * k1, x2, 1.f);
   return fmaf(2.f * x * s * (1.f - s), du, s);
+}
+// 0.5 (1 + t) + 0.5 x (1 - t^2) du/dx with t from tanh.approx.
+__device__ __forceinline__ float gelu_tanh_grad_mufu(float x) {
+  const float k0 = 0.7978845608028654f;
+  const float k01 = 0.7978845608028654f * 0.044715f;
+  const float x2 = x * x;
+  const float t = tanh_approx(x * fmaf(k01, x2, k0));
+  const float du = fmaf(3.f * k01, x2, k0);
+  return fmaf(0.5f * x * fmaf(-t, t, 1.f), du, fmaf(0.5f, t, 0.5f));
 }
 
 // Packed fp32 pairs: sm_100 executes add / mul / fma on two fp32 values in

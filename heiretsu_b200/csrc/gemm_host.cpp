@@ -42,6 +42,15 @@ static bool tma_epilogue_enabled() {
   return on;
 }
 
+// HB_GEMM_GELU selects how the activation epilogues evaluate GELU (GemmParams::gelu_mode).
+static int gelu_mode() {
+  static const int m = [] {
+    const char* v = std::getenv("HB_GEMM_GELU");
+    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : 0;
+  }();
+  return m;
+}
+
 // (The map's element type is bf16 for either 16-bit format: loads copy bits.)
 static CUtensorMap operand_map(const at::Tensor& t, int box_rows) {
   return make_tmap_2d_bf16(t.data_ptr(), t.size(1), t.size(0), t.stride(0) * 2, 64, box_rows);
@@ -88,6 +97,7 @@ void gemm(const at::Tensor& a, const at::Tensor& b, at::Tensor& c, int64_t N, in
   p.ldc = c.stride(0);
   p.status = device_status_ptr(a.get_device());
   p.f16 = f16 ? 1 : 0;
+  p.gelu_mode = gelu_mode();
   if (bias && bias->defined()) {
     TORCH_CHECK(bias->scalar_type() == at::kFloat && bias->is_contiguous() && bias->numel() >= N && N % 4 == 0,
                 "gemm: bias must be fp32 contiguous with >= N elements");

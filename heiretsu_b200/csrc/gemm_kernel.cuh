@@ -152,20 +152,59 @@ __device__ __forceinline__ void stg_put_bf16(uint8_t* stg, int lane, const float
 // GELU epilogue core: pk <- the 16-bit pre-activation pairs; v <- GELU of those
 // rounded values (so backward differentiates exactly what forward applied).
 template <bool F16>
-__device__ __forceinline__ void gelu_chunk16(float (&v)[32], uint32_t (&pk)[16]) {
+__device__ __forceinline__ void gelu_chunk16(float (&v)[32], uint32_t (&pk)[16], int mode) {
 #pragma unroll
   for (int j = 0; j < 16; ++j) pk[j] = pack16<F16>(v[2 * j], v[2 * j + 1]);
+  if (mode == 2) {
 #pragma unroll
-  for (int j = 0; j < 16; ++j) {  // half the exponentials on the transcendental unit, half on the FMA pipe
-    v[2 * j] = gelu_tanh(lo16<F16>(pk[j]));
-    v[2 * j + 1] = gelu_tanh_fma(hi16<F16>(pk[j]));
+    for (int j = 0; j < 16; ++j) {
+      v[2 * j] = gelu_tanh_mufu(lo16<F16>(pk[j]));
+      v[2 * j + 1] = gelu_tanh_mufu(hi16<F16>(pk[j]));
+    }
+  } else if (mode == 1) {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {  // half the exponentials on the transcendental unit, half on the FMA pipe
+      v[2 * j] = gelu_tanh(lo16<F16>(pk[j]));
+      v[2 * j + 1] = gelu_tanh_fma(hi16<F16>(pk[j]));
+    }
+  } else {
+#pragma unroll
+    for (int j = 0; j < 16; ++j) {
+      v[2 * j] = gelu_tanh(lo16<F16>(pk[j]));
+      v[2 * j + 1] = gelu_tanh(hi16<F16>(pk[j]));
+    }
   }
 }
-__device__ __forceinline__ void gelu_chunk(float (&v)[32], uint32_t (&pk)[16], bool f16) {
+__device__ __forceinline__ void gelu_chunk(float (&v)[32], uint32_t (&pk)[16], bool f16, int mode) {
   if (f16) {
-    gelu_chunk16<true>(v, pk);
+    gelu_chunk16<true>(v, pk, mode);
   } else {
-    gelu_chunk16<false>(v, pk);
+    gelu_chunk16<false>(v, pk, mode);
+  }
+}
+
+// v[i] *= GELU'(16-bit pre-activation of column i), eight columns from one 16-byte word.
+template <bool F16>
+__device__ __forceinline__ void dgelu8(float* v, const uint4 raw, int mode) {
+  const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
+  if (mode == 2) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] *= gelu_tanh_grad_mufu(lo16<F16>(w[q]));
+      v[2 * q + 1] *= gelu_tanh_grad_mufu(hi16<F16>(w[q]));
+    }
+  } else if (mode == 1) {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] *= gelu_tanh_grad(lo16<F16>(w[q]));
+      v[2 * q + 1] *= gelu_tanh_grad_fma(hi16<F16>(w[q]));
+    }
+  } else {
+#pragma unroll
+    for (int q = 0; q < 4; ++q) {
+      v[2 * q] *= gelu_tanh_grad(lo16<F16>(w[q]));
+      v[2 * q + 1] *= gelu_tanh_grad(hi16<F16>(w[q]));
+    }
   }
 }
 __device__ __forceinline__ void stg_put_f32(uint8_t* stg, int lane, const float (&v)[32]) {
@@ -196,7 +235,7 @@ __device__ __forceinline__ void epi_prefetch(const GemmParams& p, const void* C,
 // Step 1: combine the prefetched operand with the accumulator row (frees `pre`).
 template <int EPI>
 __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, const uint4 (&pre)[8], int lane,
-                                                  bool f16) {
+                                                  bool f16, int gelu_mode) {
   if constexpr (EPI == kEpiF32Resid || EPI == kEpiF32Acc) {
     stg_fill<true>(stg, pre, lane);
     __syncwarp();
@@ -216,19 +255,10 @@ __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, 
 #pragma unroll
     for (int g = 0; g < 4; ++g) {
       const uint4 raw = *reinterpret_cast<const uint4*>(stg + stg_off<false>(lane, g));
-      const uint32_t w[4] = {raw.x, raw.y, raw.z, raw.w};
       if (f16) {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          v[8 * g + 2 * q] *= gelu_tanh_grad(lo16<true>(w[q]));
-          v[8 * g + 2 * q + 1] *= gelu_tanh_grad_fma(hi16<true>(w[q]));
-        }
+        dgelu8<true>(v + 8 * g, raw, gelu_mode);
       } else {
-#pragma unroll
-        for (int q = 0; q < 4; ++q) {
-          v[8 * g + 2 * q] *= gelu_tanh_grad(lo16<false>(w[q]));
-          v[8 * g + 2 * q + 1] *= gelu_tanh_grad_fma(hi16<false>(w[q]));
-        }
+        dgelu8<false>(v + 8 * g, raw, gelu_mode);
       }
     }
     __syncwarp();
@@ -306,7 +336,7 @@ __device__ __forceinline__ void epi_finish(const GemmParams& p, void* C, int m_b
     // Pre-activation (rounded to the 16-bit format) goes to AUX; GELU of that
     // rounded value goes to C, so backward differentiates exactly what forward applied.
     uint32_t pk[16];
-    gelu_chunk(v, pk, p.f16 != 0);
+    gelu_chunk(v, pk, p.f16 != 0, p.gelu_mode);
 #pragma unroll
     for (int g = 0; g < 4; ++g)
       *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
@@ -355,7 +385,7 @@ __device__ __forceinline__ void epi_finish_tma(const GemmParams& p, const CUtens
     // pre-activation (16-bit) -> first 2 KB of the staging tile; GELU of the
     // rounded value -> second 2 KB; two stores.
     uint32_t pk[16];
-    gelu_chunk(v, pk, p.f16 != 0);
+    gelu_chunk(v, pk, p.f16 != 0, p.gelu_mode);
 #pragma unroll
     for (int g = 0; g < 4; ++g)
       *reinterpret_cast<uint4*>(stg + stg_off<false>(lane, g)) =
@@ -673,7 +703,7 @@ __global__ void __launch_bounds__(kGemmThreads, 1)
               bias_done = true;
             }
           }
-          if (reads) epi_apply_operand<EPI>(v, stg, pre, lane, p.f16 != 0);
+          if (reads) epi_apply_operand<EPI>(v, stg, pre, lane, p.f16 != 0, p.gelu_mode);
           if (reads && c + 1 < CH && n0 + 32 < p.N) epi_prefetch<EPI>(p, C, m_base, n0 + 32, lane, pre);
           if (tma) {
             epi_finish_tma<EPI>(p, &tmC, &tmX, row, n0, v, stg, lane, bias_done);

@@ -73,6 +73,11 @@ struct GemmParams {
   // 16-bit format of A, B and of the 16-bit outputs / AUX: 0 bf16, 1 fp16.
   int f16;
 
+  // GELU / GELU' evaluation in the activation epilogues: 0 sigmoid form, one
+  // ex2.approx per element; 1 the same with every other exponential on the FMA
+  // pipe; 2 tanh.approx.
+  int gelu_mode;
+
   // Expert-parallel combine epilogue (row-grouped GEMM with a 16-bit output;
   // cmb_world = 0: off). Output row p of this rank's expert window holds the
   // expert output of routing slot cmb_inv[p] = t * cmb_K + k (-1: padding row).
