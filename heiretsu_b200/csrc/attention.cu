@@ -60,10 +60,16 @@ __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 
 // uses three-input max over independent chains and is taken on raw scores
 // (the scale is positive); exponent arguments and row sums are computed on
 // fp32 pairs (one f32x2 instruction for two columns).
+//
+// P smem is still being read by the previous PV MMA until `pv_bar` completes its
+// phase `pv_phase` (no wait when pv_bar is null): the wait sits between the max
+// pass and the first P store, so the max pass overlaps that MMA. `ok` turns
+// false when the wait gives up.
 template <bool DIAG, bool DROP, bool F16>
 __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
                                               float scale_log2, float& m, float& l, uint32_t dkey, uint64_t pair_row,
-                                              uint32_t dthresh, float dscale) {
+                                              uint32_t dthresh, float dscale, uint64_t* pv_bar, uint32_t pv_phase,
+                                              int* status, bool& ok) {
   float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
@@ -87,6 +93,10 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
   const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
   const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_new, -m_new);
   uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  if (pv_bar != nullptr && !mbar_wait(pv_bar, pv_phase, status, 27)) {
+    ok = false;
+    return 0.f;
+  }
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
     uint32_t va[32], vb[32];
@@ -316,17 +326,18 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         }
         if (lane == 0 && sub == 0 && j < 8) HB_TRACE(8 + 24 * g + j);
         tc_fence_after();
-        // P smem is free once PV_{j-1} has completed.
-        if (j > 0 && !mbar_wait(&bar_o[g][(j - 1) & 1], ((j - 1) >> 1) & 1, p.status, 27)) {
-          ok = false;
-          break;
-        }
         if (lane == 0 && sub == 0 && j < 8) HB_TRACE(16 + 24 * g + j);
+        // P smem is free once PV_{j-1} has completed (waited inside, after the max pass).
+        uint64_t* pv_bar = j > 0 ? &bar_o[g][(j - 1) & 1] : nullptr;
+        const uint32_t pv_phase = ((j - 1) >> 1) & 1;
         const float alpha =
             (j == my_qt) ? softmax_tile<true, DROP, F16>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
-                                                    pair_row, p.drop.thresh, p.drop.scale)
+                                                    pair_row, p.drop.thresh, p.drop.scale, pv_bar, pv_phase,
+                                                    p.status, ok)
                          : softmax_tile<false, DROP, F16>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
-                                                     pair_row, p.drop.thresh, p.drop.scale);
+                                                     pair_row, p.drop.thresh, p.drop.scale, pv_bar, pv_phase,
+                                                     p.status, ok);
+        if (!ok) break;
         fence_proxy_async_smem();
         tc_fence_before();
         __syncwarp();
@@ -430,6 +441,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
   tc_fence_after();
   const uint32_t tmem = tmem_slot;
   if (threadIdx.x == 0) HB_TRACE(0);
+  // dQ alternates between two 64-column buffers (tile ii in buffer ii & 1), so the
+  // softmax warps drain tile ii-1's dQ after handing over tile ii's P^T / dS^T.
   const uint32_t tS = tmem, tDP = tmem + 128, tDV = tmem + 256, tDK = tmem + 320, tDQ = tmem + 384;
   const long lse_base = ((long)b * p.nh + h) * p.Tpad;
 
@@ -508,8 +521,8 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
         }
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
-          mma_f16_ss(tDQ, sw128_desc(dsa + ks * 2048, 16384, 1024), sw128_desc(ka + ks * 2048, 8192, 1024), idQ,
-                     ks > 0);
+          mma_f16_ss(tDQ + (ii & 1) * 64, sw128_desc(dsa + ks * 2048, 16384, 1024),
+                     sw128_desc(ka + ks * 2048, 8192, 1024), idQ, ks > 0);
         mma_commit(&bar_mma);
         mma_commit(&bar_empty[ii % BWD_STAGES]);
         if (next) issue_half(ii + 1, 1);
@@ -533,10 +546,11 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
     // dQ rows of this warp (32 queries x 32 columns) leave through one bulk
     // tensor reduce-add into the fp32 accumulator (the add happens in L2).
     uint8_t* dq_stg = sDQ + (warp - 2) * 4096;
-    auto flush_dq = [&](int qi) {
+    auto flush_dq = [&](int ii) {
+      const int qi = kt + ii;
       tc_fence_after();
       float v[32];
-      tmem_ld32(tDQ + g * 32 + lane_off, v);
+      tmem_ld32(tDQ + (ii & 1) * 64 + g * 32 + lane_off, v);
       if (lane == 0) bulk_wait_group_read0();  // the previous reduce has read the staging tile
       __syncwarp();
 #pragma unroll
@@ -623,15 +637,14 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
             dd[i >> 1] = pack16<F16>(d0, d1);
           }
         }
-        // The previous tile's MMAs read P^T / dS^T smem and wrote dQ: wait once,
-        // flush that dQ half, then overwrite this half of P^T / dS^T.
+        // The previous tile's MMAs read P^T / dS^T smem: wait once before
+        // overwriting this half (its dQ is drained after the hand-over below).
         if (!waited) {
           if (!mbar_wait(&bar_mma, (ii - 1) & 1, p.status, 48)) {
             ok = false;
             break;
           }
           if (lane == 0 && sub == 0 && ii < 8) HB_TRACE(32 + 24 * g + ii);
-          flush_dq(qi - 1);
           waited = true;
         }
 #pragma unroll
@@ -647,9 +660,12 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       __syncwarp();
       if (lane == 0) mbar_arrive(&bar_p[g]);
       if (lane == 0 && sub == 0 && ii < 8) HB_TRACE(40 + 24 * g + ii);
+      // Tile ii-1's dQ (complete: bar_mma was waited above) leaves its buffer
+      // before this warpgroup can hand over tile ii+1, whose dQ MMA reuses it.
+      if (ii > 0) flush_dq(ii - 1);
     }
     if (ok && mbar_wait(&bar_mma, (n_i - 1) & 1, p.status, 49)) {
-      flush_dq(kt + n_i - 1);
+      flush_dq(n_i - 1);
       // dK, dV columns [g*32, g*32+32) -> bf16 into the K / V columns of dqkv.
       __nv_bfloat16* drow = p.out + ((long)b * p.T + key) * p.ld_out;
       float v[32];
@@ -823,7 +839,8 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
 
 // Trace buffer for the next attention launches (nullptr turns tracing off).
 // Forward slots per CTA: 0 start, 1 Q ready (MMA warp), 2 end; for KV tile j < 8
-// and query tile g: 8+24g+j S ready, 16+24g+j previous PV done, 24+24g+j P written.
+// and query tile g: 8+24g+j S ready, 16+24g+j softmax start (the previous PV is
+// waited for inside, after the row max), 24+24g+j P written.
 // Backward slots per CTA: 0 start, 1 K/V and first Q/dO ready, 2 end; for query
 // tile i < 8: 8+i / 16+i P^T half 0 / half 1 consumed by the MMA warp; for half g:
 // 24+24g+i S^T/dP^T ready, 32+24g+i previous tile's MMAs done, 40+24g+i P^T/dS^T written.

@@ -1,5 +1,14 @@
-"""Fused expert parallelism (local-expert windows, partial outputs summed over
-NVLink) against the same model run with every expert on one GPU.
+"""Fused expert parallelism (local-expert windows; the second expert GEMM pushes
+each weighted output row into every EP rank's slot buffer over NVLink) against
+the same model run with every expert on one GPU.
+
+The slots hold 16-bit rows, so the EP forward rounds each weighted expert output
+once more than the one-GPU combine (which sums in fp32). That can flip the top-k
+choice of a token whose second and third router logits are within that rounding
+of each other in a later MoE layer, and the experts such a token leaves or joins
+then see a different batch. The routing of every MoE call is recorded on both
+sides: a few flipped tokens are allowed, the experts (and router) of their layer
+are compared loosely, everything else strictly.
 
 One process per GPU; skipped with fewer than two GPUs.
 """
@@ -44,6 +53,17 @@ def _worker(rank, world, port, q):
         from heiretsu_b200.trainer import mark_tp_sharded, replication_weight
         from heiretsu_b200.utils.ckpt import load_from_full, shard_from_full
 
+        from heiretsu_b200.models import fused_moe
+
+        routes = []  # top-k expert ids [N, k] of every MoE forward, in call order
+        orig_route = fused_moe.moe_route_and_experts
+
+        def recording_route(moe, xn2, flat=None):
+            aux, state = orig_route(moe, xn2, flat)
+            routes.append(state[1].detach().sort(dim=1).values.clone())
+            return aux, state
+
+        fused_moe.moe_route_and_experts = recording_route
         topo = init_topology(dp=1, ep=world)
         cfg = GPTConfig(block_size=256, vocab_size=1000, n_layer=4, n_head=4, n_embed=256, dropout=0.0,
                         num_experts=8, top_k=2, moe_freq=2)
@@ -62,6 +82,8 @@ def _worker(rank, world, port, q):
         _, loss_d, aux_d = dense(x, y, return_logits=False)
         (loss_d + aux_d).backward()
         dgrads = {n: p.main_grad.detach().clone() for n, p in dense.named_parameters()}
+        moe_blocks = [i for i, blk in enumerate(dense.tr.h) if hasattr(blk, "moe")]
+        dense_routes = routes[:len(moe_blocks)]
 
         model = GPT(cfg, topo=topo).to(dev)  # 4 experts per rank
         load_from_full(model, full)
@@ -69,6 +91,7 @@ def _worker(rank, world, port, q):
         flat = FlatParams(model, dev, weight_of=replication_weight(topo))
         model.fused = True
         for _ in range(2):  # the second pass reuses every buffer and barrier epoch
+            del routes[:]
             flat.zero_grad()
             _, loss_e, aux_e = model(x, y, return_logits=False)
             (loss_e + aux_e).backward()
@@ -76,17 +99,35 @@ def _worker(rank, world, port, q):
             check_status()
             check_comm_status(rank)
         expect = shard_from_full(model, {**full, **dgrads})
-        worst, worst_name = 0.0, ""
+        # (block, global expert) pairs touched by a token routed differently
+        loose, flips = set(), 0
+        for blk_i, rd, re_ in zip(moe_blocks, dense_routes, routes):
+            bad = (rd != re_).any(dim=1)
+            flips = max(flips, int(bad.sum().item()))
+            for e in torch.cat([rd[bad], re_[bad]]).flatten().tolist():
+                loose.add((blk_i, int(e)))
+        El = cfg.num_experts // world
+        worst, worst_name, worst_loose = 0.0, "", 0.0
         for n, p in model.named_parameters():
             r = _rel(p.main_grad, expect[n])
-            if r > worst:
+            parts = n.split(".")
+            blk_i = int(parts[2]) if parts[:2] == ["tr", "h"] else -1
+            is_loose = False
+            if "experts" in parts:
+                is_loose = (blk_i, rank * El + int(parts[parts.index("experts") + 1])) in loose
+            elif "router" in parts:
+                is_loose = any(b == blk_i for b, _ in loose)
+            if is_loose:
+                worst_loose = max(worst_loose, r)
+            elif r > worst:
                 worst, worst_name = r, n
-        q.put((rank, abs(loss_e.item() - loss_d.item()), abs(aux_e.item() - aux_d.item()), worst, worst_name))
+        q.put((rank, abs(loss_e.item() - loss_d.item()), abs(aux_e.item() - aux_d.item()), worst, worst_name,
+               flips, worst_loose))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
         import traceback
-        q.put((rank, traceback.format_exc(), None, None, None))
+        q.put((rank, traceback.format_exc(), None, None, None, None, None))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -101,7 +142,9 @@ def test_fused_ep2_matches_single_gpu_experts():
     res = [q.get(timeout=300) for _ in ps]
     for p in ps:
         p.join(timeout=60)
-    for rank, dloss, daux, worst, name in res:
+    for rank, dloss, daux, worst, name, flips, worst_loose in res:
         assert not isinstance(dloss, str), dloss
         assert dloss < 1e-3 and daux < 1e-4, (rank, dloss, daux)
+        assert flips <= 2, (rank, "tokens routed differently in one layer", flips)
         assert worst < 1e-2, (rank, worst, name)
+        assert worst_loose < 0.1, (rank, "experts of a flipped token", worst_loose)
