@@ -16,7 +16,9 @@
 //               128B-swizzled smem (A operand of the PV MMA), O accumulated
 //               in registers with the online-softmax rescale.
 //   While one warpgroup runs its softmax, the MMA warp computes the other
-//   tile's S or PV, so tensor core and ALUs overlap inside the CTA.
+//   tile's S or PV, so tensor core and ALUs overlap inside the CTA. A
+//   warpgroup releases S as soon as its last TMEM load of S has landed, and
+//   the next S is computed while it still exponentiates.
 //   TMEM: per tile S [128 cols] + O double buffer [2 x 64 cols].
 //
 // Backward, one CTA per (key tile of 128, head, batch), 320 threads, FA2
@@ -27,10 +29,13 @@
 //   then dV += P^T dO_i, dK += dS^T Q_i and dQ_i = dS K (the same smem tiles
 //   serve as K-major or MN-major operands); dQ_i is added to an fp32
 //   accumulator by bulk tensor reduce-adds (one 32x32 block per warp).
-//   The next tile's first half is computed while the second half of the
-//   current one is still in its softmax.
+//   As soon as a warpgroup has stored its half of P^T / dS^T, the MMA warp
+//   issues that half of the next tile's S^T / dP^T, ahead of the current
+//   tile's dV / dK / dQ, so the next softmax starts one MMA later; dQ
+//   alternates between two TMEM buffers and is drained off that path.
 #include <cuda_bf16.h>
 
+#include <cstdlib>
 #include <stdexcept>
 
 #include "attention_common.cuh"
@@ -63,13 +68,16 @@ __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 
 //
 // P smem is still being read by the previous PV MMA until `pv_bar` completes its
 // phase `pv_phase` (no wait when pv_bar is null): the wait sits between the max
-// pass and the first P store, so the max pass overlaps that MMA. `ok` turns
-// false when the wait gives up.
-template <bool DIAG, bool DROP, bool F16>
+// pass and the first P store, so the max pass overlaps that MMA. Once the last
+// TMEM load of S has completed, each warp arrives on `s_free`: the MMA warp may
+// then compute the next S into the same columns while this warp still
+// exponentiates and stores its last 64 columns. `ok` turns false when the wait
+// gives up.
+template <bool DIAG, bool DROP, bool F16, int EXPF>
 __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, uint8_t* sP, int row, int key0, int q,
                                               float scale_log2, float& m, float& l, uint32_t dkey, uint64_t pair_row,
                                               uint32_t dthresh, float dscale, uint64_t* pv_bar, uint32_t pv_phase,
-                                              int* status, bool& ok) {
+                                              uint64_t* s_free, int* status, bool& ok, uint64_t* stamp) {
   float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
 #pragma unroll 1
   for (int h = 0; h < 2; ++h) {
@@ -93,6 +101,7 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
   const float alpha = (m == -INFINITY) ? 0.f : fast_exp2(m - m_new);
   const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m_new, -m_new);
   uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  if (stamp != nullptr) *stamp = globaltimer_ns();  // phase trace: row max done
   if (pv_bar != nullptr && !mbar_wait(pv_bar, pv_phase, status, 27)) {
     ok = false;
     return 0.f;
@@ -104,6 +113,11 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
     tmem_ld32_issue(tS + lane_off + (2 * h + 1) * 32, vb);
     tmem_wait_ld_regs(va);
     tmem_pin_regs(vb);
+    if (h == 1) {  // every read of S is complete
+      tc_fence_before();
+      __syncwarp();
+      if ((threadIdx.x & 31) == 0) mbar_arrive(s_free);
+    }
 #pragma unroll
     for (int half = 0; half < 2; ++half) {
       const uint32_t* v = half ? vb : va;
@@ -113,7 +127,12 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
       for (int i = 0; i < 32; i += 2) {
         float t0, t1;
         f2_unpack(f2_fma(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), t0, t1);
-        float p0 = fast_exp2(t0), p1 = fast_exp2(t1);
+        float p0 = fast_exp2(t0), p1;
+        if ((EXPF == 1 && (i & 6) == 6) || (EXPF == 2 && (i & 2) == 2)) {
+          p1 = exp2_fma(t1);  // this share on the FMA pipe
+        } else {
+          p1 = fast_exp2(t1);
+        }
         if (DIAG) {
           if (key0 + c * 32 + i > q) p0 = 0.f;
           if (key0 + c * 32 + i + 1 > q) p1 = 0.f;
@@ -165,7 +184,8 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   uint8_t* sQ = smem;                          // [2][16 KB]
   uint8_t* sSlot = smem + 2 * kTileBytes;      // [3][16 KB]
   uint8_t* sP = sSlot + FWD_SLOTS * kTileBytes;  // [2][32 KB]
-  __shared__ uint64_t bar_q, bar_full[FWD_SLOTS], bar_empty[FWD_SLOTS], bar_s[2], bar_p[2], bar_o[2][2], bar_done;
+  __shared__ uint64_t bar_q, bar_full[FWD_SLOTS], bar_empty[FWD_SLOTS], bar_s[2], bar_sfree[2], bar_p[2], bar_o[2][2],
+      bar_done;
   __shared__ uint32_t tmem_slot;
 
   const int warp = threadIdx.x >> 5, lane = threadIdx.x & 31;
@@ -191,6 +211,7 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     }
     for (int g = 0; g < 2; ++g) {
       mbar_init(&bar_s[g], 1);
+      mbar_init(&bar_sfree[g], 4);
       mbar_init(&bar_p[g], 4);
       mbar_init(&bar_o[g][0], 1);
       mbar_init(&bar_o[g][1], 1);
@@ -271,25 +292,32 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       } else {
         ok = false;
       }
+      // Step j: S_{j+1} of each tile as soon as its softmax has read S_j (s_free),
+      // then PV_j of each tile once its P_j is in smem.
       for (int j = 0; j < n_kv && ok; ++j) {
         const bool next = j + 1 < n_kv;
-        if (hasA && j <= qt[0]) {
+        const bool a_on = hasA && j <= qt[0];
+        if (a_on && j + 1 <= qt[0]) {
+          if (!mbar_wait(&bar_sfree[0], j & 1, p.status, 29)) break;
+          tc_fence_after();
+          if (!item(fwd_k_item(j + 1), ka)) break;
+          issue_s(0, ka);
+        }
+        if (next) {
+          if (!mbar_wait(&bar_sfree[1], j & 1, p.status, 30)) break;
+          tc_fence_after();
+          if (!item(fwd_k_item(j + 1), ka)) break;
+          issue_s(1, ka);
+          mma_commit(&bar_empty[fwd_k_item(j + 1) % FWD_SLOTS]);
+        }
+        if (a_on) {
           if (!mbar_wait(&bar_p[0], j & 1, p.status, 23)) break;
           tc_fence_after();
-          if (j + 1 <= qt[0]) {
-            if (!item(fwd_k_item(j + 1), ka)) break;
-            issue_s(0, ka);
-          }
           if (!item(fwd_v_item(j, n_kv), va)) break;
           issue_pv(0, j, va);
         }
         if (!mbar_wait(&bar_p[1], j & 1, p.status, 24)) break;
         tc_fence_after();
-        if (next) {
-          if (!item(fwd_k_item(j + 1), ka)) break;
-          issue_s(1, ka);
-          mma_commit(&bar_empty[fwd_k_item(j + 1) % FWD_SLOTS]);
-        }
         if (!item(fwd_v_item(j, n_kv), va)) break;
         issue_pv(1, j, va);
         mma_commit(&bar_empty[fwd_v_item(j, n_kv) % FWD_SLOTS]);
@@ -330,13 +358,24 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
         // P smem is free once PV_{j-1} has completed (waited inside, after the max pass).
         uint64_t* pv_bar = j > 0 ? &bar_o[g][(j - 1) & 1] : nullptr;
         const uint32_t pv_phase = ((j - 1) >> 1) & 1;
-        const float alpha =
-            (j == my_qt) ? softmax_tile<true, DROP, F16>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
-                                                    pair_row, p.drop.thresh, p.drop.scale, pv_bar, pv_phase,
-                                                    p.status, ok)
-                         : softmax_tile<false, DROP, F16>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey,
-                                                     pair_row, p.drop.thresh, p.drop.scale, pv_bar, pv_phase,
-                                                     p.status, ok);
+        uint64_t* stamp = (p.trace != nullptr && lane == 0 && sub == 0 && j < 8)
+                              ? p.trace + (long)blockIdx.x * kTraceSlots + 56 + 8 * g + j
+                              : nullptr;
+#define HB_SOFTMAX(DIAG, EXPF)                                                                               \
+  softmax_tile<DIAG, DROP, F16, EXPF>(tS, lane_off, myP, row, j * kTile, q, p.scale_log2, m, l, dkey, pair_row, \
+                                      p.drop.thresh, p.drop.scale, pv_bar, pv_phase, &bar_sfree[g], p.status, ok, \
+                                      stamp)
+        float alpha;
+        if (j == my_qt) {
+          alpha = HB_SOFTMAX(true, 0);
+        } else if (p.exp_fma == 1) {
+          alpha = HB_SOFTMAX(false, 1);
+        } else if (p.exp_fma == 2) {
+          alpha = HB_SOFTMAX(false, 2);
+        } else {
+          alpha = HB_SOFTMAX(false, 0);
+        }
+#undef HB_SOFTMAX
         if (!ok) break;
         fence_proxy_async_smem();
         tc_fence_before();
@@ -493,10 +532,17 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
       for (int ii = 0; ii < n_i && ok; ++ii) {
         const uint32_t qa = smem_u32(sStage + (ii % BWD_STAGES) * BWD_STAGE);
         const uint32_t doa = qa + kTileBytes;
-        // half 0 of P^T / dS^T (queries 0..63) is in smem
+        // Half g of P^T / dS^T in smem means half g of S^T / dP^T has been read:
+        // the next tile's half g goes to the tensor core first (it heads the
+        // softmax warps' critical path), then this tile's dV / dK / dQ.
         if (!mbar_wait(&bar_p[0], ii & 1, p.status, 43)) break;
         if (ii < 8) HB_TRACE(8 + ii);
         tc_fence_after();
+        const bool next = ii + 1 < n_i;
+        if (next) {
+          if (!stage_ready(ii + 1)) break;
+          issue_half(ii + 1, 0);
+        }
 #pragma unroll
         for (int ks = 0; ks < 4; ++ks) {
           mma_f16_ss(tDV, sw128_desc(pa + ks * 32, 16, 1024), sw128_desc(doa + ks * 2048, 8192, 1024), idKM,
@@ -504,14 +550,10 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
           mma_f16_ss(tDK, sw128_desc(dsa + ks * 32, 16, 1024), sw128_desc(qa + ks * 2048, 8192, 1024), idKM,
                      (ii > 0 || ks > 0));
         }
-        const bool next = ii + 1 < n_i;
-        if (next) {
-          if (!stage_ready(ii + 1)) break;
-          issue_half(ii + 1, 0);
-        }
         if (!mbar_wait(&bar_p[1], ii & 1, p.status, 44)) break;
         if (ii < 8) HB_TRACE(16 + ii);
         tc_fence_after();
+        if (next) issue_half(ii + 1, 1);
 #pragma unroll
         for (int ks = 4; ks < 8; ++ks) {
           mma_f16_ss(tDV, sw128_desc(pa + 16384 + (ks - 4) * 32, 16, 1024), sw128_desc(doa + ks * 2048, 8192, 1024),
@@ -525,7 +567,6 @@ __global__ void __launch_bounds__(BWD_THREADS, 1)
                      sw128_desc(ka + ks * 2048, 8192, 1024), idQ, ks > 0);
         mma_commit(&bar_mma);
         mma_commit(&bar_empty[ii % BWD_STAGES]);
-        if (next) issue_half(ii + 1, 1);
       }
       mma_commit(&bar_done);
       mbar_wait(&bar_done, 0, p.status, 45);
@@ -769,6 +810,15 @@ static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
   ((drop_on) ? ((f16) ? kern<true, true> : kern<true, false>)                                \
              : ((f16) ? kern<false, true> : kern<false, false>))
 
+// HB_ATTN_EXP_FMA (0, 1, 2) sets AttnParams::exp_fma of the head_dim 64 forward.
+static int attn_exp_fma() {
+  static const int m = [] {
+    const char* v = std::getenv("HB_ATTN_EXP_FMA");
+    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : 0;
+  }();
+  return m;
+}
+
 void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, long ld_out, float* lse, int B,
                      int T, int nh, int Tpad, float scale, const DropoutArgs& drop, int h0, int nh_total, int* status,
                      bool f16, cudaStream_t s) {
@@ -790,6 +840,7 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
   p.trace = g_attn_trace;
+  p.exp_fma = attn_exp_fma();
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
@@ -840,7 +891,7 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
 // Trace buffer for the next attention launches (nullptr turns tracing off).
 // Forward slots per CTA: 0 start, 1 Q ready (MMA warp), 2 end; for KV tile j < 8
 // and query tile g: 8+24g+j S ready, 16+24g+j softmax start (the previous PV is
-// waited for inside, after the row max), 24+24g+j P written.
+// waited for inside, after the row max), 56+8g+j row max done, 24+24g+j P written.
 // Backward slots per CTA: 0 start, 1 K/V and first Q/dO ready, 2 end; for query
 // tile i < 8: 8+i / 16+i P^T half 0 / half 1 consumed by the MMA warp; for half g:
 // 24+24g+i S^T/dP^T ready, 32+24g+i previous tile's MMAs done, 40+24g+i P^T/dS^T written.

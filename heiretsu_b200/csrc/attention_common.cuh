@@ -25,6 +25,9 @@ struct AttnParams {
   // element ((b * nh_total + h0 + h) * T + q) * T + k.
   DropoutArgs drop;
   int h0, nh_total;
+  // Forward softmax (head_dim 64): share of the exponentials evaluated on the FMA
+  // pipe (exp2_fma) instead of the transcendental unit: 0 none, 1 one in eight, 2 one in four.
+  int exp_fma;
 };
 
 // Phase tracing: with a trace buffer set, the kernels stamp %globaltimer at

@@ -532,6 +532,12 @@ __device__ __forceinline__ uint16_t from_f32(float x) {
   }
 }
 
+// x rounded to the 16-bit format (nearest even) and widened back to fp32.
+template <bool F16>
+__device__ __forceinline__ float round16(float x) {
+  return to_f32<F16>(from_f32<F16>(x));
+}
+
 __device__ __forceinline__ float warp_sum(float v) {
 #pragma unroll
   for (int o = 16; o > 0; o >>= 1) v += __shfl_xor_sync(0xffffffffu, v, o);

@@ -266,7 +266,9 @@ __device__ __forceinline__ void epi_apply_operand(float (&v)[32], uint8_t* stg, 
 }
 
 // Expert-parallel combine: this thread's output row, scaled by its routing
-// weight, pushed into slot k, row t of every EP rank's receive buffer.
+// weight, pushed into slot k, row t of every EP rank's receive buffer. The row
+// is first rounded to the 16-bit output format (the value C holds), so a slot
+// holds round16(w * round16(acc)): the term the one-GPU combine adds.
 __device__ __forceinline__ void epi_combine_push(const GemmParams& p, int row, int n0, const float (&v)[32]) {
   if (row >= p.M) return;
   const int inv = p.cmb_inv[row];
@@ -276,10 +278,11 @@ __device__ __forceinline__ void epi_combine_push(const GemmParams& p, int row, i
   uint32_t pk[16];
   if (p.f16) {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) pk[j] = pack16<true>(w * v[2 * j], w * v[2 * j + 1]);
+    for (int j = 0; j < 16; ++j) pk[j] = pack16<true>(w * round16<true>(v[2 * j]), w * round16<true>(v[2 * j + 1]));
   } else {
 #pragma unroll
-    for (int j = 0; j < 16; ++j) pk[j] = pack16<false>(w * v[2 * j], w * v[2 * j + 1]);
+    for (int j = 0; j < 16; ++j)
+      pk[j] = pack16<false>(w * round16<false>(v[2 * j]), w * round16<false>(v[2 * j + 1]));
   }
   const long off = (((long)k * p.cmb_N + t) * p.N + n0) * 2;  // bytes
 #pragma unroll 1

@@ -145,6 +145,10 @@ __global__ void moe_gather_kernel(const __nv_bfloat16* __restrict__ x, const int
   uint4* dst = reinterpret_cast<uint4*>(xp + (long)(r - lo) * H);
   for (int j = lane; j < H / 8; j += 32) dst[j] = src[j];
 }
+// out[t] = resid[t] + sum_k round16(w_tk * y_tk) over the experts of this window,
+// k ascending. The terms are rounded to 16 bits exactly as the expert-parallel
+// combine's slot rows are (and summed in the same order), so the combined
+// output does not depend on the EP degree.
 template <bool F16>
 __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const int* __restrict__ pos,
                                    const float* __restrict__ topw, const float* __restrict__ resid, int N, int K,
@@ -162,10 +166,11 @@ __global__ void moe_combine_kernel(const __nv_bfloat16* __restrict__ yp, const i
       if (!HB_DCHECK(r - lo < cap, status, 301)) continue;
       const float wk = topw[(long)t * K + k];
       const uint2 raw = *reinterpret_cast<const uint2*>(yp + (long)(r - lo) * H + j);
-      acc.x += wk * lo16<F16>(raw.x);
-      acc.y += wk * hi16<F16>(raw.x);
-      acc.z += wk * lo16<F16>(raw.y);
-      acc.w += wk * hi16<F16>(raw.y);
+      // each weighted term rounded to 16 bits, as the EP combine's slots hold it
+      acc.x += round16<F16>(wk * lo16<F16>(raw.x));
+      acc.y += round16<F16>(wk * hi16<F16>(raw.x));
+      acc.z += round16<F16>(wk * lo16<F16>(raw.y));
+      acc.w += round16<F16>(wk * hi16<F16>(raw.y));
     }
     *reinterpret_cast<float4*>(out + (long)t * H + j) = acc;
   }

@@ -8,7 +8,7 @@ Forward, for the LayerNorm output xn [N, H] of this rank's tokens:
     gather     xp[pos[t, k]] = xn[t]                 (expert-grouped, 128-padded)
     expert 1   hp = GELU(xp W1_e^T)                  (row-grouped tcgen05 GEMM)
     expert 2   yp = hp W2_e^T                        (row-grouped tcgen05 GEMM)
-    combine    x_new[t] = x[t] + sum_k w[t, k] yp[pos[t, k]]
+    combine    x_new[t] = x[t] + sum_k round16(w[t, k] yp[pos[t, k]])   (fp32 sum, k ascending)
 
 The local experts' w1 (and w2) are stored back to back in the flat parameter
 buffer, so each grouped GEMM reads one [E*I, H] weight matrix and picks the
@@ -23,12 +23,14 @@ token ever has to travel: every EP rank routes all of its tokens (the router
 is replicated), gathers only the rows of its own experts (window
 [e0, e0 + E/ep) of the padded segments) and runs those experts once. The
 combine's exchange happens inside the second expert GEMM: its epilogue
-writes each output row, times the row's routing weight, as 16 bits into
-slot k, row t of every EP rank's peer-mapped slot buffer (the (token, k)
-of a row comes from the inverse map the gather records). Each (t, k) is
-owned by exactly one rank, so every slot row is written once. After one
-bounded NVLink barrier, every rank adds x + slot 0 + ... + slot K-1 in
-that order (moe_slots_reduce), so every replica gets the same bits. In
+writes each output row (rounded to 16 bits, the value yp holds), times the
+row's routing weight, as 16 bits into slot k, row t of every EP rank's
+peer-mapped slot buffer (the (token, k) of a row comes from the inverse map
+the gather records). Each (t, k) is owned by exactly one rank, so every slot
+row is written once. After one bounded NVLink barrier, every rank adds
+x + slot 0 + ... + slot K-1 in that order (moe_slots_reduce), so every
+replica gets the same bits, and they are the bits of the one-GPU combine,
+which rounds the same terms to 16 bits: the forward does not depend on ep. In
 backward the combine needs no traffic (every rank holds the full
 gradient). The input gradients of the local experts and the routing-weight
 gradients of the local slots are summed over NVLink (peer_sum) before the

@@ -2,13 +2,14 @@
 each weighted output row into every EP rank's slot buffer over NVLink) against
 the same model run with every expert on one GPU.
 
-The slots hold 16-bit rows, so the EP forward rounds each weighted expert output
-once more than the one-GPU combine (which sums in fp32). That can flip the top-k
-choice of a token whose second and third router logits are within that rounding
-of each other in a later MoE layer, and the experts such a token leaves or joins
-then see a different batch. The routing of every MoE call is recorded on both
-sides: a few flipped tokens are allowed, the experts (and router) of their layer
-are compared loosely, everything else strictly.
+The slots hold 16-bit rows round16(w * round16(acc)), and the one-GPU combine
+adds exactly those terms in the same order, so the forward is the same on
+either side; backward sums the expert input gradients across EP ranks in a
+different order (fp32). Each parameter's gradient must match the one-GPU run
+within 1e-2, or else be as close to an fp32 oracle (the plain PyTorch engine in
+fp32 on the same weights and tokens) as the one-GPU fused run is:
+err(EP) <= 2 err(one GPU) + 5e-3. The routing of every MoE call is recorded on
+both sides; at most two tokens per layer may choose differently.
 
 One process per GPU; skipped with fewer than two GPUs.
 """
@@ -85,6 +86,13 @@ def _worker(rank, world, port, q):
         moe_blocks = [i for i, blk in enumerate(dense.tr.h) if hasattr(blk, "moe")]
         dense_routes = routes[:len(moe_blocks)]
 
+        oracle = GPT(cfg).to(dev)  # plain PyTorch engine, fp32
+        oracle.load_state_dict(full)
+        _, loss_o, aux_o = oracle(x, y, return_logits=False)
+        (loss_o + aux_o).backward()
+        ograds = {n: p.grad.detach().clone() for n, p in oracle.named_parameters()}
+        del oracle
+
         model = GPT(cfg, topo=topo).to(dev)  # 4 experts per rank
         load_from_full(model, full)
         mark_tp_sharded(model)
@@ -99,35 +107,22 @@ def _worker(rank, world, port, q):
             check_status()
             check_comm_status(rank)
         expect = shard_from_full(model, {**full, **dgrads})
-        # (block, global expert) pairs touched by a token routed differently
-        loose, flips = set(), 0
-        for blk_i, rd, re_ in zip(moe_blocks, dense_routes, routes):
-            bad = (rd != re_).any(dim=1)
-            flips = max(flips, int(bad.sum().item()))
-            for e in torch.cat([rd[bad], re_[bad]]).flatten().tolist():
-                loose.add((blk_i, int(e)))
-        El = cfg.num_experts // world
-        worst, worst_name, worst_loose = 0.0, "", 0.0
+        expect_o = shard_from_full(model, {**full, **ograds})
+        flips = max(int((rd != re_).any(dim=1).sum().item()) for rd, re_ in zip(dense_routes, routes))
+        bad = []  # (name, err vs one GPU, err vs oracle, one GPU's err vs oracle)
         for n, p in model.named_parameters():
             r = _rel(p.main_grad, expect[n])
-            parts = n.split(".")
-            blk_i = int(parts[2]) if parts[:2] == ["tr", "h"] else -1
-            is_loose = False
-            if "experts" in parts:
-                is_loose = (blk_i, rank * El + int(parts[parts.index("experts") + 1])) in loose
-            elif "router" in parts:
-                is_loose = any(b == blk_i for b, _ in loose)
-            if is_loose:
-                worst_loose = max(worst_loose, r)
-            elif r > worst:
-                worst, worst_name = r, n
-        q.put((rank, abs(loss_e.item() - loss_d.item()), abs(aux_e.item() - aux_d.item()), worst, worst_name,
-               flips, worst_loose))
+            if r < 1e-2:
+                continue
+            r_ep, r_one = _rel(p.main_grad, expect_o[n]), _rel(expect[n], expect_o[n])
+            if r_ep > 2 * r_one + 5e-3:
+                bad.append((n, r, r_ep, r_one))
+        q.put((rank, abs(loss_e.item() - loss_d.item()), abs(aux_e.item() - aux_d.item()), bad, flips))
         dist.barrier()
         dist.destroy_process_group()
     except Exception:
         import traceback
-        q.put((rank, traceback.format_exc(), None, None, None, None, None))
+        q.put((rank, traceback.format_exc(), None, None, None))
 
 
 @pytest.mark.skipif(torch.cuda.device_count() < 2, reason="needs 2 GPUs")
@@ -142,9 +137,8 @@ def test_fused_ep2_matches_single_gpu_experts():
     res = [q.get(timeout=300) for _ in ps]
     for p in ps:
         p.join(timeout=60)
-    for rank, dloss, daux, worst, name, flips, worst_loose in res:
+    for rank, dloss, daux, bad, flips in res:
         assert not isinstance(dloss, str), dloss
         assert dloss < 1e-3 and daux < 1e-4, (rank, dloss, daux)
         assert flips <= 2, (rank, "tokens routed differently in one layer", flips)
-        assert worst < 1e-2, (rank, worst, name)
-        assert worst_loose < 0.1, (rank, "experts of a flipped token", worst_loose)
+        assert not bad, (rank, bad)
