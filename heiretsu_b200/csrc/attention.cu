@@ -810,11 +810,11 @@ static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
   ((drop_on) ? ((f16) ? kern<true, true> : kern<true, false>)                                \
              : ((f16) ? kern<false, true> : kern<false, false>))
 
-// HB_ATTN_EXP_FMA (0, 1, 2) sets AttnParams::exp_fma of the head_dim 64 forward.
+// HB_ATTN_EXP_FMA (0, 1, 2) sets AttnParams::exp_fma of the head_dim 64 forward (default 1).
 static int attn_exp_fma() {
   static const int m = [] {
     const char* v = std::getenv("HB_ATTN_EXP_FMA");
-    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : 0;
+    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : 1;
   }();
   return m;
 }

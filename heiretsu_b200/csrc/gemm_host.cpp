@@ -42,11 +42,13 @@ static bool tma_epilogue_enabled() {
   return on;
 }
 
-// HB_GEMM_GELU selects how the activation epilogues evaluate GELU (GemmParams::gelu_mode).
+// HB_GEMM_GELU selects how the activation epilogues evaluate GELU (GemmParams::gelu_mode);
+// default 2 (tanh.approx), which measured 1.5% faster per GPT-2 small training step than
+// the sigmoid form (20.82 vs 21.12 ms, three alternating pairs on one B200).
 static int gelu_mode() {
   static const int m = [] {
     const char* v = std::getenv("HB_GEMM_GELU");
-    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : 0;
+    return (v && v[0] >= '0' && v[0] <= '2') ? v[0] - '0' : 2;
   }();
   return m;
 }

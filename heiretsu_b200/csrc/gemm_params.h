@@ -75,7 +75,7 @@ struct GemmParams {
 
   // GELU / GELU' evaluation in the activation epilogues: 0 sigmoid form, one
   // ex2.approx per element; 1 the same with every other exponential on the FMA
-  // pipe; 2 tanh.approx.
+  // pipe; 2 tanh.approx (the default).
   int gelu_mode;
 
   // Expert-parallel combine epilogue (row-grouped GEMM with a 16-bit output;

@@ -508,3 +508,38 @@ def test_exp2_fma_derivation():
     ref = np.exp2(x.astype(np.float64))
     rel = np.abs(got - ref) / ref
     assert rel.max() < 5e-6 + 4e-7, rel.max()
+
+
+def test_attention_trace_reports():
+    """Phase arithmetic of the attention trace reports on hand-made stamps."""
+    import numpy as np
+
+    from heiretsu_b200.ops.attn_trace import backward_report, forward_report
+
+    t = np.zeros((4, 80), dtype=np.int64)  # two live CTAs, two empty rows
+    for c in range(2):
+        base = 1000 * (c + 1)
+        t[c, 0], t[c, 1], t[c, 2] = base, base + 100, base + 5000
+        for g in (0, 1):
+            for j in range(2):
+                s = base + 200 + 1000 * j
+                t[c, 8 + 24 * g + j], t[c, 16 + 24 * g + j] = s, s + 10
+                t[c, 56 + 8 * g + j], t[c, 24 + 24 * g + j] = s + 110, s + 600
+    r = forward_report(t)
+    assert r["ctas"] == 2 and r["span_us"] == 6.0 and r["first_load_ns"] == 100.0
+    first = r["tiles"][0]
+    assert (first["softmax_ns"], first["max_pass_ns"], first["turnaround_ns"]) == (600.0, 100.0, 400.0)
+    assert len(r["tiles"]) == 4 and "turnaround_ns" in r["tiles"][1]  # j = 1 still has a slot for j + 1
+
+    b = np.zeros((2, 80), dtype=np.int64)
+    b[0, 0], b[0, 1], b[0, 2] = 10, 30, 9010
+    for i in range(3):
+        for g in (0, 1):
+            r0 = 100 + 2000 * i + 50 * g
+            b[0, 24 + 24 * g + i], b[0, 40 + 24 * g + i] = r0, r0 + 1500
+            if i > 0:
+                b[0, 32 + 24 * g + i] = r0 + 700
+    rb = backward_report(b)
+    tile1 = [x for x in rb["tiles"] if x["g"] == 1 and x["i"] == 1][0]
+    assert (tile1["softmax_ns"], tile1["wait_prev_mma_ns"], tile1["turnaround_ns"]) == (1500.0, 700.0, 500.0)
+    assert rb["span_us"] == 9.0
