@@ -58,6 +58,45 @@ constexpr int FWD_SMEM = 2 * kTileBytes /*Q_A, Q_B*/ + FWD_SLOTS * kTileBytes + 
 __device__ __forceinline__ int fwd_k_item(int j) { return j == 0 ? 0 : 2 * j - 1; }
 __device__ __forceinline__ int fwd_v_item(int j, int n) { return (j == n - 1) ? 2 * n - 1 : 2 * j + 2; }
 
+// Exponentials of 32-column chunk c of this thread's score row (keys key0 + 32c
+// ..), relative to the reference max (nm2 = -m, packed): P = 2^(s * scale * log2 e
+// - m) goes to the swizzled P tile (dropped out where the mask says so), the
+// undropped values add to the row-sum pairs sum2. Arguments and sums run on fp32
+// pairs; EXPF moves a share of the exponentials to the FMA pipe.
+template <bool DIAG, bool DROP, bool F16, int EXPF>
+__device__ __forceinline__ void exp_chunk(const uint32_t (&v)[32], int c, uint8_t* sP, int row, int key0, int q,
+                                          uint64_t sl2, uint64_t nm2, uint64_t (&sum2)[2], uint32_t dkey,
+                                          uint64_t pair_row, uint32_t dthresh, float dscale) {
+#pragma unroll
+  for (int g = 0; g < 4; ++g) {  // eight columns per 16-byte store, stored as soon as they are packed
+    uint32_t pk[4];
+#pragma unroll
+    for (int i = 8 * g; i < 8 * g + 8; i += 2) {
+      float t0, t1;
+      f2_unpack(f2_fma(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), t0, t1);
+      float p0 = fast_exp2(t0), p1;
+      if ((EXPF == 1 && (i & 6) == 6) || (EXPF == 2 && (i & 2) == 2)) {
+        p1 = exp2_fma(t1);  // this share on the FMA pipe
+      } else {
+        p1 = fast_exp2(t1);
+      }
+      if (DIAG) {
+        if (key0 + c * 32 + i > q) p0 = 0.f;
+        if (key0 + c * 32 + i + 1 > q) p1 = 0.f;
+      }
+      sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));  // normaliser: undropped
+      if (DROP) {
+        float m0, m1;
+        dropout_pair(dropout_bits(dkey, pair_row + ((key0 + c * 32 + i) >> 1)), dthresh, dscale, m0, m1);
+        p0 *= m0;
+        p1 *= m1;
+      }
+      pk[(i >> 1) & 3] = pack16<F16>(p0, p1);
+    }
+    *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 4 + g)) = make_uint4(pk[0], pk[1], pk[2], pk[3]);
+  }
+}
+
 // Online softmax of one 128x128 score tile held in TMEM, for the calling
 // thread's row: updates (m, l), writes P (bf16) to the swizzled smem tile and
 // returns the rescale factor of the previous accumulator. TMEM is read in
@@ -119,38 +158,9 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
       if ((threadIdx.x & 31) == 0) mbar_arrive(s_free);
     }
 #pragma unroll
-    for (int half = 0; half < 2; ++half) {
-      const uint32_t* v = half ? vb : va;
-      const int c = 2 * h + half;
-      uint32_t pk[16];
-#pragma unroll
-      for (int i = 0; i < 32; i += 2) {
-        float t0, t1;
-        f2_unpack(f2_fma(f2_pack(__uint_as_float(v[i]), __uint_as_float(v[i + 1])), sl2, nm2), t0, t1);
-        float p0 = fast_exp2(t0), p1;
-        if ((EXPF == 1 && (i & 6) == 6) || (EXPF == 2 && (i & 2) == 2)) {
-          p1 = exp2_fma(t1);  // this share on the FMA pipe
-        } else {
-          p1 = fast_exp2(t1);
-        }
-        if (DIAG) {
-          if (key0 + c * 32 + i > q) p0 = 0.f;
-          if (key0 + c * 32 + i + 1 > q) p1 = 0.f;
-        }
-        sum2[(i >> 1) & 1] = f2_add(sum2[(i >> 1) & 1], f2_pack(p0, p1));  // normaliser: undropped
-        if (DROP) {
-          float m0, m1;
-          dropout_pair(dropout_bits(dkey, pair_row + ((key0 + c * 32 + i) >> 1)), dthresh, dscale, m0, m1);
-          p0 *= m0;
-          p1 *= m1;
-        }
-        pk[i >> 1] = pack16<F16>(p0, p1);
-      }
-#pragma unroll
-      for (int g = 0; g < 4; ++g)
-        *reinterpret_cast<uint4*>(sP + sw128_off(row, c * 4 + g)) =
-            make_uint4(pk[4 * g], pk[4 * g + 1], pk[4 * g + 2], pk[4 * g + 3]);
-    }
+    for (int half = 0; half < 2; ++half)
+      exp_chunk<DIAG, DROP, F16, EXPF>(half ? vb : va, 2 * h + half, sP, row, key0, q, sl2, nm2, sum2, dkey, pair_row,
+                                        dthresh, dscale);
   }
   float s0, s1, s2, s3;
   f2_unpack(sum2[0], s0, s1);
@@ -158,6 +168,84 @@ __device__ __forceinline__ float softmax_tile(uint32_t tS, uint32_t lane_off, ui
   l = l * alpha + ((s0 + s1) + (s2 + s3));
   m = m_new;
   return alpha;
+}
+
+// Softmax of one score tile when O is accumulated in TMEM by the PV MMAs (the
+// default form). The whole 128-score row is loaded at once (four loads in
+// flight, one wait) and S is released to the MMA warp right after; the row max
+// and the exponentials then run from registers. The exponentials are taken
+// against a reference max m that only moves when the tile's max exceeds it by
+// more than kRescaleLog2 (or on the first tile): P <= 2^kRescaleLog2 then, and
+// O in TMEM (with l) is rescaled by 2^(m_old - m_new) only on such a move, after
+// the previous PV has completed and before this P is handed over. m, l and the
+// final O / l are all relative to the same reference, so the result is exact
+// whatever the reference.
+constexpr float kRescaleLog2 = 8.f;
+
+template <bool DIAG, bool DROP, bool F16, int EXPF>
+__device__ __forceinline__ void softmax_tile_ot(uint32_t tS, uint32_t tO, uint32_t lane_off, uint8_t* sP, int row,
+                                                int key0, int q, float scale_log2, bool first, float& m, float& l,
+                                                uint32_t dkey, uint64_t pair_row, uint32_t dthresh, float dscale,
+                                                uint64_t* pv_bar, uint32_t pv_phase, uint64_t* s_free, int* status,
+                                                bool& ok, uint64_t* stamp) {
+  uint32_t v0[32], v1[32], v2[32], v3[32];
+  tmem_ld32_issue(tS + lane_off, v0);
+  tmem_ld32_issue(tS + lane_off + 32, v1);
+  tmem_ld32_issue(tS + lane_off + 64, v2);
+  tmem_ld32_issue(tS + lane_off + 96, v3);
+  tmem_wait_ld_regs(v0);
+  tmem_pin_regs(v1);
+  tmem_pin_regs(v2);
+  tmem_pin_regs(v3);
+  tc_fence_before();  // every read of S is complete: the next S may be computed
+  __syncwarp();
+  if ((threadIdx.x & 31) == 0) mbar_arrive(s_free);
+  float mx[4] = {-INFINITY, -INFINITY, -INFINITY, -INFINITY};
+#pragma unroll
+  for (int i = 0; i < 32; ++i) {
+    float a = __uint_as_float(v0[i]), b = __uint_as_float(v1[i]);
+    float c = __uint_as_float(v2[i]), d = __uint_as_float(v3[i]);
+    if (DIAG) {
+      if (key0 + i > q) a = -INFINITY;
+      if (key0 + 32 + i > q) b = -INFINITY;
+      if (key0 + 64 + i > q) c = -INFINITY;
+      if (key0 + 96 + i > q) d = -INFINITY;
+    }
+    mx[i & 3] = max3f(mx[i & 3], max3f(a, b, c), d);
+  }
+  const float mt = max3f(mx[0], mx[1], fmaxf(mx[2], mx[3])) * scale_log2;
+  float alpha = 1.f;
+  if (first) {
+    m = mt;
+  } else if (mt > m + kRescaleLog2) {
+    alpha = fast_exp2(m - mt);
+    m = mt;
+  }
+  if (stamp != nullptr) *stamp = globaltimer_ns();  // phase trace: row max done
+  if (pv_bar != nullptr && !mbar_wait(pv_bar, pv_phase, status, 27)) {  // P smem and O: previous PV done
+    ok = false;
+    return;
+  }
+  const uint64_t sl2 = f2_pack(scale_log2, scale_log2), nm2 = f2_pack(-m, -m);
+  uint64_t sum2[2] = {f2_pack(0.f, 0.f), f2_pack(0.f, 0.f)};
+  exp_chunk<DIAG, DROP, F16, EXPF>(v0, 0, sP, row, key0, q, sl2, nm2, sum2, dkey, pair_row, dthresh, dscale);
+  exp_chunk<DIAG, DROP, F16, EXPF>(v1, 1, sP, row, key0, q, sl2, nm2, sum2, dkey, pair_row, dthresh, dscale);
+  exp_chunk<DIAG, DROP, F16, EXPF>(v2, 2, sP, row, key0, q, sl2, nm2, sum2, dkey, pair_row, dthresh, dscale);
+  exp_chunk<DIAG, DROP, F16, EXPF>(v3, 3, sP, row, key0, q, sl2, nm2, sum2, dkey, pair_row, dthresh, dscale);
+  if (__any_sync(0xffffffffu, alpha != 1.f)) {  // the reference max moved: O *= alpha
+#pragma unroll 1
+    for (int h = 0; h < 2; ++h) {
+      float o[32];
+      tmem_ld32(tO + lane_off + h * 32, o);
+#pragma unroll
+      for (int i = 0; i < 32; ++i) o[i] *= alpha;
+      tmem_st32(tO + lane_off + h * 32, o);
+    }
+  }
+  float s0, s1, s2, s3;
+  f2_unpack(sum2[0], s0, s1);
+  f2_unpack(sum2[1], s2, s3);
+  l = l * alpha + ((s0 + s1) + (s2 + s3));
 }
 
 // o = o * alpha + (PV result in TMEM, 64 columns of this thread's row); o
@@ -176,7 +264,9 @@ __device__ __forceinline__ void accumulate_o(uint64_t (&o)[32], uint32_t tO, flo
   }
 }
 
-template <bool DROP, bool F16>
+// OT: O accumulated in TMEM by the PV MMAs (softmax_tile_ot); otherwise each PV
+// writes a fresh TMEM buffer that the softmax warps add into registers.
+template <bool DROP, bool F16, bool OT>
 __global__ void __launch_bounds__(FWD_THREADS, 1)
     attn_fwd_kernel(const __grid_constant__ CUtensorMap tm_qkv, AttnParams p) {
   extern __shared__ uint8_t smem_raw[];
@@ -277,12 +367,12 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
       };
       auto issue_pv = [&](int g, int j, uint32_t va) {
         const uint32_t pa = smem_u32(sP + g * 2 * kTileBytes);
-        const uint32_t tO = tmem + g * 256 + 128 + (j & 1) * 64;
+        const uint32_t tO = tmem + g * 256 + 128 + (OT ? 0 : (j & 1) * 64);
 #pragma unroll
         for (int ks = 0; ks < 8; ++ks)
           mma_f16_ss(tO, sw128_desc(pa + (ks >> 2) * 16384 + (ks & 3) * 32, 16, 1024),
-                     sw128_desc(va + ks * 2048, 8192, 1024), idO, ks > 0);
-        mma_commit(&bar_o[g][j & 1]);
+                     sw128_desc(va + ks * 2048, 8192, 1024), idO, (OT && j > 0) || ks > 0);
+        mma_commit(&bar_o[g][OT ? 0 : (j & 1)]);
       };
       uint32_t ka = 0, va = 0;
       if (ok && item(fwd_k_item(0), ka)) {
@@ -330,7 +420,76 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
     const int sub = warp & 3;
     const int row = sub * 32 + lane;
     const uint32_t lane_off = static_cast<uint32_t>(sub * 32) << 16;
-    if (g == 1 || hasA) {
+    if (OT && (g == 1 || hasA)) {
+      const int my_qt = qt[g];
+      const int n = my_qt + 1;
+      const int q = my_qt * kTile + row;
+      const uint32_t tS = tmem + g * 256, tO = tmem + g * 256 + 128;
+      uint8_t* myP = sP + g * 2 * kTileBytes;
+      float m = 0.f, l = 0.f;  // reference max (log2 domain; set by the first tile) and row sum
+      uint32_t dkey = 0;
+      uint64_t pair_row = 0;
+      if (DROP) {
+        dkey = dropout_key(*p.drop.seed, p.drop.site);
+        pair_row = ((((uint64_t)b * p.nh_total + p.h0 + h) * p.T + q) * p.T) >> 1;
+      }
+      bool ok = true;
+      for (int j = 0; j < n && ok; ++j) {
+        if (!mbar_wait(&bar_s[g], j & 1, p.status, 26)) {
+          ok = false;
+          break;
+        }
+        if (lane == 0 && sub == 0 && j < 8) HB_TRACE(8 + 24 * g + j);
+        tc_fence_after();
+        if (lane == 0 && sub == 0 && j < 8) HB_TRACE(16 + 24 * g + j);
+        // P smem and O in TMEM are free once PV_{j-1} has completed (waited inside, after the row max).
+        uint64_t* pv_bar = j > 0 ? &bar_o[g][0] : nullptr;
+        const uint32_t pv_phase = (j - 1) & 1;
+        uint64_t* stamp = (p.trace != nullptr && lane == 0 && sub == 0 && j < 8)
+                              ? p.trace + (long)blockIdx.x * kTraceSlots + 56 + 8 * g + j
+                              : nullptr;
+#define HB_SOFTMAX_OT(DIAG, EXPF)                                                                                 \
+  softmax_tile_ot<DIAG, DROP, F16, EXPF>(tS, tO, lane_off, myP, row, j * kTile, q, p.scale_log2, j == 0, m, l, dkey, \
+                                         pair_row, p.drop.thresh, p.drop.scale, pv_bar, pv_phase, &bar_sfree[g],    \
+                                         p.status, ok, stamp)
+        if (j == my_qt) {
+          HB_SOFTMAX_OT(true, 0);
+        } else if (p.exp_fma == 1) {
+          HB_SOFTMAX_OT(false, 1);
+        } else if (p.exp_fma == 2) {
+          HB_SOFTMAX_OT(false, 2);
+        } else {
+          HB_SOFTMAX_OT(false, 0);
+        }
+#undef HB_SOFTMAX_OT
+        if (!ok) break;
+        fence_proxy_async_smem();
+        tc_fence_before();
+        __syncwarp();
+        if (lane == 0) mbar_arrive(&bar_p[g]);
+        if (lane == 0 && sub == 0 && j < 8) HB_TRACE(24 + 24 * g + j);
+      }
+      if (ok && mbar_wait(&bar_o[g][0], (n - 1) & 1, p.status, 28)) {
+        tc_fence_after();
+        float oa[32], ob[32];
+        tmem_ld32(tO + lane_off, oa);
+        tmem_ld32(tO + lane_off + 32, ob);
+        if (q < p.T) {
+          const float inv = 1.f / l;
+          uint32_t w[32];
+#pragma unroll
+          for (int i = 0; i < 16; ++i) {
+            w[i] = pack16<F16>(oa[2 * i] * inv, oa[2 * i + 1] * inv);
+            w[16 + i] = pack16<F16>(ob[2 * i] * inv, ob[2 * i + 1] * inv);
+          }
+          __nv_bfloat16* dst = p.out + ((long)b * p.T + q) * p.ld_out + h * kD;
+#pragma unroll
+          for (int gg = 0; gg < 8; ++gg)
+            *reinterpret_cast<uint4*>(dst + gg * 8) = make_uint4(w[4 * gg], w[4 * gg + 1], w[4 * gg + 2], w[4 * gg + 3]);
+          p.lse[((long)b * p.nh + h) * p.Tpad + q] = -(m + log2f(l));
+        }
+      }
+    } else if (!OT && (g == 1 || hasA)) {
       const int my_qt = qt[g];
       const int n = my_qt + 1;
       const int q = my_qt * kTile + row;
@@ -810,6 +969,23 @@ static CUtensorMap qkv_map(const void* base, int B, int T, long ld, int cols) {
   ((drop_on) ? ((f16) ? kern<true, true> : kern<true, false>)                                \
              : ((f16) ? kern<false, true> : kern<false, false>))
 
+// HB_ATTN_FWD_OT=0 selects the head_dim 64 forward that accumulates O in registers
+// (the default accumulates O in TMEM: attn_fwd_kernel<., ., true>).
+static bool attn_fwd_ot() {
+  static const bool on = [] {
+    const char* v = std::getenv("HB_ATTN_FWD_OT");
+    return !(v && v[0] == '0');
+  }();
+  return on;
+}
+
+// The forward's eight (dropout, 16-bit format, O in TMEM) instantiations.
+#define HB_ATTN_FWD_PICK(drop_on, f16, ot)                                                                  \
+  ((ot) ? ((drop_on) ? ((f16) ? attn_fwd_kernel<true, true, true> : attn_fwd_kernel<true, false, true>)     \
+                     : ((f16) ? attn_fwd_kernel<false, true, true> : attn_fwd_kernel<false, false, true>))  \
+        : ((drop_on) ? ((f16) ? attn_fwd_kernel<true, true, false> : attn_fwd_kernel<true, false, false>)   \
+                     : ((f16) ? attn_fwd_kernel<false, true, false> : attn_fwd_kernel<false, false, false>)))
+
 // HB_ATTN_EXP_FMA (0, 1, 2) sets AttnParams::exp_fma of the head_dim 64 forward (default 1).
 static int attn_exp_fma() {
   static const int m = [] {
@@ -827,8 +1003,9 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   if (!attr[dev]) {
     for (int d = 0; d < 2; ++d)
       for (int h = 0; h < 2; ++h)
-        HB_CUDA_CHECK(cudaFuncSetAttribute(HB_ATTN_PICK(attn_fwd_kernel, d, h),
-                                           cudaFuncAttributeMaxDynamicSharedMemorySize, FWD_SMEM));
+        for (int o = 0; o < 2; ++o)
+          HB_CUDA_CHECK(cudaFuncSetAttribute(HB_ATTN_FWD_PICK(d, h, o), cudaFuncAttributeMaxDynamicSharedMemorySize,
+                                             FWD_SMEM));
     attr[dev] = true;
   }
   AttnParams p{};
@@ -844,7 +1021,10 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
-  HB_ATTN_PICK(attn_fwd_kernel, drop.thresh != 0, f16)<<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
+  // With dropout the O-in-TMEM form keeps the whole score row and the mask hashing
+  // live at once and spills, so dropout runs the register-accumulator form.
+  const bool drop_on = drop.thresh != 0;
+  HB_ATTN_FWD_PICK(drop_on, f16, attn_fwd_ot() && !drop_on)<<<B * nh * n_pairs, FWD_THREADS, FWD_SMEM, s>>>(tm, p);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 

@@ -186,6 +186,30 @@ def test_attention_fwd_bwd(B, T, nh):
         assert e <= 3e-2 * scale + 1e-3, (name, e, scale)
 
 
+def test_attention_fwd_growing_scores():
+    """Keys of the later tiles score far above the earlier ones (K scaled by 5 from
+    key 384 on), so the running row max grows by more than the forward's rescale
+    threshold several tiles in: the O-in-TMEM forward must rescale its accumulator.
+    Checked, with the LSE the backward consumes, against fp32 torch."""
+    torch.manual_seed(9)
+    B, T, nh = 2, 1024, 4
+    H = nh * 64
+    x = torch.randn(B, T, 3, H, device="cuda")
+    x[:, 384:, 1] *= 5.0
+    qkv = x.reshape(B * T, 3 * H).bfloat16()
+    y, lse = K().attention_fwd(qkv, B, T, nh)
+    check()
+    q, k, v = qkv.float().view(B, T, 3, nh, 64).permute(2, 0, 3, 1, 4).unbind(0)
+    ref = F.scaled_dot_product_attention(q, k, v, is_causal=True).transpose(1, 2).reshape(B * T, H)
+    err = (y.float() - ref).abs().max().item()
+    assert err < 2e-2, err
+    s = (q @ k.transpose(-1, -2)) / 8.0
+    s = s.masked_fill(torch.ones(T, T, device="cuda", dtype=torch.bool).triu(1), float("-inf"))
+    lse_ref = torch.logsumexp(s, dim=-1) / math.log(2.0)  # log2 domain
+    got = -lse[:, :, :T]
+    assert (got - lse_ref).abs().max().item() < 2e-2 * lse_ref.abs().max().item() + 1e-2
+
+
 @pytest.mark.parametrize("single_pass", [False, True])
 def test_cross_entropy_rejects_out_of_range_targets(single_pass):
     """A target outside [0, V) (not ignore_index) is no class: the kernel reads no
