@@ -452,14 +452,13 @@ __global__ void __launch_bounds__(FWD_THREADS, 1)
   softmax_tile_ot<DIAG, DROP, F16, EXPF>(tS, tO, lane_off, myP, row, j * kTile, q, p.scale_log2, j == 0, m, l, dkey, \
                                          pair_row, p.drop.thresh, p.drop.scale, pv_bar, pv_phase, &bar_sfree[g],    \
                                          p.status, ok, stamp)
+        // Two bodies: the diagonal tile's, and the off-diagonal one with one
+        // exponential in eight on the FMA pipe (measured as fast as selecting the
+        // share at run time among three compiled bodies: 49.1 us).
         if (j == my_qt) {
           HB_SOFTMAX_OT(true, 0);
-        } else if (p.exp_fma == 1) {
-          HB_SOFTMAX_OT(false, 1);
-        } else if (p.exp_fma == 2) {
-          HB_SOFTMAX_OT(false, 2);
         } else {
-          HB_SOFTMAX_OT(false, 0);
+          HB_SOFTMAX_OT(false, 1);
         }
 #undef HB_SOFTMAX_OT
         if (!ok) break;

@@ -25,9 +25,10 @@ struct AttnParams {
   // element ((b * nh_total + h0 + h) * T + q) * T + k.
   DropoutArgs drop;
   int h0, nh_total;
-  // Forward softmax (head_dim 64): share of the exponentials evaluated on the FMA
-  // pipe (exp2_fma) instead of the transcendental unit: 0 none, 1 one in eight (the
-  // default: 51.2 vs 53.2 us at B 8, T 1024, 12 heads), 2 one in four (53.2 us).
+  // Forward softmax with O in registers (head_dim 64, the dropout path): share of the
+  // exponentials evaluated on the FMA pipe (exp2_fma) instead of the transcendental
+  // unit: 0 none, 1 one in eight (the default: 51.2 vs 53.2 us at B 8, T 1024, 12
+  // heads), 2 one in four (53.2 us). The O-in-TMEM form always uses one in eight.
   int exp_fma;
 };
 
