@@ -46,6 +46,11 @@ namespace hb {
 constexpr int kD = 64;
 constexpr int kTileBytes = kTile * kD * 2;  // 16 KB
 static uint64_t* g_attn_trace = nullptr;
+static long g_attn_trace_rows = 0;  // CTAs the trace buffer has rows for
+
+// The trace buffer for a launch of `grid` CTAs: launches with more CTAs than the
+// buffer has rows are not traced (each CTA writes its own row).
+static uint64_t* attn_trace_for(long grid) { return grid <= g_attn_trace_rows ? g_attn_trace : nullptr; }
 
 // ============================================================================
 // Forward
@@ -1015,11 +1020,11 @@ void attn_fwd_launch(const __nv_bfloat16* qkv, long ld_qkv, __nv_bfloat16* out, 
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
-  p.trace = g_attn_trace;
   p.exp_fma = attn_exp_fma();
   const CUtensorMap tm = qkv_map(qkv, B, T, ld_qkv, 3 * p.Hs);
   const int n_qt = (T + kTile - 1) / kTile;
   const int n_pairs = (n_qt + 1) / 2;
+  p.trace = attn_trace_for((long)B * nh * n_pairs);
   // With dropout the O-in-TMEM form keeps the whole score row and the mask hashing
   // live at once and spills, so dropout runs the register-accumulator form.
   const bool drop_on = drop.thresh != 0;
@@ -1052,7 +1057,7 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
   p.scale = scale;
   p.scale_log2 = scale * 1.4426950408889634f;
   p.status = status;
-  p.trace = g_attn_trace;
+  p.trace = attn_trace_for((long)B * nh * ((T + kTile - 1) / kTile));
   const CUtensorMap tq = qkv_map(qkv, B, T, ld_qkv, 3 * Hs);
   const CUtensorMap td = qkv_map(dO, B, T, ld_do, Hs);
   // dQ accumulator as {Hs, T, B} fp32: 32x32 reduce boxes never cross into the next sequence.
@@ -1074,6 +1079,9 @@ void attn_bwd_launch(const __nv_bfloat16* qkv, long ld_qkv, const __nv_bfloat16*
 // Backward slots per CTA: 0 start, 1 K/V and first Q/dO ready, 2 end; for query
 // tile i < 8: 8+i / 16+i P^T half 0 / half 1 consumed by the MMA warp; for half g:
 // 24+24g+i S^T/dP^T ready, 32+24g+i previous tile's MMAs done, 40+24g+i P^T/dS^T written.
-void attn_set_trace(uint64_t* trace) { g_attn_trace = trace; }
+void attn_set_trace(uint64_t* trace, long rows) {
+  g_attn_trace = trace;
+  g_attn_trace_rows = trace != nullptr ? rows : 0;
+}
 
 }  // namespace hb

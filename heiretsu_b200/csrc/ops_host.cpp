@@ -291,17 +291,18 @@ void f32_to_bf16(const at::Tensor& x, at::Tensor& y) {
   f32_to_bf16_launch(ptr<float>(x), raw16(y), x.numel(), is_f16(y), stream());
 }
 
-void attn_set_trace(uint64_t* trace);
+void attn_set_trace(uint64_t* trace, long rows);
 
 // Phase timestamps of the following attention launches go to `trace`
-// (int64 [grid * 80] on the device); None turns tracing off.
+// (int64, 80 per CTA, on the device; a launch with more CTAs than the buffer has
+// rows of 80 is not traced); None turns tracing off.
 void attention_set_trace(const c10::optional<at::Tensor>& trace) {
   if (trace && trace->defined()) {
     TORCH_CHECK(trace->is_cuda() && trace->scalar_type() == at::kLong && trace->is_contiguous(),
                 "attention_set_trace: int64 contiguous CUDA tensor");
-    attn_set_trace(reinterpret_cast<uint64_t*>(trace->data_ptr()));
+    attn_set_trace(reinterpret_cast<uint64_t*>(trace->data_ptr()), static_cast<long>(trace->numel() / 80));
   } else {
-    attn_set_trace(nullptr);
+    attn_set_trace(nullptr, 0);
   }
 }
 

@@ -236,3 +236,31 @@ def test_cross_entropy_rejects_out_of_range_targets(single_pass):
         check_status()
     if single_pass:
         assert bool(torch.isnan(logits[5].float()).any()) and bool(torch.isfinite(logits[4].float()).all())
+
+
+def test_attention_trace_buffer_too_small_is_not_written():
+    """A trace buffer with fewer rows than the launch has CTAs turns tracing off for
+    that launch (each CTA writes its own row): nothing is written, before or past it."""
+    from heiretsu_b200.ops._C import load
+
+    ext = load()
+    B, T, nh = 2, 1024, 4  # forward grid: B * nh * 4 query-tile pairs = 32 CTAs
+    qkv = torch.randn(B * T, 3 * nh * 64, device="cuda").bfloat16()
+    backing = torch.full((64, 80), 7, dtype=torch.int64, device="cuda")
+    small = backing[:16]  # 16 rows < 32 CTAs
+    ext.attention_set_trace(small)
+    try:
+        K().attention_fwd(qkv, B, T, nh)
+        torch.cuda.synchronize()
+    finally:
+        ext.attention_set_trace(None)
+    check()
+    assert bool((backing == 7).all())
+    full = torch.zeros(32, 80, dtype=torch.int64, device="cuda")
+    ext.attention_set_trace(full)
+    try:
+        K().attention_fwd(qkv, B, T, nh)
+        torch.cuda.synchronize()
+    finally:
+        ext.attention_set_trace(None)
+    assert bool((full[:, 0] > 0).all())  # every CTA stamped its start
