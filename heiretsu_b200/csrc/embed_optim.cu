@@ -12,29 +12,40 @@
 namespace hb {
 
 // out fp32 [B*T, H] = wte[idx] + wpe[t]. One warp per token row, float4.
+// A token id outside [0, V) names no row of wte (nn.Embedding rejects it): its
+// output row becomes NaN (so the loss and the step's gradient norm are NaN and
+// the optimizer skips the step) and the status word records the bad argument.
 __global__ void embed_fwd_kernel(const int64_t* __restrict__ idx, const float* __restrict__ wte,
-                                 const float* __restrict__ wpe, float* __restrict__ out, int M, int T, int H) {
+                                 const float* __restrict__ wpe, float* __restrict__ out, int M, int T, int H, int V,
+                                 int* status) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const long tok = idx[row];
   const int t = row % T;
+  float4* o = reinterpret_cast<float4*>(out + (long)row * H);
+  if (tok < 0 || tok >= V) {
+    if (lane == 0) record_error(status, kBadArg, 410);
+    for (int j = lane; j < H / 4; j += 32) o[j] = make_float4(NAN, NAN, NAN, NAN);
+    return;
+  }
   const float4* a = reinterpret_cast<const float4*>(wte + tok * H);
   const float4* p = reinterpret_cast<const float4*>(wpe + (long)t * H);
-  float4* o = reinterpret_cast<float4*>(out + (long)row * H);
   for (int j = lane; j < H / 4; j += 32) {
     const float4 x = a[j], y = p[j];
     o[j] = make_float4(x.x + y.x, x.y + y.y, x.z + y.z, x.w + y.w);
   }
 }
 
-// dwte[idx[m]] += dx[m] (vector atomics; rows repeat across the batch).
+// dwte[idx[m]] += dx[m] (vector atomics; rows repeat across the batch). Token ids
+// outside [0, V) (reported by the forward) add nothing.
 __global__ void embed_bwd_tok_kernel(const int64_t* __restrict__ idx, const float* __restrict__ dx,
-                                     float* __restrict__ dwte, int M, int H) {
+                                     float* __restrict__ dwte, int M, int H, int V) {
   const int row = (blockIdx.x * blockDim.x + threadIdx.x) >> 5;
   const int lane = threadIdx.x & 31;
   if (row >= M) return;
   const long tok = idx[row];
+  if (tok < 0 || tok >= V) return;
   const float4* g = reinterpret_cast<const float4*>(dx + (long)row * H);
   float4* d = reinterpret_cast<float4*>(dwte + tok * H);
   for (int j = lane; j < H / 4; j += 32) atomicAdd(d + j, g[j]);
@@ -49,20 +60,20 @@ __global__ void embed_bwd_pos_kernel(const float* __restrict__ dx, float* __rest
   dwpe[i] += s;
 }
 
-void embed_fwd_launch(const int64_t* idx, const float* wte, const float* wpe, float* out, int B, int T, int H,
-                      cudaStream_t s) {
+void embed_fwd_launch(const int64_t* idx, const float* wte, const float* wpe, float* out, int B, int T, int H, int V,
+                      int* status, cudaStream_t s) {
   if (H % 4) throw std::runtime_error("embedding: H must be a multiple of 4");
   const int M = B * T;
-  embed_fwd_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(idx, wte, wpe, out, M, T, H);
+  embed_fwd_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(idx, wte, wpe, out, M, T, H, V, status);
   HB_CUDA_CHECK(cudaGetLastError());
 }
 
-void embed_bwd_launch(const int64_t* idx, const float* dx, float* dwte, float* dwpe, int B, int T, int H,
+void embed_bwd_launch(const int64_t* idx, const float* dx, float* dwte, float* dwpe, int B, int T, int H, int V,
                       cudaStream_t s) {
   if (H % 4) throw std::runtime_error("embedding: H must be a multiple of 4");
   const int M = B * T;
   if (dwte) {
-    embed_bwd_tok_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(idx, dx, dwte, M, H);
+    embed_bwd_tok_kernel<<<(M * 32 + 255) / 256, 256, 0, s>>>(idx, dx, dwte, M, H, V);
     HB_CUDA_CHECK(cudaGetLastError());
   }
   if (dwpe) {

@@ -30,8 +30,8 @@ void ce_bwd_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, con
 void ce_fused_launch(__nv_bfloat16*, long, int, int, int, const int64_t*, int, float*, float*, float*, const float*,
                      bool, int*, cudaStream_t);
 void ce_rescale_launch(__nv_bfloat16*, long, int, int, const float*, const float*, bool, cudaStream_t);
-void embed_fwd_launch(const int64_t*, const float*, const float*, float*, int, int, int, cudaStream_t);
-void embed_bwd_launch(const int64_t*, const float*, float*, float*, int, int, int, cudaStream_t);
+void embed_fwd_launch(const int64_t*, const float*, const float*, float*, int, int, int, int, int*, cudaStream_t);
+void embed_bwd_launch(const int64_t*, const float*, float*, float*, int, int, int, int, cudaStream_t);
 int sumsq_num_parts(int device);
 void sumsq_launch(const float*, long, float*, int, float, float*, bool, cudaStream_t);
 void clip_coef_launch(const float*, float, float*, float*, const float*, cudaStream_t);
@@ -75,6 +75,15 @@ static DropoutArgs make_dropout(const c10::optional<at::Tensor>& seed, int64_t s
 #define CHECK_DT(t, dt) TORCH_CHECK((t).scalar_type() == (dt), #t " has the wrong dtype")
 #define CHECK_CONTIG(t) TORCH_CHECK((t).is_contiguous(), #t " must be contiguous")
 #define CHECK_ROWS(t) TORCH_CHECK((t).dim() == 2 && (t).stride(1) == 1, #t " must be 2-D with contiguous rows")
+// Output and operand buffers are written / read up to the sizes the launch
+// derives from its main input: each must hold at least that many elements.
+#define CHECK_HOLDS(t, n) TORCH_CHECK((t).numel() >= (int64_t)(n), #t " holds fewer than " #n " elements")
+#define CHECK_F32_HOLDS(t, n) \
+  do {                        \
+    CHECK_DT(t, at::kFloat);  \
+    CHECK_CONTIG(t);          \
+    CHECK_HOLDS(t, n);        \
+  } while (0)
 
 // Data pointer of a bf16 or fp16 tensor as the kernels' 16-bit element pointer
 // (kernels take the format as a flag: is_f16).
@@ -101,6 +110,11 @@ void layernorm_fwd(const at::Tensor& x, const at::Tensor& w, const at::Tensor& b
   c10::cuda::CUDAGuard g(x.device());
   const int H = x.size(-1);
   const int M = x.numel() / H;
+  CHECK_F32_HOLDS(w, H);
+  CHECK_F32_HOLDS(b, H);
+  CHECK_HOLDS(y, (int64_t)M * H);
+  CHECK_F32_HOLDS(mean, M);
+  CHECK_F32_HOLDS(rstd, M);
   ln_fwd_launch(ptr<float>(x), ptr<float>(w), ptr<float>(b), raw16(y), ptr<float>(mean), ptr<float>(rstd), M, H,
                 static_cast<float>(eps), is_f16(y), stream());
 }
@@ -126,6 +140,14 @@ void layernorm_bwd(const at::Tensor& dy, const at::Tensor& x, const at::Tensor& 
   const int M = x.numel() / H;
   const int ctas = ln_bwd_num_ctas(M, x.get_device());
   TORCH_CHECK(scratch.numel() >= (int64_t)ctas * 2 * H, "layernorm_bwd: scratch too small");
+  CHECK_F32_HOLDS(mean, M);
+  CHECK_F32_HOLDS(rstd, M);
+  CHECK_F32_HOLDS(w, H);
+  CHECK_HOLDS(dres_in, (int64_t)M * H);
+  CHECK_HOLDS(dres, (int64_t)M * H);
+  CHECK_HOLDS(dres16, (int64_t)M * H);
+  CHECK_F32_HOLDS(dgamma, H);
+  CHECK_F32_HOLDS(dbeta, H);
   TORCH_CHECK(dy_srcs >= 1 && dy.numel() >= dy_srcs * (int64_t)M * H, "layernorm_bwd: dy holds dy_srcs slots of [M, H]");
   ln_bwd_launch(ptr<float>(dy), ptr<float>(x), ptr<float>(mean), ptr<float>(rstd), ptr<float>(w),
                 ptr<float>(dres_in), ptr<float>(dres), raw16(dres16), ptr<float>(scratch), ctas, ptr<float>(dgamma),
@@ -143,7 +165,20 @@ void resid_sum_ln(const at::Tensor& x, const at::Tensor& parts, int64_t nsrc, co
   const int H = x.size(-1);
   const int M = x.numel() / H;
   TORCH_CHECK(parts.numel() >= nsrc * (int64_t)M * H, "resid_sum_ln: parts holds nsrc slots of [M, H]");
+  CHECK_F32_HOLDS(bias, H);
+  CHECK_CONTIG(x_new);
+  CHECK_HOLDS(x_new, (int64_t)M * H);
   const bool ln = w && w->defined();
+  if (ln) {
+    TORCH_CHECK(b && b->defined() && y && y->defined() && mean && mean->defined() && rstd && rstd->defined(),
+                "resid_sum_ln: with w, also b, y, mean and rstd");
+    CHECK_F32_HOLDS((*w), H);
+    CHECK_F32_HOLDS((*b), H);
+    CHECK_CONTIG((*y));
+    CHECK_HOLDS((*y), (int64_t)M * H);
+    CHECK_F32_HOLDS((*mean), M);
+    CHECK_F32_HOLDS((*rstd), M);
+  }
   c10::cuda::CUDAGuard g(x.device());
   TORCH_CHECK(!ln || y->scalar_type() == parts.scalar_type(), "resid_sum_ln: y and parts share one 16-bit format");
   resid_sum_ln_launch(ptr<float>(x), raw16(parts), static_cast<int>(nsrc), (long)M * H, ptr<float>(bias),
@@ -157,16 +192,37 @@ void colsum_bf16(const at::Tensor& x, at::Tensor& out) {
   CHECK_ROWS(x);
   CHECK_DT(out, at::kFloat);
   TORCH_CHECK(x.size(1) % 2 == 0 && x.stride(0) % 2 == 0, "colsum_bf16: even column count required");
+  CHECK_CONTIG(out);
+  CHECK_HOLDS(out, x.size(1));
   c10::cuda::CUDAGuard g(x.device());
   colsum_bf16_launch(raw16(x), x.stride(0), x.size(0), x.size(1), ptr<float>(out), is_f16(x), stream());
 }
 
-void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
-                       at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean) {
+// The cross-entropy kernels read and write logit rows in 16-byte pieces: the row
+// stride must be a multiple of 8 elements and the base 16-byte aligned, and
+// 1 <= V <= the row width.
+static void check_ce_logits(const at::Tensor& logits, int64_t V) {
   CHECK_CUDA(logits);
   CHECK_ROWS(logits);
+  raw16(logits);
+  TORCH_CHECK(logits.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(logits.data_ptr()) % 16 == 0,
+              "cross-entropy: logit rows must start on 16-byte boundaries (row stride a multiple of 8)");
+  TORCH_CHECK(V >= 1 && V <= logits.size(1), "cross-entropy: V must be in [1, row width]");
+}
+static void check_ce_targets(const at::Tensor& targets, int64_t M) {
   CHECK_DT(targets, at::kLong);
   CHECK_CONTIG(targets);
+  CHECK_HOLDS(targets, M);
+}
+
+void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
+                       at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean) {
+  check_ce_logits(logits, V);
+  const int64_t M = logits.size(0);
+  check_ce_targets(targets, M);
+  CHECK_F32_HOLDS(lse, M);
+  CHECK_F32_HOLDS(loss_rows, M);
+  CHECK_F32_HOLDS(loss_mean, 1);
   c10::cuda::CUDAGuard g(logits.device());
   ce_fwd_launch(raw16(logits), logits.stride(0), logits.size(0), V, ptr<int64_t>(targets), ignore_index,
                 ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), nullptr, is_f16(logits),
@@ -175,8 +231,11 @@ void cross_entropy_fwd(const at::Tensor& logits, int64_t V, const at::Tensor& ta
 
 void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                        const at::Tensor& lse, const c10::optional<at::Tensor>& scale, double scale_mul) {
-  CHECK_CUDA(logits);
-  CHECK_ROWS(logits);
+  check_ce_logits(logits, V);
+  const int64_t M = logits.size(0);
+  check_ce_targets(targets, M);
+  CHECK_F32_HOLDS(lse, M);
+  if (scale && scale->defined()) CHECK_F32_HOLDS((*scale), 1);
   c10::cuda::CUDAGuard g(logits.device());
   const float* sp = (scale && scale->defined()) ? ptr<float>(*scale) : nullptr;
   ce_bwd_launch(raw16(logits), logits.stride(0), logits.size(0), V, logits.size(1), ptr<int64_t>(targets),
@@ -185,11 +244,13 @@ void cross_entropy_bwd(at::Tensor& logits, int64_t V, const at::Tensor& targets,
 
 void cross_entropy_fused(at::Tensor& logits, int64_t V, const at::Tensor& targets, int64_t ignore_index,
                          at::Tensor& lse, at::Tensor& loss_rows, at::Tensor& loss_mean, const at::Tensor& scale) {
-  CHECK_CUDA(logits);
-  CHECK_ROWS(logits);
-  CHECK_DT(targets, at::kLong);
-  CHECK_CONTIG(targets);
-  CHECK_DT(scale, at::kFloat);
+  check_ce_logits(logits, V);
+  const int64_t M = logits.size(0);
+  check_ce_targets(targets, M);
+  CHECK_F32_HOLDS(lse, M);
+  CHECK_F32_HOLDS(loss_rows, M);
+  CHECK_F32_HOLDS(loss_mean, 1);
+  CHECK_F32_HOLDS(scale, 1);
   c10::cuda::CUDAGuard g(logits.device());
   ce_fused_launch(raw16(logits), logits.stride(0), logits.size(0), V, logits.size(1), ptr<int64_t>(targets),
                   ignore_index, ptr<float>(lse), ptr<float>(loss_rows), ptr<float>(loss_mean), ptr<float>(scale),
@@ -199,8 +260,11 @@ void cross_entropy_fused(at::Tensor& logits, int64_t V, const at::Tensor& target
 void cross_entropy_rescale(at::Tensor& g, const at::Tensor& actual, const at::Tensor& expected) {
   CHECK_CUDA(g);
   CHECK_ROWS(g);
-  CHECK_DT(actual, at::kFloat);
-  CHECK_DT(expected, at::kFloat);
+  CHECK_F32_HOLDS(actual, 1);
+  CHECK_F32_HOLDS(expected, 1);
+  raw16(g);
+  TORCH_CHECK(g.stride(0) % 8 == 0 && reinterpret_cast<uintptr_t>(g.data_ptr()) % 16 == 0,
+              "cross_entropy_rescale: rows must start on 16-byte boundaries");
   c10::cuda::CUDAGuard gd(g.device());
   ce_rescale_launch(raw16(g), g.stride(0), g.size(0), g.size(1), ptr<float>(actual), ptr<float>(expected), is_f16(g),
                     stream());
@@ -215,9 +279,13 @@ void embedding_fwd(const at::Tensor& idx, const at::Tensor& wte, const at::Tenso
   CHECK_DT(wpe, at::kFloat);
   CHECK_CONTIG(wpe);
   CHECK_CONTIG(out);
+  TORCH_CHECK(idx.dim() == 2 && wte.dim() == 2 && wpe.dim() == 2 && wpe.size(1) == wte.size(1),
+              "embedding_fwd: idx [B, T], wte [V, H], wpe [P, H]");
+  TORCH_CHECK(idx.size(1) <= wpe.size(0), "embedding_fwd: sequence longer than the position table");
+  CHECK_HOLDS(out, idx.numel() * wte.size(1));
   c10::cuda::CUDAGuard g(idx.device());
   embed_fwd_launch(ptr<int64_t>(idx), ptr<float>(wte), ptr<float>(wpe), ptr<float>(out), idx.size(0), idx.size(1),
-                   wte.size(1), stream());
+                   wte.size(1), static_cast<int>(wte.size(0)), device_status_ptr(idx.get_device()), stream());
 }
 
 void embedding_bwd(const at::Tensor& idx, const at::Tensor& dx, const c10::optional<at::Tensor>& dwte,
@@ -225,10 +293,26 @@ void embedding_bwd(const at::Tensor& idx, const at::Tensor& dx, const c10::optio
   CHECK_CUDA(dx);
   CHECK_DT(dx, at::kFloat);
   CHECK_CONTIG(dx);
-  c10::cuda::CUDAGuard g(dx.device());
+  CHECK_DT(idx, at::kLong);
+  CHECK_CONTIG(idx);
+  TORCH_CHECK(idx.dim() == 2, "embedding_bwd: idx [B, T]");
   const int H = dx.size(-1);
-  embed_bwd_launch(ptr<int64_t>(idx), ptr<float>(dx), (dwte && dwte->defined()) ? ptr<float>(*dwte) : nullptr,
-                   (dwpe && dwpe->defined()) ? ptr<float>(*dwpe) : nullptr, idx.size(0), idx.size(1), H, stream());
+  CHECK_HOLDS(dx, idx.numel() * H);
+  const bool tok = dwte && dwte->defined(), pos = dwpe && dwpe->defined();
+  if (tok) {
+    CHECK_CONTIG((*dwte));
+    TORCH_CHECK(dwte->scalar_type() == at::kFloat && dwte->dim() == 2 && dwte->size(1) == H, "embedding_bwd: dwte [V, H]");
+  }
+  if (pos) {
+    CHECK_CONTIG((*dwpe));
+    TORCH_CHECK(dwpe->scalar_type() == at::kFloat && dwpe->dim() == 2 && dwpe->size(1) == H &&
+                    dwpe->size(0) >= idx.size(1),
+                "embedding_bwd: dwpe [P >= T, H]");
+  }
+  c10::cuda::CUDAGuard g(dx.device());
+  embed_bwd_launch(ptr<int64_t>(idx), ptr<float>(dx), tok ? ptr<float>(*dwte) : nullptr,
+                   pos ? ptr<float>(*dwpe) : nullptr, idx.size(0), idx.size(1), H,
+                   tok ? static_cast<int>(dwte->size(0)) : 0, stream());
 }
 
 int64_t sumsq_scratch_size() { return sumsq_num_parts(current_device()); }
@@ -240,12 +324,19 @@ void sumsq(const at::Tensor& x, at::Tensor& scratch, double weight, at::Tensor& 
   c10::cuda::CUDAGuard g(x.device());
   const int parts = sumsq_num_parts(x.get_device());
   TORCH_CHECK(scratch.numel() >= parts, "sumsq: scratch too small");
+  CHECK_DT(scratch, at::kFloat);
+  CHECK_F32_HOLDS(out, 1);
   sumsq_launch(ptr<float>(x), x.numel(), ptr<float>(scratch), parts, static_cast<float>(weight), ptr<float>(out),
                accumulate, stream());
 }
 
 void clip_coef(const at::Tensor& norm2, double max_norm, at::Tensor& coef, const c10::optional<at::Tensor>& norm,
                const c10::optional<at::Tensor>& loss_scale) {
+  CHECK_CUDA(norm2);
+  CHECK_F32_HOLDS(norm2, 1);
+  CHECK_F32_HOLDS(coef, 1);
+  if (norm && norm->defined()) CHECK_F32_HOLDS((*norm), 1);
+  if (loss_scale && loss_scale->defined()) CHECK_F32_HOLDS((*loss_scale), 1);
   c10::cuda::CUDAGuard g(norm2.device());
   clip_coef_launch(ptr<float>(norm2), static_cast<float>(max_norm), ptr<float>(coef),
                    (norm && norm->defined()) ? ptr<float>(*norm) : nullptr,

@@ -264,3 +264,35 @@ def test_attention_trace_buffer_too_small_is_not_written():
     finally:
         ext.attention_set_trace(None)
     assert bool((full[:, 0] > 0).all())  # every CTA stamped its start
+
+
+def test_embedding_rejects_out_of_range_tokens():
+    """A token id outside [0, V) names no row: the forward reads nothing for it, makes
+    its output row NaN and reports a bad argument; the backward adds nothing for it."""
+    from heiretsu_b200.ops._C import check_status
+
+    torch.manual_seed(8)
+    B, T, V, H = 2, 64, 100, 128
+    idx = torch.randint(0, V, (B, T), device="cuda")
+    idx[1, 7] = V + 5
+    idx[0, 3] = -2
+    wte = torch.randn(V, H, device="cuda")
+    wpe = torch.randn(T, H, device="cuda")
+    out = K().embedding_fwd(idx, wte, wpe).view(B, T, H)
+    torch.cuda.synchronize()
+    with pytest.raises(RuntimeError, match="bad argument"):
+        check_status()
+    assert bool(torch.isnan(out[1, 7]).all()) and bool(torch.isnan(out[0, 3]).all())
+    good = torch.ones(B, T, dtype=torch.bool, device="cuda")
+    good[1, 7] = good[0, 3] = False
+    ref = wte[idx.clamp(0, V - 1)] + wpe[None]
+    assert torch.allclose(out[good], ref[good])
+    dwte = torch.zeros(V, H, device="cuda")
+    dx = torch.randn(B * T, H, device="cuda")
+    K().embedding_bwd(idx, dx, dwte, None)
+    check()
+    ref_dwte = torch.zeros(V, H, device="cuda")
+    ref_dwte.index_add_(0, idx.view(-1)[good.view(-1)], dx[good.view(-1)])
+    assert torch.allclose(dwte, ref_dwte, atol=1e-5)
+    with pytest.raises(RuntimeError, match="position table"):
+        K().embedding_fwd(torch.zeros(1, T + 1, dtype=torch.long, device="cuda"), wte, wpe)
