@@ -50,8 +50,13 @@ void moe_route(const at::Tensor& x, const at::Tensor& wg, int64_t K, double coef
   check_i32(pos, "moe_route: pos");
   c10::cuda::CUDAGuard g(x.device());
   const int N = x.size(0), H = x.size(1), E = wg.size(0);
+  check_f32(topw, "moe_route: topw");
+  check_f32(probsum, "moe_route: probsum");
+  check_f32(aux, "moe_route: aux");
+  TORCH_CHECK(K >= 1 && K <= E, "moe_route: top-k must be in [1, E]");
   TORCH_CHECK(wg.size(1) == H && probs.numel() >= (int64_t)N * E && topi.numel() >= N * K && off.numel() >= E + 1 &&
-                  pos.numel() >= N * K,
+                  pos.numel() >= N * K && topw.numel() >= N * K && counts.numel() >= E && probsum.numel() >= E &&
+                  aux.numel() >= 1,
               "moe_route: shape mismatch");
   moe_route_launch(P<__nv_bfloat16>(x), P<float>(wg), N, H, E, K, static_cast<float>(coef), P<float>(probs),
                    P<int>(topi), P<float>(topw), P<int>(counts), P<float>(probsum), P<int>(off), P<float>(aux),
@@ -106,6 +111,13 @@ void moe_combine(const at::Tensor& yp, const at::Tensor& pos, const at::Tensor& 
     r = P<float>(*resid);
   }
   check_window(off, e0, e1);
+  check_i32(pos, "moe_combine: pos");
+  check_f32(topw, "moe_combine: topw");
+  TORCH_CHECK(out.dim() == 2 && topw.dim() == 2 && topw.size(0) >= out.size(0), "moe_combine: out [N, H], topw [N, K]");
+  TORCH_CHECK((yp.scalar_type() == at::kBFloat16 || yp.scalar_type() == at::kHalf) && yp.is_contiguous() &&
+                  yp.dim() == 2 && yp.size(1) == out.size(1),
+              "moe_combine: yp 16-bit [R, H]");
+  TORCH_CHECK(pos.numel() >= out.size(0) * topw.size(1), "moe_combine: pos holds N * K rows");
   c10::cuda::CUDAGuard g(yp.device());
   const int N = out.size(0), H = out.size(1), K = topw.size(1);
   moe_combine_launch(P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), r, N, K, H, P<float>(out), P<int>(off), e0,
@@ -116,6 +128,16 @@ void moe_combine_bwd(const at::Tensor& dy, const at::Tensor& yp, const at::Tenso
                      at::Tensor& dyp, at::Tensor& dw, const at::Tensor& off, int64_t e0, int64_t e1) {
   check_f32(dy, "moe_combine_bwd: dy");
   check_window(off, e0, e1);
+  check_i32(pos, "moe_combine_bwd: pos");
+  check_f32(topw, "moe_combine_bwd: topw");
+  check_f32(dw, "moe_combine_bwd: dw");
+  TORCH_CHECK(dy.dim() == 2 && topw.dim() == 2 && topw.size(0) >= dy.size(0), "moe_combine_bwd: dy [N, H], topw [N, K]");
+  TORCH_CHECK((yp.scalar_type() == at::kBFloat16 || yp.scalar_type() == at::kHalf) && yp.is_contiguous() &&
+                  yp.dim() == 2 && yp.size(1) == dy.size(1) && dyp.scalar_type() == yp.scalar_type() &&
+                  dyp.is_contiguous() && dyp.numel() >= yp.numel(),
+              "moe_combine_bwd: yp and dyp 16-bit [R, H] of one format");
+  TORCH_CHECK(pos.numel() >= dy.size(0) * topw.size(1) && dw.numel() >= dy.size(0) * topw.size(1),
+              "moe_combine_bwd: pos and dw hold N * K entries");
   c10::cuda::CUDAGuard g(dy.device());
   const int N = dy.size(0), H = dy.size(1), K = topw.size(1);
   moe_combine_bwd_launch(P<float>(dy), P<__nv_bfloat16>(yp), P<int>(pos), P<float>(topw), N, K, H,
@@ -128,6 +150,9 @@ void moe_unpermute(const at::Tensor& dxp, const at::Tensor& pos, int64_t K, at::
   check_f32(dxp, "moe_unpermute: dxp");
   check_f32(dx, "moe_unpermute: dx");
   check_window(off, e0, e1);
+  check_i32(pos, "moe_unpermute: pos");
+  TORCH_CHECK(dx.dim() == 2 && dxp.dim() == 2 && dxp.size(1) == dx.size(1) && pos.numel() >= dx.size(0) * K,
+              "moe_unpermute: dxp [R, H], dx [N, H], pos N * K");
   c10::cuda::CUDAGuard g(dx.device());
   moe_unpermute_launch(P<float>(dxp), P<int>(pos), dx.size(0), K, dx.size(1), P<float>(dx), P<int>(off), e0, e1,
                        dxp.size(0), device_status_ptr(dx.get_device()), S());
@@ -145,6 +170,24 @@ void moe_router_bwd(const at::Tensor& probs, const at::Tensor& topi, const at::T
                     const at::Tensor& daux, const at::Tensor& counts, double coef, const at::Tensor& wg,
                     at::Tensor& dlogits, at::Tensor& dx) {
   check_f32(dx, "moe_router_bwd: dx");
+  check_f32(probs, "moe_router_bwd: probs");
+  check_i32(topi, "moe_router_bwd: topi");
+  check_f32(topw, "moe_router_bwd: topw");
+  check_f32(dw, "moe_router_bwd: dw");
+  check_f32(daux, "moe_router_bwd: daux");
+  check_i32(counts, "moe_router_bwd: counts");
+  check_f32(wg, "moe_router_bwd: gate weight");
+  TORCH_CHECK(probs.dim() == 2 && topi.dim() == 2 && wg.dim() == 2 && wg.size(0) == probs.size(1),
+              "moe_router_bwd: probs [N, E], topi [N, K], gate weight [E, H]");
+  {
+    const int64_t n = probs.size(0), e = probs.size(1), k = topi.size(1), h = wg.size(1);
+    TORCH_CHECK(topi.size(0) >= n && topw.numel() >= n * k && dw.numel() >= n * k && daux.numel() >= 1 &&
+                    counts.numel() >= e && dx.numel() >= n * h,
+                "moe_router_bwd: sizes");
+    TORCH_CHECK((dlogits.scalar_type() == at::kBFloat16 || dlogits.scalar_type() == at::kHalf) && dlogits.dim() == 2 &&
+                    dlogits.stride(1) == 1 && dlogits.size(0) >= n && dlogits.size(1) >= e,
+                "moe_router_bwd: dlogits 16-bit [N, >= E]");
+  }
   c10::cuda::CUDAGuard g(probs.device());
   const int N = probs.size(0), E = probs.size(1), K = topi.size(1), H = wg.size(1);
   moe_router_bwd_launch(P<float>(probs), P<int>(topi), P<float>(topw), P<float>(dw), P<float>(daux), P<int>(counts),
