@@ -257,12 +257,22 @@ def _peer_sum(buf, addend, dst, n):
 
 
 def emulate_moe(setattr_fn) -> None:
-    """Install the stand-ins on models/fused_moe.py (after fused_emulation's own)."""
+    """Install the stand-ins on models/fused_moe.py, after fused_emulation's own
+    (``emulate`` or ``emulate_tp``), whose GEMM stand-in keeps the dense forms."""
     import heiretsu_b200.models.fused_moe as FM
     from heiretsu_b200.ops import gemm as G
 
     setattr_fn(FM, "_ext", lambda: FakeMoEExt)
-    setattr_fn(G, "gemm", moe_gemm)
+    prev = G.gemm  # the stand-in already installed for the dense forms (plain or TP)
+
+    def gemm(a, b, c, n, epi, a_mn, b_mn, bias=None, aux=None, resid=None, block_n=None, ag=None, rs=None,
+             grp=None, drop=None, cmb=None):
+        if grp is not None or cmb is not None or a_mn:  # the expert-grouped and weight-gradient forms
+            return moe_gemm(a, b, c, n, epi, a_mn, b_mn, bias=bias, aux=aux, grp=grp, cmb=cmb)
+        return prev(a, b, c, n, epi, a_mn, b_mn, bias=bias, aux=aux, resid=resid, block_n=block_n, ag=ag, rs=rs,
+                    grp=grp, drop=drop)
+
+    setattr_fn(G, "gemm", gemm)
     cache = {}
 
     def ep_buffers(moe, N, H, K, device, dtype=torch.bfloat16):

@@ -2,10 +2,12 @@
 with its kernels replaced by PyTorch stand-ins (tests/moe_emulation.py, on top
 of tests/fused_emulation.py): routing and padded expert windows, the grouped
 expert GEMMs, the one-GPU combine and the backward against the plain MoE model,
-and expert parallelism on 2 gloo ranks (each rank runs its own experts; the
-second expert GEMM's combine pushes rows into every rank's slot buffer; the
-backward sums partial input gradients) against the one-process fused run.
-The kernels themselves are covered by the GPU tests."""
+expert parallelism on 2 gloo ranks (each rank runs its own experts; the second
+expert GEMM's combine pushes rows into every rank's slot buffer; the backward
+sums partial input gradients) against the one-process fused run, and expert x
+tensor parallelism (ep2 x tp2, 4 gloo ranks, MoE sub-layers on TP token
+shards) against dp2 x tp2 with every expert on every rank. The kernels
+themselves are covered by the GPU tests."""
 import torch
 
 from fused_emulation import emulate
@@ -113,3 +115,70 @@ def test_emulated_fused_ep2_matches_one_process():
         for dloss, daux, worst in per_pass:
             assert dloss == 0.0 and daux == 0.0, (dloss, daux)
             assert worst < 1e-4, worst
+
+
+def _worker_ep_tp(rank, world):
+    import torch.distributed as dist
+
+    from fused_emulation import emulate_tp
+
+    from heiretsu_b200.topo import init_topology
+
+    emulate_tp(setattr)
+    emulate_moe(setattr)
+    cfg = GPTConfig(**dict(CFG, n_layer=4))
+    x, y = _batch(B=4)
+    one, _ = _model(cfg)
+    full = {k: v.detach().clone() for k, v in one.state_dict().items()}
+
+    def run(topo):
+        from heiretsu_b200.parallel.flat import FlatParams
+        from heiretsu_b200.trainer import mark_tp_sharded, replication_weight
+        from heiretsu_b200.utils.ckpt import load_from_full
+
+        torch.manual_seed(0)
+        model = GPT(cfg, topo=topo)
+        load_from_full(model, full, topo.tp_rank, topo.tp)
+        mark_tp_sharded(model)
+        flat = FlatParams(model, torch.device("cpu"), weight_of=replication_weight(topo))
+        model.fused = True
+        for _ in range(2):  # the second pass reuses both slot buffers
+            flat.zero_grad()
+            _, loss_s, aux_s = gpt_forward_fused(model, x, y, return_logits=False)
+            (loss_s + aux_s).backward()
+            for p in model.parameters():  # token-shard partials of TP-replicated parameters
+                if not getattr(p, "tp_sharded", False):
+                    dist.all_reduce(p.main_grad, group=topo.tp_group)
+        lt = loss_s.detach().clone()
+        dist.all_reduce(lt, group=topo.tp_group)
+        return model, lt.item()
+
+    from heiretsu_b200.models.fused import gpt_forward_fused
+
+    topo_ep = init_topology(dp=1, ep=2, tp=2)
+    model_ep, loss_ep = run(topo_ep)
+    topo_tp = init_topology(dp=2, tp=2)  # same TP partner and token shard for every rank, all experts
+    model_tp, loss_tp = run(topo_tp)
+    tp_grads = {n: p.main_grad for n, p in model_tp.named_parameters()}
+    E_l = cfg.num_experts // 2
+    worst = 0.0
+    for n, p in model_ep.named_parameters():
+        ref = n
+        if ".experts." in n:
+            pre, rest = n.split(".experts.", 1)
+            j, tail = rest.split(".", 1)
+            ref = f"{pre}.experts.{topo_ep.ep_rank * E_l + int(j)}.{tail}"
+        worst = max(worst, ((p.main_grad - tp_grads[ref]).norm() / (tp_grads[ref].norm() + 1e-8)).item())
+    dist.barrier()
+    return abs(loss_ep - loss_tp), worst
+
+
+def test_emulated_fused_ep2_tp2_matches_tp2():
+    """Expert x tensor parallelism (ep2 x tp2, 4 gloo ranks; the TP blocks run on token
+    shards and each EP pair shares one) against dp2 x tp2 with every expert on every
+    rank: same token shards, same TP partners, so the forward agrees bit for bit."""
+    from dist_util import run_ranks
+
+    for dloss, worst in run_ranks(_worker_ep_tp, 4):
+        assert dloss == 0.0, dloss
+        assert worst < 1e-4, worst
