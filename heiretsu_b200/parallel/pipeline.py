@@ -147,8 +147,12 @@ class StageModule(nn.Module):
     # Fused tensor parallelism keeps the residual stream token-sharded: each
     # TP rank holds B/tp whole sequences, and the stage boundary is that shard
     # (sent to the same TP rank of the next stage, 1/tp of the dense bytes).
+    def _fused_on(self, t: torch.Tensor) -> bool:
+        """Whether this stage runs the fused kernels on `t` (a CUDA tensor)."""
+        return self.fused and t.is_cuda
+
     def _tp_fused(self, t: torch.Tensor) -> bool:
-        return self.fused and self.tp > 1 and t.is_cuda
+        return self._fused_on(t) and self.tp > 1
 
     def boundary_batch(self, B: int) -> int:
         """Sequences per boundary tensor on this rank for a micro-batch of B."""
@@ -158,7 +162,7 @@ class StageModule(nn.Module):
         B, T = idx.shape
         if T > self.cfg.block_size:
             raise ValueError(f"input of {T} positions exceeds the model's block_size of {self.cfg.block_size}")
-        if self.fused and idx.is_cuda:
+        if self._fused_on(idx):
             from ..models.fused import embed_fused
             if self._tp_fused(idx):
                 from ..models.fused_tp import tp_shard_rows
@@ -178,14 +182,14 @@ class StageModule(nn.Module):
             xs = xs if xs.dtype == torch.float32 else xs.float()
             out, aux = blocks_fused_tp(self.blocks, xs, self.cfg, self.topo, Bs * self.tp, T)
             return out.view(Bs, T, H), aux / self.tp  # shard aux losses / tp sum to the mean
-        if self.fused and x.is_cuda:
+        if self._fused_on(x):
             from ..models.fused import blocks_fused
             return blocks_fused(self.blocks, x, self.cfg, recompute=self.recompute)
         from ..models.gpt import run_blocks
         return run_blocks(self.blocks, x, self.recompute)
 
     def forward_head(self, x: torch.Tensor, targets: Optional[torch.Tensor], want_logits: bool = True):
-        if self.fused and x.is_cuda:
+        if self._fused_on(x):
             from ..models.fused import head_fused
             if self._tp_fused(x):
                 # this shard's mean loss / tp: the sum over the TP group is the dense mean
