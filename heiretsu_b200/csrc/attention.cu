@@ -6,20 +6,23 @@
 // head h at h*64) through one 3-D TMA map {3*Hs, T, B}: a 128-token tile
 // never crosses into the next sequence, and rows >= T read as zeros.
 //
-// Forward, one CTA per (pair of query tiles, head, batch), 320 threads. The
-// pair is (i, n-1-i), so every CTA does the same causal work, and both tiles
-// share each K/V tile load:
+// Forward, one CTA per (pair of adjacent query tiles 2q, 2q+1, head, batch),
+// 320 threads, heaviest pairs launched first; both tiles share each K/V load:
 //   warp 0      TMA: Q_A, Q_B, then K0, K1, V0, K2, V1, ... into a 3-slot ring
-//   warp 1      MMA: S_X = Q_X K_j^T (128x128 fp32 in TMEM), O_X = P_X V_j
+//   warp 1      MMA: S_X = Q_X K_j^T (128x128 fp32 in TMEM), O_X (+)= P_X V_j
 //   warps 2-5   softmax of tile A, warps 6-9 softmax of tile B (thread =
-//               query row): row max and exp2 over S in TMEM, P -> bf16 in
-//               128B-swizzled smem (A operand of the PV MMA), O accumulated
-//               in registers with the online-softmax rescale.
+//               query row): row max and exp2 over S in TMEM, P -> 16-bit in
+//               128B-swizzled smem (A operand of the PV MMA).
+//   O is accumulated in TMEM by the PV MMAs (softmax_tile_ot: the whole score
+//   row is loaded at once, exponentials use a reference max that moves only
+//   past a threshold, and O is rescaled in TMEM only then); with dropout each
+//   PV writes a fresh TMEM buffer that the softmax warps add into registers
+//   with the online-softmax rescale (softmax_tile).
 //   While one warpgroup runs its softmax, the MMA warp computes the other
 //   tile's S or PV, so tensor core and ALUs overlap inside the CTA. A
 //   warpgroup releases S as soon as its last TMEM load of S has landed, and
 //   the next S is computed while it still exponentiates.
-//   TMEM: per tile S [128 cols] + O double buffer [2 x 64 cols].
+//   TMEM: per tile S [128 cols] + O [64 cols] (with dropout: 2 x 64).
 //
 // Backward, one CTA per (key tile of 128, head, batch), 320 threads, FA2
 // order over the query tiles i >= key tile:
