@@ -1,8 +1,8 @@
 #pragma once
 // tcgen05 GEMM core for sm_100a.
 //
-// D[m, n] = sum_k A(m, k) * B(n, k), bf16 operands, fp32 accumulation in
-// tensor memory, fused epilogues. This single kernel template serves every
+// D[m, n] = sum_k A(m, k) * B(n, k), 16-bit operands (bf16 or fp16, one format
+// per launch), fp32 accumulation in tensor memory, fused epilogues. This single kernel template serves every
 // linear layer of the model (reference: tp_linear.py:148, :224, :301 einsums;
 // moe.py:45, :90-92 nn.Linear; gpt_model.py:240 lm_head):
 //   forward  y = x W^T        A = x  [M,K] K-major,  B = W [N,K] K-major
@@ -16,7 +16,10 @@
 //   warp 1      allocates TMEM; one elected thread issues tcgen05.mma
 //               (128 x BN x 16) and commits each stage back to the producer.
 //   warps 2..9  epilogue: tcgen05.ld the fp32 accumulator (thread = row),
-//               apply bias / GELU / dGELU / residual, store to global memory.
+//               apply bias / GELU / dGELU / residual (+ dropout), store through
+//               TMA (or into a peer's receive slot for the TP reduce-scatter, and
+//               into every EP rank's combine slot for the expert-parallel combine).
+//               With an all-gather prologue they first pull peers' token shards.
 //               Two warps share each TMEM lane quarter and split the tile's
 //               columns, so eight warps drain a tile while the next one
 //               accumulates.

@@ -1,11 +1,13 @@
 // Softmax cross-entropy over the vocabulary and the MoE aux-loss reduction.
 //
 // Replaces F.cross_entropy on materialised fp32 logits (reference
-// gpt_model.py:284-287, pipeline.py:139-142). The logits stay in bf16 (written
-// by the lm_head GEMM, row stride Vp >= V, a multiple of 8):
+// gpt_model.py:284-287, pipeline.py:139-142). The logits stay in 16 bits (bf16
+// or fp16, written by the lm_head GEMM, row stride Vp >= V, a multiple of 8):
 //   forward   per row: lse = log sum_j exp(l_j) over j < V; loss = lse - l_t
 //   backward  in place: l_j <- (softmax_j - [j == t]) * scale (0 for j >= V)
 // Targets equal to `ignore_index` contribute no loss and a zero gradient row.
+// By default one kernel does both (ce_fused_kernel: the gradient is written
+// while the row is still in L2).
 #include <cuda_bf16.h>
 
 #include "common.cuh"

@@ -18,9 +18,10 @@ are read through their bf16 shadows (``p.w16``); gradients are written to
 ``p.main_grad`` (see heiretsu_b200/parallel/flat.py), so autograd never
 allocates or adds parameter gradients.
 
-Numerics: bf16 operands, fp32 accumulation, fp32 residual stream and fp32
-LayerNorm statistics -- the same precision split as the reference under
-``torch.autocast(bf16)`` (gemm in bf16, bias add / LN / residual in fp32).
+Numerics: 16-bit operands (bf16, or fp16 under ``--amp fp16``), fp32
+accumulation, fp32 residual stream and fp32 LayerNorm statistics -- the same
+precision split as the reference under ``torch.autocast`` (gemm in 16 bits, bias
+add / LN / residual in fp32).
 """
 from __future__ import annotations
 
